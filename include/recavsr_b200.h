@@ -1,0 +1,109 @@
+/*
+ * recavsr_b200 -- C ABI of the B200 (sm_100a) kernels behind ReCaVSR's DiT hot path.
+ *
+ * Every entry point is asynchronous on `stream` (a cudaStream_t passed as a
+ * plain pointer), takes raw device pointers, sizes and strides (in elements
+ * unless the name says bytes), and returns a status:
+ *   0 RC_OK, 1 RC_ERR_ARG (invalid argument; Python raises ValueError),
+ *   2 RC_ERR_CUDA, 3 RC_ERR_TIMEOUT (a bounded device wait gave up),
+ *   4 RC_ERR_UNSUPPORTED (valid but unimplemented geometry).
+ * The text of the last failure on the calling thread is returned by
+ * rc_get_last_error(). Device-side faults that kernels detect themselves are
+ * latched in an error word read (and cleared) by rc_read_device_error().
+ * bf16 tensors are passed as `const void*` (IEEE bfloat16, row-major).
+ * None of these calls allocates device memory.
+ */
+#ifndef RECAVSR_B200_H_
+#define RECAVSR_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* rc_stream_t;
+
+/* ---- library ---------------------------------------------------------- */
+int rc_abi_version(void);
+int rc_get_last_error(char* buf, size_t size);
+int rc_read_device_error(unsigned int* word);
+
+/* ---- NVFP4 / FP8 quantizers ------------------------------------------ */
+/* Replaces recavsr_infer/runtime/nvfp4.py:49-68 `quantize(matrix)`.
+ * x: bf16 [M, K] with row stride ldx (K % 16 == 0). codes: u8 [M, K/2]
+ * (even element in the low nibble). scales_swizzled: u8
+ * [ceil(M/128)*128 * ceil(K/64)*4] in the 128x4 blocked order, padding zeroed.
+ * global_scale = 1 reproduces the reference bit for bit. */
+int rc_nvfp4_quantize(const void* x, int M, int K, long long ldx, float global_scale,
+                      uint8_t* codes, uint8_t* scales_swizzled, rc_stream_t stream);
+
+/* Replaces the activation quantization of recavsr_infer/runtime/fp8.py:41-42
+ * (and the weight quantization of :32-34): scale = max(amax,1e-12)/448 written
+ * to *scale_out (device), q = e4m3(clamp(x/scale)). amax_scratch: one device
+ * u32, overwritten. */
+int rc_fp8_quantize(const void* x, int M, int K, long long ldx, unsigned int* amax_scratch,
+                    float* scale_out, uint8_t* q, rc_stream_t stream);
+
+/* ---- GEMMs (tcgen05) --------------------------------------------------- */
+/* Epilogues: 0 out = bf16(alpha*acc + bias); 1 out = bf16(out + bf16(alpha*acc+bias)*gate[n]);
+ * 2 out = bf16(out + bf16(alpha*acc+bias)); 3 (NVFP4 only) y = bf16(gelu_tanh(bf16(alpha*acc+bias)))
+ * quantized to NVFP4 into q_codes / q_scales (out optional). K % 64 == 0, N % 16 == 0. */
+#define RC_EPI_BIAS 0
+#define RC_EPI_GATED_RESIDUAL 1
+#define RC_EPI_RESIDUAL 2
+#define RC_EPI_GELU_NVFP4 3
+
+/* Replaces recavsr_infer/runtime/nvfp4.py:22-39 `nvfp4_mm` (torch._scaled_mm_v2,
+ * BlockWise1x16 / SWIZZLE_32_4_4, bias, bf16 out). */
+int rc_nvfp4_gemm(const uint8_t* a_codes, const uint8_t* a_scales, const uint8_t* b_codes,
+                  const uint8_t* b_scales, const void* bias, int M, int N, int K, float alpha,
+                  int epilogue, void* out, long long ldo, const float* gate, uint8_t* q_codes,
+                  uint8_t* q_scales, float q_global_scale, rc_stream_t stream);
+
+/* Replaces the torch._scaled_mm call of recavsr_infer/runtime/fp8.py:44-47
+ * (per-tensor scales are device pointers, use_fast_accum=False semantics). */
+int rc_fp8_gemm(const uint8_t* a, const float* scale_a, const uint8_t* b, const float* scale_b,
+                const void* bias, int M, int N, int K, float alpha, int epilogue, void* out,
+                long long ldo, const float* gate, rc_stream_t stream);
+
+/* bf16 nn.Linear (the default, unquantized DiT linears of
+ * recavsr_infer/runtime/transformer.py:95-133). */
+int rc_bf16_gemm(const void* a, const void* b, const void* bias, int M, int N, int K, int epilogue,
+                 void* out, long long ldo, const float* gate, rc_stream_t stream);
+
+/* ---- glue --------------------------------------------------------------- */
+/* LayerNorm (+affine) (+AdaLN modulation) (+fused NVFP4 quantize) of
+ * recavsr_infer/runtime/transformer.py:91-93,121,130-132 and
+ * kernels/native_norm.py:7-17. */
+int rc_ln_modulate_quant(const void* x, long long ldx, int M, int N, const void* weight,
+                         const void* bias, const float* shift, const float* scale, float eps,
+                         void* out, long long ldo, uint8_t* codes, uint8_t* scales_swizzled,
+                         float global_scale, rc_stream_t stream);
+
+/* RMSNorm across heads (+ spatial rotary) of up to two tensors:
+ * recavsr_infer/runtime/transformer.py:99-100,122 (norm_q/norm_k, PreparedBlock.spatial),
+ * kernels/native_norm.py:25-28, runtime/rope.py:23-30. */
+int rc_rmsnorm_rope(int n_tensors, const void* const* xs, const long long* ldx,
+                    const void* const* weights, void* const* outs, const long long* ldo, int M,
+                    int N, int d, int span, const float* cos, const float* sin, float eps,
+                    rc_stream_t stream);
+
+/* Temporal rotary embedding of recavsr_infer/runtime/rope.py:33-47 (apply_temporal). */
+int rc_temporal_rope(const void* x, long long ldx, void* out, long long ldo, const int* positions,
+                     const float* cos, const float* sin, int rows, int span, int heads, int d,
+                     int td, rc_stream_t stream);
+
+/* ---- KV cache ------------------------------------------------------------ */
+/* Plane copies of recavsr_infer/runtime/cache.py:121-134 (FixedKVCache.commit):
+ * plane src_planes[i] of the block's K/V -> slot dst_slots[i] of the cache. */
+int rc_kv_commit(const void* src_k, const void* src_v, long long src_ld_bytes, void* dst_k,
+                 void* dst_v, long long dst_ld_bytes, int row_bytes, int span, int n_planes,
+                 const int* src_planes, const int* dst_slots, rc_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* RECAVSR_B200_H_ */

@@ -1,0 +1,164 @@
+// Shared host/device helpers for the ReCaVSR B200 kernels.
+//
+// Status convention of every extern "C" entry point (include/recavsr_b200.h):
+//   0 = ok, 1 = invalid argument, 2 = CUDA error, 3 = device wait timed out,
+//   4 = unsupported configuration. The message of the last failure on the
+//   calling host thread is kept for rc_get_last_error().
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+#include <math.h>
+
+#define RC_OK 0
+#define RC_ERR_ARG 1
+#define RC_ERR_CUDA 2
+#define RC_ERR_TIMEOUT 3
+#define RC_ERR_UNSUPPORTED 4
+
+// Device-side error word, one per translation unit. A kernel whose bounded
+// wait gives up (or that sees an impossible index) stores a non-zero code here
+// and returns early; the host reads and clears every unit's word with
+// rc_read_device_error().
+//   bits 0..7  = kernel id, bits 8..15 = site, bits 16..31 = block id (low bits)
+static __device__ unsigned int g_rc_device_error;
+
+// Defines `unsigned int rc_take_device_error_<tag>()` for this unit.
+#define RC_DEVICE_ERROR_ACCESSOR(tag)                                              \
+  unsigned int rc_take_device_error_##tag() {                                      \
+    unsigned int v = 0, zero = 0;                                                  \
+    if (cudaMemcpyFromSymbol(&v, g_rc_device_error, sizeof(v)) != cudaSuccess)     \
+      return 0xffffffffu;                                                          \
+    if (v) cudaMemcpyToSymbol(g_rc_device_error, &zero, sizeof(zero));            \
+    return v;                                                                      \
+  }
+
+// Kernel ids stored in the low byte of the error word.
+enum RcKernelId : unsigned int {
+  kKernQuant = 1, kKernGemmNvf4 = 2, kKernGemmFp8 = 3, kKernAttention = 4,
+  kKernGlue = 5, kKernCache = 6,
+};
+
+namespace rc {
+
+int set_error(int code, const char* fmt, ...);
+int check_launch(const char* what);
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no -lcuda).
+// dims/strides: innermost first; strides are in bytes for dims 1..rank-1.
+int encode_tmap(CUtensorMap* map, CUtensorMapDataType dtype, int rank, void* base,
+                const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,
+                CUtensorMapSwizzle swizzle, const char* what);
+
+// Device: record the first error only.
+__device__ __forceinline__ void device_fail(unsigned int kernel_id, unsigned int site) {
+  unsigned int word = (kernel_id & 0xffu) | ((site & 0xffu) << 8) |
+                      ((blockIdx.x & 0xffffu) << 16);
+  atomicCAS(&g_rc_device_error, 0u, word);
+}
+
+// Wall-clock bound of any device-side wait (mbarrier phase, flag): far above
+// any legitimate wait inside one kernel, yet it guarantees that a kernel never
+// hangs the GPU. Measured on %globaltimer (nanoseconds).
+constexpr unsigned long long kWaitNs = 4000000000ull;
+
+__device__ __forceinline__ unsigned long long globaltimer_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// ---------------------------------------------------------------------------
+// FP8 E4M3 (fn variant: no infinities, 0x7f / 0xff are NaN, max finite 448).
+// Round-to-nearest-even, subnormals kept, magnitudes >= 480 (and NaN) map to
+// the NaN code 0x7f with the input's sign: the same results as PyTorch's
+// float -> float8_e4m3fn cast that the reference quantizers use.
+// Derivation: subnormal grid is k * 2^-9 (k = 0..7); the normal grid within
+// [2^e, 2^(e+1)) is 2^e * (1 + j/8). Rounding a*2^9 or the mantissa fraction
+// with rintf (RNE) gives the code directly; a carry rolls into the exponent.
+// ---------------------------------------------------------------------------
+__host__ __device__ __forceinline__ uint8_t e4m3_from_float(float v) {
+  uint32_t bits;
+#ifdef __CUDA_ARCH__
+  bits = __float_as_uint(v);
+#else
+  memcpy(&bits, &v, 4);
+#endif
+  const uint8_t sign = (uint8_t)((bits >> 24) & 0x80u);
+  const float a = fabsf(v);
+  if (!(a < 480.0f)) return (uint8_t)(sign | 0x7fu);
+  if (a < 0.015625f) {  // below 2^-6: subnormal grid of 2^-9
+    const int k = (int)rintf(a * 512.0f);
+    return (uint8_t)(sign | (uint8_t)k);  // k == 8 is exactly the min normal 0x08
+  }
+  int e;
+  const float m = frexpf(a, &e);  // a = m * 2^e, m in [0.5, 1)
+  // a = (2m) * 2^(e-1), 2m in [1, 2); biased exponent = e - 1 + 7
+  const int j = (int)rintf((2.0f * m - 1.0f) * 8.0f);
+  const int code = ((e + 6) << 3) + j;  // a carry (j == 8) bumps the exponent
+  return (uint8_t)(sign | (uint8_t)code);
+}
+
+__host__ __device__ __forceinline__ float e4m3_to_float(uint8_t c) {
+  const int s = c >> 7, e = (c >> 3) & 0xf, m = c & 7;
+  float v;
+  if (e == 0xf && m == 7) {
+    v = NAN;
+  } else if (e == 0) {
+    v = ldexpf((float)m, -9);
+  } else {
+    v = ldexpf(1.0f + (float)m * 0.125f, e - 7);
+  }
+  return s ? -v : v;
+}
+
+// E2M1 code of z (magnitudes 0, .5, 1, 1.5, 2, 3, 4, 6; ties to even) as the
+// count of thresholds passed, strict at .25/1.25/2.5/5 and inclusive at
+// .75/1.75/3.5, with the sign bit (8) set for z < 0 only (so -0 and NaN give
+// code 0). Same decision ladder as recavsr_infer/runtime/nvfp4.py:56-61.
+__host__ __device__ __forceinline__ uint32_t e2m1_code(float z) {
+  const float a = fabsf(z);
+  uint32_t c = (a > 0.25f) + (a >= 0.75f) + (a > 1.25f) + (a >= 1.75f) + (a > 2.5f) +
+               (a >= 3.5f) + (a > 5.0f);
+  return c | (z < 0.0f ? 8u : 0u);
+}
+
+// Offset of the scale byte for (row, k-block) in the 128x4 blocked layout
+// (recavsr_infer/runtime/nvfp4.py:64-67): atoms of 128 rows x 4 k-blocks,
+// k-atoms innermost; inside an atom, row r = 32*m1 + m0 and k-block kk sit at
+// m0*16 + m1*4 + kk.
+__host__ __device__ __forceinline__ size_t sf_offset(int row, int kb, int katoms) {
+  const int mb = row >> 7, r = row & 127, m0 = r & 31, m1 = r >> 5;
+  const int kt = kb >> 2, kk = kb & 3;
+  return ((size_t)(mb * katoms + kt) * 32 + m0) * 16 + m1 * 4 + kk;
+}
+
+// Round-to-nearest-even float -> bf16 bits (NaN kept quiet).
+__host__ __device__ __forceinline__ uint16_t bf16_bits(float f) {
+#ifdef __CUDA_ARCH__
+  return __bfloat16_as_ushort(__float2bfloat16_rn(f));
+#else
+  uint32_t u;
+  memcpy(&u, &f, 4);
+  if ((u & 0x7fffffffu) > 0x7f800000u) return (uint16_t)((u >> 16) | 0x40);
+  u += 0x7fffu + ((u >> 16) & 1u);
+  return (uint16_t)(u >> 16);
+#endif
+}
+__host__ __device__ __forceinline__ float bf16_to_float(uint16_t h) {
+#ifdef __CUDA_ARCH__
+  return __uint_as_float((uint32_t)h << 16);
+#else
+  uint32_t u = (uint32_t)h << 16;
+  float f;
+  memcpy(&f, &u, 4);
+  return f;
+#endif
+}
+
+}  // namespace rc

@@ -1,0 +1,512 @@
+// tcgen05 GEMM for the DiT linears: D[M,N] = epilogue(alpha * A[M,K] . B[N,K]^T + bias).
+//
+// Operand kinds (both operands K-major, 128-byte rows staged by TMA with the
+// 128-byte swizzle, 32 bytes of K per MMA instruction):
+//   NVF4 : E2M1 codes (2 per byte) with UE4M3 scales per 16 elements in the
+//          128x4 blocked layout of recavsr_infer/runtime/nvfp4.py:64-67 (the
+//          same layout the MMA consumes, so scale atoms are copied verbatim:
+//          global -> smem with a bulk copy -> TMEM with tcgen05.cp 32x128b.warpx4)
+//          -- replaces torch._scaled_mm_v2 in runtime/nvfp4.py:22-39.
+//   E4M3 : per-tensor scaled FP8, alpha = scale_a * scale_b read on device
+//          -- replaces torch._scaled_mm in runtime/fp8.py:44-47.
+//   BF16 : plain bf16 linears.
+// Accumulation is fp32 in TMEM. One CTA per SM runs a persistent loop over
+// 128 x BN output tiles with warp roles: warp 0 = TMA producer, warp 1 = MMA
+// issuer (+ TMEM owner), warps 2-5 = epilogue (TMEM -> registers -> global).
+// Epilogues fuse the block's follow-up element-wise work:
+//   BIAS           out = bf16(acc*alpha + bias)
+//   GATED_RESIDUAL h   = bf16(h + bf16(acc*alpha + bias) * gate[n])   (in place)
+//   RESIDUAL       h   = bf16(h + bf16(acc*alpha + bias))            (in place)
+//   GELU_NVF4      y   = bf16(gelu_tanh(bf16(acc*alpha + bias))), quantized to
+//                  NVFP4 (16 columns = one block) for the next linear.
+#include "sm100.cuh"
+
+namespace {
+
+enum Kind : int { KIND_NVF4 = 0, KIND_E4M3 = 1, KIND_BF16 = 2 };
+enum Epi : int { EPI_BIAS = 0, EPI_GATED_RESIDUAL = 1, EPI_RESIDUAL = 2, EPI_GELU_NVF4 = 3 };
+
+constexpr int BM = 128;
+constexpr int kRowBytes = 128;                     // K bytes per smem row / k-tile
+constexpr int kThreads = 192;                      // 6 warps
+constexpr int kSfAtomBytes = 512;                  // 128 rows x 4 scale bytes
+
+template <int KIND>
+struct KindTraits;
+template <>
+struct KindTraits<KIND_NVF4> {
+  static constexpr int kElemsPerTile = 256;   // K elements per 128-byte row
+  static constexpr bool kScaled = true;
+};
+template <>
+struct KindTraits<KIND_E4M3> {
+  static constexpr int kElemsPerTile = 128;
+  static constexpr bool kScaled = false;
+};
+template <>
+struct KindTraits<KIND_BF16> {
+  static constexpr int kElemsPerTile = 64;
+  static constexpr bool kScaled = false;
+};
+
+struct GemmParams {
+  int M, N, K;
+  int k_tiles;                 // ceil(K / elems per tile)
+  int m_blocks, n_blocks;
+  const uint8_t* sfa;          // NVF4: swizzled scales of A (padded)
+  const uint8_t* sfb;          // NVF4: swizzled scales of B
+  int sf_katoms;               // ceil(K/64): 4-block atoms along K
+  float alpha;
+  const float* alpha_ptr_a;    // E4M3: device scale of A (nullable)
+  const float* alpha_ptr_b;    // E4M3: device scale of B (nullable)
+  const __nv_bfloat16* bias;   // [N] (nullable)
+  __nv_bfloat16* out;          // [M, ldo] (BIAS / GELU_NVF4 bf16 out, nullable for GELU)
+  long long ldo;
+  const float* gate;           // [N] (GATED_RESIDUAL)
+  uint8_t* q_codes;            // GELU_NVF4: [M, N/2]
+  uint8_t* q_sf;               // GELU_NVF4: swizzled scales (N as K)
+  float q_g;                   // GELU_NVF4: global scale
+};
+
+template <int KIND, int BN, int STAGES>
+struct Smem {
+  static constexpr int kA = BM * kRowBytes;
+  static constexpr int kB = BN * kRowBytes;
+  static constexpr int kSfa = KindTraits<KIND>::kScaled ? 4 * kSfAtomBytes : 0;
+  static constexpr int kSfb = KindTraits<KIND>::kScaled ? (BN / 128) * 4 * kSfAtomBytes : 0;
+  static constexpr int offA = 0;
+  static constexpr int offB = offA + STAGES * kA;
+  static constexpr int offSfa = offB + STAGES * kB;
+  static constexpr int offSfb = offSfa + STAGES * kSfa;
+  static constexpr int offBar = offSfb + STAGES * kSfb;
+  static constexpr int kBars = 2 * STAGES + 4 + 1;
+  static constexpr int kTotal = offBar + kBars * 8 + 16;
+  static constexpr int kAlloc = kTotal + 1024;      // slack for 1024-byte alignment
+};
+
+__device__ __forceinline__ float gelu_tanh(float x) {
+  // 0.5 * x * (1 + tanh(sqrt(2/pi) * (x + 0.044715 x^3))), fp32 as in
+  // torch's gelu(approximate="tanh") for bf16 inputs.
+  const float k0 = 0.7978845608028654f, k1 = 0.044715f;
+  const float inner = __fmul_rn(k0, __fadd_rn(x, __fmul_rn(k1, __fmul_rn(__fmul_rn(x, x), x))));
+  return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, tanhf(inner)));
+}
+
+template <int KIND, int BN, int STAGES, int EPI>
+__global__ void __launch_bounds__(kThreads, 1)
+gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+            const GemmParams p) {
+  using S = Smem<KIND, BN, STAGES>;
+  constexpr bool kScaled = KindTraits<KIND>::kScaled;
+  constexpr int kMmaPerTile = 4;                     // 4 x 32 bytes of K per 128-byte row
+  constexpr int kTmemCols = 512;
+  constexpr int kSfaCols = 16;                       // 4 k-steps x 4 columns
+  constexpr int kSfbCols = 4 * (BN / 32);            // 4 k-steps x BN/32 columns
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::offBar);
+  uint64_t* empty = full + STAGES;
+  uint64_t* acc_full = empty + STAGES;     // [1]
+  uint64_t* acc_empty = acc_full + 1;      // [1]
+  uint64_t* done = acc_empty + 1;          // [1]
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(done + 2);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 3);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int num_tiles = p.m_blocks * p.n_blocks;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      sm100::mbar_init(&full[s], 1);
+      sm100::mbar_init(&empty[s], 1);
+    }
+    sm100::mbar_init(acc_full, 1);
+    sm100::mbar_init(acc_empty, 128);
+    sm100::mbar_init(done, 1);
+    *abort_flag = 0;
+    sm100::fence_mbar_init();
+  }
+  if (warp == 1) {
+    sm100::tmem_alloc(tmem_slot, kTmemCols);
+    sm100::tmem_relinquish();
+  }
+  sm100::tc_fence_before();
+  __syncthreads();
+  sm100::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tmem_acc = tmem;                           // columns [0, BN)
+  const uint32_t tmem_sfa = tmem + BN;                      // 2 x kSfaCols
+  const uint32_t tmem_sfb = tmem + BN + 2 * kSfaCols;       // 2 x kSfbCols
+
+  auto fail = [&](unsigned int site) {
+    rc::device_fail(kKernGemmNvf4 + (KIND == KIND_NVF4 ? 0 : 1), site);
+    *abort_flag = 1;
+  };
+  auto wait = [&](uint64_t* bar, uint32_t parity, unsigned int site) -> bool {
+    if (sm100::mbar_wait(bar, parity, abort_flag)) return true;
+    if (!*abort_flag) fail(site);
+    return false;
+  };
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (sm100::elect_one_sync()) {
+      sm100::tma_prefetch_desc(&tmap_a);
+      sm100::tma_prefetch_desc(&tmap_b);
+      int stage = 0;
+      uint32_t phase = 0;
+      long long issued = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        const int mb = tile % p.m_blocks, nb = tile / p.m_blocks;
+        for (int kt = 0; kt < p.k_tiles; ++kt) {
+          if (!wait(&empty[stage], phase ^ 1, 1)) { ok = false; break; }
+          uint32_t bytes = S::kA + S::kB;
+          int sfa_bytes = 0, sfb_bytes = 0;
+          if constexpr (kScaled) {
+            const int atoms = min(4, p.sf_katoms - kt * 4);
+            sfa_bytes = atoms * kSfAtomBytes;
+            bytes += sfa_bytes;
+            for (int r = 0; r < BN / 128; ++r) sfb_bytes += atoms * kSfAtomBytes;
+            bytes += sfb_bytes;
+          }
+          sm100::mbar_arrive_expect_tx(&full[stage], bytes);
+          sm100::tma_load_2d(smem + S::offA + stage * S::kA, &tmap_a, &full[stage], kt * kRowBytes, mb * BM);
+          sm100::tma_load_2d(smem + S::offB + stage * S::kB, &tmap_b, &full[stage], kt * kRowBytes, nb * BN);
+          if constexpr (kScaled) {
+            const int atoms = sfa_bytes / kSfAtomBytes;
+            const uint8_t* src_a = p.sfa + ((size_t)mb * p.sf_katoms + kt * 4) * kSfAtomBytes;
+            asm volatile(
+                "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                    sm100::smem_u32(smem + S::offSfa + stage * S::kSfa)),
+                "l"(src_a), "r"(sfa_bytes), "r"(sm100::smem_u32(&full[stage]))
+                : "memory");
+            for (int r = 0; r < BN / 128; ++r) {
+              const uint8_t* src_b =
+                  p.sfb + ((size_t)(nb * (BN / 128) + r) * p.sf_katoms + kt * 4) * kSfAtomBytes;
+              asm volatile(
+                  "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                      sm100::smem_u32(smem + S::offSfb + stage * S::kSfb + r * 4 * kSfAtomBytes)),
+                  "l"(src_b), "r"(atoms * kSfAtomBytes), "r"(sm100::smem_u32(&full[stage]))
+                  : "memory");
+            }
+            (void)atoms;
+          }
+          ++issued;
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+      }
+      // Drain: every load this thread issued must land before the CTA exits.
+      for (int s = 0; s < STAGES && issued > 0; ++s, --issued) {
+        if (stage == 0) { stage = STAGES; phase ^= 1; }
+        --stage;
+        sm100::mbar_wait(&full[stage], phase);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (sm100::elect_one_sync()) {
+      uint32_t idesc;
+      if constexpr (KIND == KIND_NVF4) idesc = sm100::idesc_nvf4(BM, BN);
+      else if constexpr (KIND == KIND_E4M3) idesc = sm100::idesc_e4m3(BM, BN);
+      else idesc = sm100::idesc_bf16(BM, BN, 0, 0);
+      int stage = 0;
+      uint32_t phase = 0, acc_phase = 0;
+      int sf_buf = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        if (!wait(acc_empty, acc_phase ^ 1, 2)) { ok = false; break; }
+        sm100::tc_fence_after();
+        for (int kt = 0; kt < p.k_tiles; ++kt) {
+          if (!wait(&full[stage], phase, 3)) { ok = false; break; }
+          sm100::tc_fence_after();
+          const uint32_t a0 = sm100::smem_u32(smem + S::offA + stage * S::kA);
+          const uint32_t b0 = sm100::smem_u32(smem + S::offB + stage * S::kB);
+          int steps = kMmaPerTile;
+          if constexpr (kScaled) {
+            steps = min(4, p.sf_katoms - kt * 4);   // K % 64 == 0: one atom per k-step
+            const uint32_t sfa_t = tmem_sfa + sf_buf * kSfaCols;
+            const uint32_t sfb_t = tmem_sfb + sf_buf * kSfbCols;
+            const uint32_t sa0 = sm100::smem_u32(smem + S::offSfa + stage * S::kSfa);
+            const uint32_t sb0 = sm100::smem_u32(smem + S::offSfb + stage * S::kSfb);
+            for (int j = 0; j < steps; ++j) {
+              sm100::tmem_cp_32x128b_warpx4(sfa_t + 4 * j, sm100::desc_sf_rows(sa0 + j * kSfAtomBytes));
+              for (int r = 0; r < BN / 128; ++r)
+                sm100::tmem_cp_32x128b_warpx4(sfb_t + j * (BN / 32) + 4 * r,
+                                              sm100::desc_sf_rows(sb0 + (r * 4 + j) * kSfAtomBytes));
+            }
+            for (int j = 0; j < steps; ++j) {
+              sm100::mma_nvf4_ss(tmem_acc, sm100::desc_kmajor_sw128(a0 + 32 * j),
+                                 sm100::desc_kmajor_sw128(b0 + 32 * j), idesc, sfa_t + 4 * j,
+                                 sfb_t + j * (BN / 32), (kt | j) != 0);
+            }
+            sf_buf ^= 1;
+          } else {
+            const int rem = (p.K - kt * KindTraits<KIND>::kElemsPerTile) /
+                            (KindTraits<KIND>::kElemsPerTile / kMmaPerTile);
+            steps = min(kMmaPerTile, rem);
+            for (int j = 0; j < steps; ++j) {
+              if constexpr (KIND == KIND_E4M3)
+                sm100::mma_f8f6f4_ss(tmem_acc, sm100::desc_kmajor_sw128(a0 + 32 * j),
+                                     sm100::desc_kmajor_sw128(b0 + 32 * j), idesc, (kt | j) != 0);
+              else
+                sm100::mma_f16_ss(tmem_acc, sm100::desc_kmajor_sw128(a0 + 32 * j),
+                                  sm100::desc_kmajor_sw128(b0 + 32 * j), idesc, (kt | j) != 0);
+            }
+          }
+          sm100::tc_commit(&empty[stage]);
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+        if (!ok) break;
+        sm100::tc_commit(acc_full);
+        acc_phase ^= 1;
+      }
+      // Make sure no MMA is still writing TMEM when the CTA tears down.
+      sm100::tc_commit(done);
+      sm100::mbar_wait(done, 0);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int quad = warp & 3;                 // TMEM lane quadrant of this warp
+    const int row_in_tile = quad * 32 + lane;
+    uint32_t acc_phase = 0;
+    float alpha = p.alpha;
+    if constexpr (KIND == KIND_E4M3) {
+      if (p.alpha_ptr_a) alpha = __fmul_rn(alpha, *p.alpha_ptr_a);
+      if (p.alpha_ptr_b) alpha = __fmul_rn(alpha, *p.alpha_ptr_b);
+    }
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+      const int mb = tile % p.m_blocks, nb = tile / p.m_blocks;
+      if (!wait(acc_full, acc_phase, 4)) break;
+      sm100::tc_fence_after();
+      const int row = mb * BM + row_in_tile;
+      const bool row_ok = row < p.M;
+      const uint32_t t_row = tmem_acc + ((uint32_t)(quad * 32) << 16);
+#pragma unroll 1
+      for (int c0 = 0; c0 < BN; c0 += 16) {
+        uint32_t r[16];
+        sm100::tmem_ld16(t_row + c0, r);
+        sm100::tmem_ld_wait();
+        const int n0 = nb * BN + c0;
+        if (n0 >= p.N) continue;
+        if (!row_ok) {
+          // Padding rows of the next linear's scale atoms must read as zero.
+          if constexpr (EPI == EPI_GELU_NVF4) p.q_sf[rc::sf_offset(row, n0 >> 4, (p.N + 63) >> 6)] = 0;
+          continue;
+        }
+        float v[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          float x = __fmul_rn(__uint_as_float(r[j]), alpha);
+          if (p.bias) x = __fadd_rn(x, __bfloat162float(p.bias[n0 + j]));
+          v[j] = rc::bf16_to_float(rc::bf16_bits(x));
+        }
+        if constexpr (EPI == EPI_GATED_RESIDUAL || EPI == EPI_RESIDUAL) {
+          __nv_bfloat16* hp = p.out + (size_t)row * p.ldo + n0;
+          const uint4 h0 = *reinterpret_cast<const uint4*>(hp);
+          const uint4 h1 = *reinterpret_cast<const uint4*>(hp + 8);
+          const uint32_t hw[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const float h = __uint_as_float((j & 1) ? (hw[j >> 1] & 0xffff0000u) : (hw[j >> 1] << 16));
+            const float add = (EPI == EPI_GATED_RESIDUAL) ? __fmul_rn(v[j], p.gate[n0 + j]) : v[j];
+            v[j] = __fadd_rn(h, add);
+          }
+        }
+        if constexpr (EPI == EPI_GELU_NVF4) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) v[j] = rc::bf16_to_float(rc::bf16_bits(gelu_tanh(v[j])));
+          float amax = 0.f;
+#pragma unroll
+          for (int j = 0; j < 16; ++j) amax = fmaxf(amax, fabsf(v[j]));
+          float sc = __fmul_rn(__fdiv_rn(amax, 6.0f), p.q_g);
+          sc = sc < 0.001953125f ? 0.001953125f : sc;
+          const uint8_t sfb = rc::e4m3_from_float(sc);
+          const float sd = rc::e4m3_to_float(sfb);
+          uint32_t lo = 0, hi = 0;
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const uint32_t code = rc::e2m1_code(__fdiv_rn(__fmul_rn(v[j], p.q_g), sd));
+            if (j < 8) lo |= code << (4 * j);
+            else hi |= code << (4 * (j - 8));
+          }
+          *reinterpret_cast<uint2*>(p.q_codes + (size_t)row * (p.N >> 1) + (n0 >> 1)) = make_uint2(lo, hi);
+          p.q_sf[rc::sf_offset(row, n0 >> 4, (p.N + 63) >> 6)] = sfb;
+          if (!p.out) continue;
+        }
+        uint32_t w[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          w[j] = (uint32_t)rc::bf16_bits(v[2 * j]) | ((uint32_t)rc::bf16_bits(v[2 * j + 1]) << 16);
+        uint4* dst = reinterpret_cast<uint4*>(p.out + (size_t)row * p.ldo + n0);
+        dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+        dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+      }
+      sm100::tc_fence_before();
+      sm100::mbar_arrive(acc_empty);
+      acc_phase ^= 1;
+    }
+  }
+
+  sm100::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    sm100::tc_fence_after();
+    sm100::tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+int g_num_sms = 0;
+int num_sms() {
+  if (!g_num_sms) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
+    if (g_num_sms <= 0) g_num_sms = 148;
+  }
+  return g_num_sms;
+}
+
+template <int KIND, int BN, int STAGES, int EPI>
+int launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, cudaStream_t stream,
+           const char* what) {
+  using S = Smem<KIND, BN, STAGES>;
+  auto kern = gemm_kernel<KIND, BN, STAGES, EPI>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kAlloc) != cudaSuccess)
+      return rc::set_error(RC_ERR_CUDA, "%s: cannot reserve %d bytes of shared memory", what, S::kAlloc);
+    attr_set = true;
+  }
+  const int tiles = p.m_blocks * p.n_blocks;
+  const int grid = tiles < num_sms() ? tiles : num_sms();
+  kern<<<grid, kThreads, S::kAlloc, stream>>>(ta, tb, p);
+  return rc::check_launch(what);
+}
+
+template <int KIND, int BN, int STAGES>
+int dispatch_epi(int epi, const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p,
+                 cudaStream_t stream, const char* what) {
+  switch (epi) {
+    case EPI_BIAS: return launch<KIND, BN, STAGES, EPI_BIAS>(ta, tb, p, stream, what);
+    case EPI_GATED_RESIDUAL: return launch<KIND, BN, STAGES, EPI_GATED_RESIDUAL>(ta, tb, p, stream, what);
+    case EPI_RESIDUAL: return launch<KIND, BN, STAGES, EPI_RESIDUAL>(ta, tb, p, stream, what);
+    case EPI_GELU_NVF4: return launch<KIND, BN, STAGES, EPI_GELU_NVF4>(ta, tb, p, stream, what);
+  }
+  return rc::set_error(RC_ERR_ARG, "%s: unknown epilogue %d", what, epi);
+}
+
+// Shared argument checks + tensor maps; `elem_bytes_x2` = 2 * bytes/element
+// (1 for fp4, 2 for fp8, 4 for bf16).
+int run_gemm(int kind, int epi, const void* a, const void* b, int M, int N, int K,
+             GemmParams& p, cudaStream_t stream, const char* what) {
+  const int ebx2 = kind == KIND_NVF4 ? 1 : (kind == KIND_E4M3 ? 2 : 4);
+  if (M < 0 || N <= 0 || K <= 0 || N % 16)
+    return rc::set_error(RC_ERR_ARG, "%s: bad shape M=%d N=%d K=%d (N %% 16 == 0)", what, M, N, K);
+  if (K % 64)
+    return rc::set_error(RC_ERR_UNSUPPORTED, "%s: K must be a multiple of 64 (K=%d)", what, K);
+  if (!a || !b) return rc::set_error(RC_ERR_ARG, "%s: null operand", what);
+  if (epi != EPI_GELU_NVF4 || p.out) {
+    if (!p.out || p.ldo < N || p.ldo % 8 || reinterpret_cast<uintptr_t>(p.out) % 16)
+      return rc::set_error(RC_ERR_ARG, "%s: output rows must be 16-byte aligned (ldo=%lld)", what, p.ldo);
+  }
+  if (epi == EPI_GATED_RESIDUAL && !p.gate) return rc::set_error(RC_ERR_ARG, "%s: gate missing", what);
+  if (epi == EPI_GELU_NVF4 && (!p.q_codes || !p.q_sf || N % 64))
+    return rc::set_error(RC_ERR_ARG, "%s: GELU/NVFP4 epilogue needs codes, scales and N %% 64 == 0", what);
+  if (M == 0) return RC_OK;
+  const uint64_t row_bytes = (uint64_t)K * ebx2 / 2;
+  CUtensorMap ta, tb;
+  const uint64_t da[2] = {row_bytes, (uint64_t)M}, db[2] = {row_bytes, (uint64_t)N};
+  const uint64_t sa[1] = {row_bytes}, sb[1] = {row_bytes};
+  const bool wide = (N % 256 == 0) && (M > 0);
+  const uint32_t boxa[2] = {128, 128}, boxb[2] = {128, (uint32_t)(wide ? 256 : 128)};
+  int r = rc::encode_tmap(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(a), da, sa, boxa,
+                          CU_TENSOR_MAP_SWIZZLE_128B, what);
+  if (r) return r;
+  r = rc::encode_tmap(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(b), db, sb, boxb,
+                      CU_TENSOR_MAP_SWIZZLE_128B, what);
+  if (r) return r;
+  const int ept = kind == KIND_NVF4 ? 256 : (kind == KIND_E4M3 ? 128 : 64);
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.k_tiles = (K + ept - 1) / ept;
+  p.m_blocks = (M + BM - 1) / BM;
+  p.sf_katoms = (K + 63) / 64;
+  if (wide) {
+    p.n_blocks = N / 256;
+    if (kind == KIND_NVF4) return dispatch_epi<KIND_NVF4, 256, 4>(epi, ta, tb, p, stream, what);
+    if (kind == KIND_E4M3) return dispatch_epi<KIND_E4M3, 256, 4>(epi, ta, tb, p, stream, what);
+    return dispatch_epi<KIND_BF16, 256, 4>(epi, ta, tb, p, stream, what);
+  }
+  p.n_blocks = (N + 127) / 128;
+  if (kind == KIND_NVF4) return dispatch_epi<KIND_NVF4, 128, 6>(epi, ta, tb, p, stream, what);
+  if (kind == KIND_E4M3) return dispatch_epi<KIND_E4M3, 128, 6>(epi, ta, tb, p, stream, what);
+  return dispatch_epi<KIND_BF16, 128, 6>(epi, ta, tb, p, stream, what);
+}
+
+}  // namespace
+
+RC_DEVICE_ERROR_ACCESSOR(gemm_nvf4)
+unsigned int rc_take_device_error_gemm_fp8() { return 0; }
+
+extern "C" {
+
+// NVFP4 block-scaled GEMM (see file header). a_codes [M, K/2], b_codes
+// [N, K/2] (row-major, K-major), scales in the swizzled layout produced by
+// rc_nvfp4_quantize. epilogue: 0 bias, 1 gated residual (out += y * gate),
+// 2 residual (out += y), 3 GELU + NVFP4 requantize into q_codes/q_scales.
+int rc_nvfp4_gemm(const uint8_t* a_codes, const uint8_t* a_scales, const uint8_t* b_codes,
+                  const uint8_t* b_scales, const void* bias, int M, int N, int K, float alpha,
+                  int epilogue, void* out, long long ldo, const float* gate, uint8_t* q_codes,
+                  uint8_t* q_scales, float q_global_scale, cudaStream_t stream) {
+  if (!a_scales || !b_scales) return rc::set_error(RC_ERR_ARG, "rc_nvfp4_gemm: null scales");
+  if (reinterpret_cast<uintptr_t>(a_scales) % 16 || reinterpret_cast<uintptr_t>(b_scales) % 16)
+    return rc::set_error(RC_ERR_ARG, "rc_nvfp4_gemm: scale buffers must be 16-byte aligned");
+  GemmParams p{};
+  p.sfa = a_scales;
+  p.sfb = b_scales;
+  p.alpha = alpha;
+  p.bias = reinterpret_cast<const __nv_bfloat16*>(bias);
+  p.out = reinterpret_cast<__nv_bfloat16*>(out);
+  p.ldo = ldo;
+  p.gate = gate;
+  p.q_codes = q_codes;
+  p.q_sf = q_scales;
+  p.q_g = q_global_scale;
+  return run_gemm(KIND_NVF4, epilogue, a_codes, b_codes, M, N, K, p, stream, "rc_nvfp4_gemm");
+}
+
+// Per-tensor FP8 (E4M3) GEMM: alpha * scale_a * scale_b * A.B^T + bias.
+int rc_fp8_gemm(const uint8_t* a, const float* scale_a, const uint8_t* b, const float* scale_b,
+                const void* bias, int M, int N, int K, float alpha, int epilogue, void* out,
+                long long ldo, const float* gate, cudaStream_t stream) {
+  GemmParams p{};
+  p.alpha = alpha;
+  p.alpha_ptr_a = scale_a;
+  p.alpha_ptr_b = scale_b;
+  p.bias = reinterpret_cast<const __nv_bfloat16*>(bias);
+  p.out = reinterpret_cast<__nv_bfloat16*>(out);
+  p.ldo = ldo;
+  p.gate = gate;
+  if (epilogue == EPI_GELU_NVF4) return rc::set_error(RC_ERR_ARG, "rc_fp8_gemm: GELU/NVFP4 epilogue is NVFP4-only");
+  return run_gemm(KIND_E4M3, epilogue, a, b, M, N, K, p, stream, "rc_fp8_gemm");
+}
+
+// bf16 GEMM with the same epilogues (plain nn.Linear path).
+int rc_bf16_gemm(const void* a, const void* b, const void* bias, int M, int N, int K, int epilogue,
+                 void* out, long long ldo, const float* gate, cudaStream_t stream) {
+  GemmParams p{};
+  p.alpha = 1.0f;
+  p.bias = reinterpret_cast<const __nv_bfloat16*>(bias);
+  p.out = reinterpret_cast<__nv_bfloat16*>(out);
+  p.ldo = ldo;
+  p.gate = gate;
+  if (epilogue == EPI_GELU_NVF4) return rc::set_error(RC_ERR_ARG, "rc_bf16_gemm: GELU/NVFP4 epilogue is NVFP4-only");
+  return run_gemm(KIND_BF16, epilogue, a, b, M, N, K, p, stream, "rc_bf16_gemm");
+}
+
+}  // extern "C"

@@ -1,0 +1,400 @@
+// Row-wise glue around the DiT linears: LayerNorm (+affine) (+AdaLN
+// modulation) with an optional fused NVFP4 quantizer, RMSNorm across heads
+// with the spatial rotary embedding, the temporal rotary embedding, and the
+// KV-cache plane commit. One warp per row; the row stays in registers as raw
+// bf16 (N <= 4096), so each input byte is read from HBM once.
+//
+// Numerics follow recavsr_infer/runtime/transformer.py:88-133 in eager order:
+//   LN in fp32 (two-pass mean / variance, rsqrt(var + eps)), then
+//   y * (1 + scale) + shift as separate fp32 roundings, then bf16;
+//   RMSNorm: bf16(x * rsqrt(mean(x^2) + eps) * w) with one rounding;
+//   rotary: (e*c - o*s, e*s + o*c) in fp32, then bf16 (runtime/rope.py:23-30).
+#include "common.cuh"
+
+namespace {
+
+constexpr int kMaxChunks = 16;  // uint4 (8 x bf16) per lane -> N <= 4096
+
+__device__ __forceinline__ void unpack8(const uint4& v, float (&f)[8]) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    f[2 * j] = __uint_as_float(w[j] << 16);
+    f[2 * j + 1] = __uint_as_float(w[j] & 0xffff0000u);
+  }
+}
+__device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
+  uint32_t w[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+    w[j] = (uint32_t)rc::bf16_bits(f[2 * j]) | ((uint32_t)rc::bf16_bits(f[2 * j + 1]) << 16);
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+struct LnArgs {
+  const __nv_bfloat16* x; long long ldx;
+  const __nv_bfloat16* weight; const __nv_bfloat16* bias;   // affine (nullable)
+  const float* shift; const float* scale;                    // modulation (nullable)
+  float eps;
+  __nv_bfloat16* out; long long ldo;                         // bf16 output (nullable)
+  uint8_t* codes; uint8_t* sf; float g;                      // NVFP4 output (nullable)
+  int M, N;
+};
+
+__global__ void __launch_bounds__(256) ln_modulate_kernel(LnArgs a) {
+  const int lane = threadIdx.x & 31;
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= a.M) return;
+  const int nch = a.N >> 3;
+  const uint4* src = reinterpret_cast<const uint4*>(a.x + (size_t)row * a.ldx);
+  uint4 raw[kMaxChunks];
+#pragma unroll
+  for (int i = 0; i < kMaxChunks; ++i) {
+    const int c = lane + 32 * i;
+    raw[i] = c < nch ? __ldg(src + c) : make_uint4(0, 0, 0, 0);
+  }
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < kMaxChunks; ++i) {
+    float f[8];
+    unpack8(raw[i], f);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) s += f[j];
+  }
+  const float mean = __fdiv_rn(warp_sum(s), (float)a.N);
+  float m2 = 0.f;
+#pragma unroll
+  for (int i = 0; i < kMaxChunks; ++i) {
+    if (lane + 32 * i < nch) {
+      float f[8];
+      unpack8(raw[i], f);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float d = f[j] - mean;
+        m2 = fmaf(d, d, m2);
+      }
+    }
+  }
+  const float var = __fdiv_rn(warp_sum(m2), (float)a.N);
+  const float rstd = rsqrtf(var + a.eps);
+  const int katoms = ((a.N >> 4) + 3) >> 2;
+#pragma unroll
+  for (int i = 0; i < kMaxChunks; ++i) {
+    const int c = lane + 32 * i;
+    if (32 * i >= nch) break;                 // warp-uniform
+    const bool live = c < nch;
+    float f[8];
+    unpack8(raw[i], f);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int n = c * 8 + j;
+      float y = __fmul_rn(f[j] - mean, rstd);
+      if (live) {
+        if (a.weight) y = __fmul_rn(y, __bfloat162float(a.weight[n]));
+        if (a.bias) y = __fadd_rn(y, __bfloat162float(a.bias[n]));
+        if (a.scale) y = __fmul_rn(y, __fadd_rn(1.0f, a.scale[n]));
+        if (a.shift) y = __fadd_rn(y, a.shift[n]);
+      }
+      f[j] = rc::bf16_to_float(rc::bf16_bits(y));  // bf16 rounding of the block output
+    }
+    if (live && a.out)
+      *reinterpret_cast<uint4*>(a.out + (size_t)row * a.ldo + (size_t)c * 8) = pack8(f);
+    if (a.codes) {
+      // 16-element quant block = chunks (2b, 2b+1) = lanes (2b', 2b'+1) of this pass.
+      float amax = 0.f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(f[j]));
+      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+      float sc = __fmul_rn(__fdiv_rn(amax, 6.0f), a.g);
+      sc = sc < 0.001953125f ? 0.001953125f : sc;
+      const uint8_t sfb = rc::e4m3_from_float(sc);
+      const float sd = rc::e4m3_to_float(sfb);
+      uint32_t word = 0;
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        word |= rc::e2m1_code(__fdiv_rn(__fmul_rn(f[j], a.g), sd)) << (4 * j);
+      if (live) *reinterpret_cast<uint32_t*>(a.codes + (size_t)row * (a.N >> 1) + (size_t)c * 4) = word;
+      // Gather the 4 scale bytes of a k-atom (lanes 8g, 8g+2, 8g+4, 8g+6).
+      const uint32_t b0 = sfb;
+      const uint32_t b1 = __shfl_down_sync(0xffffffffu, b0, 2);
+      const uint32_t b2 = __shfl_down_sync(0xffffffffu, b0, 4);
+      const uint32_t b3 = __shfl_down_sync(0xffffffffu, b0, 6);
+      if (live && (lane & 7) == 0) {
+        const int kb = c >> 1;  // first of 4 blocks
+        const size_t off = rc::sf_offset(row, kb, katoms);
+        // Blocks beyond N/16 inside the last atom are zero padding.
+        const int nkb = a.N >> 4;
+        uint32_t w = b0 | ((kb + 1 < nkb ? b1 : 0u) << 8) | ((kb + 2 < nkb ? b2 : 0u) << 16) |
+                     ((kb + 3 < nkb ? b3 : 0u) << 24);
+        *reinterpret_cast<uint32_t*>(a.sf + off) = w;
+      }
+    }
+  }
+}
+
+// Zero the scale bytes of padding rows [M, ceil(M/128)*128) and the padding
+// k-blocks of the last atom for all rows (the quantizer writes full words for
+// real rows, so only the tail rows need this).
+__global__ void sf_pad_rows_kernel(uint8_t* sf, int M, int katoms) {
+  const int pm = (M + 127) / 128 * 128;
+  const long long total = (long long)(pm - M) * katoms;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int row = M + (int)(i / katoms), kt = (int)(i % katoms);
+    *reinterpret_cast<uint32_t*>(sf + rc::sf_offset(row, kt * 4, katoms)) = 0u;
+  }
+}
+
+struct RmsArgs {
+  const __nv_bfloat16* x[2]; long long ldx[2];
+  const __nv_bfloat16* w[2];
+  __nv_bfloat16* out[2]; long long ldo[2];
+  const float* cos; const float* sin;  // [span, d] spatial tables (nullable -> no rotary)
+  float eps;
+  int M, N, d, span;
+};
+
+__global__ void __launch_bounds__(256) rmsnorm_rope_kernel(RmsArgs a) {
+  const int lane = threadIdx.x & 31;
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int t = blockIdx.y;
+  if (row >= a.M) return;
+  const int nch = a.N >> 3;
+  const uint4* src = reinterpret_cast<const uint4*>(a.x[t] + (size_t)row * a.ldx[t]);
+  uint4 raw[kMaxChunks];
+#pragma unroll
+  for (int i = 0; i < kMaxChunks; ++i) {
+    const int c = lane + 32 * i;
+    raw[i] = c < nch ? __ldg(src + c) : make_uint4(0, 0, 0, 0);
+  }
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < kMaxChunks; ++i) {
+    float f[8];
+    unpack8(raw[i], f);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) ss = fmaf(f[j], f[j], ss);
+  }
+  const float r = rsqrtf(__fdiv_rn(warp_sum(ss), (float)a.N) + a.eps);
+  const int pos = row % a.span;
+  const __nv_bfloat16* w = a.w[t];
+#pragma unroll
+  for (int i = 0; i < kMaxChunks; ++i) {
+    const int c = lane + 32 * i;
+    if (c >= nch) break;
+    float f[8];
+    unpack8(raw[i], f);
+    float wf[8];
+    if (w) unpack8(__ldg(reinterpret_cast<const uint4*>(w) + c), wf);
+    if (w) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) f[j] = rc::bf16_to_float(rc::bf16_bits(__fmul_rn(__fmul_rn(f[j], r), wf[j])));
+    }
+    if (a.cos) {
+      const int dd = (c * 8) % a.d;  // 8 | d, so a chunk never straddles heads
+      const float* cp = a.cos + (size_t)pos * a.d + dd;
+      const float* sp = a.sin + (size_t)pos * a.d + dd;
+#pragma unroll
+      for (int j = 0; j < 8; j += 2) {
+        const float cc = __ldg(cp + j), sn = __ldg(sp + j);
+        const float e = f[j], o = f[j + 1];
+        f[j] = __fsub_rn(__fmul_rn(e, cc), __fmul_rn(o, sn));
+        f[j + 1] = __fadd_rn(__fmul_rn(e, sn), __fmul_rn(o, cc));
+      }
+    }
+    *reinterpret_cast<uint4*>(a.out[t] + (size_t)row * a.ldo[t] + (size_t)c * 8) = pack8(f);
+  }
+}
+
+// Temporal rotary on the first `td` dims of every head of `planes` planes of
+// `span` tokens; plane p uses position pos[p] (runtime/rope.py:33-47).
+__global__ void temporal_rope_kernel(const __nv_bfloat16* __restrict__ x, long long ldx,
+                                     __nv_bfloat16* __restrict__ out, long long ldo,
+                                     const int* __restrict__ pos, const float* __restrict__ cos,
+                                     const float* __restrict__ sin, int rows, int span, int heads,
+                                     int d, int td) {
+  const long long pairs_per_row = (long long)heads * (d / 2);
+  const long long total = (long long)rows * pairs_per_row;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const long long row = i / pairs_per_row;
+    const int rem = (int)(i % pairs_per_row);
+    const int h = rem / (d / 2), pr = rem % (d / 2);
+    const __nv_bfloat162 v =
+        *reinterpret_cast<const __nv_bfloat162*>(x + row * ldx + (long long)h * d + 2 * pr);
+    float e = __low2float(v), o = __high2float(v);
+    if (2 * pr < td) {
+      const int p = pos[row / span];
+      const float c = cos[p * (td / 2) + pr], s = sin[p * (td / 2) + pr];
+      const float ne = __fsub_rn(__fmul_rn(e, c), __fmul_rn(o, s));
+      const float no = __fadd_rn(__fmul_rn(e, s), __fmul_rn(o, c));
+      e = ne;
+      o = no;
+    }
+    *reinterpret_cast<__nv_bfloat162*>(out + row * ldo + (long long)h * d + 2 * pr) =
+        __floats2bfloat162_rn(e, o);
+  }
+}
+
+// KV commit: copy `n` planes of `span` rows (`row_bytes` each) for K and V.
+struct CommitArgs {
+  const uint8_t* src[2]; long long src_ld[2];
+  uint8_t* dst[2]; long long dst_ld[2];
+  int src_plane[8]; int dst_plane[8];
+  int n, span, row_bytes;
+};
+
+__global__ void kv_commit_kernel(CommitArgs a) {
+  const int vec_per_row = a.row_bytes >> 4;
+  const long long per_plane = (long long)a.span * vec_per_row;
+  const long long total = 2LL * a.n * per_plane;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int t = (int)(i / (a.n * per_plane));
+    const long long r = i % (a.n * per_plane);
+    const int c = (int)(r / per_plane);
+    const long long q = r % per_plane;
+    const long long row = q / vec_per_row, v = q % vec_per_row;
+    const uint4* s = reinterpret_cast<const uint4*>(
+        a.src[t] + ((long long)a.src_plane[c] * a.span + row) * a.src_ld[t]);
+    uint4* dd = reinterpret_cast<uint4*>(
+        a.dst[t] + ((long long)a.dst_plane[c] * a.span + row) * a.dst_ld[t]);
+    dd[v] = __ldg(s + v);
+  }
+}
+
+int grid_for(long long work, int threads) {
+  long long b = (work + threads - 1) / threads;
+  return (int)(b < 1 ? 1 : (b > 148LL * 16 ? 148LL * 16 : b));
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+}  // namespace
+
+RC_DEVICE_ERROR_ACCESSOR(glue)
+
+extern "C" {
+
+// LayerNorm over the last dim N of x [M, N] (fp32 math), optional affine
+// weight/bias (bf16), optional AdaLN modulation y*(1+scale)+shift (fp32 [N]),
+// rounded to bf16 into `out` (nullable) and/or NVFP4-quantized into
+// codes [M, N/2] + swizzled scales (nullable) with global scale g.
+int rc_ln_modulate_quant(const void* x, long long ldx, int M, int N, const void* weight,
+                         const void* bias, const float* shift, const float* scale, float eps,
+                         void* out, long long ldo, uint8_t* codes, uint8_t* scales_swizzled,
+                         float global_scale, cudaStream_t stream) {
+  if (M < 0 || N <= 0 || N % 64 || N > 32 * 8 * kMaxChunks)
+    return rc::set_error(RC_ERR_ARG, "rc_ln_modulate_quant: N must be a multiple of 64 and <= 4096 (N=%d)", N);
+  if (!x || (!out && !codes) || (codes && !scales_swizzled))
+    return rc::set_error(RC_ERR_ARG, "rc_ln_modulate_quant: missing pointer");
+  if (!aligned16(x) || ldx % 8 || (out && (!aligned16(out) || ldo % 8)) ||
+      (codes && (reinterpret_cast<uintptr_t>(codes) % 4 || reinterpret_cast<uintptr_t>(scales_swizzled) % 4)))
+    return rc::set_error(RC_ERR_ARG, "rc_ln_modulate_quant: rows must be 16-byte aligned");
+  if (!(global_scale > 0.f)) return rc::set_error(RC_ERR_ARG, "rc_ln_modulate_quant: bad global scale");
+  if (M == 0) return RC_OK;
+  LnArgs a{reinterpret_cast<const __nv_bfloat16*>(x), ldx,
+           reinterpret_cast<const __nv_bfloat16*>(weight), reinterpret_cast<const __nv_bfloat16*>(bias),
+           shift, scale, eps, reinterpret_cast<__nv_bfloat16*>(out), ldo, codes, scales_swizzled,
+           global_scale, M, N};
+  ln_modulate_kernel<<<(M + 7) / 8, 256, 0, stream>>>(a);
+  int r = rc::check_launch("rc_ln_modulate_quant");
+  if (r || !codes) return r;
+  const int katoms = ((N >> 4) + 3) >> 2;
+  if (M % 128) {
+    sf_pad_rows_kernel<<<grid_for((long long)(128 - M % 128) * katoms, 256), 256, 0, stream>>>(
+        scales_swizzled, M, katoms);
+    r = rc::check_launch("rc_ln_modulate_quant(pad)");
+  }
+  return r;
+}
+
+// RMSNorm across the full row (eps, affine bf16 weight) of up to two tensors
+// (n_tensors = 1 or 2, e.g. q and k), optionally followed by the interleaved
+// rotary embedding with per-token tables cos/sin [span, d] (token = row % span).
+// A null weight skips the norm (rotary only).
+int rc_rmsnorm_rope(int n_tensors, const void* const* xs, const long long* ldx,
+                    const void* const* weights, void* const* outs, const long long* ldo, int M,
+                    int N, int d, int span, const float* cos, const float* sin, float eps,
+                    cudaStream_t stream) {
+  if (n_tensors < 1 || n_tensors > 2 || M < 0 || N <= 0 || N % 8 || N > 32 * 8 * kMaxChunks ||
+      d <= 0 || d % 8 || N % d || span <= 0)
+    return rc::set_error(RC_ERR_ARG, "rc_rmsnorm_rope: bad shape (N=%d d=%d span=%d)", N, d, span);
+  RmsArgs a{};
+  for (int t = 0; t < n_tensors; ++t) {
+    if (!xs[t] || !outs[t] || !aligned16(xs[t]) || !aligned16(outs[t]) ||
+        (weights[t] && !aligned16(weights[t])) || ldx[t] % 8 || ldo[t] % 8)
+      return rc::set_error(RC_ERR_ARG, "rc_rmsnorm_rope: tensor %d must be 16-byte aligned", t);
+    a.x[t] = reinterpret_cast<const __nv_bfloat16*>(xs[t]);
+    a.ldx[t] = ldx[t];
+    a.w[t] = reinterpret_cast<const __nv_bfloat16*>(weights[t]);  // null: rotary only
+    a.out[t] = reinterpret_cast<__nv_bfloat16*>(outs[t]);
+    a.ldo[t] = ldo[t];
+  }
+  if ((cos == nullptr) != (sin == nullptr))
+    return rc::set_error(RC_ERR_ARG, "rc_rmsnorm_rope: cos and sin go together");
+  a.cos = cos;
+  a.sin = sin;
+  a.eps = eps;
+  a.M = M;
+  a.N = N;
+  a.d = d;
+  a.span = span;
+  if (M == 0) return RC_OK;
+  dim3 grid((M + 7) / 8, n_tensors);
+  rmsnorm_rope_kernel<<<grid, 256, 0, stream>>>(a);
+  return rc::check_launch("rc_rmsnorm_rope");
+}
+
+int rc_temporal_rope(const void* x, long long ldx, void* out, long long ldo, const int* positions,
+                     const float* cos, const float* sin, int rows, int span, int heads, int d,
+                     int td, cudaStream_t stream) {
+  if (rows < 0 || span <= 0 || rows % span || heads <= 0 || d <= 0 || d % 2 || td % 2 || td > d ||
+      ldx < heads * d || ldo < heads * d)
+    return rc::set_error(RC_ERR_ARG, "rc_temporal_rope: bad shape");
+  if (rows == 0) return RC_OK;
+  if (reinterpret_cast<uintptr_t>(x) % 4 || reinterpret_cast<uintptr_t>(out) % 4 || ldx % 2 || ldo % 2)
+    return rc::set_error(RC_ERR_ARG, "rc_temporal_rope: rows must be 4-byte aligned");
+  temporal_rope_kernel<<<grid_for((long long)rows * heads * (d / 2), 256), 256, 0, stream>>>(
+      reinterpret_cast<const __nv_bfloat16*>(x), ldx, reinterpret_cast<__nv_bfloat16*>(out), ldo,
+      positions, cos, sin, rows, span, heads, d, td);
+  return rc::check_launch("rc_temporal_rope");
+}
+
+// Copy n_planes retained planes of `span` rows from the block's K/V
+// (src plane index = frame offset in the block) into cache slots.
+int rc_kv_commit(const void* src_k, const void* src_v, long long src_ld_bytes, void* dst_k,
+                 void* dst_v, long long dst_ld_bytes, int row_bytes, int span, int n_planes,
+                 const int* src_planes, const int* dst_slots, cudaStream_t stream) {
+  if (n_planes < 0 || n_planes > 8 || span <= 0 || row_bytes <= 0 || row_bytes % 16)
+    return rc::set_error(RC_ERR_ARG, "rc_kv_commit: bad shape (planes=%d row_bytes=%d)", n_planes, row_bytes);
+  if (n_planes == 0) return RC_OK;
+  if (!aligned16(src_k) || !aligned16(src_v) || !aligned16(dst_k) || !aligned16(dst_v) ||
+      src_ld_bytes % 16 || dst_ld_bytes % 16)
+    return rc::set_error(RC_ERR_ARG, "rc_kv_commit: rows must be 16-byte aligned");
+  CommitArgs a{};
+  a.src[0] = reinterpret_cast<const uint8_t*>(src_k);
+  a.src[1] = reinterpret_cast<const uint8_t*>(src_v);
+  a.dst[0] = reinterpret_cast<uint8_t*>(dst_k);
+  a.dst[1] = reinterpret_cast<uint8_t*>(dst_v);
+  a.src_ld[0] = a.src_ld[1] = src_ld_bytes;
+  a.dst_ld[0] = a.dst_ld[1] = dst_ld_bytes;
+  for (int i = 0; i < n_planes; ++i) {
+    if (src_planes[i] < 0 || dst_slots[i] < 0)
+      return rc::set_error(RC_ERR_ARG, "rc_kv_commit: negative plane index");
+    a.src_plane[i] = src_planes[i];
+    a.dst_plane[i] = dst_slots[i];
+  }
+  a.n = n_planes;
+  a.span = span;
+  a.row_bytes = row_bytes;
+  kv_commit_kernel<<<grid_for(2LL * n_planes * span * (row_bytes / 16), 256), 256, 0, stream>>>(a);
+  return rc::check_launch("rc_kv_commit");
+}
+
+}  // extern "C"

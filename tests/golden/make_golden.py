@@ -1,0 +1,359 @@
+"""Generate the golden fixtures of tests/golden/ by running the REFERENCE itself.
+
+Run in a container that has the reference checkout (default /root/reference,
+override with RECAVSR_REFERENCE):  python tests/golden/make_golden.py
+
+The reference is imported with two import shims and no other change:
+* ``diffusers.models.embeddings.get_1d_rotary_pos_embed`` (diffusers 0.37.1 is
+  not installed): the standard rotary table -- theta 10000, float64
+  frequencies theta^(-2i/dim), cos/sin of pos*freq with every pair frequency
+  repeated twice, cast to float32.
+* ``recavsr_infer.weights`` (imports the diffusers model): a stub, since only
+  ``PreparedBlock`` is needed from runtime/transformer.py.
+Nothing here is shipped: it records what the reference computes so that the
+oracle (oracle/) can be checked against it on any machine.
+"""
+from __future__ import annotations
+
+import json
+import os
+import sys
+import types
+
+import numpy as np
+import torch
+from torch import nn
+from torch.nn import functional as F
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+REPO = os.path.dirname(os.path.dirname(HERE))
+sys.path.insert(0, REPO)
+from tests.golden import recipes  # noqa: E402
+
+
+def _install_shims(ref_root: str):
+    def get_1d_rotary_pos_embed(dim, pos, theta=10000.0, use_real=False, linear_factor=1.0,
+                                ntk_factor=1.0, repeat_interleave_real=True,
+                                freqs_dtype=torch.float32):
+        if isinstance(pos, int):
+            pos = torch.arange(pos)
+        freqs = 1.0 / (theta ** (torch.arange(0, dim, 2, dtype=freqs_dtype)[: dim // 2] / dim))
+        freqs = torch.outer(pos, freqs)
+        return (freqs.cos().repeat_interleave(2, dim=1).float(),
+                freqs.sin().repeat_interleave(2, dim=1).float())
+
+    for name in ("diffusers", "diffusers.models", "diffusers.models.embeddings"):
+        sys.modules.setdefault(name, types.ModuleType(name))
+    sys.modules["diffusers.models.embeddings"].get_1d_rotary_pos_embed = get_1d_rotary_pos_embed
+    sys.path.insert(0, ref_root)
+    import recavsr_infer  # noqa: F401
+    stub = types.ModuleType("recavsr_infer.weights")
+    stub.load_block = lambda *a, **k: None
+    sys.modules["recavsr_infer.weights"] = stub
+
+
+def t16(a: np.ndarray) -> torch.Tensor:
+    return torch.from_numpy(np.ascontiguousarray(a, np.float32)).bfloat16()
+
+
+def bits(t: torch.Tensor) -> np.ndarray:
+    return t.contiguous().view(torch.int16).numpy().view(np.uint16).copy()
+
+
+# --------------------------------------------------------------------- NVFP4
+def gen_quant(out):
+    from recavsr_infer.runtime import nvfp4
+    cases = {
+        "special": recipes.quant_special_rows(64),
+        "ragged": recipes.bf16_normal(np.random.RandomState(5), (130, 96)),
+        "weights": recipes.cfg3_weight(192, 320, seed=6),
+        "cfg3_small": recipes.cfg3_activation(300, 512, seed=2),
+    }
+    for name, x in cases.items():
+        packed, scales = nvfp4.quantize(t16(x))
+        out[f"quant_{name}_x"] = bits(t16(x))
+        out[f"quant_{name}_codes"] = packed.numpy()
+        out[f"quant_{name}_scales"] = scales.numpy()
+
+
+def gen_fp8(out):
+    from recavsr_infer.runtime import fp8
+    captured = {}
+
+    def fake_scaled_mm(a, b, scale_a, scale_b, bias, out_dtype, use_fast_accum):
+        captured["q"], captured["scale"] = a, scale_a
+        return torch.zeros(a.shape[0], b.shape[1], dtype=out_dtype)
+
+    layer = object.__new__(fp8.FP8Linear)
+    nn.Module.__init__(layer)
+    layer.in_features, layer.out_features = 96, 32
+    layer.weight_packed = torch.zeros(32, 96, dtype=torch.float8_e4m3fn).view(torch.bfloat16)
+    layer.bias = None
+    layer.weight_scale = torch.tensor(1.0)
+    real = torch._scaled_mm
+    torch._scaled_mm = fake_scaled_mm
+    try:
+        for name, x in {"act": recipes.cfg3_activation(64, 96, seed=8),
+                        "weight": recipes.cfg3_weight(48, 96, seed=9)}.items():
+            layer.forward(t16(x))
+            out[f"fp8_{name}_x"] = bits(t16(x))
+            out[f"fp8_{name}_q"] = captured["q"].view(torch.uint8).numpy().copy()
+            out[f"fp8_{name}_scale"] = np.float32(captured["scale"].item())
+    finally:
+        torch._scaled_mm = real
+
+
+# -------------------------------------------------------------------- router
+def gen_router():
+    from recavsr_infer.runtime.cache import ACTIONS, FixedKVCache
+    from recavsr_infer.runtime.rope import RollingRoPE
+    rope = RollingRoPE(128, 1, 1, device="cpu")
+    result = {}
+    for action in ACTIONS:
+        cache = FixedKVCache(action, initial=5, stride=6, anchors=2)
+        start, steps = 0, []
+        for block in range(75):
+            frames = 6 if block == 0 else 2
+            origin, qpos = rope.positions(start, frames)
+            dummy = torch.zeros(1, frames, 1, 1)
+            _, _, slots, ppos = cache.history(dummy, origin=origin)
+            key = torch.arange(start, start + frames, dtype=torch.float32).view(1, frames, 1, 1)
+            cache.commit(key, key.clone(), frames=frames, start=start)
+            content = [] if cache.key is None else [int(v) for v in cache.key.view(-1).tolist()]
+            steps.append({"start": start, "frames": frames, "origin": origin,
+                          "qpos": qpos.tolist(), "slots": slots.tolist(), "ppos": ppos.tolist(),
+                          "slot_frames": content, "frame_ids": list(cache.frame_indices)})
+            start += frames
+        result[action] = {"capacity": cache.capacity, "steps": steps}
+    return result
+
+
+# ---------------------------------------------------------------------- RoPE
+def gen_rope(out):
+    from recavsr_infer.runtime.rope import RollingRoPE, apply_rotary, apply_temporal
+    r = RollingRoPE(128, 11, 20, device="cpu")
+    out["rope_tcos"], out["rope_tsin"] = r.temporal_cos.numpy(), r.temporal_sin.numpy()
+    out["rope_scos"] = r.spatial_cos.reshape(220, 128).numpy()
+    out["rope_ssin"] = r.spatial_sin.reshape(220, 128).numpy()
+    rs = np.random.RandomState(21)
+    x = recipes.bf16_normal(rs, (1, 2 * 220, 3, 128))
+    out["rope_x"] = bits(t16(x))
+    out["rope_spatial"] = bits(r.spatial(t16(x)))
+    pos = torch.tensor([4, 17], dtype=torch.int32)
+    out["rope_temporal"] = bits(apply_temporal(t16(x), pos, r.temporal_cos, r.temporal_sin, span=220))
+    c, s = r.spatial_cos, r.spatial_sin
+    out["rope_rotary"] = bits(apply_rotary(t16(x).reshape(1, 2, 220, 3, 128), c, s))
+    for h, w in ((22, 40), (34, 60)):
+        rr = RollingRoPE(128, h, w, device="cpu")
+        out[f"rope_sum_{h}x{w}"] = np.array([rr.spatial_cos.double().sum().item(),
+                                             rr.spatial_sin.double().sum().item(),
+                                             rr.temporal_cos.double().sum().item(),
+                                             rr.temporal_sin.double().sum().item()])
+
+
+# ----------------------------------------------------------------- attention
+def gen_attention(out):
+    import triton
+    from recavsr_infer.kernels import local_attention as la
+    from recavsr_infer.runtime.rope import RollingRoPE
+    # (a) dense path: sdpa_attention in fp32 and bf16 on CPU
+    H, W, heads, d, frames, cap = 4, 6, 2, 128, 2, 3
+    span = H * W
+    rs = np.random.RandomState(31)
+    q, ck, cv = (recipes.bf16_normal(rs, (1, frames * span, heads, d)) for _ in range(3))
+    pk, pv = (recipes.bf16_normal(rs, (1, cap * span, heads, d)) for _ in range(2))
+    slots = torch.tensor([2, -1, 0], dtype=torch.int32)
+    ppos = torch.tensor([5, 0, 3], dtype=torch.int32)
+    qpos = torch.tensor([6, 7], dtype=torch.int32)
+    r = RollingRoPE(d, H, W, device="cpu")
+    for dt, tag in ((torch.float32, "f32"), (torch.bfloat16, "bf16")):
+        o = la.sdpa_attention(*(t16(a).to(dt) for a in (q, ck, cv, pk, pv)), slots, ppos, qpos,
+                              r.temporal_cos, r.temporal_sin, H, W, 22, 40)
+        out[f"attn_dense_{tag}"] = o.float().numpy()
+    for n, a in zip(("q", "ck", "cv", "pk", "pv"), (q, ck, cv, pk, pv)):
+        out[f"attn_dense_{n}"] = bits(t16(a))
+    # (b) windowed path: the reference's Triton kernel under TRITON_INTERPRET=1 (fp16 only)
+    if os.environ.get("TRITON_INTERPRET") == "1":
+        for tag, (H, W, wh, ww, d, cap, sl, pp) in {
+            "win_a": (8, 16, 4, 8, 64, 3, [2, -1, 0], [3, 0, 5]),
+            "win_b": (6, 10, 3, 5, 128, 2, [1, 0], [4, 6]),
+        }.items():
+            span = H * W
+            rs = np.random.RandomState(41 + len(tag))
+            qh = [rs.standard_normal((1, 2 * span, 2, d)).astype(np.float16) for _ in range(3)]
+            ph = [rs.standard_normal((1, cap * span, 2, d)).astype(np.float16) for _ in range(2)]
+            tq = [torch.from_numpy(a) for a in qh + ph]
+            slots = torch.tensor(sl, dtype=torch.int32)
+            ppos = torch.tensor(pp, dtype=torch.int32)
+            qpos = torch.tensor([7, 8], dtype=torch.int32)
+            r = RollingRoPE(d, H, W, device="cpu")
+            o = torch.empty_like(tq[0])
+            bh, bw, bt = 4, 8, 2
+            la._paired_local[(triton.cdiv(H, bh) * triton.cdiv(W, bw), 1, 2)](
+                *tq, slots, ppos, qpos, r.temporal_cos, r.temporal_sin, o,
+                *tq[0].stride()[:3], *tq[1].stride()[:3], *tq[2].stride()[:3],
+                *tq[3].stride()[:3], *tq[4].stride()[:3],
+                H, W, 2, cap, 2, d, r.temporal_cos.shape[1] * 2, min(H, wh), min(W, ww),
+                bh, bw, bt, bh * bw * bt, 64, min(H, min(H, wh) + bh - 1),
+                min(W, min(W, ww) + bw - 1), num_warps=4, num_stages=2)
+            out[f"attn_{tag}_out"] = o.float().numpy()
+            for n, a in zip(("q", "ck", "cv", "pk", "pv"), qh + ph):
+                out[f"attn_{tag}_{n}"] = a
+            out[f"attn_{tag}_meta"] = np.array([H, W, wh, ww, d, cap] + sl + pp, np.int64)
+
+
+# --------------------------------------------------------------------- block
+class _FP32LayerNorm(nn.LayerNorm):
+    """diffusers FP32LayerNorm: layer_norm of x.float() (affine params cast to
+    float), cast back to the input dtype."""
+
+    def forward(self, x):
+        return F.layer_norm(x.float(), self.normalized_shape,
+                            None if self.weight is None else self.weight.float(),
+                            None if self.bias is None else self.bias.float(),
+                            self.eps).to(x.dtype)
+
+
+class _Attention(nn.Module):
+    """Module layout PreparedBlock reads from WanAttention
+    (models/transformer_wan.py:515-626), unfused projections."""
+
+    def __init__(self, dim, heads, cross):
+        super().__init__()
+        self.to_q, self.to_k, self.to_v = (nn.Linear(dim, dim) for _ in range(3))
+        self.to_out = nn.ModuleList([nn.Linear(dim, dim), nn.Dropout(0.0)])
+        self.norm_q = nn.RMSNorm(dim, eps=1e-6)
+        self.norm_k = nn.RMSNorm(dim, eps=1e-6)
+        self.heads, self.fused_projections, self.is_cross_attention = heads, False, cross
+
+    def precompute_cross_attention_kv(self, enc):
+        key = self.norm_k(self.to_k(enc)).unflatten(2, (self.heads, -1))
+        return key, self.to_v(enc).unflatten(2, (self.heads, -1))
+
+
+class _GeluProj(nn.Module):
+    def __init__(self, dim, inner):
+        super().__init__()
+        self.proj = nn.Linear(dim, inner)
+
+    def forward(self, x):
+        return F.gelu(self.proj(x), approximate="tanh")
+
+
+class _FeedForward(nn.Module):
+    def __init__(self, dim, inner):
+        super().__init__()
+        self.net = nn.ModuleList([_GeluProj(dim, inner), nn.Dropout(0.0), nn.Linear(inner, dim)])
+
+    def forward(self, x):
+        for m in self.net:
+            x = m(x)
+        return x
+
+
+class _Block(nn.Module):
+    def __init__(self, dim, heads, ffn):
+        super().__init__()
+        self.norm1 = _FP32LayerNorm(dim, 1e-6, elementwise_affine=False)
+        self.attn1 = _Attention(dim, heads, False)
+        self.attn2 = _Attention(dim, heads, True)
+        self.norm2 = _FP32LayerNorm(dim, 1e-6, elementwise_affine=True)
+        self.ffn = _FeedForward(dim, ffn)
+        self.norm3 = _FP32LayerNorm(dim, 1e-6, elementwise_affine=False)
+        self.scale_shift_table = nn.Parameter(torch.zeros(1, 6, dim))
+
+
+class _QuantLinear(nn.Module):
+    """NVFP4Linear with the GEMM replaced by its defining math: the reference's
+    own quantize() of activations and weights, dequantized, fp32 matmul + bias,
+    bf16 out (the GEMM oracle BASELINE states)."""
+
+    LUT = torch.tensor([0, .5, 1, 1.5, 2, 3, 4, 6, -0., -.5, -1, -1.5, -2, -3, -4, -6])
+
+    def __init__(self, linear):
+        super().__init__()
+        from recavsr_infer.runtime import nvfp4
+        self.q = nvfp4.quantize
+        self.n, self.k = linear.out_features, linear.in_features
+        self.w = self.deq(*self.q(linear.weight.detach()), self.n, self.k)
+        self.bias = linear.bias
+
+    def deq(self, packed, flat, m, k):
+        codes = torch.stack((packed & 15, packed >> 4), -1).reshape(m, k).long()
+        pm, pk = (m + 127) // 128 * 128, ((k // 16 + 3) // 4) * 4
+        sc = flat.reshape(pm // 128, pk // 4, 32, 4, 4).permute(0, 3, 2, 1, 4).reshape(pm, pk)
+        sc = sc[:m, : k // 16].contiguous().view(torch.float8_e4m3fn).float()
+        return (self.LUT[codes].reshape(m, k // 16, 16) * sc[..., None]).reshape(m, k)
+
+    def forward(self, x):
+        a = x.reshape(-1, self.k)
+        acc = self.deq(*self.q(a), a.shape[0], self.k).double() @ self.w.double().T
+        if self.bias is not None:
+            acc = acc + self.bias.double()
+        return acc.float().to(torch.bfloat16).reshape(*x.shape[:-1], self.n)
+
+
+def gen_block(out):
+    from recavsr_infer.runtime.rope import RollingRoPE
+    from recavsr_infer.runtime.transformer import PreparedBlock
+    dim, heads, ffn, H, W = 256, 2, 512, 4, 6
+    span = H * W
+    p = recipes.block_params(dim, heads, ffn)
+    b = _Block(dim, heads, ffn)
+    with torch.no_grad():
+        names = {"q": b.attn1.to_q, "k": b.attn1.to_k, "v": b.attn1.to_v, "o": b.attn1.to_out[0],
+                 "cq": b.attn2.to_q, "ck": b.attn2.to_k, "cv": b.attn2.to_v, "co": b.attn2.to_out[0],
+                 "up": b.ffn.net[0].proj, "down": b.ffn.net[2]}
+        for n, lin in names.items():
+            lin.weight.copy_(torch.from_numpy(p[n + "_w"]))
+            lin.bias.copy_(torch.from_numpy(p[n + "_b"]))
+        b.attn1.norm_q.weight.copy_(torch.from_numpy(p["norm_q"]))
+        b.attn1.norm_k.weight.copy_(torch.from_numpy(p["norm_k"]))
+        b.attn2.norm_q.weight.copy_(torch.from_numpy(p["cnorm_q"]))
+        b.attn2.norm_k.weight.copy_(torch.from_numpy(p["cnorm_k"]))
+        b.norm2.weight.copy_(torch.from_numpy(p["norm2_w"]))
+        b.norm2.bias.copy_(torch.from_numpy(p["norm2_b"]))
+        b.scale_shift_table.copy_(torch.from_numpy(p["scale_shift_table"]))
+    b = b.to(torch.bfloat16)
+    cond = types.SimpleNamespace(timestep_proj=t16(p["timestep_proj"]),
+                                 encoder_hidden_states=t16(p["encoder"]))
+    rope = RollingRoPE(dim // heads, H, W, device="cpu")
+    core = PreparedBlock(b, cond, rope, window=(22, 40)).eval()
+    for mod in list(b.modules()):          # quantize_block_linears order (transformer.py:217-224)
+        for name, child in list(mod.named_children()):
+            if isinstance(child, nn.Linear):
+                setattr(mod, name, _QuantLinear(child))
+    cap = 3
+    hidden, pk, pv = recipes.block_inputs(2 * span, cap * span, dim)
+    slots = torch.tensor([1, -1, 2], dtype=torch.int32)
+    ppos = torch.tensor([4, 0, 5], dtype=torch.int32)
+    qpos = torch.tensor([6, 7], dtype=torch.int32)
+    with torch.inference_mode():
+        h, k, v = core(t16(hidden), t16(pk).unflatten(2, (heads, -1)),
+                       t16(pv).unflatten(2, (heads, -1)), slots, ppos, qpos)
+    out["block_hidden"] = bits(h)
+    out["block_k"] = bits(k)
+    out["block_v"] = bits(v)
+    out["block_modulation"] = core.modulation.detach().float().numpy()
+    out["block_cross_k"] = bits(core.cross_k.detach())
+    out["block_cross_v"] = bits(core.cross_v.detach())
+    out["block_meta"] = np.array([dim, heads, ffn, H, W, cap], np.int64)
+
+
+def main():
+    _install_shims(os.environ.get("RECAVSR_REFERENCE", "/root/reference"))
+    torch.manual_seed(0)
+    out = {}
+    gen_quant(out)
+    gen_fp8(out)
+    gen_rope(out)
+    gen_attention(out)
+    gen_block(out)
+    np.savez_compressed(os.path.join(HERE, "reference_outputs.npz"), **out)
+    with open(os.path.join(HERE, "router.json"), "w") as f:
+        json.dump(gen_router(), f, separators=(",", ":"))
+    print("wrote", len(out), "arrays")
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,87 @@
+"""Seeded input recipes shared by the golden generator and the tests.
+
+Inputs are drawn with numpy's legacy ``RandomState`` (its streams are stable
+across numpy versions) and rounded to bf16, so fixtures only need to store the
+reference's outputs; the tests regenerate the inputs bit for bit.
+"""
+from __future__ import annotations
+
+import numpy as np
+
+from oracle.numerics import bf16_round
+
+
+def bf16_normal(rs: np.random.RandomState, shape, std=1.0) -> np.ndarray:
+    return bf16_round(rs.standard_normal(shape).astype(np.float32) * np.float32(std))
+
+
+def cfg3_activation(m: int, k: int, seed: int = 2) -> np.ndarray:
+    """N(0,1) with 0.1% of entries (chosen with the seed) multiplied by 20."""
+    rs = np.random.RandomState(seed)
+    x = rs.standard_normal((m, k)).astype(np.float32)
+    idx = rs.choice(m * k, size=max(1, (m * k) // 1000), replace=False)
+    x.reshape(-1)[idx] *= 20.0
+    return bf16_round(x)
+
+
+def cfg3_weight(n: int, k: int, seed: int = 3) -> np.ndarray:
+    rs = np.random.RandomState(seed)
+    return bf16_normal(rs, (n, k), 0.02)
+
+
+def quant_special_rows(k: int = 64) -> np.ndarray:
+    """Rows that exercise every branch of the NVFP4 quantizer: zeros, signed
+    zeros, exact E2M1 thresholds and midpoints, tiny negatives (code 8),
+    subnormal and clamped scales, scales that round to 448 and to the NaN code."""
+    rows = []
+    z = np.zeros(k, np.float32)
+    rows.append(z.copy())
+    nz = z.copy(); nz[::2] = -0.0; rows.append(nz)
+    # amax = 6 -> scale 1 -> z = x exactly: every threshold and its neighbours
+    base = np.array([6.0, 0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5.0,
+                     -0.25, -0.75, -1.25, -1.75, -2.5, -3.5, -5.0, -6.0], np.float32)
+    nxt = np.nextafter(base, np.float32(np.inf)).astype(np.float32)
+    prv = np.nextafter(base, np.float32(-np.inf)).astype(np.float32)
+    for arr in (base, nxt, prv):
+        r = np.tile(arr, k // 16).astype(np.float32)
+        r[::16] = 6.0
+        rows.append(r)
+    tiny = np.full(k, -1e-5, np.float32); tiny[::16] = 1.0; rows.append(tiny)
+    rows.append(np.full(k, 1e-6, np.float32))                  # scale clamps to 2^-9
+    rows.append(np.linspace(-0.01, 0.01, k).astype(np.float32))  # subnormal scales
+    big = np.full(k, 100.0, np.float32); big[::16] = 2688.0; rows.append(big)   # scale 448
+    nan_sc = np.full(k, 1.0, np.float32); nan_sc[::16] = 2900.0; rows.append(nan_sc)  # >= 480 -> NaN code
+    mid = np.full(k, 1.0, np.float32); mid[::16] = 2784.0; rows.append(mid)    # amax/6 = 464 tie
+    rs = np.random.RandomState(7)
+    for _ in range(5):
+        rows.append(rs.standard_normal(k).astype(np.float32) * np.float32(10.0 ** rs.uniform(-3, 2)))
+    return bf16_round(np.stack(rows))
+
+
+def block_params(dim=256, heads=2, ffn=512, enc_len=16, seed=11):
+    """Weights of a stand-in DiT block with the reference's module layout
+    (models/transformer_wan.py:786-822): N(0, 0.02) linear weights, small
+    random biases, RMSNorm/LayerNorm affine around 1/0, scale_shift_table
+    randn/sqrt(dim), timestep projection N(0,1), encoder states N(0,1)."""
+    rs = np.random.RandomState(seed)
+    p = {}
+    for name, (n, k) in {"q": (dim, dim), "k": (dim, dim), "v": (dim, dim), "o": (dim, dim),
+                         "cq": (dim, dim), "ck": (dim, dim), "cv": (dim, dim), "co": (dim, dim),
+                         "up": (ffn, dim), "down": (dim, ffn)}.items():
+        p[name + "_w"] = bf16_normal(rs, (n, k), 0.02)
+        p[name + "_b"] = bf16_normal(rs, (n,), 0.02)
+    for name in ("norm_q", "norm_k", "cnorm_q", "cnorm_k", "norm2_w"):
+        p[name] = bf16_round(1.0 + 0.1 * rs.standard_normal(dim).astype(np.float32))
+    p["norm2_b"] = bf16_normal(rs, (dim,), 0.1)
+    p["scale_shift_table"] = bf16_round(rs.standard_normal((1, 6, dim)).astype(np.float32) / np.float32(dim ** 0.5))
+    p["timestep_proj"] = bf16_normal(rs, (1, 1, 6, dim))
+    p["encoder"] = bf16_normal(rs, (1, enc_len, dim))
+    return p
+
+
+def block_inputs(n_tokens, cap_tokens, dim=256, seed=12):
+    rs = np.random.RandomState(seed)
+    hidden = bf16_normal(rs, (1, n_tokens, dim))
+    pk = bf16_normal(rs, (1, cap_tokens, dim))
+    pv = bf16_normal(rs, (1, cap_tokens, dim))
+    return hidden, pk, pv

@@ -1,0 +1,140 @@
+"""Pins the CPU oracle to outputs recorded from the reference itself
+(tests/golden/make_golden.py). CPU only."""
+import numpy as np
+import pytest
+
+from oracle import attention, block, cache, fp8, nvfp4, rope
+from oracle.numerics import bf16_from_bits, bf16_round
+from tests.golden import recipes
+
+
+@pytest.mark.parametrize("case", ["special", "ragged", "weights", "cfg3_small"])
+def test_nvfp4_quantize_bit_exact(golden, case):
+    x = bf16_from_bits(golden[f"quant_{case}_x"])
+    codes, scales = nvfp4.quantize(x)
+    np.testing.assert_array_equal(codes, golden[f"quant_{case}_codes"])
+    np.testing.assert_array_equal(scales, golden[f"quant_{case}_scales"])
+
+
+def test_nvfp4_recipes_regenerate_inputs(golden):
+    x = recipes.cfg3_activation(300, 512, seed=2)
+    np.testing.assert_array_equal(bf16_from_bits(golden["quant_cfg3_small_x"]), x)
+
+
+def test_nvfp4_dequant_roundtrip():
+    x = recipes.cfg3_activation(64, 256, seed=4)
+    c, s = nvfp4.quantize(x)
+    d = nvfp4.dequantize(c, s, 64, 256)
+    c2, s2 = nvfp4.quantize(d)   # dequantized values re-quantize to themselves
+    np.testing.assert_array_equal(nvfp4.dequantize(c2, s2, 64, 256), d)  # (-0 codes aside)
+
+
+@pytest.mark.parametrize("case", ["act", "weight"])
+def test_fp8_quantize_bit_exact(golden, case):
+    q, scale = fp8.quantize(bf16_from_bits(golden[f"fp8_{case}_x"]))
+    assert np.float32(scale) == golden[f"fp8_{case}_scale"]
+    np.testing.assert_array_equal(q, golden[f"fp8_{case}_q"])
+
+
+def test_router_matches_reference(router_golden):
+    for action, rec in router_golden.items():
+        st = cache.RouterState(action, initial=5, stride=6, anchors=2)
+        assert st.capacity == rec["capacity"]
+        content = {}
+        for step in rec["steps"]:
+            origin, qpos = cache.rope_origin(step["start"], step["frames"])
+            assert origin == step["origin"] and list(qpos) == step["qpos"]
+            slots, ppos = st.history(origin)
+            assert list(slots) == step["slots"] and list(ppos) == step["ppos"], (action, step)
+            for off, slot in st.commit(step["frames"], step["start"]):
+                content[slot] = step["start"] + off
+            if step["slot_frames"]:
+                for slot, fid in content.items():
+                    assert step["slot_frames"][slot] == fid
+            assert sorted(st.frame_to_slot) == step["frame_ids"]
+
+
+def test_rope_tables(golden):
+    tc, ts, sc, ss = rope.rolling_tables(128, 11, 20)
+    np.testing.assert_array_equal(tc, golden["rope_tcos"])
+    np.testing.assert_array_equal(ts, golden["rope_tsin"])
+    np.testing.assert_array_equal(sc, golden["rope_scos"])
+    np.testing.assert_array_equal(ss, golden["rope_ssin"])
+    for h, w in ((22, 40), (34, 60)):
+        t = rope.rolling_tables(128, h, w)
+        sums = [t[2].astype(np.float64).sum(), t[3].astype(np.float64).sum(),
+                t[0].astype(np.float64).sum(), t[1].astype(np.float64).sum()]
+        np.testing.assert_allclose(sums, golden[f"rope_sum_{h}x{w}"], rtol=0, atol=1e-9)
+
+
+def test_rope_apply(golden):
+    x = bf16_from_bits(golden["rope_x"]).reshape(1, 440, 3, 128)
+    _, _, sc, ss = rope.rolling_tables(128, 11, 20)
+    tc, ts = golden["rope_tcos"], golden["rope_tsin"]
+    sp = rope.apply_rotary(x.reshape(1, 2, 220, 3, 128), sc[None, None, :, None, :],
+                           ss[None, None, :, None, :])
+    np.testing.assert_array_equal(sp.reshape(-1), bf16_from_bits(golden["rope_spatial"]).reshape(-1))
+    np.testing.assert_array_equal(sp.reshape(-1), bf16_from_bits(golden["rope_rotary"]).reshape(-1))
+    tp = rope.apply_temporal(x[0], [4, 17], tc, ts, 220)
+    np.testing.assert_array_equal(tp.reshape(-1), bf16_from_bits(golden["rope_temporal"]).reshape(-1))
+
+
+def test_attention_dense_matches_sdpa(golden):
+    g = {n: bf16_from_bits(golden[f"attn_dense_{n}"]) for n in ("q", "ck", "cv", "pk", "pv")}
+    tc, ts, _, _ = rope.rolling_tables(128, 4, 6)
+    out = attention.routed_attention(g["q"], g["ck"], g["cv"], g["pk"], g["pv"], [2, -1, 0],
+                                     [5, 0, 3], [6, 7], tc, ts, 4, 6, 22, 40)
+    ref32 = golden["attn_dense_f32"]
+    assert np.abs(out - ref32).max() < 2e-2
+    assert np.abs(out - ref32).max() <= 2 * np.abs(bf16_round(ref32) - ref32).max() + 1e-6
+    assert np.abs(out - golden["attn_dense_bf16"]).max() < 2e-2
+
+
+@pytest.mark.parametrize("tag", ["win_a", "win_b"])
+def test_attention_window_matches_triton(golden, tag):
+    if f"attn_{tag}_out" not in golden:
+        pytest.skip("fixture generated without TRITON_INTERPRET=1")
+    H, W, wh, ww, d, cap = (int(v) for v in golden[f"attn_{tag}_meta"][:6])
+    rest = [int(v) for v in golden[f"attn_{tag}_meta"][6:]]
+    slots, ppos = rest[:cap], rest[cap:]
+    a = {n: golden[f"attn_{tag}_{n}"].astype(np.float32) for n in ("q", "ck", "cv", "pk", "pv")}
+    tc, ts, _, _ = rope.rolling_tables(d, H, W)
+    out = attention.routed_attention(a["q"], a["ck"], a["cv"], a["pk"], a["pv"], slots, ppos,
+                                     [7, 8], tc, ts, H, W, wh, ww, dtype="fp16")
+    # fp16 kernel rounds probabilities before PV; the oracle does not.
+    assert np.abs(out - golden[f"attn_{tag}_out"]).max() < 5e-3
+
+
+def _block_setup(golden):
+    dim, heads, ffn, H, W, cap = (int(v) for v in golden["block_meta"])
+    p = recipes.block_params(dim, heads, ffn)
+    tc, ts, sc, ss = rope.rolling_tables(dim // heads, H, W)
+    lin = {n: block.QuantLinear(p[n + "_w"], p[n + "_b"])
+           for n in ("q", "k", "v", "o", "cq", "co", "up", "down")}
+    params = {"_linears": lin, "modulation": golden["block_modulation"].reshape(6, dim),
+              "norm_q": p["norm_q"], "norm_k": p["norm_k"], "cnorm_q": p["cnorm_q"],
+              "norm2_w": p["norm2_w"], "norm2_b": p["norm2_b"],
+              "cross_k": bf16_from_bits(golden["block_cross_k"]).reshape(-1, heads, dim // heads),
+              "cross_v": bf16_from_bits(golden["block_cross_v"]).reshape(-1, heads, dim // heads),
+              "temporal_cos": tc, "temporal_sin": ts, "spatial_cos": sc, "spatial_sin": ss}
+    hidden, pk, pv = recipes.block_inputs(2 * H * W, cap * H * W, dim)
+    return dim, heads, H, W, params, hidden, pk, pv
+
+
+def test_block_forward_matches_reference(golden):
+    dim, heads, H, W, params, hidden, pk, pv = _block_setup(golden)
+    d = dim // heads
+    h, k, v = block.block_forward(params, hidden[0], pk[0].reshape(-1, heads, d),
+                                  pv[0].reshape(-1, heads, d), [1, -1, 2], [4, 0, 5], [6, 7],
+                                  H, W, (22, 40), heads=heads)
+    ref_h = bf16_from_bits(golden["block_hidden"]).reshape(h.shape)
+    ref_k = bf16_from_bits(golden["block_k"]).reshape(k.shape)
+    ref_v = bf16_from_bits(golden["block_v"]).reshape(v.shape)
+    # K/V come straight from the first quantized GEMMs + RMSNorm/RoPE: near bit-exact.
+    assert np.abs(k - ref_k).max() <= 2 ** -6 * np.abs(ref_k).max()
+    assert np.abs(v - ref_v).max() <= 2 ** -7 * np.abs(ref_v).max()
+    # The block output passes through 5 more quantized GEMMs whose E2M1 codes can
+    # flip on 1-ulp bf16 differences; compare in relative L2 and max-abs.
+    rel = np.linalg.norm(h - ref_h) / np.linalg.norm(ref_h)
+    assert rel < 1e-2, rel
+    assert np.abs(h - ref_h).max() < 0.1 * np.abs(ref_h).max()
