@@ -102,6 +102,24 @@ int rc_kv_commit(const void* src_k, const void* src_v, long long src_ld_bytes, v
                  void* dst_v, long long dst_ld_bytes, int row_bytes, int span, int n_planes,
                  const int* src_planes, const int* dst_slots, rc_stream_t stream);
 
+/* ---- routed attention (tcgen05) ------------------------------------------ */
+/* Replaces recavsr_infer/kernels/local_attention.py:172-260 `paired_attention`
+ * (custom op recavsr_local::paired, Triton `_paired_local`) and :286-325
+ * `sdpa_attention` (window covering the grid). q/ck/cv [B, QT*H*W, heads, d],
+ * pk/pv [B, CAP*H*W, heads, d] bf16 with strides[15] = (batch, token, head)
+ * element strides of q, ck, cv, pk, pv; slots/past_positions int32 [CAP]
+ * (slot -1 = empty), query_positions int32 [QT], cos/sin fp32 [frames, td/2]
+ * (the rolling temporal table), all on the device. out: [B, QT*H*W, heads, d]
+ * bf16 with token stride out_ld. workspace: caller-provided device scratch of
+ * rc_paired_attention_workspace(...) bytes (rotated q and K planes). d = 128. */
+long long rc_paired_attention_workspace(int B, int QT, int CAP, int H, int W, int heads, int d);
+int rc_paired_attention(const void* q, const void* ck, const void* cv, const void* pk, const void* pv,
+                        const long long* strides, const int* slots, const int* past_positions,
+                        const int* query_positions, const float* cos, const float* sin, int B,
+                        int QT, int CAP, int H, int W, int heads, int d, int td, int window_h,
+                        int window_w, void* workspace, long long workspace_bytes, void* out,
+                        long long out_ld, rc_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -32,9 +32,10 @@ _SIGNATURES = {
     "rc_rmsnorm_rope": [_I, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P, _P, _F, _P],
     "rc_temporal_rope": [_P, _LL, _P, _LL, _P, _P, _P, _I, _I, _I, _I, _I, _P],
     "rc_kv_commit": [_P, _P, _LL, _P, _P, _LL, _I, _I, _I, _P, _P, _P],
-    "rc_paired_attention": [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P,
-                            _I, _I, _I, _I, _I, _I, _I, _I, _I, _I, _I, _F, _P, _P, _P, _P],
+    "rc_paired_attention": [_P] * 11 + [_I] * 10 + [_P, _LL, _P, _LL, _P],
+    "rc_paired_attention_workspace": [_I] * 7,
 }
+_RESTYPES = {"rc_paired_attention_workspace": C.c_longlong}
 
 _lib = None
 _lock = threading.Lock()
@@ -56,7 +57,7 @@ def library() -> C.CDLL:
                     if fn is None:
                         continue
                     fn.argtypes = args
-                    fn.restype = C.c_int
+                    fn.restype = _RESTYPES.get(name, C.c_int)
                 _lib = lib
     return _lib
 

@@ -1,3 +1,597 @@
-// Routed attention (placeholder until the tcgen05 kernel lands).
+// Cache-routed self-attention of a QT-frame query block over the current
+// frames plus the routed past planes of the KV cache
+// (recavsr_infer/kernels/local_attention.py:18-169 `_paired_local` and
+// :286-325 `sdpa_attention`).
+//
+// Semantics (one batch element, one head):
+//   planes = [past planes i with slots[i] >= 0 (position past_positions[i])]
+//            + [current frames f (position query_positions[f])]
+//   q and every key get the temporal rotary embedding of their plane position
+//   on the first `td` dims (fp32 math, bf16 rounding), exactly as the reference;
+//   a query at (qy, qx) sees, in every plane, the keys of rows
+//   [top, top+WH) x cols [left, left+WW), top = clamp(qy - WH/2, 0, H - WH),
+//   left = clamp(qx - WW/2, 0, W - WW), WH = min(H, window_h), WW = min(W, window_w)
+//   (a window covering the grid = every key, the sdpa path);
+//   out = softmax(q k^T / sqrt(d)) v with fp32 accumulation.
+//
+// Two kernels per launch:
+//  1. rope_gather: rotated copies of q, the current K frames and the routed
+//     past K planes into a caller-provided workspace (slot indirection applied
+//     here, so the attention kernel reads K densely).
+//  2. attention: one CTA per (128-query tile, head). Warp 0 = TMA producer
+//     (Q once, then K (workspace) and V (cache slot / current frame) tiles of
+//     128 keys, double-buffered), warp 1 = tcgen05 MMA issuer (S = Q K^T into a
+//     double-buffered TMEM S, O += P V into TMEM), warps 2-5 = online softmax
+//     (exp2, lazily rescaled running max), P to shared memory, epilogue.
+//   Dense mode (window covers the grid): query tiles are 128 consecutive tokens,
+//   key tiles 128 consecutive tokens of a plane (4-D TMA view, the plane tail
+//   reads as zeros). Local mode: query tiles are 2 frames x 8 x 8 tokens, key
+//   tiles are 8 x 16 boxes of the union of the tile's windows (5-D TMA view).
 #include "sm100.cuh"
+
+namespace {
+
+constexpr int kD = 128;             // head dim supported by the tcgen05 kernel
+constexpr int kBM = 128;            // queries per CTA
+constexpr int kBN = 128;            // keys per tile
+constexpr int kThreads = 192;
+constexpr int kLocalQH = 8, kLocalQW = 8;   // local query tile: 2 frames x 8 x 8
+constexpr int kLocalKH = 8, kLocalKW = 16;  // local key box: 8 rows x 16 cols
+constexpr int kMaxPlanes = 16;
+constexpr float kRescaleThreshold = 8.0f;   // log2 units
+
+struct AttnParams {
+  int T, H, W, heads, QT, CAP;
+  int wh, ww;                   // effective window (clamped to the grid)
+  int local;                    // 0 dense, 1 local
+  int n_qtiles;                 // query tiles per head
+  int qtiles_x, qtiles_y;       // local: tiles along x / y per frame pair
+  float scale_log2;             // d^-0.5 * log2(e)
+  const int* slots;             // [CAP] device
+  __nv_bfloat16* out;           // [QT*T, heads, d]
+  long long out_ld;             // elements between tokens
+};
+
+struct SmemLayout {
+  static constexpr int kChunk = 128 * 128;           // 128 rows x 128 bytes
+  static constexpr int offQ = 0;                     // 2 chunks
+  static constexpr int offK = offQ + 2 * kChunk;     // 2 stages x 2 chunks
+  static constexpr int offV = offK + 4 * kChunk;     // 2 stages x 2 chunks
+  static constexpr int offP = offV + 4 * kChunk;     // 2 chunks
+  static constexpr int offBar = offP + 2 * kChunk;
+  static constexpr int kBars = 12;
+  static constexpr int offMisc = offBar + kBars * 8;
+  static constexpr int kTotal = offMisc + 16 + kMaxPlanes * 4;
+  static constexpr int kAlloc = kTotal + 1024;
+};
+
+// Enumerates the key tiles of one query tile: planes in order, tiles within.
+struct TileIter {
+  const AttnParams& p;
+  const int* splanes;   // smem: source plane index per visible plane (-1 = skip)
+  int nplanes;
+  // local-mode key rectangle
+  int ry0, ry1, rx0, rx1;
+  __device__ TileIter(const AttnParams& p_, const int* sp, int np_, int qy0, int qx0)
+      : p(p_), splanes(sp), nplanes(np_) {
+    if (p.local) {
+      const int qy1 = min(qy0 + kLocalQH, p.H) - 1, qx1 = min(qx0 + kLocalQW, p.W) - 1;
+      ry0 = min(max(qy0 - p.wh / 2, 0), p.H - p.wh);
+      ry1 = min(max(qy1 - p.wh / 2, 0), p.H - p.wh) + p.wh;
+      rx0 = min(max(qx0 - p.ww / 2, 0), p.W - p.ww);
+      rx1 = min(max(qx1 - p.ww / 2, 0), p.W - p.ww) + p.ww;
+    } else {
+      ry0 = ry1 = rx0 = rx1 = 0;
+    }
+  }
+  __device__ int tiles_per_plane() const {
+    if (!p.local) return (p.T + kBN - 1) / kBN;
+    return ((ry1 - ry0 + kLocalKH - 1) / kLocalKH) * ((rx1 - rx0 + kLocalKW - 1) / kLocalKW);
+  }
+  // tile j within a plane -> (ky0, kx0) or t0
+  __device__ void tile_origin(int j, int& a, int& b) const {
+    if (!p.local) {
+      a = j * kBN;
+      b = 0;
+    } else {
+      const int nx = (rx1 - rx0 + kLocalKW - 1) / kLocalKW;
+      a = ry0 + (j / nx) * kLocalKH;   // y
+      b = rx0 + (j % nx) * kLocalKW;   // x
+    }
+  }
+};
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
+  return (uint32_t)rc::bf16_bits(a) | ((uint32_t)rc::bf16_bits(b) << 16);
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                 const __grid_constant__ CUtensorMap tm_pv, const __grid_constant__ CUtensorMap tm_cv,
+                 const AttnParams p) {
+  using L = SmemLayout;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::offBar);
+  uint64_t* q_full = bars + 0;
+  uint64_t* kv_full = bars + 1;    // [2]
+  uint64_t* kv_empty = bars + 3;   // [2]
+  uint64_t* s_full = bars + 5;     // [2]
+  uint64_t* s_free = bars + 7;     // [2]
+  uint64_t* p_full = bars + 9;
+  uint64_t* o_done = bars + 10;
+  uint64_t* done = bars + 11;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::offMisc);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::offMisc + 4);
+  int* s_nplanes = reinterpret_cast<int*>(smem + L::offMisc + 8);
+  int* s_planes = reinterpret_cast<int*>(smem + L::offMisc + 16);   // kMaxPlanes
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int head = blockIdx.y;
+  const int qtile = blockIdx.x;
+
+  // Query tile origin.
+  int q_row0 = 0, qf0 = 0, qy0 = 0, qx0 = 0;
+  if (!p.local) {
+    q_row0 = qtile * kBM;
+  } else {
+    const int per_pair = p.qtiles_x * p.qtiles_y;
+    qf0 = (qtile / per_pair) * 2;
+    const int r = qtile % per_pair;
+    qy0 = (r / p.qtiles_x) * kLocalQH;
+    qx0 = (r % p.qtiles_x) * kLocalQW;
+  }
+
+  if (threadIdx.x == 0) {
+    sm100::mbar_init(q_full, 1);
+    for (int s = 0; s < 2; ++s) {
+      sm100::mbar_init(&kv_full[s], 1);
+      sm100::mbar_init(&kv_empty[s], 1);
+      sm100::mbar_init(&s_full[s], 1);
+      sm100::mbar_init(&s_free[s], 128);
+    }
+    sm100::mbar_init(p_full, 128);
+    sm100::mbar_init(o_done, 1);
+    sm100::mbar_init(done, 1);
+    *abort_flag = 0;
+    // Visible planes: routed past planes (slot >= 0), then the current frames.
+    int n = 0;
+    for (int i = 0; i < p.CAP; ++i)
+      if (p.slots[i] >= 0 && p.slots[i] < p.CAP) s_planes[n++] = i;
+    for (int f = 0; f < p.QT; ++f) s_planes[n++] = p.CAP + f;
+    *s_nplanes = n;
+    sm100::fence_mbar_init();
+  }
+  if (warp == 1) {
+    sm100::tmem_alloc(tmem_slot, 512);
+    sm100::tmem_relinquish();
+  }
+  sm100::tc_fence_before();
+  __syncthreads();
+  sm100::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t t_s0 = tmem, t_o = tmem + 256;
+  const int nplanes = *s_nplanes;
+  TileIter it(p, s_planes, nplanes, qy0, qx0);
+  const int tpp = it.tiles_per_plane();
+  const int n_tiles = nplanes * tpp;
+
+  auto fail = [&](unsigned int site) {
+    if (!*abort_flag) rc::device_fail(kKernAttention, site);
+    *abort_flag = 1;
+  };
+  auto wait = [&](uint64_t* bar, uint32_t parity, unsigned int site) -> bool {
+    if (sm100::mbar_wait(bar, parity, abort_flag)) return true;
+    fail(site);
+    return false;
+  };
+
+  if (warp == 0) {
+    // ----------------------------------------------------------- producer
+    if (sm100::elect_one_sync()) {
+      uint8_t* sq = smem + L::offQ;
+      sm100::mbar_arrive_expect_tx(q_full, 2 * L::kChunk);
+      for (int c = 0; c < 2; ++c) {
+        if (!p.local) sm100::tma_load_3d(sq + c * L::kChunk, &tm_q, q_full, c * 64, head, q_row0);
+        else sm100::tma_load_5d(sq + c * L::kChunk, &tm_q, q_full, c * 64, head, qx0, qy0, qf0);
+      }
+      int issued = 0;
+      for (int i = 0; i < n_tiles; ++i) {
+        const int s = i & 1;
+        if (!wait(&kv_empty[s], ((i >> 1) & 1) ^ 1, 1)) break;
+        const int plane = s_planes[i / tpp];
+        int a, b;
+        it.tile_origin(i % tpp, a, b);
+        uint8_t* sk = smem + L::offK + s * 2 * L::kChunk;
+        uint8_t* sv = smem + L::offV + s * 2 * L::kChunk;
+        sm100::mbar_arrive_expect_tx(&kv_full[s], 4 * L::kChunk);
+        const bool past = plane < p.CAP;
+        const int vplane = past ? p.slots[plane] : plane - p.CAP;
+        const CUtensorMap* vmap = past ? &tm_pv : &tm_cv;
+        for (int c = 0; c < 2; ++c) {
+          if (!p.local) {
+            sm100::tma_load_4d(sk + c * L::kChunk, &tm_k, &kv_full[s], c * 64, head, a, plane);
+            sm100::tma_load_4d(sv + c * L::kChunk, vmap, &kv_full[s], c * 64, head, a, vplane);
+          } else {
+            sm100::tma_load_5d(sk + c * L::kChunk, &tm_k, &kv_full[s], c * 64, head, b, a, plane);
+            sm100::tma_load_5d(sv + c * L::kChunk, vmap, &kv_full[s], c * 64, head, b, a, vplane);
+          }
+        }
+        ++issued;
+      }
+      // Drain the (at most two) loads still in flight before teardown.
+      for (int i = max(0, issued - 2); i < issued; ++i) sm100::mbar_wait(&kv_full[i & 1], (i >> 1) & 1);
+      sm100::mbar_wait(q_full, 0);
+    }
+  } else if (warp == 1) {
+    // ----------------------------------------------------------- MMA issuer
+    if (sm100::elect_one_sync()) {
+      constexpr uint32_t idesc_qk = sm100::idesc_bf16(kBM, kBN, 0, 0);
+      constexpr uint32_t idesc_pv = sm100::idesc_bf16(kBM, kD, 0, 1);
+      const uint32_t sq = sm100::smem_u32(smem + L::offQ);
+      const uint32_t sp = sm100::smem_u32(smem + L::offP);
+      bool ok = wait(q_full, 0, 2);
+      sm100::tc_fence_after();
+      auto issue_pv = [&](int j) -> bool {
+        if (!wait(p_full, j & 1, 3)) return false;
+        sm100::tc_fence_after();
+        const uint32_t sv = sm100::smem_u32(smem + L::offV + (j & 1) * 2 * L::kChunk);
+        for (int k = 0; k < kBN / 16; ++k) {
+          const uint64_t ad = sm100::desc_kmajor_sw128(sp + (k >> 2) * L::kChunk + (k & 3) * 32);
+          const uint64_t bd = sm100::desc_mnmajor_sw128(sv + k * 16 * 128, L::kChunk);
+          sm100::mma_f16_ss(t_o, ad, bd, idesc_pv, (j > 0 || k > 0) ? 1u : 0u);
+        }
+        sm100::tc_commit(&kv_empty[j & 1]);
+        sm100::tc_commit(o_done);
+        return true;
+      };
+      for (int i = 0; i < n_tiles && ok; ++i) {
+        const int s = i & 1;
+        if (!wait(&kv_full[s], (i >> 1) & 1, 4)) { ok = false; break; }
+        if (!wait(&s_free[s], ((i >> 1) & 1) ^ 1, 5)) { ok = false; break; }
+        sm100::tc_fence_after();
+        const uint32_t sk = sm100::smem_u32(smem + L::offK + s * 2 * L::kChunk);
+        const uint32_t t_s = t_s0 + s * 128;
+        for (int k = 0; k < kD / 16; ++k) {
+          const uint32_t off = (k >> 2) * L::kChunk + (k & 3) * 32;
+          sm100::mma_f16_ss(t_s, sm100::desc_kmajor_sw128(sq + off), sm100::desc_kmajor_sw128(sk + off),
+                            idesc_qk, k > 0 ? 1u : 0u);
+        }
+        sm100::tc_commit(&s_full[s]);
+        if (i > 0 && !issue_pv(i - 1)) { ok = false; break; }
+      }
+      if (ok && n_tiles > 0) issue_pv(n_tiles - 1);
+      sm100::tc_commit(done);
+      sm100::mbar_wait(done, 0);
+    }
+  } else {
+    // ----------------------------------------------------------- softmax
+    const int quad = warp & 3;
+    const int r = quad * 32 + lane;               // query row within the tile / TMEM lane
+    const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
+    // This row's query token.
+    int qrow = -1, qy = 0, qx = 0;
+    if (!p.local) {
+      const int t = q_row0 + r;
+      if (t < p.QT * p.T) qrow = t;
+      qy = 0;
+      qx = 0;
+    } else {
+      const int f = qf0 + (r >> 6), yy = qy0 + ((r >> 3) & 7), xx = qx0 + (r & 7);
+      if (f < p.QT && yy < p.H && xx < p.W) qrow = f * p.T + yy * p.W + xx;
+      qy = yy;
+      qx = xx;
+    }
+    const int top = min(max(qy - p.wh / 2, 0), p.H - p.wh);
+    const int left = min(max(qx - p.ww / 2, 0), p.W - p.ww);
+    float m_used = -INFINITY, l = 0.f;
+    uint8_t* sp = smem + L::offP;
+    bool ok = true;
+    for (int i = 0; i < n_tiles; ++i) {
+      const int s = i & 1;
+      if (!__all_sync(0xffffffffu, wait(&s_full[s], (i >> 1) & 1, 6))) { ok = false; break; }
+      sm100::tc_fence_after();
+      int a, b;
+      it.tile_origin(i % tpp, a, b);
+      float sc[kBN];
+#pragma unroll
+      for (int c = 0; c < kBN; c += 16) {
+        uint32_t v[16];
+        sm100::tmem_ld16(t_s0 + s * 128 + c + lane_off, v);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) sc[c + j] = __uint_as_float(v[j]);
+      }
+      sm100::tmem_ld_wait();
+      // Release the S buffer as soon as it is in registers.
+      sm100::tc_fence_before();
+      sm100::mbar_arrive(&s_free[s]);
+      float mt = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < kBN; ++j) {
+        bool valid;
+        if (!p.local) {
+          valid = a + j < p.T;
+        } else {
+          const int ky = a + j / kLocalKW, kx = b + j % kLocalKW;
+          valid = ky < p.H && kx < p.W && ky >= top && ky < top + p.wh && kx >= left && kx < left + p.ww;
+        }
+        const float x = valid ? __fmul_rn(sc[j], p.scale_log2) : -INFINITY;
+        sc[j] = x;
+        mt = fmaxf(mt, x);
+      }
+      // Lazy rescaling: move the reference max only when it grows by > 2^8.
+      float corr = 1.0f;
+      bool rescale = false;
+      if (mt > m_used + kRescaleThreshold || (m_used == -INFINITY && mt > -INFINITY)) {
+        corr = m_used == -INFINITY ? 0.f : exp2f(m_used - mt);
+        rescale = (i > 0) && m_used != -INFINITY;
+        m_used = mt;
+      }
+      const float mref = m_used == -INFINITY ? 0.f : m_used;
+      float sum = 0.f;
+#pragma unroll
+      for (int j = 0; j < kBN; ++j) {
+        const float e = exp2f(sc[j] - mref);
+        sc[j] = e;
+        sum += e;
+      }
+      l = __fmul_rn(l, corr) + sum;
+      // P and O may only change once the previous P.V has finished.
+      if (i > 0 && !__all_sync(0xffffffffu, wait(o_done, (i - 1) & 1, 7))) { ok = false; break; }
+      sm100::tc_fence_after();
+      if (__any_sync(0xffffffffu, rescale)) {
+        const float f = rescale ? corr : 1.0f;
+#pragma unroll 1
+        for (int c = 0; c < kD; c += 16) {
+          uint32_t v[16];
+          sm100::tmem_ld16(t_o + c + lane_off, v);
+          sm100::tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 16; ++j) v[j] = __float_as_uint(__uint_as_float(v[j]) * f);
+          sm100::tmem_st16(t_o + c + lane_off, v);
+        }
+        sm100::tmem_st_wait();
+      }
+      // P row -> shared memory, K-major with the 128-byte swizzle.
+#pragma unroll
+      for (int u = 0; u < kBN / 8; ++u) {
+        const int chunk = u >> 3, unit = u & 7;
+        uint4 w = make_uint4(pack_bf16x2(sc[8 * u], sc[8 * u + 1]), pack_bf16x2(sc[8 * u + 2], sc[8 * u + 3]),
+                             pack_bf16x2(sc[8 * u + 4], sc[8 * u + 5]), pack_bf16x2(sc[8 * u + 6], sc[8 * u + 7]));
+        *reinterpret_cast<uint4*>(sp + chunk * L::kChunk + r * 128 + ((unit ^ (r & 7)) << 4)) = w;
+      }
+      sm100::fence_proxy_async_smem();
+      sm100::tc_fence_before();
+      sm100::mbar_arrive(p_full);
+    }
+    if (ok && n_tiles > 0 && __all_sync(0xffffffffu, wait(o_done, (n_tiles - 1) & 1, 8))) {
+      sm100::tc_fence_after();
+      const float inv = 1.0f / fmaxf(l, 1e-20f);
+      __nv_bfloat16* dst = qrow >= 0 ? p.out + (size_t)qrow * p.out_ld + (size_t)head * kD : nullptr;
+#pragma unroll 1
+      for (int c = 0; c < kD; c += 16) {
+        uint32_t v[16];
+        sm100::tmem_ld16(t_o + c + lane_off, v);
+        sm100::tmem_ld_wait();
+        if (dst) {
+          uint32_t w[8];
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            w[j] = pack_bf16x2(__uint_as_float(v[2 * j]) * inv, __uint_as_float(v[2 * j + 1]) * inv);
+          reinterpret_cast<uint4*>(dst + c)[0] = make_uint4(w[0], w[1], w[2], w[3]);
+          reinterpret_cast<uint4*>(dst + c)[1] = make_uint4(w[4], w[5], w[6], w[7]);
+        }
+      }
+    }
+  }
+
+  sm100::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    sm100::tc_fence_after();
+    sm100::tmem_dealloc(tmem, 512);
+  }
+}
+
+// ------------------------------------------------------------------ pre-pass
+struct GatherParams {
+  const __nv_bfloat16* q; long long q_ld, q_hs;     // token / head strides (elements)
+  const __nv_bfloat16* ck; long long ck_ld, ck_hs;
+  const __nv_bfloat16* pk; long long pk_ld, pk_hs;
+  const int* slots; const int* ppos; const int* qpos;
+  const float* cos; const float* sin;          // [*, td/2]
+  __nv_bfloat16* q_out;                        // [QT*T, heads*d]
+  __nv_bfloat16* k_out;                        // [(CAP+QT)*T, heads*d]
+  int T, QT, CAP, hd, td, d;
+};
+
+// One thread = 8 consecutive elements of one token row (16 bytes).
+__global__ void rope_gather_kernel(GatherParams g) {
+  const int vec = g.hd >> 3;
+  const int planes = g.QT + g.CAP + g.QT;
+  const long long total = (long long)planes * g.T * vec;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int v = (int)(i % vec);
+    const long long tok = i / vec;
+    const int plane = (int)(tok / g.T), t = (int)(tok % g.T);
+    const int head = (v * 8) / g.d, dd = (v * 8) % g.d;
+    const __nv_bfloat16* src;
+    __nv_bfloat16* dst;
+    int pos;
+    if (plane < g.QT) {
+      src = g.q + ((long long)plane * g.T + t) * g.q_ld + head * g.q_hs;
+      dst = g.q_out + ((long long)plane * g.T + t) * g.hd;
+      pos = g.qpos[plane];
+    } else if (plane < g.QT + g.CAP) {
+      const int i2 = plane - g.QT;
+      const int slot = g.slots[i2];
+      if (slot < 0 || slot >= g.CAP) continue;
+      src = g.pk + ((long long)slot * g.T + t) * g.pk_ld + head * g.pk_hs;
+      dst = g.k_out + ((long long)i2 * g.T + t) * g.hd;
+      pos = g.ppos[i2];
+    } else {
+      const int f = plane - g.QT - g.CAP;
+      src = g.ck + ((long long)f * g.T + t) * g.ck_ld + head * g.ck_hs;
+      dst = g.k_out + ((long long)(g.CAP + f) * g.T + t) * g.hd;
+      pos = g.qpos[f];
+    }
+    uint4 raw = *reinterpret_cast<const uint4*>(src + dd);
+    if (dd < g.td) {
+      uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int pr = (dd >> 1) + j;
+        if (2 * pr < g.td) {
+          const float e = __uint_as_float(w[j] << 16), o = __uint_as_float(w[j] & 0xffff0000u);
+          const float c = g.cos[pos * (g.td >> 1) + pr], s = g.sin[pos * (g.td >> 1) + pr];
+          const float ne = __fsub_rn(__fmul_rn(e, c), __fmul_rn(o, s));
+          const float no = __fadd_rn(__fmul_rn(e, s), __fmul_rn(o, c));
+          w[j] = pack_bf16x2(ne, no);
+        }
+      }
+      raw = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+    *reinterpret_cast<uint4*>(dst + head * g.d + dd) = raw;
+  }
+}
+
+// Tensor-map views (innermost first): dense (d, heads, tokens, planes),
+// local (d, heads, W, H, planes); `ld` = elements between tokens.
+int make_view(CUtensorMap* m, const void* base, long long ld, long long hs, int heads, int T, int H,
+              int W, int planes, bool local, const char* what) {
+  if (local) {
+    const uint64_t dims[5] = {(uint64_t)kD, (uint64_t)heads, (uint64_t)W, (uint64_t)H, (uint64_t)planes};
+    const uint64_t str[4] = {(uint64_t)hs * 2, (uint64_t)ld * 2, (uint64_t)ld * 2 * W,
+                             (uint64_t)ld * 2 * T};
+    const uint32_t box[5] = {64, 1, kLocalKW, kLocalKH, 1};
+    return rc::encode_tmap(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 5, const_cast<void*>(base), dims, str, box,
+                           CU_TENSOR_MAP_SWIZZLE_128B, what);
+  }
+  const uint64_t dims[4] = {(uint64_t)kD, (uint64_t)heads, (uint64_t)T, (uint64_t)planes};
+  const uint64_t str[3] = {(uint64_t)hs * 2, (uint64_t)ld * 2, (uint64_t)ld * 2 * T};
+  const uint32_t box[4] = {64, 1, kBN, 1};
+  return rc::encode_tmap(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, str, box,
+                         CU_TENSOR_MAP_SWIZZLE_128B, what);
+}
+
+bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+int g_attr_set = 0;
+
+}  // namespace
+
 RC_DEVICE_ERROR_ACCESSOR(attention)
+
+extern "C" {
+
+long long rc_paired_attention_workspace(int B, int QT, int CAP, int H, int W, int heads, int d) {
+  if (B <= 0 || QT <= 0 || CAP < 0 || H <= 0 || W <= 0 || heads <= 0 || d <= 0) return -1;
+  return (long long)B * (2LL * QT + CAP) * H * W * heads * d * 2;
+}
+
+// strides[15]: (batch, token, head) strides in elements of q, ck, cv, pk, pv
+// (the head dim itself must be contiguous). slots / positions / rotary tables
+// live on the device; the workspace holds the rotated q and K planes.
+int rc_paired_attention(const void* q, const void* ck, const void* cv, const void* pk, const void* pv,
+                        const long long* strides, const int* slots, const int* past_positions,
+                        const int* query_positions, const float* cos, const float* sin, int B,
+                        int QT, int CAP, int H, int W, int heads, int d, int td, int window_h,
+                        int window_w, void* workspace, long long workspace_bytes, void* out,
+                        long long out_ld, cudaStream_t stream) {
+  const char* what = "rc_paired_attention";
+  if (B <= 0 || QT <= 0 || CAP < 0 || H <= 0 || W <= 0 || heads <= 0)
+    return rc::set_error(RC_ERR_ARG, "%s: bad geometry", what);
+  if (d != kD)
+    return rc::set_error(RC_ERR_UNSUPPORTED, "%s: head_dim %d (the tcgen05 kernel supports 128)", what, d);
+  if (td < 0 || td > d || td % 2 || window_h <= 0 || window_w <= 0 || CAP > kMaxPlanes - 8 || QT > 8)
+    return rc::set_error(RC_ERR_ARG, "%s: bad rotary / window / plane count", what);
+  if (!q || !ck || !cv || !out || !query_positions || !cos || !sin || !strides ||
+      (CAP && (!pk || !pv || !slots || !past_positions)))
+    return rc::set_error(RC_ERR_ARG, "%s: null pointer", what);
+  const long long need = rc_paired_attention_workspace(B, QT, CAP, H, W, heads, d);
+  if (!workspace || workspace_bytes < need || !al16(workspace))
+    return rc::set_error(RC_ERR_ARG, "%s: workspace of %lld bytes (16-byte aligned) required", what, need);
+  for (int t = 0; t < 5; ++t) {
+    if (t >= 3 && !CAP) continue;
+    if ((B > 1 && strides[3 * t] % 8) || strides[3 * t + 1] % 8 || strides[3 * t + 2] % 8)
+      return rc::set_error(RC_ERR_ARG, "%s: strides must be multiples of 8 elements (16 bytes)", what);
+  }
+  const void* ptrs[5] = {q, ck, cv, pk, pv};
+  for (int i = 0; i < 5; ++i)
+    if (ptrs[i] && !al16(ptrs[i])) return rc::set_error(RC_ERR_ARG, "%s: tensors must be 16-byte aligned", what);
+  if (!al16(out) || out_ld % 8) return rc::set_error(RC_ERR_ARG, "%s: output must be 16-byte aligned", what);
+  const int T = H * W;
+  const int wh = window_h < H ? window_h : H, ww = window_w < W ? window_w : W;
+  const bool local = wh < H || ww < W;
+  if (local && QT % 2) return rc::set_error(RC_ERR_UNSUPPORTED, "%s: local windows need an even frame count", what);
+  if (!g_attr_set) {
+    if (cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             SmemLayout::kAlloc) != cudaSuccess)
+      return rc::set_error(RC_ERR_CUDA, "%s: shared memory attribute", what);
+    g_attr_set = 1;
+  }
+  const long long hd = (long long)heads * d;
+  const long long per_batch = (2LL * QT + CAP) * T * hd;
+  for (int b = 0; b < B; ++b) {
+    __nv_bfloat16* qs = reinterpret_cast<__nv_bfloat16*>(workspace) + b * per_batch;
+    __nv_bfloat16* ks = qs + (long long)QT * T * hd;
+    const __nv_bfloat16* qb = reinterpret_cast<const __nv_bfloat16*>(q) + b * strides[0];
+    const __nv_bfloat16* ckb = reinterpret_cast<const __nv_bfloat16*>(ck) + b * strides[3];
+    const __nv_bfloat16* cvb = reinterpret_cast<const __nv_bfloat16*>(cv) + b * strides[6];
+    const __nv_bfloat16* pkb = CAP ? reinterpret_cast<const __nv_bfloat16*>(pk) + b * strides[9] : nullptr;
+    const __nv_bfloat16* pvb = CAP ? reinterpret_cast<const __nv_bfloat16*>(pv) + b * strides[12] : nullptr;
+    GatherParams g{qb, strides[1], strides[2], ckb, strides[4], strides[5], pkb, strides[10],
+                   strides[11], slots, past_positions, query_positions, cos, sin, qs, ks,
+                   T, QT, CAP, (int)hd, td, d};
+    const long long work = (2LL * QT + CAP) * T * (hd / 8);
+    long long blocks = (work + 255) / 256;
+    if (blocks > 148LL * 16) blocks = 148LL * 16;
+    rope_gather_kernel<<<(int)blocks, 256, 0, stream>>>(g);
+    int r = rc::check_launch("rc_paired_attention(rope)");
+    if (r) return r;
+    CUtensorMap tq, tk, tpv, tcv;
+    if (!local) {
+      const uint64_t dims[3] = {(uint64_t)kD, (uint64_t)heads, (uint64_t)QT * T};
+      const uint64_t str[2] = {(uint64_t)kD * 2, (uint64_t)hd * 2};
+      const uint32_t box[3] = {64, 1, kBM};
+      r = rc::encode_tmap(&tq, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, qs, dims, str, box,
+                          CU_TENSOR_MAP_SWIZZLE_128B, what);
+    } else {
+      const uint64_t dims[5] = {(uint64_t)kD, (uint64_t)heads, (uint64_t)W, (uint64_t)H, (uint64_t)QT};
+      const uint64_t str[4] = {(uint64_t)kD * 2, (uint64_t)hd * 2, (uint64_t)hd * 2 * W, (uint64_t)hd * 2 * T};
+      const uint32_t box[5] = {64, 1, kLocalQW, kLocalQH, 2};
+      r = rc::encode_tmap(&tq, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 5, qs, dims, str, box,
+                          CU_TENSOR_MAP_SWIZZLE_128B, what);
+    }
+    if (r) return r;
+    if ((r = make_view(&tk, ks, hd, d, heads, T, H, W, CAP + QT, local, what))) return r;
+    if ((r = make_view(&tcv, cvb, strides[7], strides[8], heads, T, H, W, QT, local, what))) return r;
+    if (CAP) {
+      if ((r = make_view(&tpv, pvb, strides[13], strides[14], heads, T, H, W, CAP, local, what))) return r;
+    } else {
+      tpv = tcv;
+    }
+    AttnParams p{};
+    p.T = T; p.H = H; p.W = W; p.heads = heads; p.QT = QT; p.CAP = CAP;
+    p.wh = wh; p.ww = ww; p.local = local;
+    p.scale_log2 = (float)(1.0 / sqrt((double)d) * 1.4426950408889634);
+    p.slots = slots;
+    p.out = reinterpret_cast<__nv_bfloat16*>(out) + (long long)b * QT * T * out_ld;
+    p.out_ld = out_ld;
+    if (!local) {
+      p.n_qtiles = (QT * T + kBM - 1) / kBM;
+    } else {
+      p.qtiles_x = (W + kLocalQW - 1) / kLocalQW;
+      p.qtiles_y = (H + kLocalQH - 1) / kLocalQH;
+      p.n_qtiles = (QT / 2) * p.qtiles_x * p.qtiles_y;
+    }
+    dim3 grid(p.n_qtiles, heads);
+    attention_kernel<<<grid, kThreads, SmemLayout::kAlloc, stream>>>(tq, tk, tpv, tcv, p);
+    if ((r = rc::check_launch(what))) return r;
+  }
+  return RC_OK;
+}
+
+}  // extern "C"

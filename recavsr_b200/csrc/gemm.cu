@@ -279,7 +279,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
     }
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
       const int mb = tile % p.m_blocks, nb = tile / p.m_blocks;
-      if (!wait(acc_full, acc_phase, 4)) break;
+      if (!__all_sync(0xffffffffu, wait(acc_full, acc_phase, 4))) break;
       sm100::tc_fence_after();
       const int row = mb * BM + row_in_tile;
       const bool row_ok = row < p.M;

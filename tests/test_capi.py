@@ -10,7 +10,7 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 def declared():
     with open(os.path.join(ROOT, "include", "recavsr_b200.h")) as f:
         src = f.read()
-    return sorted(set(re.findall(r"^int (rc_\w+)\(", src, flags=re.M)))
+    return sorted(set(re.findall(r"^(?:int|long long) (rc_\w+)\(", src, flags=re.M)))
 
 
 def test_header_symbols_exported():

@@ -135,10 +135,11 @@ def test_fp8_gemm(m, n, k):
     wq, sw = ofp8.quantize(w)
     ref = ofp8.fp8_mm(aq, sa, wq, sw, bias)
     out = torch.empty(m, n, dtype=torch.bfloat16, device="cuda")
-    sad = torch.tensor(sa, device="cuda")
-    swd = torch.tensor(sw, device="cuda")
-    _lib.call("rc_fp8_gemm", dev_u8(aq).data_ptr(), sad.data_ptr(), dev_u8(wq).data_ptr(),
-              swd.data_ptr(), dev_bf16(bias).data_ptr(), m, n, k, 1.0, _lib.EPI_BIAS,
+    sad = torch.tensor(sa, dtype=torch.float32, device="cuda")
+    swd = torch.tensor(sw, dtype=torch.float32, device="cuda")
+    ad, wd, bd = dev_u8(aq), dev_u8(wq), dev_bf16(bias)   # keep alive across the call
+    _lib.call("rc_fp8_gemm", ad.data_ptr(), sad.data_ptr(), wd.data_ptr(),
+              swd.data_ptr(), bd.data_ptr(), m, n, k, 1.0, _lib.EPI_BIAS,
               out.data_ptr(), n, None, _lib.stream())
     assert_no_device_error()
     assert max_rel(host(out), ref) < TOL
@@ -168,9 +169,9 @@ def test_bf16_gemm(m, n, k):
     bias = recipes.bf16_normal(rs, (n,), 0.1)
     ref = bf16_round(a.astype(np.float64) @ w.astype(np.float64).T + bias)
     out = torch.empty(m, n, dtype=torch.bfloat16, device="cuda")
-    _lib.call("rc_bf16_gemm", dev_bf16(a).data_ptr(), dev_bf16(w).data_ptr(),
-              dev_bf16(bias).data_ptr(), m, n, k, _lib.EPI_BIAS, out.data_ptr(), n, None,
-              _lib.stream())
+    ad, wd, bd = dev_bf16(a), dev_bf16(w), dev_bf16(bias)   # keep alive across the call
+    _lib.call("rc_bf16_gemm", ad.data_ptr(), wd.data_ptr(), bd.data_ptr(), m, n, k,
+              _lib.EPI_BIAS, out.data_ptr(), n, None, _lib.stream())
     assert_no_device_error()
     assert max_rel(host(out), ref) < TOL
 

@@ -132,11 +132,11 @@ def test_cache_commit_matches_router(router_golden):
             ids = torch.arange(start, start + frames, device="cuda", dtype=torch.float32)
             k = ids.view(1, frames, 1, 1).expand(1, frames, span, heads * d).reshape(1, frames * span, heads, d)
             k = k.bfloat16().contiguous()
-            c.commit(k, (k + 0.5).contiguous(), frames=frames, start=start)
+            c.commit(k, (-k).contiguous(), frames=frames, start=start)
             if step["slot_frames"]:
                 kk = c.key.float().view(c.capacity, span * heads * d)
                 vv = c.value.float().view(c.capacity, span * heads * d)
                 for slot, fid in enumerate(step["slot_frames"]):
                     if slot in c.frame_to_slot.values():
-                        assert torch.all(kk[slot] == fid) and torch.all(vv[slot] == fid + 0.5)
+                        assert torch.all(kk[slot] == fid) and torch.all(vv[slot] == -fid)
     assert_no_device_error()
