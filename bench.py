@@ -1,0 +1,375 @@
+"""Benchmark: DiT latent tokens/s of the ReCaVSR hot path on B200.
+
+Workload (the 720p x4 stream): the 30-layer streaming DiT
+layer loop (routed self-attention over the released static KV router, cross
+attention over 512 prompt tokens, NVFP4 linears, modulation / LayerNorm /
+RMSNorm / RoPE glue, KV-cache commit) on 1280x704 output = 22x40 latent
+tokens per frame (T = 880), body blocks of 2 latent frames (1760 tokens).
+Random-init weights of the released architecture (dim 3072, 24 heads x 128,
+FFN 14336), synthetic N(0,1) hidden states, prompt states and timestep
+projection. One step = one body block through all 30 layers; the 6-frame
+prefix block and enough body blocks to fill every layer's cache run as
+warm-up. Inputs/weights/caches (~4 GB) exceed L2 (126 MB), so no flush.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+
+Under torchrun each rank runs an independent stream (weak scaling, no
+collective); rank 0 prints one JSON line with the max-over-ranks time.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+DIM, HEADS, HEAD_DIM, FFN, LAYERS = 3072, 24, 128, 14336, 30
+H_TOK, W_TOK = 22, 40                  # 1280x704 / 32
+T = H_TOK * W_TOK
+BODY, PREFIX = 2, 6
+ENC_LEN = 512
+# Layer actions of the released static KV router (checkpoints/model_config.json).
+ACTIONS = ["none", "none", "recent_1", "none", "recent_2", "none", "recent_2", "recent_4", "none",
+           "recent_2_anchor", "recent_4", "recent_4_anchor", "recent_2", "recent_4_anchor", "anchor",
+           "recent_4_anchor", "recent_2", "recent_4_anchor", "recent_2_anchor", "recent_4", "recent_2",
+           "none", "recent_2_anchor", "recent_2", "none", "recent_2", "none", "recent_1", "none", "none"]
+METRIC = "DiT latent tokens/s/GPU (routed attn+NVFP4 linears); 720p x4 out frames/s"
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            m = json.load(f)
+        return m["hbm_gbs"], m["bf16_tflops"], m.get("bf16_tflops_sustained", m["bf16_tflops"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    """nvidia-smi samples during the timed region (clocks + throttle reasons)."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index, self.rows, self.proc = index, [], None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) == 7:
+                self.rows.append(parts)
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[0]) for r in self.rows if r[0].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in self.rows for n, v in zip(names, r[3:]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": float(self.rows[0][1]) if self.rows[0][1].replace(".", "").isdigit() else None,
+                "reasons": reasons, "samples": len(self.rows)}
+
+
+# -------------------------------------------------------------- model setup
+def build_stack(device, seed):
+    import torch
+    from recavsr_b200.runtime.block import FusedBlock, LayerStack, rope_tables
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    tables = rope_tables(HEAD_DIM, H_TOK, W_TOK, device)
+    rnd = lambda *s, std=1.0: (torch.randn(*s, generator=g, device=device) * std).bfloat16()
+    encoder = rnd(1, ENC_LEN, DIM)
+    blocks = []
+    for _ in range(LAYERS):
+        w = {}
+        for name, (n, k) in {"q": (DIM, DIM), "k": (DIM, DIM), "v": (DIM, DIM), "o": (DIM, DIM),
+                             "cq": (DIM, DIM), "ck": (DIM, DIM), "cv": (DIM, DIM), "co": (DIM, DIM),
+                             "up": (FFN, DIM), "down": (DIM, FFN)}.items():
+            w[name + "_w"] = rnd(n, k, std=0.02)
+            w[name + "_b"] = rnd(n, std=0.02)
+        for name in ("norm_q", "norm_k", "cnorm_q", "cnorm_k", "norm2_w"):
+            w[name] = (1 + 0.1 * torch.randn(DIM, generator=g, device=device)).bfloat16()
+        w["norm2_b"] = rnd(DIM, std=0.1)
+        w["scale_shift_table"] = rnd(1, 6, DIM, std=DIM ** -0.5)
+        w["timestep_proj"] = rnd(1, 1, 6, DIM)
+        w["encoder"] = encoder
+        w["heads"] = HEADS
+        blocks.append(FusedBlock(w, H_TOK, W_TOK, tables))
+        del w
+    torch.cuda.synchronize(device)
+    return LayerStack(blocks, ACTIONS)
+
+
+def algorithmic_flops_per_token():
+    """Linears per token (30 layers): q,k,v,o,cross-q,cross-o = 6*2*dim^2, FFN 2*2*dim*ffn."""
+    return LAYERS * (6 * 2 * DIM * DIM + 2 * 2 * DIM * FFN)
+
+
+def attention_flops_per_block(stack):
+    """Visible keys only: 4 * d * heads * Nq * T * sum over layers of (planes),
+    counted from the last block's routing table."""
+    planes = 0
+    for i, c in enumerate(stack.caches):
+        o = i * stack._row
+        planes += int((stack.route_host[o:o + c.capacity] >= 0).sum())
+    return 4 * HEAD_DIM * HEADS * (BODY * T) * T * (planes + BODY * LAYERS), planes
+
+
+# ------------------------------------------------------- kernel-level timing
+def time_kernel(fn, reps, torch):
+    s = torch.cuda.current_stream()
+    for _ in range(3):
+        fn()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    a.record(s)
+    for _ in range(reps):
+        fn()
+    b.record(s)
+    b.synchronize()
+    return a.elapsed_time(b) / reps * 1e-3
+
+
+def kernel_roofline(stack, torch):
+    """Time the ffn_up NVFP4 GEMM (the largest launch of the step) and the
+    routed attention of a recent_4_anchor layer on the step's own buffers."""
+    from recavsr_b200 import _lib
+    lib = _lib.library()
+    blk = stack.blocks[11]
+    n = BODY * T
+    ws = stack.workspace(n)
+    st = _lib.stream()
+
+    def up():
+        _lib.check(lib.rc_nvfp4_gemm(ws.a_codes.data_ptr(), ws.a_scales.data_ptr(), blk.up.codes.data_ptr(),
+                                     blk.up.scales.data_ptr(), blk.up.bias.data_ptr(), n, FFN, DIM, 1.0,
+                                     _lib.EPI_GELU_NVFP4, None, 0, None, ws.f_codes.data_ptr(),
+                                     ws.f_scales.data_ptr(), 1.0, st), "up")
+    t_up = time_kernel(up, 50, torch)
+    rd = stack.route_dev
+    o = 11 * stack._row
+    cap = stack.caches[11].capacity
+    qpos = rd[LAYERS * stack._row:]
+
+    def att():
+        blk._attention(lib, ws, stack.cache_k[11], stack.cache_v[11], rd[o:o + cap], rd[o + 8:o + 8 + cap],
+                       qpos, n, st)
+    t_att = time_kernel(att, 20, torch)
+    vis = int((stack.route_host[o:o + cap] >= 0).sum())
+    att_flops = 4 * HEAD_DIM * HEADS * n * T * (vis + BODY)
+    return {"ffn_up_s": t_up, "ffn_up_flops": 2.0 * n * FFN * DIM,
+            "attn_s": t_att, "attn_flops": float(att_flops), "attn_planes": vis + BODY}
+
+
+# ---------------------------------------------------------------- CPU side
+def cpu_baseline(sample_tokens_note=True):
+    """Oracle port of one DiT block forward (NVFP4 linears emulated, fp32
+    matmuls, numpy/BLAS on all host cores) at the bench geometry; tokens/s is
+    extrapolated to the 30-layer step."""
+    from oracle import block as oblock
+    from oracle import rope as orope
+    rs = np.random.RandomState(0)
+    f32 = lambda *s, std=1.0: (rs.standard_normal(s).astype(np.float32) * np.float32(std))
+    lin = {}
+    for name, (n, k) in {"q": (DIM, DIM), "k": (DIM, DIM), "v": (DIM, DIM), "o": (DIM, DIM),
+                         "cq": (DIM, DIM), "co": (DIM, DIM), "up": (FFN, DIM), "down": (DIM, FFN)}.items():
+        lin[name] = oblock.QuantLinear(f32(n, k, std=0.02), f32(n, std=0.02), matmul_dtype=np.float32)
+    tc, ts, sc, ss = orope.rolling_tables(HEAD_DIM, H_TOK, W_TOK)
+    p = {"_linears": lin, "modulation": f32(6, DIM), "norm_q": 1 + f32(DIM, std=0.1),
+         "norm_k": 1 + f32(DIM, std=0.1), "cnorm_q": 1 + f32(DIM, std=0.1),
+         "norm2_w": 1 + f32(DIM, std=0.1), "norm2_b": f32(DIM, std=0.1),
+         "cross_k": f32(ENC_LEN, HEADS, HEAD_DIM), "cross_v": f32(ENC_LEN, HEADS, HEAD_DIM),
+         "temporal_cos": tc, "temporal_sin": ts, "spatial_cos": sc, "spatial_sin": ss}
+    hidden = f32(BODY * T, DIM)
+    pk, pv = f32(2 * T, HEADS, HEAD_DIM), f32(2 * T, HEADS, HEAD_DIM)
+    t0 = time.perf_counter()
+    oblock.block_forward(p, hidden, pk, pv, [0, 1], [6, 7], [8, 9], H_TOK, W_TOK, (22, 40),
+                         heads=HEADS, matmul_dtype=np.float32)
+    dt = time.perf_counter() - t0
+    tokens_per_s = BODY * T / (dt * LAYERS)
+    return {"value": tokens_per_s, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+            "sample": f"1 of 30 layers (recent_2 cache, 1760 tokens), {dt:.2f} s, extrapolated x30"}
+
+
+def run_reference(args, rank, world):
+    """--impl reference: the reference's CPU formulation (oracle port) timed on
+    the host cores; rank 0 only."""
+    if rank != 0:
+        return
+    os.environ.setdefault("OMP_NUM_THREADS", str(os.cpu_count()))
+    vals = []
+    for i in range(args.warmup + args.steps):
+        r = cpu_baseline()
+        if i >= args.warmup:
+            vals.append(r["value"])
+    v = statistics.median(vals)
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": BODY * T / v * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
+        "data": "synthetic",
+        "config": {"workload": "cfg4 DiT layer loop, 1280x704 (22x40 tokens), 2-frame body block",
+                   "global_batch": 1, "seq_len": BODY * T, "parallelism": "cpu"},
+        "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+                         "sample": r["sample"]},
+        "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+# ------------------------------------------------------------------- main
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--eager", action="store_true", help="no CUDA graph (launch from Python)")
+    args = ap.parse_args()
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local = int(os.environ.get("LOCAL_RANK", 0))
+    if args.impl == "reference":
+        return run_reference(args, rank, world)
+
+    import torch
+    import torch.distributed as dist
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+    from recavsr_b200 import _lib
+    stack = build_stack(device, seed=1234 + rank)
+    g = torch.Generator(device=device)
+    g.manual_seed(99 + rank)
+    warm = max(args.warmup, 3)
+    # Prefix (6 frames) then body blocks; the caches fill within a few blocks.
+    prefix = torch.randn(PREFIX * T, DIM, generator=g, device=device).bfloat16()
+    stack.step(prefix, PREFIX)
+    body = torch.randn(BODY * T, DIM, generator=g, device=device).bfloat16()
+    h = body.clone()
+    stack.step(h, BODY)                       # eager body step: sets kernel attributes
+    use_graph = not args.eager
+    if use_graph:
+        stack.capture(BODY * T, BODY)
+    for _ in range(warm):
+        h.copy_(body)
+        stack.step(h, BODY, graphs=use_graph)
+    torch.cuda.synchronize(device)
+    if not torch.isfinite(h.float()).all():
+        raise RuntimeError("non-finite hidden state after warm-up")
+    dev_err = _lib.read_device_error()
+    if dev_err:
+        raise RuntimeError(f"device error word 0x{dev_err:08x}")
+
+    # ---- timed region: device-resident inputs
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(device)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        start.record()
+        for _ in range(args.steps):
+            stack.step(h, BODY, graphs=use_graph)
+        end.record()
+        end.synchronize()
+    t = start.elapsed_time(end) * 1e-3
+    # ---- e2e: host buffers, copies inside the timed region
+    host_in = torch.empty((BODY * T, DIM), dtype=torch.bfloat16, pin_memory=True)
+    host_in.copy_(body.cpu())
+    host_out = torch.empty_like(host_in, pin_memory=True)
+    torch.cuda.synchronize(device)
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        h.copy_(host_in, non_blocking=True)
+        stack.step(h, BODY, graphs=use_graph)
+        host_out.copy_(h, non_blocking=True)
+    e1.record()
+    e1.synchronize()
+    te = e0.elapsed_time(e1) * 1e-3
+    if world > 1:
+        tt = torch.tensor([t, te], device=device)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        t, te = float(tt[0]), float(tt[1])
+    kr = kernel_roofline(stack, torch) if rank == 0 else None
+    att_flops, planes = attention_flops_per_block(stack)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    tokens = BODY * T * args.steps * world
+    value = tokens / t
+    hbm, bf16_peak, bf16_sus, src = peaks()
+    fp4_peak = 4 * bf16_peak
+    achieved = kr["ffn_up_flops"] / kr["ffn_up_s"] / 1e12
+    cpu = None if args.no_cpu_baseline else cpu_baseline()
+    launches_per_layer = 19   # 16 kernels + 3 scale-padding kernels (M % 128 != 0)
+    out = {
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": warm, "ms_per_step": t / args.steps * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "nvfp4 linears / bf16 attention",
+        "data": "synthetic (random-init weights, N(0,1) hidden/prompt states)",
+        "config": {"workload": "cfg4 DiT layer loop (30 layers, released router), 1280x704 -> 22x40 "
+                               "tokens, 2-frame body block (1760 tokens), B=1",
+                   "global_batch": world, "seq_len": BODY * T, "parallelism": f"streams x{world}",
+                   "l2": "working set > 126 MB L2 (no flush)", "cuda_graph": use_graph},
+        "out_fps": value * 4 / T,
+        "linear_tflops": value * algorithmic_flops_per_token() / 1e12,
+        "attention_tflops": att_flops * (value / (BODY * T)) / 1e12,
+        "roofline": {"bound": "tensor", "kernel": "nvfp4 ffn_up GEMM 1760x14336x3072 (+GELU+NVFP4 epilogue)",
+                     "achieved": achieved, "peak": fp4_peak, "unit": "TFLOP/s", "frac": achieved / fp4_peak,
+                     "peak_source": f"4 x {src} bf16 dense ({bf16_peak} TFLOP/s): FP4:BF16 dense ratio 4",
+                     "traffic": None,
+                     "attention": {"achieved": kr["attn_flops"] / kr["attn_s"] / 1e12, "peak": bf16_peak,
+                                   "frac": kr["attn_flops"] / kr["attn_s"] / 1e12 / bf16_peak,
+                                   "planes": kr["attn_planes"], "unit": "TFLOP/s"}},
+        "cpu_baseline": cpu,
+        "e2e": {"value": tokens / te, "unit": "tokens/s",
+                "h2d_bytes_per_step": BODY * T * DIM * 2, "d2h_bytes_per_step": BODY * T * DIM * 2},
+        "gpu_launches": args.steps * (LAYERS * launches_per_layer + sum(
+            1 for c in stack.caches if c.capacity)),
+        "clocks": clk.summary(),
+        "attention_planes_per_block": planes + BODY * LAYERS,
+    }
+    print(json.dumps(out), flush=True)
+
+
+if __name__ == "__main__":
+    main()

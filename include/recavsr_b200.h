@@ -102,6 +102,13 @@ int rc_kv_commit(const void* src_k, const void* src_v, long long src_ld_bytes, v
                  void* dst_v, long long dst_ld_bytes, int row_bytes, int span, int n_planes,
                  const int* src_planes, const int* dst_slots, rc_stream_t stream);
 
+/* Same copies with the plan in device memory: plan = [n, (src plane, dst slot) x n],
+ * n <= max_planes <= 8, slots < capacity. Lets a captured CUDA graph of the
+ * layer loop follow the router without re-capture. */
+int rc_kv_commit_planned(const void* src_k, const void* src_v, long long src_ld_bytes, void* dst_k,
+                         void* dst_v, long long dst_ld_bytes, int row_bytes, int span,
+                         int max_planes, int capacity, const int* plan, rc_stream_t stream);
+
 /* ---- routed attention (tcgen05) ------------------------------------------ */
 /* Replaces recavsr_infer/kernels/local_attention.py:172-260 `paired_attention`
  * (custom op recavsr_local::paired, Triton `_paired_local`) and :286-325
@@ -119,6 +126,14 @@ int rc_paired_attention(const void* q, const void* ck, const void* cv, const voi
                         int QT, int CAP, int H, int W, int heads, int d, int td, int window_h,
                         int window_w, void* workspace, long long workspace_bytes, void* out,
                         long long out_ld, rc_stream_t stream);
+
+/* Unmasked attention without rotary embedding or cache (the cross-attention of
+ * recavsr_infer/runtime/transformer.py:123-128 over the precomputed prompt K/V):
+ * q [B, Nq, heads, d], k/v [B, Nk, heads, d] with strides[9] = (batch, token,
+ * head) element strides of q, k, v; out [B, Nq, heads, d] (token stride out_ld). */
+int rc_cross_attention(const void* q, const void* k, const void* v, const long long* strides, int B,
+                       int Nq, int Nk, int heads, int d, void* out, long long out_ld,
+                       rc_stream_t stream);
 
 #ifdef __cplusplus
 }

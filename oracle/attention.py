@@ -26,7 +26,7 @@ def window_bounds(coord, extent, window):
 
 
 def routed_attention(q, ck, cv, pk, pv, slots, past_positions, query_positions, cos, sin,
-                     height, width, window_h, window_w, dtype="bf16"):
+                     height, width, window_h, window_w, dtype="bf16", compute_dtype=np.float64):
     """Arrays are [B, tokens, heads, d] float32 holding bf16 (or fp16, with
     dtype="fp16") values; returns the same shape rounded to that dtype."""
     q = np.asarray(q, np.float32)
@@ -43,7 +43,7 @@ def routed_attention(q, ck, cv, pk, pv, slots, past_positions, query_positions, 
                & (xs[None, :] >= left[:, None]) & (xs[None, :] < left[:, None] + ww))
     out = np.zeros_like(q)
     for b in range(bsz):
-        qr = apply_temporal(q[b], qpos, cos, sin, span, dtype).astype(np.float64)
+        qr = apply_temporal(q[b], qpos, cos, sin, span, dtype).astype(compute_dtype)
         keys, vals, masks = [], [], []
         for s, p in zip(slots, ppos):
             if s < 0:
@@ -56,8 +56,8 @@ def routed_attention(q, ck, cv, pk, pv, slots, past_positions, query_positions, 
             keys.append(apply_temporal(ck[b, f * span:(f + 1) * span], [qpos[f]], cos, sin, span, dtype))
             vals.append(cv[b, f * span:(f + 1) * span])
             masks.append(allowed)
-        kk = np.concatenate(keys, 0).astype(np.float64)   # [nk, heads, d]
-        vv = np.concatenate(vals, 0).astype(np.float64)
+        kk = np.concatenate(keys, 0).astype(compute_dtype)   # [nk, heads, d]
+        vv = np.concatenate(vals, 0).astype(compute_dtype)
         mm = np.concatenate(masks, 1)                      # [span, nk]
         mask = np.tile(mm, (frames, 1))                    # [nq, nk]
         scale = d ** -0.5
@@ -71,15 +71,15 @@ def routed_attention(q, ck, cv, pk, pv, slots, past_positions, query_positions, 
     return round_to(out, dtype)
 
 
-def plain_attention(q, k, v):
+def plain_attention(q, k, v, compute_dtype=np.float64):
     """Unmasked SDPA (cross-attention, recavsr_infer/runtime/transformer.py:123-128).
     q [N, heads, d], k/v [L, heads, d] -> bf16-valued [N, heads, d]."""
-    q = np.asarray(q, np.float64)
-    k = np.asarray(k, np.float64)
-    v = np.asarray(v, np.float64)
+    q = np.asarray(q, compute_dtype)
+    k = np.asarray(k, compute_dtype)
+    v = np.asarray(v, compute_dtype)
     out = np.empty(q.shape, np.float32)
     for h in range(q.shape[1]):
-        sc = (q[:, h] @ k[:, h].T) * q.shape[-1] ** -0.5
+        sc = (q[:, h] @ k[:, h].T) * compute_dtype(q.shape[-1] ** -0.5)
         sc -= sc.max(1, keepdims=True)
         p = np.exp(sc)
         p /= p.sum(1, keepdims=True)

@@ -43,24 +43,28 @@ def gelu_tanh(x):
 
 
 class QuantLinear:
-    """NVFP4Linear with the weight quantized once (nvfp4.py:82-84)."""
+    """NVFP4Linear with the weight quantized once (nvfp4.py:82-84).
+    matmul_dtype float64 for parity checks, float32 for the timed CPU baseline."""
 
-    def __init__(self, weight, bias):
+    def __init__(self, weight, bias, matmul_dtype=np.float64):
         self.n, self.k = weight.shape
         self.codes, self.scales = nvfp4.quantize(np.asarray(weight, np.float32))
         self.bias = None if bias is None else np.asarray(bias, np.float32)
+        self.dtype = matmul_dtype
+        self.w = nvfp4.dequantize(self.codes, self.scales, self.n, self.k).astype(matmul_dtype)
 
     def __call__(self, x):
         x = np.asarray(x, np.float32)
         shape = x.shape
         a = x.reshape(-1, self.k)
         ac, asf = nvfp4.quantize(a)
-        out = nvfp4.nvfp4_mm(ac, asf, self.codes, self.scales, self.bias, a.shape[0], self.n, self.k)
+        out = nvfp4.nvfp4_mm(ac, asf, None, None, self.bias, a.shape[0], self.n, self.k,
+                             dtype=self.dtype, b_dequantized=self.w)
         return out.reshape(*shape[:-1], self.n)
 
 
 def block_forward(p, hidden, past_key, past_value, slots, past_positions, query_positions,
-                  height, width, window, heads=24):
+                  height, width, window, heads=24, matmul_dtype=np.float64):
     """p: dict of float32 weights (bf16 values) -- modulation [6, dim] fp32,
     {q,k,v,o,cq,co,up,down}_{w,b}, norm_q/norm_k/cnorm_q weights, norm2_{w,b},
     cross_k/cross_v [L, heads, d], temporal_cos/sin, spatial_cos/sin [HW, d].
@@ -82,12 +86,12 @@ def block_forward(p, hidden, past_key, past_value, slots, past_positions, query_
     v = v.reshape(n, heads, d)
     out = routed_attention(q[None], k[None], v[None], past_key[None], past_value[None], slots,
                            past_positions, query_positions, p["temporal_cos"], p["temporal_sin"],
-                           height, width, window[0], window[1])[0]
+                           height, width, window[0], window[1], compute_dtype=matmul_dtype)[0]
     o = lin["o"](out.reshape(n, dim))
     h = bf16_round(h + o * gate)
     norm = bf16_round(layer_norm(h, p["norm2_w"], p["norm2_b"]))
     cq = rms_norm(lin["cq"](norm), p["cnorm_q"]).reshape(n, heads, d)
-    co = plain_attention(cq, p["cross_k"], p["cross_v"]).reshape(n, dim)
+    co = plain_attention(cq, p["cross_k"], p["cross_v"], compute_dtype=matmul_dtype).reshape(n, dim)
     h = bf16_round(h + lin["co"](co))
     norm = bf16_round(layer_norm(h) * (1 + cscale) + cshift)
     up = bf16_round(gelu_tanh(lin["up"](norm)))

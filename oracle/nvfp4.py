@@ -77,11 +77,12 @@ def dequantize(packed: np.ndarray, flat_scales: np.ndarray, m: int, k: int) -> n
 
 
 def nvfp4_mm(a_packed, a_scales, b_packed, b_scales, bias, m: int, n: int, k: int,
-             alpha: float = 1.0) -> np.ndarray:
-    """bf16(alpha * dequant(A) @ dequant(B)^T + bias) as float32 values."""
-    a = dequantize(a_packed, a_scales, m, k).astype(np.float64)
-    b = dequantize(b_packed, b_scales, n, k).astype(np.float64)
-    acc = (a @ b.T) * alpha
+             alpha: float = 1.0, dtype=np.float64, b_dequantized=None) -> np.ndarray:
+    """bf16(alpha * dequant(A) @ dequant(B)^T + bias) as float32 values.
+    dtype float64 (default) for parity checks; float32 for the timed CPU baseline."""
+    a = dequantize(a_packed, a_scales, m, k).astype(dtype)
+    b = (dequantize(b_packed, b_scales, n, k) if b_dequantized is None else b_dequantized).astype(dtype)
+    acc = (a @ b.T) * dtype(alpha)
     if bias is not None:
-        acc = acc + np.asarray(bias, dtype=np.float64)[None, :]
+        acc = acc + np.asarray(bias, dtype=dtype)[None, :]
     return bf16_round(acc.astype(np.float32))

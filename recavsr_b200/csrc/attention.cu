@@ -42,6 +42,7 @@ constexpr float kRescaleThreshold = 8.0f;   // log2 units
 
 struct AttnParams {
   int T, H, W, heads, QT, CAP;
+  int Tq;                       // query tokens (dense mode validity)
   int wh, ww;                   // effective window (clamped to the grid)
   int local;                    // 0 dense, 1 local
   int n_qtiles;                 // query tiles per head
@@ -273,7 +274,7 @@ attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
     int qrow = -1, qy = 0, qx = 0;
     if (!p.local) {
       const int t = q_row0 + r;
-      if (t < p.QT * p.T) qrow = t;
+      if (t < p.Tq) qrow = t;
       qy = 0;
       qx = 0;
     } else {
@@ -574,7 +575,7 @@ int rc_paired_attention(const void* q, const void* ck, const void* cv, const voi
       tpv = tcv;
     }
     AttnParams p{};
-    p.T = T; p.H = H; p.W = W; p.heads = heads; p.QT = QT; p.CAP = CAP;
+    p.T = T; p.H = H; p.W = W; p.heads = heads; p.QT = QT; p.CAP = CAP; p.Tq = QT * T;
     p.wh = wh; p.ww = ww; p.local = local;
     p.scale_log2 = (float)(1.0 / sqrt((double)d) * 1.4426950408889634);
     p.slots = slots;
@@ -589,6 +590,60 @@ int rc_paired_attention(const void* q, const void* ck, const void* cv, const voi
     }
     dim3 grid(p.n_qtiles, heads);
     attention_kernel<<<grid, kThreads, SmemLayout::kAlloc, stream>>>(tq, tk, tpv, tcv, p);
+    if ((r = rc::check_launch(what))) return r;
+  }
+  return RC_OK;
+}
+
+// Unmasked attention without rotary embedding and without cache, e.g. the
+// cross-attention of recavsr_infer/runtime/transformer.py:123-128 (queries
+// over the 512 precomputed prompt keys). strides[9]: (batch, token, head)
+// element strides of q, k, v. Runs the same tcgen05 kernel on the inputs
+// directly (no workspace).
+int rc_cross_attention(const void* q, const void* k, const void* v, const long long* strides, int B,
+                       int Nq, int Nk, int heads, int d, void* out, long long out_ld,
+                       cudaStream_t stream) {
+  const char* what = "rc_cross_attention";
+  if (B <= 0 || Nq < 0 || Nk <= 0 || heads <= 0 || !strides)
+    return rc::set_error(RC_ERR_ARG, "%s: bad geometry", what);
+  if (d != kD)
+    return rc::set_error(RC_ERR_UNSUPPORTED, "%s: head_dim %d (the tcgen05 kernel supports 128)", what, d);
+  if (!q || !k || !v || !out) return rc::set_error(RC_ERR_ARG, "%s: null pointer", what);
+  for (int t = 0; t < 3; ++t)
+    if ((B > 1 && strides[3 * t] % 8) || strides[3 * t + 1] % 8 || strides[3 * t + 2] % 8)
+      return rc::set_error(RC_ERR_ARG, "%s: strides must be multiples of 8 elements (16 bytes)", what);
+  if (!al16(q) || !al16(k) || !al16(v) || !al16(out) || out_ld % 8)
+    return rc::set_error(RC_ERR_ARG, "%s: tensors must be 16-byte aligned", what);
+  if (Nq == 0) return RC_OK;
+  if (!g_attr_set) {
+    if (cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             SmemLayout::kAlloc) != cudaSuccess)
+      return rc::set_error(RC_ERR_CUDA, "%s: shared memory attribute", what);
+    g_attr_set = 1;
+  }
+  for (int b = 0; b < B; ++b) {
+    const __nv_bfloat16* qb = reinterpret_cast<const __nv_bfloat16*>(q) + b * strides[0];
+    const __nv_bfloat16* kb = reinterpret_cast<const __nv_bfloat16*>(k) + b * strides[3];
+    const __nv_bfloat16* vb = reinterpret_cast<const __nv_bfloat16*>(v) + b * strides[6];
+    CUtensorMap tq, tk, tv;
+    const uint64_t dims[3] = {(uint64_t)kD, (uint64_t)heads, (uint64_t)Nq};
+    const uint64_t str[2] = {(uint64_t)strides[2] * 2, (uint64_t)strides[1] * 2};
+    const uint32_t box[3] = {64, 1, kBM};
+    int r = rc::encode_tmap(&tq, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<__nv_bfloat16*>(qb),
+                            dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B, what);
+    if (r) return r;
+    if ((r = make_view(&tk, kb, strides[4], strides[5], heads, Nk, 1, Nk, 1, false, what))) return r;
+    if ((r = make_view(&tv, vb, strides[7], strides[8], heads, Nk, 1, Nk, 1, false, what))) return r;
+    AttnParams p{};
+    p.T = Nk; p.H = 1; p.W = Nk; p.heads = heads; p.QT = 1; p.CAP = 0; p.Tq = Nq;
+    p.wh = 1; p.ww = Nk; p.local = 0;
+    p.scale_log2 = (float)(1.0 / sqrt((double)d) * 1.4426950408889634);
+    p.slots = nullptr;
+    p.out = reinterpret_cast<__nv_bfloat16*>(out) + (long long)b * Nq * out_ld;
+    p.out_ld = out_ld;
+    p.n_qtiles = (Nq + kBM - 1) / kBM;
+    dim3 grid(p.n_qtiles, heads);
+    attention_kernel<<<grid, kThreads, SmemLayout::kAlloc, stream>>>(tq, tk, tv, tv, p);
     if ((r = rc::check_launch(what))) return r;
   }
   return RC_OK;

@@ -268,6 +268,30 @@ __global__ void kv_commit_kernel(CommitArgs a) {
   }
 }
 
+// Same copy with the plane plan read from device memory:
+// plan = [n, src0, dst0, src1, dst1, ...] (n <= max_planes), so a captured
+// graph stays valid while the routing changes between replays.
+__global__ void kv_commit_planned_kernel(CommitArgs a, const int* __restrict__ plan) {
+  const int n = min(plan[0], a.n);
+  const int vec_per_row = a.row_bytes >> 4;
+  const long long per_plane = (long long)a.span * vec_per_row;
+  const long long total = 2LL * a.n * per_plane;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int t = (int)(i / (a.n * per_plane));
+    const long long r = i % (a.n * per_plane);
+    const int c = (int)(r / per_plane);
+    if (c >= n) continue;
+    const int sp = plan[1 + 2 * c], dp = plan[2 + 2 * c];
+    if (sp < 0 || dp < 0 || dp >= a.dst_plane[0]) continue;   // dst_plane[0] = slot capacity
+    const long long q = r % per_plane;
+    const long long row = q / vec_per_row, v = q % vec_per_row;
+    const uint4* s = reinterpret_cast<const uint4*>(a.src[t] + ((long long)sp * a.span + row) * a.src_ld[t]);
+    uint4* dd = reinterpret_cast<uint4*>(a.dst[t] + ((long long)dp * a.span + row) * a.dst_ld[t]);
+    dd[v] = __ldg(s + v);
+  }
+}
+
 int grid_for(long long work, int threads) {
   long long b = (work + threads - 1) / threads;
   return (int)(b < 1 ? 1 : (b > 148LL * 16 ? 148LL * 16 : b));
@@ -395,6 +419,32 @@ int rc_kv_commit(const void* src_k, const void* src_v, long long src_ld_bytes, v
   a.row_bytes = row_bytes;
   kv_commit_kernel<<<grid_for(2LL * n_planes * span * (row_bytes / 16), 256), 256, 0, stream>>>(a);
   return rc::check_launch("rc_kv_commit");
+}
+
+// Device-planned variant: plan = [n, (src plane, dst slot) x n] in device
+// memory, at most max_planes copies, slots < capacity.
+int rc_kv_commit_planned(const void* src_k, const void* src_v, long long src_ld_bytes, void* dst_k,
+                         void* dst_v, long long dst_ld_bytes, int row_bytes, int span,
+                         int max_planes, int capacity, const int* plan, cudaStream_t stream) {
+  if (max_planes < 0 || max_planes > 8 || span <= 0 || row_bytes <= 0 || row_bytes % 16 || capacity < 0)
+    return rc::set_error(RC_ERR_ARG, "rc_kv_commit_planned: bad shape");
+  if (max_planes == 0 || capacity == 0) return RC_OK;
+  if (!plan || !aligned16(src_k) || !aligned16(src_v) || !aligned16(dst_k) || !aligned16(dst_v) ||
+      src_ld_bytes % 16 || dst_ld_bytes % 16)
+    return rc::set_error(RC_ERR_ARG, "rc_kv_commit_planned: rows must be 16-byte aligned");
+  CommitArgs a{};
+  a.src[0] = reinterpret_cast<const uint8_t*>(src_k);
+  a.src[1] = reinterpret_cast<const uint8_t*>(src_v);
+  a.dst[0] = reinterpret_cast<uint8_t*>(dst_k);
+  a.dst[1] = reinterpret_cast<uint8_t*>(dst_v);
+  a.src_ld[0] = a.src_ld[1] = src_ld_bytes;
+  a.dst_ld[0] = a.dst_ld[1] = dst_ld_bytes;
+  a.dst_plane[0] = capacity;
+  a.n = max_planes;
+  a.span = span;
+  a.row_bytes = row_bytes;
+  kv_commit_planned_kernel<<<grid_for(2LL * max_planes * span * (row_bytes / 16), 256), 256, 0, stream>>>(a, plan);
+  return rc::check_launch("rc_kv_commit_planned");
 }
 
 }  // extern "C"

@@ -35,7 +35,7 @@ def _check(q, ck, cv, pk, pv, slots, past_positions, query_positions, cos, sin, 
         raise ValueError("Rolling RoPE metadata mismatch.")
     if min(window_h, window_w) <= 0:
         raise ValueError("Spatial windows must be positive.")
-    if any(x.stride(-1) != 1 for x in (q, ck, cv, pk, pv)):
+    if any(x.stride(-1) != 1 for x in (q, ck, cv, pk, pv) if x.numel()):
         raise ValueError("Head dimensions must be contiguous.")
     return frames
 
