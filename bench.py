@@ -257,6 +257,8 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--eager", action="store_true", help="no CUDA graph (launch from Python)")
+    ap.add_argument("--no-kernel-timing", action="store_true",
+                    help="skip the per-kernel roofline timing (e.g. for an ncu launch list)")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
@@ -327,7 +329,7 @@ def main():
         tt = torch.tensor([t, te], device=device)
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         t, te = float(tt[0]), float(tt[1])
-    kr = kernel_roofline(stack, torch) if rank == 0 else None
+    kr = kernel_roofline(stack, torch) if rank == 0 and not args.no_kernel_timing else None
     att_flops, planes = attention_flops_per_block(stack)
     if world > 1:
         dist.barrier()
@@ -338,6 +340,9 @@ def main():
     value = tokens / t
     hbm, bf16_peak, bf16_sus, src = peaks()
     fp4_peak = 4 * bf16_peak
+    if kr is None:
+        kr = {"ffn_up_flops": 1.0, "ffn_up_s": float("inf"), "attn_flops": 1.0, "attn_s": float("inf"),
+              "attn_planes": 0}
     achieved = kr["ffn_up_flops"] / kr["ffn_up_s"] / 1e12
     cpu = None if args.no_cpu_baseline else cpu_baseline()
     launches_per_layer = 19   # 16 kernels + 3 scale-padding kernels (M % 128 != 0)

@@ -1,0 +1,130 @@
+"""Run one hot-path kernel at the benchmark's shapes, for profiling.
+
+    python -m recavsr_b200.profile_case gemm_up      # NVFP4 ffn_up 1760x14336x3072 (+GELU/NVFP4 epilogue)
+    python -m recavsr_b200.profile_case gemm_qkv     # NVFP4 QKV 1760x9216x3072
+    python -m recavsr_b200.profile_case gemm_down    # NVFP4 ffn_down 1760x3072x14336 (+gated residual)
+    python -m recavsr_b200.profile_case attention    # routed attention, 1760 queries, 4 past planes
+    python -m recavsr_b200.profile_case quant        # NVFP4 quantizer 1760x3072
+    python -m recavsr_b200.profile_case ln           # LayerNorm+AdaLN+NVFP4 1760x3072
+
+Each case allocates fresh inputs (a few hundred MB at most), runs the kernel
+`--reps` times and prints the mean CUDA-event time per launch.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+
+import torch
+
+from . import _lib
+from .runtime.nvfp4 import quantize, scale_numel
+
+M, DIM, FFN, HEADS, HD, H, W = 1760, 3072, 14336, 24, 128, 22, 40
+
+
+def _gemm(n, k, epi):
+    g = torch.Generator(device="cuda")
+    g.manual_seed(0)
+    a = torch.randn(M, k, generator=g, device="cuda").bfloat16()
+    w = (torch.randn(n, k, generator=g, device="cuda") * 0.02).bfloat16()
+    ac, asf = quantize(a)
+    wc, wsf = quantize(w)
+    bias = torch.zeros(n, dtype=torch.bfloat16, device="cuda")
+    out = torch.randn(M, n, generator=g, device="cuda").bfloat16()
+    gate = torch.ones(n, device="cuda")
+    qc = torch.empty(M, n // 2, dtype=torch.uint8, device="cuda")
+    qs = torch.empty(scale_numel(M, n), dtype=torch.uint8, device="cuda")
+    lib = _lib.library()
+
+    def run():
+        _lib.check(lib.rc_nvfp4_gemm(ac.data_ptr(), asf.data_ptr(), wc.data_ptr(), wsf.data_ptr(),
+                                     bias.data_ptr(), M, n, k, 1.0, epi,
+                                     None if epi == _lib.EPI_GELU_NVFP4 else out.data_ptr(), n,
+                                     gate.data_ptr(), qc.data_ptr(), qs.data_ptr(), 1.0,
+                                     _lib.stream()), "gemm")
+    return run, 2.0 * M * n * k, "TFLOP/s"
+
+
+def _attention(planes=4):
+    from .kernels.local_attention import routed_attention
+    from .runtime.block import rope_tables
+    g = torch.Generator(device="cuda")
+    g.manual_seed(0)
+    t = H * W
+    r = lambda *s: torch.randn(*s, generator=g, device="cuda").bfloat16()
+    q, k, v = r(1, 2 * t, HEADS, HD), r(1, 2 * t, HEADS, HD), r(1, 2 * t, HEADS, HD)
+    pk, pv = r(1, planes * t, HEADS, HD), r(1, planes * t, HEADS, HD)
+    slots = torch.arange(planes, dtype=torch.int32, device="cuda")
+    ppos = torch.arange(planes, dtype=torch.int32, device="cuda")
+    qpos = torch.tensor([planes, planes + 1], dtype=torch.int32, device="cuda")
+    tb = rope_tables(HD, H, W, "cuda")
+    out = torch.empty_like(q)
+
+    def run():
+        routed_attention(q, k, v, pk, pv, slots, ppos, qpos, tb["temporal_cos"], tb["temporal_sin"],
+                         H, W, H, W, out=out)
+    return run, 4.0 * HD * HEADS * (2 * t) * t * (planes + 2), "TFLOP/s"
+
+
+def _quant():
+    x = torch.randn(M, DIM, device="cuda").bfloat16()
+    codes = torch.empty(M, DIM // 2, dtype=torch.uint8, device="cuda")
+    sf = torch.empty(scale_numel(M, DIM), dtype=torch.uint8, device="cuda")
+    lib = _lib.library()
+
+    def run():
+        _lib.check(lib.rc_nvfp4_quantize(x.data_ptr(), M, DIM, DIM, 1.0, codes.data_ptr(), sf.data_ptr(),
+                                         _lib.stream()), "quant")
+    return run, M * DIM * 2.5625, "GB/s"
+
+
+def _ln():
+    x = torch.randn(M, DIM, device="cuda").bfloat16()
+    sh, sc = torch.randn(DIM, device="cuda"), torch.randn(DIM, device="cuda")
+    codes = torch.empty(M, DIM // 2, dtype=torch.uint8, device="cuda")
+    sf = torch.empty(scale_numel(M, DIM), dtype=torch.uint8, device="cuda")
+    lib = _lib.library()
+
+    def run():
+        _lib.check(lib.rc_ln_modulate_quant(x.data_ptr(), DIM, M, DIM, None, None, sh.data_ptr(),
+                                            sc.data_ptr(), 1e-6, None, 0, codes.data_ptr(),
+                                            sf.data_ptr(), 1.0, _lib.stream()), "ln")
+    return run, M * DIM * 2.5625, "GB/s"
+
+
+CASES = {
+    "gemm_up": lambda: _gemm(FFN, DIM, _lib.EPI_GELU_NVFP4),
+    "gemm_qkv": lambda: _gemm(3 * DIM, DIM, _lib.EPI_BIAS),
+    "gemm_o": lambda: _gemm(DIM, DIM, _lib.EPI_GATED_RESIDUAL),
+    "gemm_down": lambda: _gemm(DIM, FFN, _lib.EPI_GATED_RESIDUAL),
+    "attention": _attention,
+    "quant": _quant,
+    "ln": _ln,
+}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("case", choices=sorted(CASES))
+    ap.add_argument("--reps", type=int, default=20)
+    args = ap.parse_args()
+    run, work, unit = CASES[args.case]()
+    for _ in range(3):
+        run()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(args.reps):
+        run()
+    b.record()
+    b.synchronize()
+    dt = a.elapsed_time(b) / args.reps * 1e-3
+    rate = work / dt / (1e12 if unit == "TFLOP/s" else 1e9)
+    print(f"{args.case}: {dt * 1e6:.1f} us/launch, {rate:.1f} {unit}")
+    if _lib.read_device_error():
+        raise SystemExit("device error word set")
+
+
+if __name__ == "__main__":
+    main()

@@ -293,12 +293,12 @@ class _QuantLinear(nn.Module):
         return acc.float().to(torch.bfloat16).reshape(*x.shape[:-1], self.n)
 
 
-def gen_block(out):
+def gen_block(out, tag="block", dim=256, heads=2, ffn=512, H=4, W=6, enc_len=16, pseed=11,
+              iseed=12, cap=3, slots=(1, -1, 2), ppos=(4, 0, 5)):
     from recavsr_infer.runtime.rope import RollingRoPE
     from recavsr_infer.runtime.transformer import PreparedBlock
-    dim, heads, ffn, H, W = 256, 2, 512, 4, 6
     span = H * W
-    p = recipes.block_params(dim, heads, ffn)
+    p = recipes.block_params(dim, heads, ffn, enc_len=enc_len, seed=pseed)
     b = _Block(dim, heads, ffn)
     with torch.no_grad():
         names = {"q": b.attn1.to_q, "k": b.attn1.to_k, "v": b.attn1.to_v, "o": b.attn1.to_out[0],
@@ -323,21 +323,21 @@ def gen_block(out):
         for name, child in list(mod.named_children()):
             if isinstance(child, nn.Linear):
                 setattr(mod, name, _QuantLinear(child))
-    cap = 3
-    hidden, pk, pv = recipes.block_inputs(2 * span, cap * span, dim)
-    slots = torch.tensor([1, -1, 2], dtype=torch.int32)
-    ppos = torch.tensor([4, 0, 5], dtype=torch.int32)
+    hidden, pk, pv = recipes.block_inputs(2 * span, cap * span, dim, seed=iseed)
+    slots = torch.tensor(list(slots), dtype=torch.int32)
+    ppos = torch.tensor(list(ppos), dtype=torch.int32)
     qpos = torch.tensor([6, 7], dtype=torch.int32)
     with torch.inference_mode():
         h, k, v = core(t16(hidden), t16(pk).unflatten(2, (heads, -1)),
                        t16(pv).unflatten(2, (heads, -1)), slots, ppos, qpos)
-    out["block_hidden"] = bits(h)
-    out["block_k"] = bits(k)
-    out["block_v"] = bits(v)
-    out["block_modulation"] = core.modulation.detach().float().numpy()
-    out["block_cross_k"] = bits(core.cross_k.detach())
-    out["block_cross_v"] = bits(core.cross_v.detach())
-    out["block_meta"] = np.array([dim, heads, ffn, H, W, cap], np.int64)
+    out[f"{tag}_hidden"] = bits(h)
+    out[f"{tag}_k"] = bits(k)
+    out[f"{tag}_v"] = bits(v)
+    out[f"{tag}_modulation"] = core.modulation.detach().float().numpy()
+    out[f"{tag}_cross_k"] = bits(core.cross_k.detach())
+    out[f"{tag}_cross_v"] = bits(core.cross_v.detach())
+    out[f"{tag}_meta"] = np.array([dim, heads, ffn, H, W, cap, enc_len, pseed, iseed] + list(slots)
+                                  + list(ppos), np.int64)
 
 
 def main():
@@ -349,6 +349,8 @@ def main():
     gen_rope(out)
     gen_attention(out)
     gen_block(out)
+    gen_block(out, "block768", dim=768, heads=6, ffn=2048, H=8, W=12, enc_len=64, pseed=21,
+              iseed=22, cap=2, slots=(1, 0), ppos=(3, 4))
     np.savez_compressed(os.path.join(HERE, "reference_outputs.npz"), **out)
     with open(os.path.join(HERE, "router.json"), "w") as f:
         json.dump(gen_router(), f, separators=(",", ":"))

@@ -131,3 +131,29 @@ def test_rejects_bad_geometry():
     c = torch.zeros(22, 22, device="cuda")
     with pytest.raises(ValueError):
         paired_attention(q, q, q, e, e, i, i, qp, c, c, 4, 6, 2, 2)   # 3 frames
+
+
+@pytest.mark.parametrize("nq,nk,heads", [(192, 64, 6), (1760, 512, 24), (48, 16, 2)])
+def test_cross_attention(nq, nk, heads):
+    """Unmasked, rotary-free attention over the prompt keys (transformer.py:123-128)."""
+    import ctypes as C
+    from recavsr_b200 import _lib
+    rs = np.random.RandomState(nq + nk)
+    q = recipes.bf16_normal(rs, (nq, heads, 128))
+    k = recipes.bf16_normal(rs, (nk, heads, 128))
+    v = recipes.bf16_normal(rs, (nk, heads, 128))
+    dq, dk, dv = dev_bf16(q), dev_bf16(k), dev_bf16(v)
+    out = torch.empty(nq, heads, 128, dtype=torch.bfloat16, device="cuda")
+    hd = heads * 128
+    st = (C.c_longlong * 9)(0, hd, 128, 0, hd, 128, 0, hd, 128)
+    _lib.call("rc_cross_attention", dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), st, 1, nq, nk,
+              heads, 128, out.data_ptr(), hd, _lib.stream())
+    assert_no_device_error()
+    hs = [0, heads - 1]
+    ref = oatt.plain_attention(q[:, hs], k[:, hs], v[:, hs])
+    got = host(out)[:, hs]
+    assert np.abs(got - ref).max() <= ABS and max_rel(got, ref) <= REL
+
+
+def test_routed_attention_six_heads_small_plane():
+    _run(8, 12, 22, 40, 2, [1, 0], [3, 4], [5, 6], heads=6)
