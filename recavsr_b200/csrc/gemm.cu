@@ -12,13 +12,18 @@
 //   BF16 : plain bf16 linears.
 // Accumulation is fp32 in TMEM. One CTA per SM runs a persistent loop over
 // 128 x BN output tiles with warp roles: warp 0 = TMA producer, warp 1 = MMA
-// issuer (+ TMEM owner), warps 2-5 = epilogue (TMEM -> registers -> global).
+// issuer (+ TMEM owner), warps 2-9 = epilogue (TMEM -> registers -> global;
+// two warps per TMEM lane quadrant, each on half of the tile's columns). With
+// BN = 128 the accumulator is double-buffered in TMEM so the epilogue of one
+// tile overlaps the MMAs of the next.
 // Epilogues fuse the block's follow-up element-wise work:
 //   BIAS           out = bf16(acc*alpha + bias)
 //   GATED_RESIDUAL h   = bf16(h + bf16(acc*alpha + bias) * gate[n])   (in place)
 //   RESIDUAL       h   = bf16(h + bf16(acc*alpha + bias))            (in place)
 //   GELU_NVF4      y   = bf16(gelu_tanh(bf16(acc*alpha + bias))), quantized to
 //                  NVFP4 (16 columns = one block) for the next linear.
+#include <stdlib.h>
+
 #include "sm100.cuh"
 
 namespace {
@@ -28,7 +33,8 @@ enum Epi : int { EPI_BIAS = 0, EPI_GATED_RESIDUAL = 1, EPI_RESIDUAL = 2, EPI_GEL
 
 constexpr int BM = 128;
 constexpr int kRowBytes = 128;                     // K bytes per smem row / k-tile
-constexpr int kThreads = 192;                      // 6 warps
+constexpr int kEpiWarps = 8;                       // 2 per TMEM lane quadrant
+constexpr int kThreads = 64 + 32 * kEpiWarps;      // producer, MMA, epilogue warps
 constexpr int kSfAtomBytes = 512;                  // 128 rows x 4 scale bytes
 
 template <int KIND>
@@ -79,7 +85,7 @@ struct Smem {
   static constexpr int offSfa = offB + STAGES * kB;
   static constexpr int offSfb = offSfa + STAGES * kSfa;
   static constexpr int offBar = offSfb + STAGES * kSfb;
-  static constexpr int kBars = 2 * STAGES + 4 + 1;
+  static constexpr int kBars = 2 * STAGES + 6 + 1;
   static constexpr int kTotal = offBar + kBars * 8 + 16;
   static constexpr int kAlloc = kTotal + 1024;      // slack for 1024-byte alignment
 };
@@ -102,14 +108,16 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
   constexpr int kTmemCols = 512;
   constexpr int kSfaCols = 16;                       // 4 k-steps x 4 columns
   constexpr int kSfbCols = 4 * (BN / 32);            // 4 k-steps x BN/32 columns
+  constexpr int kAcc = BN == 128 ? 2 : 1;            // accumulator stages in TMEM
+  static_assert(kAcc * BN + 2 * (kSfaCols + kSfbCols) <= kTmemCols, "TMEM budget");
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::offBar);
   uint64_t* empty = full + STAGES;
-  uint64_t* acc_full = empty + STAGES;     // [1]
-  uint64_t* acc_empty = acc_full + 1;      // [1]
-  uint64_t* done = acc_empty + 1;          // [1]
+  uint64_t* acc_full = empty + STAGES;     // [2]
+  uint64_t* acc_empty = acc_full + 2;      // [2]
+  uint64_t* done = acc_empty + 2;          // [1]
   volatile int* abort_flag = reinterpret_cast<volatile int*>(done + 2);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 3);
 
@@ -122,8 +130,10 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
       sm100::mbar_init(&full[s], 1);
       sm100::mbar_init(&empty[s], 1);
     }
-    sm100::mbar_init(acc_full, 1);
-    sm100::mbar_init(acc_empty, 128);
+    for (int a = 0; a < 2; ++a) {
+      sm100::mbar_init(&acc_full[a], 1);
+      sm100::mbar_init(&acc_empty[a], 32 * kEpiWarps);
+    }
     sm100::mbar_init(done, 1);
     *abort_flag = 0;
     sm100::fence_mbar_init();
@@ -136,9 +146,9 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
   __syncthreads();
   sm100::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tmem_acc = tmem;                           // columns [0, BN)
-  const uint32_t tmem_sfa = tmem + BN;                      // 2 x kSfaCols
-  const uint32_t tmem_sfb = tmem + BN + 2 * kSfaCols;       // 2 x kSfbCols
+  const uint32_t tmem_acc = tmem;                                 // kAcc x BN columns
+  const uint32_t tmem_sfa = tmem + kAcc * BN;                     // 2 x kSfaCols
+  const uint32_t tmem_sfb = tmem + kAcc * BN + 2 * kSfaCols;      // 2 x kSfbCols
 
   auto fail = [&](unsigned int site) {
     rc::device_fail(kKernGemmNvf4 + (KIND == KIND_NVF4 ? 0 : 1), site);
@@ -213,12 +223,16 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
       else if constexpr (KIND == KIND_E4M3) idesc = sm100::idesc_e4m3(BM, BN);
       else idesc = sm100::idesc_bf16(BM, BN, 0, 0);
       int stage = 0;
-      uint32_t phase = 0, acc_phase = 0;
+      uint32_t phase = 0;
       int sf_buf = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-        if (!wait(acc_empty, acc_phase ^ 1, 2)) { ok = false; break; }
+      int local = 0;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++local) {
+        const int as = local % kAcc;
+        const uint32_t acc_parity = (uint32_t)((local / kAcc) & 1);
+        if (!wait(&acc_empty[as], acc_parity ^ 1, 2)) { ok = false; break; }
         sm100::tc_fence_after();
+        const uint32_t d_tmem = tmem_acc + as * BN;
         for (int kt = 0; kt < p.k_tiles; ++kt) {
           if (!wait(&full[stage], phase, 3)) { ok = false; break; }
           sm100::tc_fence_after();
@@ -238,7 +252,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
                                               sm100::desc_sf_rows(sb0 + (r * 4 + j) * kSfAtomBytes));
             }
             for (int j = 0; j < steps; ++j) {
-              sm100::mma_nvf4_ss(tmem_acc, sm100::desc_kmajor_sw128(a0 + 32 * j),
+              sm100::mma_nvf4_ss(d_tmem, sm100::desc_kmajor_sw128(a0 + 32 * j),
                                  sm100::desc_kmajor_sw128(b0 + 32 * j), idesc, sfa_t + 4 * j,
                                  sfb_t + j * (BN / 32), (kt | j) != 0);
             }
@@ -249,10 +263,10 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
             steps = min(kMmaPerTile, rem);
             for (int j = 0; j < steps; ++j) {
               if constexpr (KIND == KIND_E4M3)
-                sm100::mma_f8f6f4_ss(tmem_acc, sm100::desc_kmajor_sw128(a0 + 32 * j),
+                sm100::mma_f8f6f4_ss(d_tmem, sm100::desc_kmajor_sw128(a0 + 32 * j),
                                      sm100::desc_kmajor_sw128(b0 + 32 * j), idesc, (kt | j) != 0);
               else
-                sm100::mma_f16_ss(tmem_acc, sm100::desc_kmajor_sw128(a0 + 32 * j),
+                sm100::mma_f16_ss(d_tmem, sm100::desc_kmajor_sw128(a0 + 32 * j),
                                   sm100::desc_kmajor_sw128(b0 + 32 * j), idesc, (kt | j) != 0);
             }
           }
@@ -260,8 +274,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }
         if (!ok) break;
-        sm100::tc_commit(acc_full);
-        acc_phase ^= 1;
+        sm100::tc_commit(&acc_full[as]);
       }
       // Make sure no MMA is still writing TMEM when the CTA tears down.
       sm100::tc_commit(done);
@@ -270,22 +283,25 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
   } else {
     // ------------------------------------------------------------ epilogue
     const int quad = warp & 3;                 // TMEM lane quadrant of this warp
+    const int half = (warp - 2) >> 2;          // which half of the tile's columns
     const int row_in_tile = quad * 32 + lane;
-    uint32_t acc_phase = 0;
+    constexpr int kCols = BN / 2;
     float alpha = p.alpha;
     if constexpr (KIND == KIND_E4M3) {
       if (p.alpha_ptr_a) alpha = __fmul_rn(alpha, *p.alpha_ptr_a);
       if (p.alpha_ptr_b) alpha = __fmul_rn(alpha, *p.alpha_ptr_b);
     }
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+    int local = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
       const int mb = tile % p.m_blocks, nb = tile / p.m_blocks;
-      if (!__all_sync(0xffffffffu, wait(acc_full, acc_phase, 4))) break;
+      const int as = local % kAcc;
+      if (!__all_sync(0xffffffffu, wait(&acc_full[as], (uint32_t)((local / kAcc) & 1), 4))) break;
       sm100::tc_fence_after();
       const int row = mb * BM + row_in_tile;
       const bool row_ok = row < p.M;
-      const uint32_t t_row = tmem_acc + ((uint32_t)(quad * 32) << 16);
+      const uint32_t t_row = tmem_acc + as * BN + ((uint32_t)(quad * 32) << 16);
 #pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += 16) {
+      for (int c0 = half * kCols; c0 < (half + 1) * kCols; c0 += 16) {
         uint32_t r[16];
         sm100::tmem_ld16(t_row + c0, r);
         sm100::tmem_ld_wait();
@@ -296,11 +312,21 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
           if constexpr (EPI == EPI_GELU_NVF4) p.q_sf[rc::sf_offset(row, n0 >> 4, (p.N + 63) >> 6)] = 0;
           continue;
         }
-        float v[16];
+        float v[16], bias[16];
+        if (p.bias) {
+          const uint4* bp = reinterpret_cast<const uint4*>(p.bias + n0);
+          const uint4 b0 = __ldg(bp), b1 = __ldg(bp + 1);
+          const uint32_t bw[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            bias[2 * j] = __uint_as_float(bw[j] << 16);
+            bias[2 * j + 1] = __uint_as_float(bw[j] & 0xffff0000u);
+          }
+        }
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
           float x = __fmul_rn(__uint_as_float(r[j]), alpha);
-          if (p.bias) x = __fadd_rn(x, __bfloat162float(p.bias[n0 + j]));
+          if (p.bias) x = __fadd_rn(x, bias[j]);
           v[j] = rc::bf16_to_float(rc::bf16_bits(x));
         }
         if constexpr (EPI == EPI_GATED_RESIDUAL || EPI == EPI_RESIDUAL) {
@@ -308,10 +334,19 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
           const uint4 h0 = *reinterpret_cast<const uint4*>(hp);
           const uint4 h1 = *reinterpret_cast<const uint4*>(hp + 8);
           const uint32_t hw[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+          float gt[16];
+          if constexpr (EPI == EPI_GATED_RESIDUAL) {
+            const float4* gp = reinterpret_cast<const float4*>(p.gate + n0);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const float4 g4 = __ldg(gp + j);
+              gt[4 * j] = g4.x; gt[4 * j + 1] = g4.y; gt[4 * j + 2] = g4.z; gt[4 * j + 3] = g4.w;
+            }
+          }
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
             const float h = __uint_as_float((j & 1) ? (hw[j >> 1] & 0xffff0000u) : (hw[j >> 1] << 16));
-            const float add = (EPI == EPI_GATED_RESIDUAL) ? __fmul_rn(v[j], p.gate[n0 + j]) : v[j];
+            const float add = (EPI == EPI_GATED_RESIDUAL) ? __fmul_rn(v[j], gt[j]) : v[j];
             v[j] = __fadd_rn(h, add);
           }
         }
@@ -345,8 +380,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
         dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
       }
       sm100::tc_fence_before();
-      sm100::mbar_arrive(acc_empty);
-      acc_phase ^= 1;
+      sm100::mbar_arrive(&acc_empty[as]);
     }
   }
 
@@ -399,6 +433,18 @@ int dispatch_epi(int epi, const CUtensorMap& ta, const CUtensorMap& tb, const Ge
   return rc::set_error(RC_ERR_ARG, "%s: unknown epilogue %d", what, epi);
 }
 
+// Tile width: BN = 128 (double-buffered accumulators, epilogue overlapped) by
+// default; RECAVSR_GEMM_BN=256 selects 128x256 tiles where N allows.
+bool gemm_prefer_wide(int epi) {
+  static int choice = -1;
+  if (choice < 0) {
+    const char* e = getenv("RECAVSR_GEMM_BN");
+    choice = (e && atoi(e) == 256) ? 1 : 0;
+  }
+  (void)epi;
+  return choice == 1;
+}
+
 // Shared argument checks + tensor maps; `elem_bytes_x2` = 2 * bytes/element
 // (1 for fp4, 2 for fp8, 4 for bf16).
 int run_gemm(int kind, int epi, const void* a, const void* b, int M, int N, int K,
@@ -421,7 +467,7 @@ int run_gemm(int kind, int epi, const void* a, const void* b, int M, int N, int 
   CUtensorMap ta, tb;
   const uint64_t da[2] = {row_bytes, (uint64_t)M}, db[2] = {row_bytes, (uint64_t)N};
   const uint64_t sa[1] = {row_bytes}, sb[1] = {row_bytes};
-  const bool wide = (N % 256 == 0) && (M > 0);
+  const bool wide = (N % 256 == 0) && gemm_prefer_wide(epi);
   const uint32_t boxa[2] = {128, 128}, boxb[2] = {128, (uint32_t)(wide ? 256 : 128)};
   int r = rc::encode_tmap(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(a), da, sa, boxa,
                           CU_TENSOR_MAP_SWIZZLE_128B, what);

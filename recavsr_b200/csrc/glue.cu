@@ -1,8 +1,9 @@
 // Row-wise glue around the DiT linears: LayerNorm (+affine) (+AdaLN
 // modulation) with an optional fused NVFP4 quantizer, RMSNorm across heads
 // with the spatial rotary embedding, the temporal rotary embedding, and the
-// KV-cache plane commit. One warp per row; the row stays in registers as raw
-// bf16 (N <= 4096), so each input byte is read from HBM once.
+// KV-cache plane commit. Row kernels run one CTA per row and one thread per
+// 16-element quantization block (N <= 4096), so the row stays in registers and
+// each input byte is read from HBM once.
 //
 // Numerics follow recavsr_infer/runtime/transformer.py:88-133 in eager order:
 //   LN in fp32 (two-pass mean / variance, rsqrt(var + eps)), then
@@ -13,7 +14,6 @@
 
 namespace {
 
-constexpr int kMaxChunks = 16;  // uint4 (8 x bf16) per lane -> N <= 4096
 
 __device__ __forceinline__ void unpack8(const uint4& v, float (&f)[8]) {
   const uint32_t w[4] = {v.x, v.y, v.z, v.w};
@@ -46,94 +46,124 @@ struct LnArgs {
   int M, N;
 };
 
-__global__ void __launch_bounds__(256) ln_modulate_kernel(LnArgs a) {
-  const int lane = threadIdx.x & 31;
-  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  if (row >= a.M) return;
-  const int nch = a.N >> 3;
-  const uint4* src = reinterpret_cast<const uint4*>(a.x + (size_t)row * a.ldx);
-  uint4 raw[kMaxChunks];
+// Block-wide sum over up to 8 warps (blockDim <= 256).
+__device__ __forceinline__ float block_sum(float v, float* red) {
+  v = warp_sum(v);
+  const int w = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red[w] = v;
+  __syncthreads();
+  float t = 0.f;
+  for (int i = 0; i < nw; ++i) t += red[i];
+  return t;
+}
+
+__device__ __forceinline__ void load16(const __nv_bfloat16* p, float (&f)[16]) {
+  const uint4* q = reinterpret_cast<const uint4*>(p);
+  float a[8], b[8];
+  unpack8(__ldg(q), a);
+  unpack8(__ldg(q + 1), b);
 #pragma unroll
-  for (int i = 0; i < kMaxChunks; ++i) {
-    const int c = lane + 32 * i;
-    raw[i] = c < nch ? __ldg(src + c) : make_uint4(0, 0, 0, 0);
+  for (int j = 0; j < 8; ++j) { f[j] = a[j]; f[8 + j] = b[j]; }
+}
+__device__ __forceinline__ void loadf16(const float* p, float (&f)[16]) {
+  const float4* q = reinterpret_cast<const float4*>(p);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float4 v = __ldg(q + j);
+    f[4 * j] = v.x; f[4 * j + 1] = v.y; f[4 * j + 2] = v.z; f[4 * j + 3] = v.w;
+  }
+}
+
+// NVFP4 encode of one 16-element block held by this thread; returns the scale
+// byte and writes the 8 code bytes. Thread t of the row owns k-block t.
+__device__ __forceinline__ uint8_t quant16(const float (&f)[16], float g, uint2& packed) {
+  float amax = 0.f;
+#pragma unroll
+  for (int j = 0; j < 16; ++j) amax = fmaxf(amax, fabsf(f[j]));
+  float sc = __fmul_rn(__fdiv_rn(amax, 6.0f), g);
+  sc = sc < 0.001953125f ? 0.001953125f : sc;
+  const uint8_t sfb = rc::e4m3_from_float(sc);
+  const float sd = rc::e4m3_to_float(sfb);
+  uint32_t lo = 0, hi = 0;
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    const uint32_t c = rc::e2m1_code(__fdiv_rn(__fmul_rn(f[j], g), sd));
+    if (j < 8) lo |= c << (4 * j);
+    else hi |= c << (4 * (j - 8));
+  }
+  packed = make_uint2(lo, hi);
+  return sfb;
+}
+
+// Stores the scale bytes of 4 consecutive k-blocks (threads 4a..4a+3) as one word.
+__device__ __forceinline__ void store_sf4(uint8_t* sf, int row, int kb, int katoms, uint8_t b, bool live) {
+  const uint32_t b0 = b;
+  const uint32_t b1 = __shfl_down_sync(0xffffffffu, b0, 1);
+  const uint32_t b2 = __shfl_down_sync(0xffffffffu, b0, 2);
+  const uint32_t b3 = __shfl_down_sync(0xffffffffu, b0, 3);
+  if (live && (kb & 3) == 0)
+    *reinterpret_cast<uint32_t*>(sf + rc::sf_offset(row, kb, katoms)) =
+        b0 | (b1 << 8) | (b2 << 16) | (b3 << 24);
+}
+
+// One CTA per row, one thread per 16-element block (N/16 threads).
+__global__ void __launch_bounds__(256) ln_modulate_kernel(LnArgs a) {
+  __shared__ float red[8];
+  const int row = blockIdx.x;
+  const int t = threadIdx.x;
+  const int nkb = a.N >> 4;
+  const bool live = t < nkb;
+  const int n0 = t * 16;
+  float f[16];
+  if (live) load16(a.x + (size_t)row * a.ldx + n0, f);
+  else {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) f[j] = 0.f;
   }
   float s = 0.f;
 #pragma unroll
-  for (int i = 0; i < kMaxChunks; ++i) {
-    float f[8];
-    unpack8(raw[i], f);
-#pragma unroll
-    for (int j = 0; j < 8; ++j) s += f[j];
-  }
-  const float mean = __fdiv_rn(warp_sum(s), (float)a.N);
+  for (int j = 0; j < 16; ++j) s += f[j];
+  const float mean = __fdiv_rn(block_sum(s, red), (float)a.N);
   float m2 = 0.f;
+  if (live) {
 #pragma unroll
-  for (int i = 0; i < kMaxChunks; ++i) {
-    if (lane + 32 * i < nch) {
-      float f[8];
-      unpack8(raw[i], f);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const float d = f[j] - mean;
-        m2 = fmaf(d, d, m2);
-      }
+    for (int j = 0; j < 16; ++j) {
+      const float d = f[j] - mean;
+      m2 = fmaf(d, d, m2);
     }
   }
-  const float var = __fdiv_rn(warp_sum(m2), (float)a.N);
+  const float var = __fdiv_rn(block_sum(m2, red), (float)a.N);
   const float rstd = rsqrtf(var + a.eps);
-  const int katoms = ((a.N >> 4) + 3) >> 2;
+  if (live) {
+    float w[16], b[16], sh[16], sc[16];
+    if (a.weight) load16(a.weight + n0, w);
+    if (a.bias) load16(a.bias + n0, b);
+    if (a.scale) loadf16(a.scale + n0, sc);
+    if (a.shift) loadf16(a.shift + n0, sh);
 #pragma unroll
-  for (int i = 0; i < kMaxChunks; ++i) {
-    const int c = lane + 32 * i;
-    if (32 * i >= nch) break;                 // warp-uniform
-    const bool live = c < nch;
-    float f[8];
-    unpack8(raw[i], f);
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const int n = c * 8 + j;
+    for (int j = 0; j < 16; ++j) {
       float y = __fmul_rn(f[j] - mean, rstd);
-      if (live) {
-        if (a.weight) y = __fmul_rn(y, __bfloat162float(a.weight[n]));
-        if (a.bias) y = __fadd_rn(y, __bfloat162float(a.bias[n]));
-        if (a.scale) y = __fmul_rn(y, __fadd_rn(1.0f, a.scale[n]));
-        if (a.shift) y = __fadd_rn(y, a.shift[n]);
-      }
-      f[j] = rc::bf16_to_float(rc::bf16_bits(y));  // bf16 rounding of the block output
+      if (a.weight) y = __fmul_rn(y, w[j]);
+      if (a.bias) y = __fadd_rn(y, b[j]);
+      if (a.scale) y = __fmul_rn(y, __fadd_rn(1.0f, sc[j]));
+      if (a.shift) y = __fadd_rn(y, sh[j]);
+      f[j] = rc::bf16_to_float(rc::bf16_bits(y));
     }
-    if (live && a.out)
-      *reinterpret_cast<uint4*>(a.out + (size_t)row * a.ldo + (size_t)c * 8) = pack8(f);
-    if (a.codes) {
-      // 16-element quant block = chunks (2b, 2b+1) = lanes (2b', 2b'+1) of this pass.
-      float amax = 0.f;
+    if (a.out) {
+      float lo[8], hi[8];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(f[j]));
-      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
-      float sc = __fmul_rn(__fdiv_rn(amax, 6.0f), a.g);
-      sc = sc < 0.001953125f ? 0.001953125f : sc;
-      const uint8_t sfb = rc::e4m3_from_float(sc);
-      const float sd = rc::e4m3_to_float(sfb);
-      uint32_t word = 0;
-#pragma unroll
-      for (int j = 0; j < 8; ++j)
-        word |= rc::e2m1_code(__fdiv_rn(__fmul_rn(f[j], a.g), sd)) << (4 * j);
-      if (live) *reinterpret_cast<uint32_t*>(a.codes + (size_t)row * (a.N >> 1) + (size_t)c * 4) = word;
-      // Gather the 4 scale bytes of a k-atom (lanes 8g, 8g+2, 8g+4, 8g+6).
-      const uint32_t b0 = sfb;
-      const uint32_t b1 = __shfl_down_sync(0xffffffffu, b0, 2);
-      const uint32_t b2 = __shfl_down_sync(0xffffffffu, b0, 4);
-      const uint32_t b3 = __shfl_down_sync(0xffffffffu, b0, 6);
-      if (live && (lane & 7) == 0) {
-        const int kb = c >> 1;  // first of 4 blocks
-        const size_t off = rc::sf_offset(row, kb, katoms);
-        // Blocks beyond N/16 inside the last atom are zero padding.
-        const int nkb = a.N >> 4;
-        uint32_t w = b0 | ((kb + 1 < nkb ? b1 : 0u) << 8) | ((kb + 2 < nkb ? b2 : 0u) << 16) |
-                     ((kb + 3 < nkb ? b3 : 0u) << 24);
-        *reinterpret_cast<uint32_t*>(a.sf + off) = w;
-      }
+      for (int j = 0; j < 8; ++j) { lo[j] = f[j]; hi[j] = f[8 + j]; }
+      uint4* dst = reinterpret_cast<uint4*>(a.out + (size_t)row * a.ldo + n0);
+      dst[0] = pack8(lo);
+      dst[1] = pack8(hi);
     }
+  }
+  if (a.codes) {
+    uint2 packed;
+    const uint8_t sfb = quant16(f, a.g, packed);
+    if (live) *reinterpret_cast<uint2*>(a.codes + (size_t)row * (a.N >> 1) + (size_t)t * 8) = packed;
+    store_sf4(a.sf, row, t, (nkb + 3) >> 2, live ? sfb : 0, live);
   }
 }
 
@@ -159,56 +189,51 @@ struct RmsArgs {
   int M, N, d, span;
 };
 
+// One CTA per (row, tensor), one thread per 16 elements.
 __global__ void __launch_bounds__(256) rmsnorm_rope_kernel(RmsArgs a) {
-  const int lane = threadIdx.x & 31;
-  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  const int t = blockIdx.y;
-  if (row >= a.M) return;
-  const int nch = a.N >> 3;
-  const uint4* src = reinterpret_cast<const uint4*>(a.x[t] + (size_t)row * a.ldx[t]);
-  uint4 raw[kMaxChunks];
+  __shared__ float red[8];
+  const int row = blockIdx.x, tsel = blockIdx.y, t = threadIdx.x;
+  const int n0 = t * 16;
+  const bool live = n0 < a.N;
+  float f[16];
+  if (live) load16(a.x[tsel] + (size_t)row * a.ldx[tsel] + n0, f);
+  else {
 #pragma unroll
-  for (int i = 0; i < kMaxChunks; ++i) {
-    const int c = lane + 32 * i;
-    raw[i] = c < nch ? __ldg(src + c) : make_uint4(0, 0, 0, 0);
+    for (int j = 0; j < 16; ++j) f[j] = 0.f;
   }
-  float ss = 0.f;
+  const __nv_bfloat16* w = a.w[tsel];
+  float r = 0.f;
+  if (w) {
+    float ss = 0.f;
 #pragma unroll
-  for (int i = 0; i < kMaxChunks; ++i) {
-    float f[8];
-    unpack8(raw[i], f);
-#pragma unroll
-    for (int j = 0; j < 8; ++j) ss = fmaf(f[j], f[j], ss);
+    for (int j = 0; j < 16; ++j) ss = fmaf(f[j], f[j], ss);
+    r = rsqrtf(__fdiv_rn(block_sum(ss, red), (float)a.N) + a.eps);
   }
-  const float r = rsqrtf(__fdiv_rn(warp_sum(ss), (float)a.N) + a.eps);
-  const int pos = row % a.span;
-  const __nv_bfloat16* w = a.w[t];
+  if (!live) return;
+  if (w) {
+    float wf[16];
+    load16(w + n0, wf);
 #pragma unroll
-  for (int i = 0; i < kMaxChunks; ++i) {
-    const int c = lane + 32 * i;
-    if (c >= nch) break;
-    float f[8];
-    unpack8(raw[i], f);
-    float wf[8];
-    if (w) unpack8(__ldg(reinterpret_cast<const uint4*>(w) + c), wf);
-    if (w) {
+    for (int j = 0; j < 16; ++j) f[j] = rc::bf16_to_float(rc::bf16_bits(__fmul_rn(__fmul_rn(f[j], r), wf[j])));
+  }
+  if (a.cos) {
+    const int pos = row % a.span, dd = n0 % a.d;   // 16 | d: a thread never straddles heads
+    float c[16], sn[16];
+    loadf16(a.cos + (size_t)pos * a.d + dd, c);
+    loadf16(a.sin + (size_t)pos * a.d + dd, sn);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) f[j] = rc::bf16_to_float(rc::bf16_bits(__fmul_rn(__fmul_rn(f[j], r), wf[j])));
+    for (int j = 0; j < 16; j += 2) {
+      const float e = f[j], o = f[j + 1];
+      f[j] = __fsub_rn(__fmul_rn(e, c[j]), __fmul_rn(o, sn[j]));
+      f[j + 1] = __fadd_rn(__fmul_rn(e, sn[j]), __fmul_rn(o, c[j]));
     }
-    if (a.cos) {
-      const int dd = (c * 8) % a.d;  // 8 | d, so a chunk never straddles heads
-      const float* cp = a.cos + (size_t)pos * a.d + dd;
-      const float* sp = a.sin + (size_t)pos * a.d + dd;
-#pragma unroll
-      for (int j = 0; j < 8; j += 2) {
-        const float cc = __ldg(cp + j), sn = __ldg(sp + j);
-        const float e = f[j], o = f[j + 1];
-        f[j] = __fsub_rn(__fmul_rn(e, cc), __fmul_rn(o, sn));
-        f[j + 1] = __fadd_rn(__fmul_rn(e, sn), __fmul_rn(o, cc));
-      }
-    }
-    *reinterpret_cast<uint4*>(a.out[t] + (size_t)row * a.ldo[t] + (size_t)c * 8) = pack8(f);
   }
+  float lo[8], hi[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) { lo[j] = f[j]; hi[j] = f[8 + j]; }
+  uint4* dst = reinterpret_cast<uint4*>(a.out[tsel] + (size_t)row * a.ldo[tsel] + n0);
+  dst[0] = pack8(lo);
+  dst[1] = pack8(hi);
 }
 
 // Temporal rotary on the first `td` dims of every head of `planes` planes of
@@ -313,12 +338,14 @@ int rc_ln_modulate_quant(const void* x, long long ldx, int M, int N, const void*
                          const void* bias, const float* shift, const float* scale, float eps,
                          void* out, long long ldo, uint8_t* codes, uint8_t* scales_swizzled,
                          float global_scale, cudaStream_t stream) {
-  if (M < 0 || N <= 0 || N % 64 || N > 32 * 8 * kMaxChunks)
+  if (M < 0 || N <= 0 || N % 64 || N > 4096)
     return rc::set_error(RC_ERR_ARG, "rc_ln_modulate_quant: N must be a multiple of 64 and <= 4096 (N=%d)", N);
   if (!x || (!out && !codes) || (codes && !scales_swizzled))
     return rc::set_error(RC_ERR_ARG, "rc_ln_modulate_quant: missing pointer");
   if (!aligned16(x) || ldx % 8 || (out && (!aligned16(out) || ldo % 8)) ||
-      (codes && (reinterpret_cast<uintptr_t>(codes) % 4 || reinterpret_cast<uintptr_t>(scales_swizzled) % 4)))
+      (shift && reinterpret_cast<uintptr_t>(shift) % 16) || (scale && reinterpret_cast<uintptr_t>(scale) % 16) ||
+      (weight && !aligned16(weight)) || (bias && !aligned16(bias)) ||
+      (codes && (reinterpret_cast<uintptr_t>(codes) % 8 || reinterpret_cast<uintptr_t>(scales_swizzled) % 4)))
     return rc::set_error(RC_ERR_ARG, "rc_ln_modulate_quant: rows must be 16-byte aligned");
   if (!(global_scale > 0.f)) return rc::set_error(RC_ERR_ARG, "rc_ln_modulate_quant: bad global scale");
   if (M == 0) return RC_OK;
@@ -326,7 +353,8 @@ int rc_ln_modulate_quant(const void* x, long long ldx, int M, int N, const void*
            reinterpret_cast<const __nv_bfloat16*>(weight), reinterpret_cast<const __nv_bfloat16*>(bias),
            shift, scale, eps, reinterpret_cast<__nv_bfloat16*>(out), ldo, codes, scales_swizzled,
            global_scale, M, N};
-  ln_modulate_kernel<<<(M + 7) / 8, 256, 0, stream>>>(a);
+  const int threads = ((N / 16) + 31) / 32 * 32;
+  ln_modulate_kernel<<<M, threads, 0, stream>>>(a);
   int r = rc::check_launch("rc_ln_modulate_quant");
   if (r || !codes) return r;
   const int katoms = ((N >> 4) + 3) >> 2;
@@ -346,13 +374,14 @@ int rc_rmsnorm_rope(int n_tensors, const void* const* xs, const long long* ldx,
                     const void* const* weights, void* const* outs, const long long* ldo, int M,
                     int N, int d, int span, const float* cos, const float* sin, float eps,
                     cudaStream_t stream) {
-  if (n_tensors < 1 || n_tensors > 2 || M < 0 || N <= 0 || N % 8 || N > 32 * 8 * kMaxChunks ||
-      d <= 0 || d % 8 || N % d || span <= 0)
+  if (n_tensors < 1 || n_tensors > 2 || M < 0 || N <= 0 || N % 16 || N > 4096 ||
+      d <= 0 || d % 16 || N % d || span <= 0)
     return rc::set_error(RC_ERR_ARG, "rc_rmsnorm_rope: bad shape (N=%d d=%d span=%d)", N, d, span);
   RmsArgs a{};
   for (int t = 0; t < n_tensors; ++t) {
     if (!xs[t] || !outs[t] || !aligned16(xs[t]) || !aligned16(outs[t]) ||
-        (weights[t] && !aligned16(weights[t])) || ldx[t] % 8 || ldo[t] % 8)
+        (weights[t] && !aligned16(weights[t])) || ldx[t] % 8 || ldo[t] % 8 ||
+        (cos && (reinterpret_cast<uintptr_t>(cos) % 16 || reinterpret_cast<uintptr_t>(sin) % 16)))
       return rc::set_error(RC_ERR_ARG, "rc_rmsnorm_rope: tensor %d must be 16-byte aligned", t);
     a.x[t] = reinterpret_cast<const __nv_bfloat16*>(xs[t]);
     a.ldx[t] = ldx[t];
@@ -370,8 +399,8 @@ int rc_rmsnorm_rope(int n_tensors, const void* const* xs, const long long* ldx,
   a.d = d;
   a.span = span;
   if (M == 0) return RC_OK;
-  dim3 grid((M + 7) / 8, n_tensors);
-  rmsnorm_rope_kernel<<<grid, 256, 0, stream>>>(a);
+  dim3 grid(M, n_tensors);
+  rmsnorm_rope_kernel<<<grid, ((N / 16) + 31) / 32 * 32, 0, stream>>>(a);
   return rc::check_launch("rc_rmsnorm_rope");
 }
 

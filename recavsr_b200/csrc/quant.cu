@@ -13,70 +13,54 @@
 
 namespace {
 
-constexpr int kQRows = 128;       // rows per CTA (one scale atom row-block)
-constexpr int kQBlocks = 16;      // 16-element blocks per row per CTA (256 columns)
-constexpr int kQThreads = 256;
+constexpr int kQRows = 128;       // rows per CTA (one scale-atom row block)
+constexpr int kQThreads = 512;    // 128 rows x 4 k-blocks (one 64-column k-atom)
 
+// One thread per 16-element block; the CTA covers one scale atom (128 rows x
+// 4 k-blocks = 512 bytes of scales, written as 32 coalesced 16-byte lines).
 __global__ void __launch_bounds__(kQThreads)
 nvfp4_quantize_kernel(const __nv_bfloat16* __restrict__ x, int M, int K, long long ldx, float g,
                       uint8_t* __restrict__ codes, uint8_t* __restrict__ scales) {
-  __shared__ __align__(16) uint8_t s_sf[kQRows][kQBlocks];
-  const int nkb = K >> 4;                      // 16-element blocks per row
-  const int katoms = (nkb + 3) >> 2;           // padded k-blocks / 4
-  const int kb0 = blockIdx.x * kQBlocks;
-  const int row0 = blockIdx.y * kQRows;
-  for (int i = threadIdx.x; i < kQRows * kQBlocks; i += kQThreads) {
-    const int r = i / kQBlocks, kbl = i % kQBlocks;
-    const int row = row0 + r, kb = kb0 + kbl;
-    uint8_t sf = 0;
-    if (row < M && kb < nkb) {
-      const uint4* src = reinterpret_cast<const uint4*>(x + (size_t)row * ldx + (size_t)kb * 16);
-      uint4 v0 = __ldg(src), v1 = __ldg(src + 1);
-      const uint32_t w[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
-      float f[16];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        f[2 * j] = __uint_as_float(w[j] << 16);
-        f[2 * j + 1] = __uint_as_float(w[j] & 0xffff0000u);
-      }
-      float amax = 0.0f;
-#pragma unroll
-      for (int j = 0; j < 16; ++j) amax = fmaxf(amax, fabsf(f[j]));
-      float sc = __fmul_rn(__fdiv_rn(amax, 6.0f), g);
-      sc = sc < 0.001953125f ? 0.001953125f : sc;   // clamp_min(2^-9); NaN passes through
-      sf = rc::e4m3_from_float(sc);
-      const float sd = rc::e4m3_to_float(sf);
-      uint32_t lo = 0, hi = 0;
-#pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const float z = __fdiv_rn(__fmul_rn(f[j], g), sd);
-        const uint32_t c = rc::e2m1_code(z);
-        if (j < 8) lo |= c << (4 * j);
-        else hi |= c << (4 * (j - 8));
-      }
-      *reinterpret_cast<uint2*>(codes + (size_t)row * (K >> 1) + (size_t)kb * 8) =
-          make_uint2(lo, hi);
-    }
-    s_sf[r][kbl] = sf;
-  }
-  __syncthreads();
-  // Scales: this CTA owns 128 rows x 4 k-atoms; each 16-byte line holds
-  // rows {m0, m0+32, m0+64, m0+96} x 4 k-blocks.
+  __shared__ __align__(16) uint8_t s_line[32][16];
+  const int nkb = K >> 4;
+  const int katoms = (nkb + 3) >> 2;
+  const int kt = blockIdx.x;
   const int t = threadIdx.x;
-  if (t < 128) {
-    const int ga = t >> 5, m0 = t & 31;
-    const int kt = (kb0 >> 2) + ga;
-    if (kt < katoms) {
-      uint32_t word[4];
+  const int r = t >> 2, kk = t & 3;         // row in the atom, k-block in the atom
+  const int row = blockIdx.y * kQRows + r, kb = kt * 4 + kk;
+  uint8_t sf = 0;
+  if (row < M && kb < nkb) {
+    const uint4* src = reinterpret_cast<const uint4*>(x + (size_t)row * ldx + (size_t)kb * 16);
+    uint4 v0 = __ldg(src), v1 = __ldg(src + 1);
+    const uint32_t w[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+    float f[16];
 #pragma unroll
-      for (int m1 = 0; m1 < 4; ++m1) {
-        const uint8_t* src = &s_sf[m1 * 32 + m0][ga * 4];
-        word[m1] = (uint32_t)src[0] | ((uint32_t)src[1] << 8) | ((uint32_t)src[2] << 16) |
-                   ((uint32_t)src[3] << 24);
-      }
-      const size_t off = ((size_t)(blockIdx.y * katoms + kt) * 32 + m0) * 16;
-      *reinterpret_cast<uint4*>(scales + off) = make_uint4(word[0], word[1], word[2], word[3]);
+    for (int j = 0; j < 8; ++j) {
+      f[2 * j] = __uint_as_float(w[j] << 16);
+      f[2 * j + 1] = __uint_as_float(w[j] & 0xffff0000u);
     }
+    float amax = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) amax = fmaxf(amax, fabsf(f[j]));
+    float sc = __fmul_rn(__fdiv_rn(amax, 6.0f), g);
+    sc = sc < 0.001953125f ? 0.001953125f : sc;   // clamp_min(2^-9); NaN passes through
+    sf = rc::e4m3_from_float(sc);
+    const float sd = rc::e4m3_to_float(sf);
+    uint32_t lo = 0, hi = 0;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const uint32_t c = rc::e2m1_code(__fdiv_rn(__fmul_rn(f[j], g), sd));
+      if (j < 8) lo |= c << (4 * j);
+      else hi |= c << (4 * (j - 8));
+    }
+    *reinterpret_cast<uint2*>(codes + (size_t)row * (K >> 1) + (size_t)kb * 8) = make_uint2(lo, hi);
+  }
+  // Atom line m0 holds rows {m0, m0+32, m0+64, m0+96} x 4 k-blocks.
+  s_line[r & 31][(r >> 5) * 4 + kk] = sf;
+  __syncthreads();
+  if (t < 32) {
+    const uint4 line = *reinterpret_cast<const uint4*>(s_line[t]);
+    *reinterpret_cast<uint4*>(scales + ((size_t)(blockIdx.y * katoms + kt) * 32 + t) * 16) = line;
   }
 }
 
@@ -157,7 +141,7 @@ int rc_nvfp4_quantize(const void* x, int M, int K, long long ldx, float global_s
     return rc::set_error(RC_ERR_ARG, "rc_nvfp4_quantize: global scale must be positive");
   if (M == 0) return RC_OK;
   const int nkb = K / 16;
-  dim3 grid((nkb + kQBlocks - 1) / kQBlocks, (M + kQRows - 1) / kQRows);
+  dim3 grid((nkb + 3) / 4, (M + kQRows - 1) / kQRows);
   nvfp4_quantize_kernel<<<grid, kQThreads, 0, stream>>>(
       reinterpret_cast<const __nv_bfloat16*>(x), M, K, ldx, global_scale, codes, scales_swizzled);
   return rc::check_launch("rc_nvfp4_quantize");

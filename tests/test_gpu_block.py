@@ -216,8 +216,10 @@ def _oracle_stack_step(params_list, routers, caches, hidden, start, frames, H, W
     span = H * W
     d = hidden.shape[1] // heads
     h = hidden
+    routes = []
     for i, (prm, rt) in enumerate(zip(params_list, routers)):
         slots, ppos = rt.history(origin)
+        routes.append((list(slots), list(ppos)))
         cap = rt.capacity
         pk = caches[i][0] if cap else np.zeros((0, heads, d), np.float32)
         pv = caches[i][1] if cap else np.zeros((0, heads, d), np.float32)
@@ -226,12 +228,14 @@ def _oracle_stack_step(params_list, routers, caches, hidden, start, frames, H, W
         for off, slot in rt.commit(frames, start):
             caches[i][0][slot * span:(slot + 1) * span] = k[off * span:(off + 1) * span]
             caches[i][1][slot * span:(slot + 1) * span] = v[off * span:(off + 1) * span]
-    return h
+    return h, routes
 
 
 def test_layer_stack_streaming_and_graph_replay():
-    """3 layers, prefix + 8 body blocks: eager stack vs the oracle's router +
-    block loop, and graph replay bit-identical to eager."""
+    """3 layers, prefix + 8 body blocks. Per block the oracle starts from the
+    stack's own cache contents (teacher forcing, so NVFP4 code flips do not
+    compound across blocks); routing tables must equal the oracle router's
+    exactly, and graph replay must be bit-identical to eager launches."""
     from recavsr_b200.runtime.block import FusedBlock, LayerStack, rope_tables
     dim, heads, ffn, H, W = 256, 2, 512, 4, 6
     span = H * W
@@ -246,14 +250,14 @@ def test_layer_stack_streaming_and_graph_replay():
     params = [_oracle_params(p, H, W, heads, host(b.cross_k), host(b.cross_v), host(b.modulation))
               for p, b in zip(ps, eager.blocks)]
     routers = [RouterState(a) for a in actions]
-    caches = [(np.zeros((r.capacity * span, heads, 128), np.float32),
-               np.zeros((r.capacity * span, heads, 128), np.float32)) for r in routers]
     rs = np.random.RandomState(5)
     start = 0
     captured = False
     for blk_i in range(9):
         frames = 6 if blk_i == 0 else 2
         x = bf16_round(rs.standard_normal((frames * span, dim)).astype(np.float32))
+        caches = [(host(eager.cache_k[i])[0].copy(), host(eager.cache_v[i])[0].copy())
+                  for i in range(3)]
         he = dev_bf16(x)
         eager.step(he, frames)
         hg = dev_bf16(x)
@@ -263,8 +267,14 @@ def test_layer_stack_streaming_and_graph_replay():
             captured = True
         else:
             graphed.step(hg, frames, graphs=(frames == 2 and captured))
-        ref = _oracle_stack_step(params, routers, caches, x, start, frames, H, W, heads)
+        ref, routes = _oracle_stack_step(params, routers, caches, x, start, frames, H, W, heads)
         start += frames
+        for i, (slots, ppos) in enumerate(routes):
+            o = i * eager._row
+            cap = eager.caches[i].capacity
+            assert eager.route_host[o:o + cap].tolist() == (slots or [-1] * cap)
+            if slots:
+                assert eager.route_host[o + 8:o + 8 + cap].tolist() == ppos
         got = host(he)
         _close(got, ref, BLOCK_REL_L2, BLOCK_MAX_FRAC)
         np.testing.assert_array_equal(host(hg), got)
