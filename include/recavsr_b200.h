@@ -117,23 +117,28 @@ int rc_kv_commit_planned(const void* src_k, const void* src_v, long long src_ld_
  * element strides of q, ck, cv, pk, pv; slots/past_positions int32 [CAP]
  * (slot -1 = empty), query_positions int32 [QT], cos/sin fp32 [frames, td/2]
  * (the rolling temporal table), all on the device. out: [B, QT*H*W, heads, d]
- * bf16 with token stride out_ld. workspace: caller-provided device scratch of
- * rc_paired_attention_workspace(...) bytes (rotated q and K planes). d = 128. */
+ * bf16 with token stride out_ld (nullable when out_codes is given).
+ * out_codes/out_scales (optional, B = 1): the output also NVFP4-quantized as
+ * rc_nvfp4_quantize would quantize it ([QT*H*W, heads*d/2] codes + swizzled
+ * scales), ready for the o-proj GEMM. workspace: caller-provided device scratch
+ * of rc_paired_attention_workspace(...) bytes (rotated q and K planes). d = 128. */
 long long rc_paired_attention_workspace(int B, int QT, int CAP, int H, int W, int heads, int d);
 int rc_paired_attention(const void* q, const void* ck, const void* cv, const void* pk, const void* pv,
                         const long long* strides, const int* slots, const int* past_positions,
                         const int* query_positions, const float* cos, const float* sin, int B,
                         int QT, int CAP, int H, int W, int heads, int d, int td, int window_h,
                         int window_w, void* workspace, long long workspace_bytes, void* out,
-                        long long out_ld, rc_stream_t stream);
+                        long long out_ld, uint8_t* out_codes, uint8_t* out_scales,
+                        rc_stream_t stream);
 
 /* Unmasked attention without rotary embedding or cache (the cross-attention of
  * recavsr_infer/runtime/transformer.py:123-128 over the precomputed prompt K/V):
  * q [B, Nq, heads, d], k/v [B, Nk, heads, d] with strides[9] = (batch, token,
- * head) element strides of q, k, v; out [B, Nq, heads, d] (token stride out_ld). */
+ * head) element strides of q, k, v; out [B, Nq, heads, d] (token stride out_ld),
+ * optional NVFP4 copy of the output in out_codes/out_scales (B = 1). */
 int rc_cross_attention(const void* q, const void* k, const void* v, const long long* strides, int B,
                        int Nq, int Nk, int heads, int d, void* out, long long out_ld,
-                       rc_stream_t stream);
+                       uint8_t* out_codes, uint8_t* out_scales, rc_stream_t stream);
 
 #ifdef __cplusplus
 }

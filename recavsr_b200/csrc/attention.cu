@@ -49,8 +49,10 @@ struct AttnParams {
   int qtiles_x, qtiles_y;       // local: tiles along x / y per frame pair
   float scale_log2;             // d^-0.5 * log2(e)
   const int* slots;             // [CAP] device
-  __nv_bfloat16* out;           // [QT*T, heads, d]
+  __nv_bfloat16* out;           // [QT*T, heads, d] (nullable when q_codes is set)
   long long out_ld;             // elements between tokens
+  uint8_t* q_codes;             // optional NVFP4 output [Tq, heads*d/2]
+  uint8_t* q_sf;                // its swizzled scales (heads*d as K)
 };
 
 struct SmemLayout {
@@ -58,9 +60,9 @@ struct SmemLayout {
   static constexpr int offQ = 0;                     // 2 chunks
   static constexpr int offK = offQ + 2 * kChunk;     // 2 stages x 2 chunks
   static constexpr int offV = offK + 4 * kChunk;     // 2 stages x 2 chunks
-  static constexpr int offP = offV + 4 * kChunk;     // 2 chunks
-  static constexpr int offBar = offP + 2 * kChunk;
-  static constexpr int kBars = 12;
+  static constexpr int offP = offV + 4 * kChunk;     // 2 buffers x 2 chunks
+  static constexpr int offBar = offP + 4 * kChunk;
+  static constexpr int kBars = 16;
   static constexpr int offMisc = offBar + kBars * 8;
   static constexpr int kTotal = offMisc + 16 + kMaxPlanes * 4;
   static constexpr int kAlloc = kTotal + 1024;
@@ -105,6 +107,22 @@ struct TileIter {
 __device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
   return (uint32_t)rc::bf16_bits(a) | ((uint32_t)rc::bf16_bits(b) << 16);
 }
+__device__ __forceinline__ float fast_exp2(float x) {   // MUFU ex2 (as tl.exp2)
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+#define RC_TMEM_LD_X32(taddr, r)                                                               \
+  asm volatile(                                                                                \
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"   \
+      "%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"       \
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),    \
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),             \
+        "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]),          \
+        "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),          \
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),          \
+        "=r"(r[31])                                                                            \
+      : "r"(taddr))
 
 __global__ void __launch_bounds__(kThreads, 1)
 attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
@@ -119,9 +137,9 @@ attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
   uint64_t* kv_empty = bars + 3;   // [2]
   uint64_t* s_full = bars + 5;     // [2]
   uint64_t* s_free = bars + 7;     // [2]
-  uint64_t* p_full = bars + 9;
-  uint64_t* o_done = bars + 10;
-  uint64_t* done = bars + 11;
+  uint64_t* p_full = bars + 9;     // [2] one per P buffer
+  uint64_t* o_done = bars + 11;    // [2] P.V on P buffer b finished
+  uint64_t* done = bars + 13;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::offMisc);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::offMisc + 4);
   int* s_nplanes = reinterpret_cast<int*>(smem + L::offMisc + 8);
@@ -145,14 +163,14 @@ attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
 
   if (threadIdx.x == 0) {
     sm100::mbar_init(q_full, 1);
-    for (int s = 0; s < 2; ++s) {
-      sm100::mbar_init(&kv_full[s], 1);
-      sm100::mbar_init(&kv_empty[s], 1);
-      sm100::mbar_init(&s_full[s], 1);
-      sm100::mbar_init(&s_free[s], 128);
+    for (int s2 = 0; s2 < 2; ++s2) {
+      sm100::mbar_init(&kv_full[s2], 1);
+      sm100::mbar_init(&kv_empty[s2], 1);
+      sm100::mbar_init(&s_full[s2], 1);
+      sm100::mbar_init(&s_free[s2], 128);
+      sm100::mbar_init(&p_full[s2], 128);
+      sm100::mbar_init(&o_done[s2], 1);
     }
-    sm100::mbar_init(p_full, 128);
-    sm100::mbar_init(o_done, 1);
     sm100::mbar_init(done, 1);
     *abort_flag = 0;
     // Visible planes: routed past planes (slot >= 0), then the current frames.
@@ -198,24 +216,24 @@ attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       }
       int issued = 0;
       for (int i = 0; i < n_tiles; ++i) {
-        const int s = i & 1;
-        if (!wait(&kv_empty[s], ((i >> 1) & 1) ^ 1, 1)) break;
+        const int st = i & 1;
+        if (!wait(&kv_empty[st], ((i >> 1) & 1) ^ 1, 1)) break;
         const int plane = s_planes[i / tpp];
         int a, b;
         it.tile_origin(i % tpp, a, b);
-        uint8_t* sk = smem + L::offK + s * 2 * L::kChunk;
-        uint8_t* sv = smem + L::offV + s * 2 * L::kChunk;
-        sm100::mbar_arrive_expect_tx(&kv_full[s], 4 * L::kChunk);
+        uint8_t* sk = smem + L::offK + st * 2 * L::kChunk;
+        uint8_t* sv = smem + L::offV + st * 2 * L::kChunk;
+        sm100::mbar_arrive_expect_tx(&kv_full[st], 4 * L::kChunk);
         const bool past = plane < p.CAP;
         const int vplane = past ? p.slots[plane] : plane - p.CAP;
         const CUtensorMap* vmap = past ? &tm_pv : &tm_cv;
         for (int c = 0; c < 2; ++c) {
           if (!p.local) {
-            sm100::tma_load_4d(sk + c * L::kChunk, &tm_k, &kv_full[s], c * 64, head, a, plane);
-            sm100::tma_load_4d(sv + c * L::kChunk, vmap, &kv_full[s], c * 64, head, a, vplane);
+            sm100::tma_load_4d(sk + c * L::kChunk, &tm_k, &kv_full[st], c * 64, head, a, plane);
+            sm100::tma_load_4d(sv + c * L::kChunk, vmap, &kv_full[st], c * 64, head, a, vplane);
           } else {
-            sm100::tma_load_5d(sk + c * L::kChunk, &tm_k, &kv_full[s], c * 64, head, b, a, plane);
-            sm100::tma_load_5d(sv + c * L::kChunk, vmap, &kv_full[s], c * 64, head, b, a, vplane);
+            sm100::tma_load_5d(sk + c * L::kChunk, &tm_k, &kv_full[st], c * 64, head, b, a, plane);
+            sm100::tma_load_5d(sv + c * L::kChunk, vmap, &kv_full[st], c * 64, head, b, a, vplane);
           }
         }
         ++issued;
@@ -230,12 +248,12 @@ attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       constexpr uint32_t idesc_qk = sm100::idesc_bf16(kBM, kBN, 0, 0);
       constexpr uint32_t idesc_pv = sm100::idesc_bf16(kBM, kD, 0, 1);
       const uint32_t sq = sm100::smem_u32(smem + L::offQ);
-      const uint32_t sp = sm100::smem_u32(smem + L::offP);
       bool ok = wait(q_full, 0, 2);
       sm100::tc_fence_after();
       auto issue_pv = [&](int j) -> bool {
-        if (!wait(p_full, j & 1, 3)) return false;
+        if (!wait(&p_full[j & 1], (j >> 1) & 1, 3)) return false;
         sm100::tc_fence_after();
+        const uint32_t sp = sm100::smem_u32(smem + L::offP + (j & 1) * 2 * L::kChunk);
         const uint32_t sv = sm100::smem_u32(smem + L::offV + (j & 1) * 2 * L::kChunk);
         for (int k = 0; k < kBN / 16; ++k) {
           const uint64_t ad = sm100::desc_kmajor_sw128(sp + (k >> 2) * L::kChunk + (k & 3) * 32);
@@ -243,22 +261,22 @@ attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
           sm100::mma_f16_ss(t_o, ad, bd, idesc_pv, (j > 0 || k > 0) ? 1u : 0u);
         }
         sm100::tc_commit(&kv_empty[j & 1]);
-        sm100::tc_commit(o_done);
+        sm100::tc_commit(&o_done[j & 1]);
         return true;
       };
       for (int i = 0; i < n_tiles && ok; ++i) {
-        const int s = i & 1;
-        if (!wait(&kv_full[s], (i >> 1) & 1, 4)) { ok = false; break; }
-        if (!wait(&s_free[s], ((i >> 1) & 1) ^ 1, 5)) { ok = false; break; }
+        const int st = i & 1;
+        if (!wait(&kv_full[st], (i >> 1) & 1, 4)) { ok = false; break; }
+        if (!wait(&s_free[st], ((i >> 1) & 1) ^ 1, 5)) { ok = false; break; }
         sm100::tc_fence_after();
-        const uint32_t sk = sm100::smem_u32(smem + L::offK + s * 2 * L::kChunk);
-        const uint32_t t_s = t_s0 + s * 128;
+        const uint32_t sk = sm100::smem_u32(smem + L::offK + st * 2 * L::kChunk);
+        const uint32_t t_s = t_s0 + st * 128;
         for (int k = 0; k < kD / 16; ++k) {
           const uint32_t off = (k >> 2) * L::kChunk + (k & 3) * 32;
           sm100::mma_f16_ss(t_s, sm100::desc_kmajor_sw128(sq + off), sm100::desc_kmajor_sw128(sk + off),
                             idesc_qk, k > 0 ? 1u : 0u);
         }
-        sm100::tc_commit(&s_full[s]);
+        sm100::tc_commit(&s_full[st]);
         if (i > 0 && !issue_pv(i - 1)) { ok = false; break; }
       }
       if (ok && n_tiles > 0) issue_pv(n_tiles - 1);
@@ -270,13 +288,10 @@ attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
     const int quad = warp & 3;
     const int r = quad * 32 + lane;               // query row within the tile / TMEM lane
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
-    // This row's query token.
     int qrow = -1, qy = 0, qx = 0;
     if (!p.local) {
       const int t = q_row0 + r;
       if (t < p.Tq) qrow = t;
-      qy = 0;
-      qx = 0;
     } else {
       const int f = qf0 + (r >> 6), yy = qy0 + ((r >> 3) & 7), xx = qx0 + (r & 7);
       if (f < p.QT && yy < p.H && xx < p.W) qrow = f * p.T + yy * p.W + xx;
@@ -285,62 +300,92 @@ attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
     }
     const int top = min(max(qy - p.wh / 2, 0), p.H - p.wh);
     const int left = min(max(qx - p.ww / 2, 0), p.W - p.ww);
+    const float scale = p.scale_log2;
     float m_used = -INFINITY, l = 0.f;
-    uint8_t* sp = smem + L::offP;
     bool ok = true;
     for (int i = 0; i < n_tiles; ++i) {
-      const int s = i & 1;
-      if (!__all_sync(0xffffffffu, wait(&s_full[s], (i >> 1) & 1, 6))) { ok = false; break; }
+      const int st = i & 1;
+      if (!__all_sync(0xffffffffu, wait(&s_full[st], (i >> 1) & 1, 6))) { ok = false; break; }
       sm100::tc_fence_after();
       int a, b;
       it.tile_origin(i % tpp, a, b);
-      float sc[kBN];
-#pragma unroll
-      for (int c = 0; c < kBN; c += 16) {
-        uint32_t v[16];
-        sm100::tmem_ld16(t_s0 + s * 128 + c + lane_off, v);
-#pragma unroll
-        for (int j = 0; j < 16; ++j) sc[c + j] = __uint_as_float(v[j]);
-      }
-      sm100::tmem_ld_wait();
-      // Release the S buffer as soon as it is in registers.
-      sm100::tc_fence_before();
-      sm100::mbar_arrive(&s_free[s]);
+      const bool full_tile = !p.local && a + kBN <= p.T;
+      const uint32_t t_s = t_s0 + st * 128 + lane_off;
+      // Pass 1: row max over the tile (raw scores; scale > 0 commutes with max).
       float mt = -INFINITY;
+#pragma unroll 1
+      for (int c = 0; c < kBN; c += 32) {
+        uint32_t v[32];
+        RC_TMEM_LD_X32(t_s + c, v);
+        sm100::tmem_ld_wait();
+        if (full_tile) {
 #pragma unroll
-      for (int j = 0; j < kBN; ++j) {
-        bool valid;
-        if (!p.local) {
-          valid = a + j < p.T;
+          for (int j = 0; j < 32; ++j) mt = fmaxf(mt, __uint_as_float(v[j]));
         } else {
-          const int ky = a + j / kLocalKW, kx = b + j % kLocalKW;
-          valid = ky < p.H && kx < p.W && ky >= top && ky < top + p.wh && kx >= left && kx < left + p.ww;
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            bool valid;
+            if (!p.local) {
+              valid = a + c + j < p.T;
+            } else {
+              const int jj = c + j, ky = a + jj / kLocalKW, kx = b + jj % kLocalKW;
+              valid = ky < p.H && kx < p.W && ky >= top && ky < top + p.wh && kx >= left && kx < left + p.ww;
+            }
+            if (valid) mt = fmaxf(mt, __uint_as_float(v[j]));
+          }
         }
-        const float x = valid ? __fmul_rn(sc[j], p.scale_log2) : -INFINITY;
-        sc[j] = x;
-        mt = fmaxf(mt, x);
       }
+      mt = mt == -INFINITY ? -INFINITY : mt * scale;
       // Lazy rescaling: move the reference max only when it grows by > 2^8.
       float corr = 1.0f;
       bool rescale = false;
       if (mt > m_used + kRescaleThreshold || (m_used == -INFINITY && mt > -INFINITY)) {
-        corr = m_used == -INFINITY ? 0.f : exp2f(m_used - mt);
+        corr = m_used == -INFINITY ? 0.f : fast_exp2(m_used - mt);
         rescale = (i > 0) && m_used != -INFINITY;
         m_used = mt;
       }
       const float mref = m_used == -INFINITY ? 0.f : m_used;
+      // The P buffer of this tile was last read by the P.V of tile i-2.
+      if (i >= 2 && !__all_sync(0xffffffffu, wait(&o_done[st], ((i >> 1) - 1) & 1, 7))) { ok = false; break; }
+      uint8_t* sp = smem + L::offP + st * 2 * L::kChunk;
+      // Pass 2: exponentials, row sum, P (bf16) to shared memory (K-major, 128B swizzle).
       float sum = 0.f;
+#pragma unroll 1
+      for (int c = 0; c < kBN; c += 32) {
+        uint32_t v[32];
+        RC_TMEM_LD_X32(t_s + c, v);
+        sm100::tmem_ld_wait();
+        float e[32];
 #pragma unroll
-      for (int j = 0; j < kBN; ++j) {
-        const float e = exp2f(sc[j] - mref);
-        sc[j] = e;
-        sum += e;
+        for (int j = 0; j < 32; ++j) {
+          bool valid = true;
+          if (!full_tile) {
+            if (!p.local) {
+              valid = a + c + j < p.T;
+            } else {
+              const int jj = c + j, ky = a + jj / kLocalKW, kx = b + jj % kLocalKW;
+              valid = ky < p.H && kx < p.W && ky >= top && ky < top + p.wh && kx >= left && kx < left + p.ww;
+            }
+          }
+          e[j] = valid ? fast_exp2(fmaf(__uint_as_float(v[j]), scale, -mref)) : 0.f;
+          sum += e[j];
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int unit = (c >> 3) + u, chunk = unit >> 3, lu = unit & 7;
+          const uint4 w = make_uint4(pack_bf16x2(e[8 * u], e[8 * u + 1]), pack_bf16x2(e[8 * u + 2], e[8 * u + 3]),
+                                     pack_bf16x2(e[8 * u + 4], e[8 * u + 5]), pack_bf16x2(e[8 * u + 6], e[8 * u + 7]));
+          *reinterpret_cast<uint4*>(sp + chunk * L::kChunk + r * 128 + ((lu ^ (r & 7)) << 4)) = w;
+        }
       }
+      // S is fully consumed: the MMA may overwrite this buffer with S(i+2).
+      sm100::tc_fence_before();
+      sm100::mbar_arrive(&s_free[st]);
       l = __fmul_rn(l, corr) + sum;
-      // P and O may only change once the previous P.V has finished.
-      if (i > 0 && !__all_sync(0xffffffffu, wait(o_done, (i - 1) & 1, 7))) { ok = false; break; }
-      sm100::tc_fence_after();
+      // O changes only when a row's reference max moved (rare); then wait for P.V(i-1).
       if (__any_sync(0xffffffffu, rescale)) {
+        if (!__all_sync(0xffffffffu, wait(&o_done[st ^ 1], ((i - 1) >> 1) & 1, 9))) { ok = false; break; }
+        sm100::tc_fence_after();
         const float f = rescale ? corr : 1.0f;
 #pragma unroll 1
         for (int c = 0; c < kD; c += 16) {
@@ -353,37 +398,58 @@ attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
         }
         sm100::tmem_st_wait();
       }
-      // P row -> shared memory, K-major with the 128-byte swizzle.
-#pragma unroll
-      for (int u = 0; u < kBN / 8; ++u) {
-        const int chunk = u >> 3, unit = u & 7;
-        uint4 w = make_uint4(pack_bf16x2(sc[8 * u], sc[8 * u + 1]), pack_bf16x2(sc[8 * u + 2], sc[8 * u + 3]),
-                             pack_bf16x2(sc[8 * u + 4], sc[8 * u + 5]), pack_bf16x2(sc[8 * u + 6], sc[8 * u + 7]));
-        *reinterpret_cast<uint4*>(sp + chunk * L::kChunk + r * 128 + ((unit ^ (r & 7)) << 4)) = w;
-      }
       sm100::fence_proxy_async_smem();
       sm100::tc_fence_before();
-      sm100::mbar_arrive(p_full);
+      sm100::mbar_arrive(&p_full[st]);
     }
-    if (ok && n_tiles > 0 && __all_sync(0xffffffffu, wait(o_done, (n_tiles - 1) & 1, 8))) {
+    if (ok && n_tiles > 0 &&
+        __all_sync(0xffffffffu, wait(&o_done[(n_tiles - 1) & 1], ((n_tiles - 1) >> 1) & 1, 8))) {
       sm100::tc_fence_after();
       const float inv = 1.0f / fmaxf(l, 1e-20f);
-      __nv_bfloat16* dst = qrow >= 0 ? p.out + (size_t)qrow * p.out_ld + (size_t)head * kD : nullptr;
+      __nv_bfloat16* dst = (qrow >= 0 && p.out) ? p.out + (size_t)qrow * p.out_ld + (size_t)head * kD : nullptr;
+      const int katoms = (p.heads * kD) >> 6;
 #pragma unroll 1
       for (int c = 0; c < kD; c += 16) {
         uint32_t v[16];
         sm100::tmem_ld16(t_o + c + lane_off, v);
         sm100::tmem_ld_wait();
+        float y[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) y[j] = rc::bf16_to_float(rc::bf16_bits(__uint_as_float(v[j]) * inv));
         if (dst) {
           uint32_t w[8];
 #pragma unroll
-          for (int j = 0; j < 8; ++j)
-            w[j] = pack_bf16x2(__uint_as_float(v[2 * j]) * inv, __uint_as_float(v[2 * j + 1]) * inv);
+          for (int j = 0; j < 8; ++j) w[j] = pack_bf16x2(y[2 * j], y[2 * j + 1]);
           reinterpret_cast<uint4*>(dst + c)[0] = make_uint4(w[0], w[1], w[2], w[3]);
           reinterpret_cast<uint4*>(dst + c)[1] = make_uint4(w[4], w[5], w[6], w[7]);
         }
+        if (p.q_codes && qrow >= 0) {
+          // NVFP4 of the bf16 output (16 columns = one block), for the o-proj GEMM.
+          float amax = 0.f;
+#pragma unroll
+          for (int j = 0; j < 16; ++j) amax = rc::absmax_nan(amax, y[j]);
+          float sc = __fdiv_rn(amax, 6.0f);
+          sc = sc < 0.001953125f ? 0.001953125f : sc;
+          const uint8_t sfb = rc::e4m3_from_float(sc);
+          const rc::E2m1Bounds bd(rc::e4m3_to_float(sfb));
+          uint32_t lo = 0, hi = 0;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            lo |= bd.code(y[j]) << (4 * j);
+            hi |= bd.code(y[8 + j]) << (4 * j);
+          }
+          const int kb = (head * kD + c) >> 4;
+          *reinterpret_cast<uint2*>(p.q_codes + (size_t)qrow * (p.heads * kD / 2) + (kb << 3)) = make_uint2(lo, hi);
+          p.q_sf[rc::sf_offset(qrow, kb, katoms)] = sfb;
+        }
       }
     }
+  }
+  // Zero the scale bytes of the padding rows (to a multiple of 128) for this head.
+  if (p.q_sf && qtile == 0) {
+    const int pm = (p.Tq + 127) / 128 * 128, katoms = (p.heads * kD) >> 6;
+    for (int i = threadIdx.x; i < (pm - p.Tq) * 8; i += blockDim.x)
+      p.q_sf[rc::sf_offset(p.Tq + i / 8, head * 8 + i % 8, katoms)] = 0;
   }
 
   sm100::tc_fence_before();
@@ -500,7 +566,8 @@ int rc_paired_attention(const void* q, const void* ck, const void* cv, const voi
                         const int* query_positions, const float* cos, const float* sin, int B,
                         int QT, int CAP, int H, int W, int heads, int d, int td, int window_h,
                         int window_w, void* workspace, long long workspace_bytes, void* out,
-                        long long out_ld, cudaStream_t stream) {
+                        long long out_ld, uint8_t* out_codes, uint8_t* out_scales,
+                        cudaStream_t stream) {
   const char* what = "rc_paired_attention";
   if (B <= 0 || QT <= 0 || CAP < 0 || H <= 0 || W <= 0 || heads <= 0)
     return rc::set_error(RC_ERR_ARG, "%s: bad geometry", what);
@@ -508,9 +575,11 @@ int rc_paired_attention(const void* q, const void* ck, const void* cv, const voi
     return rc::set_error(RC_ERR_UNSUPPORTED, "%s: head_dim %d (the tcgen05 kernel supports 128)", what, d);
   if (td < 0 || td > d || td % 2 || window_h <= 0 || window_w <= 0 || CAP > kMaxPlanes - 8 || QT > 8)
     return rc::set_error(RC_ERR_ARG, "%s: bad rotary / window / plane count", what);
-  if (!q || !ck || !cv || !out || !query_positions || !cos || !sin || !strides ||
-      (CAP && (!pk || !pv || !slots || !past_positions)))
+  if (!q || !ck || !cv || (!out && !out_codes) || !query_positions || !cos || !sin || !strides ||
+      (CAP && (!pk || !pv || !slots || !past_positions)) || (!out_codes != !out_scales))
     return rc::set_error(RC_ERR_ARG, "%s: null pointer", what);
+  if (out_codes && ((heads * d) % 64 || reinterpret_cast<uintptr_t>(out_codes) % 8))
+    return rc::set_error(RC_ERR_ARG, "%s: NVFP4 output needs heads*d %% 64 == 0 and 8-byte alignment", what);
   const long long need = rc_paired_attention_workspace(B, QT, CAP, H, W, heads, d);
   if (!workspace || workspace_bytes < need || !al16(workspace))
     return rc::set_error(RC_ERR_ARG, "%s: workspace of %lld bytes (16-byte aligned) required", what, need);
@@ -522,7 +591,7 @@ int rc_paired_attention(const void* q, const void* ck, const void* cv, const voi
   const void* ptrs[5] = {q, ck, cv, pk, pv};
   for (int i = 0; i < 5; ++i)
     if (ptrs[i] && !al16(ptrs[i])) return rc::set_error(RC_ERR_ARG, "%s: tensors must be 16-byte aligned", what);
-  if (!al16(out) || out_ld % 8) return rc::set_error(RC_ERR_ARG, "%s: output must be 16-byte aligned", what);
+  if (out && (!al16(out) || out_ld % 8)) return rc::set_error(RC_ERR_ARG, "%s: output must be 16-byte aligned", what);
   const int T = H * W;
   const int wh = window_h < H ? window_h : H, ww = window_w < W ? window_w : W;
   const bool local = wh < H || ww < W;
@@ -579,8 +648,11 @@ int rc_paired_attention(const void* q, const void* ck, const void* cv, const voi
     p.wh = wh; p.ww = ww; p.local = local;
     p.scale_log2 = (float)(1.0 / sqrt((double)d) * 1.4426950408889634);
     p.slots = slots;
-    p.out = reinterpret_cast<__nv_bfloat16*>(out) + (long long)b * QT * T * out_ld;
+    p.out = out ? reinterpret_cast<__nv_bfloat16*>(out) + (long long)b * QT * T * out_ld : nullptr;
     p.out_ld = out_ld;
+    if (out_codes && B > 1) return rc::set_error(RC_ERR_UNSUPPORTED, "%s: NVFP4 output needs B == 1", what);
+    p.q_codes = out_codes;
+    p.q_sf = out_scales;
     if (!local) {
       p.n_qtiles = (QT * T + kBM - 1) / kBM;
     } else {
@@ -602,17 +674,20 @@ int rc_paired_attention(const void* q, const void* ck, const void* cv, const voi
 // directly (no workspace).
 int rc_cross_attention(const void* q, const void* k, const void* v, const long long* strides, int B,
                        int Nq, int Nk, int heads, int d, void* out, long long out_ld,
-                       cudaStream_t stream) {
+                       uint8_t* out_codes, uint8_t* out_scales, cudaStream_t stream) {
   const char* what = "rc_cross_attention";
   if (B <= 0 || Nq < 0 || Nk <= 0 || heads <= 0 || !strides)
     return rc::set_error(RC_ERR_ARG, "%s: bad geometry", what);
   if (d != kD)
     return rc::set_error(RC_ERR_UNSUPPORTED, "%s: head_dim %d (the tcgen05 kernel supports 128)", what, d);
-  if (!q || !k || !v || !out) return rc::set_error(RC_ERR_ARG, "%s: null pointer", what);
+  if (!q || !k || !v || (!out && !out_codes) || (!out_codes != !out_scales))
+    return rc::set_error(RC_ERR_ARG, "%s: null pointer", what);
+  if (out_codes && (B > 1 || (heads * d) % 64 || reinterpret_cast<uintptr_t>(out_codes) % 8))
+    return rc::set_error(RC_ERR_ARG, "%s: NVFP4 output needs B == 1 and heads*d %% 64 == 0", what);
   for (int t = 0; t < 3; ++t)
     if ((B > 1 && strides[3 * t] % 8) || strides[3 * t + 1] % 8 || strides[3 * t + 2] % 8)
       return rc::set_error(RC_ERR_ARG, "%s: strides must be multiples of 8 elements (16 bytes)", what);
-  if (!al16(q) || !al16(k) || !al16(v) || !al16(out) || out_ld % 8)
+  if (!al16(q) || !al16(k) || !al16(v) || (out && (!al16(out) || out_ld % 8)))
     return rc::set_error(RC_ERR_ARG, "%s: tensors must be 16-byte aligned", what);
   if (Nq == 0) return RC_OK;
   if (!g_attr_set) {
@@ -639,8 +714,10 @@ int rc_cross_attention(const void* q, const void* k, const void* v, const long l
     p.wh = 1; p.ww = Nk; p.local = 0;
     p.scale_log2 = (float)(1.0 / sqrt((double)d) * 1.4426950408889634);
     p.slots = nullptr;
-    p.out = reinterpret_cast<__nv_bfloat16*>(out) + (long long)b * Nq * out_ld;
+    p.out = out ? reinterpret_cast<__nv_bfloat16*>(out) + (long long)b * Nq * out_ld : nullptr;
     p.out_ld = out_ld;
+    p.q_codes = out_codes;
+    p.q_sf = out_scales;
     p.n_qtiles = (Nq + kBM - 1) / kBM;
     dim3 grid(p.n_qtiles, heads);
     attention_kernel<<<grid, kThreads, SmemLayout::kAlloc, stream>>>(tq, tk, tv, tv, p);

@@ -128,6 +128,35 @@ __host__ __device__ __forceinline__ uint32_t e2m1_code(float z) {
   return c | (z < 0.0f ? 8u : 0u);
 }
 
+// Division-free E2M1 ladder for bf16 inputs x and an E4M3 scale s (global
+// scale 1). Exactness: x has 8 significant bits, s at most 4 and every
+// threshold t at most 3, so t*s is exact in fp32 and any x != t*s lies at
+// least 2^-9 (relative) away from it -- far more than the 2^-24 rounding of
+// fp32 division -- hence fl(|x|/s) > t  <=>  |x| > t*s (and likewise for >=).
+// The codes therefore equal e2m1_code(x / s) bit for bit. A NaN scale (block
+// amax >= 2784 or non-finite) gives code 0 for every element, as x / NaN does.
+struct E2m1Bounds {
+  float b[7];
+  bool nan;
+  __host__ __device__ __forceinline__ explicit E2m1Bounds(float s) {
+    b[0] = 0.25f * s; b[1] = 0.75f * s; b[2] = 1.25f * s; b[3] = 1.75f * s;
+    b[4] = 2.5f * s;  b[5] = 3.5f * s;  b[6] = 5.0f * s;
+    nan = !(s == s);
+  }
+  __host__ __device__ __forceinline__ uint32_t code(float x) const {
+    const float a = fabsf(x);
+    const uint32_t c = (a > b[0]) + (a >= b[1]) + (a > b[2]) + (a >= b[3]) + (a > b[4]) +
+                       (a >= b[5]) + (a > b[6]);
+    return nan ? 0u : (c | (x < 0.0f ? 8u : 0u));
+  }
+};
+
+// NaN-propagating max of |x| (torch's amax propagates NaN).
+__host__ __device__ __forceinline__ float absmax_nan(float m, float x) {
+  const float a = fabsf(x);
+  return (a > m || a != a) ? a : m;
+}
+
 // Offset of the scale byte for (row, k-block) in the 128x4 blocked layout
 // (recavsr_infer/runtime/nvfp4.py:64-67): atoms of 128 rows x 4 k-blocks,
 // k-atoms innermost; inside an atom, row r = 32*m1 + m0 and k-block kk sit at

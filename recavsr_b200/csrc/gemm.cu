@@ -355,17 +355,27 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
           for (int j = 0; j < 16; ++j) v[j] = rc::bf16_to_float(rc::bf16_bits(gelu_tanh(v[j])));
           float amax = 0.f;
 #pragma unroll
-          for (int j = 0; j < 16; ++j) amax = fmaxf(amax, fabsf(v[j]));
+          for (int j = 0; j < 16; ++j) amax = rc::absmax_nan(amax, v[j]);
           float sc = __fmul_rn(__fdiv_rn(amax, 6.0f), p.q_g);
           sc = sc < 0.001953125f ? 0.001953125f : sc;
           const uint8_t sfb = rc::e4m3_from_float(sc);
           const float sd = rc::e4m3_to_float(sfb);
           uint32_t lo = 0, hi = 0;
+          if (p.q_g == 1.0f) {
+            const rc::E2m1Bounds bd(sd);
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const uint32_t code = rc::e2m1_code(__fdiv_rn(__fmul_rn(v[j], p.q_g), sd));
-            if (j < 8) lo |= code << (4 * j);
-            else hi |= code << (4 * (j - 8));
+            for (int j = 0; j < 16; ++j) {
+              const uint32_t code = bd.code(v[j]);
+              if (j < 8) lo |= code << (4 * j);
+              else hi |= code << (4 * (j - 8));
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const uint32_t code = rc::e2m1_code(__fdiv_rn(__fmul_rn(v[j], p.q_g), sd));
+              if (j < 8) lo |= code << (4 * j);
+              else hi |= code << (4 * (j - 8));
+            }
           }
           *reinterpret_cast<uint2*>(p.q_codes + (size_t)row * (p.N >> 1) + (n0 >> 1)) = make_uint2(lo, hi);
           p.q_sf[rc::sf_offset(row, n0 >> 4, (p.N + 63) >> 6)] = sfb;

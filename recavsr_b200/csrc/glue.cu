@@ -1,9 +1,9 @@
 // Row-wise glue around the DiT linears: LayerNorm (+affine) (+AdaLN
 // modulation) with an optional fused NVFP4 quantizer, RMSNorm across heads
 // with the spatial rotary embedding, the temporal rotary embedding, and the
-// KV-cache plane commit. Row kernels run one CTA per row and one thread per
-// 16-element quantization block (N <= 4096), so the row stays in registers and
-// each input byte is read from HBM once.
+// KV-cache plane commit. Row kernels run one CTA per row and one thread per 8
+// elements (a lane pair per 16-element quantization block, N <= 4096), so the
+// row stays in registers and each input byte is read from HBM once.
 //
 // Numerics follow recavsr_infer/runtime/transformer.py:88-133 in eager order:
 //   LN in fp32 (two-pass mean / variance, rsqrt(var + eps)), then
@@ -46,7 +46,7 @@ struct LnArgs {
   int M, N;
 };
 
-// Block-wide sum over up to 8 warps (blockDim <= 256).
+// Block-wide sum over up to 16 warps (blockDim <= 512).
 __device__ __forceinline__ float block_sum(float v, float* red) {
   v = warp_sum(v);
   const int w = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
@@ -58,77 +58,69 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
   return t;
 }
 
-__device__ __forceinline__ void load16(const __nv_bfloat16* p, float (&f)[16]) {
-  const uint4* q = reinterpret_cast<const uint4*>(p);
-  float a[8], b[8];
-  unpack8(__ldg(q), a);
-  unpack8(__ldg(q + 1), b);
-#pragma unroll
-  for (int j = 0; j < 8; ++j) { f[j] = a[j]; f[8 + j] = b[j]; }
-}
-__device__ __forceinline__ void loadf16(const float* p, float (&f)[16]) {
+__device__ __forceinline__ void loadf8(const float* p, float (&f)[8]) {
   const float4* q = reinterpret_cast<const float4*>(p);
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const float4 v = __ldg(q + j);
-    f[4 * j] = v.x; f[4 * j + 1] = v.y; f[4 * j + 2] = v.z; f[4 * j + 3] = v.w;
-  }
+  const float4 a = __ldg(q), b = __ldg(q + 1);
+  f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w; f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
 }
 
-// NVFP4 encode of one 16-element block held by this thread; returns the scale
-// byte and writes the 8 code bytes. Thread t of the row owns k-block t.
-__device__ __forceinline__ uint8_t quant16(const float (&f)[16], float g, uint2& packed) {
+// NVFP4 encode of one 16-element block split over a lane pair (lanes 2b and
+// 2b+1 hold elements 0-7 and 8-15). Returns this lane's 4 code bytes; both
+// lanes get the block's scale byte.
+__device__ __forceinline__ uint32_t quant8_pair(const float (&f)[8], float g, uint8_t& sfb) {
   float amax = 0.f;
 #pragma unroll
-  for (int j = 0; j < 16; ++j) amax = fmaxf(amax, fabsf(f[j]));
+  for (int j = 0; j < 8; ++j) amax = rc::absmax_nan(amax, f[j]);
+  amax = rc::absmax_nan(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
   float sc = __fmul_rn(__fdiv_rn(amax, 6.0f), g);
   sc = sc < 0.001953125f ? 0.001953125f : sc;
-  const uint8_t sfb = rc::e4m3_from_float(sc);
+  sfb = rc::e4m3_from_float(sc);
   const float sd = rc::e4m3_to_float(sfb);
-  uint32_t lo = 0, hi = 0;
+  uint32_t w = 0;
+  if (g == 1.0f) {
+    const rc::E2m1Bounds bd(sd);
 #pragma unroll
-  for (int j = 0; j < 16; ++j) {
-    const uint32_t c = rc::e2m1_code(__fdiv_rn(__fmul_rn(f[j], g), sd));
-    if (j < 8) lo |= c << (4 * j);
-    else hi |= c << (4 * (j - 8));
+    for (int j = 0; j < 8; ++j) w |= bd.code(f[j]) << (4 * j);
+  } else {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) w |= rc::e2m1_code(__fdiv_rn(__fmul_rn(f[j], g), sd)) << (4 * j);
   }
-  packed = make_uint2(lo, hi);
-  return sfb;
+  return w;
 }
 
-// Stores the scale bytes of 4 consecutive k-blocks (threads 4a..4a+3) as one word.
-__device__ __forceinline__ void store_sf4(uint8_t* sf, int row, int kb, int katoms, uint8_t b, bool live) {
+// Scale bytes of 4 consecutive k-blocks = lanes 8a, 8a+2, 8a+4, 8a+6: one word.
+__device__ __forceinline__ void store_sf4_pairs(uint8_t* sf, int row, int kb, int katoms, uint8_t b,
+                                                bool live) {
   const uint32_t b0 = b;
-  const uint32_t b1 = __shfl_down_sync(0xffffffffu, b0, 1);
-  const uint32_t b2 = __shfl_down_sync(0xffffffffu, b0, 2);
-  const uint32_t b3 = __shfl_down_sync(0xffffffffu, b0, 3);
-  if (live && (kb & 3) == 0)
+  const uint32_t b1 = __shfl_down_sync(0xffffffffu, b0, 2);
+  const uint32_t b2 = __shfl_down_sync(0xffffffffu, b0, 4);
+  const uint32_t b3 = __shfl_down_sync(0xffffffffu, b0, 6);
+  if (live && (threadIdx.x & 7) == 0)
     *reinterpret_cast<uint32_t*>(sf + rc::sf_offset(row, kb, katoms)) =
         b0 | (b1 << 8) | (b2 << 16) | (b3 << 24);
 }
 
-// One CTA per row, one thread per 16-element block (N/16 threads).
-__global__ void __launch_bounds__(256) ln_modulate_kernel(LnArgs a) {
-  __shared__ float red[8];
+// One CTA per row, one thread per 8 elements (N/8 threads, N <= 4096).
+__global__ void __launch_bounds__(512) ln_modulate_kernel(LnArgs a) {
+  __shared__ float red[16];
   const int row = blockIdx.x;
   const int t = threadIdx.x;
-  const int nkb = a.N >> 4;
-  const bool live = t < nkb;
-  const int n0 = t * 16;
-  float f[16];
-  if (live) load16(a.x + (size_t)row * a.ldx + n0, f);
+  const bool live = t * 8 < a.N;
+  const int n0 = t * 8;
+  float f[8];
+  if (live) unpack8(__ldg(reinterpret_cast<const uint4*>(a.x + (size_t)row * a.ldx + n0)), f);
   else {
 #pragma unroll
-    for (int j = 0; j < 16; ++j) f[j] = 0.f;
+    for (int j = 0; j < 8; ++j) f[j] = 0.f;
   }
   float s = 0.f;
 #pragma unroll
-  for (int j = 0; j < 16; ++j) s += f[j];
+  for (int j = 0; j < 8; ++j) s += f[j];
   const float mean = __fdiv_rn(block_sum(s, red), (float)a.N);
   float m2 = 0.f;
   if (live) {
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
+    for (int j = 0; j < 8; ++j) {
       const float d = f[j] - mean;
       m2 = fmaf(d, d, m2);
     }
@@ -136,13 +128,13 @@ __global__ void __launch_bounds__(256) ln_modulate_kernel(LnArgs a) {
   const float var = __fdiv_rn(block_sum(m2, red), (float)a.N);
   const float rstd = rsqrtf(var + a.eps);
   if (live) {
-    float w[16], b[16], sh[16], sc[16];
-    if (a.weight) load16(a.weight + n0, w);
-    if (a.bias) load16(a.bias + n0, b);
-    if (a.scale) loadf16(a.scale + n0, sc);
-    if (a.shift) loadf16(a.shift + n0, sh);
+    float w[8], b[8], sh[8], sc[8];
+    if (a.weight) unpack8(__ldg(reinterpret_cast<const uint4*>(a.weight + n0)), w);
+    if (a.bias) unpack8(__ldg(reinterpret_cast<const uint4*>(a.bias + n0)), b);
+    if (a.scale) loadf8(a.scale + n0, sc);
+    if (a.shift) loadf8(a.shift + n0, sh);
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
+    for (int j = 0; j < 8; ++j) {
       float y = __fmul_rn(f[j] - mean, rstd);
       if (a.weight) y = __fmul_rn(y, w[j]);
       if (a.bias) y = __fadd_rn(y, b[j]);
@@ -150,20 +142,13 @@ __global__ void __launch_bounds__(256) ln_modulate_kernel(LnArgs a) {
       if (a.shift) y = __fadd_rn(y, sh[j]);
       f[j] = rc::bf16_to_float(rc::bf16_bits(y));
     }
-    if (a.out) {
-      float lo[8], hi[8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) { lo[j] = f[j]; hi[j] = f[8 + j]; }
-      uint4* dst = reinterpret_cast<uint4*>(a.out + (size_t)row * a.ldo + n0);
-      dst[0] = pack8(lo);
-      dst[1] = pack8(hi);
-    }
+    if (a.out) *reinterpret_cast<uint4*>(a.out + (size_t)row * a.ldo + n0) = pack8(f);
   }
   if (a.codes) {
-    uint2 packed;
-    const uint8_t sfb = quant16(f, a.g, packed);
-    if (live) *reinterpret_cast<uint2*>(a.codes + (size_t)row * (a.N >> 1) + (size_t)t * 8) = packed;
-    store_sf4(a.sf, row, t, (nkb + 3) >> 2, live ? sfb : 0, live);
+    uint8_t sfb;
+    const uint32_t w = quant8_pair(f, a.g, sfb);
+    if (live) *reinterpret_cast<uint32_t*>(a.codes + (size_t)row * (a.N >> 1) + (size_t)t * 4) = w;
+    store_sf4_pairs(a.sf, row, t >> 1, ((a.N >> 4) + 3) >> 2, live ? sfb : 0, live);
   }
 }
 
@@ -189,51 +174,46 @@ struct RmsArgs {
   int M, N, d, span;
 };
 
-// One CTA per (row, tensor), one thread per 16 elements.
-__global__ void __launch_bounds__(256) rmsnorm_rope_kernel(RmsArgs a) {
-  __shared__ float red[8];
+// One CTA per (row, tensor), one thread per 8 elements.
+__global__ void __launch_bounds__(512) rmsnorm_rope_kernel(RmsArgs a) {
+  __shared__ float red[16];
   const int row = blockIdx.x, tsel = blockIdx.y, t = threadIdx.x;
-  const int n0 = t * 16;
+  const int n0 = t * 8;
   const bool live = n0 < a.N;
-  float f[16];
-  if (live) load16(a.x[tsel] + (size_t)row * a.ldx[tsel] + n0, f);
+  float f[8];
+  if (live) unpack8(__ldg(reinterpret_cast<const uint4*>(a.x[tsel] + (size_t)row * a.ldx[tsel] + n0)), f);
   else {
 #pragma unroll
-    for (int j = 0; j < 16; ++j) f[j] = 0.f;
+    for (int j = 0; j < 8; ++j) f[j] = 0.f;
   }
   const __nv_bfloat16* w = a.w[tsel];
   float r = 0.f;
   if (w) {
     float ss = 0.f;
 #pragma unroll
-    for (int j = 0; j < 16; ++j) ss = fmaf(f[j], f[j], ss);
+    for (int j = 0; j < 8; ++j) ss = fmaf(f[j], f[j], ss);
     r = rsqrtf(__fdiv_rn(block_sum(ss, red), (float)a.N) + a.eps);
   }
   if (!live) return;
   if (w) {
-    float wf[16];
-    load16(w + n0, wf);
+    float wf[8];
+    unpack8(__ldg(reinterpret_cast<const uint4*>(w + n0)), wf);
 #pragma unroll
-    for (int j = 0; j < 16; ++j) f[j] = rc::bf16_to_float(rc::bf16_bits(__fmul_rn(__fmul_rn(f[j], r), wf[j])));
+    for (int j = 0; j < 8; ++j) f[j] = rc::bf16_to_float(rc::bf16_bits(__fmul_rn(__fmul_rn(f[j], r), wf[j])));
   }
   if (a.cos) {
-    const int pos = row % a.span, dd = n0 % a.d;   // 16 | d: a thread never straddles heads
-    float c[16], sn[16];
-    loadf16(a.cos + (size_t)pos * a.d + dd, c);
-    loadf16(a.sin + (size_t)pos * a.d + dd, sn);
+    const int pos = row % a.span, dd = n0 % a.d;   // 8 | d: a thread never straddles heads
+    float c[8], sn[8];
+    loadf8(a.cos + (size_t)pos * a.d + dd, c);
+    loadf8(a.sin + (size_t)pos * a.d + dd, sn);
 #pragma unroll
-    for (int j = 0; j < 16; j += 2) {
+    for (int j = 0; j < 8; j += 2) {
       const float e = f[j], o = f[j + 1];
       f[j] = __fsub_rn(__fmul_rn(e, c[j]), __fmul_rn(o, sn[j]));
       f[j + 1] = __fadd_rn(__fmul_rn(e, sn[j]), __fmul_rn(o, c[j]));
     }
   }
-  float lo[8], hi[8];
-#pragma unroll
-  for (int j = 0; j < 8; ++j) { lo[j] = f[j]; hi[j] = f[8 + j]; }
-  uint4* dst = reinterpret_cast<uint4*>(a.out[tsel] + (size_t)row * a.ldo[tsel] + n0);
-  dst[0] = pack8(lo);
-  dst[1] = pack8(hi);
+  *reinterpret_cast<uint4*>(a.out[tsel] + (size_t)row * a.ldo[tsel] + n0) = pack8(f);
 }
 
 // Temporal rotary on the first `td` dims of every head of `planes` planes of
@@ -353,7 +333,7 @@ int rc_ln_modulate_quant(const void* x, long long ldx, int M, int N, const void*
            reinterpret_cast<const __nv_bfloat16*>(weight), reinterpret_cast<const __nv_bfloat16*>(bias),
            shift, scale, eps, reinterpret_cast<__nv_bfloat16*>(out), ldo, codes, scales_swizzled,
            global_scale, M, N};
-  const int threads = ((N / 16) + 31) / 32 * 32;
+  const int threads = ((N / 8) + 31) / 32 * 32;
   ln_modulate_kernel<<<M, threads, 0, stream>>>(a);
   int r = rc::check_launch("rc_ln_modulate_quant");
   if (r || !codes) return r;
@@ -374,8 +354,8 @@ int rc_rmsnorm_rope(int n_tensors, const void* const* xs, const long long* ldx,
                     const void* const* weights, void* const* outs, const long long* ldo, int M,
                     int N, int d, int span, const float* cos, const float* sin, float eps,
                     cudaStream_t stream) {
-  if (n_tensors < 1 || n_tensors > 2 || M < 0 || N <= 0 || N % 16 || N > 4096 ||
-      d <= 0 || d % 16 || N % d || span <= 0)
+  if (n_tensors < 1 || n_tensors > 2 || M < 0 || N <= 0 || N % 8 || N > 4096 ||
+      d <= 0 || d % 8 || N % d || span <= 0)
     return rc::set_error(RC_ERR_ARG, "rc_rmsnorm_rope: bad shape (N=%d d=%d span=%d)", N, d, span);
   RmsArgs a{};
   for (int t = 0; t < n_tensors; ++t) {
@@ -400,7 +380,7 @@ int rc_rmsnorm_rope(int n_tensors, const void* const* xs, const long long* ldx,
   a.span = span;
   if (M == 0) return RC_OK;
   dim3 grid(M, n_tensors);
-  rmsnorm_rope_kernel<<<grid, ((N / 16) + 31) / 32 * 32, 0, stream>>>(a);
+  rmsnorm_rope_kernel<<<grid, ((N / 8) + 31) / 32 * 32, 0, stream>>>(a);
   return rc::check_launch("rc_rmsnorm_rope");
 }
 

@@ -41,17 +41,27 @@ nvfp4_quantize_kernel(const __nv_bfloat16* __restrict__ x, int M, int K, long lo
     }
     float amax = 0.0f;
 #pragma unroll
-    for (int j = 0; j < 16; ++j) amax = fmaxf(amax, fabsf(f[j]));
+    for (int j = 0; j < 16; ++j) amax = rc::absmax_nan(amax, f[j]);
     float sc = __fmul_rn(__fdiv_rn(amax, 6.0f), g);
     sc = sc < 0.001953125f ? 0.001953125f : sc;   // clamp_min(2^-9); NaN passes through
     sf = rc::e4m3_from_float(sc);
     const float sd = rc::e4m3_to_float(sf);
     uint32_t lo = 0, hi = 0;
+    if (g == 1.0f) {
+      const rc::E2m1Bounds bd(sd);
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      const uint32_t c = rc::e2m1_code(__fdiv_rn(__fmul_rn(f[j], g), sd));
-      if (j < 8) lo |= c << (4 * j);
-      else hi |= c << (4 * (j - 8));
+      for (int j = 0; j < 16; ++j) {
+        const uint32_t c = bd.code(f[j]);
+        if (j < 8) lo |= c << (4 * j);
+        else hi |= c << (4 * (j - 8));
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const uint32_t c = rc::e2m1_code(__fdiv_rn(__fmul_rn(f[j], g), sd));
+        if (j < 8) lo |= c << (4 * j);
+        else hi |= c << (4 * (j - 8));
+      }
     }
     *reinterpret_cast<uint2*>(codes + (size_t)row * (K >> 1) + (size_t)kb * 8) = make_uint2(lo, hi);
   }

@@ -71,7 +71,7 @@ def routed_attention(q, ck, cv, pk, pv, slots, past_positions, query_positions, 
               pk.data_ptr() if cap else None, pv.data_ptr() if cap else None, st,
               _lib.ptr(si), _lib.ptr(pp), qp.data_ptr(), cc.data_ptr(), ss.data_ptr(),
               b, frames, cap, height, width, heads, d, cos.shape[-1] * 2, window_h, window_w,
-              ws.data_ptr(), ws_bytes, out.data_ptr(), out.stride(1), _lib.stream(dev))
+              ws.data_ptr(), ws_bytes, out.data_ptr(), out.stride(1), None, None, _lib.stream(dev))
     return out
 
 

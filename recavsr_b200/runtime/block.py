@@ -6,10 +6,10 @@
   LN1+AdaLN -> NVFP4 codes (one quantization shared by q, k and v)
   one QKV GEMM (N = 3*dim, bias)             [the reference runs 3 GEMMs + 3 quantizers]
   RMSNorm(q), RMSNorm(k) + spatial RoPE      (one kernel, both tensors)
-  routed attention (temporal RoPE, cache planes read in place via slot ids)
-  NVFP4 quantize -> o-proj GEMM, epilogue h = h + y * gate
-  LN2(affine) -> NVFP4 -> cross-q GEMM -> RMSNorm -> cross attention (512 keys)
-  NVFP4 quantize -> cross-o GEMM, epilogue h = h + y
+  routed attention (temporal RoPE, cache planes read in place via slot ids),
+      output quantized to NVFP4 in its epilogue -> o-proj GEMM, epilogue h = h + y * gate
+  LN2(affine) -> NVFP4 -> cross-q GEMM -> RMSNorm -> cross attention (512 keys),
+      NVFP4 epilogue -> cross-o GEMM, epilogue h = h + y
   LN3+AdaLN -> NVFP4 -> ffn_up GEMM, epilogue GELU(tanh) -> NVFP4 codes for ffn_down
   ffn_down GEMM, epilogue h = h + y * cgate
 All intermediate roundings (bf16 outputs of every linear, of the norms and of
@@ -168,11 +168,10 @@ class FusedBlock(torch.nn.Module):
                                 (C.c_longlong * 2)(dim, dim), n, dim, self.head_dim,
                                 self.height * self.width, self.tables["spatial_cos"].data_ptr(),
                                 self.tables["spatial_sin"].data_ptr(), _EPS, st), "rmsnorm_rope")
-        # 4. routed attention
-        self._attention(lib, ws, past_key, past_value, slots, past_positions, query_positions, n, st)
+        # 4. routed attention, output NVFP4-quantized in its epilogue
+        self._attention(lib, ws, past_key, past_value, slots, past_positions, query_positions, n, st,
+                        quantized=True)
         # 5. o-proj with gated residual
-        chk(lib.rc_nvfp4_quantize(ws.attn.data_ptr(), n, dim, dim, 1.0, ws.a_codes.data_ptr(),
-                                  ws.a_scales.data_ptr(), st), "quant_o")
         self._gemm(lib, ws.a_codes, ws.a_scales, self.o, n, _lib.EPI_GATED_RESIDUAL, h, st, gate)
         # 6. cross attention
         chk(lib.rc_ln_modulate_quant(h.data_ptr(), dim, n, dim, self.norm2_w.data_ptr(),
@@ -187,9 +186,8 @@ class FusedBlock(torch.nn.Module):
         strides = (C.c_longlong * 9)(0, dim, hd, 0, dim, hd, 0, dim, hd)
         chk(lib.rc_cross_attention(ws.q_rot.data_ptr(), self.cross_k.data_ptr(),
                                    self.cross_v.data_ptr(), strides, 1, n, self.cross_k.shape[0],
-                                   self.heads, hd, ws.attn.data_ptr(), dim, st), "cross_attn")
-        chk(lib.rc_nvfp4_quantize(ws.attn.data_ptr(), n, dim, dim, 1.0, ws.a_codes.data_ptr(),
-                                  ws.a_scales.data_ptr(), st), "quant_co")
+                                   self.heads, hd, None, dim, ws.a_codes.data_ptr(),
+                                   ws.a_scales.data_ptr(), st), "cross_attn")
         self._gemm(lib, ws.a_codes, ws.a_scales, self.co, n, _lib.EPI_RESIDUAL, h, st)
         # 7. FFN
         chk(lib.rc_ln_modulate_quant(h.data_ptr(), dim, n, dim, None, None, cshift.data_ptr(),
@@ -208,7 +206,9 @@ class FusedBlock(torch.nn.Module):
                                      out.data_ptr(), out.stride(0), _lib.ptr(gate), None, None,
                                      1.0, st), "nvfp4_gemm")
 
-    def _attention(self, lib, ws, past_key, past_value, slots, ppos, qpos, n, st):
+    def _attention(self, lib, ws, past_key, past_value, slots, ppos, qpos, n, st, quantized=False):
+        """Routed attention into ws.attn (bf16) or, with quantized=True, straight
+        into the NVFP4 operand of the o-proj (ws.a_codes / ws.a_scales)."""
         dim, hd, heads = self.dim, self.head_dim, self.heads
         span = self.height * self.width
         frames = n // span
@@ -226,7 +226,10 @@ class FusedBlock(torch.nn.Module):
             slots.data_ptr() if cap else None, ppos.data_ptr() if cap else None, qpos.data_ptr(),
             self.tables["temporal_cos"].data_ptr(), self.tables["temporal_sin"].data_ptr(),
             1, frames, cap, self.height, self.width, heads, hd, self.tables["temporal_cos"].shape[1] * 2,
-            wh, ww, ws.attn_ws.data_ptr(), ws.attn_ws.numel(), ws.attn.data_ptr(), dim, st),
+            wh, ww, ws.attn_ws.data_ptr(), ws.attn_ws.numel(),
+            None if quantized else ws.attn.data_ptr(), dim,
+            ws.a_codes.data_ptr() if quantized else None,
+            ws.a_scales.data_ptr() if quantized else None, st),
             "attention")
 
 

@@ -147,7 +147,7 @@ def test_cross_attention(nq, nk, heads):
     hd = heads * 128
     st = (C.c_longlong * 9)(0, hd, 128, 0, hd, 128, 0, hd, 128)
     _lib.call("rc_cross_attention", dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), st, 1, nq, nk,
-              heads, 128, out.data_ptr(), hd, _lib.stream())
+              heads, 128, out.data_ptr(), hd, None, None, _lib.stream())
     assert_no_device_error()
     hs = [0, heads - 1]
     ref = oatt.plain_attention(q[:, hs], k[:, hs], v[:, hs])
@@ -157,3 +157,37 @@ def test_cross_attention(nq, nk, heads):
 
 def test_routed_attention_six_heads_small_plane():
     _run(8, 12, 22, 40, 2, [1, 0], [3, 4], [5, 6], heads=6)
+
+
+def test_attention_fused_nvfp4_output():
+    """The optional NVFP4 output equals rc_nvfp4_quantize of the bf16 output."""
+    import ctypes as C
+    from recavsr_b200 import _lib
+    from recavsr_b200.runtime.block import rope_tables
+    from recavsr_b200.runtime.nvfp4 import quantize, scale_numel
+    H, W, heads = 22, 40, 24
+    t = H * W
+    rs = np.random.RandomState(9)
+    q, k, v = (dev_bf16(recipes.bf16_normal(rs, (1, 2 * t, heads, 128))) for _ in range(3))
+    pk, pv = (dev_bf16(recipes.bf16_normal(rs, (1, 2 * t, heads, 128))) for _ in range(2))
+    tb = rope_tables(128, H, W, "cuda")
+    slots = torch.tensor([1, 0], dtype=torch.int32, device="cuda")
+    ppos = torch.tensor([3, 4], dtype=torch.int32, device="cuda")
+    qpos = torch.tensor([5, 6], dtype=torch.int32, device="cuda")
+    n, dim = 2 * t, heads * 128
+    out = torch.empty(1, n, heads, 128, dtype=torch.bfloat16, device="cuda")
+    codes = torch.empty(n, dim // 2, dtype=torch.uint8, device="cuda")
+    sf = torch.full((scale_numel(n, dim),), 0x5A, dtype=torch.uint8, device="cuda")
+    wsb = _lib.library().rc_paired_attention_workspace(1, 2, 2, H, W, heads, 128)
+    ws = torch.empty(wsb, dtype=torch.uint8, device="cuda")
+    st = []
+    for x in (q, k, v, pk, pv):
+        st += [x.stride(0), x.stride(1), x.stride(2)]
+    _lib.call("rc_paired_attention", q.data_ptr(), k.data_ptr(), v.data_ptr(), pk.data_ptr(),
+              pv.data_ptr(), (C.c_longlong * 15)(*st), slots.data_ptr(), ppos.data_ptr(),
+              qpos.data_ptr(), tb["temporal_cos"].data_ptr(), tb["temporal_sin"].data_ptr(), 1, 2, 2,
+              H, W, heads, 128, 44, H, W, ws.data_ptr(), wsb, out.data_ptr(), dim, codes.data_ptr(),
+              sf.data_ptr(), _lib.stream())
+    rc_, rs_ = quantize(out.reshape(n, dim))
+    assert_no_device_error()
+    assert torch.equal(codes, rc_) and torch.equal(sf, rs_)

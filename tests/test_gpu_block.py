@@ -176,7 +176,7 @@ def test_fused_block_stagewise_vs_oracle():
     strides = (C.c_longlong * 9)(0, dim, 128, 0, dim, 128, 0, dim, 128)
     _lib.check(lib.rc_cross_attention(ws.q_rot.data_ptr(), blk.cross_k.data_ptr(),
                                       blk.cross_v.data_ptr(), strides, 1, n, blk.cross_k.shape[0],
-                                      heads, 128, ws.attn.data_ptr(), dim, st), "cross")
+                                      heads, 128, ws.attn.data_ptr(), dim, None, None, st), "cross")
     sync()
     ca = host(ws.attn)
     rca = plain_attention(host(ws.q_rot).reshape(n, heads, 128), host(blk.cross_k), host(blk.cross_v))

@@ -6,7 +6,7 @@ import torch
 
 from oracle import fp8 as ofp8
 from oracle import nvfp4 as onv
-from oracle.numerics import bf16_from_bits
+from oracle.numerics import bf16_from_bits, bf16_round
 from tests.golden import recipes
 from tests.util import assert_no_device_error, dev_bf16
 
@@ -69,3 +69,28 @@ def test_fp8_quantize_cfg3():
     rq, rscale = ofp8.quantize(x)
     assert np.float32(scale.item()) == rscale
     np.testing.assert_array_equal(q.cpu().numpy(), rq)
+
+
+def test_nvfp4_quantize_every_bf16_value_every_scale():
+    """Blocks [6s, x, ...] pin the block scale to each E4M3 value s in turn and
+    run every bf16 x with |x| <= 6s through the device quantizer."""
+    from recavsr_b200.runtime import nvfp4
+    from oracle.numerics import bf16_from_bits, e4m3_decode
+    allx = bf16_from_bits(np.arange(65536, dtype=np.uint32).astype(np.uint16))
+    allx = allx[np.isfinite(allx)]
+    rows = []
+    for s in e4m3_decode(np.arange(1, 127, dtype=np.uint8)):
+        amax = np.float32(6.0) * s
+        if amax != bf16_round(amax) or amax / np.float32(6.0) < 2.0 ** -9:
+            continue
+        xs = allx[np.abs(allx) <= amax]
+        pad = (-len(xs)) % 15
+        xs = np.concatenate([xs, np.zeros(pad, np.float32)]).reshape(-1, 15)
+        rows.append(np.concatenate([np.full((len(xs), 1), amax, np.float32), xs], 1))
+    blocks = np.concatenate(rows, 0)
+    n = (len(blocks) // 64) * 64
+    x = blocks[:n].reshape(-1, 16 * 64)              # 64 blocks per row
+    codes, scales = nvfp4.quantize(dev_bf16(x))
+    rc, rs = onv.quantize(x)
+    np.testing.assert_array_equal(codes.cpu().numpy(), rc)
+    np.testing.assert_array_equal(scales.cpu().numpy(), rs)

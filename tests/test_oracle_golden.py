@@ -143,3 +143,24 @@ def test_block_forward_matches_reference(golden, tag):
     rel = np.linalg.norm(h - ref_h) / np.linalg.norm(ref_h)
     assert rel < 0.06, rel
     assert np.abs(h - ref_h).max() < 0.15 * np.abs(ref_h).max()
+
+
+def test_division_free_e2m1_ladder_is_exact():
+    """The kernels code NVFP4 without dividing: |x| compared against t*s for the
+    seven E2M1 thresholds t. For every bf16 x and every positive E4M3 scale s
+    this equals the reference ladder applied to fl32(x / s) (exhaustive)."""
+    from oracle.numerics import bf16_from_bits, e4m3_decode
+    x = bf16_from_bits(np.arange(65536, dtype=np.uint32).astype(np.uint16))
+    x = x[~np.isnan(x)]
+    scales = e4m3_decode(np.arange(1, 127, dtype=np.uint8))
+    thr = ((0.25, False), (0.75, True), (1.25, False), (1.75, True), (2.5, False), (3.5, True), (5.0, False))
+    ax = np.abs(x)
+    for s in scales.astype(np.float32):
+        with np.errstate(over="ignore", invalid="ignore"):
+            ref = nvfp4.e2m1_codes((x / s).astype(np.float32))
+        code = np.zeros(x.shape, np.uint8)
+        for t, inclusive in thr:
+            b = np.float32(t) * s          # exact: <= 7 significant bits
+            code += (ax >= b) if inclusive else (ax > b)
+        code |= (x < 0).astype(np.uint8) * 8
+        np.testing.assert_array_equal(code, ref)
