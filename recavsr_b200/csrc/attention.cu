@@ -21,8 +21,10 @@
 //  2. attention: one CTA per (128-query tile, head). Warp 0 = TMA producer
 //     (Q once, then K (workspace) and V (cache slot / current frame) tiles of
 //     128 keys, double-buffered), warp 1 = tcgen05 MMA issuer (S = Q K^T into a
-//     double-buffered TMEM S, O += P V into TMEM), warps 2-5 = online softmax
-//     (exp2, lazily rescaled running max), P to shared memory, epilogue.
+//     double-buffered TMEM S, O += P V into TMEM), warps 2-9 = online softmax
+//     (two warps per TMEM lane quadrant, 64 key columns each; exp2 with a
+//     lazily rescaled running max; P double-buffered in shared memory so the
+//     softmax of tile i+1 overlaps the P.V of tile i), then the epilogue.
 //   Dense mode (window covers the grid): query tiles are 128 consecutive tokens,
 //   key tiles 128 consecutive tokens of a plane (4-D TMA view, the plane tail
 //   reads as zeros). Local mode: query tiles are 2 frames x 8 x 8 tokens, key
@@ -34,7 +36,7 @@ namespace {
 constexpr int kD = 128;             // head dim supported by the tcgen05 kernel
 constexpr int kBM = 128;            // queries per CTA
 constexpr int kBN = 128;            // keys per tile
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;             // producer, MMA, 8 softmax warps
 constexpr int kLocalQH = 8, kLocalQW = 8;   // local query tile: 2 frames x 8 x 8
 constexpr int kLocalKH = 8, kLocalKW = 16;  // local key box: 8 rows x 16 cols
 constexpr int kMaxPlanes = 16;
@@ -64,7 +66,8 @@ struct SmemLayout {
   static constexpr int offBar = offP + 4 * kChunk;
   static constexpr int kBars = 16;
   static constexpr int offMisc = offBar + kBars * 8;
-  static constexpr int kTotal = offMisc + 16 + kMaxPlanes * 4;
+  static constexpr int offRed = offMisc + 16 + kMaxPlanes * 4;   // [2][2][128] floats
+  static constexpr int kTotal = offRed + 2 * 2 * 128 * 4;
   static constexpr int kAlloc = kTotal + 1024;
 };
 
@@ -167,8 +170,8 @@ attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       sm100::mbar_init(&kv_full[s2], 1);
       sm100::mbar_init(&kv_empty[s2], 1);
       sm100::mbar_init(&s_full[s2], 1);
-      sm100::mbar_init(&s_free[s2], 128);
-      sm100::mbar_init(&p_full[s2], 128);
+      sm100::mbar_init(&s_free[s2], 256);
+      sm100::mbar_init(&p_full[s2], 256);
       sm100::mbar_init(&o_done[s2], 1);
     }
     sm100::mbar_init(done, 1);
@@ -285,9 +288,15 @@ attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
     }
   } else {
     // ----------------------------------------------------------- softmax
+    // Two warps per TMEM lane quadrant: `half` selects key columns
+    // [64*half, 64*half+64) of S, the matching P chunk and O columns.
     const int quad = warp & 3;
+    const int half = (warp - 2) >> 2;
     const int r = quad * 32 + lane;               // query row within the tile / TMEM lane
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
+    const int cbase = half * 64;
+    float* red = reinterpret_cast<float*>(smem + L::offRed);   // [2 tiles][2 halves][128 rows]
+    auto pair_sync = [&]() { asm volatile("bar.sync %0, 64;" ::"r"(1 + quad) : "memory"); };
     int qrow = -1, qy = 0, qx = 0;
     if (!p.local) {
       const int t = q_row0 + r;
@@ -310,31 +319,57 @@ attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       int a, b;
       it.tile_origin(i % tpp, a, b);
       const bool full_tile = !p.local && a + kBN <= p.T;
-      const uint32_t t_s = t_s0 + st * 128 + lane_off;
-      // Pass 1: row max over the tile (raw scores; scale > 0 commutes with max).
-      float mt = -INFINITY;
-#pragma unroll 1
-      for (int c = 0; c < kBN; c += 32) {
-        uint32_t v[32];
-        RC_TMEM_LD_X32(t_s + c, v);
+      float v[64];
+      {
+        const uint32_t t_s = t_s0 + st * 128 + cbase + lane_off;
+        uint32_t r0[16], r1[16], r2[16], r3[16];
+        sm100::tmem_ld16(t_s, r0);
+        sm100::tmem_ld16(t_s + 16, r1);
+        sm100::tmem_ld16(t_s + 32, r2);
+        sm100::tmem_ld16(t_s + 48, r3);
         sm100::tmem_ld_wait();
-        if (full_tile) {
 #pragma unroll
-          for (int j = 0; j < 32; ++j) mt = fmaxf(mt, __uint_as_float(v[j]));
-        } else {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            bool valid;
-            if (!p.local) {
-              valid = a + c + j < p.T;
-            } else {
-              const int jj = c + j, ky = a + jj / kLocalKW, kx = b + jj % kLocalKW;
-              valid = ky < p.H && kx < p.W && ky >= top && ky < top + p.wh && kx >= left && kx < left + p.ww;
-            }
-            if (valid) mt = fmaxf(mt, __uint_as_float(v[j]));
-          }
+        for (int j = 0; j < 16; ++j) {
+          v[j] = __uint_as_float(r0[j]);
+          v[16 + j] = __uint_as_float(r1[j]);
+          v[32 + j] = __uint_as_float(r2[j]);
+          v[48 + j] = __uint_as_float(r3[j]);
         }
       }
+      // S is in registers: the MMA may overwrite this buffer with S(i+2).
+      sm100::tc_fence_before();
+      sm100::mbar_arrive(&s_free[st]);
+      if (!full_tile) {
+        // Validity of this warp's 64 keys as a bit mask: dense = a prefix of the
+        // plane; local = 4 box rows x 16 box columns intersected with the window.
+        uint64_t mask;
+        if (!p.local) {
+          const int cnt = min(max(p.T - (a + cbase), 0), 64);
+          mask = cnt >= 64 ? ~0ull : ((1ull << cnt) - 1ull);
+        } else {
+          uint32_t cols = 0;
+#pragma unroll
+          for (int x = 0; x < kLocalKW; ++x) {
+            const int kx = b + x;
+            cols |= (kx < p.W && kx >= left && kx < left + p.ww) ? (1u << x) : 0u;
+          }
+          mask = 0;
+#pragma unroll
+          for (int y = 0; y < 4; ++y) {
+            const int ky = a + (cbase >> 4) + y;
+            if (ky < p.H && ky >= top && ky < top + p.wh) mask |= (uint64_t)cols << (16 * y);
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < 64; ++j) v[j] = ((mask >> j) & 1ull) ? v[j] : -INFINITY;
+      }
+      float mt = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < 64; ++j) mt = fmaxf(mt, v[j]);
+      // Row max over both halves (raw scores; scale > 0 commutes with max).
+      red[(st * 2 + half) * 128 + r] = mt;
+      pair_sync();
+      mt = fmaxf(mt, red[(st * 2 + (half ^ 1)) * 128 + r]);
       mt = mt == -INFINITY ? -INFINITY : mt * scale;
       // Lazy rescaling: move the reference max only when it grows by > 2^8.
       float corr = 1.0f;
@@ -345,56 +380,35 @@ attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
         m_used = mt;
       }
       const float mref = m_used == -INFINITY ? 0.f : m_used;
+      float sum = 0.f;
+#pragma unroll
+      for (int j = 0; j < 64; ++j) {
+        v[j] = fast_exp2(fmaf(v[j], scale, -mref));   // exp2(-inf) = 0 for masked keys
+        sum += v[j];
+      }
+      l = __fmul_rn(l, corr) + sum;
       // The P buffer of this tile was last read by the P.V of tile i-2.
       if (i >= 2 && !__all_sync(0xffffffffu, wait(&o_done[st], ((i >> 1) - 1) & 1, 7))) { ok = false; break; }
-      uint8_t* sp = smem + L::offP + st * 2 * L::kChunk;
-      // Pass 2: exponentials, row sum, P (bf16) to shared memory (K-major, 128B swizzle).
-      float sum = 0.f;
-#pragma unroll 1
-      for (int c = 0; c < kBN; c += 32) {
-        uint32_t v[32];
-        RC_TMEM_LD_X32(t_s + c, v);
-        sm100::tmem_ld_wait();
-        float e[32];
+      uint8_t* sp = smem + L::offP + st * 2 * L::kChunk + half * L::kChunk;
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          bool valid = true;
-          if (!full_tile) {
-            if (!p.local) {
-              valid = a + c + j < p.T;
-            } else {
-              const int jj = c + j, ky = a + jj / kLocalKW, kx = b + jj % kLocalKW;
-              valid = ky < p.H && kx < p.W && ky >= top && ky < top + p.wh && kx >= left && kx < left + p.ww;
-            }
-          }
-          e[j] = valid ? fast_exp2(fmaf(__uint_as_float(v[j]), scale, -mref)) : 0.f;
-          sum += e[j];
-        }
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int unit = (c >> 3) + u, chunk = unit >> 3, lu = unit & 7;
-          const uint4 w = make_uint4(pack_bf16x2(e[8 * u], e[8 * u + 1]), pack_bf16x2(e[8 * u + 2], e[8 * u + 3]),
-                                     pack_bf16x2(e[8 * u + 4], e[8 * u + 5]), pack_bf16x2(e[8 * u + 6], e[8 * u + 7]));
-          *reinterpret_cast<uint4*>(sp + chunk * L::kChunk + r * 128 + ((lu ^ (r & 7)) << 4)) = w;
-        }
+      for (int u = 0; u < 8; ++u) {
+        const uint4 w = make_uint4(pack_bf16x2(v[8 * u], v[8 * u + 1]), pack_bf16x2(v[8 * u + 2], v[8 * u + 3]),
+                                   pack_bf16x2(v[8 * u + 4], v[8 * u + 5]), pack_bf16x2(v[8 * u + 6], v[8 * u + 7]));
+        *reinterpret_cast<uint4*>(sp + r * 128 + ((u ^ (r & 7)) << 4)) = w;
       }
-      // S is fully consumed: the MMA may overwrite this buffer with S(i+2).
-      sm100::tc_fence_before();
-      sm100::mbar_arrive(&s_free[st]);
-      l = __fmul_rn(l, corr) + sum;
       // O changes only when a row's reference max moved (rare); then wait for P.V(i-1).
       if (__any_sync(0xffffffffu, rescale)) {
         if (!__all_sync(0xffffffffu, wait(&o_done[st ^ 1], ((i - 1) >> 1) & 1, 9))) { ok = false; break; }
         sm100::tc_fence_after();
         const float f = rescale ? corr : 1.0f;
 #pragma unroll 1
-        for (int c = 0; c < kD; c += 16) {
-          uint32_t v[16];
-          sm100::tmem_ld16(t_o + c + lane_off, v);
+        for (int c = cbase; c < cbase + 64; c += 16) {
+          uint32_t w[16];
+          sm100::tmem_ld16(t_o + c + lane_off, w);
           sm100::tmem_ld_wait();
 #pragma unroll
-          for (int j = 0; j < 16; ++j) v[j] = __float_as_uint(__uint_as_float(v[j]) * f);
-          sm100::tmem_st16(t_o + c + lane_off, v);
+          for (int j = 0; j < 16; ++j) w[j] = __float_as_uint(__uint_as_float(w[j]) * f);
+          sm100::tmem_st16(t_o + c + lane_off, w);
         }
         sm100::tmem_st_wait();
       }
@@ -402,6 +416,10 @@ attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       sm100::tc_fence_before();
       sm100::mbar_arrive(&p_full[st]);
     }
+    // Row sum over both halves.
+    red[half * 128 + r] = l;
+    pair_sync();
+    l += red[(half ^ 1) * 128 + r];
     if (ok && n_tiles > 0 &&
         __all_sync(0xffffffffu, wait(&o_done[(n_tiles - 1) & 1], ((n_tiles - 1) >> 1) & 1, 8))) {
       sm100::tc_fence_after();
@@ -409,13 +427,13 @@ attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       __nv_bfloat16* dst = (qrow >= 0 && p.out) ? p.out + (size_t)qrow * p.out_ld + (size_t)head * kD : nullptr;
       const int katoms = (p.heads * kD) >> 6;
 #pragma unroll 1
-      for (int c = 0; c < kD; c += 16) {
-        uint32_t v[16];
-        sm100::tmem_ld16(t_o + c + lane_off, v);
+      for (int c = cbase; c < cbase + 64; c += 16) {
+        uint32_t w16[16];
+        sm100::tmem_ld16(t_o + c + lane_off, w16);
         sm100::tmem_ld_wait();
         float y[16];
 #pragma unroll
-        for (int j = 0; j < 16; ++j) y[j] = rc::bf16_to_float(rc::bf16_bits(__uint_as_float(v[j]) * inv));
+        for (int j = 0; j < 16; ++j) y[j] = rc::bf16_to_float(rc::bf16_bits(__uint_as_float(w16[j]) * inv));
         if (dst) {
           uint32_t w[8];
 #pragma unroll
