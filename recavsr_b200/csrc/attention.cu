@@ -68,7 +68,7 @@ struct SmemLayout {
   static constexpr int offMisc = offBar + kBars * 8;
   static constexpr int offRed = offMisc + 16 + kMaxPlanes * 4;   // [2][2][128] floats
   static constexpr int kTotal = offRed + 2 * 2 * 128 * 4;
-  static constexpr int kAlloc = kTotal + 1024;
+  static constexpr int kAlloc = kTotal;
 };
 
 // Enumerates the key tiles of one query tile: planes in order, tiles within.
@@ -132,8 +132,8 @@ attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
                  const __grid_constant__ CUtensorMap tm_pv, const __grid_constant__ CUtensorMap tm_cv,
                  const AttnParams p) {
   using L = SmemLayout;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // 1024-byte alignment: the 128-byte TMA swizzle pattern repeats every 1024 bytes.
+  extern __shared__ __align__(1024) uint8_t smem[];
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::offBar);
   uint64_t* q_full = bars + 0;
   uint64_t* kv_full = bars + 1;    // [2]
@@ -491,54 +491,81 @@ struct GatherParams {
   int T, QT, CAP, hd, td, d;
 };
 
-// One thread = 8 consecutive elements of one token row (16 bytes).
+// One thread = 8 consecutive elements of one token row (16 bytes); each
+// thread keeps kGatherUnroll independent loads in flight.
+constexpr int kGatherUnroll = 4;
+
+__device__ __forceinline__ bool gather_src(const GatherParams& g, long long i, int vec,
+                                           const __nv_bfloat16*& src, __nv_bfloat16*& dst, int& pos,
+                                           int& dd) {
+  const int v = (int)(i % vec);
+  const long long tok = i / vec;
+  const int plane = (int)(tok / g.T), t = (int)(tok % g.T);
+  const int head = (v * 8) / g.d;
+  dd = (v * 8) % g.d;
+  if (plane < g.QT) {
+    src = g.q + ((long long)plane * g.T + t) * g.q_ld + head * g.q_hs;
+    dst = g.q_out + ((long long)plane * g.T + t) * g.hd;
+    pos = g.qpos[plane];
+  } else if (plane < g.QT + g.CAP) {
+    const int i2 = plane - g.QT;
+    const int slot = g.slots[i2];
+    if (slot < 0 || slot >= g.CAP) return false;
+    src = g.pk + ((long long)slot * g.T + t) * g.pk_ld + head * g.pk_hs;
+    dst = g.k_out + ((long long)i2 * g.T + t) * g.hd;
+    pos = g.ppos[i2];
+  } else {
+    const int f = plane - g.QT - g.CAP;
+    src = g.ck + ((long long)f * g.T + t) * g.ck_ld + head * g.ck_hs;
+    dst = g.k_out + ((long long)(g.CAP + f) * g.T + t) * g.hd;
+    pos = g.qpos[f];
+  }
+  src += dd;
+  dst += head * g.d + dd;
+  return true;
+}
+
 __global__ void rope_gather_kernel(GatherParams g) {
   const int vec = g.hd >> 3;
   const int planes = g.QT + g.CAP + g.QT;
   const long long total = (long long)planes * g.T * vec;
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
-       i += (long long)gridDim.x * blockDim.x) {
-    const int v = (int)(i % vec);
-    const long long tok = i / vec;
-    const int plane = (int)(tok / g.T), t = (int)(tok % g.T);
-    const int head = (v * 8) / g.d, dd = (v * 8) % g.d;
-    const __nv_bfloat16* src;
-    __nv_bfloat16* dst;
-    int pos;
-    if (plane < g.QT) {
-      src = g.q + ((long long)plane * g.T + t) * g.q_ld + head * g.q_hs;
-      dst = g.q_out + ((long long)plane * g.T + t) * g.hd;
-      pos = g.qpos[plane];
-    } else if (plane < g.QT + g.CAP) {
-      const int i2 = plane - g.QT;
-      const int slot = g.slots[i2];
-      if (slot < 0 || slot >= g.CAP) continue;
-      src = g.pk + ((long long)slot * g.T + t) * g.pk_ld + head * g.pk_hs;
-      dst = g.k_out + ((long long)i2 * g.T + t) * g.hd;
-      pos = g.ppos[i2];
-    } else {
-      const int f = plane - g.QT - g.CAP;
-      src = g.ck + ((long long)f * g.T + t) * g.ck_ld + head * g.ck_hs;
-      dst = g.k_out + ((long long)(g.CAP + f) * g.T + t) * g.hd;
-      pos = g.qpos[f];
-    }
-    uint4 raw = *reinterpret_cast<const uint4*>(src + dd);
-    if (dd < g.td) {
-      uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  for (long long base = blockIdx.x * (long long)blockDim.x + threadIdx.x; base < total;
+       base += stride * kGatherUnroll) {
+    uint4 raw[kGatherUnroll];
+    __nv_bfloat16* dst[kGatherUnroll];
+    int pos[kGatherUnroll], dd[kGatherUnroll];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int pr = (dd >> 1) + j;
-        if (2 * pr < g.td) {
-          const float e = __uint_as_float(w[j] << 16), o = __uint_as_float(w[j] & 0xffff0000u);
-          const float c = g.cos[pos * (g.td >> 1) + pr], s = g.sin[pos * (g.td >> 1) + pr];
-          const float ne = __fsub_rn(__fmul_rn(e, c), __fmul_rn(o, s));
-          const float no = __fadd_rn(__fmul_rn(e, s), __fmul_rn(o, c));
-          w[j] = pack_bf16x2(ne, no);
-        }
-      }
-      raw = make_uint4(w[0], w[1], w[2], w[3]);
+    for (int u = 0; u < kGatherUnroll; ++u) {
+      const long long i = base + u * stride;
+      const __nv_bfloat16* src;
+      dst[u] = nullptr;
+      if (i < total && gather_src(g, i, vec, src, dst[u], pos[u], dd[u]))
+        raw[u] = *reinterpret_cast<const uint4*>(src);
+      else
+        dst[u] = nullptr;
     }
-    *reinterpret_cast<uint4*>(dst + head * g.d + dd) = raw;
+#pragma unroll
+    for (int u = 0; u < kGatherUnroll; ++u) {
+      if (!dst[u]) continue;
+      uint4 r4 = raw[u];
+      if (dd[u] < g.td) {
+        uint32_t w[4] = {r4.x, r4.y, r4.z, r4.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int pr = (dd[u] >> 1) + j;
+          if (2 * pr < g.td) {
+            const float e = __uint_as_float(w[j] << 16), o = __uint_as_float(w[j] & 0xffff0000u);
+            const float c = g.cos[pos[u] * (g.td >> 1) + pr], sn = g.sin[pos[u] * (g.td >> 1) + pr];
+            const float ne = __fsub_rn(__fmul_rn(e, c), __fmul_rn(o, sn));
+            const float no = __fadd_rn(__fmul_rn(e, sn), __fmul_rn(o, c));
+            w[j] = pack_bf16x2(ne, no);
+          }
+        }
+        r4 = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+      *reinterpret_cast<uint4*>(dst[u]) = r4;
+    }
   }
 }
 

@@ -87,7 +87,7 @@ struct Smem {
   static constexpr int offBar = offSfb + STAGES * kSfb;
   static constexpr int kBars = 2 * STAGES + 6 + 1;
   static constexpr int kTotal = offBar + kBars * 8 + 16;
-  static constexpr int kAlloc = kTotal + 1024;      // slack for 1024-byte alignment
+  static constexpr int kAlloc = kTotal;
 };
 
 __device__ __forceinline__ float gelu_tanh(float x) {
@@ -111,8 +111,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
   constexpr int kAcc = BN == 128 ? 2 : 1;            // accumulator stages in TMEM
   static_assert(kAcc * BN + 2 * (kSfaCols + kSfbCols) <= kTmemCols, "TMEM budget");
 
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // 1024-byte alignment: the 128-byte TMA swizzle pattern repeats every 1024 bytes.
+  extern __shared__ __align__(1024) uint8_t smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::offBar);
   uint64_t* empty = full + STAGES;
   uint64_t* acc_full = empty + STAGES;     // [2]

@@ -46,18 +46,6 @@ struct LnArgs {
   int M, N;
 };
 
-// Block-wide sum over up to 16 warps (blockDim <= 512).
-__device__ __forceinline__ float block_sum(float v, float* red) {
-  v = warp_sum(v);
-  const int w = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
-  __syncthreads();
-  if ((threadIdx.x & 31) == 0) red[w] = v;
-  __syncthreads();
-  float t = 0.f;
-  for (int i = 0; i < nw; ++i) t += red[i];
-  return t;
-}
-
 __device__ __forceinline__ void loadf8(const float* p, float (&f)[8]) {
   const float4* q = reinterpret_cast<const float4*>(p);
   const float4 a = __ldg(q), b = __ldg(q + 1);
@@ -100,55 +88,98 @@ __device__ __forceinline__ void store_sf4_pairs(uint8_t* sf, int row, int kb, in
         b0 | (b1 << 8) | (b2 << 16) | (b3 << 24);
 }
 
-// One CTA per row, one thread per 8 elements (N/8 threads, N <= 4096).
+// Several rows per CTA (kRowsPerCta), one thread per 8 elements of each row
+// (N/8 threads, N <= 4096): every thread has kRowsPerCta independent 16-byte
+// loads in flight before the first reduction.
+constexpr int kRowsPerCta = 4;
+
+// Block-wide sums of R values per thread (one per row) over up to 16 warps.
+template <int R>
+__device__ __forceinline__ void block_sums(float (&v)[R], float (*red)[16]) {
+#pragma unroll
+  for (int k = 0; k < R; ++k) v[k] = warp_sum(v[k]);
+  const int w = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) {
+#pragma unroll
+    for (int k = 0; k < R; ++k) red[k][w] = v[k];
+  }
+  __syncthreads();
+#pragma unroll
+  for (int k = 0; k < R; ++k) {
+    float t = 0.f;
+    for (int i = 0; i < nw; ++i) t += red[k][i];
+    v[k] = t;
+  }
+}
+
 __global__ void __launch_bounds__(512) ln_modulate_kernel(LnArgs a) {
-  __shared__ float red[16];
-  const int row = blockIdx.x;
+  __shared__ float red[kRowsPerCta][16];
+  const int row0 = blockIdx.x * kRowsPerCta;
   const int t = threadIdx.x;
   const bool live = t * 8 < a.N;
   const int n0 = t * 8;
-  float f[8];
-  if (live) unpack8(__ldg(reinterpret_cast<const uint4*>(a.x + (size_t)row * a.ldx + n0)), f);
-  else {
+  float f[kRowsPerCta][8];
+  uint4 raw[kRowsPerCta];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) f[j] = 0.f;
+  for (int k = 0; k < kRowsPerCta; ++k)
+    raw[k] = (live && row0 + k < a.M)
+                 ? __ldg(reinterpret_cast<const uint4*>(a.x + (size_t)(row0 + k) * a.ldx + n0))
+                 : make_uint4(0, 0, 0, 0);
+  float s[kRowsPerCta];
+#pragma unroll
+  for (int k = 0; k < kRowsPerCta; ++k) {
+    unpack8(raw[k], f[k]);
+    s[k] = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) s[k] += f[k][j];
   }
-  float s = 0.f;
+  block_sums<kRowsPerCta>(s, red);
+  float mean[kRowsPerCta], m2[kRowsPerCta];
 #pragma unroll
-  for (int j = 0; j < 8; ++j) s += f[j];
-  const float mean = __fdiv_rn(block_sum(s, red), (float)a.N);
-  float m2 = 0.f;
-  if (live) {
+  for (int k = 0; k < kRowsPerCta; ++k) {
+    mean[k] = __fdiv_rn(s[k], (float)a.N);
+    m2[k] = 0.f;
+    if (live) {
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const float d = f[j] - mean;
-      m2 = fmaf(d, d, m2);
+      for (int j = 0; j < 8; ++j) {
+        const float d = f[k][j] - mean[k];
+        m2[k] = fmaf(d, d, m2[k]);
+      }
     }
   }
-  const float var = __fdiv_rn(block_sum(m2, red), (float)a.N);
-  const float rstd = rsqrtf(var + a.eps);
+  block_sums<kRowsPerCta>(m2, red);
+  float w[8], b[8], sh[8], sc[8];
   if (live) {
-    float w[8], b[8], sh[8], sc[8];
     if (a.weight) unpack8(__ldg(reinterpret_cast<const uint4*>(a.weight + n0)), w);
     if (a.bias) unpack8(__ldg(reinterpret_cast<const uint4*>(a.bias + n0)), b);
     if (a.scale) loadf8(a.scale + n0, sc);
     if (a.shift) loadf8(a.shift + n0, sh);
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      float y = __fmul_rn(f[j] - mean, rstd);
-      if (a.weight) y = __fmul_rn(y, w[j]);
-      if (a.bias) y = __fadd_rn(y, b[j]);
-      if (a.scale) y = __fmul_rn(y, __fadd_rn(1.0f, sc[j]));
-      if (a.shift) y = __fadd_rn(y, sh[j]);
-      f[j] = rc::bf16_to_float(rc::bf16_bits(y));
-    }
-    if (a.out) *reinterpret_cast<uint4*>(a.out + (size_t)row * a.ldo + n0) = pack8(f);
   }
-  if (a.codes) {
-    uint8_t sfb;
-    const uint32_t w = quant8_pair(f, a.g, sfb);
-    if (live) *reinterpret_cast<uint32_t*>(a.codes + (size_t)row * (a.N >> 1) + (size_t)t * 4) = w;
-    store_sf4_pairs(a.sf, row, t >> 1, ((a.N >> 4) + 3) >> 2, live ? sfb : 0, live);
+  const int katoms = ((a.N >> 4) + 3) >> 2;
+#pragma unroll
+  for (int k = 0; k < kRowsPerCta; ++k) {
+    const int row = row0 + k;
+    const bool ok = live && row < a.M;
+    const float rstd = rsqrtf(__fdiv_rn(m2[k], (float)a.N) + a.eps);
+    if (ok) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        float y = __fmul_rn(f[k][j] - mean[k], rstd);
+        if (a.weight) y = __fmul_rn(y, w[j]);
+        if (a.bias) y = __fadd_rn(y, b[j]);
+        if (a.scale) y = __fmul_rn(y, __fadd_rn(1.0f, sc[j]));
+        if (a.shift) y = __fadd_rn(y, sh[j]);
+        f[k][j] = rc::bf16_to_float(rc::bf16_bits(y));
+      }
+      if (a.out) *reinterpret_cast<uint4*>(a.out + (size_t)row * a.ldo + n0) = pack8(f[k]);
+    }
+    if (a.codes && row < a.M) {   // row-uniform branch: shuffles see the whole warp
+      uint8_t sfb;
+      const uint32_t wq = quant8_pair(f[k], a.g, sfb);
+      if (ok) *reinterpret_cast<uint32_t*>(a.codes + (size_t)row * (a.N >> 1) + (size_t)t * 4) = wq;
+      store_sf4_pairs(a.sf, row, t >> 1, katoms, ok ? sfb : 0, ok);
+    }
   }
 }
 
@@ -174,46 +205,60 @@ struct RmsArgs {
   int M, N, d, span;
 };
 
-// One CTA per (row, tensor), one thread per 8 elements.
+// kRowsPerCta rows of one tensor per CTA, one thread per 8 elements.
 __global__ void __launch_bounds__(512) rmsnorm_rope_kernel(RmsArgs a) {
-  __shared__ float red[16];
-  const int row = blockIdx.x, tsel = blockIdx.y, t = threadIdx.x;
+  __shared__ float red[kRowsPerCta][16];
+  const int row0 = blockIdx.x * kRowsPerCta, tsel = blockIdx.y, t = threadIdx.x;
   const int n0 = t * 8;
   const bool live = n0 < a.N;
-  float f[8];
-  if (live) unpack8(__ldg(reinterpret_cast<const uint4*>(a.x[tsel] + (size_t)row * a.ldx[tsel] + n0)), f);
-  else {
+  float f[kRowsPerCta][8];
+  uint4 raw[kRowsPerCta];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) f[j] = 0.f;
-  }
+  for (int k = 0; k < kRowsPerCta; ++k)
+    raw[k] = (live && row0 + k < a.M)
+                 ? __ldg(reinterpret_cast<const uint4*>(a.x[tsel] + (size_t)(row0 + k) * a.ldx[tsel] + n0))
+                 : make_uint4(0, 0, 0, 0);
+#pragma unroll
+  for (int k = 0; k < kRowsPerCta; ++k) unpack8(raw[k], f[k]);
   const __nv_bfloat16* w = a.w[tsel];
-  float r = 0.f;
+  float r[kRowsPerCta];
   if (w) {
-    float ss = 0.f;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) ss = fmaf(f[j], f[j], ss);
-    r = rsqrtf(__fdiv_rn(block_sum(ss, red), (float)a.N) + a.eps);
+    for (int k = 0; k < kRowsPerCta; ++k) {
+      r[k] = 0.f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) r[k] = fmaf(f[k][j], f[k][j], r[k]);
+    }
+    block_sums<kRowsPerCta>(r, red);
+#pragma unroll
+    for (int k = 0; k < kRowsPerCta; ++k) r[k] = rsqrtf(__fdiv_rn(r[k], (float)a.N) + a.eps);
   }
   if (!live) return;
-  if (w) {
-    float wf[8];
-    unpack8(__ldg(reinterpret_cast<const uint4*>(w + n0)), wf);
+  float wf[8];
+  if (w) unpack8(__ldg(reinterpret_cast<const uint4*>(w + n0)), wf);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) f[j] = rc::bf16_to_float(rc::bf16_bits(__fmul_rn(__fmul_rn(f[j], r), wf[j])));
-  }
-  if (a.cos) {
-    const int pos = row % a.span, dd = n0 % a.d;   // 8 | d: a thread never straddles heads
-    float c[8], sn[8];
-    loadf8(a.cos + (size_t)pos * a.d + dd, c);
-    loadf8(a.sin + (size_t)pos * a.d + dd, sn);
+  for (int k = 0; k < kRowsPerCta; ++k) {
+    const int row = row0 + k;
+    if (row >= a.M) break;
+    if (w) {
 #pragma unroll
-    for (int j = 0; j < 8; j += 2) {
-      const float e = f[j], o = f[j + 1];
-      f[j] = __fsub_rn(__fmul_rn(e, c[j]), __fmul_rn(o, sn[j]));
-      f[j + 1] = __fadd_rn(__fmul_rn(e, sn[j]), __fmul_rn(o, c[j]));
+      for (int j = 0; j < 8; ++j)
+        f[k][j] = rc::bf16_to_float(rc::bf16_bits(__fmul_rn(__fmul_rn(f[k][j], r[k]), wf[j])));
     }
+    if (a.cos) {
+      const int pos = row % a.span, dd = n0 % a.d;   // 8 | d: a thread never straddles heads
+      float c[8], sn[8];
+      loadf8(a.cos + (size_t)pos * a.d + dd, c);
+      loadf8(a.sin + (size_t)pos * a.d + dd, sn);
+#pragma unroll
+      for (int j = 0; j < 8; j += 2) {
+        const float e = f[k][j], o = f[k][j + 1];
+        f[k][j] = __fsub_rn(__fmul_rn(e, c[j]), __fmul_rn(o, sn[j]));
+        f[k][j + 1] = __fadd_rn(__fmul_rn(e, sn[j]), __fmul_rn(o, c[j]));
+      }
+    }
+    *reinterpret_cast<uint4*>(a.out[tsel] + (size_t)row * a.ldo[tsel] + n0) = pack8(f[k]);
   }
-  *reinterpret_cast<uint4*>(a.out[tsel] + (size_t)row * a.ldo[tsel] + n0) = pack8(f);
 }
 
 // Temporal rotary on the first `td` dims of every head of `planes` planes of
@@ -276,24 +321,37 @@ __global__ void kv_commit_kernel(CommitArgs a) {
 // Same copy with the plane plan read from device memory:
 // plan = [n, src0, dst0, src1, dst1, ...] (n <= max_planes), so a captured
 // graph stays valid while the routing changes between replays.
+constexpr int kCopyUnroll = 4;   // independent 16-byte loads in flight per thread
+
 __global__ void kv_commit_planned_kernel(CommitArgs a, const int* __restrict__ plan) {
   const int n = min(plan[0], a.n);
   const int vec_per_row = a.row_bytes >> 4;
   const long long per_plane = (long long)a.span * vec_per_row;
   const long long total = 2LL * a.n * per_plane;
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
-       i += (long long)gridDim.x * blockDim.x) {
-    const int t = (int)(i / (a.n * per_plane));
-    const long long r = i % (a.n * per_plane);
-    const int c = (int)(r / per_plane);
-    if (c >= n) continue;
-    const int sp = plan[1 + 2 * c], dp = plan[2 + 2 * c];
-    if (sp < 0 || dp < 0 || dp >= a.dst_plane[0]) continue;   // dst_plane[0] = slot capacity
-    const long long q = r % per_plane;
-    const long long row = q / vec_per_row, v = q % vec_per_row;
-    const uint4* s = reinterpret_cast<const uint4*>(a.src[t] + ((long long)sp * a.span + row) * a.src_ld[t]);
-    uint4* dd = reinterpret_cast<uint4*>(a.dst[t] + ((long long)dp * a.span + row) * a.dst_ld[t]);
-    dd[v] = __ldg(s + v);
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  for (long long base = blockIdx.x * (long long)blockDim.x + threadIdx.x; base < total;
+       base += stride * kCopyUnroll) {
+    uint4 val[kCopyUnroll];
+    uint4* dst[kCopyUnroll];
+#pragma unroll
+    for (int u = 0; u < kCopyUnroll; ++u) {
+      const long long i = base + u * stride;
+      dst[u] = nullptr;
+      if (i >= total) continue;
+      const int t = (int)(i / (a.n * per_plane));
+      const long long r = i % (a.n * per_plane);
+      const int c = (int)(r / per_plane);
+      if (c >= n) continue;
+      const int sp = plan[1 + 2 * c], dp = plan[2 + 2 * c];
+      if (sp < 0 || dp < 0 || dp >= a.dst_plane[0]) continue;   // dst_plane[0] = slot capacity
+      const long long q = r % per_plane;
+      const long long row = q / vec_per_row, v = q % vec_per_row;
+      val[u] = __ldg(reinterpret_cast<const uint4*>(a.src[t] + ((long long)sp * a.span + row) * a.src_ld[t]) + v);
+      dst[u] = reinterpret_cast<uint4*>(a.dst[t] + ((long long)dp * a.span + row) * a.dst_ld[t]) + v;
+    }
+#pragma unroll
+    for (int u = 0; u < kCopyUnroll; ++u)
+      if (dst[u]) *dst[u] = val[u];
   }
 }
 
@@ -334,7 +392,7 @@ int rc_ln_modulate_quant(const void* x, long long ldx, int M, int N, const void*
            shift, scale, eps, reinterpret_cast<__nv_bfloat16*>(out), ldo, codes, scales_swizzled,
            global_scale, M, N};
   const int threads = ((N / 8) + 31) / 32 * 32;
-  ln_modulate_kernel<<<M, threads, 0, stream>>>(a);
+  ln_modulate_kernel<<<(M + kRowsPerCta - 1) / kRowsPerCta, threads, 0, stream>>>(a);
   int r = rc::check_launch("rc_ln_modulate_quant");
   if (r || !codes) return r;
   const int katoms = ((N >> 4) + 3) >> 2;
@@ -379,7 +437,7 @@ int rc_rmsnorm_rope(int n_tensors, const void* const* xs, const long long* ldx,
   a.d = d;
   a.span = span;
   if (M == 0) return RC_OK;
-  dim3 grid(M, n_tensors);
+  dim3 grid((M + kRowsPerCta - 1) / kRowsPerCta, n_tensors);
   rmsnorm_rope_kernel<<<grid, ((N / 8) + 31) / 32 * 32, 0, stream>>>(a);
   return rc::check_launch("rc_rmsnorm_rope");
 }
