@@ -88,9 +88,11 @@ __device__ __forceinline__ void store_sf4_pairs(uint8_t* sf, int row, int kb, in
         b0 | (b1 << 8) | (b2 << 16) | (b3 << 24);
 }
 
-// Several rows per CTA (kRowsPerCta), one thread per 8 elements of each row
-// (N/8 threads, N <= 4096): every thread has kRowsPerCta independent 16-byte
-// loads in flight before the first reduction.
+// Rows per CTA, one thread per 8 elements of each row (N/8 threads, N <= 4096):
+// every thread has that many independent 16-byte loads in flight before the
+// first reduction. LayerNorm keeps one row (its modulation vectors already
+// take registers); RMSNorm takes four.
+constexpr int kLnRows = 1;
 constexpr int kRowsPerCta = 4;
 
 // Block-wide sums of R values per thread (one per row) over up to 16 warps.
@@ -114,30 +116,30 @@ __device__ __forceinline__ void block_sums(float (&v)[R], float (*red)[16]) {
 }
 
 __global__ void __launch_bounds__(512) ln_modulate_kernel(LnArgs a) {
-  __shared__ float red[kRowsPerCta][16];
-  const int row0 = blockIdx.x * kRowsPerCta;
+  __shared__ float red[kLnRows][16];
+  const int row0 = blockIdx.x * kLnRows;
   const int t = threadIdx.x;
   const bool live = t * 8 < a.N;
   const int n0 = t * 8;
-  float f[kRowsPerCta][8];
-  uint4 raw[kRowsPerCta];
+  float f[kLnRows][8];
+  uint4 raw[kLnRows];
 #pragma unroll
-  for (int k = 0; k < kRowsPerCta; ++k)
+  for (int k = 0; k < kLnRows; ++k)
     raw[k] = (live && row0 + k < a.M)
                  ? __ldg(reinterpret_cast<const uint4*>(a.x + (size_t)(row0 + k) * a.ldx + n0))
                  : make_uint4(0, 0, 0, 0);
-  float s[kRowsPerCta];
+  float s[kLnRows];
 #pragma unroll
-  for (int k = 0; k < kRowsPerCta; ++k) {
+  for (int k = 0; k < kLnRows; ++k) {
     unpack8(raw[k], f[k]);
     s[k] = 0.f;
 #pragma unroll
     for (int j = 0; j < 8; ++j) s[k] += f[k][j];
   }
-  block_sums<kRowsPerCta>(s, red);
-  float mean[kRowsPerCta], m2[kRowsPerCta];
+  block_sums<kLnRows>(s, red);
+  float mean[kLnRows], m2[kLnRows];
 #pragma unroll
-  for (int k = 0; k < kRowsPerCta; ++k) {
+  for (int k = 0; k < kLnRows; ++k) {
     mean[k] = __fdiv_rn(s[k], (float)a.N);
     m2[k] = 0.f;
     if (live) {
@@ -148,7 +150,7 @@ __global__ void __launch_bounds__(512) ln_modulate_kernel(LnArgs a) {
       }
     }
   }
-  block_sums<kRowsPerCta>(m2, red);
+  block_sums<kLnRows>(m2, red);
   float w[8], b[8], sh[8], sc[8];
   if (live) {
     if (a.weight) unpack8(__ldg(reinterpret_cast<const uint4*>(a.weight + n0)), w);
@@ -158,7 +160,7 @@ __global__ void __launch_bounds__(512) ln_modulate_kernel(LnArgs a) {
   }
   const int katoms = ((a.N >> 4) + 3) >> 2;
 #pragma unroll
-  for (int k = 0; k < kRowsPerCta; ++k) {
+  for (int k = 0; k < kLnRows; ++k) {
     const int row = row0 + k;
     const bool ok = live && row < a.M;
     const float rstd = rsqrtf(__fdiv_rn(m2[k], (float)a.N) + a.eps);
@@ -392,7 +394,7 @@ int rc_ln_modulate_quant(const void* x, long long ldx, int M, int N, const void*
            shift, scale, eps, reinterpret_cast<__nv_bfloat16*>(out), ldo, codes, scales_swizzled,
            global_scale, M, N};
   const int threads = ((N / 8) + 31) / 32 * 32;
-  ln_modulate_kernel<<<(M + kRowsPerCta - 1) / kRowsPerCta, threads, 0, stream>>>(a);
+  ln_modulate_kernel<<<(M + kLnRows - 1) / kLnRows, threads, 0, stream>>>(a);
   int r = rc::check_launch("rc_ln_modulate_quant");
   if (r || !codes) return r;
   const int katoms = ((N >> 4) + 3) >> 2;
