@@ -1,6 +1,6 @@
 """Benchmark: DiT latent tokens/s of the ReCaVSR hot path on B200.
 
-Workload (the 720p x4 stream): the 30-layer streaming DiT
+Workload (the 720p x4 streaming configuration): the 30-layer streaming DiT
 layer loop (routed self-attention over the released static KV router, cross
 attention over 512 prompt tokens, NVFP4 linears, modulation / LayerNorm /
 RMSNorm / RoPE glue, KV-cache commit) on 1280x704 output = 22x40 latent

@@ -1,7 +1,9 @@
 """Generate the golden fixtures of tests/golden/ by running the REFERENCE itself.
 
-Run in a container that has the reference checkout (default /root/reference,
-override with RECAVSR_REFERENCE):  python tests/golden/make_golden.py
+Run where a checkout of the reference exists:
+    python tests/golden/make_golden.py <reference checkout>
+(or set RECAVSR_REFERENCE). Under TRITON_INTERPRET=1 it also records the
+reference's Triton kernel on windowed cases.
 
 The reference is imported with two import shims and no other change:
 * ``diffusers.models.embeddings.get_1d_rotary_pos_embed`` (diffusers 0.37.1 is
@@ -266,7 +268,7 @@ class _Block(nn.Module):
 class _QuantLinear(nn.Module):
     """NVFP4Linear with the GEMM replaced by its defining math: the reference's
     own quantize() of activations and weights, dequantized, fp32 matmul + bias,
-    bf16 out (the GEMM oracle BASELINE states)."""
+    bf16 out (the GEMM's defining math, the parity target for the GEMM)."""
 
     LUT = torch.tensor([0, .5, 1, 1.5, 2, 3, 4, 6, -0., -.5, -1, -1.5, -2, -3, -4, -6])
 
@@ -341,7 +343,10 @@ def gen_block(out, tag="block", dim=256, heads=2, ffn=512, H=4, W=6, enc_len=16,
 
 
 def main():
-    _install_shims(os.environ.get("RECAVSR_REFERENCE", "/root/reference"))
+    ref = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("RECAVSR_REFERENCE")
+    if not ref:
+        raise SystemExit("usage: make_golden.py <reference checkout>  (or set RECAVSR_REFERENCE)")
+    _install_shims(ref)
     torch.manual_seed(0)
     out = {}
     gen_quant(out)
