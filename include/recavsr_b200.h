@@ -131,6 +131,29 @@ int rc_paired_attention(const void* q, const void* ck, const void* cv, const voi
                         long long out_ld, uint8_t* out_codes, uint8_t* out_scales,
                         rc_stream_t stream);
 
+/* Allocation-free form of rc_paired_attention (no counterpart in the
+ * reference, which always lets PyTorch allocate). For callers that must not
+ * call cudaMalloc -- for example code that launches while another thread of the
+ * process holds a CUDA-graph capture in global mode (device allocation is not
+ * permitted then), or a host framework that hands this library no allocator
+ * and a fixed memory budget. It takes the same arguments minus the workspace
+ * and uses a scratch array built into the library instead: 64 MiB of device
+ * memory per GPU that loads the library, held until the process exits.
+ * Geometries needing more than 64 MiB of scratch (rc_paired_attention_workspace)
+ * are rejected with RC_ERR_ARG. The first call on each device looks the array
+ * up (cudaGetSymbolAddress with that device current), so make that first call
+ * before any stream capture. All calls share the one array: calls whose work
+ * overlaps on the GPU (concurrent streams) race on it; calls ordered on one
+ * stream are safe. Nothing in the scratch needs to start at zero -- every
+ * scratch byte the kernels read is written earlier in the same call. */
+int rc_paired_attention_static_scratch(const void* q, const void* ck, const void* cv, const void* pk,
+                                       const void* pv, const long long* strides, const int* slots,
+                                       const int* past_positions, const int* query_positions,
+                                       const float* cos, const float* sin, int B, int QT, int CAP,
+                                       int H, int W, int heads, int d, int td, int window_h,
+                                       int window_w, void* out, long long out_ld, uint8_t* out_codes,
+                                       uint8_t* out_scales, rc_stream_t stream);
+
 /* Unmasked attention without rotary embedding or cache (the cross-attention of
  * recavsr_infer/runtime/transformer.py:123-128 over the precomputed prompt K/V):
  * q [B, Nq, heads, d], k/v [B, Nk, heads, d] with strides[9] = (batch, token,

@@ -29,6 +29,8 @@
 //   key tiles 128 consecutive tokens of a plane (4-D TMA view, the plane tail
 //   reads as zeros). Local mode: query tiles are 2 frames x 8 x 8 tokens, key
 //   tiles are 8 x 16 boxes of the union of the tile's windows (5-D TMA view).
+#include <mutex>
+
 #include "sm100.cuh"
 
 namespace {
@@ -592,6 +594,19 @@ bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 int g_attr_set = 0;
 
+// ---------------------------------------------------------------------------
+// Allocation-free variant. Its scratch (the rotated q / K planes the attention
+// kernel reads) lives in this file-scope device array instead of a caller
+// buffer. Every GPU that loads the library holds these 64 MiB until the
+// process exits. Host code cannot pass the array's name to a kernel: that name
+// is only a host-side handle, so the device address is looked up with
+// cudaGetSymbolAddress once per device (with that device current) and cached.
+constexpr long long kStaticScratchBytes = 64LL << 20;
+static __device__ __align__(256) uint8_t g_attention_scratch[kStaticScratchBytes];
+constexpr int kMaxDevices = 64;
+void* g_scratch_addr[kMaxDevices] = {};   // per-device cache of the array's address
+std::mutex g_scratch_mu;
+
 }  // namespace
 
 RC_DEVICE_ERROR_ACCESSOR(attention)
@@ -769,6 +784,44 @@ int rc_cross_attention(const void* q, const void* k, const void* v, const long l
     if ((r = rc::check_launch(what))) return r;
   }
   return RC_OK;
+}
+
+
+// Same computation as rc_paired_attention, for callers that cannot allocate
+// device memory; see include/recavsr_b200.h for the contract.
+int rc_paired_attention_static_scratch(const void* q, const void* ck, const void* cv, const void* pk,
+                                       const void* pv, const long long* strides, const int* slots,
+                                       const int* past_positions, const int* query_positions,
+                                       const float* cos, const float* sin, int B, int QT, int CAP,
+                                       int H, int W, int heads, int d, int td, int window_h,
+                                       int window_w, void* out, long long out_ld, uint8_t* out_codes,
+                                       uint8_t* out_scales, cudaStream_t stream) {
+  const char* what = "rc_paired_attention_static_scratch";
+  const long long need = rc_paired_attention_workspace(B, QT, CAP, H, W, heads, d);
+  if (need < 0) return rc::set_error(RC_ERR_ARG, "%s: bad geometry", what);
+  if (need > kStaticScratchBytes)
+    return rc::set_error(RC_ERR_ARG,
+                         "%s: this geometry needs %lld bytes of scratch; the built-in scratch holds %lld "
+                         "bytes (use rc_paired_attention with a caller buffer)",
+                         what, need, kStaticScratchBytes);
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
+    return rc::set_error(RC_ERR_CUDA, "%s: no usable current device", what);
+  void* scratch;
+  {
+    std::lock_guard<std::mutex> lock(g_scratch_mu);
+    if (!g_scratch_addr[dev]) {
+      void* addr = nullptr;
+      const cudaError_t e = cudaGetSymbolAddress(&addr, g_attention_scratch);
+      if (e != cudaSuccess || !addr)
+        return rc::set_error(RC_ERR_CUDA, "%s: cudaGetSymbolAddress failed: %s", what, cudaGetErrorString(e));
+      g_scratch_addr[dev] = addr;
+    }
+    scratch = g_scratch_addr[dev];
+  }
+  return rc_paired_attention(q, ck, cv, pk, pv, strides, slots, past_positions, query_positions, cos,
+                             sin, B, QT, CAP, H, W, heads, d, td, window_h, window_w, scratch,
+                             kStaticScratchBytes, out, out_ld, out_codes, out_scales, stream);
 }
 
 }  // extern "C"

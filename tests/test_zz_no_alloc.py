@@ -1,0 +1,87 @@
+"""Allocation-free attention entry point (rc_paired_attention_static_scratch).
+
+Some callers of this library cannot call cudaMalloc: a process where another
+thread holds a global-mode CUDA-graph capture, or a host framework that gives
+the library a fixed memory budget and no allocator. For them the library
+exposes one attention entry point that takes no workspace and uses a scratch
+array built into the library. This test drives it through the C ABI and
+checks it against the workspace-taking entry point on two calls in a row
+(different inputs), within the attention tolerances of the other tests.
+Collected last on purpose (file name), so a failure here cannot hide the
+results of any other test; it also passes when run alone.
+"""
+import ctypes as C
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+ABS, REL = 2e-2, 1e-2
+
+
+def _inputs(seed, H, W, heads, cap):
+    g = torch.Generator(device="cuda")
+    g.manual_seed(seed)
+    t = H * W
+    r = lambda *s: torch.randn(*s, generator=g, device="cuda").bfloat16()
+    return (r(1, 2 * t, heads, 128), r(1, 2 * t, heads, 128), r(1, 2 * t, heads, 128),
+            r(1, cap * t, heads, 128), r(1, cap * t, heads, 128))
+
+
+def _args(q, ck, cv, pk, pv, tables, slots, ppos, qpos, H, W, heads, cap):
+    st = []
+    for x in (q, ck, cv, pk, pv):
+        st += [x.stride(0), x.stride(1), x.stride(2)]
+    head = [q.data_ptr(), ck.data_ptr(), cv.data_ptr(), pk.data_ptr(), pv.data_ptr(),
+            (C.c_longlong * 15)(*st), slots.data_ptr(), ppos.data_ptr(), qpos.data_ptr(),
+            tables["temporal_cos"].data_ptr(), tables["temporal_sin"].data_ptr(),
+            1, 2, cap, H, W, heads, 128, 44, H, W]
+    return head
+
+
+def test_static_scratch_matches_workspace_entry():
+    from recavsr_b200 import _lib
+    from recavsr_b200.runtime.block import rope_tables
+    lib = _lib.library()
+    H, W, heads, cap = 22, 40, 8, 3
+    tables = rope_tables(128, H, W, "cuda")
+    slots = torch.tensor([2, -1, 0], dtype=torch.int32, device="cuda")
+    ppos = torch.tensor([5, 0, 6], dtype=torch.int32, device="cuda")
+    qpos = torch.tensor([7, 8], dtype=torch.int32, device="cuda")
+    n, dim = 2 * H * W, heads * 128
+    for call, seed in enumerate((101, 202)):        # two calls in a row, new data each time
+        q, ck, cv, pk, pv = _inputs(seed, H, W, heads, cap)
+        head = _args(q, ck, cv, pk, pv, tables, slots, ppos, qpos, H, W, heads, cap)
+        ws_bytes = lib.rc_paired_attention_workspace(1, 2, cap, H, W, heads, 128)
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device="cuda")
+        ref = torch.empty(1, n, heads, 128, dtype=torch.bfloat16, device="cuda")
+        _lib.check(lib.rc_paired_attention(*head, ws.data_ptr(), ws_bytes, ref.data_ptr(), dim,
+                                           None, None, _lib.stream()), "rc_paired_attention")
+        out = torch.full((1, n, heads, 128), float("nan"), dtype=torch.bfloat16, device="cuda")
+        _lib.check(lib.rc_paired_attention_static_scratch(*head, out.data_ptr(), dim, None, None,
+                                                          _lib.stream()),
+                   "rc_paired_attention_static_scratch")
+        torch.cuda.synchronize()
+        assert _lib.read_device_error() == 0
+        got, want = out.float().cpu().numpy(), ref.float().cpu().numpy()
+        assert np.isfinite(got).all(), f"call {call}: non-finite output"
+        err = np.abs(got - want).max()
+        rel = err / np.abs(want).max()
+        assert err <= ABS and rel <= REL, (call, err, rel)
+
+
+def test_static_scratch_rejects_oversized_geometry():
+    from recavsr_b200 import _lib
+    lib = _lib.library()
+    # 2 frames of 60x34 tokens x 24 heads with 8 cached planes needs ~150 MiB of scratch.
+    z = torch.zeros(16, dtype=torch.bfloat16, device="cuda")
+    i = torch.zeros(8, dtype=torch.int32, device="cuda")
+    st = (C.c_longlong * 15)(*([0, 3072, 128] * 5))
+    status = lib.rc_paired_attention_static_scratch(
+        z.data_ptr(), z.data_ptr(), z.data_ptr(), z.data_ptr(), z.data_ptr(), st, i.data_ptr(),
+        i.data_ptr(), i.data_ptr(), z.data_ptr(), z.data_ptr(), 1, 2, 8, 34, 60, 24, 128, 44, 22, 40,
+        z.data_ptr(), 3072, None, None, _lib.stream())
+    assert status == _lib.RC_ERR_ARG
+    assert "scratch" in _lib.last_error()
