@@ -15,7 +15,9 @@
 // issuer (+ TMEM owner), warps 2-9 = epilogue (TMEM -> registers -> global;
 // two warps per TMEM lane quadrant, each on half of the tile's columns). With
 // BN = 128 the accumulator is double-buffered in TMEM so the epilogue of one
-// tile overlaps the MMAs of the next.
+// tile overlaps the MMAs of the next; with BN = 256 the epilogue drains the
+// accumulator into registers first and releases it, which gives the same
+// overlap with a single accumulator.
 // Epilogues fuse the block's follow-up element-wise work:
 //   BIAS           out = bf16(acc*alpha + bias)
 //   GATED_RESIDUAL h   = bf16(h + bf16(acc*alpha + bias) * gate[n])   (in place)
@@ -91,11 +93,12 @@ struct Smem {
 };
 
 __device__ __forceinline__ float gelu_tanh(float x) {
-  // 0.5 * x * (1 + tanh(sqrt(2/pi) * (x + 0.044715 x^3))), fp32 as in
-  // torch's gelu(approximate="tanh") for bf16 inputs.
-  const float k0 = 0.7978845608028654f, k1 = 0.044715f;
-  const float inner = __fmul_rn(k0, __fadd_rn(x, __fmul_rn(k1, __fmul_rn(__fmul_rn(x, x), x))));
-  return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, tanhf(inner)));
+  // GELU(tanh) = 0.5 x (1 + tanh(u)), u = sqrt(2/pi) (x + 0.044715 x^3), evaluated
+  // as the identical x / (1 + exp(-2u)) with the fast exp / divide: a few fp32
+  // ulps from tanhf, invisible after the bf16 rounding in all but ~1e-3 of
+  // elements (where the bf16 result moves by one ulp).
+  const float u = 0.7978845608028654f * fmaf(0.044715f * x, x * x, x);
+  return __fdividef(x, 1.0f + __expf(-2.0f * u));
 }
 
 template <int KIND, int BN, int STAGES, int EPI>
@@ -282,30 +285,39 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
     }
   } else {
     // ------------------------------------------------------------ epilogue
+    // Each thread owns one accumulator row (TMEM lane) and half of the tile's
+    // columns. It first drains its columns from TMEM into registers and releases
+    // the accumulator, so the next tile's MMAs overlap this tile's epilogue math.
     const int quad = warp & 3;                 // TMEM lane quadrant of this warp
     const int half = (warp - 2) >> 2;          // which half of the tile's columns
     const int row_in_tile = quad * 32 + lane;
     constexpr int kCols = BN / 2;
+    int local = 0;
     float alpha = p.alpha;
     if constexpr (KIND == KIND_E4M3) {
       if (p.alpha_ptr_a) alpha = __fmul_rn(alpha, *p.alpha_ptr_a);
       if (p.alpha_ptr_b) alpha = __fmul_rn(alpha, *p.alpha_ptr_b);
     }
-    int local = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
       const int mb = tile % p.m_blocks, nb = tile / p.m_blocks;
       const int as = local % kAcc;
       if (!__all_sync(0xffffffffu, wait(&acc_full[as], (uint32_t)((local / kAcc) & 1), 4))) break;
       sm100::tc_fence_after();
+      uint32_t acc[kCols];
+      {
+        const uint32_t t_row = tmem_acc + as * BN + half * kCols + ((uint32_t)(quad * 32) << 16);
+#pragma unroll
+        for (int c = 0; c < kCols; c += 16)
+          sm100::tmem_ld16(t_row + c, *reinterpret_cast<uint32_t(*)[16]>(&acc[c]));
+        sm100::tmem_ld_wait();
+      }
+      sm100::tc_fence_before();
+      sm100::mbar_arrive(&acc_empty[as]);      // accumulator free: next tile may start
       const int row = mb * BM + row_in_tile;
       const bool row_ok = row < p.M;
-      const uint32_t t_row = tmem_acc + as * BN + ((uint32_t)(quad * 32) << 16);
-#pragma unroll 1
-      for (int c0 = half * kCols; c0 < (half + 1) * kCols; c0 += 16) {
-        uint32_t r[16];
-        sm100::tmem_ld16(t_row + c0, r);
-        sm100::tmem_ld_wait();
-        const int n0 = nb * BN + c0;
+#pragma unroll
+      for (int cc = 0; cc < kCols; cc += 16) {
+        const int n0 = nb * BN + half * kCols + cc;
         if (n0 >= p.N) continue;
         if (!row_ok) {
           // Padding rows of the next linear's scale atoms must read as zero.
@@ -325,7 +337,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
         }
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
-          float x = __fmul_rn(__uint_as_float(r[j]), alpha);
+          float x = __fmul_rn(__uint_as_float(acc[cc + j]), alpha);
           if (p.bias) x = __fadd_rn(x, bias[j]);
           v[j] = rc::bf16_to_float(rc::bf16_bits(x));
         }
@@ -364,10 +376,9 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
           if (p.q_g == 1.0f) {
             const rc::E2m1Bounds bd(sd);
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              const uint32_t code = bd.code(v[j]);
-              if (j < 8) lo |= code << (4 * j);
-              else hi |= code << (4 * (j - 8));
+            for (int j = 0; j < 8; ++j) {
+              lo |= bd.code(v[j]) << (4 * j);
+              hi |= bd.code(v[8 + j]) << (4 * j);
             }
           } else {
 #pragma unroll
@@ -389,8 +400,6 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
         dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
         dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
       }
-      sm100::tc_fence_before();
-      sm100::mbar_arrive(&acc_empty[as]);
     }
   }
 
@@ -443,16 +452,25 @@ int dispatch_epi(int epi, const CUtensorMap& ta, const CUtensorMap& tb, const Ge
   return rc::set_error(RC_ERR_ARG, "%s: unknown epilogue %d", what, epi);
 }
 
-// Tile width: BN = 128 (double-buffered accumulators, epilogue overlapped) by
-// default; RECAVSR_GEMM_BN=256 selects 128x256 tiles where N allows.
-bool gemm_prefer_wide(int epi) {
-  static int choice = -1;
-  if (choice < 0) {
+int num_sms();
+
+// Tile width. 128 x 256 tiles move a third less operand data per FLOP than
+// 128 x 128 and win when the mainloop dominates: at least ~2 waves of wide
+// tiles, or a long K. 128 x 128 tiles (double-buffered accumulators) win for
+// short-K GEMMs with few tiles (wave quantization) and for the GELU + NVFP4
+// epilogue, whose math per tile outruns a short mainloop.
+// RECAVSR_GEMM_BN=128 / 256 forces one width.
+bool gemm_prefer_wide(int epi, int M, int N, int K) {
+  static int forced = -2;
+  if (forced == -2) {
     const char* e = getenv("RECAVSR_GEMM_BN");
-    choice = (e && atoi(e) == 256) ? 1 : 0;
+    forced = e ? (atoi(e) == 256 ? 1 : (atoi(e) == 128 ? 0 : -1)) : -1;
   }
-  (void)epi;
-  return choice == 1;
+  if (N % 256) return false;
+  if (forced >= 0) return forced == 1;
+  if (epi == EPI_GELU_NVF4) return false;
+  const long long wide_tiles = (long long)((M + 127) / 128) * (N / 256);
+  return wide_tiles >= 2LL * num_sms() || K >= 8192;
 }
 
 // Shared argument checks + tensor maps; `elem_bytes_x2` = 2 * bytes/element
@@ -477,7 +495,7 @@ int run_gemm(int kind, int epi, const void* a, const void* b, int M, int N, int 
   CUtensorMap ta, tb;
   const uint64_t da[2] = {row_bytes, (uint64_t)M}, db[2] = {row_bytes, (uint64_t)N};
   const uint64_t sa[1] = {row_bytes}, sb[1] = {row_bytes};
-  const bool wide = (N % 256 == 0) && gemm_prefer_wide(epi);
+  const bool wide = gemm_prefer_wide(epi, M, N, K);
   const uint32_t boxa[2] = {128, 128}, boxb[2] = {128, (uint32_t)(wide ? 256 : 128)};
   int r = rc::encode_tmap(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(a), da, sa, boxa,
                           CU_TENSOR_MAP_SWIZZLE_128B, what);

@@ -1,9 +1,10 @@
 // Row-wise glue around the DiT linears: LayerNorm (+affine) (+AdaLN
 // modulation) with an optional fused NVFP4 quantizer, RMSNorm across heads
 // with the spatial rotary embedding, the temporal rotary embedding, and the
-// KV-cache plane commit. Row kernels run one CTA per row and one thread per 8
-// elements (a lane pair per 16-element quantization block, N <= 4096), so the
-// row stays in registers and each input byte is read from HBM once.
+// KV-cache plane commit. Row kernels run one 128-thread CTA per row with up to
+// four 8-element chunks per thread (a lane pair per 16-element quantization
+// block, N <= 4096), so the row stays in registers and each input byte is read
+// from HBM once.
 //
 // Numerics follow recavsr_infer/runtime/transformer.py:88-133 in eager order:
 //   LN in fp32 (two-pass mean / variance, rsqrt(var + eps)), then
@@ -88,99 +89,88 @@ __device__ __forceinline__ void store_sf4_pairs(uint8_t* sf, int row, int kb, in
         b0 | (b1 << 8) | (b2 << 16) | (b3 << 24);
 }
 
-// Rows per CTA, one thread per 8 elements of each row (N/8 threads, N <= 4096):
-// every thread has that many independent 16-byte loads in flight before the
-// first reduction. LayerNorm keeps one row (its modulation vectors already
-// take registers); RMSNorm takes four.
-constexpr int kLnRows = 1;
-constexpr int kRowsPerCta = 4;
+// Row kernels: one CTA of kRowThreads threads per row; thread t owns the
+// 8-element chunks t, t + kRowThreads, ... (at most kRowChunks of them, so
+// N <= kRowThreads * 8 * kRowChunks = 4096). Every thread issues all of its
+// chunk loads before the first reduction; the small CTA keeps many rows
+// resident per SM to hide the load -> reduce -> store latency of each row.
+constexpr int kRowThreads = 128;
+constexpr int kRowChunks = 4;
 
-// Block-wide sums of R values per thread (one per row) over up to 16 warps.
-template <int R>
-__device__ __forceinline__ void block_sums(float (&v)[R], float (*red)[16]) {
-#pragma unroll
-  for (int k = 0; k < R; ++k) v[k] = warp_sum(v[k]);
-  const int w = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
+__device__ __forceinline__ float row_sum(float v, float* red) {
+  v = warp_sum(v);
   __syncthreads();
-  if ((threadIdx.x & 31) == 0) {
-#pragma unroll
-    for (int k = 0; k < R; ++k) red[k][w] = v[k];
-  }
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
   __syncthreads();
-#pragma unroll
-  for (int k = 0; k < R; ++k) {
-    float t = 0.f;
-    for (int i = 0; i < nw; ++i) t += red[k][i];
-    v[k] = t;
-  }
+  return red[0] + red[1] + red[2] + red[3];
 }
 
-__global__ void __launch_bounds__(512) ln_modulate_kernel(LnArgs a) {
-  __shared__ float red[kLnRows][16];
-  const int row0 = blockIdx.x * kLnRows;
+__global__ void __launch_bounds__(kRowThreads, 6) ln_modulate_kernel(LnArgs a) {
+  __shared__ float red[4];
+  const int row = blockIdx.x;
   const int t = threadIdx.x;
-  const bool live = t * 8 < a.N;
-  const int n0 = t * 8;
-  float f[kLnRows][8];
-  uint4 raw[kLnRows];
+  const int nch = a.N >> 3;
+  uint4 raw[kRowChunks];
 #pragma unroll
-  for (int k = 0; k < kLnRows; ++k)
-    raw[k] = (live && row0 + k < a.M)
-                 ? __ldg(reinterpret_cast<const uint4*>(a.x + (size_t)(row0 + k) * a.ldx + n0))
-                 : make_uint4(0, 0, 0, 0);
-  float s[kLnRows];
-#pragma unroll
-  for (int k = 0; k < kLnRows; ++k) {
-    unpack8(raw[k], f[k]);
-    s[k] = 0.f;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) s[k] += f[k][j];
+  for (int i = 0; i < kRowChunks; ++i) {
+    const int c = t + i * kRowThreads;
+    raw[i] = c < nch ? __ldg(reinterpret_cast<const uint4*>(a.x + (size_t)row * a.ldx) + c)
+                     : make_uint4(0, 0, 0, 0);
   }
-  block_sums<kLnRows>(s, red);
-  float mean[kLnRows], m2[kLnRows];
+  float s = 0.f;
 #pragma unroll
-  for (int k = 0; k < kLnRows; ++k) {
-    mean[k] = __fdiv_rn(s[k], (float)a.N);
-    m2[k] = 0.f;
-    if (live) {
+  for (int i = 0; i < kRowChunks; ++i) {
+    float f[8];
+    unpack8(raw[i], f);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) s += f[j];
+  }
+  const float mean = __fdiv_rn(row_sum(s, red), (float)a.N);
+  float m2 = 0.f;
+#pragma unroll
+  for (int i = 0; i < kRowChunks; ++i) {
+    if (t + i * kRowThreads < nch) {
+      float f[8];
+      unpack8(raw[i], f);
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        const float d = f[k][j] - mean[k];
-        m2[k] = fmaf(d, d, m2[k]);
+        const float d = f[j] - mean;
+        m2 = fmaf(d, d, m2);
       }
     }
   }
-  block_sums<kLnRows>(m2, red);
-  float w[8], b[8], sh[8], sc[8];
-  if (live) {
-    if (a.weight) unpack8(__ldg(reinterpret_cast<const uint4*>(a.weight + n0)), w);
-    if (a.bias) unpack8(__ldg(reinterpret_cast<const uint4*>(a.bias + n0)), b);
-    if (a.scale) loadf8(a.scale + n0, sc);
-    if (a.shift) loadf8(a.shift + n0, sh);
-  }
+  const float rstd = rsqrtf(__fdiv_rn(row_sum(m2, red), (float)a.N) + a.eps);
   const int katoms = ((a.N >> 4) + 3) >> 2;
 #pragma unroll
-  for (int k = 0; k < kLnRows; ++k) {
-    const int row = row0 + k;
-    const bool ok = live && row < a.M;
-    const float rstd = rsqrtf(__fdiv_rn(m2[k], (float)a.N) + a.eps);
-    if (ok) {
+  for (int i = 0; i < kRowChunks; ++i) {
+    if (i * kRowThreads >= nch) break;                 // CTA-uniform
+    const int c = t + i * kRowThreads;
+    const bool live = c < nch;
+    const int n0 = c * 8;
+    float f[8];
+    unpack8(raw[i], f);
+    if (live) {
+      float w[8], b[8], sh[8], sc[8];
+      if (a.weight) unpack8(__ldg(reinterpret_cast<const uint4*>(a.weight + n0)), w);
+      if (a.bias) unpack8(__ldg(reinterpret_cast<const uint4*>(a.bias + n0)), b);
+      if (a.scale) loadf8(a.scale + n0, sc);
+      if (a.shift) loadf8(a.shift + n0, sh);
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        float y = __fmul_rn(f[k][j] - mean[k], rstd);
+        float y = __fmul_rn(f[j] - mean, rstd);
         if (a.weight) y = __fmul_rn(y, w[j]);
         if (a.bias) y = __fadd_rn(y, b[j]);
         if (a.scale) y = __fmul_rn(y, __fadd_rn(1.0f, sc[j]));
         if (a.shift) y = __fadd_rn(y, sh[j]);
-        f[k][j] = rc::bf16_to_float(rc::bf16_bits(y));
+        f[j] = rc::bf16_to_float(rc::bf16_bits(y));
       }
-      if (a.out) *reinterpret_cast<uint4*>(a.out + (size_t)row * a.ldo + n0) = pack8(f[k]);
+      if (a.out) *reinterpret_cast<uint4*>(a.out + (size_t)row * a.ldo + n0) = pack8(f);
     }
-    if (a.codes && row < a.M) {   // row-uniform branch: shuffles see the whole warp
+    if (a.codes) {
       uint8_t sfb;
-      const uint32_t wq = quant8_pair(f[k], a.g, sfb);
-      if (ok) *reinterpret_cast<uint32_t*>(a.codes + (size_t)row * (a.N >> 1) + (size_t)t * 4) = wq;
-      store_sf4_pairs(a.sf, row, t >> 1, katoms, ok ? sfb : 0, ok);
+      const uint32_t wq = quant8_pair(f, a.g, sfb);
+      if (live) *reinterpret_cast<uint32_t*>(a.codes + (size_t)row * (a.N >> 1) + (size_t)c * 4) = wq;
+      store_sf4_pairs(a.sf, row, c >> 1, katoms, live ? sfb : 0, live);
     }
   }
 }
@@ -207,59 +197,64 @@ struct RmsArgs {
   int M, N, d, span;
 };
 
-// kRowsPerCta rows of one tensor per CTA, one thread per 8 elements.
-__global__ void __launch_bounds__(512) rmsnorm_rope_kernel(RmsArgs a) {
-  __shared__ float red[kRowsPerCta][16];
-  const int row0 = blockIdx.x * kRowsPerCta, tsel = blockIdx.y, t = threadIdx.x;
-  const int n0 = t * 8;
-  const bool live = n0 < a.N;
-  float f[kRowsPerCta][8];
-  uint4 raw[kRowsPerCta];
+// One CTA of kRowThreads threads per (row, tensor); thread t owns chunks
+// t, t + kRowThreads, ... of 8 elements.
+__global__ void __launch_bounds__(kRowThreads, 8) rmsnorm_rope_kernel(RmsArgs a) {
+  __shared__ float red[4];
+  const int row = blockIdx.x, t = threadIdx.x;
+  const bool second = blockIdx.y != 0;            // select, not index: keeps the params in registers
+  const __nv_bfloat16* xp = second ? a.x[1] : a.x[0];
+  const long long ldx = second ? a.ldx[1] : a.ldx[0];
+  __nv_bfloat16* op = second ? a.out[1] : a.out[0];
+  const long long ldo = second ? a.ldo[1] : a.ldo[0];
+  const int nch = a.N >> 3;
+  uint4 raw[kRowChunks];
 #pragma unroll
-  for (int k = 0; k < kRowsPerCta; ++k)
-    raw[k] = (live && row0 + k < a.M)
-                 ? __ldg(reinterpret_cast<const uint4*>(a.x[tsel] + (size_t)(row0 + k) * a.ldx[tsel] + n0))
-                 : make_uint4(0, 0, 0, 0);
-#pragma unroll
-  for (int k = 0; k < kRowsPerCta; ++k) unpack8(raw[k], f[k]);
-  const __nv_bfloat16* w = a.w[tsel];
-  float r[kRowsPerCta];
-  if (w) {
-#pragma unroll
-    for (int k = 0; k < kRowsPerCta; ++k) {
-      r[k] = 0.f;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) r[k] = fmaf(f[k][j], f[k][j], r[k]);
-    }
-    block_sums<kRowsPerCta>(r, red);
-#pragma unroll
-    for (int k = 0; k < kRowsPerCta; ++k) r[k] = rsqrtf(__fdiv_rn(r[k], (float)a.N) + a.eps);
+  for (int i = 0; i < kRowChunks; ++i) {
+    const int c = t + i * kRowThreads;
+    raw[i] = c < nch ? __ldg(reinterpret_cast<const uint4*>(xp + (size_t)row * ldx) + c)
+                     : make_uint4(0, 0, 0, 0);
   }
-  if (!live) return;
-  float wf[8];
-  if (w) unpack8(__ldg(reinterpret_cast<const uint4*>(w + n0)), wf);
+  const __nv_bfloat16* w = second ? a.w[1] : a.w[0];
+  float r = 0.f;
+  if (w) {
+    float ss = 0.f;
 #pragma unroll
-  for (int k = 0; k < kRowsPerCta; ++k) {
-    const int row = row0 + k;
-    if (row >= a.M) break;
+    for (int i = 0; i < kRowChunks; ++i) {
+      float f[8];
+      unpack8(raw[i], f);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ss = fmaf(f[j], f[j], ss);
+    }
+    r = rsqrtf(__fdiv_rn(row_sum(ss, red), (float)a.N) + a.eps);
+  }
+  const int pos = row % a.span;
+#pragma unroll
+  for (int i = 0; i < kRowChunks; ++i) {
+    const int c = t + i * kRowThreads;
+    if (c >= nch) break;
+    const int n0 = c * 8;
+    float f[8];
+    unpack8(raw[i], f);
     if (w) {
+      float wf[8];
+      unpack8(__ldg(reinterpret_cast<const uint4*>(w + n0)), wf);
 #pragma unroll
-      for (int j = 0; j < 8; ++j)
-        f[k][j] = rc::bf16_to_float(rc::bf16_bits(__fmul_rn(__fmul_rn(f[k][j], r[k]), wf[j])));
+      for (int j = 0; j < 8; ++j) f[j] = rc::bf16_to_float(rc::bf16_bits(__fmul_rn(__fmul_rn(f[j], r), wf[j])));
     }
     if (a.cos) {
-      const int pos = row % a.span, dd = n0 % a.d;   // 8 | d: a thread never straddles heads
-      float c[8], sn[8];
-      loadf8(a.cos + (size_t)pos * a.d + dd, c);
+      const int dd = n0 % a.d;   // 8 | d: a chunk never straddles heads
+      float cs[8], sn[8];
+      loadf8(a.cos + (size_t)pos * a.d + dd, cs);
       loadf8(a.sin + (size_t)pos * a.d + dd, sn);
 #pragma unroll
       for (int j = 0; j < 8; j += 2) {
-        const float e = f[k][j], o = f[k][j + 1];
-        f[k][j] = __fsub_rn(__fmul_rn(e, c[j]), __fmul_rn(o, sn[j]));
-        f[k][j + 1] = __fadd_rn(__fmul_rn(e, sn[j]), __fmul_rn(o, c[j]));
+        const float e = f[j], o = f[j + 1];
+        f[j] = __fsub_rn(__fmul_rn(e, cs[j]), __fmul_rn(o, sn[j]));
+        f[j + 1] = __fadd_rn(__fmul_rn(e, sn[j]), __fmul_rn(o, cs[j]));
       }
     }
-    *reinterpret_cast<uint4*>(a.out[tsel] + (size_t)row * a.ldo[tsel] + n0) = pack8(f[k]);
+    *reinterpret_cast<uint4*>(op + (size_t)row * ldo + n0) = pack8(f);
   }
 }
 
@@ -393,8 +388,7 @@ int rc_ln_modulate_quant(const void* x, long long ldx, int M, int N, const void*
            reinterpret_cast<const __nv_bfloat16*>(weight), reinterpret_cast<const __nv_bfloat16*>(bias),
            shift, scale, eps, reinterpret_cast<__nv_bfloat16*>(out), ldo, codes, scales_swizzled,
            global_scale, M, N};
-  const int threads = ((N / 8) + 31) / 32 * 32;
-  ln_modulate_kernel<<<(M + kLnRows - 1) / kLnRows, threads, 0, stream>>>(a);
+  ln_modulate_kernel<<<M, kRowThreads, 0, stream>>>(a);
   int r = rc::check_launch("rc_ln_modulate_quant");
   if (r || !codes) return r;
   const int katoms = ((N >> 4) + 3) >> 2;
@@ -439,8 +433,8 @@ int rc_rmsnorm_rope(int n_tensors, const void* const* xs, const long long* ldx,
   a.d = d;
   a.span = span;
   if (M == 0) return RC_OK;
-  dim3 grid((M + kRowsPerCta - 1) / kRowsPerCta, n_tensors);
-  rmsnorm_rope_kernel<<<grid, ((N / 8) + 31) / 32 * 32, 0, stream>>>(a);
+  dim3 grid(M, n_tensors);
+  rmsnorm_rope_kernel<<<grid, kRowThreads, 0, stream>>>(a);
   return rc::check_launch("rc_rmsnorm_rope");
 }
 

@@ -7,8 +7,9 @@
     python -m recavsr_b200.profile_case quant        # NVFP4 quantizer 1760x3072
     python -m recavsr_b200.profile_case ln           # LayerNorm+AdaLN+NVFP4 1760x3072
 
-Each case allocates fresh inputs (a few hundred MB at most), runs the kernel
-`--reps` times and prints the mean CUDA-event time per launch.
+Each case allocates fresh inputs (a few hundred MB at most), captures `--reps`
+launches in a CUDA graph, replays it and prints the mean CUDA-event time per
+launch (inputs stay L2-resident between launches, as in the layer loop).
 """
 from __future__ import annotations
 
@@ -113,10 +114,21 @@ def main():
     for _ in range(3):
         run()
     torch.cuda.synchronize()
+    # Replay the launches from a CUDA graph so host launch overhead stays out
+    # of the per-launch device time.
+    graph = torch.cuda.CUDAGraph()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        with torch.cuda.graph(graph, stream=side):
+            for _ in range(args.reps):
+                run()
+    torch.cuda.current_stream().wait_stream(side)
+    graph.replay()
+    torch.cuda.synchronize()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record()
-    for _ in range(args.reps):
-        run()
+    graph.replay()
     b.record()
     b.synchronize()
     dt = a.elapsed_time(b) / args.reps * 1e-3
