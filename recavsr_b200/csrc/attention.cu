@@ -1,7 +1,8 @@
 // Cache-routed self-attention of a QT-frame query block over the current
 // frames plus the routed past planes of the KV cache
 // (recavsr_infer/kernels/local_attention.py:18-169 `_paired_local` and
-// :286-325 `sdpa_attention`).
+// :286-325 `sdpa_attention`), and the rotary-free cross-attention of
+// recavsr_infer/runtime/transformer.py:123-128.
 //
 // Semantics (one batch element, one head):
 //   planes = [past planes i with slots[i] >= 0 (position past_positions[i])]
@@ -15,18 +16,22 @@
 //   out = softmax(q k^T / sqrt(d)) v with fp32 accumulation.
 //
 // Two kernels per launch:
-//  1. rope_gather: rotated copies of q, the current K frames and the routed
-//     past K planes into a caller-provided workspace (slot indirection applied
-//     here, so the attention kernel reads K densely).
-//  2. attention: one CTA per (128-query tile, head). Warp 0 = TMA producer
-//     (Q once, then K (workspace) and V (cache slot / current frame) tiles of
-//     128 keys, double-buffered), warp 1 = tcgen05 MMA issuer (S = Q K^T into a
-//     double-buffered TMEM S, O += P V into TMEM), warps 2-9 = online softmax
-//     (two warps per TMEM lane quadrant, 64 key columns each; exp2 with a
-//     lazily rescaled running max; P double-buffered in shared memory so the
-//     softmax of tile i+1 overlaps the P.V of tile i), then the epilogue.
+//  1. rope_gather: temporally rotated copies of the current K frames and the
+//     routed past K planes into a caller-provided workspace (the slot
+//     indirection is applied here, so the attention kernel reads K densely).
+//  2. attention: one CTA per (128-query tile, head), operands staged by TMA.
+//     Warp 0 = producer: the raw Q tile once, then K tiles (workspace) and V
+//     tiles (read in place from the cache slot / current frame), 128 keys each,
+//     double-buffered.
+//     Warps 2-9 = softmax: first they rotate Q (temporal RoPE, fp32 math) and
+//     store it into tensor memory; then, per key tile, two warps per TMEM lane
+//     quadrant (64 keys each) load S, apply the window mask, keep a lazily
+//     rescaled running max, compute exp2 and store P (bf16) into tensor memory.
+//     Warp 1 = MMA issuer: S = Q K^T and O += P V both read their A operand
+//     (Q, P) from tensor memory, so only K and V stream from shared memory.
+//   TMEM columns: S [0,128) | O [128,256) | Q [256,320) | P0 [320,384) | P1 [384,448).
 //   Dense mode (window covers the grid): query tiles are 128 consecutive tokens,
-//   key tiles 128 consecutive tokens of a plane (4-D TMA view, the plane tail
+//   key tiles 128 consecutive tokens of a plane (4-D TMA view; the plane tail
 //   reads as zeros). Local mode: query tiles are 2 frames x 8 x 8 tokens, key
 //   tiles are 8 x 16 boxes of the union of the tile's windows (5-D TMA view).
 #include <mutex>
@@ -38,11 +43,14 @@ namespace {
 constexpr int kD = 128;             // head dim supported by the tcgen05 kernel
 constexpr int kBM = 128;            // queries per CTA
 constexpr int kBN = 128;            // keys per tile
-constexpr int kThreads = 320;             // producer, MMA, 8 softmax warps
+constexpr int kThreads = 320;       // producer, MMA, 8 softmax warps
 constexpr int kLocalQH = 8, kLocalQW = 8;   // local query tile: 2 frames x 8 x 8
 constexpr int kLocalKH = 8, kLocalKW = 16;  // local key box: 8 rows x 16 cols
 constexpr int kMaxPlanes = 16;
 constexpr float kRescaleThreshold = 8.0f;   // log2 units
+
+// Tensor-memory column map (512 columns allocated).
+constexpr uint32_t kTmS = 0, kTmO = 128, kTmQ = 256, kTmP = 320;   // P buffers at 320 and 384
 
 struct AttnParams {
   int T, H, W, heads, QT, CAP;
@@ -53,7 +61,11 @@ struct AttnParams {
   int qtiles_x, qtiles_y;       // local: tiles along x / y per frame pair
   float scale_log2;             // d^-0.5 * log2(e)
   const int* slots;             // [CAP] device
-  __nv_bfloat16* out;           // [QT*T, heads, d] (nullable when q_codes is set)
+  const int* qpos;              // [QT] device query plane positions (null: no query rotation)
+  const float* cos;             // [positions, td/2] temporal rotary table
+  const float* sin;
+  int td;                       // rotated leading dims of each head (even, <= d)
+  __nv_bfloat16* out;           // [Tq, heads, d] (nullable when q_codes is set)
   long long out_ld;             // elements between tokens
   uint8_t* q_codes;             // optional NVFP4 output [Tq, heads*d/2]
   uint8_t* q_sf;                // its swizzled scales (heads*d as K)
@@ -61,11 +73,10 @@ struct AttnParams {
 
 struct SmemLayout {
   static constexpr int kChunk = 128 * 128;           // 128 rows x 128 bytes
-  static constexpr int offQ = 0;                     // 2 chunks
+  static constexpr int offQ = 0;                     // 2 chunks (raw Q, read once)
   static constexpr int offK = offQ + 2 * kChunk;     // 2 stages x 2 chunks
   static constexpr int offV = offK + 4 * kChunk;     // 2 stages x 2 chunks
-  static constexpr int offP = offV + 4 * kChunk;     // 2 buffers x 2 chunks
-  static constexpr int offBar = offP + 4 * kChunk;
+  static constexpr int offBar = offV + 4 * kChunk;
   static constexpr int kBars = 16;
   static constexpr int offMisc = offBar + kBars * 8;
   static constexpr int offRed = offMisc + 16 + kMaxPlanes * 4;   // [2][2][128] floats
@@ -76,12 +87,8 @@ struct SmemLayout {
 // Enumerates the key tiles of one query tile: planes in order, tiles within.
 struct TileIter {
   const AttnParams& p;
-  const int* splanes;   // smem: source plane index per visible plane (-1 = skip)
-  int nplanes;
-  // local-mode key rectangle
-  int ry0, ry1, rx0, rx1;
-  __device__ TileIter(const AttnParams& p_, const int* sp, int np_, int qy0, int qx0)
-      : p(p_), splanes(sp), nplanes(np_) {
+  int ry0, ry1, rx0, rx1;       // local-mode key rectangle
+  __device__ TileIter(const AttnParams& p_, int qy0, int qx0) : p(p_) {
     if (p.local) {
       const int qy1 = min(qy0 + kLocalQH, p.H) - 1, qx1 = min(qx0 + kLocalQW, p.W) - 1;
       ry0 = min(max(qy0 - p.wh / 2, 0), p.H - p.wh);
@@ -96,15 +103,15 @@ struct TileIter {
     if (!p.local) return (p.T + kBN - 1) / kBN;
     return ((ry1 - ry0 + kLocalKH - 1) / kLocalKH) * ((rx1 - rx0 + kLocalKW - 1) / kLocalKW);
   }
-  // tile j within a plane -> (ky0, kx0) or t0
+  // tile j within a plane -> first token (dense) or box origin (ky0, kx0) (local)
   __device__ void tile_origin(int j, int& a, int& b) const {
     if (!p.local) {
       a = j * kBN;
       b = 0;
     } else {
       const int nx = (rx1 - rx0 + kLocalKW - 1) / kLocalKW;
-      a = ry0 + (j / nx) * kLocalKH;   // y
-      b = rx0 + (j % nx) * kLocalKW;   // x
+      a = ry0 + (j / nx) * kLocalKH;
+      b = rx0 + (j % nx) * kLocalKW;
     }
   }
 };
@@ -117,17 +124,23 @@ __device__ __forceinline__ float fast_exp2(float x) {   // MUFU ex2 (as tl.exp2)
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
-#define RC_TMEM_LD_X32(taddr, r)                                                               \
-  asm volatile(                                                                                \
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"   \
-      "%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"       \
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),    \
-        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),             \
-        "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]),          \
-        "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),          \
-        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),          \
-        "=r"(r[31])                                                                            \
-      : "r"(taddr))
+
+// Rotates the bf16 pairs (even, odd) = (lo, hi) half of each word by the
+// angle of `pair0 + j` (fp32 math, bf16 rounding of each output).
+template <int N>
+__device__ __forceinline__ void rotate_pairs(uint32_t (&w)[N], int pair0, int td, const float* cs,
+                                             const float* sn) {
+#pragma unroll
+  for (int j = 0; j < N; ++j) {
+    const int pr = pair0 + j;
+    if (2 * pr < td) {
+      const float e = __uint_as_float(w[j] << 16), o = __uint_as_float(w[j] & 0xffff0000u);
+      const float c = __ldg(cs + pr), s = __ldg(sn + pr);
+      w[j] = pack_bf16x2(__fsub_rn(__fmul_rn(e, c), __fmul_rn(o, s)),
+                         __fadd_rn(__fmul_rn(e, s), __fmul_rn(o, c)));
+    }
+  }
+}
 
 __global__ void __launch_bounds__(kThreads, 1)
 attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
@@ -137,14 +150,15 @@ attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
   // 1024-byte alignment: the 128-byte TMA swizzle pattern repeats every 1024 bytes.
   extern __shared__ __align__(1024) uint8_t smem[];
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::offBar);
-  uint64_t* q_full = bars + 0;
-  uint64_t* kv_full = bars + 1;    // [2]
-  uint64_t* kv_empty = bars + 3;   // [2]
-  uint64_t* s_full = bars + 5;     // [2]
-  uint64_t* s_free = bars + 7;     // [2]
-  uint64_t* p_full = bars + 9;     // [2] one per P buffer
-  uint64_t* o_done = bars + 11;    // [2] P.V on P buffer b finished
-  uint64_t* done = bars + 13;
+  uint64_t* q_full = bars + 0;     // raw Q landed in shared memory
+  uint64_t* q_tmem = bars + 1;     // rotated Q stored in tensor memory (256 arrivals)
+  uint64_t* kv_full = bars + 2;    // [2]
+  uint64_t* kv_empty = bars + 4;   // [2]
+  uint64_t* s_full = bars + 6;     // S = Q K^T of the current tile finished
+  uint64_t* s_free = bars + 7;     // S loaded by all softmax threads (256 arrivals)
+  uint64_t* p_full = bars + 8;     // [2] P buffer written (256 arrivals)
+  uint64_t* o_done = bars + 10;    // [2] P.V reading P buffer b finished
+  uint64_t* done = bars + 12;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::offMisc);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::offMisc + 4);
   int* s_nplanes = reinterpret_cast<int*>(smem + L::offMisc + 8);
@@ -168,14 +182,15 @@ attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
 
   if (threadIdx.x == 0) {
     sm100::mbar_init(q_full, 1);
+    sm100::mbar_init(q_tmem, 256);
     for (int s2 = 0; s2 < 2; ++s2) {
       sm100::mbar_init(&kv_full[s2], 1);
       sm100::mbar_init(&kv_empty[s2], 1);
-      sm100::mbar_init(&s_full[s2], 1);
-      sm100::mbar_init(&s_free[s2], 256);
       sm100::mbar_init(&p_full[s2], 256);
       sm100::mbar_init(&o_done[s2], 1);
     }
+    sm100::mbar_init(s_full, 1);
+    sm100::mbar_init(s_free, 256);
     sm100::mbar_init(done, 1);
     *abort_flag = 0;
     // Visible planes: routed past planes (slot >= 0), then the current frames.
@@ -194,9 +209,9 @@ attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
   __syncthreads();
   sm100::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t t_s0 = tmem, t_o = tmem + 256;
+  const uint32_t t_s = tmem + kTmS, t_o = tmem + kTmO, t_q = tmem + kTmQ;
   const int nplanes = *s_nplanes;
-  TileIter it(p, s_planes, nplanes, qy0, qx0);
+  TileIter it(p, qy0, qx0);
   const int tpp = it.tiles_per_plane();
   const int n_tiles = nplanes * tpp;
 
@@ -252,19 +267,16 @@ attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
     if (sm100::elect_one_sync()) {
       constexpr uint32_t idesc_qk = sm100::idesc_bf16(kBM, kBN, 0, 0);
       constexpr uint32_t idesc_pv = sm100::idesc_bf16(kBM, kD, 0, 1);
-      const uint32_t sq = sm100::smem_u32(smem + L::offQ);
-      bool ok = wait(q_full, 0, 2);
+      bool ok = wait(q_tmem, 0, 2);
       sm100::tc_fence_after();
       auto issue_pv = [&](int j) -> bool {
         if (!wait(&p_full[j & 1], (j >> 1) & 1, 3)) return false;
         sm100::tc_fence_after();
-        const uint32_t sp = sm100::smem_u32(smem + L::offP + (j & 1) * 2 * L::kChunk);
+        const uint32_t t_p = tmem + kTmP + (uint32_t)(j & 1) * 64;
         const uint32_t sv = sm100::smem_u32(smem + L::offV + (j & 1) * 2 * L::kChunk);
-        for (int k = 0; k < kBN / 16; ++k) {
-          const uint64_t ad = sm100::desc_kmajor_sw128(sp + (k >> 2) * L::kChunk + (k & 3) * 32);
-          const uint64_t bd = sm100::desc_mnmajor_sw128(sv + k * 16 * 128, L::kChunk);
-          sm100::mma_f16_ss(t_o, ad, bd, idesc_pv, (j > 0 || k > 0) ? 1u : 0u);
-        }
+        for (int k = 0; k < kBN / 16; ++k)
+          sm100::mma_f16_ts(t_o, t_p + 8 * k, sm100::desc_mnmajor_sw128(sv + k * 16 * 128, L::kChunk),
+                            idesc_pv, (j > 0 || k > 0) ? 1u : 0u);
         sm100::tc_commit(&kv_empty[j & 1]);
         sm100::tc_commit(&o_done[j & 1]);
         return true;
@@ -272,16 +284,14 @@ attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       for (int i = 0; i < n_tiles && ok; ++i) {
         const int st = i & 1;
         if (!wait(&kv_full[st], (i >> 1) & 1, 4)) { ok = false; break; }
-        if (!wait(&s_free[st], ((i >> 1) & 1) ^ 1, 5)) { ok = false; break; }
+        if (!wait(s_free, (i & 1) ^ 1, 5)) { ok = false; break; }   // S(i-1) is in registers
         sm100::tc_fence_after();
         const uint32_t sk = sm100::smem_u32(smem + L::offK + st * 2 * L::kChunk);
-        const uint32_t t_s = t_s0 + st * 128;
-        for (int k = 0; k < kD / 16; ++k) {
-          const uint32_t off = (k >> 2) * L::kChunk + (k & 3) * 32;
-          sm100::mma_f16_ss(t_s, sm100::desc_kmajor_sw128(sq + off), sm100::desc_kmajor_sw128(sk + off),
+        for (int k = 0; k < kD / 16; ++k)
+          sm100::mma_f16_ts(t_s, t_q + 8 * k,
+                            sm100::desc_kmajor_sw128(sk + (k >> 2) * L::kChunk + (k & 3) * 32),
                             idesc_qk, k > 0 ? 1u : 0u);
-        }
-        sm100::tc_commit(&s_full[st]);
+        sm100::tc_commit(s_full);
         if (i > 0 && !issue_pv(i - 1)) { ok = false; break; }
       }
       if (ok && n_tiles > 0) issue_pv(n_tiles - 1);
@@ -290,45 +300,76 @@ attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
     }
   } else {
     // ----------------------------------------------------------- softmax
-    // Two warps per TMEM lane quadrant: `half` selects key columns
-    // [64*half, 64*half+64) of S, the matching P chunk and O columns.
+    // Two warps per TMEM lane quadrant: `half` selects head dims
+    // [64*half, 64*half+64) of Q and O, and key columns [64*half, 64*half+64)
+    // of S and P.
     const int quad = warp & 3;
     const int half = (warp - 2) >> 2;
     const int r = quad * 32 + lane;               // query row within the tile / TMEM lane
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
     const int cbase = half * 64;
     float* red = reinterpret_cast<float*>(smem + L::offRed);   // [2 tiles][2 halves][128 rows]
-    auto pair_sync = [&]() { asm volatile("bar.sync %0, 64;" ::"r"(1 + quad) : "memory"); };
-    int qrow = -1, qy = 0, qx = 0;
+    // Both warps of a pair pass the same number of pair barriers on every path
+    // (one per key tile, then one for the row sum): an early exit drains the rest.
+    int pair_syncs = 0;
+    auto pair_sync = [&]() {
+      asm volatile("bar.sync %0, 64;" ::"r"(1 + quad) : "memory");
+      ++pair_syncs;
+    };
+    int qrow = -1, qf = 0, qy = 0, qx = 0;
     if (!p.local) {
       const int t = q_row0 + r;
       if (t < p.Tq) qrow = t;
+      qf = t / p.T;
     } else {
       const int f = qf0 + (r >> 6), yy = qy0 + ((r >> 3) & 7), xx = qx0 + (r & 7);
       if (f < p.QT && yy < p.H && xx < p.W) qrow = f * p.T + yy * p.W + xx;
+      qf = f;
       qy = yy;
       qx = xx;
     }
+    bool ok = __all_sync(0xffffffffu, wait(q_full, 0, 10));
+    if (ok) {
+      // This thread's 64 dims of its Q row -> temporal RoPE -> tensor memory.
+      uint32_t qv[32];
+      const uint8_t* src = smem + L::offQ + half * L::kChunk + r * 128;
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const uint4 w = *reinterpret_cast<const uint4*>(src + ((u ^ (r & 7)) << 4));
+        qv[4 * u] = w.x;
+        qv[4 * u + 1] = w.y;
+        qv[4 * u + 2] = w.z;
+        qv[4 * u + 3] = w.w;
+      }
+      if (p.qpos && qrow >= 0 && cbase < p.td) {
+        const int pos = p.qpos[qf];
+        rotate_pairs(qv, cbase >> 1, p.td, p.cos + (size_t)pos * (p.td >> 1),
+                     p.sin + (size_t)pos * (p.td >> 1));
+      }
+      sm100::tmem_st32(t_q + half * 32 + lane_off, qv);
+      sm100::tmem_st_wait();
+    }
+    sm100::tc_fence_before();
+    sm100::mbar_arrive(q_tmem);
     const int top = min(max(qy - p.wh / 2, 0), p.H - p.wh);
     const int left = min(max(qx - p.ww / 2, 0), p.W - p.ww);
     const float scale = p.scale_log2;
     float m_used = -INFINITY, l = 0.f;
-    bool ok = true;
-    for (int i = 0; i < n_tiles; ++i) {
+    for (int i = 0; i < n_tiles && ok; ++i) {
       const int st = i & 1;
-      if (!__all_sync(0xffffffffu, wait(&s_full[st], (i >> 1) & 1, 6))) { ok = false; break; }
+      if (!__all_sync(0xffffffffu, wait(s_full, i & 1, 6))) { ok = false; break; }
       sm100::tc_fence_after();
       int a, b;
       it.tile_origin(i % tpp, a, b);
       const bool full_tile = !p.local && a + kBN <= p.T;
       float v[64];
       {
-        const uint32_t t_s = t_s0 + st * 128 + cbase + lane_off;
+        const uint32_t ts = t_s + cbase + lane_off;
         uint32_t r0[16], r1[16], r2[16], r3[16];
-        sm100::tmem_ld16(t_s, r0);
-        sm100::tmem_ld16(t_s + 16, r1);
-        sm100::tmem_ld16(t_s + 32, r2);
-        sm100::tmem_ld16(t_s + 48, r3);
+        sm100::tmem_ld16(ts, r0);
+        sm100::tmem_ld16(ts + 16, r1);
+        sm100::tmem_ld16(ts + 32, r2);
+        sm100::tmem_ld16(ts + 48, r3);
         sm100::tmem_ld_wait();
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
@@ -338,9 +379,9 @@ attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
           v[48 + j] = __uint_as_float(r3[j]);
         }
       }
-      // S is in registers: the MMA may overwrite this buffer with S(i+2).
+      // S is in registers: the MMA may write S of the next tile.
       sm100::tc_fence_before();
-      sm100::mbar_arrive(&s_free[st]);
+      sm100::mbar_arrive(s_free);
       if (!full_tile) {
         // Validity of this warp's 64 keys as a bit mask: dense = a prefix of the
         // plane; local = 4 box rows x 16 box columns intersected with the window.
@@ -382,22 +423,21 @@ attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
         m_used = mt;
       }
       const float mref = m_used == -INFINITY ? 0.f : m_used;
-      float sum = 0.f;
+      float sum0 = 0.f, sum1 = 0.f;
+      uint32_t pk[32];
 #pragma unroll
-      for (int j = 0; j < 64; ++j) {
-        v[j] = fast_exp2(fmaf(v[j], scale, -mref));   // exp2(-inf) = 0 for masked keys
-        sum += v[j];
+      for (int j = 0; j < 32; ++j) {
+        const float e0 = fast_exp2(fmaf(v[2 * j], scale, -mref));   // exp2(-inf) = 0 when masked
+        const float e1 = fast_exp2(fmaf(v[2 * j + 1], scale, -mref));
+        sum0 += e0;
+        sum1 += e1;
+        pk[j] = pack_bf16x2(e0, e1);
       }
-      l = __fmul_rn(l, corr) + sum;
+      l = __fmul_rn(l, corr) + (sum0 + sum1);
       // The P buffer of this tile was last read by the P.V of tile i-2.
       if (i >= 2 && !__all_sync(0xffffffffu, wait(&o_done[st], ((i >> 1) - 1) & 1, 7))) { ok = false; break; }
-      uint8_t* sp = smem + L::offP + st * 2 * L::kChunk + half * L::kChunk;
-#pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const uint4 w = make_uint4(pack_bf16x2(v[8 * u], v[8 * u + 1]), pack_bf16x2(v[8 * u + 2], v[8 * u + 3]),
-                                   pack_bf16x2(v[8 * u + 4], v[8 * u + 5]), pack_bf16x2(v[8 * u + 6], v[8 * u + 7]));
-        *reinterpret_cast<uint4*>(sp + r * 128 + ((u ^ (r & 7)) << 4)) = w;
-      }
+      sm100::tc_fence_after();
+      sm100::tmem_st32(tmem + kTmP + (uint32_t)st * 64 + half * 32 + lane_off, pk);
       // O changes only when a row's reference max moved (rare); then wait for P.V(i-1).
       if (__any_sync(0xffffffffu, rescale)) {
         if (!__all_sync(0xffffffffu, wait(&o_done[st ^ 1], ((i - 1) >> 1) & 1, 9))) { ok = false; break; }
@@ -412,12 +452,12 @@ attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
           for (int j = 0; j < 16; ++j) w[j] = __float_as_uint(__uint_as_float(w[j]) * f);
           sm100::tmem_st16(t_o + c + lane_off, w);
         }
-        sm100::tmem_st_wait();
       }
-      sm100::fence_proxy_async_smem();
+      sm100::tmem_st_wait();
       sm100::tc_fence_before();
       sm100::mbar_arrive(&p_full[st]);
     }
+    while (pair_syncs < n_tiles) pair_sync();
     // Row sum over both halves.
     red[half * 128 + r] = l;
     pair_sync();
@@ -483,13 +523,11 @@ attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
 
 // ------------------------------------------------------------------ pre-pass
 struct GatherParams {
-  const __nv_bfloat16* q; long long q_ld, q_hs;     // token / head strides (elements)
-  const __nv_bfloat16* ck; long long ck_ld, ck_hs;
+  const __nv_bfloat16* ck; long long ck_ld, ck_hs;   // token / head strides (elements)
   const __nv_bfloat16* pk; long long pk_ld, pk_hs;
   const int* slots; const int* ppos; const int* qpos;
-  const float* cos; const float* sin;          // [*, td/2]
-  __nv_bfloat16* q_out;                        // [QT*T, heads*d]
-  __nv_bfloat16* k_out;                        // [(CAP+QT)*T, heads*d]
+  const float* cos; const float* sin;                 // [*, td/2]
+  __nv_bfloat16* k_out;                               // [(CAP+QT)*T, heads*d]
   int T, QT, CAP, hd, td, d;
 };
 
@@ -497,6 +535,8 @@ struct GatherParams {
 // thread keeps kGatherUnroll independent loads in flight.
 constexpr int kGatherUnroll = 4;
 
+// Workspace plane order: routed past planes [0, CAP) (slot indirection
+// applied), then the current frames.
 __device__ __forceinline__ bool gather_src(const GatherParams& g, long long i, int vec,
                                            const __nv_bfloat16*& src, __nv_bfloat16*& dst, int& pos,
                                            int& dd) {
@@ -505,32 +545,24 @@ __device__ __forceinline__ bool gather_src(const GatherParams& g, long long i, i
   const int plane = (int)(tok / g.T), t = (int)(tok % g.T);
   const int head = (v * 8) / g.d;
   dd = (v * 8) % g.d;
-  if (plane < g.QT) {
-    src = g.q + ((long long)plane * g.T + t) * g.q_ld + head * g.q_hs;
-    dst = g.q_out + ((long long)plane * g.T + t) * g.hd;
-    pos = g.qpos[plane];
-  } else if (plane < g.QT + g.CAP) {
-    const int i2 = plane - g.QT;
-    const int slot = g.slots[i2];
+  if (plane < g.CAP) {
+    const int slot = g.slots[plane];
     if (slot < 0 || slot >= g.CAP) return false;
     src = g.pk + ((long long)slot * g.T + t) * g.pk_ld + head * g.pk_hs;
-    dst = g.k_out + ((long long)i2 * g.T + t) * g.hd;
-    pos = g.ppos[i2];
+    pos = g.ppos[plane];
   } else {
-    const int f = plane - g.QT - g.CAP;
+    const int f = plane - g.CAP;
     src = g.ck + ((long long)f * g.T + t) * g.ck_ld + head * g.ck_hs;
-    dst = g.k_out + ((long long)(g.CAP + f) * g.T + t) * g.hd;
     pos = g.qpos[f];
   }
   src += dd;
-  dst += head * g.d + dd;
+  dst = g.k_out + ((long long)plane * g.T + t) * g.hd + head * g.d + dd;
   return true;
 }
 
 __global__ void rope_gather_kernel(GatherParams g) {
   const int vec = g.hd >> 3;
-  const int planes = g.QT + g.CAP + g.QT;
-  const long long total = (long long)planes * g.T * vec;
+  const long long total = (long long)(g.CAP + g.QT) * g.T * vec;
   const long long stride = (long long)gridDim.x * blockDim.x;
   for (long long base = blockIdx.x * (long long)blockDim.x + threadIdx.x; base < total;
        base += stride * kGatherUnroll) {
@@ -553,17 +585,8 @@ __global__ void rope_gather_kernel(GatherParams g) {
       uint4 r4 = raw[u];
       if (dd[u] < g.td) {
         uint32_t w[4] = {r4.x, r4.y, r4.z, r4.w};
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const int pr = (dd[u] >> 1) + j;
-          if (2 * pr < g.td) {
-            const float e = __uint_as_float(w[j] << 16), o = __uint_as_float(w[j] & 0xffff0000u);
-            const float c = g.cos[pos[u] * (g.td >> 1) + pr], sn = g.sin[pos[u] * (g.td >> 1) + pr];
-            const float ne = __fsub_rn(__fmul_rn(e, c), __fmul_rn(o, sn));
-            const float no = __fadd_rn(__fmul_rn(e, sn), __fmul_rn(o, c));
-            w[j] = pack_bf16x2(ne, no);
-          }
-        }
+        rotate_pairs(w, dd[u] >> 1, g.td, g.cos + (size_t)pos[u] * (g.td >> 1),
+                     g.sin + (size_t)pos[u] * (g.td >> 1));
         r4 = make_uint4(w[0], w[1], w[2], w[3]);
       }
       *reinterpret_cast<uint4*>(dst[u]) = r4;
@@ -571,8 +594,9 @@ __global__ void rope_gather_kernel(GatherParams g) {
   }
 }
 
-// Tensor-map views (innermost first): dense (d, heads, tokens, planes),
-// local (d, heads, W, H, planes); `ld` = elements between tokens.
+// Key / value views (innermost first): dense (d, heads, tokens, planes) with
+// 128-token boxes, local (d, heads, W, H, planes) with 8 x 16 boxes;
+// `ld` = elements between tokens, `hs` = between heads.
 int make_view(CUtensorMap* m, const void* base, long long ld, long long hs, int heads, int T, int H,
               int W, int planes, bool local, const char* what) {
   if (local) {
@@ -590,12 +614,41 @@ int make_view(CUtensorMap* m, const void* base, long long ld, long long hs, int 
                          CU_TENSOR_MAP_SWIZZLE_128B, what);
 }
 
+// Query views: dense (d, heads, tokens) with 128-token boxes; local
+// (d, heads, W, H, frames) with 8 x 8 x 2-frame boxes.
+int make_query_view(CUtensorMap* m, const void* base, long long ld, long long hs, int heads, int T,
+                    int H, int W, int frames, bool local, const char* what) {
+  if (local) {
+    const uint64_t dims[5] = {(uint64_t)kD, (uint64_t)heads, (uint64_t)W, (uint64_t)H, (uint64_t)frames};
+    const uint64_t str[4] = {(uint64_t)hs * 2, (uint64_t)ld * 2, (uint64_t)ld * 2 * W,
+                             (uint64_t)ld * 2 * T};
+    const uint32_t box[5] = {64, 1, kLocalQW, kLocalQH, 2};
+    return rc::encode_tmap(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 5, const_cast<void*>(base), dims, str, box,
+                           CU_TENSOR_MAP_SWIZZLE_128B, what);
+  }
+  const uint64_t dims[3] = {(uint64_t)kD, (uint64_t)heads, (uint64_t)frames * T};
+  const uint64_t str[2] = {(uint64_t)hs * 2, (uint64_t)ld * 2};
+  const uint32_t box[3] = {64, 1, kBM};
+  return rc::encode_tmap(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, str, box,
+                         CU_TENSOR_MAP_SWIZZLE_128B, what);
+}
+
 bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 int g_attr_set = 0;
 
+int ensure_smem_attr(const char* what) {
+  if (!g_attr_set) {
+    if (cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             SmemLayout::kAlloc) != cudaSuccess)
+      return rc::set_error(RC_ERR_CUDA, "%s: shared memory attribute", what);
+    g_attr_set = 1;
+  }
+  return RC_OK;
+}
+
 // ---------------------------------------------------------------------------
-// Allocation-free variant. Its scratch (the rotated q / K planes the attention
+// Allocation-free variant. Its scratch (the rotated K planes the attention
 // kernel reads) lives in this file-scope device array instead of a caller
 // buffer. Every GPU that loads the library holds these 64 MiB until the
 // process exits. Host code cannot pass the array's name to a kernel: that name
@@ -615,12 +668,12 @@ extern "C" {
 
 long long rc_paired_attention_workspace(int B, int QT, int CAP, int H, int W, int heads, int d) {
   if (B <= 0 || QT <= 0 || CAP < 0 || H <= 0 || W <= 0 || heads <= 0 || d <= 0) return -1;
-  return (long long)B * (2LL * QT + CAP) * H * W * heads * d * 2;
+  return (long long)B * (QT + CAP) * H * W * heads * d * 2;
 }
 
 // strides[15]: (batch, token, head) strides in elements of q, ck, cv, pk, pv
 // (the head dim itself must be contiguous). slots / positions / rotary tables
-// live on the device; the workspace holds the rotated q and K planes.
+// live on the device; the workspace holds the rotated K planes.
 int rc_paired_attention(const void* q, const void* ck, const void* cv, const void* pk, const void* pv,
                         const long long* strides, const int* slots, const int* past_positions,
                         const int* query_positions, const float* cos, const float* sin, int B,
@@ -656,46 +709,27 @@ int rc_paired_attention(const void* q, const void* ck, const void* cv, const voi
   const int wh = window_h < H ? window_h : H, ww = window_w < W ? window_w : W;
   const bool local = wh < H || ww < W;
   if (local && QT % 2) return rc::set_error(RC_ERR_UNSUPPORTED, "%s: local windows need an even frame count", what);
-  if (!g_attr_set) {
-    if (cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             SmemLayout::kAlloc) != cudaSuccess)
-      return rc::set_error(RC_ERR_CUDA, "%s: shared memory attribute", what);
-    g_attr_set = 1;
-  }
+  if (out_codes && B > 1) return rc::set_error(RC_ERR_UNSUPPORTED, "%s: NVFP4 output needs B == 1", what);
+  int r = ensure_smem_attr(what);
+  if (r) return r;
   const long long hd = (long long)heads * d;
-  const long long per_batch = (2LL * QT + CAP) * T * hd;
+  const long long per_batch = (long long)(QT + CAP) * T * hd;
   for (int b = 0; b < B; ++b) {
-    __nv_bfloat16* qs = reinterpret_cast<__nv_bfloat16*>(workspace) + b * per_batch;
-    __nv_bfloat16* ks = qs + (long long)QT * T * hd;
+    __nv_bfloat16* ks = reinterpret_cast<__nv_bfloat16*>(workspace) + b * per_batch;
     const __nv_bfloat16* qb = reinterpret_cast<const __nv_bfloat16*>(q) + b * strides[0];
     const __nv_bfloat16* ckb = reinterpret_cast<const __nv_bfloat16*>(ck) + b * strides[3];
     const __nv_bfloat16* cvb = reinterpret_cast<const __nv_bfloat16*>(cv) + b * strides[6];
     const __nv_bfloat16* pkb = CAP ? reinterpret_cast<const __nv_bfloat16*>(pk) + b * strides[9] : nullptr;
     const __nv_bfloat16* pvb = CAP ? reinterpret_cast<const __nv_bfloat16*>(pv) + b * strides[12] : nullptr;
-    GatherParams g{qb, strides[1], strides[2], ckb, strides[4], strides[5], pkb, strides[10],
-                   strides[11], slots, past_positions, query_positions, cos, sin, qs, ks,
-                   T, QT, CAP, (int)hd, td, d};
-    const long long work = (2LL * QT + CAP) * T * (hd / 8);
+    GatherParams g{ckb, strides[4], strides[5], pkb, strides[10], strides[11], slots, past_positions,
+                   query_positions, cos, sin, ks, T, QT, CAP, (int)hd, td, d};
+    const long long work = (long long)(QT + CAP) * T * (hd / 8);
     long long blocks = (work + 255) / 256;
     if (blocks > 148LL * 16) blocks = 148LL * 16;
     rope_gather_kernel<<<(int)blocks, 256, 0, stream>>>(g);
-    int r = rc::check_launch("rc_paired_attention(rope)");
-    if (r) return r;
+    if ((r = rc::check_launch("rc_paired_attention(rope)"))) return r;
     CUtensorMap tq, tk, tpv, tcv;
-    if (!local) {
-      const uint64_t dims[3] = {(uint64_t)kD, (uint64_t)heads, (uint64_t)QT * T};
-      const uint64_t str[2] = {(uint64_t)kD * 2, (uint64_t)hd * 2};
-      const uint32_t box[3] = {64, 1, kBM};
-      r = rc::encode_tmap(&tq, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, qs, dims, str, box,
-                          CU_TENSOR_MAP_SWIZZLE_128B, what);
-    } else {
-      const uint64_t dims[5] = {(uint64_t)kD, (uint64_t)heads, (uint64_t)W, (uint64_t)H, (uint64_t)QT};
-      const uint64_t str[4] = {(uint64_t)kD * 2, (uint64_t)hd * 2, (uint64_t)hd * 2 * W, (uint64_t)hd * 2 * T};
-      const uint32_t box[5] = {64, 1, kLocalQW, kLocalQH, 2};
-      r = rc::encode_tmap(&tq, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 5, qs, dims, str, box,
-                          CU_TENSOR_MAP_SWIZZLE_128B, what);
-    }
-    if (r) return r;
+    if ((r = make_query_view(&tq, qb, strides[1], strides[2], heads, T, H, W, QT, local, what))) return r;
     if ((r = make_view(&tk, ks, hd, d, heads, T, H, W, CAP + QT, local, what))) return r;
     if ((r = make_view(&tcv, cvb, strides[7], strides[8], heads, T, H, W, QT, local, what))) return r;
     if (CAP) {
@@ -708,9 +742,12 @@ int rc_paired_attention(const void* q, const void* ck, const void* cv, const voi
     p.wh = wh; p.ww = ww; p.local = local;
     p.scale_log2 = (float)(1.0 / sqrt((double)d) * 1.4426950408889634);
     p.slots = slots;
+    p.qpos = query_positions;
+    p.cos = cos;
+    p.sin = sin;
+    p.td = td;
     p.out = out ? reinterpret_cast<__nv_bfloat16*>(out) + (long long)b * QT * T * out_ld : nullptr;
     p.out_ld = out_ld;
-    if (out_codes && B > 1) return rc::set_error(RC_ERR_UNSUPPORTED, "%s: NVFP4 output needs B == 1", what);
     p.q_codes = out_codes;
     p.q_sf = out_scales;
     if (!local) {
@@ -750,23 +787,14 @@ int rc_cross_attention(const void* q, const void* k, const void* v, const long l
   if (!al16(q) || !al16(k) || !al16(v) || (out && (!al16(out) || out_ld % 8)))
     return rc::set_error(RC_ERR_ARG, "%s: tensors must be 16-byte aligned", what);
   if (Nq == 0) return RC_OK;
-  if (!g_attr_set) {
-    if (cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             SmemLayout::kAlloc) != cudaSuccess)
-      return rc::set_error(RC_ERR_CUDA, "%s: shared memory attribute", what);
-    g_attr_set = 1;
-  }
+  int r = ensure_smem_attr(what);
+  if (r) return r;
   for (int b = 0; b < B; ++b) {
     const __nv_bfloat16* qb = reinterpret_cast<const __nv_bfloat16*>(q) + b * strides[0];
     const __nv_bfloat16* kb = reinterpret_cast<const __nv_bfloat16*>(k) + b * strides[3];
     const __nv_bfloat16* vb = reinterpret_cast<const __nv_bfloat16*>(v) + b * strides[6];
     CUtensorMap tq, tk, tv;
-    const uint64_t dims[3] = {(uint64_t)kD, (uint64_t)heads, (uint64_t)Nq};
-    const uint64_t str[2] = {(uint64_t)strides[2] * 2, (uint64_t)strides[1] * 2};
-    const uint32_t box[3] = {64, 1, kBM};
-    int r = rc::encode_tmap(&tq, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<__nv_bfloat16*>(qb),
-                            dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B, what);
-    if (r) return r;
+    if ((r = make_query_view(&tq, qb, strides[1], strides[2], heads, Nq, 1, Nq, 1, false, what))) return r;
     if ((r = make_view(&tk, kb, strides[4], strides[5], heads, Nk, 1, Nk, 1, false, what))) return r;
     if ((r = make_view(&tv, vb, strides[7], strides[8], heads, Nk, 1, Nk, 1, false, what))) return r;
     AttnParams p{};
@@ -774,6 +802,8 @@ int rc_cross_attention(const void* q, const void* k, const void* v, const long l
     p.wh = 1; p.ww = Nk; p.local = 0;
     p.scale_log2 = (float)(1.0 / sqrt((double)d) * 1.4426950408889634);
     p.slots = nullptr;
+    p.qpos = nullptr;       // no rotary embedding
+    p.td = 0;
     p.out = out ? reinterpret_cast<__nv_bfloat16*>(out) + (long long)b * Nq * out_ld : nullptr;
     p.out_ld = out_ld;
     p.q_codes = out_codes;
@@ -785,7 +815,6 @@ int rc_cross_attention(const void* q, const void* k, const void* v, const long l
   }
   return RC_OK;
 }
-
 
 // Same computation as rc_paired_attention, for callers that cannot allocate
 // device memory; see include/recavsr_b200.h for the contract.

@@ -75,7 +75,7 @@ def test_static_scratch_matches_workspace_entry():
 def test_static_scratch_rejects_oversized_geometry():
     from recavsr_b200 import _lib
     lib = _lib.library()
-    # 2 frames of 60x34 tokens x 24 heads with 8 cached planes needs ~150 MiB of scratch.
+    # 2 frames of 60x34 tokens x 24 heads with 8 cached planes needs ~120 MiB of scratch.
     z = torch.zeros(16, dtype=torch.bfloat16, device="cuda")
     i = torch.zeros(8, dtype=torch.int32, device="cuda")
     st = (C.c_longlong * 15)(*([0, 3072, 128] * 5))
