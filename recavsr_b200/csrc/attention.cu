@@ -116,8 +116,11 @@ struct TileIter {
   }
 };
 
-__device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
-  return (uint32_t)rc::bf16_bits(a) | ((uint32_t)rc::bf16_bits(b) << 16);
+using rc::pack_bf16x2;
+__device__ __forceinline__ float max3(float a, float b, float c) {   // three-input max (sm_100)
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
 }
 __device__ __forceinline__ float fast_exp2(float x) {   // MUFU ex2 (as tl.exp2)
   float y;
@@ -406,9 +409,17 @@ attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
 #pragma unroll
         for (int j = 0; j < 64; ++j) v[j] = ((mask >> j) & 1ull) ? v[j] : -INFINITY;
       }
-      float mt = -INFINITY;
+      // Row max of this warp's 64 columns: 8 independent three-input chains.
+      float mx[8];
 #pragma unroll
-      for (int j = 0; j < 64; ++j) mt = fmaxf(mt, v[j]);
+      for (int k = 0; k < 8; ++k) mx[k] = max3(v[k], v[k + 8], v[k + 16]);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) mx[k] = max3(mx[k], v[k + 24], v[k + 32]);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) mx[k] = max3(mx[k], v[k + 40], v[k + 48]);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) mx[k] = fmaxf(mx[k], v[k + 56]);
+      float mt = max3(max3(mx[0], mx[1], mx[2]), max3(mx[3], mx[4], mx[5]), fmaxf(mx[6], mx[7]));
       // Row max over both halves (raw scores; scale > 0 commutes with max).
       red[(st * 2 + half) * 128 + r] = mt;
       pair_sync();
@@ -423,17 +434,17 @@ attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
         m_used = mt;
       }
       const float mref = m_used == -INFINITY ? 0.f : m_used;
-      float sum0 = 0.f, sum1 = 0.f;
+      float sum[4] = {0.f, 0.f, 0.f, 0.f};
       uint32_t pk[32];
 #pragma unroll
       for (int j = 0; j < 32; ++j) {
         const float e0 = fast_exp2(fmaf(v[2 * j], scale, -mref));   // exp2(-inf) = 0 when masked
         const float e1 = fast_exp2(fmaf(v[2 * j + 1], scale, -mref));
-        sum0 += e0;
-        sum1 += e1;
+        sum[(2 * j) & 3] += e0;
+        sum[(2 * j + 1) & 3] += e1;
         pk[j] = pack_bf16x2(e0, e1);
       }
-      l = __fmul_rn(l, corr) + (sum0 + sum1);
+      l = __fmul_rn(l, corr) + ((sum[0] + sum[1]) + (sum[2] + sum[3]));
       // The P buffer of this tile was last read by the P.V of tile i-2.
       if (i >= 2 && !__all_sync(0xffffffffu, wait(&o_done[st], ((i >> 1) - 1) & 1, 7))) { ok = false; break; }
       sm100::tc_fence_after();
@@ -485,19 +496,9 @@ attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
         }
         if (p.q_codes && qrow >= 0) {
           // NVFP4 of the bf16 output (16 columns = one block), for the o-proj GEMM.
-          float amax = 0.f;
-#pragma unroll
-          for (int j = 0; j < 16; ++j) amax = rc::absmax_nan(amax, y[j]);
-          float sc = __fdiv_rn(amax, 6.0f);
-          sc = sc < 0.001953125f ? 0.001953125f : sc;
-          const uint8_t sfb = rc::e4m3_from_float(sc);
-          const rc::E2m1Bounds bd(rc::e4m3_to_float(sfb));
-          uint32_t lo = 0, hi = 0;
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            lo |= bd.code(y[j]) << (4 * j);
-            hi |= bd.code(y[8 + j]) << (4 * j);
-          }
+          uint8_t sfb;
+          uint32_t lo, hi;
+          rc::nvfp4_encode16(y, sfb, lo, hi);
           const int kb = (head * kD + c) >> 4;
           *reinterpret_cast<uint2*>(p.q_codes + (size_t)qrow * (p.heads * kD / 2) + (kb << 3)) = make_uint2(lo, hi);
           p.q_sf[rc::sf_offset(qrow, kb, katoms)] = sfb;

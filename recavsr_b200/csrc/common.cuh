@@ -128,33 +128,92 @@ __host__ __device__ __forceinline__ uint32_t e2m1_code(float z) {
   return c | (z < 0.0f ? 8u : 0u);
 }
 
-// Division-free E2M1 ladder for bf16 inputs x and an E4M3 scale s (global
-// scale 1). Exactness: x has 8 significant bits, s at most 4 and every
-// threshold t at most 3, so t*s is exact in fp32 and any x != t*s lies at
-// least 2^-9 (relative) away from it -- far more than the 2^-24 rounding of
-// fp32 division -- hence fl(|x|/s) > t  <=>  |x| > t*s (and likewise for >=).
-// The codes therefore equal e2m1_code(x / s) bit for bit. A NaN scale (block
-// amax >= 2784 or non-finite) gives code 0 for every element, as x / NaN does.
-struct E2m1Bounds {
-  float b[7];
-  bool nan;
-  __host__ __device__ __forceinline__ explicit E2m1Bounds(float s) {
-    b[0] = 0.25f * s; b[1] = 0.75f * s; b[2] = 1.25f * s; b[3] = 1.75f * s;
-    b[4] = 2.5f * s;  b[5] = 3.5f * s;  b[6] = 5.0f * s;
-    nan = !(s == s);
-  }
-  __host__ __device__ __forceinline__ uint32_t code(float x) const {
-    const float a = fabsf(x);
-    const uint32_t c = (a > b[0]) + (a >= b[1]) + (a > b[2]) + (a >= b[3]) + (a > b[4]) +
-                       (a >= b[5]) + (a > b[6]);
-    return nan ? 0u : (c | (x < 0.0f ? 8u : 0u));
-  }
-};
-
 // NaN-propagating max of |x| (torch's amax propagates NaN).
 __host__ __device__ __forceinline__ float absmax_nan(float m, float x) {
   const float a = fabsf(x);
   return (a > m || a != a) ? a : m;
+}
+
+// (a, b) -> bf16x2 word with a in the low half (one cvt.rn.bf16x2.f32).
+__device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+// NaN-propagating max of three magnitudes (three-input max.NaN, sm_100).
+__device__ __forceinline__ float absmax3_nan(float a, float b, float c) {
+  float d;
+  asm("max.NaN.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(fabsf(a)), "f"(fabsf(b)), "f"(fabsf(c)));
+  return d;
+}
+
+// Eight fp32 values -> eight E2M1 codes (round to nearest even, saturating to
+// +-6), value j in nibble j, by the hardware e2m1x2 conversion.
+__device__ __forceinline__ uint32_t e2m1x8_rn(const float* q) {
+  uint32_t out;
+  asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b0, %2, %1;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b1, %4, %3;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b2, %6, %5;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b3, %8, %7;\n\t"
+      "mov.b32 %0, {b0, b1, b2, b3};\n\t}"
+      : "=r"(out)
+      : "f"(q[0]), "f"(q[1]), "f"(q[2]), "f"(q[3]), "f"(q[4]), "f"(q[5]), "f"(q[6]), "f"(q[7]));
+  return out;
+}
+
+// NVFP4 encoding of bf16-valued x with global scale 1
+// (recavsr_infer/runtime/nvfp4.py:49-61): scale byte e4m3(max(amax/6, 2^-9))
+// and codes e2m1(fl(x / s)), bit for bit. nvfp4_codes8 codes 8 values for a
+// finite scale s; nvfp4_encode16 does a whole 16-element block.
+//   The quotient: q = x * r with r ~ 1/s (MUFU reciprocal), refined once by the
+//   exact residual, q' = q + (x - q*s) * r. The codes only depend on which side
+//   of each E2M1 rounding threshold t (0.25, 0.75, ..., 5) fl(x/s) falls, and on
+//   exact ties x = t*s. Away from ties x/s lies at least 2^-9 (relative) from
+//   every t (x has 8 significant bits, t*s at most 7), far beyond the ~2^-21
+//   error of q'; at a tie the residual is exact and q' rounds to t itself, where
+//   the conversion's round-to-nearest-even breaks the tie as the reference's
+//   strict / inclusive thresholds do. x = -0 gives q' = +0 (code 0, no sign,
+//   like the reference's z < 0 test); a NaN scale (NaN or huge amax) gives code
+//   0 for every element, as x / NaN does.
+__device__ __forceinline__ uint32_t nvfp4_codes8(const float* x, float s) {
+  float r;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(s));
+  const float2 r2 = make_float2(r, r), ns2 = make_float2(-s, -s);
+  float q[8];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float2 xv = make_float2(x[2 * j], x[2 * j + 1]);
+    const float2 q0 = __fmul2_rn(xv, r2);
+    const float2 rem = __ffma2_rn(q0, ns2, xv);
+    const float2 q1 = __ffma2_rn(rem, r2, q0);
+    q[2 * j] = q1.x;
+    q[2 * j + 1] = q1.y;
+  }
+  return e2m1x8_rn(q);
+}
+
+// Scale byte of a block from its (NaN-propagating) amax, global scale 1.
+__device__ __forceinline__ uint8_t nvfp4_scale_byte(float amax) {
+  float sc = __fdiv_rn(amax, 6.0f);
+  sc = sc < 0.001953125f ? 0.001953125f : sc;   // clamp_min(2^-9); NaN passes through
+  return e4m3_from_float(sc);
+}
+
+__device__ __forceinline__ void nvfp4_encode16(const float (&x)[16], uint8_t& sfb, uint32_t& lo,
+                                               uint32_t& hi) {
+  float m[5];
+#pragma unroll
+  for (int j = 0; j < 5; ++j) m[j] = absmax3_nan(x[3 * j], x[3 * j + 1], x[3 * j + 2]);
+  const float amax = absmax3_nan(absmax3_nan(m[0], m[1], m[2]), absmax3_nan(m[3], m[4], x[15]), 0.0f);
+  sfb = nvfp4_scale_byte(amax);
+  if (sfb == 0x7f) {   // NaN scale
+    lo = hi = 0;
+    return;
+  }
+  const float s = e4m3_to_float(sfb);
+  lo = nvfp4_codes8(x, s);
+  hi = nvfp4_codes8(x + 8, s);
 }
 
 // Offset of the scale byte for (row, k-block) in the 128x4 blocked layout

@@ -92,13 +92,30 @@ struct Smem {
   static constexpr int kAlloc = kTotal;
 };
 
-__device__ __forceinline__ float gelu_tanh(float x) {
-  // GELU(tanh) = 0.5 x (1 + tanh(u)), u = sqrt(2/pi) (x + 0.044715 x^3), evaluated
-  // as the identical x / (1 + exp(-2u)) with the fast exp / divide: a few fp32
-  // ulps from tanhf, invisible after the bf16 rounding in all but ~1e-3 of
-  // elements (where the bf16 result moves by one ulp).
-  const float u = 0.7978845608028654f * fmaf(0.044715f * x, x * x, x);
-  return __fdividef(x, 1.0f + __expf(-2.0f * u));
+// GELU(tanh) of two bf16-valued inputs: 0.5 x (1 + tanh(u)), u = sqrt(2/pi)
+// (x + 0.044715 x^3), evaluated as the identical x / (1 + 2^(x (k1 + k3 x^2)))
+// with k1 = -2 sqrt(2/pi) log2(e), k3 = 0.044715 k1, on packed fp32 pairs with
+// the MUFU exp2 / reciprocal: a few fp32 ulps from tanhf, invisible after the
+// bf16 rounding in all but ~1e-3 of elements (one bf16 ulp there). Large
+// negative x gives -0 (exp2 overflows to inf, its reciprocal is 0).
+__device__ __forceinline__ float2 gelu_tanh2(float2 x) {
+  constexpr float k1 = -2.0f * 0.7978845608028654f * 1.4426950408889634f;
+  constexpr float k3 = 0.044715f * k1;
+  const float2 t = __fmul2_rn(x, x);
+  const float2 z = __fmul2_rn(__ffma2_rn(t, make_float2(k3, k3), make_float2(k1, k1)), x);
+  float2 e, r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e.x) : "f"(z.x));
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e.y) : "f"(z.y));
+  const float2 d = __fadd2_rn(e, make_float2(1.0f, 1.0f));
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r.x) : "f"(d.x));
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r.y) : "f"(d.y));
+  return __fmul2_rn(x, r);
+}
+
+// bf16x2 word -> the two values as fp32 (low half first).
+__device__ __forceinline__ void unpack_bf16x2(uint32_t w, float& a, float& b) {
+  a = __uint_as_float(w << 16);
+  b = __uint_as_float(w & 0xffff0000u);
 }
 
 template <int KIND, int BN, int STAGES, int EPI>
@@ -324,22 +341,30 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
           if constexpr (EPI == EPI_GELU_NVF4) p.q_sf[rc::sf_offset(row, n0 >> 4, (p.N + 63) >> 6)] = 0;
           continue;
         }
-        float v[16], bias[16];
-        if (p.bias) {
-          const uint4* bp = reinterpret_cast<const uint4*>(p.bias + n0);
-          const uint4 b0 = __ldg(bp), b1 = __ldg(bp + 1);
-          const uint32_t bw[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+        // y = bf16(acc * alpha + bias), two columns per packed fp32 op.
+        float v[16];
+        uint32_t w[8];
+        {
+          uint32_t bw[8];
+          if (p.bias) {
+            const uint4* bp = reinterpret_cast<const uint4*>(p.bias + n0);
+            const uint4 b0 = __ldg(bp), b1 = __ldg(bp + 1);
+            bw[0] = b0.x; bw[1] = b0.y; bw[2] = b0.z; bw[3] = b0.w;
+            bw[4] = b1.x; bw[5] = b1.y; bw[6] = b1.z; bw[7] = b1.w;
+          }
+          const float2 alpha2 = make_float2(alpha, alpha);
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
-            bias[2 * j] = __uint_as_float(bw[j] << 16);
-            bias[2 * j + 1] = __uint_as_float(bw[j] & 0xffff0000u);
+            float2 x = __fmul2_rn(make_float2(__uint_as_float(acc[cc + 2 * j]), __uint_as_float(acc[cc + 2 * j + 1])),
+                                  alpha2);
+            if (p.bias) {
+              float2 b;
+              unpack_bf16x2(bw[j], b.x, b.y);
+              x = __fadd2_rn(x, b);
+            }
+            w[j] = rc::pack_bf16x2(x.x, x.y);
+            unpack_bf16x2(w[j], v[2 * j], v[2 * j + 1]);
           }
-        }
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          float x = __fmul_rn(__uint_as_float(acc[cc + j]), alpha);
-          if (p.bias) x = __fadd_rn(x, bias[j]);
-          v[j] = rc::bf16_to_float(rc::bf16_bits(x));
         }
         if constexpr (EPI == EPI_GATED_RESIDUAL || EPI == EPI_RESIDUAL) {
           __nv_bfloat16* hp = p.out + (size_t)row * p.ldo + n0;
@@ -356,31 +381,34 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
             }
           }
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const float h = __uint_as_float((j & 1) ? (hw[j >> 1] & 0xffff0000u) : (hw[j >> 1] << 16));
-            const float add = (EPI == EPI_GATED_RESIDUAL) ? __fmul_rn(v[j], gt[j]) : v[j];
-            v[j] = __fadd_rn(h, add);
+          for (int j = 0; j < 8; ++j) {
+            float2 h;
+            unpack_bf16x2(hw[j], h.x, h.y);
+            float2 add = make_float2(v[2 * j], v[2 * j + 1]);
+            if constexpr (EPI == EPI_GATED_RESIDUAL) add = __fmul2_rn(add, make_float2(gt[2 * j], gt[2 * j + 1]));
+            const float2 o = __fadd2_rn(h, add);
+            w[j] = rc::pack_bf16x2(o.x, o.y);
           }
         }
         if constexpr (EPI == EPI_GELU_NVF4) {
 #pragma unroll
-          for (int j = 0; j < 16; ++j) v[j] = rc::bf16_to_float(rc::bf16_bits(gelu_tanh(v[j])));
-          float amax = 0.f;
-#pragma unroll
-          for (int j = 0; j < 16; ++j) amax = rc::absmax_nan(amax, v[j]);
-          float sc = __fmul_rn(__fdiv_rn(amax, 6.0f), p.q_g);
-          sc = sc < 0.001953125f ? 0.001953125f : sc;
-          const uint8_t sfb = rc::e4m3_from_float(sc);
-          const float sd = rc::e4m3_to_float(sfb);
+          for (int j = 0; j < 8; ++j) {
+            const float2 g = gelu_tanh2(make_float2(v[2 * j], v[2 * j + 1]));
+            w[j] = rc::pack_bf16x2(g.x, g.y);
+            unpack_bf16x2(w[j], v[2 * j], v[2 * j + 1]);
+          }
+          uint8_t sfb;
           uint32_t lo = 0, hi = 0;
           if (p.q_g == 1.0f) {
-            const rc::E2m1Bounds bd(sd);
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              lo |= bd.code(v[j]) << (4 * j);
-              hi |= bd.code(v[8 + j]) << (4 * j);
-            }
+            rc::nvfp4_encode16(v, sfb, lo, hi);
           } else {
+            float amax = 0.f;
+#pragma unroll
+            for (int j = 0; j < 16; ++j) amax = rc::absmax_nan(amax, v[j]);
+            float sc = __fmul_rn(__fdiv_rn(amax, 6.0f), p.q_g);
+            sc = sc < 0.001953125f ? 0.001953125f : sc;
+            sfb = rc::e4m3_from_float(sc);
+            const float sd = rc::e4m3_to_float(sfb);
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
               const uint32_t code = rc::e2m1_code(__fdiv_rn(__fmul_rn(v[j], p.q_g), sd));
@@ -392,10 +420,6 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
           p.q_sf[rc::sf_offset(row, n0 >> 4, (p.N + 63) >> 6)] = sfb;
           if (!p.out) continue;
         }
-        uint32_t w[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j)
-          w[j] = (uint32_t)rc::bf16_bits(v[2 * j]) | ((uint32_t)rc::bf16_bits(v[2 * j + 1]) << 16);
         uint4* dst = reinterpret_cast<uint4*>(p.out + (size_t)row * p.ldo + n0);
         dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
         dst[1] = make_uint4(w[4], w[5], w[6], w[7]);

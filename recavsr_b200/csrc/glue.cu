@@ -61,16 +61,16 @@ __device__ __forceinline__ uint32_t quant8_pair(const float (&f)[8], float g, ui
 #pragma unroll
   for (int j = 0; j < 8; ++j) amax = rc::absmax_nan(amax, f[j]);
   amax = rc::absmax_nan(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+  if (g == 1.0f) {
+    sfb = rc::nvfp4_scale_byte(amax);
+    return sfb == 0x7f ? 0u : rc::nvfp4_codes8(f, rc::e4m3_to_float(sfb));
+  }
   float sc = __fmul_rn(__fdiv_rn(amax, 6.0f), g);
   sc = sc < 0.001953125f ? 0.001953125f : sc;
   sfb = rc::e4m3_from_float(sc);
   const float sd = rc::e4m3_to_float(sfb);
   uint32_t w = 0;
-  if (g == 1.0f) {
-    const rc::E2m1Bounds bd(sd);
-#pragma unroll
-    for (int j = 0; j < 8; ++j) w |= bd.code(f[j]) << (4 * j);
-  } else {
+  {
 #pragma unroll
     for (int j = 0; j < 8; ++j) w |= rc::e2m1_code(__fdiv_rn(__fmul_rn(f[j], g), sd)) << (4 * j);
   }

@@ -39,23 +39,17 @@ nvfp4_quantize_kernel(const __nv_bfloat16* __restrict__ x, int M, int K, long lo
       f[2 * j] = __uint_as_float(w[j] << 16);
       f[2 * j + 1] = __uint_as_float(w[j] & 0xffff0000u);
     }
-    float amax = 0.0f;
-#pragma unroll
-    for (int j = 0; j < 16; ++j) amax = rc::absmax_nan(amax, f[j]);
-    float sc = __fmul_rn(__fdiv_rn(amax, 6.0f), g);
-    sc = sc < 0.001953125f ? 0.001953125f : sc;   // clamp_min(2^-9); NaN passes through
-    sf = rc::e4m3_from_float(sc);
-    const float sd = rc::e4m3_to_float(sf);
     uint32_t lo = 0, hi = 0;
     if (g == 1.0f) {
-      const rc::E2m1Bounds bd(sd);
-#pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const uint32_t c = bd.code(f[j]);
-        if (j < 8) lo |= c << (4 * j);
-        else hi |= c << (4 * (j - 8));
-      }
+      rc::nvfp4_encode16(f, sf, lo, hi);
     } else {
+      float amax = 0.0f;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) amax = rc::absmax_nan(amax, f[j]);
+      float sc = __fmul_rn(__fdiv_rn(amax, 6.0f), g);
+      sc = sc < 0.001953125f ? 0.001953125f : sc;   // clamp_min(2^-9); NaN passes through
+      sf = rc::e4m3_from_float(sc);
+      const float sd = rc::e4m3_to_float(sf);
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
         const uint32_t c = rc::e2m1_code(__fdiv_rn(__fmul_rn(f[j], g), sd));

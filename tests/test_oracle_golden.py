@@ -145,22 +145,28 @@ def test_block_forward_matches_reference(golden, tag):
     assert np.abs(h - ref_h).max() < 0.15 * np.abs(ref_h).max()
 
 
-def test_division_free_e2m1_ladder_is_exact():
-    """The kernels code NVFP4 without dividing: |x| compared against t*s for the
-    seven E2M1 thresholds t. For every bf16 x and every positive E4M3 scale s
-    this equals the reference ladder applied to fl32(x / s) (exhaustive)."""
+def test_refined_quotient_e2m1_codes_are_exact():
+    """The kernels code NVFP4 (global scale 1) as e2m1_rn(q1) with q0 = x*r,
+    q1 = fma(fma(-q0, s, x), r, q0) and r the hardware's approximate 1/s; the
+    e2m1 conversion rounds to nearest even. For every bf16 x and every E4M3
+    scale s with |x| <= 16 s (a block's scale is e4m3(amax / 6), so its
+    elements satisfy |x| / s <= 6.4), and r up to 64 ulps away from 1/s,
+    this equals the reference ladder applied to fl32(x / s) (exhaustive; the
+    hardware conversion itself is checked exhaustively on the GPU by
+    test_gpu_quant)."""
     from oracle.numerics import bf16_from_bits, e4m3_decode
     x = bf16_from_bits(np.arange(65536, dtype=np.uint32).astype(np.uint16))
-    x = x[~np.isnan(x)]
-    scales = e4m3_decode(np.arange(1, 127, dtype=np.uint8))
-    thr = ((0.25, False), (0.75, True), (1.25, False), (1.75, True), (2.5, False), (3.5, True), (5.0, False))
-    ax = np.abs(x)
-    for s in scales.astype(np.float32):
-        with np.errstate(over="ignore", invalid="ignore"):
-            ref = nvfp4.e2m1_codes((x / s).astype(np.float32))
-        code = np.zeros(x.shape, np.uint8)
-        for t, inclusive in thr:
-            b = np.float32(t) * s          # exact: <= 7 significant bits
-            code += (ax >= b) if inclusive else (ax > b)
-        code |= (x < 0).astype(np.uint8) * 8
-        np.testing.assert_array_equal(code, ref)
+    x = x[np.isfinite(x)]
+    scales = e4m3_decode(np.arange(1, 127, dtype=np.uint8)).astype(np.float32)
+    for s in scales:
+        xs = x[np.abs(x) <= np.float32(16) * s]
+        ref = nvfp4.e2m1_codes((xs / s).astype(np.float32))
+        r0 = np.float32(1.0) / s
+        ulp = np.spacing(r0)
+        for r in r0 + ulp * np.array([-64, -1, 0, 1, 64], np.float32):   # MUFU rcp is within 1 ulp
+            q0 = (xs * r).astype(np.float32)
+            rem = (xs.astype(np.float64) - q0.astype(np.float64) * np.float64(s)).astype(np.float32)  # exact
+            q1 = (rem.astype(np.float64) * np.float64(r) + q0.astype(np.float64)).astype(np.float32)
+            # e2m1 round-to-nearest-even (the ladder is RNE), sign from the sign bit
+            code = nvfp4.e2m1_codes(np.abs(q1)) | (np.signbit(q1).astype(np.uint8) * 8)
+            np.testing.assert_array_equal(code, ref)
