@@ -22,7 +22,8 @@
 //  2. attention: one CTA per (128-query tile, head), operands staged by TMA.
 //     Warp 0 = producer: the raw Q tile once, then K tiles (workspace) and V
 //     tiles (read in place from the cache slot / current frame), 128 keys each,
-//     double-buffered.
+//     in two 3-stage rings; K runs two tiles ahead of V, and a K stage is
+//     released as soon as its Q K^T finishes.
 //     Warps 2-9 = softmax: first they rotate Q (temporal RoPE, fp32 math) and
 //     store it into tensor memory; then, per key tile, two warps per TMEM lane
 //     quadrant (64 keys each) load S, apply the window mask, keep a lazily
@@ -73,11 +74,12 @@ struct AttnParams {
 
 struct SmemLayout {
   static constexpr int kChunk = 128 * 128;           // 128 rows x 128 bytes
+  static constexpr int kStages = 3;                  // K ring and V ring depth
   static constexpr int offQ = 0;                     // 2 chunks (raw Q, read once)
-  static constexpr int offK = offQ + 2 * kChunk;     // 2 stages x 2 chunks
-  static constexpr int offV = offK + 4 * kChunk;     // 2 stages x 2 chunks
-  static constexpr int offBar = offV + 4 * kChunk;
-  static constexpr int kBars = 16;
+  static constexpr int offK = offQ + 2 * kChunk;     // kStages x 2 chunks
+  static constexpr int offV = offK + 2 * kStages * kChunk;
+  static constexpr int offBar = offV + 2 * kStages * kChunk;
+  static constexpr int kBars = 24;
   static constexpr int offMisc = offBar + kBars * 8;
   static constexpr int offRed = offMisc + 16 + kMaxPlanes * 4;   // [2][2][128] floats
   static constexpr int kTotal = offRed + 2 * 2 * 128 * 4;
@@ -99,19 +101,46 @@ struct TileIter {
       ry0 = ry1 = rx0 = rx1 = 0;
     }
   }
-  __device__ int tiles_per_plane() const {
-    if (!p.local) return (p.T + kBN - 1) / kBN;
-    return ((ry1 - ry0 + kLocalKH - 1) / kLocalKH) * ((rx1 - rx0 + kLocalKW - 1) / kLocalKW);
+  // Tiles per plane: dense = nx runs of 128 tokens; local = nx x ny boxes.
+  __device__ int tiles_x() const {
+    return !p.local ? (p.T + kBN - 1) / kBN : (rx1 - rx0 + kLocalKW - 1) / kLocalKW;
   }
-  // tile j within a plane -> first token (dense) or box origin (ky0, kx0) (local)
-  __device__ void tile_origin(int j, int& a, int& b) const {
-    if (!p.local) {
-      a = j * kBN;
+  __device__ int tiles_y() const { return !p.local ? 1 : (ry1 - ry0 + kLocalKH - 1) / kLocalKH; }
+};
+
+// Position of a key tile in the enumeration (visible-plane index, box column,
+// box row), advanced incrementally; origin() gives the first token (dense) or
+// the box origin (ky0, kx0) (local).
+struct TileCursor {
+  int plane = 0, tx = 0, ty = 0;
+  __device__ void advance(int nx, int ny) {
+    if (++tx == nx) {
+      tx = 0;
+      if (++ty == ny) {
+        ty = 0;
+        ++plane;
+      }
+    }
+  }
+  __device__ void origin(const TileIter& it, int& a, int& b) const {
+    if (!it.p.local) {
+      a = tx * kBN;
       b = 0;
     } else {
-      const int nx = (rx1 - rx0 + kLocalKW - 1) / kLocalKW;
-      a = ry0 + (j / nx) * kLocalKH;
-      b = rx0 + (j % nx) * kLocalKW;
+      a = it.ry0 + ty * kLocalKH;
+      b = it.rx0 + tx * kLocalKW;
+    }
+  }
+};
+
+// Position in a ring of kStages buffers: stage index and phase parity.
+struct Ring {
+  int stage = 0;
+  uint32_t phase = 0;
+  __device__ void advance(int n) {
+    if (++stage == n) {
+      stage = 0;
+      phase ^= 1u;
     }
   }
 };
@@ -155,13 +184,16 @@ attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::offBar);
   uint64_t* q_full = bars + 0;     // raw Q landed in shared memory
   uint64_t* q_tmem = bars + 1;     // rotated Q stored in tensor memory (256 arrivals)
-  uint64_t* kv_full = bars + 2;    // [2]
-  uint64_t* kv_empty = bars + 4;   // [2]
-  uint64_t* s_full = bars + 6;     // S = Q K^T of the current tile finished
-  uint64_t* s_free = bars + 7;     // S loaded by all softmax threads (256 arrivals)
-  uint64_t* p_full = bars + 8;     // [2] P buffer written (256 arrivals)
-  uint64_t* o_done = bars + 10;    // [2] P.V reading P buffer b finished
-  uint64_t* done = bars + 12;
+  constexpr int kS = L::kStages;
+  uint64_t* k_full = bars + 2;             // [kS] K tile landed
+  uint64_t* k_empty = k_full + kS;         // [kS] Q K^T reading the K stage finished
+  uint64_t* v_full = k_empty + kS;         // [kS] V tile landed
+  uint64_t* v_empty = v_full + kS;         // [kS] P.V reading the V stage finished
+  uint64_t* s_full = v_empty + kS;         // S = Q K^T of the current tile finished
+  uint64_t* s_free = s_full + 1;           // S loaded by all softmax threads (256 arrivals)
+  uint64_t* p_full = s_free + 1;           // [2] P buffer written (256 arrivals)
+  uint64_t* o_done = p_full + 2;           // [2] P.V reading P buffer b finished
+  uint64_t* done = o_done + 2;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::offMisc);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::offMisc + 4);
   int* s_nplanes = reinterpret_cast<int*>(smem + L::offMisc + 8);
@@ -186,9 +218,13 @@ attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
   if (threadIdx.x == 0) {
     sm100::mbar_init(q_full, 1);
     sm100::mbar_init(q_tmem, 256);
+    for (int s2 = 0; s2 < kS; ++s2) {
+      sm100::mbar_init(&k_full[s2], 1);
+      sm100::mbar_init(&k_empty[s2], 1);
+      sm100::mbar_init(&v_full[s2], 1);
+      sm100::mbar_init(&v_empty[s2], 1);
+    }
     for (int s2 = 0; s2 < 2; ++s2) {
-      sm100::mbar_init(&kv_full[s2], 1);
-      sm100::mbar_init(&kv_empty[s2], 1);
       sm100::mbar_init(&p_full[s2], 256);
       sm100::mbar_init(&o_done[s2], 1);
     }
@@ -215,8 +251,8 @@ attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
   const uint32_t t_s = tmem + kTmS, t_o = tmem + kTmO, t_q = tmem + kTmQ;
   const int nplanes = *s_nplanes;
   TileIter it(p, qy0, qx0);
-  const int tpp = it.tiles_per_plane();
-  const int n_tiles = nplanes * tpp;
+  const int nx = it.tiles_x(), ny = it.tiles_y();
+  const int n_tiles = nplanes * nx * ny;
 
   auto fail = [&](unsigned int site) {
     if (!*abort_flag) rc::device_fail(kKernAttention, site);
@@ -237,32 +273,55 @@ attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
         if (!p.local) sm100::tma_load_3d(sq + c * L::kChunk, &tm_q, q_full, c * 64, head, q_row0);
         else sm100::tma_load_5d(sq + c * L::kChunk, &tm_q, q_full, c * 64, head, qx0, qy0, qf0);
       }
-      int issued = 0;
-      for (int i = 0; i < n_tiles; ++i) {
-        const int st = i & 1;
-        if (!wait(&kv_empty[st], ((i >> 1) & 1) ^ 1, 1)) break;
-        const int plane = s_planes[i / tpp];
+      // K runs two tiles ahead of V: Q K^T of a tile comes one pipeline step
+      // before its P.V, and a K stage frees up as soon as its Q K^T finishes.
+      TileCursor kc, vc;
+      Ring kr, vr;
+      int nk = 0, nv = 0;
+      bool ok = true;
+      auto load = [&](bool is_k, const TileCursor& c, const Ring& r) -> bool {
+        uint64_t* full = is_k ? &k_full[r.stage] : &v_full[r.stage];
+        if (!wait(is_k ? &k_empty[r.stage] : &v_empty[r.stage], r.phase ^ 1u, is_k ? 1 : 11)) return false;
+        const int plane = s_planes[c.plane];
         int a, b;
-        it.tile_origin(i % tpp, a, b);
-        uint8_t* sk = smem + L::offK + st * 2 * L::kChunk;
-        uint8_t* sv = smem + L::offV + st * 2 * L::kChunk;
-        sm100::mbar_arrive_expect_tx(&kv_full[st], 4 * L::kChunk);
-        const bool past = plane < p.CAP;
-        const int vplane = past ? p.slots[plane] : plane - p.CAP;
-        const CUtensorMap* vmap = past ? &tm_pv : &tm_cv;
-        for (int c = 0; c < 2; ++c) {
-          if (!p.local) {
-            sm100::tma_load_4d(sk + c * L::kChunk, &tm_k, &kv_full[st], c * 64, head, a, plane);
-            sm100::tma_load_4d(sv + c * L::kChunk, vmap, &kv_full[st], c * 64, head, a, vplane);
-          } else {
-            sm100::tma_load_5d(sk + c * L::kChunk, &tm_k, &kv_full[st], c * 64, head, b, a, plane);
-            sm100::tma_load_5d(sv + c * L::kChunk, vmap, &kv_full[st], c * 64, head, b, a, vplane);
-          }
+        c.origin(it, a, b);
+        uint8_t* dst = smem + (is_k ? L::offK : L::offV) + r.stage * 2 * L::kChunk;
+        const CUtensorMap* map;
+        int src_plane;
+        if (is_k) {
+          map = &tm_k;
+          src_plane = plane;
+        } else if (plane < p.CAP) {
+          map = &tm_pv;
+          src_plane = p.slots[plane];
+        } else {
+          map = &tm_cv;
+          src_plane = plane - p.CAP;
         }
-        ++issued;
+        sm100::mbar_arrive_expect_tx(full, 2 * L::kChunk);
+        for (int ch = 0; ch < 2; ++ch) {
+          if (!p.local) sm100::tma_load_4d(dst + ch * L::kChunk, map, full, ch * 64, head, a, src_plane);
+          else sm100::tma_load_5d(dst + ch * L::kChunk, map, full, ch * 64, head, b, a, src_plane);
+        }
+        return true;
+      };
+      for (int i = 0; i < n_tiles + 2 && ok; ++i) {
+        if (i < n_tiles) {
+          if (!(ok = load(true, kc, kr))) break;
+          kc.advance(nx, ny);
+          kr.advance(kS);
+          ++nk;
+        }
+        if (i >= 2) {
+          if (!(ok = load(false, vc, vr))) break;
+          vc.advance(nx, ny);
+          vr.advance(kS);
+          ++nv;
+        }
       }
-      // Drain the (at most two) loads still in flight before teardown.
-      for (int i = max(0, issued - 2); i < issued; ++i) sm100::mbar_wait(&kv_full[i & 1], (i >> 1) & 1);
+      // Drain the loads still in flight (at most kS per ring) before teardown.
+      for (int j = max(0, nk - kS); j < nk; ++j) sm100::mbar_wait(&k_full[j % kS], (j / kS) & 1);
+      for (int j = max(0, nv - kS); j < nv; ++j) sm100::mbar_wait(&v_full[j % kS], (j / kS) & 1);
       sm100::mbar_wait(q_full, 0);
     }
   } else if (warp == 1) {
@@ -272,29 +331,33 @@ attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       constexpr uint32_t idesc_pv = sm100::idesc_bf16(kBM, kD, 0, 1);
       bool ok = wait(q_tmem, 0, 2);
       sm100::tc_fence_after();
+      Ring kr, vr;
       auto issue_pv = [&](int j) -> bool {
+        if (!wait(&v_full[vr.stage], vr.phase, 12)) return false;
         if (!wait(&p_full[j & 1], (j >> 1) & 1, 3)) return false;
         sm100::tc_fence_after();
         const uint32_t t_p = tmem + kTmP + (uint32_t)(j & 1) * 64;
-        const uint32_t sv = sm100::smem_u32(smem + L::offV + (j & 1) * 2 * L::kChunk);
+        const uint32_t sv = sm100::smem_u32(smem + L::offV + vr.stage * 2 * L::kChunk);
         for (int k = 0; k < kBN / 16; ++k)
           sm100::mma_f16_ts(t_o, t_p + 8 * k, sm100::desc_mnmajor_sw128(sv + k * 16 * 128, L::kChunk),
                             idesc_pv, (j > 0 || k > 0) ? 1u : 0u);
-        sm100::tc_commit(&kv_empty[j & 1]);
+        sm100::tc_commit(&v_empty[vr.stage]);
         sm100::tc_commit(&o_done[j & 1]);
+        vr.advance(kS);
         return true;
       };
       for (int i = 0; i < n_tiles && ok; ++i) {
-        const int st = i & 1;
-        if (!wait(&kv_full[st], (i >> 1) & 1, 4)) { ok = false; break; }
+        if (!wait(&k_full[kr.stage], kr.phase, 4)) { ok = false; break; }
         if (!wait(s_free, (i & 1) ^ 1, 5)) { ok = false; break; }   // S(i-1) is in registers
         sm100::tc_fence_after();
-        const uint32_t sk = sm100::smem_u32(smem + L::offK + st * 2 * L::kChunk);
+        const uint32_t sk = sm100::smem_u32(smem + L::offK + kr.stage * 2 * L::kChunk);
         for (int k = 0; k < kD / 16; ++k)
           sm100::mma_f16_ts(t_s, t_q + 8 * k,
                             sm100::desc_kmajor_sw128(sk + (k >> 2) * L::kChunk + (k & 3) * 32),
                             idesc_qk, k > 0 ? 1u : 0u);
         sm100::tc_commit(s_full);
+        sm100::tc_commit(&k_empty[kr.stage]);
+        kr.advance(kS);
         if (i > 0 && !issue_pv(i - 1)) { ok = false; break; }
       }
       if (ok && n_tiles > 0) issue_pv(n_tiles - 1);
@@ -358,12 +421,13 @@ attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
     const int left = min(max(qx - p.ww / 2, 0), p.W - p.ww);
     const float scale = p.scale_log2;
     float m_used = -INFINITY, l = 0.f;
-    for (int i = 0; i < n_tiles && ok; ++i) {
+    TileCursor cur;
+    for (int i = 0; i < n_tiles && ok; ++i, cur.advance(nx, ny)) {
       const int st = i & 1;
       if (!__all_sync(0xffffffffu, wait(s_full, i & 1, 6))) { ok = false; break; }
       sm100::tc_fence_after();
       int a, b;
-      it.tile_origin(i % tpp, a, b);
+      cur.origin(it, a, b);
       const bool full_tile = !p.local && a + kBN <= p.T;
       float v[64];
       {
