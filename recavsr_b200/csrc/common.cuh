@@ -193,11 +193,40 @@ __device__ __forceinline__ uint32_t nvfp4_codes8(const float* x, float s) {
   return e2m1x8_rn(q);
 }
 
+// fl32(a / 6) for a bf16-valued a >= 0 without a division: q = a * fl(1/6),
+// refined once by the exact residual. Bit-identical to IEEE division for every
+// finite non-negative bf16 a (checked exhaustively by
+// tests/test_oracle_golden.py::test_div6_is_exact_for_bf16); NaN and inf give NaN.
+__device__ __forceinline__ float div6_bf16(float a) {
+  constexpr float r6 = 1.0f / 6.0f;
+  const float q = a * r6;
+  return fmaf(fmaf(-q, 6.0f, a), r6, q);
+}
+
+// E4M3 code of v >= 0 (or NaN), round to nearest even, subnormals kept; as
+// e4m3_from_float: above 464 (the tie between 448 and the next step, which is
+// the NaN code) and for NaN the result is the NaN code 0x7f. The hardware
+// conversion saturates instead, so it only sees v <= 464.
+__device__ __forceinline__ uint8_t e4m3_rn_nonneg(float v) {
+  if (!(v <= 464.0f)) return 0x7f;
+  uint16_t r;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(0.0f), "f"(v));
+  return (uint8_t)(r & 0xff);
+}
+
+// Value of a non-negative, non-NaN E4M3 code: its 7 magnitude bits placed at
+// bit 20 of an fp32 read as 2^(E-127) (1 + M/8) (or the fp32 subnormal M 2^-129
+// when E = 0), times 2^120 -> 2^(E-7) (1 + M/8) (or M 2^-9). Needs fp32
+// subnormals kept (no flush-to-zero), which is the default.
+__device__ __forceinline__ float e4m3_nonneg_to_float(uint8_t c) {
+  return __uint_as_float((uint32_t)(c & 0x7f) << 20) * 0x1p120f;
+}
+
 // Scale byte of a block from its (NaN-propagating) amax, global scale 1.
 __device__ __forceinline__ uint8_t nvfp4_scale_byte(float amax) {
-  float sc = __fdiv_rn(amax, 6.0f);
+  float sc = div6_bf16(amax);
   sc = sc < 0.001953125f ? 0.001953125f : sc;   // clamp_min(2^-9); NaN passes through
-  return e4m3_from_float(sc);
+  return e4m3_rn_nonneg(sc);
 }
 
 __device__ __forceinline__ void nvfp4_encode16(const float (&x)[16], uint8_t& sfb, uint32_t& lo,
@@ -211,7 +240,7 @@ __device__ __forceinline__ void nvfp4_encode16(const float (&x)[16], uint8_t& sf
     lo = hi = 0;
     return;
   }
-  const float s = e4m3_to_float(sfb);
+  const float s = e4m3_nonneg_to_float(sfb);
   lo = nvfp4_codes8(x, s);
   hi = nvfp4_codes8(x + 8, s);
 }

@@ -24,6 +24,19 @@ __device__ __forceinline__ void unpack8(const uint4& v, float (&f)[8]) {
     f[2 * j + 1] = __uint_as_float(w[j] & 0xffff0000u);
   }
 }
+// Same as unpack8, but opaque to common-subexpression elimination: a row
+// kernel re-expands its packed bf16 registers in each pass instead of keeping
+// every expanded fp32 value alive across passes (which would spill).
+__device__ __forceinline__ void unpack8_fresh(const uint4& v, float (&f)[8]) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    uint32_t lo, hi;
+    asm volatile("shl.b32 %0, %2, 16;\n\tand.b32 %1, %2, 0xffff0000;" : "=r"(lo), "=r"(hi) : "r"(w[j]));
+    f[2 * j] = __uint_as_float(lo);
+    f[2 * j + 1] = __uint_as_float(hi);
+  }
+}
 __device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
   uint32_t w[4];
 #pragma unroll
@@ -53,17 +66,22 @@ __device__ __forceinline__ void loadf8(const float* p, float (&f)[8]) {
   f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w; f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
 }
 
+__device__ __forceinline__ void loadf8_plain(const float* p, float (&f)[8]) {
+  const float4* q = reinterpret_cast<const float4*>(p);
+  const float4 a = q[0], b = q[1];
+  f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w; f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+}
+
 // NVFP4 encode of one 16-element block split over a lane pair (lanes 2b and
 // 2b+1 hold elements 0-7 and 8-15). Returns this lane's 4 code bytes; both
 // lanes get the block's scale byte.
 __device__ __forceinline__ uint32_t quant8_pair(const float (&f)[8], float g, uint8_t& sfb) {
-  float amax = 0.f;
-#pragma unroll
-  for (int j = 0; j < 8; ++j) amax = rc::absmax_nan(amax, f[j]);
-  amax = rc::absmax_nan(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+  float amax = rc::absmax3_nan(rc::absmax3_nan(f[0], f[1], f[2]), rc::absmax3_nan(f[3], f[4], f[5]),
+                               rc::absmax3_nan(f[6], f[7], 0.0f));
+  amax = rc::absmax3_nan(amax, __shfl_xor_sync(0xffffffffu, amax, 1), 0.0f);
   if (g == 1.0f) {
     sfb = rc::nvfp4_scale_byte(amax);
-    return sfb == 0x7f ? 0u : rc::nvfp4_codes8(f, rc::e4m3_to_float(sfb));
+    return sfb == 0x7f ? 0u : rc::nvfp4_codes8(f, rc::e4m3_nonneg_to_float(sfb));
   }
   float sc = __fmul_rn(__fdiv_rn(amax, 6.0f), g);
   sc = sc < 0.001953125f ? 0.001953125f : sc;
@@ -91,18 +109,21 @@ __device__ __forceinline__ void store_sf4_pairs(uint8_t* sf, int row, int kb, in
 
 // Row kernels: one CTA of kRowThreads threads per row; thread t owns the
 // 8-element chunks t, t + kRowThreads, ... (at most kRowChunks of them, so
-// N <= kRowThreads * 8 * kRowChunks = 4096). Every thread issues all of its
-// chunk loads before the first reduction; the small CTA keeps many rows
-// resident per SM to hide the load -> reduce -> store latency of each row.
+// N <= 4096) and issues all of its loads before the first reduction. The
+// straight-line code per row is short (a few chunks per thread), so thousands
+// of small CTAs stay resident and hide the load -> reduce -> store latency.
+// Lanes (2m, 2m+1) of a warp hold one 16-element quantization block and lanes
+// 8a..8a+7 one scale-atom column.
 constexpr int kRowThreads = 128;
 constexpr int kRowChunks = 4;
 
 __device__ __forceinline__ float row_sum(float v, float* red) {
   v = warp_sum(v);
-  __syncthreads();
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
   __syncthreads();
-  return red[0] + red[1] + red[2] + red[3];
+  const float t = (red[0] + red[1]) + (red[2] + red[3]);
+  __syncthreads();   // red is reused by the next reduction
+  return t;
 }
 
 __global__ void __launch_bounds__(kRowThreads, 6) ln_modulate_kernel(LnArgs a) {
@@ -131,7 +152,7 @@ __global__ void __launch_bounds__(kRowThreads, 6) ln_modulate_kernel(LnArgs a) {
   for (int i = 0; i < kRowChunks; ++i) {
     if (t + i * kRowThreads < nch) {
       float f[8];
-      unpack8(raw[i], f);
+      unpack8_fresh(raw[i], f);
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         const float d = f[j] - mean;
@@ -141,6 +162,8 @@ __global__ void __launch_bounds__(kRowThreads, 6) ln_modulate_kernel(LnArgs a) {
   }
   const float rstd = rsqrtf(__fdiv_rn(row_sum(m2, red), (float)a.N) + a.eps);
   const int katoms = ((a.N >> 4) + 3) >> 2;
+  const float2 nmean = make_float2(-mean, -mean), rstd2 = make_float2(rstd, rstd);
+  const float2 one2 = make_float2(1.0f, 1.0f);
 #pragma unroll
   for (int i = 0; i < kRowChunks; ++i) {
     if (i * kRowThreads >= nch) break;                 // CTA-uniform
@@ -148,23 +171,28 @@ __global__ void __launch_bounds__(kRowThreads, 6) ln_modulate_kernel(LnArgs a) {
     const bool live = c < nch;
     const int n0 = c * 8;
     float f[8];
-    unpack8(raw[i], f);
+    unpack8_fresh(raw[i], f);
     if (live) {
       float w[8], b[8], sh[8], sc[8];
       if (a.weight) unpack8(__ldg(reinterpret_cast<const uint4*>(a.weight + n0)), w);
       if (a.bias) unpack8(__ldg(reinterpret_cast<const uint4*>(a.bias + n0)), b);
       if (a.scale) loadf8(a.scale + n0, sc);
       if (a.shift) loadf8(a.shift + n0, sh);
+      // fl(fl(x - mean) * rstd), then each affine / modulation step rounded
+      // separately, two columns per packed fp32 op; bf16 at the end.
+      uint32_t h[4];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        float y = __fmul_rn(f[j] - mean, rstd);
-        if (a.weight) y = __fmul_rn(y, w[j]);
-        if (a.bias) y = __fadd_rn(y, b[j]);
-        if (a.scale) y = __fmul_rn(y, __fadd_rn(1.0f, sc[j]));
-        if (a.shift) y = __fadd_rn(y, sh[j]);
-        f[j] = rc::bf16_to_float(rc::bf16_bits(y));
+      for (int j = 0; j < 4; ++j) {
+        float2 y = __fmul2_rn(__fadd2_rn(make_float2(f[2 * j], f[2 * j + 1]), nmean), rstd2);
+        if (a.weight) y = __fmul2_rn(y, make_float2(w[2 * j], w[2 * j + 1]));
+        if (a.bias) y = __fadd2_rn(y, make_float2(b[2 * j], b[2 * j + 1]));
+        if (a.scale) y = __fmul2_rn(y, __fadd2_rn(one2, make_float2(sc[2 * j], sc[2 * j + 1])));
+        if (a.shift) y = __fadd2_rn(y, make_float2(sh[2 * j], sh[2 * j + 1]));
+        h[j] = rc::pack_bf16x2(y.x, y.y);
+        f[2 * j] = __uint_as_float(h[j] << 16);
+        f[2 * j + 1] = __uint_as_float(h[j] & 0xffff0000u);
       }
-      if (a.out) *reinterpret_cast<uint4*>(a.out + (size_t)row * a.ldo + n0) = pack8(f);
+      if (a.out) *reinterpret_cast<uint4*>(a.out + (size_t)row * a.ldo + n0) = make_uint4(h[0], h[1], h[2], h[3]);
     }
     if (a.codes) {
       uint8_t sfb;
@@ -198,7 +226,9 @@ struct RmsArgs {
 };
 
 // One CTA of kRowThreads threads per (row, tensor); thread t owns chunks
-// t, t + kRowThreads, ... of 8 elements.
+// t, t + kRowThreads, ... of 8 elements. When 8 * kRowThreads is a whole
+// number of heads, all of a thread's chunks sit at the same offset within a
+// head and its rotary coefficients are loaded once.
 __global__ void __launch_bounds__(kRowThreads, 8) rmsnorm_rope_kernel(RmsArgs a) {
   __shared__ float red[4];
   const int row = blockIdx.x, t = threadIdx.x;
@@ -207,6 +237,7 @@ __global__ void __launch_bounds__(kRowThreads, 8) rmsnorm_rope_kernel(RmsArgs a)
   const long long ldx = second ? a.ldx[1] : a.ldx[0];
   __nv_bfloat16* op = second ? a.out[1] : a.out[0];
   const long long ldo = second ? a.ldo[1] : a.ldo[0];
+  const __nv_bfloat16* w = second ? a.w[1] : a.w[0];
   const int nch = a.N >> 3;
   uint4 raw[kRowChunks];
 #pragma unroll
@@ -215,7 +246,14 @@ __global__ void __launch_bounds__(kRowThreads, 8) rmsnorm_rope_kernel(RmsArgs a)
     raw[i] = c < nch ? __ldg(reinterpret_cast<const uint4*>(xp + (size_t)row * ldx) + c)
                      : make_uint4(0, 0, 0, 0);
   }
-  const __nv_bfloat16* w = second ? a.w[1] : a.w[0];
+  const int pos = row % a.span;
+  const bool same_dd = ((8 * kRowThreads) % a.d) == 0;
+  float cs[8], sn[8];
+  if (a.cos && same_dd) {
+    const int dd = (t * 8) % a.d;
+    loadf8(a.cos + (size_t)pos * a.d + dd, cs);
+    loadf8(a.sin + (size_t)pos * a.d + dd, sn);
+  }
   float r = 0.f;
   if (w) {
     float ss = 0.f;
@@ -228,25 +266,31 @@ __global__ void __launch_bounds__(kRowThreads, 8) rmsnorm_rope_kernel(RmsArgs a)
     }
     r = rsqrtf(__fdiv_rn(row_sum(ss, red), (float)a.N) + a.eps);
   }
-  const int pos = row % a.span;
 #pragma unroll
   for (int i = 0; i < kRowChunks; ++i) {
     const int c = t + i * kRowThreads;
     if (c >= nch) break;
     const int n0 = c * 8;
     float f[8];
-    unpack8(raw[i], f);
+    unpack8_fresh(raw[i], f);
     if (w) {
       float wf[8];
       unpack8(__ldg(reinterpret_cast<const uint4*>(w + n0)), wf);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) f[j] = rc::bf16_to_float(rc::bf16_bits(__fmul_rn(__fmul_rn(f[j], r), wf[j])));
+      for (int j = 0; j < 4; ++j) {
+        const float2 y = __fmul2_rn(__fmul2_rn(make_float2(f[2 * j], f[2 * j + 1]), make_float2(r, r)),
+                                    make_float2(wf[2 * j], wf[2 * j + 1]));
+        const uint32_t h = rc::pack_bf16x2(y.x, y.y);
+        f[2 * j] = __uint_as_float(h << 16);
+        f[2 * j + 1] = __uint_as_float(h & 0xffff0000u);
+      }
     }
     if (a.cos) {
-      const int dd = n0 % a.d;   // 8 | d: a chunk never straddles heads
-      float cs[8], sn[8];
-      loadf8(a.cos + (size_t)pos * a.d + dd, cs);
-      loadf8(a.sin + (size_t)pos * a.d + dd, sn);
+      if (!same_dd) {
+        const int dd = n0 % a.d;   // 8 | d: a chunk never straddles heads
+        loadf8(a.cos + (size_t)pos * a.d + dd, cs);
+        loadf8(a.sin + (size_t)pos * a.d + dd, sn);
+      }
 #pragma unroll
       for (int j = 0; j < 8; j += 2) {
         const float e = f[j], o = f[j + 1];
@@ -433,8 +477,7 @@ int rc_rmsnorm_rope(int n_tensors, const void* const* xs, const long long* ldx,
   a.d = d;
   a.span = span;
   if (M == 0) return RC_OK;
-  dim3 grid(M, n_tensors);
-  rmsnorm_rope_kernel<<<grid, kRowThreads, 0, stream>>>(a);
+  rmsnorm_rope_kernel<<<dim3(M, n_tensors), kRowThreads, 0, stream>>>(a);
   return rc::check_launch("rc_rmsnorm_rope");
 }
 

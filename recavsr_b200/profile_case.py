@@ -6,6 +6,7 @@
     python -m recavsr_b200.profile_case attention    # routed attention, 1760 queries, 4 past planes
     python -m recavsr_b200.profile_case quant        # NVFP4 quantizer 1760x3072
     python -m recavsr_b200.profile_case ln           # LayerNorm+AdaLN+NVFP4 1760x3072
+    python -m recavsr_b200.profile_case rms          # RMSNorm+spatial RoPE of q and k, 1760x3072 each
 
 Each case allocates fresh inputs (a few hundred MB at most), captures `--reps`
 launches in a CUDA graph, replays it and prints the mean CUDA-event time per
@@ -94,6 +95,23 @@ def _ln():
     return run, M * DIM * 2.5625, "GB/s"
 
 
+def _rms():
+    qkv = torch.randn(M, 3 * DIM, device="cuda").bfloat16()
+    wq, wk = torch.rand(DIM, device="cuda").bfloat16(), torch.rand(DIM, device="cuda").bfloat16()
+    q_rot, k_rot = (torch.empty(M, DIM, dtype=torch.bfloat16, device="cuda") for _ in range(2))
+    cos, sin = (torch.rand(H * W, HD, device="cuda") for _ in range(2))
+    lib = _lib.library()
+
+    def run():
+        _lib.check(lib.rc_rmsnorm_rope(2, (C.c_void_p * 2)(qkv.data_ptr(), qkv[:, DIM:].data_ptr()),
+                                       (C.c_longlong * 2)(3 * DIM, 3 * DIM),
+                                       (C.c_void_p * 2)(wq.data_ptr(), wk.data_ptr()),
+                                       (C.c_void_p * 2)(q_rot.data_ptr(), k_rot.data_ptr()),
+                                       (C.c_longlong * 2)(DIM, DIM), M, DIM, HD, H * W,
+                                       cos.data_ptr(), sin.data_ptr(), 1e-6, _lib.stream()), "rms")
+    return run, 2 * M * DIM * 4, "GB/s"
+
+
 CASES = {
     "gemm_up": lambda: _gemm(FFN, DIM, _lib.EPI_GELU_NVFP4),
     "gemm_qkv": lambda: _gemm(3 * DIM, DIM, _lib.EPI_BIAS),
@@ -102,6 +120,7 @@ CASES = {
     "attention": _attention,
     "quant": _quant,
     "ln": _ln,
+    "rms": _rms,
 }
 
 

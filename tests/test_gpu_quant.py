@@ -94,3 +94,25 @@ def test_nvfp4_quantize_every_bf16_value_every_scale():
     rc, rs = onv.quantize(x)
     np.testing.assert_array_equal(codes.cpu().numpy(), rc)
     np.testing.assert_array_equal(scales.cpu().numpy(), rs)
+
+
+def test_nvfp4_quantize_every_bf16_amax():
+    """Blocks [a, a/3, -a/7, 0, ...] for every finite positive bf16 a (plus inf
+    and NaN blocks): the block scale e4m3(max(a/6, 2^-9)) is computed without
+    division on the device and must match the oracle's bytes exactly."""
+    from recavsr_b200.runtime import nvfp4
+    from oracle.numerics import bf16_from_bits
+    amax = bf16_from_bits(np.arange(1, 0x7F80, dtype=np.uint32).astype(np.uint16)).astype(np.float32)
+    amax = np.concatenate([amax, np.array([np.inf, np.nan], np.float32)])
+    blocks = np.zeros((len(amax), 16), np.float32)
+    blocks[:, 0] = amax
+    with np.errstate(invalid="ignore"):
+        blocks[:, 1] = bf16_round(amax / 3)
+        blocks[:, 2] = bf16_round(-amax / 7)
+    n = (len(blocks) + 63) // 64 * 64
+    blocks = np.concatenate([blocks, np.zeros((n - len(blocks), 16), np.float32)])
+    x = blocks.reshape(-1, 16 * 64)
+    codes, scales = nvfp4.quantize(dev_bf16(x))
+    rc, rs = onv.quantize(x)
+    np.testing.assert_array_equal(scales.cpu().numpy(), rs)
+    np.testing.assert_array_equal(codes.cpu().numpy(), rc)

@@ -170,3 +170,28 @@ def test_refined_quotient_e2m1_codes_are_exact():
             # e2m1 round-to-nearest-even (the ladder is RNE), sign from the sign bit
             code = nvfp4.e2m1_codes(np.abs(q1)) | (np.signbit(q1).astype(np.uint8) * 8)
             np.testing.assert_array_equal(code, ref)
+
+
+def test_div6_is_exact_for_bf16():
+    """The kernels compute the NVFP4 block scale amax / 6 without dividing:
+    q = amax * fl(1/6), refined once by the exact residual. For every finite
+    non-negative bf16 amax this equals IEEE fp32 division (exhaustive, with the
+    final fma rounded exactly)."""
+    from fractions import Fraction
+    from oracle.numerics import bf16_from_bits
+    a = bf16_from_bits(np.arange(0, 0x7F80, dtype=np.uint32).astype(np.uint16)).astype(np.float32)
+    ref = (a / np.float32(6)).astype(np.float32)
+    r6 = np.float32(1) / np.float32(6)
+    q = (a * r6).astype(np.float32)
+    rem = (a.astype(np.float64) - q.astype(np.float64) * 6.0).astype(np.float32)   # exact
+    approx = (rem.astype(np.float64) * np.float64(r6) + q.astype(np.float64)).astype(np.float32)
+    # Double rounding through float64 can only matter next to an fp32 midpoint:
+    # re-round those few candidates exactly.
+    fr6 = Fraction(float(r6))
+    for i in np.nonzero(approx != ref)[0].tolist() + list(range(0, len(a), 997)):
+        exact = Fraction(float(rem[i])) * fr6 + Fraction(float(q[i]))
+        cands = [np.nextafter(approx[i], np.float32(-np.inf)), approx[i], np.nextafter(approx[i], np.float32(np.inf))]
+        dist = [abs(Fraction(float(c)) - exact) for c in cands]
+        best = min(range(3), key=lambda k: (dist[k], int(np.float32(cands[k]).view(np.uint32)) & 1))
+        approx[i] = cands[best]
+    np.testing.assert_array_equal(approx, ref)
