@@ -19,22 +19,29 @@
 //  1. rope_gather: temporally rotated copies of the current K frames and the
 //     routed past K planes into a caller-provided workspace (the slot
 //     indirection is applied here, so the attention kernel reads K densely).
-//  2. attention: one CTA per (128-query tile, head), operands staged by TMA.
-//     Warp 0 = producer: the raw Q tile once, then K tiles (workspace) and V
-//     tiles (read in place from the cache slot / current frame), 128 keys each,
-//     in two 3-stage rings; K runs two tiles ahead of V, and a K stage is
-//     released as soon as its Q K^T finishes.
-//     Warps 2-9 = softmax: first they rotate Q (temporal RoPE, fp32 math) and
-//     store it into tensor memory; then, per key tile, two warps per TMEM lane
-//     quadrant (64 keys each) load S, apply the window mask, keep a lazily
-//     rescaled running max, compute exp2 and store P (bf16) into tensor memory.
-//     Warp 1 = MMA issuer: S = Q K^T and O += P V both read their A operand
-//     (Q, P) from tensor memory, so only K and V stream from shared memory.
-//   TMEM columns: S [0,128) | O [128,256) | Q [256,320) | P0 [320,384) | P1 [384,448).
-//   Dense mode (window covers the grid): query tiles are 128 consecutive tokens,
-//   key tiles 128 consecutive tokens of a plane (4-D TMA view; the plane tail
-//   reads as zeros). Local mode: query tiles are 2 frames x 8 x 8 tokens, key
-//   tiles are 8 x 16 boxes of the union of the tile's windows (5-D TMA view).
+//  2. attention: one CTA per (128-query tile, head).
+//     Warp 0 = TMA producer: the raw Q tile once, then K tiles (workspace) and
+//     V tiles (read in place from the cache slot / current frame) of 128 keys
+//     in two 3-stage rings, K two tiles ahead of V.
+//     The keys of every tile are split between two independent softmax slots:
+//     slot 0 (warps 2-5) takes keys 0-63, slot 1 (warps 6-9) keys 64-127. Each
+//     slot keeps its own S, P and O in tensor memory and its own running max /
+//     sum per row, one thread per query row (TMEM lane): per 64-key block it
+//     loads S, applies the window mask, keeps a lazily rescaled running max,
+//     computes exp2 and stores P (bf16). The two warps of a TMEM lane quadrant
+//     (one per slot) never wait for each other until the end, where they
+//     combine (O_0, m_0, l_0) and (O_1, m_1, l_1) into the output.
+//     Warp 1 = MMA issuer: S_x = Q K_x^T and O_x += P_x V_x, A operands (Q, P)
+//     in tensor memory; an event loop issues each slot's next MMA as soon as
+//     its inputs are ready, so the slots run out of phase and one slot's
+//     softmax overlaps the other's MMAs.
+//   TMEM columns: S_0 [0,64) | S_1 [64,128) | P_0 [128,160) | P_1 [160,192) |
+//   Q [192,256) | O_0 [256,384) | O_1 [384,512).
+//   Dense mode (window covers the grid): a query tile = 128 consecutive tokens,
+//   a key tile = 128 consecutive tokens of a plane (4-D TMA view; the plane
+//   tail reads as zeros). Local mode: a query tile = 2 frames x 8 x 8 tokens, a
+//   key tile = an 8 x 16 box of the union of the tile's windows (5-D TMA
+//   view); slot 0 / 1 take its box rows 0-3 / 4-7.
 #include <mutex>
 
 #include "sm100.cuh"
@@ -42,16 +49,17 @@
 namespace {
 
 constexpr int kD = 128;             // head dim supported by the tcgen05 kernel
-constexpr int kBM = 128;            // queries per CTA
-constexpr int kBN = 128;            // keys per tile
-constexpr int kThreads = 320;       // producer, MMA, 8 softmax warps
+constexpr int kBM = 128;            // queries per CTA (one TMEM lane each)
+constexpr int kBN = 128;            // keys per K / V tile
+constexpr int kSB = 64;             // keys per slot and tile
+constexpr int kThreads = 320;       // producer, MMA, 2 slots x 4 softmax warps
 constexpr int kLocalQH = 8, kLocalQW = 8;   // local query tile: 2 frames x 8 x 8
 constexpr int kLocalKH = 8, kLocalKW = 16;  // local key box: 8 rows x 16 cols
 constexpr int kMaxPlanes = 16;
 constexpr float kRescaleThreshold = 8.0f;   // log2 units
 
-// Tensor-memory column map (512 columns allocated).
-constexpr uint32_t kTmS = 0, kTmO = 128, kTmQ = 256, kTmP = 320;   // P buffers at 320 and 384
+// Tensor-memory column map (512 columns allocated); slot x adds x * width.
+constexpr uint32_t kTmS = 0, kTmP = 128, kTmQ = 192, kTmO = 256;
 
 struct AttnParams {
   int T, H, W, heads, QT, CAP;
@@ -81,12 +89,12 @@ struct SmemLayout {
   static constexpr int offBar = offV + 2 * kStages * kChunk;
   static constexpr int kBars = 24;
   static constexpr int offMisc = offBar + kBars * 8;
-  static constexpr int offRed = offMisc + 16 + kMaxPlanes * 4;   // [2][2][128] floats
+  static constexpr int offRed = offMisc + 16 + kMaxPlanes * 4;   // [2 slots][2][128] floats
   static constexpr int kTotal = offRed + 2 * 2 * 128 * 4;
   static constexpr int kAlloc = kTotal;
 };
 
-// Enumerates the key tiles of one query tile: planes in order, tiles within.
+// Key rectangle of one query tile (local mode) and the key tiles per plane.
 struct TileIter {
   const AttnParams& p;
   int ry0, ry1, rx0, rx1;       // local-mode key rectangle
@@ -133,7 +141,7 @@ struct TileCursor {
   }
 };
 
-// Position in a ring of kStages buffers: stage index and phase parity.
+// Position in a ring of buffers: stage index and phase parity.
 struct Ring {
   int stage = 0;
   uint32_t phase = 0;
@@ -199,20 +207,20 @@ attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
                  const __grid_constant__ CUtensorMap tm_pv, const __grid_constant__ CUtensorMap tm_cv,
                  const AttnParams p) {
   using L = SmemLayout;
+  constexpr int kS = L::kStages;
   // 1024-byte alignment: the 128-byte TMA swizzle pattern repeats every 1024 bytes.
   extern __shared__ __align__(1024) uint8_t smem[];
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::offBar);
-  uint64_t* q_full = bars + 0;     // raw Q landed in shared memory
-  uint64_t* q_tmem = bars + 1;     // rotated Q stored in tensor memory (256 arrivals)
-  constexpr int kS = L::kStages;
+  uint64_t* q_full = bars + 0;             // raw Q landed in shared memory
+  uint64_t* q_tmem = bars + 1;             // rotated Q stored in tensor memory (256 arrivals)
   uint64_t* k_full = bars + 2;             // [kS] K tile landed
-  uint64_t* k_empty = k_full + kS;         // [kS] Q K^T reading the K stage finished
+  uint64_t* k_empty = k_full + kS;         // [kS] both slots' Q K^T read the K stage
   uint64_t* v_full = k_empty + kS;         // [kS] V tile landed
-  uint64_t* v_empty = v_full + kS;         // [kS] P.V reading the V stage finished
-  uint64_t* s_full = v_empty + kS;         // S = Q K^T of the current tile finished
-  uint64_t* s_free = s_full + 1;           // S loaded by all softmax threads (256 arrivals)
-  uint64_t* p_full = s_free + 1;           // [2] P buffer written (256 arrivals)
-  uint64_t* o_done = p_full + 2;           // [2] P.V reading P buffer b finished
+  uint64_t* v_empty = v_full + kS;         // [kS] both slots' P.V read the V stage
+  uint64_t* s_full = v_empty + kS;         // [2] S_x of the slot's current block finished
+  uint64_t* s_free = s_full + 2;           // [2] S_x loaded by the slot's threads (128 arrivals)
+  uint64_t* p_full = s_free + 2;           // [2] P_x written (128 arrivals)
+  uint64_t* o_done = p_full + 2;           // [2] P_x.V finished
   uint64_t* done = o_done + 2;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::offMisc);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::offMisc + 4);
@@ -244,12 +252,12 @@ attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       sm100::mbar_init(&v_full[s2], 1);
       sm100::mbar_init(&v_empty[s2], 1);
     }
-    for (int s2 = 0; s2 < 2; ++s2) {
-      sm100::mbar_init(&p_full[s2], 256);
-      sm100::mbar_init(&o_done[s2], 1);
+    for (int x = 0; x < 2; ++x) {
+      sm100::mbar_init(&s_full[x], 1);
+      sm100::mbar_init(&s_free[x], 128);
+      sm100::mbar_init(&p_full[x], 128);
+      sm100::mbar_init(&o_done[x], 1);
     }
-    sm100::mbar_init(s_full, 1);
-    sm100::mbar_init(s_free, 256);
     sm100::mbar_init(done, 1);
     *abort_flag = 0;
     // Visible planes: routed past planes (slot >= 0), then the current frames.
@@ -268,7 +276,6 @@ attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
   __syncthreads();
   sm100::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t t_s = tmem + kTmS, t_o = tmem + kTmO, t_q = tmem + kTmQ;
   const int nplanes = *s_nplanes;
   TileIter it(p, qy0, qx0);
   const int nx = it.tiles_x(), ny = it.tiles_y();
@@ -293,7 +300,7 @@ attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
         if (!p.local) sm100::tma_load_3d(sq + c * L::kChunk, &tm_q, q_full, c * 64, head, q_row0);
         else sm100::tma_load_5d(sq + c * L::kChunk, &tm_q, q_full, c * 64, head, qx0, qy0, qf0);
       }
-      // K runs two tiles ahead of V: Q K^T of a tile comes one pipeline step
+      // K runs two tiles ahead of V: Q K^T of a tile comes a pipeline step
       // before its P.V, and a K stage frees up as soon as its Q K^T finishes.
       TileCursor kc, vc;
       Ring kr, vr;
@@ -347,61 +354,74 @@ attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
   } else if (warp == 1) {
     // ----------------------------------------------------------- MMA issuer
     if (sm100::elect_one_sync()) {
-      constexpr uint32_t idesc_qk = sm100::idesc_bf16(kBM, kBN, 0, 0);
+      constexpr uint32_t idesc_qk = sm100::idesc_bf16(kBM, kSB, 0, 0);
       constexpr uint32_t idesc_pv = sm100::idesc_bf16(kBM, kD, 0, 1);
       bool ok = wait(q_tmem, 0, 2);
       sm100::tc_fence_after();
-      Ring kr, vr;
-      auto issue_pv = [&](int j) -> bool {
-        if (!wait(&v_full[vr.stage], vr.phase, 12)) return false;
-        if (!wait(&p_full[j & 1], (j >> 1) & 1, 3)) return false;
-        sm100::tc_fence_after();
-        const uint32_t t_p = tmem + kTmP + (uint32_t)(j & 1) * 64;
-        const uint32_t sv = sm100::smem_u32(smem + L::offV + vr.stage * 2 * L::kChunk);
-        for (int k = 0; k < kBN / 16; ++k)
-          sm100::mma_f16_ts(t_o, t_p + 8 * k, sm100::desc_mnmajor_sw128(sv + k * 16 * 128, L::kChunk),
-                            idesc_pv, (j > 0 || k > 0) ? 1u : 0u);
-        sm100::tc_commit(&v_empty[vr.stage]);
-        sm100::tc_commit(&o_done[j & 1]);
-        vr.advance(kS);
-        return true;
-      };
-      for (int i = 0; i < n_tiles && ok; ++i) {
-        if (!wait(&k_full[kr.stage], kr.phase, 4)) { ok = false; break; }
-        if (!wait(s_free, (i & 1) ^ 1, 5)) { ok = false; break; }   // S(i-1) is in registers
-        sm100::tc_fence_after();
-        const uint32_t sk = sm100::smem_u32(smem + L::offK + kr.stage * 2 * L::kChunk);
-        for (int k = 0; k < kD / 16; ++k)
-          sm100::mma_f16_ts(t_s, t_q + 8 * k,
-                            sm100::desc_kmajor_sw128(sk + (k >> 2) * L::kChunk + (k & 3) * 32),
-                            idesc_qk, k > 0 ? 1u : 0u);
-        sm100::tc_commit(s_full);
-        sm100::tc_commit(&k_empty[kr.stage]);
-        kr.advance(kS);
-        if (i > 0 && !issue_pv(i - 1)) { ok = false; break; }
+      // Per slot: the next Q K^T (ns) and P.V (np) block to issue. Slot x's
+      // S_x(i) needs K tile i and S_x(i-1) read; its P_x(i).V needs V tile i
+      // and P_x(i) written. A ring stage is released once both slots issued
+      // their MMAs on it.
+      int ns[2] = {0, 0}, np[2] = {0, 0};
+      int k_rel = 0, v_rel = 0;
+      unsigned long long t_idle = 0;
+      while (ok && (np[0] < n_tiles || np[1] < n_tiles)) {
+        bool progress = false;
+#pragma unroll
+        for (int x = 0; x < 2; ++x) {
+          const int i = ns[x];
+          if (i < n_tiles && i <= np[x] + 1 && (i == 0 || sm100::mbar_test(&s_free[x], (i - 1) & 1)) &&
+              sm100::mbar_test(&k_full[i % kS], (i / kS) & 1)) {
+            sm100::tc_fence_after();
+            const uint32_t sk = sm100::smem_u32(smem + L::offK + (i % kS) * 2 * L::kChunk) + x * kSB * 128;
+            for (int k = 0; k < kD / 16; ++k)
+              sm100::mma_f16_ts(tmem + kTmS + x * kSB, tmem + kTmQ + 8 * k,
+                                sm100::desc_kmajor_sw128(sk + (k >> 2) * L::kChunk + (k & 3) * 32),
+                                idesc_qk, k > 0 ? 1u : 0u);
+            sm100::tc_commit(&s_full[x]);
+            ns[x] = i + 1;
+            progress = true;
+          }
+          const int j = np[x];
+          if (j < ns[x] && sm100::mbar_test(&p_full[x], j & 1) && sm100::mbar_test(&v_full[j % kS], (j / kS) & 1)) {
+            sm100::tc_fence_after();
+            const uint32_t sv = sm100::smem_u32(smem + L::offV + (j % kS) * 2 * L::kChunk);
+            for (int k = 0; k < kSB / 16; ++k)
+              sm100::mma_f16_ts(tmem + kTmO + x * kD, tmem + kTmP + x * 32 + 8 * k,
+                                sm100::desc_mnmajor_sw128(sv + (x * (kSB / 16) + k) * 16 * 128, L::kChunk),
+                                idesc_pv, (j > 0 || k > 0) ? 1u : 0u);
+            sm100::tc_commit(&o_done[x]);
+            np[x] = j + 1;
+            progress = true;
+          }
+        }
+        while (k_rel < min(ns[0], ns[1])) sm100::tc_commit(&k_empty[k_rel++ % kS]);
+        while (v_rel < min(np[0], np[1])) sm100::tc_commit(&v_empty[v_rel++ % kS]);
+        if (progress) {
+          t_idle = 0;
+        } else {
+          const unsigned long long now = rc::globaltimer_ns();
+          if (!t_idle) t_idle = now;
+          if (*abort_flag || now - t_idle > rc::kWaitNs) {
+            fail(3);
+            ok = false;
+          }
+        }
       }
-      if (ok && n_tiles > 0) issue_pv(n_tiles - 1);
       sm100::tc_commit(done);
       sm100::mbar_wait(done, 0);
     }
   } else {
     // ----------------------------------------------------------- softmax
-    // Two warps per TMEM lane quadrant: `half` selects head dims
-    // [64*half, 64*half+64) of Q and O, and key columns [64*half, 64*half+64)
-    // of S and P.
+    // Slot x = (warp - 2) / 4; the warp's TMEM lane quadrant is warp % 4 and
+    // each thread owns one query row; the two warps of a quadrant (one per
+    // slot) hold the same rows.
     const int quad = warp & 3;
-    const int half = (warp - 2) >> 2;
+    const int x = (warp - 2) >> 2;
     const int r = quad * 32 + lane;               // query row within the tile / TMEM lane
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
-    const int cbase = half * 64;
-    float* red = reinterpret_cast<float*>(smem + L::offRed);   // [2 tiles][2 halves][128 rows]
-    // Both warps of a pair pass the same number of pair barriers on every path
-    // (one per key tile, then one for the row sum): an early exit drains the rest.
-    int pair_syncs = 0;
-    auto pair_sync = [&]() {
-      asm volatile("bar.sync %0, 64;" ::"r"(1 + quad) : "memory");
-      ++pair_syncs;
-    };
+    const uint32_t t_s = tmem + kTmS + x * kSB + lane_off;
+    const uint32_t t_p = tmem + kTmP + x * 32 + lane_off;
     int qrow = -1, qf = 0, qy = 0, qx = 0;
     if (!p.local) {
       const int t = q_row0 + r;
@@ -416,9 +436,10 @@ attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
     }
     bool ok = __all_sync(0xffffffffu, wait(q_full, 0, 10));
     if (ok) {
-      // This thread's 64 dims of its Q row -> temporal RoPE -> tensor memory.
+      // Slot x rotates head dims [64x, 64x + 64) of its Q row (temporal RoPE,
+      // fp32 math, bf16 rounding) into tensor memory.
       uint32_t qv[32];
-      const uint8_t* src = smem + L::offQ + half * L::kChunk + r * 128;
+      const uint8_t* src = smem + L::offQ + x * L::kChunk + r * 128;
 #pragma unroll
       for (int u = 0; u < 8; ++u) {
         const uint4 w = *reinterpret_cast<const uint4*>(src + ((u ^ (r & 7)) << 4));
@@ -427,12 +448,11 @@ attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
         qv[4 * u + 2] = w.z;
         qv[4 * u + 3] = w.w;
       }
-      if (p.qpos && qrow >= 0 && cbase < p.td) {
+      if (p.qpos && qrow >= 0 && x * 64 < p.td) {
         const int pos = p.qpos[qf];
-        rotate_pairs(qv, cbase >> 1, p.td, p.cos + (size_t)pos * (p.td >> 1),
-                     p.sin + (size_t)pos * (p.td >> 1));
+        rotate_pairs(qv, x * 32, p.td, p.cos + (size_t)pos * (p.td >> 1), p.sin + (size_t)pos * (p.td >> 1));
       }
-      sm100::tmem_st32(t_q + half * 32 + lane_off, qv);
+      sm100::tmem_st32(tmem + kTmQ + x * 32 + lane_off, qv);
       sm100::tmem_st_wait();
     }
     sm100::tc_fence_before();
@@ -440,23 +460,21 @@ attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
     const int top = min(max(qy - p.wh / 2, 0), p.H - p.wh);
     const int left = min(max(qx - p.ww / 2, 0), p.W - p.ww);
     const float scale = p.scale_log2;
+    const uint32_t t_o = tmem + kTmO + x * kD + lane_off;
     float m_used = -INFINITY, l = 0.f;
     TileCursor cur;
     for (int i = 0; i < n_tiles && ok; ++i, cur.advance(nx, ny)) {
-      const int st = i & 1;
-      if (!__all_sync(0xffffffffu, wait(s_full, i & 1, 6))) { ok = false; break; }
-      sm100::tc_fence_after();
       int a, b;
       cur.origin(it, a, b);
-      const bool full_tile = !p.local && a + kBN <= p.T;
+      if (!__all_sync(0xffffffffu, wait(&s_full[x], i & 1, 6))) { ok = false; break; }
+      sm100::tc_fence_after();
       float v[64];
       {
-        const uint32_t ts = t_s + cbase + lane_off;
         uint32_t r0[16], r1[16], r2[16], r3[16];
-        sm100::tmem_ld16(ts, r0);
-        sm100::tmem_ld16(ts + 16, r1);
-        sm100::tmem_ld16(ts + 32, r2);
-        sm100::tmem_ld16(ts + 48, r3);
+        sm100::tmem_ld16(t_s, r0);
+        sm100::tmem_ld16(t_s + 16, r1);
+        sm100::tmem_ld16(t_s + 32, r2);
+        sm100::tmem_ld16(t_s + 48, r3);
         sm100::tmem_ld_wait();
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
@@ -466,34 +484,36 @@ attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
           v[48 + j] = __uint_as_float(r3[j]);
         }
       }
-      // S is in registers: the MMA may write S of the next tile.
+      // S_x is in registers: the MMA may write the slot's next block.
       sm100::tc_fence_before();
-      sm100::mbar_arrive(s_free);
-      if (!full_tile) {
-        // Validity of this warp's 64 keys as a bit mask: dense = a prefix of the
-        // plane; local = 4 box rows x 16 box columns intersected with the window.
+      sm100::mbar_arrive(&s_free[x]);
+      if (p.local || a + (x + 1) * kSB > p.T) {
+        // Validity of the slot's 64 keys as a bit mask: dense = a prefix of
+        // the plane; local = 4 box rows x 16 box columns intersected with the window.
         uint64_t mask;
         if (!p.local) {
-          const int cnt = min(max(p.T - (a + cbase), 0), 64);
+          const int cnt = min(max(p.T - (a + x * kSB), 0), 64);
           mask = cnt >= 64 ? ~0ull : ((1ull << cnt) - 1ull);
         } else {
           uint32_t cols = 0;
 #pragma unroll
-          for (int x = 0; x < kLocalKW; ++x) {
-            const int kx = b + x;
-            cols |= (kx < p.W && kx >= left && kx < left + p.ww) ? (1u << x) : 0u;
+          for (int j = 0; j < kLocalKW; ++j) {
+            const int kx = b + j;
+            cols |= (kx < p.W && kx >= left && kx < left + p.ww) ? (1u << j) : 0u;
           }
           mask = 0;
 #pragma unroll
           for (int y = 0; y < 4; ++y) {
-            const int ky = a + (cbase >> 4) + y;
+            const int ky = a + x * 4 + y;
             if (ky < p.H && ky >= top && ky < top + p.wh) mask |= (uint64_t)cols << (16 * y);
           }
         }
+        if (mask != ~0ull) {
 #pragma unroll
-        for (int j = 0; j < 64; ++j) v[j] = ((mask >> j) & 1ull) ? v[j] : -INFINITY;
+          for (int j = 0; j < 64; ++j) v[j] = ((mask >> j) & 1ull) ? v[j] : -INFINITY;
+        }
       }
-      // Row max of this warp's 64 columns: 8 independent three-input chains.
+      // Row max of the block: 8 independent three-input chains.
       float mx[8];
 #pragma unroll
       for (int k = 0; k < 8; ++k) mx[k] = max3(v[k], v[k + 8], v[k + 16]);
@@ -504,11 +524,7 @@ attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
 #pragma unroll
       for (int k = 0; k < 8; ++k) mx[k] = fmaxf(mx[k], v[k + 56]);
       float mt = max3(max3(mx[0], mx[1], mx[2]), max3(mx[3], mx[4], mx[5]), fmaxf(mx[6], mx[7]));
-      // Row max over both halves (raw scores; scale > 0 commutes with max).
-      red[(st * 2 + half) * 128 + r] = mt;
-      pair_sync();
-      mt = fmaxf(mt, red[(st * 2 + (half ^ 1)) * 128 + r]);
-      mt = mt == -INFINITY ? -INFINITY : mt * scale;
+      mt = mt == -INFINITY ? -INFINITY : mt * scale;   // scale > 0 commutes with max
       // Lazy rescaling: move the reference max only when it grows by > 2^8.
       float corr = 1.0f;
       bool rescale = false;
@@ -519,72 +535,85 @@ attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       }
       const float mref = m_used == -INFINITY ? 0.f : m_used;
       // P = exp2(s * scale - mref), two columns per packed op: three of every
-      // four column pairs on the MUFU, the fourth by the FMA-pipe polynomial
-      // (the MUFU and the tensor pipe need equal time per tile at d = 128).
+      // four column pairs on the MUFU, the fourth by the FMA-pipe polynomial.
       // Masked scores (-inf) give 0 either way.
       const float2 scale2 = make_float2(scale, scale), nmref2 = make_float2(-mref, -mref);
       float2 sum2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
       uint32_t pk[32];
 #pragma unroll
       for (int j = 0; j < 32; ++j) {
-        const float2 x = __ffma2_rn(make_float2(v[2 * j], v[2 * j + 1]), scale2, nmref2);
+        const float2 xv = __ffma2_rn(make_float2(v[2 * j], v[2 * j + 1]), scale2, nmref2);
         float2 e;
         if ((j & 3) == 3) {
-          e = exp2_poly2(x);
+          e = exp2_poly2(xv);
         } else {
-          e.x = fast_exp2(x.x);
-          e.y = fast_exp2(x.y);
+          e.x = fast_exp2(xv.x);
+          e.y = fast_exp2(xv.y);
         }
         sum2[j & 1] = __fadd2_rn(sum2[j & 1], e);
         pk[j] = pack_bf16x2(e.x, e.y);
       }
       l = __fmul_rn(l, corr) + ((sum2[0].x + sum2[0].y) + (sum2[1].x + sum2[1].y));
-      // The P buffer of this tile was last read by the P.V of tile i-2.
-      if (i >= 2 && !__all_sync(0xffffffffu, wait(&o_done[st], ((i >> 1) - 1) & 1, 7))) { ok = false; break; }
+      // P_x of the previous block was read by its P.V (which also leaves O_x stable).
+      if (i > 0 && !__all_sync(0xffffffffu, wait(&o_done[x], (i - 1) & 1, 7))) { ok = false; break; }
       sm100::tc_fence_after();
-      sm100::tmem_st32(tmem + kTmP + (uint32_t)st * 64 + half * 32 + lane_off, pk);
-      // O changes only when a row's reference max moved (rare); then wait for P.V(i-1).
+      sm100::tmem_st32(t_p, pk);
+      // O changes only when a row's reference max moved (rare).
       if (__any_sync(0xffffffffu, rescale)) {
-        if (!__all_sync(0xffffffffu, wait(&o_done[st ^ 1], ((i - 1) >> 1) & 1, 9))) { ok = false; break; }
-        sm100::tc_fence_after();
         const float f = rescale ? corr : 1.0f;
 #pragma unroll 1
-        for (int c = cbase; c < cbase + 64; c += 16) {
+        for (int c = 0; c < kD; c += 16) {
           uint32_t w[16];
-          sm100::tmem_ld16(t_o + c + lane_off, w);
+          sm100::tmem_ld16(t_o + c, w);
           sm100::tmem_ld_wait();
 #pragma unroll
           for (int j = 0; j < 16; ++j) w[j] = __float_as_uint(__uint_as_float(w[j]) * f);
-          sm100::tmem_st16(t_o + c + lane_off, w);
+          sm100::tmem_st16(t_o + c, w);
         }
       }
       sm100::tmem_st_wait();
       sm100::tc_fence_before();
-      sm100::mbar_arrive(&p_full[st]);
+      sm100::mbar_arrive(&p_full[x]);
     }
-    while (pair_syncs < n_tiles) pair_sync();
-    // Row sum over both halves.
-    red[half * 128 + r] = l;
-    pair_sync();
-    l += red[(half ^ 1) * 128 + r];
-    if (ok && n_tiles > 0 &&
-        __all_sync(0xffffffffu, wait(&o_done[(n_tiles - 1) & 1], ((n_tiles - 1) >> 1) & 1, 8))) {
-      sm100::tc_fence_after();
-      const float inv = 1.0f / fmaxf(l, 1e-20f);
+    // Combine the two slots: out = (O_0 2^(m_0 - m) + O_1 2^(m_1 - m)) /
+    // (l_0 2^(m_0 - m) + l_1 2^(m_1 - m)), m = max(m_0, m_1); slot x writes
+    // head dims [64x, 64x + 64).
+    const bool fin = ok && n_tiles > 0 && __all_sync(0xffffffffu, wait(&o_done[x], (n_tiles - 1) & 1, 8));
+    float* red = reinterpret_cast<float*>(smem + L::offRed);   // [slot][m, l][row]
+    red[(x * 2 + 0) * 128 + r] = fin ? m_used : NAN;
+    red[(x * 2 + 1) * 128 + r] = l;
+    sm100::tc_fence_before();
+    asm volatile("bar.sync %0, 64;" ::"r"(1 + quad) : "memory");
+    sm100::tc_fence_after();
+    const float m0 = red[0 * 128 + r], l0 = red[1 * 128 + r];
+    const float m1 = red[2 * 128 + r], l1 = red[3 * 128 + r];
+    if (fin && m0 == m0 && m1 == m1) {
+      const float m = fmaxf(m0, m1);
+      const float a0 = m0 == -INFINITY ? 0.f : fast_exp2(m0 - m);
+      const float a1 = m1 == -INFINITY ? 0.f : fast_exp2(m1 - m);
+      const float inv = 1.0f / fmaxf(__fadd_rn(__fmul_rn(l0, a0), __fmul_rn(l1, a1)), 1e-20f);
+      const float2 c0 = make_float2(a0 * inv, a0 * inv), c1 = make_float2(a1 * inv, a1 * inv);
       __nv_bfloat16* dst = (qrow >= 0 && p.out) ? p.out + (size_t)qrow * p.out_ld + (size_t)head * kD : nullptr;
       const int katoms = (p.heads * kD) >> 6;
+      const uint32_t o0 = tmem + kTmO + lane_off, o1 = tmem + kTmO + kD + lane_off;
 #pragma unroll 1
-      for (int c = cbase; c < cbase + 64; c += 16) {
-        uint32_t w16[16];
-        sm100::tmem_ld16(t_o + c + lane_off, w16);
+      for (int c = x * 64; c < x * 64 + 64; c += 16) {
+        uint32_t w0[16], w1[16];
+        sm100::tmem_ld16(o0 + c, w0);
+        sm100::tmem_ld16(o1 + c, w1);
         sm100::tmem_ld_wait();
         float y[16];
+        uint32_t w[8];
 #pragma unroll
-        for (int j = 0; j < 16; ++j) y[j] = rc::bf16_to_float(rc::bf16_bits(__uint_as_float(w16[j]) * inv));
+        for (int j = 0; j < 8; ++j) {
+          const float2 s0 = make_float2(__uint_as_float(w0[2 * j]), __uint_as_float(w0[2 * j + 1]));
+          const float2 s1 = make_float2(__uint_as_float(w1[2 * j]), __uint_as_float(w1[2 * j + 1]));
+          const float2 o = __ffma2_rn(s1, c1, __fmul2_rn(s0, c0));
+          w[j] = pack_bf16x2(o.x, o.y);
+          y[2 * j] = __uint_as_float(w[j] << 16);
+          y[2 * j + 1] = __uint_as_float(w[j] & 0xffff0000u);
+        }
         if (dst) {
-          uint32_t w[8];
-#pragma unroll
-          for (int j = 0; j < 8; ++j) w[j] = pack_bf16x2(y[2 * j], y[2 * j + 1]);
           reinterpret_cast<uint4*>(dst + c)[0] = make_uint4(w[0], w[1], w[2], w[3]);
           reinterpret_cast<uint4*>(dst + c)[1] = make_uint4(w[4], w[5], w[6], w[7]);
         }
