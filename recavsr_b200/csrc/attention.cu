@@ -20,9 +20,9 @@
 //     routed past K planes into a caller-provided workspace (the slot
 //     indirection is applied here, so the attention kernel reads K densely).
 //  2. attention: one CTA per (128-query tile, head).
-//     Warp 0 = TMA producer: the raw Q tile once, then K tiles (workspace) and
-//     V tiles (read in place from the cache slot / current frame) of 128 keys
-//     in two 3-stage rings, K two tiles ahead of V.
+//     Warp 0 = TMA producer: K tiles (workspace) and V tiles (read in place
+//     from the cache slot / current frame) of 128 keys in a 4-stage K ring and
+//     a 3-stage V ring, K three tiles ahead of V.
 //     The keys of every tile are split between two independent softmax slots:
 //     slot 0 (warps 2-5) takes keys 0-63, slot 1 (warps 6-9) keys 64-127. Each
 //     slot keeps its own S, P and O in tensor memory and its own running max /
@@ -30,7 +30,9 @@
 //     loads S, applies the window mask, keeps a lazily rescaled running max,
 //     computes exp2 and stores P (bf16). The two warps of a TMEM lane quadrant
 //     (one per slot) never wait for each other until the end, where they
-//     combine (O_0, m_0, l_0) and (O_1, m_1, l_1) into the output.
+//     combine (O_0, m_0, l_0) and (O_1, m_1, l_1) into the output. First, each
+//     slot loads half of every thread's Q row from global memory, rotates it
+//     and stores it into tensor memory.
 //     Warp 1 = MMA issuer: S_x = Q K_x^T and O_x += P_x V_x, A operands (Q, P)
 //     in tensor memory; an event loop issues each slot's next MMA as soon as
 //     its inputs are ready, so the slots run out of phase and one slot's
@@ -62,6 +64,8 @@ constexpr float kRescaleThreshold = 8.0f;   // log2 units
 constexpr uint32_t kTmS = 0, kTmP = 128, kTmQ = 192, kTmO = 256;
 
 struct AttnParams {
+  const __nv_bfloat16* q;       // raw queries (head dim contiguous)
+  long long q_ld, q_hs;         // elements between tokens / heads
   int T, H, W, heads, QT, CAP;
   int Tq;                       // query tokens (dense mode validity)
   int wh, ww;                   // effective window (clamped to the grid)
@@ -82,11 +86,11 @@ struct AttnParams {
 
 struct SmemLayout {
   static constexpr int kChunk = 128 * 128;           // 128 rows x 128 bytes
-  static constexpr int kStages = 3;                  // K ring and V ring depth
-  static constexpr int offQ = 0;                     // 2 chunks (raw Q, read once)
-  static constexpr int offK = offQ + 2 * kChunk;     // kStages x 2 chunks
-  static constexpr int offV = offK + 2 * kStages * kChunk;
-  static constexpr int offBar = offV + 2 * kStages * kChunk;
+  static constexpr int kStagesK = 4;                 // K ring depth
+  static constexpr int kStagesV = 3;                 // V ring depth
+  static constexpr int offK = 0;                     // kStagesK x 2 chunks
+  static constexpr int offV = offK + 2 * kStagesK * kChunk;
+  static constexpr int offBar = offV + 2 * kStagesV * kChunk;
   static constexpr int kBars = 24;
   static constexpr int offMisc = offBar + kBars * 8;
   static constexpr int offRed = offMisc + 16 + kMaxPlanes * 4;   // [2 slots][2][128] floats
@@ -203,21 +207,20 @@ __device__ __forceinline__ void rotate_pairs(uint32_t (&w)[N], int pair0, int td
 }
 
 __global__ void __launch_bounds__(kThreads, 1)
-attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+attention_kernel(const __grid_constant__ CUtensorMap tm_k,
                  const __grid_constant__ CUtensorMap tm_pv, const __grid_constant__ CUtensorMap tm_cv,
                  const AttnParams p) {
   using L = SmemLayout;
-  constexpr int kS = L::kStages;
+  constexpr int kSK = L::kStagesK, kSV = L::kStagesV;
   // 1024-byte alignment: the 128-byte TMA swizzle pattern repeats every 1024 bytes.
   extern __shared__ __align__(1024) uint8_t smem[];
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::offBar);
-  uint64_t* q_full = bars + 0;             // raw Q landed in shared memory
-  uint64_t* q_tmem = bars + 1;             // rotated Q stored in tensor memory (256 arrivals)
-  uint64_t* k_full = bars + 2;             // [kS] K tile landed
-  uint64_t* k_empty = k_full + kS;         // [kS] both slots' Q K^T read the K stage
-  uint64_t* v_full = k_empty + kS;         // [kS] V tile landed
-  uint64_t* v_empty = v_full + kS;         // [kS] both slots' P.V read the V stage
-  uint64_t* s_full = v_empty + kS;         // [2] S_x of the slot's current block finished
+  uint64_t* q_tmem = bars + 0;             // rotated Q stored in tensor memory (256 arrivals)
+  uint64_t* k_full = bars + 1;             // [kSK] K tile landed
+  uint64_t* k_empty = k_full + kSK;        // [kSK] both slots' Q K^T read the K stage
+  uint64_t* v_full = k_empty + kSK;        // [kSV] V tile landed
+  uint64_t* v_empty = v_full + kSV;        // [kSV] both slots' P.V read the V stage
+  uint64_t* s_full = v_empty + kSV;        // [2] S_x of the slot's current block finished
   uint64_t* s_free = s_full + 2;           // [2] S_x loaded by the slot's threads (128 arrivals)
   uint64_t* p_full = s_free + 2;           // [2] P_x written (128 arrivals)
   uint64_t* o_done = p_full + 2;           // [2] P_x.V finished
@@ -244,11 +247,12 @@ attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
   }
 
   if (threadIdx.x == 0) {
-    sm100::mbar_init(q_full, 1);
     sm100::mbar_init(q_tmem, 256);
-    for (int s2 = 0; s2 < kS; ++s2) {
+    for (int s2 = 0; s2 < kSK; ++s2) {
       sm100::mbar_init(&k_full[s2], 1);
       sm100::mbar_init(&k_empty[s2], 1);
+    }
+    for (int s2 = 0; s2 < kSV; ++s2) {
       sm100::mbar_init(&v_full[s2], 1);
       sm100::mbar_init(&v_empty[s2], 1);
     }
@@ -294,14 +298,9 @@ attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
   if (warp == 0) {
     // ----------------------------------------------------------- producer
     if (sm100::elect_one_sync()) {
-      uint8_t* sq = smem + L::offQ;
-      sm100::mbar_arrive_expect_tx(q_full, 2 * L::kChunk);
-      for (int c = 0; c < 2; ++c) {
-        if (!p.local) sm100::tma_load_3d(sq + c * L::kChunk, &tm_q, q_full, c * 64, head, q_row0);
-        else sm100::tma_load_5d(sq + c * L::kChunk, &tm_q, q_full, c * 64, head, qx0, qy0, qf0);
-      }
-      // K runs two tiles ahead of V: Q K^T of a tile comes a pipeline step
-      // before its P.V, and a K stage frees up as soon as its Q K^T finishes.
+      // K runs three tiles ahead of V: Q K^T of a tile comes a pipeline step
+      // before its P.V, and a K stage frees up as soon as both slots' Q K^T on
+      // it finish (slot 1 trails slot 0 by about one block).
       TileCursor kc, vc;
       Ring kr, vr;
       int nk = 0, nv = 0;
@@ -332,24 +331,24 @@ attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
         }
         return true;
       };
-      for (int i = 0; i < n_tiles + 2 && ok; ++i) {
+      constexpr int kLead = kSK - 1;
+      for (int i = 0; i < n_tiles + kLead && ok; ++i) {
         if (i < n_tiles) {
           if (!(ok = load(true, kc, kr))) break;
           kc.advance(nx, ny);
-          kr.advance(kS);
+          kr.advance(kSK);
           ++nk;
         }
-        if (i >= 2) {
+        if (i >= kLead) {
           if (!(ok = load(false, vc, vr))) break;
           vc.advance(nx, ny);
-          vr.advance(kS);
+          vr.advance(kSV);
           ++nv;
         }
       }
-      // Drain the loads still in flight (at most kS per ring) before teardown.
-      for (int j = max(0, nk - kS); j < nk; ++j) sm100::mbar_wait(&k_full[j % kS], (j / kS) & 1);
-      for (int j = max(0, nv - kS); j < nv; ++j) sm100::mbar_wait(&v_full[j % kS], (j / kS) & 1);
-      sm100::mbar_wait(q_full, 0);
+      // Drain the loads still in flight (at most one ring's depth) before teardown.
+      for (int j = max(0, nk - kSK); j < nk; ++j) sm100::mbar_wait(&k_full[j % kSK], (j / kSK) & 1);
+      for (int j = max(0, nv - kSV); j < nv; ++j) sm100::mbar_wait(&v_full[j % kSV], (j / kSV) & 1);
     }
   } else if (warp == 1) {
     // ----------------------------------------------------------- MMA issuer
@@ -369,11 +368,15 @@ attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
         bool progress = false;
 #pragma unroll
         for (int x = 0; x < 2; ++x) {
+          // Slot 1 starts one softmax block behind slot 0 (its first Q K^T waits
+          // for slot 0's first P): the slots then run out of phase, one in its
+          // exp2 loop while the other loads S, reduces and stores P.
           const int i = ns[x];
           if (i < n_tiles && i <= np[x] + 1 && (i == 0 || sm100::mbar_test(&s_free[x], (i - 1) & 1)) &&
-              sm100::mbar_test(&k_full[i % kS], (i / kS) & 1)) {
+              (x == 0 || i > 0 || n_tiles == 1 || sm100::mbar_test(&p_full[0], 0)) &&
+              sm100::mbar_test(&k_full[i % kSK], (i / kSK) & 1)) {
             sm100::tc_fence_after();
-            const uint32_t sk = sm100::smem_u32(smem + L::offK + (i % kS) * 2 * L::kChunk) + x * kSB * 128;
+            const uint32_t sk = sm100::smem_u32(smem + L::offK + (i % kSK) * 2 * L::kChunk) + x * kSB * 128;
             for (int k = 0; k < kD / 16; ++k)
               sm100::mma_f16_ts(tmem + kTmS + x * kSB, tmem + kTmQ + 8 * k,
                                 sm100::desc_kmajor_sw128(sk + (k >> 2) * L::kChunk + (k & 3) * 32),
@@ -383,9 +386,9 @@ attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
             progress = true;
           }
           const int j = np[x];
-          if (j < ns[x] && sm100::mbar_test(&p_full[x], j & 1) && sm100::mbar_test(&v_full[j % kS], (j / kS) & 1)) {
+          if (j < ns[x] && sm100::mbar_test(&p_full[x], j & 1) && sm100::mbar_test(&v_full[j % kSV], (j / kSV) & 1)) {
             sm100::tc_fence_after();
-            const uint32_t sv = sm100::smem_u32(smem + L::offV + (j % kS) * 2 * L::kChunk);
+            const uint32_t sv = sm100::smem_u32(smem + L::offV + (j % kSV) * 2 * L::kChunk);
             for (int k = 0; k < kSB / 16; ++k)
               sm100::mma_f16_ts(tmem + kTmO + x * kD, tmem + kTmP + x * 32 + 8 * k,
                                 sm100::desc_mnmajor_sw128(sv + (x * (kSB / 16) + k) * 16 * 128, L::kChunk),
@@ -395,11 +398,12 @@ attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
             progress = true;
           }
         }
-        while (k_rel < min(ns[0], ns[1])) sm100::tc_commit(&k_empty[k_rel++ % kS]);
-        while (v_rel < min(np[0], np[1])) sm100::tc_commit(&v_empty[v_rel++ % kS]);
+        while (k_rel < min(ns[0], ns[1])) sm100::tc_commit(&k_empty[k_rel++ % kSK]);
+        while (v_rel < min(np[0], np[1])) sm100::tc_commit(&v_empty[v_rel++ % kSV]);
         if (progress) {
           t_idle = 0;
         } else {
+          __nanosleep(32);   // back off: the softmax warps share this SM sub-partition
           const unsigned long long now = rc::globaltimer_ns();
           if (!t_idle) t_idle = now;
           if (*abort_flag || now - t_idle > rc::kWaitNs) {
@@ -434,15 +438,18 @@ attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       qy = yy;
       qx = xx;
     }
-    bool ok = __all_sync(0xffffffffu, wait(q_full, 0, 10));
-    if (ok) {
-      // Slot x rotates head dims [64x, 64x + 64) of its Q row (temporal RoPE,
-      // fp32 math, bf16 rounding) into tensor memory.
+    bool ok = true;
+    {
+      // Slot x loads head dims [64x, 64x + 64) of its Q row (zeros past the
+      // last query) and rotates them (temporal RoPE, fp32 math, bf16 rounding)
+      // into tensor memory.
       uint32_t qv[32];
-      const uint8_t* src = smem + L::offQ + x * L::kChunk + r * 128;
+      const uint4* src = qrow >= 0 ? reinterpret_cast<const uint4*>(p.q + (size_t)qrow * p.q_ld +
+                                                                      (size_t)head * p.q_hs + x * 64)
+                                   : nullptr;
 #pragma unroll
       for (int u = 0; u < 8; ++u) {
-        const uint4 w = *reinterpret_cast<const uint4*>(src + ((u ^ (r & 7)) << 4));
+        const uint4 w = src ? __ldg(src + u) : make_uint4(0, 0, 0, 0);
         qv[4 * u] = w.x;
         qv[4 * u + 1] = w.y;
         qv[4 * u + 2] = w.z;
@@ -738,25 +745,6 @@ int make_view(CUtensorMap* m, const void* base, long long ld, long long hs, int 
                          CU_TENSOR_MAP_SWIZZLE_128B, what);
 }
 
-// Query views: dense (d, heads, tokens) with 128-token boxes; local
-// (d, heads, W, H, frames) with 8 x 8 x 2-frame boxes.
-int make_query_view(CUtensorMap* m, const void* base, long long ld, long long hs, int heads, int T,
-                    int H, int W, int frames, bool local, const char* what) {
-  if (local) {
-    const uint64_t dims[5] = {(uint64_t)kD, (uint64_t)heads, (uint64_t)W, (uint64_t)H, (uint64_t)frames};
-    const uint64_t str[4] = {(uint64_t)hs * 2, (uint64_t)ld * 2, (uint64_t)ld * 2 * W,
-                             (uint64_t)ld * 2 * T};
-    const uint32_t box[5] = {64, 1, kLocalQW, kLocalQH, 2};
-    return rc::encode_tmap(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 5, const_cast<void*>(base), dims, str, box,
-                           CU_TENSOR_MAP_SWIZZLE_128B, what);
-  }
-  const uint64_t dims[3] = {(uint64_t)kD, (uint64_t)heads, (uint64_t)frames * T};
-  const uint64_t str[2] = {(uint64_t)hs * 2, (uint64_t)ld * 2};
-  const uint32_t box[3] = {64, 1, kBM};
-  return rc::encode_tmap(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, str, box,
-                         CU_TENSOR_MAP_SWIZZLE_128B, what);
-}
-
 bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 int g_attr_set = 0;
@@ -852,8 +840,7 @@ int rc_paired_attention(const void* q, const void* ck, const void* cv, const voi
     if (blocks > 148LL * 16) blocks = 148LL * 16;
     rope_gather_kernel<<<(int)blocks, 256, 0, stream>>>(g);
     if ((r = rc::check_launch("rc_paired_attention(rope)"))) return r;
-    CUtensorMap tq, tk, tpv, tcv;
-    if ((r = make_query_view(&tq, qb, strides[1], strides[2], heads, T, H, W, QT, local, what))) return r;
+    CUtensorMap tk, tpv, tcv;
     if ((r = make_view(&tk, ks, hd, d, heads, T, H, W, CAP + QT, local, what))) return r;
     if ((r = make_view(&tcv, cvb, strides[7], strides[8], heads, T, H, W, QT, local, what))) return r;
     if (CAP) {
@@ -862,6 +849,7 @@ int rc_paired_attention(const void* q, const void* ck, const void* cv, const voi
       tpv = tcv;
     }
     AttnParams p{};
+    p.q = qb; p.q_ld = strides[1]; p.q_hs = strides[2];
     p.T = T; p.H = H; p.W = W; p.heads = heads; p.QT = QT; p.CAP = CAP; p.Tq = QT * T;
     p.wh = wh; p.ww = ww; p.local = local;
     p.scale_log2 = (float)(1.0 / sqrt((double)d) * 1.4426950408889634);
@@ -882,7 +870,7 @@ int rc_paired_attention(const void* q, const void* ck, const void* cv, const voi
       p.n_qtiles = (QT / 2) * p.qtiles_x * p.qtiles_y;
     }
     dim3 grid(p.n_qtiles, heads);
-    attention_kernel<<<grid, kThreads, SmemLayout::kAlloc, stream>>>(tq, tk, tpv, tcv, p);
+    attention_kernel<<<grid, kThreads, SmemLayout::kAlloc, stream>>>(tk, tpv, tcv, p);
     if ((r = rc::check_launch(what))) return r;
   }
   return RC_OK;
@@ -917,11 +905,11 @@ int rc_cross_attention(const void* q, const void* k, const void* v, const long l
     const __nv_bfloat16* qb = reinterpret_cast<const __nv_bfloat16*>(q) + b * strides[0];
     const __nv_bfloat16* kb = reinterpret_cast<const __nv_bfloat16*>(k) + b * strides[3];
     const __nv_bfloat16* vb = reinterpret_cast<const __nv_bfloat16*>(v) + b * strides[6];
-    CUtensorMap tq, tk, tv;
-    if ((r = make_query_view(&tq, qb, strides[1], strides[2], heads, Nq, 1, Nq, 1, false, what))) return r;
+    CUtensorMap tk, tv;
     if ((r = make_view(&tk, kb, strides[4], strides[5], heads, Nk, 1, Nk, 1, false, what))) return r;
     if ((r = make_view(&tv, vb, strides[7], strides[8], heads, Nk, 1, Nk, 1, false, what))) return r;
     AttnParams p{};
+    p.q = qb; p.q_ld = strides[1]; p.q_hs = strides[2];
     p.T = Nk; p.H = 1; p.W = Nk; p.heads = heads; p.QT = 1; p.CAP = 0; p.Tq = Nq;
     p.wh = 1; p.ww = Nk; p.local = 0;
     p.scale_log2 = (float)(1.0 / sqrt((double)d) * 1.4426950408889634);
@@ -934,7 +922,7 @@ int rc_cross_attention(const void* q, const void* k, const void* v, const long l
     p.q_sf = out_scales;
     p.n_qtiles = (Nq + kBM - 1) / kBM;
     dim3 grid(p.n_qtiles, heads);
-    attention_kernel<<<grid, kThreads, SmemLayout::kAlloc, stream>>>(tq, tk, tv, tv, p);
+    attention_kernel<<<grid, kThreads, SmemLayout::kAlloc, stream>>>(tk, tv, tv, p);
     if ((r = rc::check_launch(what))) return r;
   }
   return RC_OK;
