@@ -34,9 +34,10 @@
 //     slot loads half of every thread's Q row from global memory, rotates it
 //     and stores it into tensor memory.
 //     Warp 1 = MMA issuer: S_x = Q K_x^T and O_x += P_x V_x, A operands (Q, P)
-//     in tensor memory; an event loop issues each slot's next MMA as soon as
-//     its inputs are ready, so the slots run out of phase and one slot's
-//     softmax overlaps the other's MMAs.
+//     in tensor memory. Slot 1 starts one block behind slot 0, so the slots
+//     run out of phase and one slot's softmax overlaps the other's MMAs; the
+//     issuer waits (suspending) on each MMA's inputs in the order they become
+//     ready.
 //   TMEM columns: S_0 [0,64) | S_1 [64,128) | P_0 [128,160) | P_1 [160,192) |
 //   Q [192,256) | O_0 [256,384) | O_1 [384,512).
 //   Dense mode (window covers the grid): a query tile = 128 consecutive tokens,
@@ -357,60 +358,48 @@ attention_kernel(const __grid_constant__ CUtensorMap tm_k,
       constexpr uint32_t idesc_pv = sm100::idesc_bf16(kBM, kD, 0, 1);
       bool ok = wait(q_tmem, 0, 2);
       sm100::tc_fence_after();
-      // Per slot: the next Q K^T (ns) and P.V (np) block to issue. Slot x's
-      // S_x(i) needs K tile i and S_x(i-1) read; its P_x(i).V needs V tile i
-      // and P_x(i) written. A ring stage is released once both slots issued
-      // their MMAs on it.
-      int ns[2] = {0, 0}, np[2] = {0, 0};
-      int k_rel = 0, v_rel = 0;
-      unsigned long long t_idle = 0;
-      while (ok && (np[0] < n_tiles || np[1] < n_tiles)) {
-        bool progress = false;
-#pragma unroll
-        for (int x = 0; x < 2; ++x) {
-          // Slot 1 starts one softmax block behind slot 0 (its first Q K^T waits
-          // for slot 0's first P): the slots then run out of phase, one in its
-          // exp2 loop while the other loads S, reduces and stores P.
-          const int i = ns[x];
-          if (i < n_tiles && i <= np[x] + 1 && (i == 0 || sm100::mbar_test(&s_free[x], (i - 1) & 1)) &&
-              (x == 0 || i > 0 || n_tiles == 1 || sm100::mbar_test(&p_full[0], 0)) &&
-              sm100::mbar_test(&k_full[i % kSK], (i / kSK) & 1)) {
-            sm100::tc_fence_after();
-            const uint32_t sk = sm100::smem_u32(smem + L::offK + (i % kSK) * 2 * L::kChunk) + x * kSB * 128;
-            for (int k = 0; k < kD / 16; ++k)
-              sm100::mma_f16_ts(tmem + kTmS + x * kSB, tmem + kTmQ + 8 * k,
-                                sm100::desc_kmajor_sw128(sk + (k >> 2) * L::kChunk + (k & 3) * 32),
-                                idesc_qk, k > 0 ? 1u : 0u);
-            sm100::tc_commit(&s_full[x]);
-            ns[x] = i + 1;
-            progress = true;
-          }
-          const int j = np[x];
-          if (j < ns[x] && sm100::mbar_test(&p_full[x], j & 1) && sm100::mbar_test(&v_full[j % kSV], (j / kSV) & 1)) {
-            sm100::tc_fence_after();
-            const uint32_t sv = sm100::smem_u32(smem + L::offV + (j % kSV) * 2 * L::kChunk);
-            for (int k = 0; k < kSB / 16; ++k)
-              sm100::mma_f16_ts(tmem + kTmO + x * kD, tmem + kTmP + x * 32 + 8 * k,
-                                sm100::desc_mnmajor_sw128(sv + (x * (kSB / 16) + k) * 16 * 128, L::kChunk),
-                                idesc_pv, (j > 0 || k > 0) ? 1u : 0u);
-            sm100::tc_commit(&o_done[x]);
-            np[x] = j + 1;
-            progress = true;
-          }
-        }
-        while (k_rel < min(ns[0], ns[1])) sm100::tc_commit(&k_empty[k_rel++ % kSK]);
-        while (v_rel < min(np[0], np[1])) sm100::tc_commit(&v_empty[v_rel++ % kSV]);
-        if (progress) {
-          t_idle = 0;
-        } else {
-          __nanosleep(32);   // back off: the softmax warps share this SM sub-partition
-          const unsigned long long now = rc::globaltimer_ns();
-          if (!t_idle) t_idle = now;
-          if (*abort_flag || now - t_idle > rc::kWaitNs) {
-            fail(3);
-            ok = false;
-          }
-        }
+      // Issue order, per key tile i: S_0(i+1), S_1(i+1), P_0(i).V, P_1(i).V --
+      // the order in which their inputs become ready once slot 1 trails slot 0
+      // (its first Q K^T waits for slot 0's first P). S_x(i) needs K tile i and
+      // S_x(i-1) read; P_x(i).V needs V tile i and P_x(i) written. A ring stage
+      // is released after both slots' MMAs on it.
+      auto issue_s = [&](int x, int i) -> bool {
+        if (i > 0 && !wait(&s_free[x], (i - 1) & 1, 5)) return false;
+        if (!wait(&k_full[i % kSK], (i / kSK) & 1, 4)) return false;
+        sm100::tc_fence_after();
+        const uint32_t sk = sm100::smem_u32(smem + L::offK + (i % kSK) * 2 * L::kChunk) + x * kSB * 128;
+        for (int k = 0; k < kD / 16; ++k)
+          sm100::mma_f16_ts(tmem + kTmS + x * kSB, tmem + kTmQ + 8 * k,
+                            sm100::desc_kmajor_sw128(sk + (k >> 2) * L::kChunk + (k & 3) * 32),
+                            idesc_qk, k > 0 ? 1u : 0u);
+        sm100::tc_commit(&s_full[x]);
+        if (x == 1) sm100::tc_commit(&k_empty[i % kSK]);   // both slots done with K tile i
+        return true;
+      };
+      auto issue_pv = [&](int x, int j) -> bool {
+        if (!wait(&p_full[x], j & 1, 3)) return false;
+        if (x == 0 && !wait(&v_full[j % kSV], (j / kSV) & 1, 12)) return false;
+        sm100::tc_fence_after();
+        const uint32_t sv = sm100::smem_u32(smem + L::offV + (j % kSV) * 2 * L::kChunk);
+        for (int k = 0; k < kSB / 16; ++k)
+          sm100::mma_f16_ts(tmem + kTmO + x * kD, tmem + kTmP + x * 32 + 8 * k,
+                            sm100::desc_mnmajor_sw128(sv + (x * (kSB / 16) + k) * 16 * 128, L::kChunk),
+                            idesc_pv, (j > 0 || k > 0) ? 1u : 0u);
+        sm100::tc_commit(&o_done[x]);
+        if (x == 1) sm100::tc_commit(&v_empty[j % kSV]);   // both slots done with V tile j
+        return true;
+      };
+      if (ok && n_tiles > 0) {
+        ok = issue_s(0, 0);
+        // Slot 1 starts one softmax block behind slot 0: the slots then run out
+        // of phase, one in its exp2 loop while the other loads S, reduces and
+        // stores P.
+        if (ok && n_tiles > 1) ok = wait(&p_full[0], 0, 13);
+        ok = ok && issue_s(1, 0);
+      }
+      for (int i = 0; i < n_tiles && ok; ++i) {
+        if (i + 1 < n_tiles) ok = issue_s(0, i + 1) && issue_s(1, i + 1);
+        ok = ok && issue_pv(0, i) && issue_pv(1, i);
       }
       sm100::tc_commit(done);
       sm100::mbar_wait(done, 0);
