@@ -363,14 +363,18 @@ attention_kernel(const __grid_constant__ CUtensorMap tm_k,
       // (its first Q K^T waits for slot 0's first P). S_x(i) needs K tile i and
       // S_x(i-1) read; P_x(i).V needs V tile i and P_x(i) written. A ring stage
       // is released after both slots' MMAs on it.
+      // Base descriptors of K stage 0 / V stage 0; every MMA adds constant offsets.
+      const uint64_t dk0 = sm100::desc_kmajor_sw128(sm100::smem_u32(smem + L::offK));
+      const uint64_t dv0 = sm100::desc_mnmajor_sw128(sm100::smem_u32(smem + L::offV), L::kChunk);
       auto issue_s = [&](int x, int i) -> bool {
         if (i > 0 && !wait(&s_free[x], (i - 1) & 1, 5)) return false;
         if (!wait(&k_full[i % kSK], (i / kSK) & 1, 4)) return false;
         sm100::tc_fence_after();
-        const uint32_t sk = sm100::smem_u32(smem + L::offK + (i % kSK) * 2 * L::kChunk) + x * kSB * 128;
+        const uint64_t dk = sm100::desc_add(dk0, (i % kSK) * 2 * L::kChunk + x * kSB * 128);
+        const uint32_t ts = tmem + kTmS + x * kSB;
+#pragma unroll
         for (int k = 0; k < kD / 16; ++k)
-          sm100::mma_f16_ts(tmem + kTmS + x * kSB, tmem + kTmQ + 8 * k,
-                            sm100::desc_kmajor_sw128(sk + (k >> 2) * L::kChunk + (k & 3) * 32),
+          sm100::mma_f16_ts(ts, tmem + kTmQ + 8 * k, sm100::desc_add(dk, (k >> 2) * L::kChunk + (k & 3) * 32),
                             idesc_qk, k > 0 ? 1u : 0u);
         sm100::tc_commit(&s_full[x]);
         if (x == 1) sm100::tc_commit(&k_empty[i % kSK]);   // both slots done with K tile i
@@ -380,11 +384,11 @@ attention_kernel(const __grid_constant__ CUtensorMap tm_k,
         if (!wait(&p_full[x], j & 1, 3)) return false;
         if (x == 0 && !wait(&v_full[j % kSV], (j / kSV) & 1, 12)) return false;
         sm100::tc_fence_after();
-        const uint32_t sv = sm100::smem_u32(smem + L::offV + (j % kSV) * 2 * L::kChunk);
+        const uint64_t dv = sm100::desc_add(dv0, (j % kSV) * 2 * L::kChunk + x * kSB * 128);
+        const uint32_t to = tmem + kTmO + x * kD, tp = tmem + kTmP + x * 32;
+#pragma unroll
         for (int k = 0; k < kSB / 16; ++k)
-          sm100::mma_f16_ts(tmem + kTmO + x * kD, tmem + kTmP + x * 32 + 8 * k,
-                            sm100::desc_mnmajor_sw128(sv + (x * (kSB / 16) + k) * 16 * 128, L::kChunk),
-                            idesc_pv, (j > 0 || k > 0) ? 1u : 0u);
+          sm100::mma_f16_ts(to, tp + 8 * k, sm100::desc_add(dv, k * 16 * 128), idesc_pv, (j > 0 || k > 0) ? 1u : 0u);
         sm100::tc_commit(&o_done[x]);
         if (x == 1) sm100::tc_commit(&v_empty[j % kSV]);   // both slots done with V tile j
         return true;

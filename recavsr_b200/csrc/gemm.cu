@@ -247,6 +247,34 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
       int sf_buf = 0;
       bool ok = true;
       int local = 0;
+      // Base descriptors of stage 0; every MMA / scale copy adds constant
+      // offsets, which keeps the issuing thread's instruction stream short.
+      const uint64_t da0 = sm100::desc_kmajor_sw128(sm100::smem_u32(smem + S::offA));
+      const uint64_t db0 = sm100::desc_kmajor_sw128(sm100::smem_u32(smem + S::offB));
+      uint64_t dsa0 = 0, dsb0 = 0;
+      if constexpr (kScaled) {
+        dsa0 = sm100::desc_sf_rows(sm100::smem_u32(smem + S::offSfa));
+        dsb0 = sm100::desc_sf_rows(sm100::smem_u32(smem + S::offSfb));
+      }
+      // One k-step j (0..3) of a k-tile: its scale copies (block-scaled kinds)
+      // and its MMA.
+      auto copy_sf = [&](int j, uint32_t sfa_t, uint32_t sfb_t, uint64_t dsa, uint64_t dsb) {
+        sm100::tmem_cp_32x128b_warpx4(sfa_t + 4 * j, sm100::desc_add(dsa, j * kSfAtomBytes));
+#pragma unroll
+        for (int r = 0; r < BN / 128; ++r)
+          sm100::tmem_cp_32x128b_warpx4(sfb_t + j * (BN / 32) + 4 * r,
+                                        sm100::desc_add(dsb, (r * 4 + j) * kSfAtomBytes));
+      };
+      auto mma = [&](int j, uint32_t d_tmem, uint64_t da, uint64_t db, uint32_t sfa_t, uint32_t sfb_t,
+                     uint32_t acc) {
+        const uint64_t a = sm100::desc_add(da, 32 * j), b = sm100::desc_add(db, 32 * j);
+        if constexpr (KIND == KIND_NVF4)
+          sm100::mma_nvf4_ss(d_tmem, a, b, idesc, sfa_t + 4 * j, sfb_t + j * (BN / 32), acc);
+        else if constexpr (KIND == KIND_E4M3)
+          sm100::mma_f8f6f4_ss(d_tmem, a, b, idesc, acc);
+        else
+          sm100::mma_f16_ss(d_tmem, a, b, idesc, acc);
+      };
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++local) {
         const int as = local % kAcc;
         const uint32_t acc_parity = (uint32_t)((local / kAcc) & 1);
@@ -256,39 +284,35 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
         for (int kt = 0; kt < p.k_tiles; ++kt) {
           if (!wait(&full[stage], phase, 3)) { ok = false; break; }
           sm100::tc_fence_after();
-          const uint32_t a0 = sm100::smem_u32(smem + S::offA + stage * S::kA);
-          const uint32_t b0 = sm100::smem_u32(smem + S::offB + stage * S::kB);
-          int steps = kMmaPerTile;
+          const uint64_t da = sm100::desc_add(da0, stage * S::kA);
+          const uint64_t db = sm100::desc_add(db0, stage * S::kB);
+          uint32_t sfa_t = 0, sfb_t = 0;
+          uint64_t dsa = 0, dsb = 0;
+          int steps;
           if constexpr (kScaled) {
             steps = min(4, p.sf_katoms - kt * 4);   // K % 64 == 0: one atom per k-step
-            const uint32_t sfa_t = tmem_sfa + sf_buf * kSfaCols;
-            const uint32_t sfb_t = tmem_sfb + sf_buf * kSfbCols;
-            const uint32_t sa0 = sm100::smem_u32(smem + S::offSfa + stage * S::kSfa);
-            const uint32_t sb0 = sm100::smem_u32(smem + S::offSfb + stage * S::kSfb);
-            for (int j = 0; j < steps; ++j) {
-              sm100::tmem_cp_32x128b_warpx4(sfa_t + 4 * j, sm100::desc_sf_rows(sa0 + j * kSfAtomBytes));
-              for (int r = 0; r < BN / 128; ++r)
-                sm100::tmem_cp_32x128b_warpx4(sfb_t + j * (BN / 32) + 4 * r,
-                                              sm100::desc_sf_rows(sb0 + (r * 4 + j) * kSfAtomBytes));
-            }
-            for (int j = 0; j < steps; ++j) {
-              sm100::mma_nvf4_ss(d_tmem, sm100::desc_kmajor_sw128(a0 + 32 * j),
-                                 sm100::desc_kmajor_sw128(b0 + 32 * j), idesc, sfa_t + 4 * j,
-                                 sfb_t + j * (BN / 32), (kt | j) != 0);
-            }
+            sfa_t = tmem_sfa + sf_buf * kSfaCols;
+            sfb_t = tmem_sfb + sf_buf * kSfbCols;
+            dsa = sm100::desc_add(dsa0, stage * S::kSfa);
+            dsb = sm100::desc_add(dsb0, stage * S::kSfb);
             sf_buf ^= 1;
           } else {
             const int rem = (p.K - kt * KindTraits<KIND>::kElemsPerTile) /
                             (KindTraits<KIND>::kElemsPerTile / kMmaPerTile);
             steps = min(kMmaPerTile, rem);
-            for (int j = 0; j < steps; ++j) {
-              if constexpr (KIND == KIND_E4M3)
-                sm100::mma_f8f6f4_ss(d_tmem, sm100::desc_kmajor_sw128(a0 + 32 * j),
-                                     sm100::desc_kmajor_sw128(b0 + 32 * j), idesc, (kt | j) != 0);
-              else
-                sm100::mma_f16_ss(d_tmem, sm100::desc_kmajor_sw128(a0 + 32 * j),
-                                  sm100::desc_kmajor_sw128(b0 + 32 * j), idesc, (kt | j) != 0);
+          }
+          if (steps == kMmaPerTile) {          // full k-tile: straight-line issue
+            if constexpr (kScaled) {
+#pragma unroll
+              for (int j = 0; j < kMmaPerTile; ++j) copy_sf(j, sfa_t, sfb_t, dsa, dsb);
             }
+#pragma unroll
+            for (int j = 0; j < kMmaPerTile; ++j) mma(j, d_tmem, da, db, sfa_t, sfb_t, (kt | j) != 0);
+          } else {
+            if constexpr (kScaled) {
+              for (int j = 0; j < steps; ++j) copy_sf(j, sfa_t, sfb_t, dsa, dsb);
+            }
+            for (int j = 0; j < steps; ++j) mma(j, d_tmem, da, db, sfa_t, sfb_t, (kt | j) != 0);
           }
           sm100::tc_commit(&empty[stage]);
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
@@ -478,11 +502,10 @@ int dispatch_epi(int epi, const CUtensorMap& ta, const CUtensorMap& tb, const Ge
 
 int num_sms();
 
-// Tile width. 128 x 256 tiles move a third less operand data per FLOP than
-// 128 x 128 and win when the mainloop dominates: at least ~2 waves of wide
-// tiles, or a long K. 128 x 128 tiles (double-buffered accumulators) win for
-// short-K GEMMs with few tiles (wave quantization) and for the GELU + NVFP4
-// epilogue, whose math per tile outruns a short mainloop.
+// Tile width. 128 x 256 tiles (single accumulator, register-drained
+// epilogue) move a third less operand data per FLOP than 128 x 128 tiles, but
+// the 128 x 128 tiles overlap each tile's epilogue with the next tile's
+// mainloop (double-buffered accumulator) and quantize better onto 148 SMs.
 // RECAVSR_GEMM_BN=128 / 256 forces one width.
 bool gemm_prefer_wide(int epi, int M, int N, int K) {
   static int forced = -2;
@@ -492,9 +515,11 @@ bool gemm_prefer_wide(int epi, int M, int N, int K) {
   }
   if (N % 256) return false;
   if (forced >= 0) return forced == 1;
-  if (epi == EPI_GELU_NVF4) return false;
-  const long long wide_tiles = (long long)((M + 127) / 128) * (N / 256);
-  return wide_tiles >= 2LL * num_sms() || K >= 8192;
+  // With a short MMA issue path the 128-column tile (double-buffered
+  // accumulator, epilogue overlapped) is the faster one at every DiT shape
+  // (M = 1760: QKV, o-proj, ffn_up and ffn_down all measured).
+  (void)epi; (void)M; (void)K;
+  return false;
 }
 
 // Shared argument checks + tensor maps; `elem_bytes_x2` = 2 * bytes/element

@@ -278,6 +278,15 @@ __device__ __forceinline__ uint64_t desc_kmajor_sw128(uint32_t saddr) {
 __device__ __forceinline__ uint64_t desc_mnmajor_sw128(uint32_t saddr, uint32_t mn_chunk_bytes) {
   return smem_desc(saddr, mn_chunk_bytes, 1024, kSwizzle128B);
 }
+// The same descriptor for an operand `byte_offset` bytes further on (the start
+// address field holds address / 16 in 14 bits, enough for all of shared memory,
+// so adding to the whole descriptor only changes that field). Issuing an MMA
+// per k-step from a base descriptor plus constant offsets keeps the single
+// issuing thread's instruction stream short; rebuilding every descriptor made
+// the MMA issue, not the tensor core, the limit.
+__device__ __forceinline__ uint64_t desc_add(uint64_t desc, uint32_t byte_offset) {
+  return desc + (uint64_t)(byte_offset >> 4);
+}
 // Scale-factor source for tcgen05.cp 32x128b: 32 rows of 16 bytes, dense.
 __device__ __forceinline__ uint64_t desc_sf_rows(uint32_t saddr) {
   return smem_desc(saddr, 0, 128, kSwizzleNone);

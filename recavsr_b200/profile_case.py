@@ -7,6 +7,8 @@
     python -m recavsr_b200.profile_case quant        # NVFP4 quantizer 1760x3072
     python -m recavsr_b200.profile_case ln           # LayerNorm+AdaLN+NVFP4 1760x3072
     python -m recavsr_b200.profile_case rms          # RMSNorm+spatial RoPE of q and k, 1760x3072 each
+    python -m recavsr_b200.profile_case gemm_sweep   # NVFP4 / FP8 linears, M x (K, N) sweep + quantizers
+    python -m recavsr_b200.profile_case attention_sweep  # 30-layer routed attention, scopes 0/1/2/4/8
 
 Each case allocates fresh inputs (a few hundred MB at most), captures `--reps`
 launches in a CUDA graph, replays it and prints the mean CUDA-event time per
@@ -124,11 +126,127 @@ CASES = {
 }
 
 
+def _graph_time(run, reps):
+    """Mean device time per call of `run`, replayed from a CUDA graph."""
+    for _ in range(3):
+        run()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        with torch.cuda.graph(graph, stream=side):
+            for _ in range(reps):
+                run()
+    torch.cuda.current_stream().wait_stream(side)
+    graph.replay()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    graph.replay()
+    b.record()
+    b.synchronize()
+    return a.elapsed_time(b) / reps * 1e-3
+
+
+def _cfg3_operands(m, n, k, g):
+    """Activation N(0,1) with 0.1% of the entries x20 (outliers), weight N(0, 0.02)."""
+    a = torch.randn(m, k, generator=g, device="cuda")
+    mask = torch.rand(m, k, generator=g, device="cuda") < 1e-3
+    a = torch.where(mask, a * 20, a).bfloat16()
+    w = (torch.randn(n, k, generator=g, device="cuda") * 0.02).bfloat16()
+    return a, w
+
+
+def gemm_sweep(reps=10):
+    """NVFP4 / FP8 linear sweep: M in {1760, 3520, 7040} x (K, N) in {(3072, 3072),
+    (3072, 14336), (14336, 3072)}, bias epilogue, plus the NVFP4 and FP8
+    quantizers on the activation (GB/s of algorithmic bytes)."""
+    from .runtime import fp8
+    lib = _lib.library()
+    g = torch.Generator(device="cuda")
+    g.manual_seed(2)
+    print("path   M     K      N      us       TFLOP/s  | quant us  GB/s")
+    for m in (1760, 3520, 7040):
+        for k, n in ((3072, 3072), (3072, 14336), (14336, 3072)):
+            a, w = _cfg3_operands(m, n, k, g)
+            bias = torch.zeros(n, dtype=torch.bfloat16, device="cuda")
+            out = torch.empty(m, n, dtype=torch.bfloat16, device="cuda")
+            ac, asf = quantize(a)
+            wc, wsf = quantize(w)
+
+            def nvf4():
+                _lib.check(lib.rc_nvfp4_gemm(ac.data_ptr(), asf.data_ptr(), wc.data_ptr(), wsf.data_ptr(),
+                                             bias.data_ptr(), m, n, k, 1.0, _lib.EPI_BIAS, out.data_ptr(), n,
+                                             None, None, None, 1.0, _lib.stream()), "nvfp4_gemm")
+
+            def nvf4_quant():
+                quantize(a)
+            t = _graph_time(nvf4, reps)
+            tq = _graph_time(nvf4_quant, reps)
+            print(f"nvfp4 {m:5d} {k:6d} {n:6d} {t * 1e6:8.1f} {2.0 * m * n * k / t / 1e12:9.1f}"
+                  f"  | {tq * 1e6:7.1f} {m * k * 2.5625 / tq / 1e9:7.1f}")
+            aq, sa = fp8.quantize(a)
+            wq, sw = fp8.quantize(w)
+
+            def f8():
+                _lib.check(lib.rc_fp8_gemm(aq.data_ptr(), sa.data_ptr(), wq.data_ptr(), sw.data_ptr(),
+                                           bias.data_ptr(), m, n, k, 1.0, _lib.EPI_BIAS, out.data_ptr(), n,
+                                           None, _lib.stream()), "fp8_gemm")
+
+            def f8_quant():
+                fp8.quantize(a)
+            t = _graph_time(f8, reps)
+            tq = _graph_time(f8_quant, reps)
+            print(f"fp8   {m:5d} {k:6d} {n:6d} {t * 1e6:8.1f} {2.0 * m * n * k / t / 1e12:9.1f}"
+                  f"  | {tq * 1e6:7.1f} {m * k * 3.0 / tq / 1e9:7.1f}")
+            del a, w, ac, asf, wc, wsf, aq, wq, out
+
+
+def attention_sweep(reps=5):
+    """Routed-attention microbenchmark: 30 layers x 24 heads x 128, T = 880
+    (22 x 40), 2-frame query block (1760 queries), layer i attends to
+    [0, 1, 2, 4, 8][i % 5] routed planes of an 8-plane ring plus the 2 current
+    frames; FLOPs count visible keys only: 4 d heads Nq T sum(scope + 2)."""
+    from .kernels.local_attention import routed_attention
+    from .runtime.block import rope_tables
+    g = torch.Generator(device="cuda")
+    g.manual_seed(1)
+    t = H * W
+    r = lambda *sh: (torch.randn(*sh, generator=g, device="cuda") / HD ** 0.5).bfloat16()
+    q, k, v = r(1, 2 * t, HEADS, HD), r(1, 2 * t, HEADS, HD), r(1, 2 * t, HEADS, HD)
+    ring_k, ring_v = r(1, 8 * t, HEADS, HD), r(1, 8 * t, HEADS, HD)
+    tb = rope_tables(HD, H, W, "cuda")
+    out = torch.empty_like(q)
+    calls = []
+    for layer in range(30):
+        scope = (0, 1, 2, 4, 8)[layer % 5]
+        slots = torch.full((8,), -1, dtype=torch.int32, device="cuda")
+        slots[:scope] = torch.arange(8 - scope, 8, dtype=torch.int32, device="cuda")
+        ppos = torch.zeros(8, dtype=torch.int32, device="cuda")
+        ppos[:scope] = torch.arange(12 - scope, 12, dtype=torch.int32, device="cuda")
+        calls.append((slots, ppos))
+    qpos = torch.tensor([12, 13], dtype=torch.int32, device="cuda")
+
+    def run():
+        for slots, ppos in calls:
+            routed_attention(q, k, v, ring_k, ring_v, slots, ppos, qpos, tb["temporal_cos"],
+                             tb["temporal_sin"], H, W, H, W, out=out)
+    flops = 4.0 * HD * HEADS * (2 * t) * t * sum((0, 1, 2, 4, 8)[i % 5] + 2 for i in range(30))
+    dt = _graph_time(run, reps)
+    print(f"attention sweep: {dt * 1e3:.3f} ms per 30-layer block, {flops / dt / 1e12:.1f} TFLOP/s "
+          f"({flops:.3e} FLOP, {flops / (2 * t):.3e} FLOP/token)")
+
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=sorted(CASES))
+    ap.add_argument("case", choices=sorted(CASES) + ["gemm_sweep", "attention_sweep"])
     ap.add_argument("--reps", type=int, default=20)
     args = ap.parse_args()
+    if args.case == "gemm_sweep":
+        return gemm_sweep()
+    if args.case == "attention_sweep":
+        return attention_sweep()
     run, work, unit = CASES[args.case]()
     for _ in range(3):
         run()
