@@ -44,6 +44,17 @@ ACTIONS = ["none", "none", "recent_1", "none", "recent_2", "none", "recent_2", "
            "none", "recent_2_anchor", "recent_2", "none", "recent_2", "none", "recent_1", "none", "none"]
 METRIC = "DiT latent tokens/s/GPU (routed attn+NVFP4 linears); 720p x4 out frames/s"
 
+# DRAM bytes per launch of the roofline kernels (dram__bytes_read.sum +
+# dram__bytes_write.sum, one ncu capture of the same shapes through
+# `python -m recavsr_b200.profile_case gemm_up|attention`); a profiler figure,
+# not measured by this script.
+PROFILED_DRAM = {
+    "ffn_up": {"read": 27992320, "write": 67328,
+               "source": "ncu on profile_case gemm_up (1760x14336x3072, GELU+NVFP4 epilogue)"},
+    "attention": {"read": 75758080, "write": 2477824,
+                  "source": "ncu on profile_case attention (1760 queries, 4 routed + 2 current planes)"},
+}
+
 
 def peaks():
     try:
@@ -191,6 +202,16 @@ def kernel_roofline(stack, torch):
     att_flops = 4 * HEAD_DIM * HEADS * n * T * (vis + BODY)
     return {"ffn_up_s": t_up, "ffn_up_flops": 2.0 * n * FFN * DIM,
             "attn_s": t_att, "attn_flops": float(att_flops), "attn_planes": vis + BODY}
+
+
+def ffn_up_bytes():
+    """Algorithmic bytes of one ffn_up launch: NVFP4 activation and weight codes
+    + scales in, NVFP4 codes + scales of the GELU output out, bf16 bias."""
+    n = BODY * T
+    codes = lambda m, k: m * k // 2
+    scales = lambda m, k: (m + 127) // 128 * 128 * ((k // 16 + 3) // 4 * 4)
+    return (codes(n, DIM) + scales(n, DIM) + codes(FFN, DIM) + scales(FFN, DIM) + 2 * FFN
+            + codes(n, FFN) + scales(n, FFN))
 
 
 # ---------------------------------------------------------------- CPU side
@@ -345,7 +366,7 @@ def main():
               "attn_planes": 0}
     achieved = kr["ffn_up_flops"] / kr["ffn_up_s"] / 1e12
     cpu = None if args.no_cpu_baseline else cpu_baseline()
-    launches_per_layer = 17   # 14 kernels + 3 scale-padding kernels (M % 128 != 0)
+    launches_per_layer = 14   # see FusedBlock.run: LN x3, GEMM x6, RMSNorm x2, gather + attention, cross attention
     out = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": warm, "ms_per_step": t / args.steps * 1e3, "higher_is_better": True,
@@ -361,10 +382,14 @@ def main():
         "roofline": {"bound": "tensor", "kernel": "nvfp4 ffn_up GEMM 1760x14336x3072 (+GELU+NVFP4 epilogue)",
                      "achieved": achieved, "peak": fp4_peak, "unit": "TFLOP/s", "frac": achieved / fp4_peak,
                      "peak_source": f"4 x {src} bf16 dense ({bf16_peak} TFLOP/s): FP4:BF16 dense ratio 4",
-                     "traffic": None,
+                     "traffic": PROFILED_DRAM["ffn_up"]["read"] + PROFILED_DRAM["ffn_up"]["write"],
+                     "traffic_source": PROFILED_DRAM["ffn_up"]["source"],
+                     "algorithmic_bytes": ffn_up_bytes(),
                      "attention": {"achieved": kr["attn_flops"] / kr["attn_s"] / 1e12, "peak": bf16_peak,
                                    "frac": kr["attn_flops"] / kr["attn_s"] / 1e12 / bf16_peak,
-                                   "planes": kr["attn_planes"], "unit": "TFLOP/s"}},
+                                   "planes": kr["attn_planes"], "unit": "TFLOP/s",
+                                   "traffic": PROFILED_DRAM["attention"]["read"] + PROFILED_DRAM["attention"]["write"],
+                                   "traffic_source": PROFILED_DRAM["attention"]["source"]}},
         "cpu_baseline": cpu,
         "e2e": {"value": tokens / te, "unit": "tokens/s",
                 "h2d_bytes_per_step": BODY * T * DIM * 2, "d2h_bytes_per_step": BODY * T * DIM * 2},

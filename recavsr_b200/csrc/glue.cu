@@ -130,6 +130,15 @@ __global__ void __launch_bounds__(kRowThreads, 6) ln_modulate_kernel(LnArgs a) {
   __shared__ float red[4];
   const int row = blockIdx.x;
   const int t = threadIdx.x;
+  if (row >= a.M) {
+    // One extra CTA (launched when M % 128 != 0): zero the scale words of the
+    // padding rows [M, ceil(M/128)*128) so the next GEMM reads zeros there.
+    const int katoms = ((a.N >> 4) + 3) >> 2;
+    const int pad = (a.M + 127) / 128 * 128 - a.M;
+    for (int i = t; i < pad * katoms; i += kRowThreads)
+      *reinterpret_cast<uint32_t*>(a.sf + rc::sf_offset(a.M + i / katoms, (i % katoms) * 4, katoms)) = 0u;
+    return;
+  }
   const int nch = a.N >> 3;
   uint4 raw[kRowChunks];
 #pragma unroll
@@ -200,19 +209,6 @@ __global__ void __launch_bounds__(kRowThreads, 6) ln_modulate_kernel(LnArgs a) {
       if (live) *reinterpret_cast<uint32_t*>(a.codes + (size_t)row * (a.N >> 1) + (size_t)c * 4) = wq;
       store_sf4_pairs(a.sf, row, c >> 1, katoms, live ? sfb : 0, live);
     }
-  }
-}
-
-// Zero the scale bytes of padding rows [M, ceil(M/128)*128) and the padding
-// k-blocks of the last atom for all rows (the quantizer writes full words for
-// real rows, so only the tail rows need this).
-__global__ void sf_pad_rows_kernel(uint8_t* sf, int M, int katoms) {
-  const int pm = (M + 127) / 128 * 128;
-  const long long total = (long long)(pm - M) * katoms;
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
-       i += (long long)gridDim.x * blockDim.x) {
-    const int row = M + (int)(i / katoms), kt = (int)(i % katoms);
-    *reinterpret_cast<uint32_t*>(sf + rc::sf_offset(row, kt * 4, katoms)) = 0u;
   }
 }
 
@@ -432,16 +428,8 @@ int rc_ln_modulate_quant(const void* x, long long ldx, int M, int N, const void*
            reinterpret_cast<const __nv_bfloat16*>(weight), reinterpret_cast<const __nv_bfloat16*>(bias),
            shift, scale, eps, reinterpret_cast<__nv_bfloat16*>(out), ldo, codes, scales_swizzled,
            global_scale, M, N};
-  ln_modulate_kernel<<<M, kRowThreads, 0, stream>>>(a);
-  int r = rc::check_launch("rc_ln_modulate_quant");
-  if (r || !codes) return r;
-  const int katoms = ((N >> 4) + 3) >> 2;
-  if (M % 128) {
-    sf_pad_rows_kernel<<<grid_for((long long)(128 - M % 128) * katoms, 256), 256, 0, stream>>>(
-        scales_swizzled, M, katoms);
-    r = rc::check_launch("rc_ln_modulate_quant(pad)");
-  }
-  return r;
+  ln_modulate_kernel<<<M + ((codes && M % 128) ? 1 : 0), kRowThreads, 0, stream>>>(a);
+  return rc::check_launch("rc_ln_modulate_quant");
 }
 
 // RMSNorm across the full row (eps, affine bf16 weight) of up to two tensors
