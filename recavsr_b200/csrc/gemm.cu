@@ -12,8 +12,9 @@
 //   BF16 : plain bf16 linears.
 // Accumulation is fp32 in TMEM. One CTA per SM runs a persistent loop over
 // 128 x BN output tiles with warp roles: warp 0 = TMA producer, warp 1 = MMA
-// issuer (+ TMEM owner), warps 2-9 = epilogue (TMEM -> registers -> global;
-// two warps per TMEM lane quadrant, each on half of the tile's columns). With
+// issuer (+ TMEM owner), the other warps = epilogue (TMEM -> registers ->
+// global; two or four warps per TMEM lane quadrant, each on an equal share of
+// the tile's columns, see epi_warps). With
 // BN = 128 the accumulator is double-buffered in TMEM so the epilogue of one
 // tile overlaps the MMAs of the next; with BN = 256 the epilogue drains the
 // accumulator into registers first and releases it, which gives the same
@@ -35,8 +36,13 @@ enum Epi : int { EPI_BIAS = 0, EPI_GATED_RESIDUAL = 1, EPI_RESIDUAL = 2, EPI_GEL
 
 constexpr int BM = 128;
 constexpr int kRowBytes = 128;                     // K bytes per smem row / k-tile
-constexpr int kEpiWarps = 8;                       // 2 per TMEM lane quadrant
-constexpr int kThreads = 64 + 32 * kEpiWarps;      // producer, MMA, epilogue warps
+// Epilogue warps per CTA: 4 per TMEM lane quadrant for the GELU + NVFP4
+// epilogue (latency-bound math), 2 per quadrant for the light epilogues (more
+// warps there only compete with the MMA issuer for its SM sub-partition).
+template <int EPI>
+constexpr int epi_warps() { return EPI == EPI_GELU_NVF4 ? 16 : 8; }
+template <int EPI>
+constexpr int gemm_threads() { return 64 + 32 * epi_warps<EPI>(); }   // producer, MMA, epilogue
 constexpr int kSfAtomBytes = 512;                  // 128 rows x 4 scale bytes
 
 template <int KIND>
@@ -119,7 +125,7 @@ __device__ __forceinline__ void unpack_bf16x2(uint32_t w, float& a, float& b) {
 }
 
 template <int KIND, int BN, int STAGES, int EPI>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(gemm_threads<EPI>(), 1)
 gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
             const GemmParams p) {
   using S = Smem<KIND, BN, STAGES>;
@@ -152,7 +158,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
     }
     for (int a = 0; a < 2; ++a) {
       sm100::mbar_init(&acc_full[a], 1);
-      sm100::mbar_init(&acc_empty[a], 32 * kEpiWarps);
+      sm100::mbar_init(&acc_empty[a], 32 * epi_warps<EPI>());
     }
     sm100::mbar_init(done, 1);
     *abort_flag = 0;
@@ -326,13 +332,13 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
     }
   } else {
     // ------------------------------------------------------------ epilogue
-    // Each thread owns one accumulator row (TMEM lane) and half of the tile's
-    // columns. It first drains its columns from TMEM into registers and releases
+    // Each thread owns one accumulator row (TMEM lane) and a share of the
+    // tile's columns. It first drains its columns from TMEM into registers and releases
     // the accumulator, so the next tile's MMAs overlap this tile's epilogue math.
     const int quad = warp & 3;                 // TMEM lane quadrant of this warp
-    const int half = (warp - 2) >> 2;          // which half of the tile's columns
+    const int part = (warp - 2) >> 2;          // which share of the tile's columns
     const int row_in_tile = quad * 32 + lane;
-    constexpr int kCols = BN / 2;
+    constexpr int kCols = BN / (epi_warps<EPI>() / 4);
     int local = 0;
     float alpha = p.alpha;
     if constexpr (KIND == KIND_E4M3) {
@@ -346,7 +352,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
       sm100::tc_fence_after();
       uint32_t acc[kCols];
       {
-        const uint32_t t_row = tmem_acc + as * BN + half * kCols + ((uint32_t)(quad * 32) << 16);
+        const uint32_t t_row = tmem_acc + as * BN + part * kCols + ((uint32_t)(quad * 32) << 16);
 #pragma unroll
         for (int c = 0; c < kCols; c += 16)
           sm100::tmem_ld16(t_row + c, *reinterpret_cast<uint32_t(*)[16]>(&acc[c]));
@@ -358,7 +364,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
       const bool row_ok = row < p.M;
 #pragma unroll
       for (int cc = 0; cc < kCols; cc += 16) {
-        const int n0 = nb * BN + half * kCols + cc;
+        const int n0 = nb * BN + part * kCols + cc;
         if (n0 >= p.N) continue;
         if (!row_ok) {
           // Padding rows of the next linear's scale atoms must read as zero.
@@ -484,7 +490,7 @@ int launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, cu
   }
   const int tiles = p.m_blocks * p.n_blocks;
   const int grid = tiles < num_sms() ? tiles : num_sms();
-  kern<<<grid, kThreads, S::kAlloc, stream>>>(ta, tb, p);
+  kern<<<grid, gemm_threads<EPI>(), S::kAlloc, stream>>>(ta, tb, p);
   return rc::check_launch(what);
 }
 
