@@ -231,6 +231,8 @@ attention_kernel(const __grid_constant__ CUtensorMap tm_k,
   int* s_nplanes = reinterpret_cast<int*>(smem + L::offMisc + 8);
   int* s_planes = reinterpret_cast<int*>(smem + L::offMisc + 16);   // kMaxPlanes
 
+  rc::pdl_trigger();
+  rc::pdl_wait();   // the previous kernel's outputs are visible from here
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int head = blockIdx.y;
   const int qtile = blockIdx.x;
@@ -685,6 +687,8 @@ __device__ __forceinline__ bool gather_src(const GatherParams& g, long long i, i
 }
 
 __global__ void rope_gather_kernel(GatherParams g) {
+  rc::pdl_trigger();
+  rc::pdl_wait();
   const int vec = g.hd >> 3;
   const long long total = (long long)(g.CAP + g.QT) * g.T * vec;
   const long long stride = (long long)gridDim.x * blockDim.x;
@@ -831,8 +835,9 @@ int rc_paired_attention(const void* q, const void* ck, const void* cv, const voi
     const long long work = (long long)(QT + CAP) * T * (hd / 8);
     long long blocks = (work + 255) / 256;
     if (blocks > 148LL * 16) blocks = 148LL * 16;
-    rope_gather_kernel<<<(int)blocks, 256, 0, stream>>>(g);
-    if ((r = rc::check_launch("rc_paired_attention(rope)"))) return r;
+    if ((r = rc::check_launch(rc::launch_pdl(rope_gather_kernel, dim3((int)blocks), dim3(256), 0, stream, g),
+                              "rc_paired_attention(rope)")))
+      return r;
     CUtensorMap tk, tpv, tcv;
     if ((r = make_view(&tk, ks, hd, d, heads, T, H, W, CAP + QT, local, what))) return r;
     if ((r = make_view(&tcv, cvb, strides[7], strides[8], heads, T, H, W, QT, local, what))) return r;
@@ -863,8 +868,10 @@ int rc_paired_attention(const void* q, const void* ck, const void* cv, const voi
       p.n_qtiles = (QT / 2) * p.qtiles_x * p.qtiles_y;
     }
     dim3 grid(p.n_qtiles, heads);
-    attention_kernel<<<grid, kThreads, SmemLayout::kAlloc, stream>>>(tk, tpv, tcv, p);
-    if ((r = rc::check_launch(what))) return r;
+    if ((r = rc::check_launch(
+             rc::launch_pdl(attention_kernel, grid, dim3(kThreads), SmemLayout::kAlloc, stream, tk, tpv, tcv, p),
+             what)))
+      return r;
   }
   return RC_OK;
 }
@@ -915,8 +922,10 @@ int rc_cross_attention(const void* q, const void* k, const void* v, const long l
     p.q_sf = out_scales;
     p.n_qtiles = (Nq + kBM - 1) / kBM;
     dim3 grid(p.n_qtiles, heads);
-    attention_kernel<<<grid, kThreads, SmemLayout::kAlloc, stream>>>(tk, tv, tv, p);
-    if ((r = rc::check_launch(what))) return r;
+    if ((r = rc::check_launch(
+             rc::launch_pdl(attention_kernel, grid, dim3(kThreads), SmemLayout::kAlloc, stream, tk, tv, tv, p),
+             what)))
+      return r;
   }
   return RC_OK;
 }

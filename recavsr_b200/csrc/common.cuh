@@ -48,12 +48,41 @@ namespace rc {
 
 int set_error(int code, const char* fmt, ...);
 int check_launch(const char* what);
+int check_launch(cudaError_t launched, const char* what);   // result of launch_pdl
 
 // cuTensorMapEncodeTiled through the runtime's driver entry point (no -lcuda).
 // dims/strides: innermost first; strides are in bytes for dims 1..rank-1.
 int encode_tmap(CUtensorMap* map, CUtensorMapDataType dtype, int rank, void* base,
                 const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,
                 CUtensorMapSwizzle swizzle, const char* what);
+
+// Programmatic dependent launch. Every kernel of the library is launched with
+// launch_pdl (below) and starts with pdl_trigger(); pdl_wait(): the next
+// kernel in the stream may begin launching onto SMs this grid frees up (its
+// prologue -- barrier init, TMEM allocation, tensor-map prefetch -- overlaps
+// this grid's tail), and no kernel reads global memory before pdl_wait(),
+// which returns once the preceding grid has completed and its writes are
+// visible. Because every kernel waits on its predecessor before finishing,
+// the ordering is transitive along the stream.
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// Launch `kernel` on `stream` with programmatic stream serialization allowed.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                              cudaStream_t stream, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
 
 // Device: record the first error only.
 __device__ __forceinline__ void device_fail(unsigned int kernel_id, unsigned int site) {

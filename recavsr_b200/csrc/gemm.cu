@@ -171,6 +171,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
   sm100::tc_fence_before();
   __syncthreads();
   sm100::tc_fence_after();
+  rc::pdl_trigger();
+  rc::pdl_wait();   // the previous kernel's outputs (our A operand) are visible from here
   const uint32_t tmem = *tmem_slot;
   const uint32_t tmem_acc = tmem;                                 // kAcc x BN columns
   const uint32_t tmem_sfa = tmem + kAcc * BN;                     // 2 x kSfaCols
@@ -490,8 +492,7 @@ int launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, cu
   }
   const int tiles = p.m_blocks * p.n_blocks;
   const int grid = tiles < num_sms() ? tiles : num_sms();
-  kern<<<grid, gemm_threads<EPI>(), S::kAlloc, stream>>>(ta, tb, p);
-  return rc::check_launch(what);
+  return rc::check_launch(rc::launch_pdl(kern, grid, dim3(gemm_threads<EPI>()), S::kAlloc, stream, ta, tb, p), what);
 }
 
 template <int KIND, int BN, int STAGES>

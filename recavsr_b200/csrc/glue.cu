@@ -128,6 +128,8 @@ __device__ __forceinline__ float row_sum(float v, float* red) {
 
 __global__ void __launch_bounds__(kRowThreads, 6) ln_modulate_kernel(LnArgs a) {
   __shared__ float red[4];
+  rc::pdl_trigger();
+  rc::pdl_wait();
   const int row = blockIdx.x;
   const int t = threadIdx.x;
   if (row >= a.M) {
@@ -227,6 +229,8 @@ struct RmsArgs {
 // head and its rotary coefficients are loaded once.
 __global__ void __launch_bounds__(kRowThreads, 8) rmsnorm_rope_kernel(RmsArgs a) {
   __shared__ float red[4];
+  rc::pdl_trigger();
+  rc::pdl_wait();
   const int row = blockIdx.x, t = threadIdx.x;
   const bool second = blockIdx.y != 0;            // select, not index: keeps the params in registers
   const __nv_bfloat16* xp = second ? a.x[1] : a.x[0];
@@ -305,6 +309,8 @@ __global__ void temporal_rope_kernel(const __nv_bfloat16* __restrict__ x, long l
                                      const int* __restrict__ pos, const float* __restrict__ cos,
                                      const float* __restrict__ sin, int rows, int span, int heads,
                                      int d, int td) {
+  rc::pdl_trigger();
+  rc::pdl_wait();
   const long long pairs_per_row = (long long)heads * (d / 2);
   const long long total = (long long)rows * pairs_per_row;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
@@ -337,6 +343,8 @@ struct CommitArgs {
 };
 
 __global__ void kv_commit_kernel(CommitArgs a) {
+  rc::pdl_trigger();
+  rc::pdl_wait();
   const int vec_per_row = a.row_bytes >> 4;
   const long long per_plane = (long long)a.span * vec_per_row;
   const long long total = 2LL * a.n * per_plane;
@@ -361,6 +369,8 @@ __global__ void kv_commit_kernel(CommitArgs a) {
 constexpr int kCopyUnroll = 4;   // independent 16-byte loads in flight per thread
 
 __global__ void kv_commit_planned_kernel(CommitArgs a, const int* __restrict__ plan) {
+  rc::pdl_trigger();
+  rc::pdl_wait();
   const int n = min(plan[0], a.n);
   const int vec_per_row = a.row_bytes >> 4;
   const long long per_plane = (long long)a.span * vec_per_row;
@@ -428,8 +438,9 @@ int rc_ln_modulate_quant(const void* x, long long ldx, int M, int N, const void*
            reinterpret_cast<const __nv_bfloat16*>(weight), reinterpret_cast<const __nv_bfloat16*>(bias),
            shift, scale, eps, reinterpret_cast<__nv_bfloat16*>(out), ldo, codes, scales_swizzled,
            global_scale, M, N};
-  ln_modulate_kernel<<<M + ((codes && M % 128) ? 1 : 0), kRowThreads, 0, stream>>>(a);
-  return rc::check_launch("rc_ln_modulate_quant");
+  return rc::check_launch(rc::launch_pdl(ln_modulate_kernel, dim3(M + ((codes && M % 128) ? 1 : 0)),
+                                         dim3(kRowThreads), 0, stream, a),
+                          "rc_ln_modulate_quant");
 }
 
 // RMSNorm across the full row (eps, affine bf16 weight) of up to two tensors
@@ -465,8 +476,9 @@ int rc_rmsnorm_rope(int n_tensors, const void* const* xs, const long long* ldx,
   a.d = d;
   a.span = span;
   if (M == 0) return RC_OK;
-  rmsnorm_rope_kernel<<<dim3(M, n_tensors), kRowThreads, 0, stream>>>(a);
-  return rc::check_launch("rc_rmsnorm_rope");
+  return rc::check_launch(
+      rc::launch_pdl(rmsnorm_rope_kernel, dim3(M, n_tensors), dim3(kRowThreads), 0, stream, a),
+      "rc_rmsnorm_rope");
 }
 
 int rc_temporal_rope(const void* x, long long ldx, void* out, long long ldo, const int* positions,
@@ -478,10 +490,11 @@ int rc_temporal_rope(const void* x, long long ldx, void* out, long long ldo, con
   if (rows == 0) return RC_OK;
   if (reinterpret_cast<uintptr_t>(x) % 4 || reinterpret_cast<uintptr_t>(out) % 4 || ldx % 2 || ldo % 2)
     return rc::set_error(RC_ERR_ARG, "rc_temporal_rope: rows must be 4-byte aligned");
-  temporal_rope_kernel<<<grid_for((long long)rows * heads * (d / 2), 256), 256, 0, stream>>>(
-      reinterpret_cast<const __nv_bfloat16*>(x), ldx, reinterpret_cast<__nv_bfloat16*>(out), ldo,
-      positions, cos, sin, rows, span, heads, d, td);
-  return rc::check_launch("rc_temporal_rope");
+  return rc::check_launch(
+      rc::launch_pdl(temporal_rope_kernel, dim3(grid_for((long long)rows * heads * (d / 2), 256)), dim3(256), 0,
+                     stream, reinterpret_cast<const __nv_bfloat16*>(x), ldx,
+                     reinterpret_cast<__nv_bfloat16*>(out), ldo, positions, cos, sin, rows, span, heads, d, td),
+      "rc_temporal_rope");
 }
 
 // Copy n_planes retained planes of `span` rows from the block's K/V
@@ -511,8 +524,9 @@ int rc_kv_commit(const void* src_k, const void* src_v, long long src_ld_bytes, v
   a.n = n_planes;
   a.span = span;
   a.row_bytes = row_bytes;
-  kv_commit_kernel<<<grid_for(2LL * n_planes * span * (row_bytes / 16), 256), 256, 0, stream>>>(a);
-  return rc::check_launch("rc_kv_commit");
+  return rc::check_launch(rc::launch_pdl(kv_commit_kernel, dim3(grid_for(2LL * n_planes * span * (row_bytes / 16), 256)),
+                                         dim3(256), 0, stream, a),
+                          "rc_kv_commit");
 }
 
 // Device-planned variant: plan = [n, (src plane, dst slot) x n] in device
@@ -537,8 +551,10 @@ int rc_kv_commit_planned(const void* src_k, const void* src_v, long long src_ld_
   a.n = max_planes;
   a.span = span;
   a.row_bytes = row_bytes;
-  kv_commit_planned_kernel<<<grid_for(2LL * max_planes * span * (row_bytes / 16), 256), 256, 0, stream>>>(a, plan);
-  return rc::check_launch("rc_kv_commit_planned");
+  return rc::check_launch(
+      rc::launch_pdl(kv_commit_planned_kernel, dim3(grid_for(2LL * max_planes * span * (row_bytes / 16), 256)),
+                     dim3(256), 0, stream, a, plan),
+      "rc_kv_commit_planned");
 }
 
 }  // extern "C"

@@ -22,6 +22,8 @@ __global__ void __launch_bounds__(kQThreads)
 nvfp4_quantize_kernel(const __nv_bfloat16* __restrict__ x, int M, int K, long long ldx, float g,
                       uint8_t* __restrict__ codes, uint8_t* __restrict__ scales) {
   __shared__ __align__(16) uint8_t s_line[32][16];
+  rc::pdl_trigger();
+  rc::pdl_wait();
   const int nkb = K >> 4;
   const int katoms = (nkb + 3) >> 2;
   const int kt = blockIdx.x;
@@ -71,6 +73,8 @@ nvfp4_quantize_kernel(const __nv_bfloat16* __restrict__ x, int M, int K, long lo
 // ---------------------------------------------------------------- FP8
 __global__ void absmax_bf16_kernel(const __nv_bfloat16* __restrict__ x, int M, int K, long long ldx,
                                    unsigned int* __restrict__ amax_bits) {
+  rc::pdl_trigger();
+  rc::pdl_wait();
   float m = 0.0f;
   const int kv = K >> 3;  // uint4 per row
   const long long total = (long long)M * kv;
@@ -96,6 +100,8 @@ __global__ void absmax_bf16_kernel(const __nv_bfloat16* __restrict__ x, int M, i
 __global__ void fp8_quantize_kernel(const __nv_bfloat16* __restrict__ x, int M, int K, long long ldx,
                                     const unsigned int* __restrict__ amax_bits,
                                     float* __restrict__ scale_out, uint8_t* __restrict__ q) {
+  rc::pdl_trigger();
+  rc::pdl_wait();
   float amax = __uint_as_float(*amax_bits);
   amax = amax < 1e-12f ? 1e-12f : amax;         // clamp_min(1e-12); NaN passes through
   const float scale = __fdiv_rn(amax, 448.0f);
@@ -146,9 +152,10 @@ int rc_nvfp4_quantize(const void* x, int M, int K, long long ldx, float global_s
   if (M == 0) return RC_OK;
   const int nkb = K / 16;
   dim3 grid((nkb + 3) / 4, (M + kQRows - 1) / kQRows);
-  nvfp4_quantize_kernel<<<grid, kQThreads, 0, stream>>>(
-      reinterpret_cast<const __nv_bfloat16*>(x), M, K, ldx, global_scale, codes, scales_swizzled);
-  return rc::check_launch("rc_nvfp4_quantize");
+  return rc::check_launch(
+      rc::launch_pdl(nvfp4_quantize_kernel, grid, dim3(kQThreads), 0, stream,
+                     reinterpret_cast<const __nv_bfloat16*>(x), M, K, ldx, global_scale, codes, scales_swizzled),
+      "rc_nvfp4_quantize");
 }
 
 // amax_scratch: one 32-bit device word, overwritten by this call.
@@ -165,13 +172,14 @@ int rc_fp8_quantize(const void* x, int M, int K, long long ldx, unsigned int* am
     return rc::set_error(RC_ERR_CUDA, "rc_fp8_quantize: memset failed");
   if (M == 0) return RC_OK;
   const long long work = (long long)M * (K / 8);
-  absmax_bf16_kernel<<<grid_for(work, 256), 256, 0, stream>>>(
-      reinterpret_cast<const __nv_bfloat16*>(x), M, K, ldx, amax_scratch);
-  int rc_ = rc::check_launch("rc_fp8_quantize(amax)");
+  int rc_ = rc::check_launch(rc::launch_pdl(absmax_bf16_kernel, dim3(grid_for(work, 256)), dim3(256), 0, stream,
+                                            reinterpret_cast<const __nv_bfloat16*>(x), M, K, ldx, amax_scratch),
+                             "rc_fp8_quantize(amax)");
   if (rc_) return rc_;
-  fp8_quantize_kernel<<<grid_for(work, 256), 256, 0, stream>>>(
-      reinterpret_cast<const __nv_bfloat16*>(x), M, K, ldx, amax_scratch, scale_out, q);
-  return rc::check_launch("rc_fp8_quantize");
+  return rc::check_launch(rc::launch_pdl(fp8_quantize_kernel, dim3(grid_for(work, 256)), dim3(256), 0, stream,
+                                         reinterpret_cast<const __nv_bfloat16*>(x), M, K, ldx,
+                                         static_cast<const unsigned int*>(amax_scratch), scale_out, q),
+                          "rc_fp8_quantize");
 }
 
 }  // extern "C"

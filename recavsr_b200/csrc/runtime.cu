@@ -31,6 +31,14 @@ int check_launch(const char* what) {
   return RC_OK;
 }
 
+int check_launch(cudaError_t launched, const char* what) {
+  if (launched != cudaSuccess) {
+    cudaGetLastError();   // clear the sticky-free launch error
+    return set_error(RC_ERR_CUDA, "%s: launch failed: %s", what, cudaGetErrorString(launched));
+  }
+  return check_launch(what);
+}
+
 int encode_tmap(CUtensorMap* map, CUtensorMapDataType dtype, int rank, void* base,
                 const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,
                 CUtensorMapSwizzle swizzle, const char* what) {
