@@ -121,7 +121,8 @@ int rc_kv_commit_planned(const void* src_k, const void* src_v, long long src_ld_
  * out_codes/out_scales (optional, B = 1): the output also NVFP4-quantized as
  * rc_nvfp4_quantize would quantize it ([QT*H*W, heads*d/2] codes + swizzled
  * scales), ready for the o-proj GEMM. workspace: caller-provided device scratch
- * of rc_paired_attention_workspace(...) bytes (rotated K planes). d = 128. */
+ * of rc_paired_attention_workspace(...) bytes (rotated K planes, then about
+ * 10.6 MB of tail-split partials and counters). d = 128. */
 long long rc_paired_attention_workspace(int B, int QT, int CAP, int H, int W, int heads, int d);
 int rc_paired_attention(const void* q, const void* ck, const void* cv, const void* pk, const void* pv,
                         const long long* strides, const int* slots, const int* past_positions,

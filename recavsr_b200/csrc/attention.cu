@@ -19,7 +19,11 @@
 //  1. rope_gather: temporally rotated copies of the current K frames and the
 //     routed past K planes into a caller-provided workspace (the slot
 //     indirection is applied here, so the attention kernel reads K densely).
-//  2. attention: one CTA per (128-query tile, head).
+//  2. attention: one CTA per (128-query tile, head) = one unit. With one CTA
+//     per SM the units run in waves; the units of the last, partial wave are
+//     split over their key tiles into up to four pieces (CTAs) that write
+//     unnormalised partials, and the last piece of a unit to finish merges
+//     them (flash-decoding style split-K, applied to the tail wave only).
 //     Warp 0 = TMA producer: K tiles (workspace) and V tiles (read in place
 //     from the cache slot / current frame) of 128 keys in a 4-stage K ring and
 //     a 3-stage V ring, K three tiles ahead of V.
@@ -45,6 +49,8 @@
 //   tail reads as zeros). Local mode: a query tile = 2 frames x 8 x 8 tokens, a
 //   key tile = an 8 x 16 box of the union of the tile's windows (5-D TMA
 //   view); slot 0 / 1 take its box rows 0-3 / 4-7.
+#include <stdlib.h>
+
 #include <mutex>
 
 #include "sm100.cuh"
@@ -83,7 +89,21 @@ struct AttnParams {
   long long out_ld;             // elements between tokens
   uint8_t* q_codes;             // optional NVFP4 output [Tq, heads*d/2]
   uint8_t* q_sf;                // its swizzled scales (heads*d as K)
+  // Tail split: units (query tile, head) [0, n_regular) run whole, one CTA
+  // each; every later unit runs as `split` CTAs ("pieces"), each over a
+  // contiguous range of its key tiles. A piece writes its unnormalised partial
+  // (O, running max m, sum l) to `part`; the last piece of a unit to finish
+  // (per-unit arrival counter) merges them into the outputs.
+  int n_regular, split;
+  float* part;                  // [pieces][kPartFloats]
+  int* counters;                // [tail units], zero at launch
 };
+
+// Partial of one piece: O as [d/4][128 rows][4] floats (a warp's float4 stores
+// of one column quad are contiguous), then m[128] and l[128] (log2 units).
+constexpr int kPartO = kD * kBM, kPartFloats = kPartO + 2 * kBM;
+constexpr int kMaxSplit = 4;          // pieces per unit
+constexpr int kMaxPieces = 160;       // pieces per launch (>= SMs of a B200)
 
 struct SmemLayout {
   static constexpr int kChunk = 128 * 128;           // 128 rows x 128 bytes
@@ -126,6 +146,12 @@ struct TileIter {
 // the box origin (ky0, kx0) (local).
 struct TileCursor {
   int plane = 0, tx = 0, ty = 0;
+  __device__ void seek(int t, int nx, int ny) {   // the t-th tile of the enumeration
+    plane = t / (nx * ny);
+    const int r = t - plane * nx * ny;
+    ty = r / nx;
+    tx = r - ty * nx;
+  }
   __device__ void advance(int nx, int ny) {
     if (++tx == nx) {
       tx = 0;
@@ -200,7 +226,7 @@ __device__ __forceinline__ void rotate_pairs(uint32_t (&w)[N], int pair0, int td
     const int pr = pair0 + j;
     if (2 * pr < td) {
       const float e = __uint_as_float(w[j] << 16), o = __uint_as_float(w[j] & 0xffff0000u);
-      const float c = __ldg(cs + pr), s = __ldg(sn + pr);
+      const float c = rc::ld_in(cs + pr), s = rc::ld_in(sn + pr);
       w[j] = pack_bf16x2(__fsub_rn(__fmul_rn(e, c), __fmul_rn(o, s)),
                          __fadd_rn(__fmul_rn(e, s), __fmul_rn(o, c)));
     }
@@ -234,8 +260,16 @@ attention_kernel(const __grid_constant__ CUtensorMap tm_k,
   rc::pdl_trigger();
   rc::pdl_wait();   // the previous kernel's outputs are visible from here
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int head = blockIdx.y;
-  const int qtile = blockIdx.x;
+  // Unit (query tile, head) and key-tile piece of this CTA.
+  int unit = blockIdx.x, piece = 0, nsplit = 1;
+  if (unit >= p.n_regular) {
+    const int t = unit - p.n_regular;
+    unit = p.n_regular + t / p.split;
+    piece = t - (unit - p.n_regular) * p.split;
+    nsplit = p.split;
+  }
+  const int head = unit / p.n_qtiles;
+  const int qtile = unit - head * p.n_qtiles;
 
   // Query tile origin.
   int q_row0 = 0, qf0 = 0, qy0 = 0, qx0 = 0;
@@ -286,7 +320,10 @@ attention_kernel(const __grid_constant__ CUtensorMap tm_k,
   const int nplanes = *s_nplanes;
   TileIter it(p, qy0, qx0);
   const int nx = it.tiles_x(), ny = it.tiles_y();
-  const int n_tiles = nplanes * nx * ny;
+  // This CTA's key tiles: [t0, t0 + n_tiles) of the unit's nplanes * nx * ny.
+  const int n_all = nplanes * nx * ny;
+  const int t0 = piece * n_all / nsplit;
+  const int n_tiles = (piece + 1) * n_all / nsplit - t0;
 
   auto fail = [&](unsigned int site) {
     if (!*abort_flag) rc::device_fail(kKernAttention, site);
@@ -304,7 +341,9 @@ attention_kernel(const __grid_constant__ CUtensorMap tm_k,
       // K runs three tiles ahead of V: Q K^T of a tile comes a pipeline step
       // before its P.V, and a K stage frees up as soon as both slots' Q K^T on
       // it finish (slot 1 trails slot 0 by about one block).
-      TileCursor kc, vc;
+      TileCursor kc;
+      kc.seek(t0, nx, ny);
+      TileCursor vc = kc;
       Ring kr, vr;
       int nk = 0, nv = 0;
       bool ok = true;
@@ -444,7 +483,7 @@ attention_kernel(const __grid_constant__ CUtensorMap tm_k,
                                    : nullptr;
 #pragma unroll
       for (int u = 0; u < 8; ++u) {
-        const uint4 w = src ? __ldg(src + u) : make_uint4(0, 0, 0, 0);
+        const uint4 w = src ? rc::ld_in(src + u) : make_uint4(0, 0, 0, 0);
         qv[4 * u] = w.x;
         qv[4 * u + 1] = w.y;
         qv[4 * u + 2] = w.z;
@@ -465,6 +504,7 @@ attention_kernel(const __grid_constant__ CUtensorMap tm_k,
     const uint32_t t_o = tmem + kTmO + x * kD + lane_off;
     float m_used = -INFINITY, l = 0.f;
     TileCursor cur;
+    cur.seek(t0, nx, ny);
     for (int i = 0; i < n_tiles && ok; ++i, cur.advance(nx, ny)) {
       int a, b;
       cur.origin(it, a, b);
@@ -589,50 +629,144 @@ attention_kernel(const __grid_constant__ CUtensorMap tm_k,
     sm100::tc_fence_after();
     const float m0 = red[0 * 128 + r], l0 = red[1 * 128 + r];
     const float m1 = red[2 * 128 + r], l1 = red[3 * 128 + r];
-    if (fin && m0 == m0 && m1 == m1) {
-      const float m = fmaxf(m0, m1);
-      const float a0 = m0 == -INFINITY ? 0.f : fast_exp2(m0 - m);
-      const float a1 = m1 == -INFINITY ? 0.f : fast_exp2(m1 - m);
-      const float inv = 1.0f / fmaxf(__fadd_rn(__fmul_rn(l0, a0), __fmul_rn(l1, a1)), 1e-20f);
-      const float2 c0 = make_float2(a0 * inv, a0 * inv), c1 = make_float2(a1 * inv, a1 * inv);
-      __nv_bfloat16* dst = (qrow >= 0 && p.out) ? p.out + (size_t)qrow * p.out_ld + (size_t)head * kD : nullptr;
-      const int katoms = (p.heads * kD) >> 6;
-      const uint32_t o0 = tmem + kTmO + lane_off, o1 = tmem + kTmO + kD + lane_off;
-#pragma unroll 1
-      for (int c = x * 64; c < x * 64 + 64; c += 16) {
-        uint32_t w0[16], w1[16];
-        sm100::tmem_ld16(o0 + c, w0);
-        sm100::tmem_ld16(o1 + c, w1);
-        sm100::tmem_ld_wait();
-        float y[16];
-        uint32_t w[8];
+    const bool valid = fin && m0 == m0 && m1 == m1;
+    const float m = valid ? fmaxf(m0, m1) : -INFINITY;
+    const float a0 = (!valid || m0 == -INFINITY) ? 0.f : fast_exp2(m0 - m);
+    const float a1 = (!valid || m1 == -INFINITY) ? 0.f : fast_exp2(m1 - m);
+    const float lsum = valid ? __fadd_rn(__fmul_rn(l0, a0), __fmul_rn(l1, a1)) : 0.f;
+    const uint32_t o0 = tmem + kTmO + lane_off, o1 = tmem + kTmO + kD + lane_off;
+    __nv_bfloat16* dst = (qrow >= 0 && p.out) ? p.out + (size_t)qrow * p.out_ld + (size_t)head * kD : nullptr;
+    const int katoms = (p.heads * kD) >> 6;
+    // Writes output columns [c, c + 16) of this row: bf16, and NVFP4 of the
+    // bf16 values (16 columns = one block) for the o-proj GEMM.
+    auto emit = [&](int c, const float (&o)[16]) {
+      float y[16];
+      uint32_t w[8];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const float2 s0 = make_float2(__uint_as_float(w0[2 * j]), __uint_as_float(w0[2 * j + 1]));
-          const float2 s1 = make_float2(__uint_as_float(w1[2 * j]), __uint_as_float(w1[2 * j + 1]));
-          const float2 o = __ffma2_rn(s1, c1, __fmul2_rn(s0, c0));
-          w[j] = pack_bf16x2(o.x, o.y);
-          y[2 * j] = __uint_as_float(w[j] << 16);
-          y[2 * j + 1] = __uint_as_float(w[j] & 0xffff0000u);
+      for (int j = 0; j < 8; ++j) {
+        w[j] = pack_bf16x2(o[2 * j], o[2 * j + 1]);
+        y[2 * j] = __uint_as_float(w[j] << 16);
+        y[2 * j + 1] = __uint_as_float(w[j] & 0xffff0000u);
+      }
+      if (dst) {
+        reinterpret_cast<uint4*>(dst + c)[0] = make_uint4(w[0], w[1], w[2], w[3]);
+        reinterpret_cast<uint4*>(dst + c)[1] = make_uint4(w[4], w[5], w[6], w[7]);
+      }
+      if (p.q_codes && qrow >= 0) {
+        uint8_t sfb;
+        uint32_t lo, hi;
+        rc::nvfp4_encode16(y, sfb, lo, hi);
+        const int kb = (head * kD + c) >> 4;
+        *reinterpret_cast<uint2*>(p.q_codes + (size_t)qrow * (p.heads * kD / 2) + (kb << 3)) = make_uint2(lo, hi);
+        p.q_sf[rc::sf_offset(qrow, kb, katoms)] = sfb;
+      }
+    };
+    if (nsplit == 1) {
+      if (valid) {
+        const float inv = 1.0f / fmaxf(lsum, 1e-20f);
+        const float2 c0 = make_float2(a0 * inv, a0 * inv), c1 = make_float2(a1 * inv, a1 * inv);
+#pragma unroll 1
+        for (int c = x * 64; c < x * 64 + 64; c += 16) {
+          uint32_t w0[16], w1[16];
+          sm100::tmem_ld16(o0 + c, w0);
+          sm100::tmem_ld16(o1 + c, w1);
+          sm100::tmem_ld_wait();
+          float o[16];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const float2 s0 = make_float2(__uint_as_float(w0[2 * j]), __uint_as_float(w0[2 * j + 1]));
+            const float2 s1 = make_float2(__uint_as_float(w1[2 * j]), __uint_as_float(w1[2 * j + 1]));
+            const float2 v = __ffma2_rn(s1, c1, __fmul2_rn(s0, c0));
+            o[2 * j] = v.x;
+            o[2 * j + 1] = v.y;
+          }
+          emit(c, o);
         }
-        if (dst) {
-          reinterpret_cast<uint4*>(dst + c)[0] = make_uint4(w[0], w[1], w[2], w[3]);
-          reinterpret_cast<uint4*>(dst + c)[1] = make_uint4(w[4], w[5], w[6], w[7]);
+      }
+    } else {
+      // Piece of a split unit: store the partial (O_0 a_0 + O_1 a_1, m, l);
+      // the last piece to arrive merges all of the unit's partials:
+      // out = sum_q O_q 2^(m_q - M) / sum_q l_q 2^(m_q - M), M = max_q m_q.
+      // A piece without keys (or whose rows saw only masked keys) stores
+      // m = -inf and no O.
+      const int tail_unit = unit - p.n_regular;
+      float* mine = p.part + (size_t)(tail_unit * nsplit + piece) * kPartFloats;
+      if (m > -INFINITY) {
+        const float2 c0 = make_float2(a0, a0), c1 = make_float2(a1, a1);
+#pragma unroll 1
+        for (int c = x * 64; c < x * 64 + 64; c += 16) {
+          uint32_t w0[16], w1[16];
+          sm100::tmem_ld16(o0 + c, w0);
+          sm100::tmem_ld16(o1 + c, w1);
+          sm100::tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            float4 v;
+            float2 s0 = make_float2(__uint_as_float(w0[4 * j]), __uint_as_float(w0[4 * j + 1]));
+            float2 s1 = make_float2(__uint_as_float(w1[4 * j]), __uint_as_float(w1[4 * j + 1]));
+            const float2 lo = __ffma2_rn(s1, c1, __fmul2_rn(s0, c0));
+            s0 = make_float2(__uint_as_float(w0[4 * j + 2]), __uint_as_float(w0[4 * j + 3]));
+            s1 = make_float2(__uint_as_float(w1[4 * j + 2]), __uint_as_float(w1[4 * j + 3]));
+            const float2 hi = __ffma2_rn(s1, c1, __fmul2_rn(s0, c0));
+            v = make_float4(lo.x, lo.y, hi.x, hi.y);
+            __stcg(reinterpret_cast<float4*>(mine) + ((c >> 2) + j) * kBM + r, v);
+          }
         }
-        if (p.q_codes && qrow >= 0) {
-          // NVFP4 of the bf16 output (16 columns = one block), for the o-proj GEMM.
-          uint8_t sfb;
-          uint32_t lo, hi;
-          rc::nvfp4_encode16(y, sfb, lo, hi);
-          const int kb = (head * kD + c) >> 4;
-          *reinterpret_cast<uint2*>(p.q_codes + (size_t)qrow * (p.heads * kD / 2) + (kb << 3)) = make_uint2(lo, hi);
-          p.q_sf[rc::sf_offset(qrow, kb, katoms)] = sfb;
+      }
+      if (x == 0) {
+        __stcg(mine + kPartO + r, m);
+        __stcg(mine + kPartO + kBM + r, lsum);
+      }
+      // Release the partial, then count the arrival (one thread per CTA).
+      __threadfence();
+      int* s_last = reinterpret_cast<int*>(smem + L::offMisc + 12);
+      asm volatile("bar.sync 5, 256;" ::: "memory");
+      if (threadIdx.x == 64) *s_last = atomicAdd(&p.counters[tail_unit], 1) == nsplit - 1;
+      asm volatile("bar.sync 5, 256;" ::: "memory");
+      if (*s_last) {
+        __threadfence();   // acquire: the other pieces' partials are visible from here
+        const float* base = p.part + (size_t)tail_unit * nsplit * kPartFloats;
+        float mq[kMaxSplit], cq[kMaxSplit];
+        float mm = -INFINITY;
+#pragma unroll
+        for (int q = 0; q < kMaxSplit; ++q) {
+          mq[q] = q < nsplit ? __ldcg(base + q * kPartFloats + kPartO + r) : -INFINITY;
+          mm = fmaxf(mm, mq[q]);
+        }
+        float ls = 0.f;
+#pragma unroll
+        for (int q = 0; q < kMaxSplit; ++q) {
+          cq[q] = mq[q] == -INFINITY ? 0.f : fast_exp2(mq[q] - mm);
+          if (mq[q] > -INFINITY) ls = __fadd_rn(ls, __fmul_rn(__ldcg(base + q * kPartFloats + kPartO + kBM + r), cq[q]));
+        }
+        const float inv = 1.0f / fmaxf(ls, 1e-20f);
+#pragma unroll
+        for (int q = 0; q < kMaxSplit; ++q) cq[q] *= inv;
+#pragma unroll 1
+        for (int c = x * 64; c < x * 64 + 64; c += 16) {
+          float o[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) o[j] = 0.f;
+#pragma unroll
+          for (int q = 0; q < kMaxSplit; ++q) {
+            if (mq[q] == -INFINITY) continue;
+            const float4* src = reinterpret_cast<const float4*>(base + q * kPartFloats) + (c >> 2) * kBM + r;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const float4 v = __ldcg(src + j * kBM);
+              o[4 * j] = fmaf(v.x, cq[q], o[4 * j]);
+              o[4 * j + 1] = fmaf(v.y, cq[q], o[4 * j + 1]);
+              o[4 * j + 2] = fmaf(v.z, cq[q], o[4 * j + 2]);
+              o[4 * j + 3] = fmaf(v.w, cq[q], o[4 * j + 3]);
+            }
+          }
+          emit(c, o);
         }
       }
     }
   }
   // Zero the scale bytes of the padding rows (to a multiple of 128) for this head.
-  if (p.q_sf && qtile == 0) {
+  if (p.q_sf && qtile == 0 && piece == 0) {
     const int pm = (p.Tq + 127) / 128 * 128, katoms = (p.heads * kD) >> 6;
     for (int i = threadIdx.x; i < (pm - p.Tq) * 8; i += blockDim.x)
       p.q_sf[rc::sf_offset(p.Tq + i / 8, head * 8 + i % 8, katoms)] = 0;
@@ -655,6 +789,8 @@ struct GatherParams {
   const float* cos; const float* sin;                 // [*, td/2]
   __nv_bfloat16* k_out;                               // [(CAP+QT)*T, heads*d]
   int T, QT, CAP, hd, td, d;
+  int* counters;                                      // tail-split arrival counters to zero
+  int n_counters;
 };
 
 // One thread = 8 consecutive elements of one token row (16 bytes); each
@@ -689,6 +825,8 @@ __device__ __forceinline__ bool gather_src(const GatherParams& g, long long i, i
 __global__ void rope_gather_kernel(GatherParams g) {
   rc::pdl_trigger();
   rc::pdl_wait();
+  if (blockIdx.x == 0)
+    for (int i = threadIdx.x; i < g.n_counters; i += blockDim.x) g.counters[i] = 0;
   const int vec = g.hd >> 3;
   const long long total = (long long)(g.CAP + g.QT) * g.T * vec;
   const long long stride = (long long)gridDim.x * blockDim.x;
@@ -744,6 +882,37 @@ int make_view(CUtensorMap* m, const void* base, long long ld, long long hs, int 
 
 bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
+// Workspace tail after the rotated K planes: the pieces' partials, then one
+// arrival counter per split unit (at most one per piece).
+constexpr long long kSplitBytes = (long long)kMaxPieces * kPartFloats * 4 + kMaxPieces * 4;
+long long split_offset(long long planes_bytes) { return (planes_bytes + 255) / 256 * 256; }
+
+// Tail split of `units` equal units over the SMs (one CTA per SM at a time):
+// the units of the last, partial wave run as `split` pieces each, so that wave
+// ends about `split` times sooner. `max_tiles` bounds the key tiles of a unit.
+// RECAVSR_ATTN_SPLIT=n caps the pieces per unit (1 = no split).
+void plan_split(int units, int max_tiles, bool can_split, int& n_regular, int& split) {
+  static int cap = -1;
+  if (cap < 0) {
+    const char* e = getenv("RECAVSR_ATTN_SPLIT");
+    cap = e ? atoi(e) : kMaxSplit;
+    cap = cap < 1 ? 1 : (cap > kMaxSplit ? kMaxSplit : cap);
+  }
+  n_regular = units;
+  split = 1;
+  if (!can_split) return;
+  const int sms = rc::sm_count();
+  const int tail = units % sms;
+  if (!tail) return;
+  int s = sms / tail;
+  s = s < cap ? s : cap;
+  s = s < max_tiles / 2 ? s : max_tiles / 2;   // at least two key tiles per piece
+  while (s > 1 && tail * s > kMaxPieces) --s;
+  if (s < 2) return;
+  n_regular = units - tail;
+  split = s;
+}
+
 int g_attr_set = 0;
 
 int ensure_smem_attr(const char* what) {
@@ -777,7 +946,7 @@ extern "C" {
 
 long long rc_paired_attention_workspace(int B, int QT, int CAP, int H, int W, int heads, int d) {
   if (B <= 0 || QT <= 0 || CAP < 0 || H <= 0 || W <= 0 || heads <= 0 || d <= 0) return -1;
-  return (long long)B * (QT + CAP) * H * W * heads * d * 2;
+  return split_offset((long long)B * (QT + CAP) * H * W * heads * d * 2) + kSplitBytes;
 }
 
 // strides[15]: (batch, token, head) strides in elements of q, ck, cv, pk, pv
@@ -823,6 +992,10 @@ int rc_paired_attention(const void* q, const void* ck, const void* cv, const voi
   if (r) return r;
   const long long hd = (long long)heads * d;
   const long long per_batch = (long long)(QT + CAP) * T * hd;
+  // Split region (reused by every batch element: the launches are stream-ordered).
+  uint8_t* split_base = reinterpret_cast<uint8_t*>(workspace) + split_offset((long long)B * per_batch * 2);
+  float* part = reinterpret_cast<float*>(split_base);
+  int* counters = reinterpret_cast<int*>(split_base + (long long)kMaxPieces * kPartFloats * 4);
   for (int b = 0; b < B; ++b) {
     __nv_bfloat16* ks = reinterpret_cast<__nv_bfloat16*>(workspace) + b * per_batch;
     const __nv_bfloat16* qb = reinterpret_cast<const __nv_bfloat16*>(q) + b * strides[0];
@@ -831,7 +1004,7 @@ int rc_paired_attention(const void* q, const void* ck, const void* cv, const voi
     const __nv_bfloat16* pkb = CAP ? reinterpret_cast<const __nv_bfloat16*>(pk) + b * strides[9] : nullptr;
     const __nv_bfloat16* pvb = CAP ? reinterpret_cast<const __nv_bfloat16*>(pv) + b * strides[12] : nullptr;
     GatherParams g{ckb, strides[4], strides[5], pkb, strides[10], strides[11], slots, past_positions,
-                   query_positions, cos, sin, ks, T, QT, CAP, (int)hd, td, d};
+                   query_positions, cos, sin, ks, T, QT, CAP, (int)hd, td, d, counters, kMaxPieces};
     const long long work = (long long)(QT + CAP) * T * (hd / 8);
     long long blocks = (work + 255) / 256;
     if (blocks > 148LL * 16) blocks = 148LL * 16;
@@ -867,7 +1040,15 @@ int rc_paired_attention(const void* q, const void* ck, const void* cv, const voi
       p.qtiles_y = (H + kLocalQH - 1) / kLocalQH;
       p.n_qtiles = (QT / 2) * p.qtiles_x * p.qtiles_y;
     }
-    dim3 grid(p.n_qtiles, heads);
+    // Key tiles of a unit: every visible plane x the tiles of its key rectangle.
+    const int per_plane = !local ? (T + kBN - 1) / kBN
+                                 : ((wh + kLocalQH - 1 + kLocalKH - 1) / kLocalKH) *
+                                       ((ww + kLocalQW - 1 + kLocalKW - 1) / kLocalKW);
+    const int units = p.n_qtiles * heads;
+    plan_split(units, (CAP + QT) * per_plane, true, p.n_regular, p.split);
+    p.part = part;
+    p.counters = counters;
+    dim3 grid(p.n_regular + (units - p.n_regular) * p.split);
     if ((r = rc::check_launch(
              rc::launch_pdl(attention_kernel, grid, dim3(kThreads), SmemLayout::kAlloc, stream, tk, tpv, tcv, p),
              what)))
@@ -921,7 +1102,9 @@ int rc_cross_attention(const void* q, const void* k, const void* v, const long l
     p.q_codes = out_codes;
     p.q_sf = out_scales;
     p.n_qtiles = (Nq + kBM - 1) / kBM;
-    dim3 grid(p.n_qtiles, heads);
+    p.n_regular = p.n_qtiles * heads;   // no workspace: no tail split
+    p.split = 1;
+    dim3 grid(p.n_regular);
     if ((r = rc::check_launch(
              rc::launch_pdl(attention_kernel, grid, dim3(kThreads), SmemLayout::kAlloc, stream, tk, tv, tv, p),
              what)))

@@ -49,6 +49,7 @@ namespace rc {
 int set_error(int code, const char* fmt, ...);
 int check_launch(const char* what);
 int check_launch(cudaError_t launched, const char* what);   // result of launch_pdl
+int sm_count();   // streaming multiprocessors of the current device (cached per device)
 
 // cuTensorMapEncodeTiled through the runtime's driver entry point (no -lcuda).
 // dims/strides: innermost first; strides are in bytes for dims 1..rank-1.
@@ -66,6 +67,39 @@ int encode_tmap(CUtensorMap* map, CUtensorMapDataType dtype, int rank, void* bas
 // the ordering is transitive along the stream.
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// Global loads of kernel inputs. With programmatic dependent launch a kernel
+// is resident while the kernels before it in the stream still write its
+// inputs, so the read-only non-coherent path (ld.global.nc, which __ldg and
+// `const __restrict__` pointers select) does not apply: it is defined only for
+// data that nothing writes during the kernel's lifetime, and the compiler may
+// schedule such loads ahead of pdl_wait(). These are ordinary coherent loads,
+// kept in program order after pdl_wait() by `volatile`.
+__device__ __forceinline__ uint4 ld_in(const uint4* p) {
+  uint4 v;
+  asm volatile("ld.global.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+  return v;
+}
+__device__ __forceinline__ float4 ld_in(const float4* p) {
+  float4 v;
+  asm volatile("ld.global.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "l"(p));
+  return v;
+}
+__device__ __forceinline__ float ld_in(const float* p) {
+  float v;
+  asm volatile("ld.global.f32 %0, [%1];" : "=f"(v) : "l"(p));
+  return v;
+}
+__device__ __forceinline__ int ld_in(const int* p) {
+  int v;
+  asm volatile("ld.global.s32 %0, [%1];" : "=r"(v) : "l"(p));
+  return v;
+}
+__device__ __forceinline__ unsigned int ld_in(const unsigned int* p) {
+  unsigned int v;
+  asm volatile("ld.global.u32 %0, [%1];" : "=r"(v) : "l"(p));
+  return v;
+}
 
 // Launch `kernel` on `stream` with programmatic stream serialization allowed.
 template <typename... KArgs, typename... Args>

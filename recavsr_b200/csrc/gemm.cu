@@ -380,7 +380,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
           uint32_t bw[8];
           if (p.bias) {
             const uint4* bp = reinterpret_cast<const uint4*>(p.bias + n0);
-            const uint4 b0 = __ldg(bp), b1 = __ldg(bp + 1);
+            const uint4 b0 = rc::ld_in(bp), b1 = rc::ld_in(bp + 1);
             bw[0] = b0.x; bw[1] = b0.y; bw[2] = b0.z; bw[3] = b0.w;
             bw[4] = b1.x; bw[5] = b1.y; bw[6] = b1.z; bw[7] = b1.w;
           }
@@ -408,7 +408,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
             const float4* gp = reinterpret_cast<const float4*>(p.gate + n0);
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
-              const float4 g4 = __ldg(gp + j);
+              const float4 g4 = rc::ld_in(gp + j);
               gt[4 * j] = g4.x; gt[4 * j + 1] = g4.y; gt[4 * j + 2] = g4.z; gt[4 * j + 3] = g4.w;
             }
           }
@@ -468,17 +468,6 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
   }
 }
 
-int g_num_sms = 0;
-int num_sms() {
-  if (!g_num_sms) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
-    if (g_num_sms <= 0) g_num_sms = 148;
-  }
-  return g_num_sms;
-}
-
 template <int KIND, int BN, int STAGES, int EPI>
 int launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, cudaStream_t stream,
            const char* what) {
@@ -491,7 +480,7 @@ int launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, cu
     attr_set = true;
   }
   const int tiles = p.m_blocks * p.n_blocks;
-  const int grid = tiles < num_sms() ? tiles : num_sms();
+  const int grid = tiles < rc::sm_count() ? tiles : rc::sm_count();
   return rc::check_launch(rc::launch_pdl(kern, grid, dim3(gemm_threads<EPI>()), S::kAlloc, stream, ta, tb, p), what);
 }
 
@@ -506,8 +495,6 @@ int dispatch_epi(int epi, const CUtensorMap& ta, const CUtensorMap& tb, const Ge
   }
   return rc::set_error(RC_ERR_ARG, "%s: unknown epilogue %d", what, epi);
 }
-
-int num_sms();
 
 // Tile width. 128 x 256 tiles (single accumulator, register-drained
 // epilogue) move a third less operand data per FLOP than 128 x 128 tiles, but

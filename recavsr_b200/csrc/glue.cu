@@ -62,7 +62,7 @@ struct LnArgs {
 
 __device__ __forceinline__ void loadf8(const float* p, float (&f)[8]) {
   const float4* q = reinterpret_cast<const float4*>(p);
-  const float4 a = __ldg(q), b = __ldg(q + 1);
+  const float4 a = rc::ld_in(q), b = rc::ld_in(q + 1);
   f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w; f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
 }
 
@@ -146,7 +146,7 @@ __global__ void __launch_bounds__(kRowThreads, 6) ln_modulate_kernel(LnArgs a) {
 #pragma unroll
   for (int i = 0; i < kRowChunks; ++i) {
     const int c = t + i * kRowThreads;
-    raw[i] = c < nch ? __ldg(reinterpret_cast<const uint4*>(a.x + (size_t)row * a.ldx) + c)
+    raw[i] = c < nch ? rc::ld_in(reinterpret_cast<const uint4*>(a.x + (size_t)row * a.ldx) + c)
                      : make_uint4(0, 0, 0, 0);
   }
   float s = 0.f;
@@ -185,8 +185,8 @@ __global__ void __launch_bounds__(kRowThreads, 6) ln_modulate_kernel(LnArgs a) {
     unpack8_fresh(raw[i], f);
     if (live) {
       float w[8], b[8], sh[8], sc[8];
-      if (a.weight) unpack8(__ldg(reinterpret_cast<const uint4*>(a.weight + n0)), w);
-      if (a.bias) unpack8(__ldg(reinterpret_cast<const uint4*>(a.bias + n0)), b);
+      if (a.weight) unpack8(rc::ld_in(reinterpret_cast<const uint4*>(a.weight + n0)), w);
+      if (a.bias) unpack8(rc::ld_in(reinterpret_cast<const uint4*>(a.bias + n0)), b);
       if (a.scale) loadf8(a.scale + n0, sc);
       if (a.shift) loadf8(a.shift + n0, sh);
       // fl(fl(x - mean) * rstd), then each affine / modulation step rounded
@@ -243,7 +243,7 @@ __global__ void __launch_bounds__(kRowThreads, 8) rmsnorm_rope_kernel(RmsArgs a)
 #pragma unroll
   for (int i = 0; i < kRowChunks; ++i) {
     const int c = t + i * kRowThreads;
-    raw[i] = c < nch ? __ldg(reinterpret_cast<const uint4*>(xp + (size_t)row * ldx) + c)
+    raw[i] = c < nch ? rc::ld_in(reinterpret_cast<const uint4*>(xp + (size_t)row * ldx) + c)
                      : make_uint4(0, 0, 0, 0);
   }
   const int pos = row % a.span;
@@ -275,7 +275,7 @@ __global__ void __launch_bounds__(kRowThreads, 8) rmsnorm_rope_kernel(RmsArgs a)
     unpack8_fresh(raw[i], f);
     if (w) {
       float wf[8];
-      unpack8(__ldg(reinterpret_cast<const uint4*>(w + n0)), wf);
+      unpack8(rc::ld_in(reinterpret_cast<const uint4*>(w + n0)), wf);
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const float2 y = __fmul2_rn(__fmul2_rn(make_float2(f[2 * j], f[2 * j + 1]), make_float2(r, r)),
@@ -304,10 +304,10 @@ __global__ void __launch_bounds__(kRowThreads, 8) rmsnorm_rope_kernel(RmsArgs a)
 
 // Temporal rotary on the first `td` dims of every head of `planes` planes of
 // `span` tokens; plane p uses position pos[p] (runtime/rope.py:33-47).
-__global__ void temporal_rope_kernel(const __nv_bfloat16* __restrict__ x, long long ldx,
-                                     __nv_bfloat16* __restrict__ out, long long ldo,
-                                     const int* __restrict__ pos, const float* __restrict__ cos,
-                                     const float* __restrict__ sin, int rows, int span, int heads,
+__global__ void temporal_rope_kernel(const __nv_bfloat16* x, long long ldx,
+                                     __nv_bfloat16* out, long long ldo,
+                                     const int* pos, const float* cos,
+                                     const float* sin, int rows, int span, int heads,
                                      int d, int td) {
   rc::pdl_trigger();
   rc::pdl_wait();
@@ -359,7 +359,7 @@ __global__ void kv_commit_kernel(CommitArgs a) {
         a.src[t] + ((long long)a.src_plane[c] * a.span + row) * a.src_ld[t]);
     uint4* dd = reinterpret_cast<uint4*>(
         a.dst[t] + ((long long)a.dst_plane[c] * a.span + row) * a.dst_ld[t]);
-    dd[v] = __ldg(s + v);
+    dd[v] = rc::ld_in(s + v);
   }
 }
 
@@ -368,7 +368,7 @@ __global__ void kv_commit_kernel(CommitArgs a) {
 // graph stays valid while the routing changes between replays.
 constexpr int kCopyUnroll = 4;   // independent 16-byte loads in flight per thread
 
-__global__ void kv_commit_planned_kernel(CommitArgs a, const int* __restrict__ plan) {
+__global__ void kv_commit_planned_kernel(CommitArgs a, const int* plan) {
   rc::pdl_trigger();
   rc::pdl_wait();
   const int n = min(plan[0], a.n);
@@ -393,7 +393,7 @@ __global__ void kv_commit_planned_kernel(CommitArgs a, const int* __restrict__ p
       if (sp < 0 || dp < 0 || dp >= a.dst_plane[0]) continue;   // dst_plane[0] = slot capacity
       const long long q = r % per_plane;
       const long long row = q / vec_per_row, v = q % vec_per_row;
-      val[u] = __ldg(reinterpret_cast<const uint4*>(a.src[t] + ((long long)sp * a.span + row) * a.src_ld[t]) + v);
+      val[u] = rc::ld_in(reinterpret_cast<const uint4*>(a.src[t] + ((long long)sp * a.span + row) * a.src_ld[t]) + v);
       dst[u] = reinterpret_cast<uint4*>(a.dst[t] + ((long long)dp * a.span + row) * a.dst_ld[t]) + v;
     }
 #pragma unroll

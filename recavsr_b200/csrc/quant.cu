@@ -19,8 +19,8 @@ constexpr int kQThreads = 512;    // 128 rows x 4 k-blocks (one 64-column k-atom
 // One thread per 16-element block; the CTA covers one scale atom (128 rows x
 // 4 k-blocks = 512 bytes of scales, written as 32 coalesced 16-byte lines).
 __global__ void __launch_bounds__(kQThreads)
-nvfp4_quantize_kernel(const __nv_bfloat16* __restrict__ x, int M, int K, long long ldx, float g,
-                      uint8_t* __restrict__ codes, uint8_t* __restrict__ scales) {
+nvfp4_quantize_kernel(const __nv_bfloat16* x, int M, int K, long long ldx, float g,
+                      uint8_t* codes, uint8_t* scales) {
   __shared__ __align__(16) uint8_t s_line[32][16];
   rc::pdl_trigger();
   rc::pdl_wait();
@@ -33,7 +33,7 @@ nvfp4_quantize_kernel(const __nv_bfloat16* __restrict__ x, int M, int K, long lo
   uint8_t sf = 0;
   if (row < M && kb < nkb) {
     const uint4* src = reinterpret_cast<const uint4*>(x + (size_t)row * ldx + (size_t)kb * 16);
-    uint4 v0 = __ldg(src), v1 = __ldg(src + 1);
+    uint4 v0 = rc::ld_in(src), v1 = rc::ld_in(src + 1);
     const uint32_t w[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
     float f[16];
 #pragma unroll
@@ -71,8 +71,8 @@ nvfp4_quantize_kernel(const __nv_bfloat16* __restrict__ x, int M, int K, long lo
 }
 
 // ---------------------------------------------------------------- FP8
-__global__ void absmax_bf16_kernel(const __nv_bfloat16* __restrict__ x, int M, int K, long long ldx,
-                                   unsigned int* __restrict__ amax_bits) {
+__global__ void absmax_bf16_kernel(const __nv_bfloat16* x, int M, int K, long long ldx,
+                                   unsigned int* amax_bits) {
   rc::pdl_trigger();
   rc::pdl_wait();
   float m = 0.0f;
@@ -81,7 +81,7 @@ __global__ void absmax_bf16_kernel(const __nv_bfloat16* __restrict__ x, int M, i
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
        i += (long long)gridDim.x * blockDim.x) {
     const long long row = i / kv, c = i % kv;
-    uint4 v = __ldg(reinterpret_cast<const uint4*>(x + row * ldx) + c);
+    uint4 v = rc::ld_in(reinterpret_cast<const uint4*>(x + row * ldx) + c);
     const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
@@ -97,12 +97,11 @@ __global__ void absmax_bf16_kernel(const __nv_bfloat16* __restrict__ x, int M, i
   if ((threadIdx.x & 31) == 0 && mb) atomicMax(amax_bits, mb);
 }
 
-__global__ void fp8_quantize_kernel(const __nv_bfloat16* __restrict__ x, int M, int K, long long ldx,
-                                    const unsigned int* __restrict__ amax_bits,
-                                    float* __restrict__ scale_out, uint8_t* __restrict__ q) {
+__global__ void fp8_quantize_kernel(const __nv_bfloat16* x, int M, int K, long long ldx,
+                                    const unsigned int* amax_bits, float* scale_out, uint8_t* q) {
   rc::pdl_trigger();
   rc::pdl_wait();
-  float amax = __uint_as_float(*amax_bits);
+  float amax = __uint_as_float(rc::ld_in(amax_bits));
   amax = amax < 1e-12f ? 1e-12f : amax;         // clamp_min(1e-12); NaN passes through
   const float scale = __fdiv_rn(amax, 448.0f);
   if (blockIdx.x == 0 && threadIdx.x == 0 && scale_out) *scale_out = scale;
@@ -111,7 +110,7 @@ __global__ void fp8_quantize_kernel(const __nv_bfloat16* __restrict__ x, int M, 
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
        i += (long long)gridDim.x * blockDim.x) {
     const long long row = i / kv, c = i % kv;
-    uint4 v = __ldg(reinterpret_cast<const uint4*>(x + row * ldx) + c);
+    uint4 v = rc::ld_in(reinterpret_cast<const uint4*>(x + row * ldx) + c);
     const uint32_t w[4] = {v.x, v.y, v.z, v.w};
     uint32_t out[2] = {0, 0};
 #pragma unroll

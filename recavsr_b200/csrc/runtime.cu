@@ -39,6 +39,19 @@ int check_launch(cudaError_t launched, const char* what) {
   return check_launch(what);
 }
 
+int sm_count() {
+  constexpr int kMaxDevices = 64;
+  static int cache[kMaxDevices] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return 148;
+  if (!cache[dev]) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    cache[dev] = n > 0 ? n : 148;
+  }
+  return cache[dev];
+}
+
 int encode_tmap(CUtensorMap* map, CUtensorMapDataType dtype, int rank, void* base,
                 const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,
                 CUtensorMapSwizzle swizzle, const char* what) {

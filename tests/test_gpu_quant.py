@@ -71,6 +71,20 @@ def test_fp8_quantize_cfg3():
     np.testing.assert_array_equal(q.cpu().numpy(), rq)
 
 
+def test_fp8_quantize_back_to_back():
+    """Many quantizations queued without a host sync: the quantize kernel of
+    each call starts while its amax kernel still runs (programmatic dependent
+    launch) and must read the finished amax, never a partial one."""
+    from recavsr_b200.runtime import fp8
+    x = recipes.cfg3_activation(1760, 3072, seed=5)
+    rq, rscale = ofp8.quantize(x)
+    xd = dev_bf16(x)
+    outs = [fp8.quantize(xd) for _ in range(40)]
+    for q, scale in outs:
+        assert np.float32(scale.item()) == rscale
+        np.testing.assert_array_equal(q.cpu().numpy(), rq)
+
+
 def test_nvfp4_quantize_every_bf16_value_every_scale():
     """Blocks [6s, x, ...] pin the block scale to each E4M3 value s in turn and
     run every bf16 x with |x| <= 6s through the device quantizer."""
