@@ -184,10 +184,11 @@ def kernel_roofline(stack, torch):
     st = _lib.stream()
 
     def up():
-        _lib.check(lib.rc_nvfp4_gemm(ws.a_codes.data_ptr(), ws.a_scales.data_ptr(), blk.up.codes.data_ptr(),
-                                     blk.up.scales.data_ptr(), blk.up.bias.data_ptr(), n, FFN, DIM, 1.0,
-                                     _lib.EPI_GELU_NVFP4, None, 0, None, ws.f_codes.data_ptr(),
-                                     ws.f_scales.data_ptr(), 1.0, st), "up")
+        _lib.check(lib.rc_nvfp4_gemm_ws(ws.a_codes.data_ptr(), ws.a_scales.data_ptr(), blk.up.codes.data_ptr(),
+                                        blk.up.scales.data_ptr(), blk.up.bias.data_ptr(), n, FFN, DIM, 1.0,
+                                        _lib.EPI_GELU_NVFP4, None, 0, None, ws.f_codes.data_ptr(),
+                                        ws.f_scales.data_ptr(), 1.0, ws.gemm_ws.data_ptr(),
+                                        ws.gemm_ws.numel(), st), "up")
     t_up = time_kernel(up, 50, torch)
     rd = stack.route_dev
     o = 11 * stack._row

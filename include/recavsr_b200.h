@@ -62,6 +62,19 @@ int rc_nvfp4_gemm(const uint8_t* a_codes, const uint8_t* a_scales, const uint8_t
                   int epilogue, void* out, long long ldo, const float* gate, uint8_t* q_codes,
                   uint8_t* q_scales, float q_global_scale, rc_stream_t stream);
 
+/* rc_nvfp4_gemm with a split-K workspace: the tiles of the last, partial wave
+ * of the persistent grid run as up to 4 k-ranges each (fp32 partials in the
+ * workspace, summed in a fixed order by the last range to finish). workspace:
+ * rc_gemm_split_workspace() bytes, 16-byte aligned, zero-filled before first
+ * use (each successful call leaves it zero-filled); calls sharing one
+ * workspace must be ordered on one stream. */
+long long rc_gemm_split_workspace(void);
+int rc_nvfp4_gemm_ws(const uint8_t* a_codes, const uint8_t* a_scales, const uint8_t* b_codes,
+                     const uint8_t* b_scales, const void* bias, int M, int N, int K, float alpha,
+                     int epilogue, void* out, long long ldo, const float* gate, uint8_t* q_codes,
+                     uint8_t* q_scales, float q_global_scale, void* workspace,
+                     long long workspace_bytes, rc_stream_t stream);
+
 /* Replaces the torch._scaled_mm call of recavsr_infer/runtime/fp8.py:44-47
  * (per-tensor scales are device pointers, use_fast_accum=False semantics). */
 int rc_fp8_gemm(const uint8_t* a, const float* scale_a, const uint8_t* b, const float* scale_b,

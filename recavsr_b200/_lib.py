@@ -26,6 +26,8 @@ _SIGNATURES = {
     "rc_nvfp4_quantize": [_P, _I, _I, _LL, _F, _P, _P, _P],
     "rc_fp8_quantize": [_P, _I, _I, _LL, _P, _P, _P, _P],
     "rc_nvfp4_gemm": [_P, _P, _P, _P, _P, _I, _I, _I, _F, _I, _P, _LL, _P, _P, _P, _F, _P],
+    "rc_gemm_split_workspace": [],
+    "rc_nvfp4_gemm_ws": [_P, _P, _P, _P, _P, _I, _I, _I, _F, _I, _P, _LL, _P, _P, _P, _F, _P, _LL, _P],
     "rc_fp8_gemm": [_P, _P, _P, _P, _P, _I, _I, _I, _F, _I, _P, _LL, _P, _P],
     "rc_bf16_gemm": [_P, _P, _P, _I, _I, _I, _I, _P, _LL, _P, _P],
     "rc_ln_modulate_quant": [_P, _LL, _I, _I, _P, _P, _P, _P, _F, _P, _LL, _P, _P, _F, _P],
@@ -38,7 +40,7 @@ _SIGNATURES = {
     "rc_paired_attention_static_scratch": [_P] * 11 + [_I] * 10 + [_P, _LL, _P, _P, _P],
     "rc_kv_commit_planned": [_P, _P, _LL, _P, _P, _LL, _I, _I, _I, _I, _P, _P],
 }
-_RESTYPES = {"rc_paired_attention_workspace": C.c_longlong}
+_RESTYPES = {"rc_paired_attention_workspace": C.c_longlong, "rc_gemm_split_workspace": C.c_longlong}
 
 _lib = None
 _lock = threading.Lock()

@@ -80,7 +80,28 @@ struct GemmParams {
   uint8_t* q_codes;            // GELU_NVF4: [M, N/2]
   uint8_t* q_sf;               // GELU_NVF4: swizzled scales (N as K)
   float q_g;                   // GELU_NVF4: global scale
+  // Tail split-K: tiles [0, n_regular) run whole; every later tile runs as
+  // `split` work units over contiguous k-tile ranges. Each unit stores its fp32
+  // partial tile in `part`; the last unit of a tile to finish (per-tile arrival
+  // counter) sums the partials in unit order and runs the epilogue.
+  int n_regular, split;
+  float* part;                 // [units of split tiles][BM x BN] as [BN/4][BM][4]
+  int* counters;               // [split tiles]; zero between launches (the merging unit resets it)
 };
+
+constexpr int kMaxSplit = 4;       // units per split tile
+constexpr int kMaxPieces = 160;    // split units per launch (>= SMs of a B200)
+
+// Work unit u of the persistent schedule: tile, k-tile range and the index of
+// the unit among the split units (-1 for a whole tile).
+struct Unit {
+  int tile, kt0, kt1, piece;
+};
+__device__ __forceinline__ Unit unit_of(const GemmParams& p, int u) {
+  if (u < p.n_regular) return {u, 0, p.k_tiles, -1};
+  const int t = u - p.n_regular, tt = t / p.split, pc = t - tt * p.split;
+  return {p.n_regular + tt, pc * p.k_tiles / p.split, (pc + 1) * p.k_tiles / p.split, t};
+}
 
 template <int KIND, int BN, int STAGES>
 struct Smem {
@@ -149,7 +170,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int num_tiles = p.m_blocks * p.n_blocks;
+  const int num_units = p.n_regular + (p.m_blocks * p.n_blocks - p.n_regular) * p.split;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -197,9 +218,10 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
       uint32_t phase = 0;
       long long issued = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-        const int mb = tile % p.m_blocks, nb = tile / p.m_blocks;
-        for (int kt = 0; kt < p.k_tiles; ++kt) {
+      for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
+        const Unit un = unit_of(p, u);
+        const int mb = un.tile % p.m_blocks, nb = un.tile / p.m_blocks;
+        for (int kt = un.kt0; kt < un.kt1; ++kt) {
           if (!wait(&empty[stage], phase ^ 1, 1)) { ok = false; break; }
           uint32_t bytes = S::kA + S::kB;
           int sfa_bytes = 0, sfb_bytes = 0;
@@ -283,13 +305,14 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
         else
           sm100::mma_f16_ss(d_tmem, a, b, idesc, acc);
       };
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++local) {
+      for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x, ++local) {
+        const Unit un = unit_of(p, u);
         const int as = local % kAcc;
         const uint32_t acc_parity = (uint32_t)((local / kAcc) & 1);
         if (!wait(&acc_empty[as], acc_parity ^ 1, 2)) { ok = false; break; }
         sm100::tc_fence_after();
         const uint32_t d_tmem = tmem_acc + as * BN;
-        for (int kt = 0; kt < p.k_tiles; ++kt) {
+        for (int kt = un.kt0; kt < un.kt1; ++kt) {
           if (!wait(&full[stage], phase, 3)) { ok = false; break; }
           sm100::tc_fence_after();
           const uint64_t da = sm100::desc_add(da0, stage * S::kA);
@@ -315,12 +338,12 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
               for (int j = 0; j < kMmaPerTile; ++j) copy_sf(j, sfa_t, sfb_t, dsa, dsb);
             }
 #pragma unroll
-            for (int j = 0; j < kMmaPerTile; ++j) mma(j, d_tmem, da, db, sfa_t, sfb_t, (kt | j) != 0);
+            for (int j = 0; j < kMmaPerTile; ++j) mma(j, d_tmem, da, db, sfa_t, sfb_t, (kt != un.kt0) | (j != 0));
           } else {
             if constexpr (kScaled) {
               for (int j = 0; j < steps; ++j) copy_sf(j, sfa_t, sfb_t, dsa, dsb);
             }
-            for (int j = 0; j < steps; ++j) mma(j, d_tmem, da, db, sfa_t, sfb_t, (kt | j) != 0);
+            for (int j = 0; j < steps; ++j) mma(j, d_tmem, da, db, sfa_t, sfb_t, (kt != un.kt0) | (j != 0));
           }
           sm100::tc_commit(&empty[stage]);
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
@@ -347,21 +370,73 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
       if (p.alpha_ptr_a) alpha = __fmul_rn(alpha, *p.alpha_ptr_a);
       if (p.alpha_ptr_b) alpha = __fmul_rn(alpha, *p.alpha_ptr_b);
     }
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
-      const int mb = tile % p.m_blocks, nb = tile / p.m_blocks;
+    int* s_flags = reinterpret_cast<int*>(done + 4);   // [0] last unit of the tile, [1] a warp failed
+    if (threadIdx.x == 64) s_flags[1] = 0;
+    asm volatile("bar.sync 1, %0;" ::"r"(32 * epi_warps<EPI>()) : "memory");
+    for (int u = blockIdx.x; u < num_units; u += gridDim.x, ++local) {
+      const Unit un = unit_of(p, u);
+      const int mb = un.tile % p.m_blocks, nb = un.tile / p.m_blocks;
       const int as = local % kAcc;
-      if (!__all_sync(0xffffffffu, wait(&acc_full[as], (uint32_t)((local / kAcc) & 1), 4))) break;
-      sm100::tc_fence_after();
+      const bool got = __all_sync(0xffffffffu, wait(&acc_full[as], (uint32_t)((local / kAcc) & 1), 4));
+      if (!got && (BN != 128 || un.piece < 0)) break;
       uint32_t acc[kCols];
-      {
+      if (got) {
+        sm100::tc_fence_after();
         const uint32_t t_row = tmem_acc + as * BN + part * kCols + ((uint32_t)(quad * 32) << 16);
 #pragma unroll
         for (int c = 0; c < kCols; c += 16)
           sm100::tmem_ld16(t_row + c, *reinterpret_cast<uint32_t(*)[16]>(&acc[c]));
         sm100::tmem_ld_wait();
+        sm100::tc_fence_before();
+        sm100::mbar_arrive(&acc_empty[as]);      // accumulator free: next tile may start
       }
-      sm100::tc_fence_before();
-      sm100::mbar_arrive(&acc_empty[as]);      // accumulator free: next tile may start
+      if (BN == 128 && un.piece >= 0) {   // (the host splits 128-column tiles only)
+        // Split tile: store this unit's partial, count the arrival; the last
+        // unit to arrive sums every unit's partial in unit order.
+        float4* mine = reinterpret_cast<float4*>(p.part + (size_t)un.piece * (BM * BN));
+        if (got) {
+#pragma unroll
+          for (int c = 0; c < kCols; c += 4)
+            __stcg(mine + ((part * kCols + c) >> 2) * BM + row_in_tile,
+                   make_float4(__uint_as_float(acc[c]), __uint_as_float(acc[c + 1]),
+                               __uint_as_float(acc[c + 2]), __uint_as_float(acc[c + 3])));
+        } else if (lane == 0) {
+          s_flags[1] = 1;
+        }
+        __threadfence();
+        asm volatile("bar.sync 1, %0;" ::"r"(32 * epi_warps<EPI>()) : "memory");
+        const int tail_tile = un.tile - p.n_regular;
+        if (threadIdx.x == 64)
+          s_flags[0] = !s_flags[1] && atomicAdd(&p.counters[tail_tile], 1) == p.split - 1;
+        asm volatile("bar.sync 1, %0;" ::"r"(32 * epi_warps<EPI>()) : "memory");
+        if (s_flags[1]) break;
+        if (!s_flags[0]) continue;
+        __threadfence();   // acquire: the other units' partials are visible from here
+        // All of a unit's loads are issued before any is used: one L2 round
+        // trip per unit, not one per column quad.
+        const float4* src = reinterpret_cast<const float4*>(p.part + (size_t)tail_tile * p.split * (BM * BN)) +
+                            ((part * kCols) >> 2) * BM + row_in_tile;
+        float4 sum[kCols / 4];
+#pragma unroll
+        for (int i = 0; i < kCols / 4; ++i) sum[i] = __ldcg(src + i * BM);
+        for (int q = 1; q < p.split; ++q) {
+          float4 v[kCols / 4];
+#pragma unroll
+          for (int i = 0; i < kCols / 4; ++i) v[i] = __ldcg(src + (size_t)q * (BM * BN / 4) + i * BM);
+#pragma unroll
+          for (int i = 0; i < kCols / 4; ++i) {
+            sum[i].x += v[i].x; sum[i].y += v[i].y; sum[i].z += v[i].z; sum[i].w += v[i].w;
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < kCols / 4; ++i) {
+          acc[4 * i] = __float_as_uint(sum[i].x);
+          acc[4 * i + 1] = __float_as_uint(sum[i].y);
+          acc[4 * i + 2] = __float_as_uint(sum[i].z);
+          acc[4 * i + 3] = __float_as_uint(sum[i].w);
+        }
+        if (threadIdx.x == 64) p.counters[tail_tile] = 0;   // ready for the next launch
+      }
       const int row = mb * BM + row_in_tile;
       const bool row_ok = row < p.M;
 #pragma unroll
@@ -468,6 +543,36 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
   }
 }
 
+// Tail split-K. The persistent CTAs take the tiles round-robin, so the last
+// `tiles % sms` tiles form a partial wave; those run as `split` k-ranges each,
+// so that wave ends about `split` times sooner. Storing and merging the fp32
+// partials costs about as much as 4-8 k-tiles of MMA, so every range keeps at
+// least 8 k-tiles (measured on M = 1760: the split gains 3% on ffn_down,
+// K = 14336, and loses 16% on o-proj, K = 3072, which therefore stays whole).
+// RECAVSR_GEMM_SPLIT=n caps the units per tile (1 = no split).
+void plan_split(int tiles, int sms, bool can_split, GemmParams& p) {
+  static int cap = -1;
+  if (cap < 0) {
+    const char* e = getenv("RECAVSR_GEMM_SPLIT");
+    cap = e ? atoi(e) : kMaxSplit;
+    cap = cap < 1 ? 1 : (cap > kMaxSplit ? kMaxSplit : cap);
+  }
+  p.n_regular = tiles;
+  p.split = 1;
+  const int tail = tiles % sms;
+  if (!can_split || !tail) return;
+  int s = sms / tail;
+  s = s < cap ? s : cap;
+  s = s < p.k_tiles / 8 ? s : p.k_tiles / 8;
+  while (s > 1 && tail * s > kMaxPieces) --s;
+  if (s < 2) return;
+  p.n_regular = tiles - tail;
+  p.split = s;
+}
+
+constexpr long long kSplitPartBytes = (long long)kMaxPieces * BM * 128 * 4;
+constexpr long long kSplitWorkspaceBytes = kSplitPartBytes + kMaxPieces * 4;
+
 template <int KIND, int BN, int STAGES, int EPI>
 int launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, cudaStream_t stream,
            const char* what) {
@@ -480,8 +585,12 @@ int launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, cu
     attr_set = true;
   }
   const int tiles = p.m_blocks * p.n_blocks;
-  const int grid = tiles < rc::sm_count() ? tiles : rc::sm_count();
-  return rc::check_launch(rc::launch_pdl(kern, grid, dim3(gemm_threads<EPI>()), S::kAlloc, stream, ta, tb, p), what);
+  const int sms = rc::sm_count();
+  GemmParams q = p;
+  plan_split(tiles, sms, BN == 128 && p.part != nullptr, q);
+  const int units = q.n_regular + (tiles - q.n_regular) * q.split;
+  const int grid = units < sms ? units : sms;
+  return rc::check_launch(rc::launch_pdl(kern, grid, dim3(gemm_threads<EPI>()), S::kAlloc, stream, ta, tb, q), what);
 }
 
 template <int KIND, int BN, int STAGES>
@@ -595,6 +704,40 @@ int rc_nvfp4_gemm(const uint8_t* a_codes, const uint8_t* a_scales, const uint8_t
   p.q_sf = q_scales;
   p.q_g = q_global_scale;
   return run_gemm(KIND_NVF4, epilogue, a_codes, b_codes, M, N, K, p, stream, "rc_nvfp4_gemm");
+}
+
+long long rc_gemm_split_workspace(void) { return kSplitWorkspaceBytes; }
+
+// rc_nvfp4_gemm with a split-K workspace (rc_gemm_split_workspace() bytes,
+// 16-byte aligned, zero-filled before its first use; every successful call
+// leaves it zero-filled). Calls that share a workspace must be ordered on one
+// stream.
+int rc_nvfp4_gemm_ws(const uint8_t* a_codes, const uint8_t* a_scales, const uint8_t* b_codes,
+                     const uint8_t* b_scales, const void* bias, int M, int N, int K, float alpha,
+                     int epilogue, void* out, long long ldo, const float* gate, uint8_t* q_codes,
+                     uint8_t* q_scales, float q_global_scale, void* workspace, long long workspace_bytes,
+                     cudaStream_t stream) {
+  const char* what = "rc_nvfp4_gemm_ws";
+  if (!a_scales || !b_scales) return rc::set_error(RC_ERR_ARG, "%s: null scales", what);
+  if (reinterpret_cast<uintptr_t>(a_scales) % 16 || reinterpret_cast<uintptr_t>(b_scales) % 16)
+    return rc::set_error(RC_ERR_ARG, "%s: scale buffers must be 16-byte aligned", what);
+  if (!workspace || workspace_bytes < kSplitWorkspaceBytes || reinterpret_cast<uintptr_t>(workspace) % 16)
+    return rc::set_error(RC_ERR_ARG, "%s: workspace of %lld bytes (16-byte aligned) required", what,
+                         kSplitWorkspaceBytes);
+  GemmParams p{};
+  p.sfa = a_scales;
+  p.sfb = b_scales;
+  p.alpha = alpha;
+  p.bias = reinterpret_cast<const __nv_bfloat16*>(bias);
+  p.out = reinterpret_cast<__nv_bfloat16*>(out);
+  p.ldo = ldo;
+  p.gate = gate;
+  p.q_codes = q_codes;
+  p.q_sf = q_scales;
+  p.q_g = q_global_scale;
+  p.part = reinterpret_cast<float*>(workspace);
+  p.counters = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(workspace) + kSplitPartBytes);
+  return run_gemm(KIND_NVF4, epilogue, a_codes, b_codes, M, N, K, p, stream, what);
 }
 
 // Per-tensor FP8 (E4M3) GEMM: alpha * scale_a * scale_b * A.B^T + bias.

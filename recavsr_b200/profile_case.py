@@ -40,13 +40,14 @@ def _gemm(n, k, epi):
     qc = torch.empty(M, n // 2, dtype=torch.uint8, device="cuda")
     qs = torch.empty(scale_numel(M, n), dtype=torch.uint8, device="cuda")
     lib = _lib.library()
+    sws = torch.zeros(lib.rc_gemm_split_workspace(), dtype=torch.uint8, device="cuda")
 
     def run():
-        _lib.check(lib.rc_nvfp4_gemm(ac.data_ptr(), asf.data_ptr(), wc.data_ptr(), wsf.data_ptr(),
-                                     bias.data_ptr(), M, n, k, 1.0, epi,
-                                     None if epi == _lib.EPI_GELU_NVFP4 else out.data_ptr(), n,
-                                     gate.data_ptr(), qc.data_ptr(), qs.data_ptr(), 1.0,
-                                     _lib.stream()), "gemm")
+        _lib.check(lib.rc_nvfp4_gemm_ws(ac.data_ptr(), asf.data_ptr(), wc.data_ptr(), wsf.data_ptr(),
+                                        bias.data_ptr(), M, n, k, 1.0, epi,
+                                        None if epi == _lib.EPI_GELU_NVFP4 else out.data_ptr(), n,
+                                        gate.data_ptr(), qc.data_ptr(), qs.data_ptr(), 1.0,
+                                        sws.data_ptr(), sws.numel(), _lib.stream()), "gemm")
     return run, 2.0 * M * n * k, "TFLOP/s"
 
 

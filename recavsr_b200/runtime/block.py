@@ -158,7 +158,7 @@ class FusedBlock(torch.nn.Module):
                                      scale.data_ptr(), _EPS, None, 0, ws.a_codes.data_ptr(),
                                      ws.a_scales.data_ptr(), 1.0, st), "ln1")
         # 2. fused QKV
-        self._gemm(lib, ws.a_codes, ws.a_scales, self.qkv, n, _lib.EPI_BIAS, ws.qkv, st)
+        self._gemm(lib, ws, ws.a_codes, ws.a_scales, self.qkv, n, _lib.EPI_BIAS, ws.qkv, st)
         # 3. RMSNorm + spatial RoPE of q and k
         q_in, k_in = ws.qkv[:, :dim], ws.qkv[:, dim:2 * dim]
         chk(lib.rc_rmsnorm_rope(2, (C.c_void_p * 2)(q_in.data_ptr(), k_in.data_ptr()),
@@ -172,12 +172,12 @@ class FusedBlock(torch.nn.Module):
         self._attention(lib, ws, past_key, past_value, slots, past_positions, query_positions, n, st,
                         quantized=True)
         # 5. o-proj with gated residual
-        self._gemm(lib, ws.a_codes, ws.a_scales, self.o, n, _lib.EPI_GATED_RESIDUAL, h, st, gate)
+        self._gemm(lib, ws, ws.a_codes, ws.a_scales, self.o, n, _lib.EPI_GATED_RESIDUAL, h, st, gate)
         # 6. cross attention
         chk(lib.rc_ln_modulate_quant(h.data_ptr(), dim, n, dim, self.norm2_w.data_ptr(),
                                      self.norm2_b.data_ptr(), None, None, _EPS, None, 0,
                                      ws.a_codes.data_ptr(), ws.a_scales.data_ptr(), 1.0, st), "ln2")
-        self._gemm(lib, ws.a_codes, ws.a_scales, self.cq, n, _lib.EPI_BIAS, ws.cq, st)
+        self._gemm(lib, ws, ws.a_codes, ws.a_scales, self.cq, n, _lib.EPI_BIAS, ws.cq, st)
         chk(lib.rc_rmsnorm_rope(1, (C.c_void_p * 1)(ws.cq.data_ptr()), (C.c_longlong * 1)(dim),
                                 (C.c_void_p * 1)(self.cnorm_q.data_ptr()),
                                 (C.c_void_p * 1)(ws.q_rot.data_ptr()), (C.c_longlong * 1)(dim),
@@ -188,23 +188,25 @@ class FusedBlock(torch.nn.Module):
                                    self.cross_v.data_ptr(), strides, 1, n, self.cross_k.shape[0],
                                    self.heads, hd, None, dim, ws.a_codes.data_ptr(),
                                    ws.a_scales.data_ptr(), st), "cross_attn")
-        self._gemm(lib, ws.a_codes, ws.a_scales, self.co, n, _lib.EPI_RESIDUAL, h, st)
+        self._gemm(lib, ws, ws.a_codes, ws.a_scales, self.co, n, _lib.EPI_RESIDUAL, h, st)
         # 7. FFN
         chk(lib.rc_ln_modulate_quant(h.data_ptr(), dim, n, dim, None, None, cshift.data_ptr(),
                                      cscale.data_ptr(), _EPS, None, 0, ws.a_codes.data_ptr(),
                                      ws.a_scales.data_ptr(), 1.0, st), "ln3")
-        chk(lib.rc_nvfp4_gemm(ws.a_codes.data_ptr(), ws.a_scales.data_ptr(), self.up.codes.data_ptr(),
-                              self.up.scales.data_ptr(), _lib.ptr(self.up.bias), n, self.up.n,
-                              self.up.k, 1.0, _lib.EPI_GELU_NVFP4, None, 0, None,
-                              ws.f_codes.data_ptr(), ws.f_scales.data_ptr(), 1.0, st), "ffn_up")
-        self._gemm(lib, ws.f_codes, ws.f_scales, self.down, n, _lib.EPI_GATED_RESIDUAL, h, st, cgate)
+        chk(lib.rc_nvfp4_gemm_ws(ws.a_codes.data_ptr(), ws.a_scales.data_ptr(), self.up.codes.data_ptr(),
+                                 self.up.scales.data_ptr(), _lib.ptr(self.up.bias), n, self.up.n,
+                                 self.up.k, 1.0, _lib.EPI_GELU_NVFP4, None, 0, None,
+                                 ws.f_codes.data_ptr(), ws.f_scales.data_ptr(), 1.0,
+                                 ws.gemm_ws.data_ptr(), ws.gemm_ws.numel(), st), "ffn_up")
+        self._gemm(lib, ws, ws.f_codes, ws.f_scales, self.down, n, _lib.EPI_GATED_RESIDUAL, h, st, cgate)
 
     # ------------------------------------------------------------ helpers
-    def _gemm(self, lib, codes, scales, w: _Quantized, m, epi, out, st, gate=None):
-        _lib.check(lib.rc_nvfp4_gemm(codes.data_ptr(), scales.data_ptr(), w.codes.data_ptr(),
-                                     w.scales.data_ptr(), _lib.ptr(w.bias), m, w.n, w.k, 1.0, epi,
-                                     out.data_ptr(), out.stride(0), _lib.ptr(gate), None, None,
-                                     1.0, st), "nvfp4_gemm")
+    def _gemm(self, lib, ws, codes, scales, w: _Quantized, m, epi, out, st, gate=None):
+        _lib.check(lib.rc_nvfp4_gemm_ws(codes.data_ptr(), scales.data_ptr(), w.codes.data_ptr(),
+                                        w.scales.data_ptr(), _lib.ptr(w.bias), m, w.n, w.k, 1.0, epi,
+                                        out.data_ptr(), out.stride(0), _lib.ptr(gate), None, None,
+                                        1.0, ws.gemm_ws.data_ptr(), ws.gemm_ws.numel(), st),
+                   "nvfp4_gemm")
 
     def _attention(self, lib, ws, past_key, past_value, slots, ppos, qpos, n, st, quantized=False):
         """Routed attention into ws.attn (bf16) or, with quantized=True, straight
@@ -253,6 +255,10 @@ class Workspace:
         ws = _lib.library().rc_paired_attention_workspace(1, frames, max_cap, block.height,
                                                           block.width, block.heads, block.head_dim)
         self.attn_ws = torch.empty((ws,), dtype=torch.uint8, device=dev)
+        # Split-K partials and arrival counters of the NVFP4 GEMMs (zero-filled;
+        # the GEMMs leave it zero-filled).
+        self.gemm_ws = torch.zeros((_lib.library().rc_gemm_split_workspace(),), dtype=torch.uint8,
+                                   device=dev)
 
 
 def rope_tables(head_dim: int, height: int, width: int, device) -> dict:

@@ -48,6 +48,21 @@ def quantize(matrix: torch.Tensor, global_scale: float = 1.0) -> tuple[torch.Ten
     return packed, scales
 
 
+_SPLIT_WS: dict = {}
+
+
+def split_workspace(device: torch.device) -> torch.Tensor:
+    """The zero-filled split-K workspace of the NVFP4 GEMM, one per (device,
+    stream): calls sharing a workspace must be ordered on one stream."""
+    device = torch.device(device)
+    key = (device.index if device.index is not None else torch.cuda.current_device(), _lib.stream(device))
+    ws = _SPLIT_WS.get(key)
+    if ws is None:
+        ws = torch.zeros((_lib.library().rc_gemm_split_workspace(),), dtype=torch.uint8, device=device)
+        _SPLIT_WS[key] = ws
+    return ws
+
+
 def gemm(values, weights, scales, weight_scales, bias=None, *, alpha=1.0,
          out: torch.Tensor | None = None) -> torch.Tensor:
     """bf16 [M, N] = alpha * A . B^T + bias on the tcgen05 block-scaled path."""
@@ -58,10 +73,11 @@ def gemm(values, weights, scales, weight_scales, bias=None, *, alpha=1.0,
         raise ValueError("NVFP4 operand widths disagree.")
     if out is None:
         out = torch.empty((m, n), dtype=torch.bfloat16, device=a.device)
-    _lib.call("rc_nvfp4_gemm", a.data_ptr(), scales.view(torch.uint8).data_ptr(), b.data_ptr(),
+    ws = split_workspace(a.device)
+    _lib.call("rc_nvfp4_gemm_ws", a.data_ptr(), scales.view(torch.uint8).data_ptr(), b.data_ptr(),
               weight_scales.view(torch.uint8).data_ptr(), _lib.ptr(bias), m, n, k, float(alpha),
               _lib.EPI_BIAS, out.data_ptr(), out.stride(0), None, None, None, 1.0,
-              _lib.stream(a.device))
+              ws.data_ptr(), ws.numel(), _lib.stream(a.device))
     return out
 
 

@@ -117,7 +117,7 @@ def test_fused_block_stagewise_vs_oracle():
     a_ref = onv.dequantize(rc_, rs_, n, dim)
     assert np.mean(a_dev != a_ref) < 0.01
     # QKV GEMM on the kernel's own codes: 1e-2 rel of the dequantized matmul
-    blk._gemm(lib, ws.a_codes, ws.a_scales, blk.qkv, n, _lib.EPI_BIAS, ws.qkv, st)
+    blk._gemm(lib, ws, ws.a_codes, ws.a_scales, blk.qkv, n, _lib.EPI_BIAS, ws.qkv, st)
     sync()
     wq = np.concatenate([p["q_w"], p["k_w"], p["v_w"]], 0)
     bq = np.concatenate([p["q_b"], p["k_b"], p["v_b"]])
@@ -155,7 +155,7 @@ def test_fused_block_stagewise_vs_oracle():
     # o-proj, gated residual (exact on identical inputs)
     _lib.check(lib.rc_nvfp4_quantize(ws.attn.data_ptr(), n, dim, dim, 1.0, ws.a_codes.data_ptr(),
                                      ws.a_scales.data_ptr(), st), "q")
-    blk._gemm(lib, ws.a_codes, ws.a_scales, blk.o, n, _lib.EPI_GATED_RESIDUAL, h, st, gate)
+    blk._gemm(lib, ws, ws.a_codes, ws.a_scales, blk.o, n, _lib.EPI_GATED_RESIDUAL, h, st, gate)
     sync()
     h1 = bf16_round(hidden[0] + lin["o"](att) * mod[2])
     assert np.abs(host(h) - h1).max() <= 1e-2 * np.abs(h1).max()
@@ -164,7 +164,7 @@ def test_fused_block_stagewise_vs_oracle():
     _lib.check(lib.rc_ln_modulate_quant(h.data_ptr(), dim, n, dim, blk.norm2_w.data_ptr(),
                                         blk.norm2_b.data_ptr(), None, None, 1e-6, None, 0,
                                         ws.a_codes.data_ptr(), ws.a_scales.data_ptr(), 1.0, st), "ln2")
-    blk._gemm(lib, ws.a_codes, ws.a_scales, blk.cq, n, _lib.EPI_BIAS, ws.cq, st)
+    blk._gemm(lib, ws, ws.a_codes, ws.a_scales, blk.cq, n, _lib.EPI_BIAS, ws.cq, st)
     sync()
     cq_ref = onv.nvfp4_mm(ws.a_codes.cpu().numpy(), ws.a_scales.cpu().numpy(), *onv.quantize(p["cq_w"]),
                           p["cq_b"], n, dim, dim)
@@ -183,7 +183,7 @@ def test_fused_block_stagewise_vs_oracle():
     assert np.abs(ca - rca.reshape(n, dim)).max() <= 2e-2
     _lib.check(lib.rc_nvfp4_quantize(ws.attn.data_ptr(), n, dim, dim, 1.0, ws.a_codes.data_ptr(),
                                      ws.a_scales.data_ptr(), st), "q2")
-    blk._gemm(lib, ws.a_codes, ws.a_scales, blk.co, n, _lib.EPI_RESIDUAL, h, st)
+    blk._gemm(lib, ws, ws.a_codes, ws.a_scales, blk.co, n, _lib.EPI_RESIDUAL, h, st)
     sync()
     h2 = bf16_round(h1 + lin["co"](ca))
     assert np.abs(host(h) - h2).max() <= 1e-2 * np.abs(h2).max()
@@ -202,7 +202,7 @@ def test_fused_block_stagewise_vs_oracle():
     up_dev = onv.dequantize(ws.f_codes.cpu().numpy(), ws.f_scales.cpu().numpy(), n, ffn)
     uc, us = onv.quantize(up_ref)
     assert np.mean(up_dev != onv.dequantize(uc, us, n, ffn)) < 0.01
-    blk._gemm(lib, ws.f_codes, ws.f_scales, blk.down, n, _lib.EPI_GATED_RESIDUAL, h, st, cgate)
+    blk._gemm(lib, ws, ws.f_codes, ws.f_scales, blk.down, n, _lib.EPI_GATED_RESIDUAL, h, st, cgate)
     sync()
     y = onv.nvfp4_mm(ws.f_codes.cpu().numpy(), ws.f_scales.cpu().numpy(), *onv.quantize(p["down_w"]),
                      p["down_b"], n, dim, ffn)

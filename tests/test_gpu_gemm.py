@@ -76,15 +76,23 @@ def test_nvfp4_gemm_alpha_global_scale():
     assert max_rel(host(out), ref) < 0.2
 
 
-def _lib_gemm(epi, m, n, k, ac, asf, wc, wsf, bias, out, gate=None, qc=None, qs=None):
+def _lib_gemm(epi, m, n, k, ac, asf, wc, wsf, bias, out, gate=None, qc=None, qs=None, split=True):
+    """rc_nvfp4_gemm_ws (tail split-K with a workspace) or, split=False, rc_nvfp4_gemm."""
     from recavsr_b200 import _lib
-    _lib.call("rc_nvfp4_gemm", ac.data_ptr(), asf.data_ptr(), wc.data_ptr(), wsf.data_ptr(),
-              _lib.ptr(bias), m, n, k, 1.0, epi, _lib.ptr(out), 0 if out is None else out.stride(0),
-              _lib.ptr(gate), _lib.ptr(qc), _lib.ptr(qs), 1.0, _lib.stream())
+    from recavsr_b200.runtime.nvfp4 import split_workspace
+    args = [ac.data_ptr(), asf.data_ptr(), wc.data_ptr(), wsf.data_ptr(), _lib.ptr(bias), m, n, k, 1.0,
+            epi, _lib.ptr(out), 0 if out is None else out.stride(0), _lib.ptr(gate), _lib.ptr(qc),
+            _lib.ptr(qs), 1.0]
+    if split:
+        ws = split_workspace(ac.device)
+        _lib.call("rc_nvfp4_gemm_ws", *args, ws.data_ptr(), ws.numel(), _lib.stream())
+    else:
+        _lib.call("rc_nvfp4_gemm", *args, _lib.stream())
 
 
-@pytest.mark.parametrize("m,n,k", [(1760, 3072, 3072), (200, 256, 512)])
-def test_nvfp4_gemm_gated_residual(m, n, k):
+@pytest.mark.parametrize("split", [True, False])
+@pytest.mark.parametrize("m,n,k", [(1760, 3072, 3072), (200, 256, 512), (256, 3072, 14336)])
+def test_nvfp4_gemm_gated_residual(m, n, k, split):
     from recavsr_b200 import _lib
     a, w, bias, ac, asf, wc, wsf = _operands(m, n, k, seed=9)
     h = recipes.bf16_normal(np.random.RandomState(3), (m, n))
@@ -93,16 +101,39 @@ def test_nvfp4_gemm_gated_residual(m, n, k):
     ref = bf16_round(h + y * gate)
     hd = dev_bf16(h)
     _lib_gemm(_lib.EPI_GATED_RESIDUAL, m, n, k, dev_u8(ac), dev_u8(asf), dev_u8(wc), dev_u8(wsf),
-              dev_bf16(bias), hd, gate=torch.from_numpy(gate).cuda())
+              dev_bf16(bias), hd, gate=torch.from_numpy(gate).cuda(), split=split)
     assert max_rel(host(hd), ref) < TOL
     hd2 = dev_bf16(h)
     _lib_gemm(_lib.EPI_RESIDUAL, m, n, k, dev_u8(ac), dev_u8(asf), dev_u8(wc), dev_u8(wsf),
-              dev_bf16(bias), hd2)
+              dev_bf16(bias), hd2, split=split)
     assert max_rel(host(hd2), bf16_round(h + y)) < TOL
     assert_no_device_error()
 
 
-@pytest.mark.parametrize("m,n,k", [(1760, 14336, 3072), (130, 512, 256)])
+def test_nvfp4_gemm_split_back_to_back():
+    """Split-K GEMMs queued back to back on one workspace (each merge resets its
+    tile counter for the next call) give identical results; split and unsplit
+    results differ only by the fp32 summation order."""
+    from recavsr_b200 import _lib
+    from recavsr_b200.runtime.nvfp4 import split_workspace
+    m, n, k = 1760, 3072, 14336            # 336 tiles: the last 40 run as 3 k-ranges each
+    a, w, bias, ac, asf, wc, wsf = _operands(m, n, k, seed=21)
+    y = onv.nvfp4_mm(ac, asf, wc, wsf, bias, m, n, k)
+    dac, dasf, dwc, dwsf, db = dev_u8(ac), dev_u8(asf), dev_u8(wc), dev_u8(wsf), dev_bf16(bias)
+    outs = [torch.empty(m, n, dtype=torch.bfloat16, device="cuda") for _ in range(6)]
+    for o in outs:
+        _lib_gemm(_lib.EPI_BIAS, m, n, k, dac, dasf, dwc, dwsf, db, o)
+    plain = torch.empty(m, n, dtype=torch.bfloat16, device="cuda")
+    _lib_gemm(_lib.EPI_BIAS, m, n, k, dac, dasf, dwc, dwsf, db, plain, split=False)
+    assert_no_device_error()
+    for o in outs:
+        assert max_rel(host(o), y) < TOL
+        assert torch.equal(o, outs[0])                       # fixed summation order
+    assert max_rel(host(outs[0]), host(plain)) < 2 ** -8      # summation order only
+    assert int(split_workspace(dac.device)[-640:].count_nonzero()) == 0   # counters back at zero
+
+
+@pytest.mark.parametrize("m,n,k", [(1760, 14336, 3072), (130, 512, 256), (256, 3072, 8192)])
 def test_nvfp4_gemm_gelu_requantize(m, n, k):
     """ffn_up epilogue: GELU(tanh) then NVFP4 codes/scales for ffn_down. The
     re-quantized operand must dequantize to the oracle's within one E2M1 step
