@@ -73,32 +73,12 @@ __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;"
 // inputs, so the read-only non-coherent path (ld.global.nc, which __ldg and
 // `const __restrict__` pointers select) does not apply: it is defined only for
 // data that nothing writes during the kernel's lifetime, and the compiler may
-// schedule such loads ahead of pdl_wait(). These are ordinary coherent loads,
-// kept in program order after pdl_wait() by `volatile`.
-__device__ __forceinline__ uint4 ld_in(const uint4* p) {
-  uint4 v;
-  asm volatile("ld.global.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
-  return v;
-}
-__device__ __forceinline__ float4 ld_in(const float4* p) {
-  float4 v;
-  asm volatile("ld.global.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "l"(p));
-  return v;
-}
-__device__ __forceinline__ float ld_in(const float* p) {
-  float v;
-  asm volatile("ld.global.f32 %0, [%1];" : "=f"(v) : "l"(p));
-  return v;
-}
-__device__ __forceinline__ int ld_in(const int* p) {
-  int v;
-  asm volatile("ld.global.s32 %0, [%1];" : "=r"(v) : "l"(p));
-  return v;
-}
-__device__ __forceinline__ unsigned int ld_in(const unsigned int* p) {
-  unsigned int v;
-  asm volatile("ld.global.u32 %0, [%1];" : "=r"(v) : "l"(p));
-  return v;
+// schedule such loads ahead of pdl_wait(). These are ordinary coherent loads
+// through a pointer the compiler cannot prove read-only; the "memory" clobber
+// of pdl_wait() keeps them after it, and independent loads still overlap.
+template <typename T>
+__device__ __forceinline__ T ld_in(const T* p) {
+  return *p;
 }
 
 // Launch `kernel` on `stream` with programmatic stream serialization allowed.

@@ -243,6 +243,9 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("case", choices=sorted(CASES) + ["gemm_sweep", "attention_sweep"])
     ap.add_argument("--reps", type=int, default=20)
+    ap.add_argument("--seconds", type=float, default=0.0,
+                    help="also replay for this long and report the sustained per-launch time "
+                         "(sample clocks / power alongside to see the power cap)")
     args = ap.parse_args()
     if args.case == "gemm_sweep":
         return gemm_sweep()
@@ -272,6 +275,16 @@ def main():
     dt = a.elapsed_time(b) / args.reps * 1e-3
     rate = work / dt / (1e12 if unit == "TFLOP/s" else 1e9)
     print(f"{args.case}: {dt * 1e6:.1f} us/launch, {rate:.1f} {unit}")
+    if args.seconds > 0:
+        n = max(1, int(args.seconds / (dt * args.reps)))
+        a.record()
+        for _ in range(n):
+            graph.replay()
+        b.record()
+        b.synchronize()
+        ds = a.elapsed_time(b) / (n * args.reps) * 1e-3
+        rs = work / ds / (1e12 if unit == "TFLOP/s" else 1e9)
+        print(f"{args.case} sustained {a.elapsed_time(b) / 1e3:.1f} s: {ds * 1e6:.1f} us/launch, {rs:.1f} {unit}")
     if _lib.read_device_error():
         raise SystemExit("device error word set")
 
