@@ -793,69 +793,82 @@ struct GatherParams {
   int n_counters;
 };
 
-// One thread = 8 consecutive elements of one token row (16 bytes); each
-// thread keeps kGatherUnroll independent loads in flight.
-constexpr int kGatherUnroll = 4;
-
-// Workspace plane order: routed past planes [0, CAP) (slot indirection
-// applied), then the current frames.
-__device__ __forceinline__ bool gather_src(const GatherParams& g, long long i, int vec,
-                                           const __nv_bfloat16*& src, __nv_bfloat16*& dst, int& pos,
-                                           int& dd) {
-  const int v = (int)(i % vec);
-  const long long tok = i / vec;
-  const int plane = (int)(tok / g.T), t = (int)(tok % g.T);
-  const int head = (v * 8) / g.d;
-  dd = (v * 8) % g.d;
-  if (plane < g.CAP) {
-    const int slot = g.slots[plane];
-    if (slot < 0 || slot >= g.CAP) return false;
-    src = g.pk + ((long long)slot * g.T + t) * g.pk_ld + head * g.pk_hs;
-    pos = g.ppos[plane];
-  } else {
-    const int f = plane - g.CAP;
-    src = g.ck + ((long long)f * g.T + t) * g.ck_ld + head * g.ck_hs;
-    pos = g.qpos[f];
-  }
-  src += dd;
-  dst = g.k_out + ((long long)plane * g.T + t) * g.hd + head * g.d + dd;
-  return true;
-}
+// One CTA = kGatherRows token rows of one plane (blockIdx.y): the plane's
+// source (cache slot or current frame) and position are read once per CTA.
+// Thread t owns 16-byte vectors t, t + blockDim.x, ... of every row, so its
+// head, offset within the head and rotary coefficients are fixed for the CTA;
+// a vector's row loads are all in flight before its stores (32-bit offsets
+// within the plane). Workspace plane order: routed past planes [0, CAP) (slot
+// indirection applied), then the current frames.
+constexpr int kGatherRows = 8;
 
 __global__ void rope_gather_kernel(GatherParams g) {
   rc::pdl_trigger();
   rc::pdl_wait();
-  if (blockIdx.x == 0)
+  if (blockIdx.x == 0 && blockIdx.y == 0)
     for (int i = threadIdx.x; i < g.n_counters; i += blockDim.x) g.counters[i] = 0;
-  const int vec = g.hd >> 3;
-  const long long total = (long long)(g.CAP + g.QT) * g.T * vec;
-  const long long stride = (long long)gridDim.x * blockDim.x;
-  for (long long base = blockIdx.x * (long long)blockDim.x + threadIdx.x; base < total;
-       base += stride * kGatherUnroll) {
-    uint4 raw[kGatherUnroll];
-    __nv_bfloat16* dst[kGatherUnroll];
-    int pos[kGatherUnroll], dd[kGatherUnroll];
+  const int plane = blockIdx.y;
+  const __nv_bfloat16* src_base;
+  long long ld, hs;
+  int pos;
+  if (plane < g.CAP) {
+    const int slot = g.slots[plane];
+    if (slot < 0 || slot >= g.CAP) return;   // not visible: the attention never reads this plane
+    src_base = g.pk + (long long)slot * g.T * g.pk_ld;
+    ld = g.pk_ld;
+    hs = g.pk_hs;
+    pos = g.ppos[plane];
+  } else {
+    const int f = plane - g.CAP;
+    src_base = g.ck + (long long)f * g.T * g.ck_ld;
+    ld = g.ck_ld;
+    hs = g.ck_hs;
+    pos = g.qpos[f];
+  }
+  const int t0 = blockIdx.x * kGatherRows;
+  const int rows = min(kGatherRows, g.T - t0);
+  __nv_bfloat16* dst_base = g.k_out + ((long long)plane * g.T + t0) * g.hd;
+  src_base += (long long)t0 * ld;
+  const int vec = g.hd >> 3, dvec = g.d >> 3;
+  for (int v = threadIdx.x; v < vec; v += blockDim.x) {
+    const int head = v / dvec, dd = (v - head * dvec) * 8;
+    const __nv_bfloat16* src = src_base + head * hs + dd;
+    __nv_bfloat16* dst = dst_base + v * 8;
+    uint4 raw[kGatherRows];
 #pragma unroll
-    for (int u = 0; u < kGatherUnroll; ++u) {
-      const long long i = base + u * stride;
-      const __nv_bfloat16* src;
-      dst[u] = nullptr;
-      if (i < total && gather_src(g, i, vec, src, dst[u], pos[u], dd[u]))
-        raw[u] = *reinterpret_cast<const uint4*>(src);
-      else
-        dst[u] = nullptr;
+    for (int r = 0; r < kGatherRows; ++r)
+      if (r < rows) raw[r] = rc::ld_in(reinterpret_cast<const uint4*>(src + r * ld));
+    const bool rot = dd < g.td;
+    float c[4] = {1.f, 1.f, 1.f, 1.f}, sn[4] = {0.f, 0.f, 0.f, 0.f};
+    if (rot) {
+      const float* cs = g.cos + (size_t)pos * (g.td >> 1);
+      const float* ss = g.sin + (size_t)pos * (g.td >> 1);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int pr = (dd >> 1) + j;
+        if (2 * pr < g.td) {
+          c[j] = rc::ld_in(cs + pr);
+          sn[j] = rc::ld_in(ss + pr);
+        }
+      }
     }
 #pragma unroll
-    for (int u = 0; u < kGatherUnroll; ++u) {
-      if (!dst[u]) continue;
-      uint4 r4 = raw[u];
-      if (dd[u] < g.td) {
+    for (int r = 0; r < kGatherRows; ++r) {
+      if (r >= rows) continue;
+      uint4 r4 = raw[r];
+      if (rot) {
         uint32_t w[4] = {r4.x, r4.y, r4.z, r4.w};
-        rotate_pairs(w, dd[u] >> 1, g.td, g.cos + (size_t)pos[u] * (g.td >> 1),
-                     g.sin + (size_t)pos[u] * (g.td >> 1));
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          if (2 * ((dd >> 1) + j) < g.td) {
+            const float e = __uint_as_float(w[j] << 16), o = __uint_as_float(w[j] & 0xffff0000u);
+            w[j] = pack_bf16x2(__fsub_rn(__fmul_rn(e, c[j]), __fmul_rn(o, sn[j])),
+                               __fadd_rn(__fmul_rn(e, sn[j]), __fmul_rn(o, c[j])));
+          }
+        }
         r4 = make_uint4(w[0], w[1], w[2], w[3]);
       }
-      *reinterpret_cast<uint4*>(dst[u]) = r4;
+      *reinterpret_cast<uint4*>(dst + (long long)r * g.hd) = r4;
     }
   }
 }
@@ -1005,10 +1018,10 @@ int rc_paired_attention(const void* q, const void* ck, const void* cv, const voi
     const __nv_bfloat16* pvb = CAP ? reinterpret_cast<const __nv_bfloat16*>(pv) + b * strides[12] : nullptr;
     GatherParams g{ckb, strides[4], strides[5], pkb, strides[10], strides[11], slots, past_positions,
                    query_positions, cos, sin, ks, T, QT, CAP, (int)hd, td, d, counters, kMaxPieces};
-    const long long work = (long long)(QT + CAP) * T * (hd / 8);
-    long long blocks = (work + 255) / 256;
-    if (blocks > 148LL * 16) blocks = 148LL * 16;
-    if ((r = rc::check_launch(rc::launch_pdl(rope_gather_kernel, dim3((int)blocks), dim3(256), 0, stream, g),
+    const int vec = (int)(hd / 8);
+    const int threads = vec < 512 ? (vec + 31) / 32 * 32 : 512;
+    if ((r = rc::check_launch(rc::launch_pdl(rope_gather_kernel, dim3((T + kGatherRows - 1) / kGatherRows, QT + CAP),
+                                             dim3(threads), 0, stream, g),
                               "rc_paired_attention(rope)")))
       return r;
     CUtensorMap tk, tpv, tcv;

@@ -365,40 +365,33 @@ __global__ void kv_commit_kernel(CommitArgs a) {
 
 // Same copy with the plane plan read from device memory:
 // plan = [n, src0, dst0, src1, dst1, ...] (n <= max_planes), so a captured
-// graph stays valid while the routing changes between replays.
-constexpr int kCopyUnroll = 4;   // independent 16-byte loads in flight per thread
+// graph stays valid while the routing changes between replays. One CTA =
+// kCommitRows rows of one plan entry (blockIdx.y) of K or V (blockIdx.z): the
+// plan is read once per CTA and the row loop uses 32-bit offsets, with all of
+// a thread's row loads in flight before its stores.
+constexpr int kCommitRows = 8;
+constexpr int kCommitThreads = 128;
 
-__global__ void kv_commit_planned_kernel(CommitArgs a, const int* plan) {
+__global__ void __launch_bounds__(kCommitThreads) kv_commit_planned_kernel(CommitArgs a, const int* plan) {
   rc::pdl_trigger();
   rc::pdl_wait();
-  const int n = min(plan[0], a.n);
-  const int vec_per_row = a.row_bytes >> 4;
-  const long long per_plane = (long long)a.span * vec_per_row;
-  const long long total = 2LL * a.n * per_plane;
-  const long long stride = (long long)gridDim.x * blockDim.x;
-  for (long long base = blockIdx.x * (long long)blockDim.x + threadIdx.x; base < total;
-       base += stride * kCopyUnroll) {
-    uint4 val[kCopyUnroll];
-    uint4* dst[kCopyUnroll];
+  const int c = blockIdx.y, t = blockIdx.z;
+  if (c >= min(plan[0], a.n)) return;
+  const int sp = plan[1 + 2 * c], dp = plan[2 + 2 * c];
+  if (sp < 0 || dp < 0 || dp >= a.dst_plane[0]) return;   // dst_plane[0] = slot capacity
+  const int vec = a.row_bytes >> 4;
+  const int r0 = blockIdx.x * kCommitRows;
+  const int rows = min(kCommitRows, a.span - r0);
+  const uint8_t* src = a.src[t] + ((long long)sp * a.span + r0) * a.src_ld[t];
+  uint8_t* dst = a.dst[t] + ((long long)dp * a.span + r0) * a.dst_ld[t];
+  for (int v = threadIdx.x; v < vec; v += kCommitThreads) {
+    uint4 val[kCommitRows];
 #pragma unroll
-    for (int u = 0; u < kCopyUnroll; ++u) {
-      const long long i = base + u * stride;
-      dst[u] = nullptr;
-      if (i >= total) continue;
-      const int t = (int)(i / (a.n * per_plane));
-      const long long r = i % (a.n * per_plane);
-      const int c = (int)(r / per_plane);
-      if (c >= n) continue;
-      const int sp = plan[1 + 2 * c], dp = plan[2 + 2 * c];
-      if (sp < 0 || dp < 0 || dp >= a.dst_plane[0]) continue;   // dst_plane[0] = slot capacity
-      const long long q = r % per_plane;
-      const long long row = q / vec_per_row, v = q % vec_per_row;
-      val[u] = rc::ld_in(reinterpret_cast<const uint4*>(a.src[t] + ((long long)sp * a.span + row) * a.src_ld[t]) + v);
-      dst[u] = reinterpret_cast<uint4*>(a.dst[t] + ((long long)dp * a.span + row) * a.dst_ld[t]) + v;
-    }
+    for (int r = 0; r < kCommitRows; ++r)
+      if (r < rows) val[r] = rc::ld_in(reinterpret_cast<const uint4*>(src + r * a.src_ld[t]) + v);
 #pragma unroll
-    for (int u = 0; u < kCopyUnroll; ++u)
-      if (dst[u]) *dst[u] = val[u];
+    for (int r = 0; r < kCommitRows; ++r)
+      if (r < rows) reinterpret_cast<uint4*>(dst + r * a.dst_ld[t])[v] = val[r];
   }
 }
 
@@ -552,8 +545,8 @@ int rc_kv_commit_planned(const void* src_k, const void* src_v, long long src_ld_
   a.span = span;
   a.row_bytes = row_bytes;
   return rc::check_launch(
-      rc::launch_pdl(kv_commit_planned_kernel, dim3(grid_for(2LL * max_planes * span * (row_bytes / 16), 256)),
-                     dim3(256), 0, stream, a, plan),
+      rc::launch_pdl(kv_commit_planned_kernel, dim3((span + kCommitRows - 1) / kCommitRows, max_planes, 2),
+                     dim3(kCommitThreads), 0, stream, a, plan),
       "rc_kv_commit_planned");
 }
 
