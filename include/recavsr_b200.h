@@ -177,6 +177,16 @@ int rc_cross_attention(const void* q, const void* k, const void* v, const long l
                        int Nq, int Nk, int heads, int d, void* out, long long out_ld,
                        uint8_t* out_codes, uint8_t* out_scales, rc_stream_t stream);
 
+/* rc_cross_attention with a tail-split workspace of rc_cross_attention_workspace()
+ * bytes (16-byte aligned, zero-filled before its first use; each successful call
+ * leaves it zero-filled; calls sharing one must be ordered on one stream): the
+ * query tiles of the last partial wave run as key-range pieces. */
+long long rc_cross_attention_workspace(void);
+int rc_cross_attention_ws(const void* q, const void* k, const void* v, const long long* strides, int B,
+                          int Nq, int Nk, int heads, int d, void* out, long long out_ld,
+                          uint8_t* out_codes, uint8_t* out_scales, void* workspace,
+                          long long workspace_bytes, rc_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -725,6 +725,7 @@ attention_kernel(const __grid_constant__ CUtensorMap tm_k,
       asm volatile("bar.sync 5, 256;" ::: "memory");
       if (*s_last) {
         __threadfence();   // acquire: the other pieces' partials are visible from here
+        if (threadIdx.x == 64) p.counters[tail_unit] = 0;   // every piece has arrived: ready for the next launch
         const float* base = p.part + (size_t)tail_unit * nsplit * kPartFloats;
         float mq[kMaxSplit], cq[kMaxSplit];
         float mm = -INFINITY;
@@ -919,7 +920,7 @@ void plan_split(int units, int max_tiles, bool can_split, int& n_regular, int& s
   if (!tail) return;
   int s = sms / tail;
   s = s < cap ? s : cap;
-  s = s < max_tiles / 2 ? s : max_tiles / 2;   // at least two key tiles per piece
+  s = s < max_tiles / 4 ? s : max_tiles / 4;   // at least four key tiles per piece
   while (s > 1 && tail * s > kMaxPieces) --s;
   if (s < 2) return;
   n_regular = units - tail;
@@ -1075,10 +1076,31 @@ int rc_paired_attention(const void* q, const void* ck, const void* cv, const voi
 // over the 512 precomputed prompt keys). strides[9]: (batch, token, head)
 // element strides of q, k, v. Runs the same tcgen05 kernel on the inputs
 // directly (no workspace).
+long long rc_cross_attention_workspace(void) { return kSplitBytes; }
+
+int rc_cross_attention_ws(const void* q, const void* k, const void* v, const long long* strides, int B,
+                          int Nq, int Nk, int heads, int d, void* out, long long out_ld,
+                          uint8_t* out_codes, uint8_t* out_scales, void* workspace,
+                          long long workspace_bytes, cudaStream_t stream);
+
 int rc_cross_attention(const void* q, const void* k, const void* v, const long long* strides, int B,
                        int Nq, int Nk, int heads, int d, void* out, long long out_ld,
                        uint8_t* out_codes, uint8_t* out_scales, cudaStream_t stream) {
+  return rc_cross_attention_ws(q, k, v, strides, B, Nq, Nk, heads, d, out, out_ld, out_codes, out_scales,
+                               nullptr, 0, stream);
+}
+
+// Same, with a tail-split workspace (rc_cross_attention_workspace() bytes,
+// 16-byte aligned, zero-filled before its first use; every successful call
+// leaves it zero-filled): the query tiles of the last partial wave run as
+// key-range pieces. A null workspace runs every unit whole.
+int rc_cross_attention_ws(const void* q, const void* k, const void* v, const long long* strides, int B,
+                          int Nq, int Nk, int heads, int d, void* out, long long out_ld,
+                          uint8_t* out_codes, uint8_t* out_scales, void* workspace,
+                          long long workspace_bytes, cudaStream_t stream) {
   const char* what = "rc_cross_attention";
+  if (workspace && (workspace_bytes < kSplitBytes || !al16(workspace)))
+    return rc::set_error(RC_ERR_ARG, "%s: workspace of %lld bytes (16-byte aligned) required", what, kSplitBytes);
   if (B <= 0 || Nq < 0 || Nk <= 0 || heads <= 0 || !strides)
     return rc::set_error(RC_ERR_ARG, "%s: bad geometry", what);
   if (d != kD)
@@ -1115,9 +1137,13 @@ int rc_cross_attention(const void* q, const void* k, const void* v, const long l
     p.q_codes = out_codes;
     p.q_sf = out_scales;
     p.n_qtiles = (Nq + kBM - 1) / kBM;
-    p.n_regular = p.n_qtiles * heads;   // no workspace: no tail split
-    p.split = 1;
-    dim3 grid(p.n_regular);
+    const int units = p.n_qtiles * heads;
+    plan_split(units, (Nk + kBN - 1) / kBN, workspace != nullptr, p.n_regular, p.split);
+    p.part = reinterpret_cast<float*>(workspace);
+    p.counters = workspace ? reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(workspace) +
+                                                    (long long)kMaxPieces * kPartFloats * 4)
+                           : nullptr;
+    dim3 grid(p.n_regular + (units - p.n_regular) * p.split);
     if ((r = rc::check_launch(
              rc::launch_pdl(attention_kernel, grid, dim3(kThreads), SmemLayout::kAlloc, stream, tk, tv, tv, p),
              what)))

@@ -246,6 +246,16 @@ __global__ void __launch_bounds__(kRowThreads, 8) rmsnorm_rope_kernel(RmsArgs a)
     raw[i] = c < nch ? rc::ld_in(reinterpret_cast<const uint4*>(xp + (size_t)row * ldx) + c)
                      : make_uint4(0, 0, 0, 0);
   }
+  // The norm weights of this thread's chunks, loaded with the row (a store
+  // through `op` could alias them and would keep later loads behind it).
+  uint4 wraw[kRowChunks];
+  if (w) {
+#pragma unroll
+    for (int i = 0; i < kRowChunks; ++i) {
+      const int c = t + i * kRowThreads;
+      wraw[i] = c < nch ? rc::ld_in(reinterpret_cast<const uint4*>(w) + c) : make_uint4(0, 0, 0, 0);
+    }
+  }
   const int pos = row % a.span;
   const bool same_dd = ((8 * kRowThreads) % a.d) == 0;
   float cs[8], sn[8];
@@ -275,7 +285,7 @@ __global__ void __launch_bounds__(kRowThreads, 8) rmsnorm_rope_kernel(RmsArgs a)
     unpack8_fresh(raw[i], f);
     if (w) {
       float wf[8];
-      unpack8(rc::ld_in(reinterpret_cast<const uint4*>(w + n0)), wf);
+      unpack8(wraw[i], wf);
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const float2 y = __fmul2_rn(__fmul2_rn(make_float2(f[2 * j], f[2 * j + 1]), make_float2(r, r)),

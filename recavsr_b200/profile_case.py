@@ -115,12 +115,34 @@ def _rms():
     return run, 2 * M * DIM * 4, "GB/s"
 
 
+def _cross_attention(nk=512):
+    """Cross-attention of the body block over the prompt keys, NVFP4 output
+    (as the block runs it), with the tail-split workspace."""
+    g = torch.Generator(device="cuda")
+    g.manual_seed(0)
+    r = lambda *sh: torch.randn(*sh, generator=g, device="cuda").bfloat16()
+    q, k, v = r(M, HEADS, HD), r(nk, HEADS, HD), r(nk, HEADS, HD)
+    dim = HEADS * HD
+    codes = torch.empty(M, dim // 2, dtype=torch.uint8, device="cuda")
+    sf = torch.empty(scale_numel(M, dim), dtype=torch.uint8, device="cuda")
+    lib = _lib.library()
+    ws = torch.zeros(lib.rc_cross_attention_workspace(), dtype=torch.uint8, device="cuda")
+    st = (C.c_longlong * 9)(0, dim, HD, 0, dim, HD, 0, dim, HD)
+
+    def run():
+        _lib.check(lib.rc_cross_attention_ws(q.data_ptr(), k.data_ptr(), v.data_ptr(), st, 1, M, nk, HEADS,
+                                             HD, None, dim, codes.data_ptr(), sf.data_ptr(), ws.data_ptr(),
+                                             ws.numel(), _lib.stream()), "cross")
+    return run, 4.0 * HD * HEADS * M * nk, "TFLOP/s"
+
+
 CASES = {
     "gemm_up": lambda: _gemm(FFN, DIM, _lib.EPI_GELU_NVFP4),
     "gemm_qkv": lambda: _gemm(3 * DIM, DIM, _lib.EPI_BIAS),
     "gemm_o": lambda: _gemm(DIM, DIM, _lib.EPI_GATED_RESIDUAL),
     "gemm_down": lambda: _gemm(DIM, FFN, _lib.EPI_GATED_RESIDUAL),
     "attention": _attention,
+    "cross_attention": _cross_attention,
     "quant": _quant,
     "ln": _ln,
     "rms": _rms,

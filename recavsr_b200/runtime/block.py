@@ -184,10 +184,11 @@ class FusedBlock(torch.nn.Module):
                                 n, dim, self.head_dim, 1, None, None, _EPS, st), "cross_rms")
         hd = self.head_dim
         strides = (C.c_longlong * 9)(0, dim, hd, 0, dim, hd, 0, dim, hd)
-        chk(lib.rc_cross_attention(ws.q_rot.data_ptr(), self.cross_k.data_ptr(),
-                                   self.cross_v.data_ptr(), strides, 1, n, self.cross_k.shape[0],
-                                   self.heads, hd, None, dim, ws.a_codes.data_ptr(),
-                                   ws.a_scales.data_ptr(), st), "cross_attn")
+        chk(lib.rc_cross_attention_ws(ws.q_rot.data_ptr(), self.cross_k.data_ptr(),
+                                      self.cross_v.data_ptr(), strides, 1, n, self.cross_k.shape[0],
+                                      self.heads, hd, None, dim, ws.a_codes.data_ptr(),
+                                      ws.a_scales.data_ptr(), ws.cross_ws.data_ptr(), ws.cross_ws.numel(),
+                                      st), "cross_attn")
         self._gemm(lib, ws, ws.a_codes, ws.a_scales, self.co, n, _lib.EPI_RESIDUAL, h, st)
         # 7. FFN
         chk(lib.rc_ln_modulate_quant(h.data_ptr(), dim, n, dim, None, None, cshift.data_ptr(),
@@ -259,6 +260,10 @@ class Workspace:
         # the GEMMs leave it zero-filled).
         self.gemm_ws = torch.zeros((_lib.library().rc_gemm_split_workspace(),), dtype=torch.uint8,
                                    device=dev)
+        # Tail-split partials and counters of the cross-attention (zero-filled;
+        # the kernel leaves it zero-filled).
+        self.cross_ws = torch.zeros((_lib.library().rc_cross_attention_workspace(),), dtype=torch.uint8,
+                                    device=dev)
 
 
 def rope_tables(head_dim: int, height: int, width: int, device) -> dict:

@@ -133,9 +133,13 @@ def test_rejects_bad_geometry():
         paired_attention(q, q, q, e, e, i, i, qp, c, c, 4, 6, 2, 2)   # 3 frames
 
 
-@pytest.mark.parametrize("nq,nk,heads", [(192, 64, 6), (1760, 512, 24), (48, 16, 2)])
-def test_cross_attention(nq, nk, heads):
-    """Unmasked, rotary-free attention over the prompt keys (transformer.py:123-128)."""
+@pytest.mark.parametrize("split", [False, True])
+@pytest.mark.parametrize("nq,nk,heads", [(192, 64, 6), (1760, 512, 24), (1760, 2048, 24), (48, 16, 2)])
+def test_cross_attention(nq, nk, heads, split):
+    """Unmasked, rotary-free attention over the prompt keys (transformer.py:123-128);
+    split=True passes a tail-split workspace, twice in a row (1760 x 24 heads
+    over 2048 keys: the last wave's 40 query tiles run as three key-range
+    pieces each; over 512 keys the units are too short to split)."""
     import ctypes as C
     from recavsr_b200 import _lib
     rs = np.random.RandomState(nq + nk)
@@ -146,10 +150,18 @@ def test_cross_attention(nq, nk, heads):
     out = torch.empty(nq, heads, 128, dtype=torch.bfloat16, device="cuda")
     hd = heads * 128
     st = (C.c_longlong * 9)(0, hd, 128, 0, hd, 128, 0, hd, 128)
-    _lib.call("rc_cross_attention", dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), st, 1, nq, nk,
-              heads, 128, out.data_ptr(), hd, None, None, _lib.stream())
+    if split:
+        wsb = _lib.library().rc_cross_attention_workspace()
+        ws = torch.zeros(wsb, dtype=torch.uint8, device="cuda")
+        for _ in range(2):
+            _lib.call("rc_cross_attention_ws", dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), st, 1, nq,
+                      nk, heads, 128, out.data_ptr(), hd, None, None, ws.data_ptr(), wsb, _lib.stream())
+        assert int(ws[-640:].count_nonzero()) == 0   # the arrival counters are back at zero
+    else:
+        _lib.call("rc_cross_attention", dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), st, 1, nq, nk,
+                  heads, 128, out.data_ptr(), hd, None, None, _lib.stream())
     assert_no_device_error()
-    hs = [0, heads - 1]
+    hs = [0, 13 % heads, heads - 1]
     ref = oatt.plain_attention(q[:, hs], k[:, hs], v[:, hs])
     got = host(out)[:, hs]
     assert np.abs(got - ref).max() <= ABS and max_rel(got, ref) <= REL
