@@ -618,11 +618,13 @@ bool gemm_prefer_wide(int epi, int M, int N, int K) {
   }
   if (N % 256) return false;
   if (forced >= 0) return forced == 1;
-  // With a short MMA issue path the 128-column tile (double-buffered
-  // accumulator, epilogue overlapped) is the faster one at every DiT shape
-  // (M = 1760: QKV, o-proj, ffn_up and ffn_down all measured).
-  (void)epi; (void)M; (void)K;
-  return false;
+  // Measured on M = 1760 (same box, A/B): the 256-column tile wins only for
+  // the wide GELU + NVFP4 GEMM (ffn_up, N = 14336: 45.9 vs 48.0 us), where
+  // halving the MMA and scale-copy instructions per FLOP outweighs the
+  // exposed epilogue; it loses on o-proj / ffn_down (wave quantization at
+  // N = 3072) and ties on QKV.
+  (void)M; (void)K;
+  return epi == EPI_GELU_NVF4 && N >= 12288;
 }
 
 // Shared argument checks + tensor maps; `elem_bytes_x2` = 2 * bytes/element
