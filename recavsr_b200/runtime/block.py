@@ -298,6 +298,8 @@ class LayerStack:
         self.span = b0.height * b0.width
         self.rope = b0.tables["rope"]
         self._ws: dict[int, Workspace] = {}
+        self._io: dict[int, dict] = {}          # step_host staging buffers and events per token count
+        self._copy_stream = None
         self._graphs: dict[int, torch.cuda.CUDAGraph] = {}
         self.reset()
 
@@ -308,7 +310,14 @@ class LayerStack:
         L = len(self.blocks)
         # Device routing table: per layer [slots(8) | ppos(8) | plan(1+2*8)] + qpos(8).
         self._row = 8 + 8 + 17
-        self.route_host = torch.zeros((L * self._row + 8,), dtype=torch.int32, pin_memory=True)
+        # Pinned routing tables in a ring: the host may run several blocks ahead
+        # of the device, and a block's host-to-device copy reads its table when
+        # the stream reaches it, so a table is rewritten only after its copy ran.
+        self._route_ring = [torch.zeros((L * self._row + 8,), dtype=torch.int32, pin_memory=True)
+                            for _ in range(4)]
+        self._route_copied = [None] * len(self._route_ring)
+        self._route_i = 0
+        self.route_host = self._route_ring[0]
         self.route_dev = torch.zeros_like(self.route_host, device=self.device)
         shape = lambda c: (1, max(c.capacity, 1) * self.span, self.heads, self.head_dim)
         self.cache_k = [torch.zeros(shape(c), dtype=torch.bfloat16, device=self.device) for c in self.caches]
@@ -321,7 +330,12 @@ class LayerStack:
         return self._ws[n]
 
     def _plan(self, frames):
-        """Host routing for one block: fills route_host, advances the routers."""
+        """Host routing for one block: fills the next table of the ring (route_host),
+        advances the routers."""
+        j = self._route_i % len(self._route_ring)
+        if self._route_copied[j] is not None:
+            self._route_copied[j].synchronize()        # its previous upload has run
+        self.route_host = self._route_ring[j]
         origin, _ = self.rope.positions(self.latent_offset, frames)
         qpos = [self.latent_offset - origin + f for f in range(frames)]
         r = self.route_host
@@ -367,7 +381,7 @@ class LayerStack:
         if n != frames * self.span:
             raise ValueError("hidden must hold `frames` complete planes.")
         self._plan(frames)
-        self.route_dev.copy_(self.route_host, non_blocking=True)
+        self._upload_route()
         if not graphs:
             self._layers(hidden, n, frames)
             return hidden
@@ -378,6 +392,65 @@ class LayerStack:
         g.replay()
         hidden.copy_(self._static[n])
         return hidden
+
+    def step_host(self, host_in: torch.Tensor, host_out: torch.Tensor, frames: int) -> None:
+        """One body block from pinned host memory to pinned host memory through
+        the captured graph: the host-to-device copy of this block's hidden state
+        and the device-to-host copy of its result run on a copy stream, so they
+        overlap the previous / next block's layer loop (double-buffered staging).
+        Asynchronous: call sync_host() before reading host_out."""
+        n = host_in.shape[0]
+        if n != frames * self.span or host_out.shape != host_in.shape:
+            raise ValueError("host_in / host_out must hold `frames` complete planes.")
+        if n not in self._graphs:
+            raise RuntimeError("capture() the graph for this token count first")
+        io = self._io.get(n)
+        if io is None:
+            mk = lambda: torch.empty((n, self.dim), dtype=torch.bfloat16, device=self.device)
+            io = {"in": [mk(), mk()], "out": [mk(), mk()], "k": 0,
+                  "in_ready": [torch.cuda.Event() for _ in range(2)],
+                  "consumed": [torch.cuda.Event() for _ in range(2)],
+                  "done": [torch.cuda.Event() for _ in range(2)],
+                  "drained": [torch.cuda.Event() for _ in range(2)]}
+            for e in io["consumed"] + io["drained"]:
+                e.record(torch.cuda.current_stream(self.device))
+            self._io[n] = io
+        if self._copy_stream is None:
+            self._copy_stream = torch.cuda.Stream(self.device)
+        k = io["k"] & 1
+        comp, cs = torch.cuda.current_stream(self.device), self._copy_stream
+        with torch.cuda.stream(cs):
+            cs.wait_event(io["consumed"][k])          # the block two steps back has read this buffer
+            io["in"][k].copy_(host_in, non_blocking=True)
+            io["in_ready"][k].record(cs)
+        self._plan(frames)
+        self._upload_route()
+        comp.wait_event(io["in_ready"][k])
+        self._static[n].copy_(io["in"][k])
+        io["consumed"][k].record(comp)
+        self._graphs[n].replay()
+        comp.wait_event(io["drained"][k])             # its previous result has left the device
+        io["out"][k].copy_(self._static[n])
+        io["done"][k].record(comp)
+        with torch.cuda.stream(cs):
+            cs.wait_event(io["done"][k])
+            host_out.copy_(io["out"][k], non_blocking=True)
+            io["drained"][k].record(cs)
+        io["k"] += 1
+
+    def _upload_route(self) -> None:
+        """Host-to-device copy of the table _plan just filled, on the current stream."""
+        j = self._route_i % len(self._route_ring)
+        self.route_dev.copy_(self.route_host, non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record(torch.cuda.current_stream(self.device))
+        self._route_copied[j] = ev
+        self._route_i += 1
+
+    def sync_host(self) -> None:
+        """Make the current stream wait for every step_host copy issued so far."""
+        if self._copy_stream is not None:
+            torch.cuda.current_stream(self.device).wait_stream(self._copy_stream)
 
     def capture(self, n: int, frames: int):
         """Capture one block of the layer loop for a token count n (after at

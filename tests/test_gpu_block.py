@@ -235,7 +235,9 @@ def test_layer_stack_streaming_and_graph_replay():
     """3 layers, prefix + 8 body blocks. Per block the oracle starts from the
     stack's own cache contents (teacher forcing, so NVFP4 code flips do not
     compound across blocks); routing tables must equal the oracle router's
-    exactly, and graph replay must be bit-identical to eager launches."""
+    exactly, graph replay must be bit-identical to eager launches, and so must
+    the host-to-host streaming path (step_host, copies overlapping the
+    neighbouring blocks, no host sync until the end)."""
     from recavsr_b200.runtime.block import FusedBlock, LayerStack, rope_tables
     dim, heads, ffn, H, W = 256, 2, 512, 4, 6
     span = H * W
@@ -246,7 +248,8 @@ def test_layer_stack_streaming_and_graph_replay():
     def make():
         return LayerStack([FusedBlock(_weights(p, heads), H, W, tables) for p in ps], actions)
 
-    eager, graphed = make(), make()
+    eager, graphed, streamed = make(), make(), make()
+    pending = []   # (pinned input, pinned output, eager result) of streamed body blocks
     params = [_oracle_params(p, H, W, heads, host(b.cross_k), host(b.cross_v), host(b.modulation))
               for p, b in zip(ps, eager.blocks)]
     routers = [RouterState(a) for a in actions]
@@ -261,12 +264,22 @@ def test_layer_stack_streaming_and_graph_replay():
         he = dev_bf16(x)
         eager.step(he, frames)
         hg = dev_bf16(x)
+        stream_now = frames == 2 and captured
         if frames == 2 and not captured:
             graphed.step(hg, frames)          # eager first body step sets kernel attributes
             graphed.capture(2 * span, 2)
+            hs = dev_bf16(x)
+            streamed.step(hs, frames)
+            streamed.capture(2 * span, 2)
             captured = True
         else:
             graphed.step(hg, frames, graphs=(frames == 2 and captured))
+            if not stream_now:
+                streamed.step(dev_bf16(x), frames)
+        if stream_now:
+            hin = torch.tensor(x).bfloat16().pin_memory()
+            hout = torch.empty_like(hin).pin_memory()
+            streamed.step_host(hin, hout, frames)
         ref, routes = _oracle_stack_step(params, routers, caches, x, start, frames, H, W, heads)
         start += frames
         for i, (slots, ppos) in enumerate(routes):
@@ -278,4 +291,11 @@ def test_layer_stack_streaming_and_graph_replay():
         got = host(he)
         _close(got, ref, BLOCK_REL_L2, BLOCK_MAX_FRAC)
         np.testing.assert_array_equal(host(hg), got)
+        if stream_now:
+            pending.append((hin, hout, got))
+    streamed.sync_host()
+    torch.cuda.synchronize()
+    assert len(pending) == 7
+    for hin, hout, got in pending:
+        np.testing.assert_array_equal(hout.float().numpy(), got)
     assert_no_device_error()
