@@ -67,20 +67,39 @@ def peaks():
 
 # ------------------------------------------------------------------ clocks
 class ClockSampler:
-    """nvidia-smi samples during the timed region (clocks + throttle reasons)."""
+    """SM clock, power and clock-event reasons sampled during the timed region:
+    NVML read every 10 ms from a thread (read-only queries; the GPU is found
+    by the PCI bus id of the torch device, so CUDA_VISIBLE_DEVICES remapping
+    does not matter), or `nvidia-smi -lms 100` where NVML is unavailable."""
 
+    REASONS = (("hw_slowdown", 0x8 | 0x80), ("sw_power_cap", 0x4), ("sw_thermal_slowdown", 0x20),
+               ("hw_thermal_slowdown", 0x40))
     FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
               "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
               "clocks_event_reasons.sw_power_cap")
 
     def __init__(self, index: int):
-        self.index, self.rows, self.proc = index, [], None
+        self.index, self.rows, self.proc, self.nvml, self.stop = index, [], None, None, False
+        self.max_mhz = None
 
     def __enter__(self):
         try:
+            import pynvml
+            import torch
+            pynvml.nvmlInit()
+            pr = torch.cuda.get_device_properties(self.index)
+            bus = f"{pr.pci_domain_id:08X}:{pr.pci_bus_id:02X}:{pr.pci_device_id:02X}.0"
+            self.nvml = (pynvml, pynvml.nvmlDeviceGetHandleByPciBusId(bus))
+            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(self.nvml[1], pynvml.NVML_CLOCK_SM))
+            self.thread = threading.Thread(target=self._poll, daemon=True)
+            self.thread.start()
+            return self
+        except Exception:
+            self.nvml = None
+        try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
+                 "--format=csv,noheader,nounits", "-lms", "100"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
@@ -88,29 +107,50 @@ class ClockSampler:
             self.proc = None
         return self
 
+    def _poll(self):
+        nv, h = self.nvml
+        while not self.stop:
+            try:
+                sm = float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM))
+                mask = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                power = nv.nvmlDeviceGetPowerUsage(h) / 1000.0
+            except Exception:
+                break
+            self.rows.append((sm, power, mask))
+            time.sleep(0.01)
+
     def _read(self):
         for line in self.proc.stdout:
             parts = [p.strip() for p in line.split(",")]
             if len(parts) == 7:
-                self.rows.append(parts)
+                try:
+                    self.max_mhz = float(parts[1])
+                    mask = sum(bit for (name, bit), v in zip(
+                        (("hw_slowdown", 0x8), ("hw_thermal_slowdown", 0x40), ("sw_thermal_slowdown", 0x20),
+                         ("sw_power_cap", 0x4)), parts[3:]) if v.lower() == "active")
+                    self.rows.append((float(parts[0]), float(parts[2]), mask))
+                except ValueError:
+                    pass
 
     def __exit__(self, *exc):
+        self.stop = True
         if self.proc:
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
             except subprocess.TimeoutExpired:
                 self.proc.kill()
+        elif self.nvml:
+            self.thread.join(timeout=1)
 
     def summary(self):
         if not self.rows:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        sm = [float(r[0]) for r in self.rows if r[0].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({n for r in self.rows for n, v in zip(names, r[3:]) if v.lower() == "active"})
-        return {"sm_mhz": statistics.median(sm) if sm else None,
-                "sm_max_mhz": float(self.rows[0][1]) if self.rows[0][1].replace(".", "").isdigit() else None,
-                "reasons": reasons, "samples": len(self.rows)}
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unsampled"]}
+        reasons = sorted({name for _, _, m in self.rows for name, bits in self.REASONS if m & bits})
+        return {"sm_mhz": statistics.median(r[0] for r in self.rows), "sm_max_mhz": self.max_mhz,
+                "reasons": reasons, "samples": len(self.rows),
+                "power_w": statistics.median(r[1] for r in self.rows),
+                "source": "nvml" if self.nvml else "nvidia-smi"}
 
 
 # -------------------------------------------------------------- model setup
