@@ -379,91 +379,54 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
       const int as = local % kAcc;
       const bool got = __all_sync(0xffffffffu, wait(&acc_full[as], (uint32_t)((local / kAcc) & 1), 4));
       if (!got && (BN != 128 || un.piece < 0)) break;
-      uint32_t acc[kCols];
-      if (got) {
-        sm100::tc_fence_after();
-        const uint32_t t_row = tmem_acc + as * BN + part * kCols + ((uint32_t)(quad * 32) << 16);
-#pragma unroll
-        for (int c = 0; c < kCols; c += 16)
-          sm100::tmem_ld16(t_row + c, *reinterpret_cast<uint32_t(*)[16]>(&acc[c]));
-        sm100::tmem_ld_wait();
-        sm100::tc_fence_before();
-        sm100::mbar_arrive(&acc_empty[as]);      // accumulator free: next tile may start
-      }
-      if (BN == 128 && un.piece >= 0) {   // (the host splits 128-column tiles only)
-        // Split tile: store this unit's partial, count the arrival; the last
-        // unit to arrive sums every unit's partial in unit order.
-        float4* mine = reinterpret_cast<float4*>(p.part + (size_t)un.piece * (BM * BN));
-        if (got) {
-#pragma unroll
-          for (int c = 0; c < kCols; c += 4)
-            __stcg(mine + ((part * kCols + c) >> 2) * BM + row_in_tile,
-                   make_float4(__uint_as_float(acc[c]), __uint_as_float(acc[c + 1]),
-                               __uint_as_float(acc[c + 2]), __uint_as_float(acc[c + 3])));
-        } else if (lane == 0) {
-          s_flags[1] = 1;
-        }
-        __threadfence();
-        asm volatile("bar.sync 1, %0;" ::"r"(32 * epi_warps<EPI>()) : "memory");
-        const int tail_tile = un.tile - p.n_regular;
-        if (threadIdx.x == 64)
-          s_flags[0] = !s_flags[1] && atomicAdd(&p.counters[tail_tile], 1) == p.split - 1;
-        asm volatile("bar.sync 1, %0;" ::"r"(32 * epi_warps<EPI>()) : "memory");
-        if (s_flags[1]) break;
-        if (!s_flags[0]) continue;
-        __threadfence();   // acquire: the other units' partials are visible from here
-        // All of a unit's loads are issued before any is used: one L2 round
-        // trip per unit, not one per column quad.
-        const float4* src = reinterpret_cast<const float4*>(p.part + (size_t)tail_tile * p.split * (BM * BN)) +
-                            ((part * kCols) >> 2) * BM + row_in_tile;
-        float4 sum[kCols / 4];
-#pragma unroll
-        for (int i = 0; i < kCols / 4; ++i) sum[i] = __ldcg(src + i * BM);
-        for (int q = 1; q < p.split; ++q) {
-          float4 v[kCols / 4];
-#pragma unroll
-          for (int i = 0; i < kCols / 4; ++i) v[i] = __ldcg(src + (size_t)q * (BM * BN / 4) + i * BM);
-#pragma unroll
-          for (int i = 0; i < kCols / 4; ++i) {
-            sum[i].x += v[i].x; sum[i].y += v[i].y; sum[i].z += v[i].z; sum[i].w += v[i].w;
-          }
-        }
-#pragma unroll
-        for (int i = 0; i < kCols / 4; ++i) {
-          acc[4 * i] = __float_as_uint(sum[i].x);
-          acc[4 * i + 1] = __float_as_uint(sum[i].y);
-          acc[4 * i + 2] = __float_as_uint(sum[i].z);
-          acc[4 * i + 3] = __float_as_uint(sum[i].w);
-        }
-        if (threadIdx.x == 64) p.counters[tail_tile] = 0;   // ready for the next launch
-      }
+      const uint32_t t_row = tmem_acc + as * BN + part * kCols + ((uint32_t)(quad * 32) << 16);
       const int row = mb * BM + row_in_tile;
       const bool row_ok = row < p.M;
-#pragma unroll
-      for (int cc = 0; cc < kCols; cc += 16) {
+      // Per 16-column chunk: the bias / residual / gate operands (zero-filled
+      // past the matrix edge).
+      struct Ops {
+        uint4 b0, b1, h0, h1;
+        float4 g[4];
+      };
+      auto load_ops = [&](int cc) -> Ops {
+        Ops o{};
         const int n0 = nb * BN + part * kCols + cc;
-        if (n0 >= p.N) continue;
+        if (!row_ok || n0 >= p.N) return o;
+        if (p.bias) {
+          const uint4* bp = reinterpret_cast<const uint4*>(p.bias + n0);
+          o.b0 = rc::ld_in(bp);
+          o.b1 = rc::ld_in(bp + 1);
+        }
+        if constexpr (EPI == EPI_GATED_RESIDUAL || EPI == EPI_RESIDUAL) {
+          const uint4* hp = reinterpret_cast<const uint4*>(p.out + (size_t)row * p.ldo + n0);
+          o.h0 = hp[0];
+          o.h1 = hp[1];
+        }
+        if constexpr (EPI == EPI_GATED_RESIDUAL) {
+          const float4* gp = reinterpret_cast<const float4*>(p.gate + n0);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) o.g[j] = rc::ld_in(gp + j);
+        }
+        return o;
+      };
+      // Epilogue math and stores of one chunk from its accumulator words.
+      auto emit_chunk = [&](int cc, const uint32_t* a16, const Ops& o) {
+        const int n0 = nb * BN + part * kCols + cc;
+        if (n0 >= p.N) return;
         if (!row_ok) {
           // Padding rows of the next linear's scale atoms must read as zero.
           if constexpr (EPI == EPI_GELU_NVF4) p.q_sf[rc::sf_offset(row, n0 >> 4, (p.N + 63) >> 6)] = 0;
-          continue;
+          return;
         }
         // y = bf16(acc * alpha + bias), two columns per packed fp32 op.
         float v[16];
         uint32_t w[8];
         {
-          uint32_t bw[8];
-          if (p.bias) {
-            const uint4* bp = reinterpret_cast<const uint4*>(p.bias + n0);
-            const uint4 b0 = rc::ld_in(bp), b1 = rc::ld_in(bp + 1);
-            bw[0] = b0.x; bw[1] = b0.y; bw[2] = b0.z; bw[3] = b0.w;
-            bw[4] = b1.x; bw[5] = b1.y; bw[6] = b1.z; bw[7] = b1.w;
-          }
+          const uint32_t bw[8] = {o.b0.x, o.b0.y, o.b0.z, o.b0.w, o.b1.x, o.b1.y, o.b1.z, o.b1.w};
           const float2 alpha2 = make_float2(alpha, alpha);
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
-            float2 x = __fmul2_rn(make_float2(__uint_as_float(acc[cc + 2 * j]), __uint_as_float(acc[cc + 2 * j + 1])),
-                                  alpha2);
+            float2 x = __fmul2_rn(make_float2(__uint_as_float(a16[2 * j]), __uint_as_float(a16[2 * j + 1])), alpha2);
             if (p.bias) {
               float2 b;
               unpack_bf16x2(bw[j], b.x, b.y);
@@ -474,27 +437,18 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
           }
         }
         if constexpr (EPI == EPI_GATED_RESIDUAL || EPI == EPI_RESIDUAL) {
-          __nv_bfloat16* hp = p.out + (size_t)row * p.ldo + n0;
-          const uint4 h0 = *reinterpret_cast<const uint4*>(hp);
-          const uint4 h1 = *reinterpret_cast<const uint4*>(hp + 8);
-          const uint32_t hw[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
-          float gt[16];
-          if constexpr (EPI == EPI_GATED_RESIDUAL) {
-            const float4* gp = reinterpret_cast<const float4*>(p.gate + n0);
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const float4 g4 = rc::ld_in(gp + j);
-              gt[4 * j] = g4.x; gt[4 * j + 1] = g4.y; gt[4 * j + 2] = g4.z; gt[4 * j + 3] = g4.w;
-            }
-          }
+          const uint32_t hw[8] = {o.h0.x, o.h0.y, o.h0.z, o.h0.w, o.h1.x, o.h1.y, o.h1.z, o.h1.w};
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
             float2 h;
             unpack_bf16x2(hw[j], h.x, h.y);
             float2 add = make_float2(v[2 * j], v[2 * j + 1]);
-            if constexpr (EPI == EPI_GATED_RESIDUAL) add = __fmul2_rn(add, make_float2(gt[2 * j], gt[2 * j + 1]));
-            const float2 o = __fadd2_rn(h, add);
-            w[j] = rc::pack_bf16x2(o.x, o.y);
+            if constexpr (EPI == EPI_GATED_RESIDUAL) {
+              const float4 g4 = o.g[j >> 1];
+              add = __fmul2_rn(add, (j & 1) ? make_float2(g4.z, g4.w) : make_float2(g4.x, g4.y));
+            }
+            const float2 r = __fadd2_rn(h, add);
+            w[j] = rc::pack_bf16x2(r.x, r.y);
           }
         }
         if constexpr (EPI == EPI_GELU_NVF4) {
@@ -525,11 +479,113 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
           }
           *reinterpret_cast<uint2*>(p.q_codes + (size_t)row * (p.N >> 1) + (n0 >> 1)) = make_uint2(lo, hi);
           p.q_sf[rc::sf_offset(row, n0 >> 4, (p.N + 63) >> 6)] = sfb;
-          if (!p.out) continue;
+          if (!p.out) return;
         }
         uint4* dst = reinterpret_cast<uint4*>(p.out + (size_t)row * p.ldo + n0);
         dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
         dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+      };
+      if (BN == 128 && un.piece >= 0) {   // (the host splits 128-column tiles only)
+        // Split tile: store this unit's partial, count the arrival. The last
+        // unit to arrive sums every unit's partial in unit order (per chunk,
+        // all units' words loaded together) into its own accumulator in TMEM
+        // and then runs the whole-tile epilogue below on it.
+        float4* mine = reinterpret_cast<float4*>(p.part + (size_t)un.piece * (BM * BN));
+        if (got) {
+          sm100::tc_fence_after();
+#pragma unroll
+          for (int cc = 0; cc < kCols; cc += 16) {
+            uint32_t a16[16];
+            sm100::tmem_ld16(t_row + cc, a16);
+            sm100::tmem_ld_wait();
+#pragma unroll
+            for (int c = 0; c < 16; c += 4)
+              __stcg(mine + ((part * kCols + cc + c) >> 2) * BM + row_in_tile,
+                     make_float4(__uint_as_float(a16[c]), __uint_as_float(a16[c + 1]),
+                                 __uint_as_float(a16[c + 2]), __uint_as_float(a16[c + 3])));
+          }
+        } else if (lane == 0) {
+          s_flags[1] = 1;
+        }
+        __threadfence();
+        asm volatile("bar.sync 1, %0;" ::"r"(32 * epi_warps<EPI>()) : "memory");
+        const int tail_tile = un.tile - p.n_regular;
+        if (threadIdx.x == 64)
+          s_flags[0] = !s_flags[1] && atomicAdd(&p.counters[tail_tile], 1) == p.split - 1;
+        asm volatile("bar.sync 1, %0;" ::"r"(32 * epi_warps<EPI>()) : "memory");
+        if (s_flags[1]) break;
+        if (!s_flags[0]) {
+          sm100::tc_fence_before();
+          sm100::mbar_arrive(&acc_empty[as]);      // accumulator free: next tile may start
+          continue;
+        }
+        __threadfence();   // acquire: the other units' partials are visible from here
+        const float4* src = reinterpret_cast<const float4*>(p.part + (size_t)tail_tile * p.split * (BM * BN)) +
+                            ((part * kCols) >> 2) * BM + row_in_tile;
+#pragma unroll 1
+        for (int cc = 0; cc < kCols; cc += 16) {
+          float4 q4[kMaxSplit][4];
+#pragma unroll
+          for (int q = 0; q < kMaxSplit; ++q)
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              if (q < p.split) q4[q][i] = __ldcg(src + (size_t)q * (BM * BN / 4) + ((cc >> 2) + i) * BM);
+          uint32_t a16[16];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            float4 sum = q4[0][i];
+#pragma unroll
+            for (int q = 1; q < kMaxSplit; ++q) {
+              if (q < p.split) {
+                sum.x += q4[q][i].x; sum.y += q4[q][i].y; sum.z += q4[q][i].z; sum.w += q4[q][i].w;
+              }
+            }
+            a16[4 * i] = __float_as_uint(sum.x);
+            a16[4 * i + 1] = __float_as_uint(sum.y);
+            a16[4 * i + 2] = __float_as_uint(sum.z);
+            a16[4 * i + 3] = __float_as_uint(sum.w);
+          }
+          sm100::tmem_st16(t_row + cc, a16);
+        }
+        sm100::tmem_st_wait();
+        if (threadIdx.x == 64) p.counters[tail_tile] = 0;   // ready for the next launch
+      }
+      if constexpr (kAcc == 2 && (EPI == EPI_GATED_RESIDUAL || EPI == EPI_RESIDUAL)) {
+        // Residual epilogues: per 16-column chunk, a TMEM load of its
+        // accumulator words; the next chunk's residual / gate / bias are loaded
+        // before this chunk's stores (a store to the residual buffer would
+        // otherwise keep them behind its round trip). The accumulator stays
+        // allocated until the tile's last chunk has been read; with two
+        // accumulator stages the MMA needs it again only two tiles later.
+        // (o-proj 1760 x 3072 x 3072: 23.6 -> 22.3 us.)
+        sm100::tc_fence_after();
+        Ops cur = load_ops(0);
+#pragma unroll
+        for (int cc = 0; cc < kCols; cc += 16) {
+          uint32_t a16[16];
+          sm100::tmem_ld16(t_row + cc, a16);
+          sm100::tmem_ld_wait();
+          Ops nxt;
+          if (cc + 16 < kCols) nxt = load_ops(cc + 16);
+          emit_chunk(cc, a16, cur);
+          cur = nxt;
+        }
+        sm100::tc_fence_before();
+        sm100::mbar_arrive(&acc_empty[as]);      // accumulator free
+      } else {
+        // Other epilogues: drain the tile's columns from TMEM into registers
+        // and release the accumulator first, so the next tile's MMAs overlap
+        // this tile's epilogue math (essential with a single accumulator).
+        uint32_t acc[kCols];
+        sm100::tc_fence_after();
+#pragma unroll
+        for (int c = 0; c < kCols; c += 16)
+          sm100::tmem_ld16(t_row + c, *reinterpret_cast<uint32_t(*)[16]>(&acc[c]));
+        sm100::tmem_ld_wait();
+        sm100::tc_fence_before();
+        sm100::mbar_arrive(&acc_empty[as]);      // accumulator free: next tile may start
+#pragma unroll
+        for (int cc = 0; cc < kCols; cc += 16) emit_chunk(cc, &acc[cc], load_ops(cc));
       }
     }
   }
