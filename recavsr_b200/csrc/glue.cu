@@ -126,7 +126,15 @@ __device__ __forceinline__ float row_sum(float v, float* red) {
   return t;
 }
 
-__global__ void __launch_bounds__(kRowThreads, 6) ln_modulate_kernel(LnArgs a) {
+// CH = chunks per thread (ceil(N / 8 / kRowThreads)); AFF / MOD: whether an
+// affine weight / bias or a modulation scale / shift may be present (register
+// arrays are sized for the inputs the launch has).
+template <int CH, bool AFF, bool MOD>
+constexpr int ln_min_blocks() {   // 6 resident CTAs where the registers allow it
+  return (CH * ((AFF ? 8 : 0) + (MOD ? 16 : 0)) > 48) ? 4 : 6;
+}
+template <int CH, bool AFF, bool MOD>
+__global__ void __launch_bounds__(kRowThreads, ln_min_blocks<CH, AFF, MOD>()) ln_modulate_kernel(LnArgs a) {
   __shared__ float red[4];
   rc::pdl_trigger();
   rc::pdl_wait();
@@ -142,16 +150,16 @@ __global__ void __launch_bounds__(kRowThreads, 6) ln_modulate_kernel(LnArgs a) {
     return;
   }
   const int nch = a.N >> 3;
-  uint4 raw[kRowChunks];
+  uint4 raw[CH];
 #pragma unroll
-  for (int i = 0; i < kRowChunks; ++i) {
+  for (int i = 0; i < CH; ++i) {
     const int c = t + i * kRowThreads;
     raw[i] = c < nch ? rc::ld_in(reinterpret_cast<const uint4*>(a.x + (size_t)row * a.ldx) + c)
                      : make_uint4(0, 0, 0, 0);
   }
   float s = 0.f;
 #pragma unroll
-  for (int i = 0; i < kRowChunks; ++i) {
+  for (int i = 0; i < CH; ++i) {
     float f[8];
     unpack8(raw[i], f);
 #pragma unroll
@@ -160,7 +168,7 @@ __global__ void __launch_bounds__(kRowThreads, 6) ln_modulate_kernel(LnArgs a) {
   const float mean = __fdiv_rn(row_sum(s, red), (float)a.N);
   float m2 = 0.f;
 #pragma unroll
-  for (int i = 0; i < kRowChunks; ++i) {
+  for (int i = 0; i < CH; ++i) {
     if (t + i * kRowThreads < nch) {
       float f[8];
       unpack8_fresh(raw[i], f);
@@ -172,11 +180,30 @@ __global__ void __launch_bounds__(kRowThreads, 6) ln_modulate_kernel(LnArgs a) {
     }
   }
   const float rstd = rsqrtf(__fdiv_rn(row_sum(m2, red), (float)a.N) + a.eps);
+  // Every per-column vector of this thread's chunks, loaded together before
+  // the first store (a store through a byte pointer may alias them, so a load
+  // inside the chunk loop would wait behind the previous chunk's stores).
+  uint4 wraw[AFF ? CH : 1], braw[AFF ? CH : 1];
+  float sc[MOD ? CH : 1][8], sh[MOD ? CH : 1][8];
+#pragma unroll
+  for (int i = 0; i < CH; ++i) {
+    const int c = t + i * kRowThreads;
+    const bool live = c < nch;
+    const int n0 = c * 8;
+    if constexpr (AFF) {
+      wraw[i] = live && a.weight ? rc::ld_in(reinterpret_cast<const uint4*>(a.weight + n0)) : make_uint4(0, 0, 0, 0);
+      braw[i] = live && a.bias ? rc::ld_in(reinterpret_cast<const uint4*>(a.bias + n0)) : make_uint4(0, 0, 0, 0);
+    }
+    if constexpr (MOD) {
+      if (live && a.scale) loadf8(a.scale + n0, sc[i]);
+      if (live && a.shift) loadf8(a.shift + n0, sh[i]);
+    }
+  }
   const int katoms = ((a.N >> 4) + 3) >> 2;
   const float2 nmean = make_float2(-mean, -mean), rstd2 = make_float2(rstd, rstd);
   const float2 one2 = make_float2(1.0f, 1.0f);
 #pragma unroll
-  for (int i = 0; i < kRowChunks; ++i) {
+  for (int i = 0; i < CH; ++i) {
     if (i * kRowThreads >= nch) break;                 // CTA-uniform
     const int c = t + i * kRowThreads;
     const bool live = c < nch;
@@ -184,21 +211,25 @@ __global__ void __launch_bounds__(kRowThreads, 6) ln_modulate_kernel(LnArgs a) {
     float f[8];
     unpack8_fresh(raw[i], f);
     if (live) {
-      float w[8], b[8], sh[8], sc[8];
-      if (a.weight) unpack8(rc::ld_in(reinterpret_cast<const uint4*>(a.weight + n0)), w);
-      if (a.bias) unpack8(rc::ld_in(reinterpret_cast<const uint4*>(a.bias + n0)), b);
-      if (a.scale) loadf8(a.scale + n0, sc);
-      if (a.shift) loadf8(a.shift + n0, sh);
+      float w[8], b[8];
+      if constexpr (AFF) {
+        if (a.weight) unpack8(wraw[i], w);
+        if (a.bias) unpack8(braw[i], b);
+      }
       // fl(fl(x - mean) * rstd), then each affine / modulation step rounded
       // separately, two columns per packed fp32 op; bf16 at the end.
       uint32_t h[4];
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         float2 y = __fmul2_rn(__fadd2_rn(make_float2(f[2 * j], f[2 * j + 1]), nmean), rstd2);
-        if (a.weight) y = __fmul2_rn(y, make_float2(w[2 * j], w[2 * j + 1]));
-        if (a.bias) y = __fadd2_rn(y, make_float2(b[2 * j], b[2 * j + 1]));
-        if (a.scale) y = __fmul2_rn(y, __fadd2_rn(one2, make_float2(sc[2 * j], sc[2 * j + 1])));
-        if (a.shift) y = __fadd2_rn(y, make_float2(sh[2 * j], sh[2 * j + 1]));
+        if constexpr (AFF) {
+          if (a.weight) y = __fmul2_rn(y, make_float2(w[2 * j], w[2 * j + 1]));
+          if (a.bias) y = __fadd2_rn(y, make_float2(b[2 * j], b[2 * j + 1]));
+        }
+        if constexpr (MOD) {
+          if (a.scale) y = __fmul2_rn(y, __fadd2_rn(one2, make_float2(sc[i][2 * j], sc[i][2 * j + 1])));
+          if (a.shift) y = __fadd2_rn(y, make_float2(sh[i][2 * j], sh[i][2 * j + 1]));
+        }
         h[j] = rc::pack_bf16x2(y.x, y.y);
         f[2 * j] = __uint_as_float(h[j] << 16);
         f[2 * j + 1] = __uint_as_float(h[j] & 0xffff0000u);
@@ -441,8 +472,16 @@ int rc_ln_modulate_quant(const void* x, long long ldx, int M, int N, const void*
            reinterpret_cast<const __nv_bfloat16*>(weight), reinterpret_cast<const __nv_bfloat16*>(bias),
            shift, scale, eps, reinterpret_cast<__nv_bfloat16*>(out), ldo, codes, scales_swizzled,
            global_scale, M, N};
-  return rc::check_launch(rc::launch_pdl(ln_modulate_kernel, dim3(M + ((codes && M % 128) ? 1 : 0)),
-                                         dim3(kRowThreads), 0, stream, a),
+  const int ch = ((N >> 3) + kRowThreads - 1) / kRowThreads;   // 1..kRowChunks
+  const bool aff = weight || bias, mod = shift || scale;
+  using K = void (*)(LnArgs);
+  static const K table[kRowChunks][4] = {
+      {ln_modulate_kernel<1, false, false>, ln_modulate_kernel<1, true, false>, ln_modulate_kernel<1, false, true>, ln_modulate_kernel<1, true, true>},
+      {ln_modulate_kernel<2, false, false>, ln_modulate_kernel<2, true, false>, ln_modulate_kernel<2, false, true>, ln_modulate_kernel<2, true, true>},
+      {ln_modulate_kernel<3, false, false>, ln_modulate_kernel<3, true, false>, ln_modulate_kernel<3, false, true>, ln_modulate_kernel<3, true, true>},
+      {ln_modulate_kernel<4, false, false>, ln_modulate_kernel<4, true, false>, ln_modulate_kernel<4, false, true>, ln_modulate_kernel<4, true, true>}};
+  const K kern = table[ch - 1][(aff ? 1 : 0) + (mod ? 2 : 0)];
+  return rc::check_launch(rc::launch_pdl(kern, dim3(M + ((codes && M % 128) ? 1 : 0)), dim3(kRowThreads), 0, stream, a),
                           "rc_ln_modulate_quant");
 }
 
