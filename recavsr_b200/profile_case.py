@@ -140,6 +140,7 @@ CASES = {
     "gemm_up": lambda: _gemm(FFN, DIM, _lib.EPI_GELU_NVFP4),
     "gemm_qkv": lambda: _gemm(3 * DIM, DIM, _lib.EPI_BIAS),
     "gemm_o": lambda: _gemm(DIM, DIM, _lib.EPI_GATED_RESIDUAL),
+    "gemm_cq": lambda: _gemm(DIM, DIM, _lib.EPI_BIAS),
     "gemm_down": lambda: _gemm(DIM, FFN, _lib.EPI_GATED_RESIDUAL),
     "attention": _attention,
     "cross_attention": _cross_attention,
