@@ -51,25 +51,30 @@ def _gemm(n, k, epi):
     return run, 2.0 * M * n * k, "TFLOP/s"
 
 
-def _attention(planes=4):
+def _attention(planes=4, h=H, w=W, window=None):
+    """Routed attention of a 2-frame query block over `planes` routed planes
+    plus the 2 current frames; window None = the grid (the sdpa path), else
+    (wh, ww) local windows. FLOPs count visible keys only."""
     from .kernels.local_attention import routed_attention
     from .runtime.block import rope_tables
     g = torch.Generator(device="cuda")
     g.manual_seed(0)
-    t = H * W
+    t = h * w
+    wh, ww = window if window else (h, w)
     r = lambda *s: torch.randn(*s, generator=g, device="cuda").bfloat16()
     q, k, v = r(1, 2 * t, HEADS, HD), r(1, 2 * t, HEADS, HD), r(1, 2 * t, HEADS, HD)
     pk, pv = r(1, planes * t, HEADS, HD), r(1, planes * t, HEADS, HD)
     slots = torch.arange(planes, dtype=torch.int32, device="cuda")
     ppos = torch.arange(planes, dtype=torch.int32, device="cuda")
     qpos = torch.tensor([planes, planes + 1], dtype=torch.int32, device="cuda")
-    tb = rope_tables(HD, H, W, "cuda")
+    tb = rope_tables(HD, h, w, "cuda")
     out = torch.empty_like(q)
 
     def run():
         routed_attention(q, k, v, pk, pv, slots, ppos, qpos, tb["temporal_cos"], tb["temporal_sin"],
-                         H, W, H, W, out=out)
-    return run, 4.0 * HD * HEADS * (2 * t) * t * (planes + 2), "TFLOP/s"
+                         h, w, wh, ww, out=out)
+    keys = min(h, wh) * min(w, ww)          # per query and visible plane
+    return run, 4.0 * HD * HEADS * (2 * t) * keys * (planes + 2), "TFLOP/s"
 
 
 def _quant():
@@ -143,6 +148,8 @@ CASES = {
     "gemm_cq": lambda: _gemm(DIM, DIM, _lib.EPI_BIAS),
     "gemm_down": lambda: _gemm(DIM, FFN, _lib.EPI_GATED_RESIDUAL),
     "attention": _attention,
+    # cfg5 stream: 1080p output (34 x 60 tokens), 22 x 40 local windows
+    "attention_local_1080p": lambda: _attention(planes=4, h=34, w=60, window=(22, 40)),
     "cross_attention": _cross_attention,
     "quant": _quant,
     "ln": _ln,
