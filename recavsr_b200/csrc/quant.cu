@@ -71,64 +71,144 @@ nvfp4_quantize_kernel(const __nv_bfloat16* x, int M, int K, long long ldx, float
 }
 
 // ---------------------------------------------------------------- FP8
-__global__ void absmax_bf16_kernel(const __nv_bfloat16* x, int M, int K, long long ldx,
-                                   unsigned int* amax_bits) {
-  rc::pdl_trigger();
-  rc::pdl_wait();
-  float m = 0.0f;
-  const int kv = K >> 3;  // uint4 per row
-  const long long total = (long long)M * kv;
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
-       i += (long long)gridDim.x * blockDim.x) {
-    const long long row = i / kv, c = i % kv;
-    uint4 v = rc::ld_in(reinterpret_cast<const uint4*>(x + row * ldx) + c);
-    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const float a = __uint_as_float(w[j] << 16), b = __uint_as_float(w[j] & 0xffff0000u);
-      // NaN must win (torch amax propagates NaN): compare on the bit pattern.
-      m = __uint_as_float(max(__float_as_uint(m), __float_as_uint(fabsf(a))));
-      m = __uint_as_float(max(__float_as_uint(m), __float_as_uint(fabsf(b))));
-    }
-  }
-  unsigned int mb = __float_as_uint(m);
-#pragma unroll
-  for (int o = 16; o; o >>= 1) mb = max(mb, __shfl_xor_sync(0xffffffffu, mb, o));
-  if ((threadIdx.x & 31) == 0 && mb) atomicMax(amax_bits, mb);
+// Both passes walk the matrix as 16-byte vectors of 8 bf16 (index i = row *
+// K/8 + column vector), kF8Unroll vectors in flight per thread. kDense: rows
+// are packed (ldx == K), so vector i sits at x + 8 i and no division is needed.
+constexpr int kF8Threads = 256;
+constexpr int kF8Unroll = 4;
+
+template <bool kDense>
+__device__ __forceinline__ uint4 f8_load(const __nv_bfloat16* x, long long kv, long long ldx, long long i) {
+  if (kDense) return rc::ld_in(reinterpret_cast<const uint4*>(x) + i);
+  const long long row = i / kv;
+  return rc::ld_in(reinterpret_cast<const uint4*>(x + row * ldx) + (i - row * kv));
 }
 
-__global__ void fp8_quantize_kernel(const __nv_bfloat16* x, int M, int K, long long ldx,
-                                    const unsigned int* amax_bits, float* scale_out, uint8_t* q) {
+// max over the 8 elements of |x| as fp32 bit patterns: a bf16 is the high half
+// of its fp32, clearing the sign gives |x|, and unsigned order of non-negative
+// fp32 patterns is numeric order with NaN above +inf (torch's amax propagates
+// NaN, so NaN must win).
+__device__ __forceinline__ uint32_t absmax8_bits(uint4 v) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+  uint32_t m = 0;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) m = max(m, max((w[j] << 16) & 0x7fffffffu, w[j] & 0x7fff0000u));
+  return m;
+}
+
+template <bool kDense>
+__global__ void __launch_bounds__(kF8Threads) absmax_bf16_kernel(const __nv_bfloat16* x, int M, int K,
+                                                                  long long ldx, unsigned int* amax_bits) {
+  rc::pdl_trigger();
+  rc::pdl_wait();
+  const long long kv = K >> 3, total = (long long)M * kv;
+  const long long stride = (long long)gridDim.x * kF8Threads;
+  long long i = blockIdx.x * (long long)kF8Threads + threadIdx.x;
+  uint32_t m = 0;
+  for (; i + (kF8Unroll - 1) * stride < total; i += kF8Unroll * stride) {
+    uint4 v[kF8Unroll];
+#pragma unroll
+    for (int u = 0; u < kF8Unroll; ++u) v[u] = f8_load<kDense>(x, kv, ldx, i + u * stride);
+#pragma unroll
+    for (int u = 0; u < kF8Unroll; ++u) m = max(m, absmax8_bits(v[u]));
+  }
+  for (; i < total; i += stride) m = max(m, absmax8_bits(f8_load<kDense>(x, kv, ldx, i)));
+#pragma unroll
+  for (int o = 16; o; o >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
+  __shared__ uint32_t s_max[kF8Threads / 32];
+  if ((threadIdx.x & 31) == 0) s_max[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    m = threadIdx.x < kF8Threads / 32 ? s_max[threadIdx.x] : 0u;
+#pragma unroll
+    for (int o = 4; o; o >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (threadIdx.x == 0 && m) atomicMax(amax_bits, m);
+  }
+}
+
+// Four fp32 -> four E4M3 bytes (element 0 in the low byte). The clamp to
+// +-448 of the reference is the conversion's satfinite (finite values above
+// 448 and +-inf give +-448, the same codes the clamp gives); only NaN differs:
+// the reference's encoder gives sign | 0x7f, the conversion a fixed NaN code.
+// Clamped finite values never produce a 0x7f magnitude (448 is 0x7e), so the
+// 0x7f magnitudes are exactly the NaN inputs and are patched from the signs.
+__device__ __forceinline__ uint32_t e4m3x4(const float (&z)[4]) {
+  uint16_t lo, hi;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(lo) : "f"(z[1]), "f"(z[0]));
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(hi) : "f"(z[3]), "f"(z[2]));
+  uint32_t q = (uint32_t)lo | ((uint32_t)hi << 16);
+  if (__vcmpeq4(q & 0x7f7f7f7fu, 0x7f7f7f7fu)) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      if (z[j] != z[j]) {
+        const uint32_t code = 0x7fu | ((__float_as_uint(z[j]) >> 24) & 0x80u);
+        q = (q & ~(0xffu << (8 * j))) | (code << (8 * j));
+      }
+  }
+  return q;
+}
+
+// x / scale for the 8 elements of one vector, IEEE-rounded like torch's
+// division. kRecip (scale finite and normal, every call whose input is
+// finite): with y = RN(1/scale), q = RN(|x| y) and one step of Markstein's
+// correction (P. Markstein, IBM J. Res. Develop. 34(1), 1990: r = |x| - scale
+// q exactly by one fma, q' = RN(q + r y)) give RN(|x| / scale); the sign is
+// put back afterwards so that -0 and negative underflow keep it. An
+// exhaustive CPU replay of this sequence over every bf16 |x| <= amax and
+// every scale a bf16 amax yields (4.7e8 pairs) matches correctly rounded
+// division bit for bit. Otherwise (scale inf or NaN) a full division.
+template <bool kRecip>
+__device__ __forceinline__ uint2 fp8_codes8(uint4 v, float scale, float recip) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+  float z[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const uint32_t h = (j & 1) ? (w[j >> 1] & 0xffff0000u) : (w[j >> 1] << 16);
+    if (kRecip) {
+      const float ax = __uint_as_float(h & 0x7fffffffu);
+      const float q = __fmul_rn(ax, recip);
+      const float r = __fmaf_rn(-q, scale, ax);
+      z[j] = __uint_as_float(__float_as_uint(__fmaf_rn(r, recip, q)) | (h & 0x80000000u));
+    } else {
+      z[j] = __fdiv_rn(__uint_as_float(h), scale);
+    }
+  }
+  const float z0[4] = {z[0], z[1], z[2], z[3]}, z1[4] = {z[4], z[5], z[6], z[7]};
+  return make_uint2(e4m3x4(z0), e4m3x4(z1));
+}
+
+template <bool kDense, bool kRecip>
+__device__ __forceinline__ void fp8_quantize_rows(const __nv_bfloat16* x, long long kv, long long ldx,
+                                                  long long total, float scale, uint2* out) {
+  const float recip = kRecip ? __frcp_rn(scale) : 0.0f;
+  const long long stride = (long long)gridDim.x * kF8Threads;
+  long long i = blockIdx.x * (long long)kF8Threads + threadIdx.x;
+  for (; i + (kF8Unroll - 1) * stride < total; i += kF8Unroll * stride) {
+    uint4 v[kF8Unroll];
+#pragma unroll
+    for (int u = 0; u < kF8Unroll; ++u) v[u] = f8_load<kDense>(x, kv, ldx, i + u * stride);
+#pragma unroll
+    for (int u = 0; u < kF8Unroll; ++u) out[i + u * stride] = fp8_codes8<kRecip>(v[u], scale, recip);
+  }
+  for (; i < total; i += stride) out[i] = fp8_codes8<kRecip>(f8_load<kDense>(x, kv, ldx, i), scale, recip);
+}
+
+template <bool kDense>
+__global__ void __launch_bounds__(kF8Threads) fp8_quantize_kernel(const __nv_bfloat16* x, int M, int K,
+                                                                   long long ldx, const unsigned int* amax_bits,
+                                                                   float* scale_out, uint8_t* q) {
   rc::pdl_trigger();
   rc::pdl_wait();
   float amax = __uint_as_float(rc::ld_in(amax_bits));
   amax = amax < 1e-12f ? 1e-12f : amax;         // clamp_min(1e-12); NaN passes through
   const float scale = __fdiv_rn(amax, 448.0f);
   if (blockIdx.x == 0 && threadIdx.x == 0 && scale_out) *scale_out = scale;
-  const int kv = K >> 3;
-  const long long total = (long long)M * kv;
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
-       i += (long long)gridDim.x * blockDim.x) {
-    const long long row = i / kv, c = i % kv;
-    uint4 v = rc::ld_in(reinterpret_cast<const uint4*>(x + row * ldx) + c);
-    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-    uint32_t out[2] = {0, 0};
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const uint32_t h = (j & 1) ? (w[j >> 1] & 0xffff0000u) : (w[j >> 1] << 16);
-      float z = __fdiv_rn(__uint_as_float(h), scale);
-      z = z > 448.0f ? 448.0f : (z < -448.0f ? -448.0f : z);
-      out[j >> 2] |= (uint32_t)rc::e4m3_from_float(z) << (8 * (j & 3));
-    }
-    *reinterpret_cast<uint2*>(q + row * (long long)K + c * 8) = make_uint2(out[0], out[1]);
-  }
-}
-
-int grid_for(long long work, int threads) {
-  long long b = (work + threads - 1) / threads;
-  int sms = 148;
-  long long cap = (long long)sms * 8;
-  return (int)(b < 1 ? 1 : (b > cap ? cap : b));
+  const long long kv = K >> 3, total = (long long)M * kv;
+  uint2* out = reinterpret_cast<uint2*>(q);     // q is packed M x K: vector i -> bytes 8i..8i+7
+  if (isfinite(scale) && scale >= 0x1p-126f)    // normal and finite; uniform over the grid
+    fp8_quantize_rows<kDense, true>(x, kv, ldx, total, scale, out);
+  else
+    fp8_quantize_rows<kDense, false>(x, kv, ldx, total, scale, out);
 }
 
 }  // namespace
@@ -170,14 +250,24 @@ int rc_fp8_quantize(const void* x, int M, int K, long long ldx, unsigned int* am
   if (cudaMemsetAsync(amax_scratch, 0, sizeof(unsigned int), stream) != cudaSuccess)
     return rc::set_error(RC_ERR_CUDA, "rc_fp8_quantize: memset failed");
   if (M == 0) return RC_OK;
+  // kF8Unroll vectors per thread per pass, at most 4 CTAs per SM (one wave).
   const long long work = (long long)M * (K / 8);
-  int rc_ = rc::check_launch(rc::launch_pdl(absmax_bf16_kernel, dim3(grid_for(work, 256)), dim3(256), 0, stream,
-                                            reinterpret_cast<const __nv_bfloat16*>(x), M, K, ldx, amax_scratch),
+  long long blocks = (work + kF8Threads * kF8Unroll - 1) / (kF8Threads * kF8Unroll);
+  const long long cap = 4LL * rc::sm_count();
+  const dim3 grid((unsigned)(blocks > cap ? cap : blocks));
+  const bool dense = ldx == K;
+  const auto* xb = reinterpret_cast<const __nv_bfloat16*>(x);
+  int rc_ = rc::check_launch(dense ? rc::launch_pdl(absmax_bf16_kernel<true>, grid, dim3(kF8Threads), 0, stream,
+                                                    xb, M, K, ldx, amax_scratch)
+                                   : rc::launch_pdl(absmax_bf16_kernel<false>, grid, dim3(kF8Threads), 0, stream,
+                                                    xb, M, K, ldx, amax_scratch),
                              "rc_fp8_quantize(amax)");
   if (rc_) return rc_;
-  return rc::check_launch(rc::launch_pdl(fp8_quantize_kernel, dim3(grid_for(work, 256)), dim3(256), 0, stream,
-                                         reinterpret_cast<const __nv_bfloat16*>(x), M, K, ldx,
-                                         static_cast<const unsigned int*>(amax_scratch), scale_out, q),
+  const auto* amax = static_cast<const unsigned int*>(amax_scratch);
+  return rc::check_launch(dense ? rc::launch_pdl(fp8_quantize_kernel<true>, grid, dim3(kF8Threads), 0, stream,
+                                                 xb, M, K, ldx, amax, scale_out, q)
+                                : rc::launch_pdl(fp8_quantize_kernel<false>, grid, dim3(kF8Threads), 0, stream,
+                                                 xb, M, K, ldx, amax, scale_out, q),
                           "rc_fp8_quantize");
 }
 

@@ -89,6 +89,21 @@ def _quant():
     return run, M * DIM * 2.5625, "GB/s"
 
 
+def _quant_fp8(m=M, k=DIM):
+    """Per-tensor FP8 quantizer (amax pass + quantize pass); GB/s of
+    algorithmic bytes (bf16 in once, e4m3 out)."""
+    x = torch.randn(m, k, device="cuda").bfloat16()
+    q = torch.empty(m, k, dtype=torch.uint8, device="cuda")
+    scratch = torch.empty(2, dtype=torch.int32, device="cuda")
+    scale = torch.empty((), dtype=torch.float32, device="cuda")
+    lib = _lib.library()
+
+    def run():
+        _lib.check(lib.rc_fp8_quantize(x.data_ptr(), m, k, k, scratch.data_ptr(), scale.data_ptr(),
+                                       q.data_ptr(), _lib.stream()), "quant_fp8")
+    return run, m * k * 3.0, "GB/s"
+
+
 def _ln():
     x = torch.randn(M, DIM, device="cuda").bfloat16()
     sh, sc = torch.randn(DIM, device="cuda"), torch.randn(DIM, device="cuda")
@@ -152,6 +167,8 @@ CASES = {
     "attention_local_1080p": lambda: _attention(planes=4, h=34, w=60, window=(22, 40)),
     "cross_attention": _cross_attention,
     "quant": _quant,
+    "quant_fp8": _quant_fp8,
+    "quant_fp8_large": lambda: _quant_fp8(7040, 14336),
     "ln": _ln,
     "rms": _rms,
 }

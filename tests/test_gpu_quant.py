@@ -85,6 +85,74 @@ def test_fp8_quantize_back_to_back():
         np.testing.assert_array_equal(q.cpu().numpy(), rq)
 
 
+def test_fp8_quantize_strided_rows():
+    """Rows with a pitch larger than K take the indexed (non-packed) path."""
+    from recavsr_b200.runtime import fp8
+    x = recipes.cfg3_activation(300, 1024, seed=6)
+    big = torch.zeros(300, 1280, dtype=torch.bfloat16, device="cuda")
+    big[:, 256:1280] = dev_bf16(x)
+    q, scale = fp8.quantize(big[:, 256:1280])
+    rq, rscale = ofp8.quantize(x)
+    assert np.float32(scale.item()) == rscale
+    np.testing.assert_array_equal(q.cpu().numpy(), rq)
+    assert_no_device_error()
+
+
+@pytest.mark.parametrize("amax", [448.0, 1.0, 3.0e-3, 6.0e4, 2.0 ** -100, 3.0e38])
+def test_fp8_quantize_every_bf16_value(amax):
+    """Every finite bf16 x with |x| <= amax, quantized with scale amax/448:
+    covers each E4M3 rounding boundary, the subnormal codes and the zeros."""
+    from recavsr_b200.runtime import fp8
+    from oracle.numerics import bf16_from_bits
+    amax = bf16_round(np.array([amax], np.float32))[0]
+    allx = bf16_from_bits(np.arange(65536, dtype=np.uint32).astype(np.uint16)).astype(np.float32)
+    xs = allx[np.abs(allx) <= amax]
+    xs = np.concatenate([[amax], xs])
+    xs = np.concatenate([xs, np.zeros((-len(xs)) % 1024, np.float32)]).reshape(-1, 1024)
+    q, scale = fp8.quantize(dev_bf16(xs))
+    rq, rscale = ofp8.quantize(xs)
+    assert np.float32(scale.item()) == rscale
+    np.testing.assert_array_equal(q.cpu().numpy(), rq)
+
+
+def test_fp8_quantize_many_scales():
+    """64 amax values spread over the bf16 range (each a separate call, so
+    each its own per-tensor scale), every bf16 |x| <= amax of both signs."""
+    from recavsr_b200.runtime import fp8
+    from oracle.numerics import bf16_from_bits
+    allx = bf16_from_bits(np.arange(65536, dtype=np.uint32).astype(np.uint16)).astype(np.float32)
+    allx = allx[np.isfinite(allx)]
+    pos = np.sort(allx[allx > 0])
+    rng = np.random.default_rng(11)
+    for amax in pos[np.sort(rng.choice(len(pos), 64, replace=False))]:
+        xs = np.concatenate([[amax], allx[np.abs(allx) <= amax]])
+        xs = np.concatenate([xs, np.zeros((-len(xs)) % 512, np.float32)]).reshape(-1, 512)
+        q, scale = fp8.quantize(dev_bf16(xs))
+        rq, rscale = ofp8.quantize(xs)
+        assert np.float32(scale.item()) == rscale, amax
+        np.testing.assert_array_equal(q.cpu().numpy(), rq, err_msg=f"amax={amax}")
+
+
+@pytest.mark.parametrize("special", [np.inf, -np.inf, np.nan])
+def test_fp8_quantize_non_finite(special):
+    """An inf makes the scale inf (finite values -> signed zeros, inf/inf ->
+    NaN code); a NaN makes the scale NaN and every code the NaN code. The
+    sign of a NaN that a division creates is the platform's default NaN
+    (negative on x86, positive on the GPU), so NaN codes compare by
+    magnitude; every other code is bit-exact."""
+    from recavsr_b200.runtime import fp8
+    x = recipes.cfg3_activation(64, 256, seed=7)
+    x[5, 17] = special
+    q, scale = fp8.quantize(dev_bf16(x))
+    rq, rscale = ofp8.quantize(x)
+    got = np.float32(scale.item())
+    assert got == rscale or (np.isnan(got) and np.isnan(rscale))
+    q = q.cpu().numpy()
+    nan_code = (rq & 0x7F) == 0x7F
+    np.testing.assert_array_equal(q[~nan_code], rq[~nan_code])
+    np.testing.assert_array_equal(q[nan_code] & 0x7F, rq[nan_code] & 0x7F)
+
+
 def test_nvfp4_quantize_every_bf16_value_every_scale():
     """Blocks [6s, x, ...] pin the block scale to each E4M3 value s in turn and
     run every bf16 x with |x| <= 6s through the device quantizer."""
