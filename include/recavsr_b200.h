@@ -117,10 +117,13 @@ int rc_kv_commit(const void* src_k, const void* src_v, long long src_ld_bytes, v
 
 /* Same copies with the plan in device memory: plan = [n, (src plane, dst slot) x n],
  * n <= max_planes <= 8, slots < capacity. Lets a captured CUDA graph of the
- * layer loop follow the router without re-capture. */
-int rc_kv_commit_planned(const void* src_k, const void* src_v, long long src_ld_bytes, void* dst_k,
-                         void* dst_v, long long dst_ld_bytes, int row_bytes, int span,
-                         int max_planes, int capacity, const int* plan, rc_stream_t stream);
+ * layer loop follow the router without re-capture. K and V have their own
+ * source row strides (the block's V is a column range of the fused QKV output,
+ * cache.py:85-133 takes key and value as separate tensors). */
+int rc_kv_commit_planned(const void* src_k, const void* src_v, long long src_ld_k_bytes,
+                         long long src_ld_v_bytes, void* dst_k, void* dst_v, long long dst_ld_bytes,
+                         int row_bytes, int span, int max_planes, int capacity, const int* plan,
+                         rc_stream_t stream);
 
 /* ---- routed attention (tcgen05) ------------------------------------------ */
 /* Replaces recavsr_infer/kernels/local_attention.py:172-260 `paired_attention`

@@ -40,7 +40,7 @@ _SIGNATURES = {
     "rc_cross_attention_workspace": [],
     "rc_cross_attention_ws": [_P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _LL, _P, _P, _P, _LL, _P],
     "rc_paired_attention_static_scratch": [_P] * 11 + [_I] * 10 + [_P, _LL, _P, _P, _P],
-    "rc_kv_commit_planned": [_P, _P, _LL, _P, _P, _LL, _I, _I, _I, _I, _P, _P],
+    "rc_kv_commit_planned": [_P, _P, _LL, _LL, _P, _P, _LL, _I, _I, _I, _I, _P, _P],
 }
 _RESTYPES = {"rc_paired_attention_workspace": C.c_longlong, "rc_gemm_split_workspace": C.c_longlong,
              "rc_cross_attention_workspace": C.c_longlong}

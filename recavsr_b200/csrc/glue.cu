@@ -573,21 +573,25 @@ int rc_kv_commit(const void* src_k, const void* src_v, long long src_ld_bytes, v
 
 // Device-planned variant: plan = [n, (src plane, dst slot) x n] in device
 // memory, at most max_planes copies, slots < capacity.
-int rc_kv_commit_planned(const void* src_k, const void* src_v, long long src_ld_bytes, void* dst_k,
-                         void* dst_v, long long dst_ld_bytes, int row_bytes, int span,
-                         int max_planes, int capacity, const int* plan, cudaStream_t stream) {
+int rc_kv_commit_planned(const void* src_k, const void* src_v, long long src_ld_k_bytes,
+                         long long src_ld_v_bytes, void* dst_k, void* dst_v, long long dst_ld_bytes,
+                         int row_bytes, int span, int max_planes, int capacity, const int* plan,
+                         cudaStream_t stream) {
   if (max_planes < 0 || max_planes > 8 || span <= 0 || row_bytes <= 0 || row_bytes % 16 || capacity < 0)
     return rc::set_error(RC_ERR_ARG, "rc_kv_commit_planned: bad shape");
   if (max_planes == 0 || capacity == 0) return RC_OK;
   if (!plan || !aligned16(src_k) || !aligned16(src_v) || !aligned16(dst_k) || !aligned16(dst_v) ||
-      src_ld_bytes % 16 || dst_ld_bytes % 16)
+      src_ld_k_bytes % 16 || src_ld_v_bytes % 16 || dst_ld_bytes % 16)
     return rc::set_error(RC_ERR_ARG, "rc_kv_commit_planned: rows must be 16-byte aligned");
+  if (src_ld_k_bytes < row_bytes || src_ld_v_bytes < row_bytes || dst_ld_bytes < row_bytes)
+    return rc::set_error(RC_ERR_ARG, "rc_kv_commit_planned: row stride below row_bytes");
   CommitArgs a{};
   a.src[0] = reinterpret_cast<const uint8_t*>(src_k);
   a.src[1] = reinterpret_cast<const uint8_t*>(src_v);
   a.dst[0] = reinterpret_cast<uint8_t*>(dst_k);
   a.dst[1] = reinterpret_cast<uint8_t*>(dst_v);
-  a.src_ld[0] = a.src_ld[1] = src_ld_bytes;
+  a.src_ld[0] = src_ld_k_bytes;
+  a.src_ld[1] = src_ld_v_bytes;
   a.dst_ld[0] = a.dst_ld[1] = dst_ld_bytes;
   a.dst_plane[0] = capacity;
   a.n = max_planes;

@@ -149,13 +149,26 @@ class FusedBlock(torch.nn.Module):
         """In-place layer on h [N, dim]; leaves k (ws.k_rot) and v (ws.qkv) for the commit."""
         lib = _lib.library()
         st = _lib.stream(h.device)
+        self.pre_attention(lib, h, ws, st)
+        # 4. routed attention, output NVFP4-quantized in its epilogue
+        self._attention(lib, ws, past_key, past_value, slots, past_positions, query_positions,
+                        h.shape[0], st, quantized=True)
+        self.post_attention(lib, h, ws, st)
+
+    def pre_attention(self, lib, h, ws, st, spatial=None):
+        """Steps 1-3 of the layer on h [N, dim]: LN1 + AdaLN -> NVFP4, the fused
+        QKV GEMM (ws.qkv), RMSNorm + spatial RoPE of q and k (ws.q_rot, ws.k_rot).
+        spatial = (cos, sin, span) replaces the block's own spatial tables (a
+        token shard passes the rows of its own tokens with span = N)."""
         n, dim = h.shape
         mod = self.modulation
-        shift, scale, gate, cshift, cscale, cgate = (mod[i] for i in range(6))
         chk = _lib.check
+        if spatial is None:
+            spatial = (self.tables["spatial_cos"], self.tables["spatial_sin"], self.height * self.width)
+        scos, ssin, span = spatial
         # 1. LN1 + AdaLN -> NVFP4
-        chk(lib.rc_ln_modulate_quant(h.data_ptr(), dim, n, dim, None, None, shift.data_ptr(),
-                                     scale.data_ptr(), _EPS, None, 0, ws.a_codes.data_ptr(),
+        chk(lib.rc_ln_modulate_quant(h.data_ptr(), dim, n, dim, None, None, mod[0].data_ptr(),
+                                     mod[1].data_ptr(), _EPS, None, 0, ws.a_codes.data_ptr(),
                                      ws.a_scales.data_ptr(), 1.0, st), "ln1")
         # 2. fused QKV
         self._gemm(lib, ws, ws.a_codes, ws.a_scales, self.qkv, n, _lib.EPI_BIAS, ws.qkv, st)
@@ -166,11 +179,16 @@ class FusedBlock(torch.nn.Module):
                                 (C.c_void_p * 2)(self.norm_q.data_ptr(), self.norm_k.data_ptr()),
                                 (C.c_void_p * 2)(ws.q_rot.data_ptr(), ws.k_rot.data_ptr()),
                                 (C.c_longlong * 2)(dim, dim), n, dim, self.head_dim,
-                                self.height * self.width, self.tables["spatial_cos"].data_ptr(),
-                                self.tables["spatial_sin"].data_ptr(), _EPS, st), "rmsnorm_rope")
-        # 4. routed attention, output NVFP4-quantized in its epilogue
-        self._attention(lib, ws, past_key, past_value, slots, past_positions, query_positions, n, st,
-                        quantized=True)
+                                span, scos.data_ptr(), ssin.data_ptr(), _EPS, st), "rmsnorm_rope")
+
+    def post_attention(self, lib, h, ws, st):
+        """Steps 5-7 of the layer on h [N, dim], with the attention output's NVFP4
+        operand in ws.a_codes / ws.a_scales: o-proj with gated residual, cross
+        attention block, FFN block."""
+        n, dim = h.shape
+        mod = self.modulation
+        gate, cshift, cscale, cgate = mod[2], mod[3], mod[4], mod[5]
+        chk = _lib.check
         # 5. o-proj with gated residual
         self._gemm(lib, ws, ws.a_codes, ws.a_scales, self.o, n, _lib.EPI_GATED_RESIDUAL, h, st, gate)
         # 6. cross attention
@@ -239,7 +257,7 @@ class FusedBlock(torch.nn.Module):
 class Workspace:
     """Per-token-count scratch shared by all layers of a stack."""
 
-    def __init__(self, block: FusedBlock, n: int, max_cap: int = 8):
+    def __init__(self, block: FusedBlock, n: int, max_cap: int = 8, attention: bool = True):
         dev, dim = block.device, block.dim
         span = block.height * block.width
         frames = n // span
@@ -253,9 +271,10 @@ class Workspace:
         self.cq = torch.empty((n, dim), dtype=torch.bfloat16, device=dev)
         self.f_codes = torch.empty((n, block.ffn // 2), dtype=torch.uint8, device=dev)
         self.f_scales = torch.empty((scale_numel(n, block.ffn),), dtype=torch.uint8, device=dev)
-        ws = _lib.library().rc_paired_attention_workspace(1, frames, max_cap, block.height,
-                                                          block.width, block.heads, block.head_dim)
-        self.attn_ws = torch.empty((ws,), dtype=torch.uint8, device=dev)
+        if attention:       # a token shard of a head-sharded stack attends elsewhere
+            ws = _lib.library().rc_paired_attention_workspace(1, frames, max_cap, block.height,
+                                                              block.width, block.heads, block.head_dim)
+            self.attn_ws = torch.empty((ws,), dtype=torch.uint8, device=dev)
         # Split-K partials and arrival counters of the NVFP4 GEMMs (zero-filled;
         # the GEMMs leave it zero-filled).
         self.gemm_ws = torch.zeros((_lib.library().rc_gemm_split_workspace(),), dtype=torch.uint8,
@@ -295,6 +314,8 @@ class LayerStack:
         self.router = (initial, stride, anchors)
         b0 = blocks[0]
         self.device, self.dim, self.heads, self.head_dim = b0.device, b0.dim, b0.heads, b0.head_dim
+        if not hasattr(self, "cache_heads"):
+            self.cache_heads = self.heads        # a head-sharded stack caches its own heads only
         self.span = b0.height * b0.width
         self.rope = b0.tables["rope"]
         self._ws: dict[int, Workspace] = {}
@@ -319,7 +340,7 @@ class LayerStack:
         self._route_i = 0
         self.route_host = self._route_ring[0]
         self.route_dev = torch.zeros_like(self.route_host, device=self.device)
-        shape = lambda c: (1, max(c.capacity, 1) * self.span, self.heads, self.head_dim)
+        shape = lambda c: (1, max(c.capacity, 1) * self.span, self.cache_heads, self.head_dim)
         self.cache_k = [torch.zeros(shape(c), dtype=torch.bfloat16, device=self.device) for c in self.caches]
         self.cache_v = [torch.zeros(shape(c), dtype=torch.bfloat16, device=self.device) for c in self.caches]
         self.latent_offset = 0
@@ -372,8 +393,9 @@ class LayerStack:
             if cap:
                 _lib.check(lib.rc_kv_commit_planned(
                     ws.k_rot.data_ptr(), ws.qkv[:, 2 * self.dim:].data_ptr(), ws.k_rot.stride(0) * 2,
-                    self.cache_k[i].data_ptr(), self.cache_v[i].data_ptr(), row_bytes, row_bytes,
-                    self.span, frames, cap, rd[o + 16:].data_ptr(), st), "kv_commit")
+                    ws.qkv.stride(0) * 2, self.cache_k[i].data_ptr(), self.cache_v[i].data_ptr(),
+                    row_bytes, row_bytes, self.span, frames, cap, rd[o + 16:].data_ptr(), st),
+                    "kv_commit")
 
     def step(self, hidden: torch.Tensor, frames: int, *, graphs: bool = False) -> torch.Tensor:
         """hidden [N, dim] bf16 on the device, updated in place through all layers."""

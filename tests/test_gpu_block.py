@@ -237,7 +237,10 @@ def test_layer_stack_streaming_and_graph_replay():
     compound across blocks); routing tables must equal the oracle router's
     exactly, graph replay must be bit-identical to eager launches, and so must
     the host-to-host streaming path (step_host, copies overlapping the
-    neighbouring blocks, no host sync until the end)."""
+    neighbouring blocks, no host sync until the end). The K / V planes each
+    block commits to the cache must match the oracle's k / v of that layer
+    (K is a column range of its own buffer, V of the fused QKV output, so the
+    two source row strides differ)."""
     from recavsr_b200.runtime.block import FusedBlock, LayerStack, rope_tables
     dim, heads, ffn, H, W = 256, 2, 512, 4, 6
     span = H * W
@@ -282,6 +285,11 @@ def test_layer_stack_streaming_and_graph_replay():
             streamed.step_host(hin, hout, frames)
         ref, routes = _oracle_stack_step(params, routers, caches, x, start, frames, H, W, heads)
         start += frames
+        for i in range(3):
+            if eager.caches[i].capacity:
+                for t, dev_cache in enumerate((eager.cache_k, eager.cache_v)):
+                    _close(host(dev_cache[i])[0].reshape(-1), caches[i][t].reshape(-1),
+                           BLOCK_REL_L2, BLOCK_MAX_FRAC)
         for i, (slots, ppos) in enumerate(routes):
             o = i * eager._row
             cap = eager.caches[i].capacity
