@@ -11,10 +11,12 @@ projection. One step = one body block through all 30 layers; the 6-frame
 prefix block and enough body blocks to fill every layer's cache run as
 warm-up. Inputs/weights/caches (~4 GB) exceed L2 (126 MB), so no flush.
 
-  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference] [--head-shard]
 
 Under torchrun each rank runs an independent stream (weak scaling, no
 collective); rank 0 prints one JSON line with the max-over-ranks time.
+--head-shard instead runs one 3840x2176 stream split by heads over the ranks
+(NCCL all-to-all at the attention boundary; strong scaling).
 """
 from __future__ import annotations
 
@@ -155,11 +157,16 @@ class ClockSampler:
 
 # -------------------------------------------------------------- model setup
 def build_stack(device, seed):
+    from recavsr_b200.runtime.block import LayerStack
+    return LayerStack(build_blocks(device, seed, H_TOK, W_TOK), ACTIONS)
+
+
+def build_blocks(device, seed, h_tok, w_tok):
     import torch
-    from recavsr_b200.runtime.block import FusedBlock, LayerStack, rope_tables
+    from recavsr_b200.runtime.block import FusedBlock, rope_tables
     g = torch.Generator(device=device)
     g.manual_seed(seed)
-    tables = rope_tables(HEAD_DIM, H_TOK, W_TOK, device)
+    tables = rope_tables(HEAD_DIM, h_tok, w_tok, device)
     rnd = lambda *s, std=1.0: (torch.randn(*s, generator=g, device=device) * std).bfloat16()
     encoder = rnd(1, ENC_LEN, DIM)
     blocks = []
@@ -177,10 +184,10 @@ def build_stack(device, seed):
         w["timestep_proj"] = rnd(1, 1, 6, DIM)
         w["encoder"] = encoder
         w["heads"] = HEADS
-        blocks.append(FusedBlock(w, H_TOK, W_TOK, tables))
+        blocks.append(FusedBlock(w, h_tok, w_tok, tables))
         del w
     torch.cuda.synchronize(device)
-    return LayerStack(blocks, ACTIONS)
+    return blocks
 
 
 def algorithmic_flops_per_token():
@@ -310,6 +317,102 @@ def run_reference(args, rank, world):
     }), flush=True)
 
 
+# ------------------------------------------------- single stream, head-sharded
+H_4K, W_4K = 68, 120                   # 3840x2176 model raster / 32
+T_4K = H_4K * W_4K
+
+
+def run_head_shard(args, rank, world, local):
+    """--head-shard: one 3840x2176 stream (T = 8160 tokens per latent frame,
+    2-frame body blocks of 16320 tokens, 22x40 local windows) split over the
+    torchrun ranks by heads (24 / N per rank) with two NCCL all-to-alls per
+    layer; tokens/s of the one stream (strong scaling). Every rank builds the
+    same weights and the same block inputs and works on its own shard."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+    from recavsr_b200 import _lib
+    from recavsr_b200.runtime.head_shard import HeadShardedStack
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+    stack = HeadShardedStack(build_blocks(device, 1234, H_4K, W_4K), ACTIONS, rank=rank, world=world)
+    g = torch.Generator(device=device)
+    g.manual_seed(99)
+    shard = lambda x: x[rank * (x.shape[0] // world):(rank + 1) * (x.shape[0] // world)].contiguous()
+    prefix = shard(torch.randn(PREFIX * T_4K, DIM, generator=g, device=device).bfloat16())
+    stack.step(prefix, PREFIX)
+    body = shard(torch.randn(BODY * T_4K, DIM, generator=g, device=device).bfloat16())
+    h = body.clone()
+    warm = max(args.warmup, 3)
+    for _ in range(warm):
+        h.copy_(body)
+        stack.step(h, BODY)
+    torch.cuda.synchronize(device)
+    if not torch.isfinite(h.float()).all():
+        raise RuntimeError("non-finite hidden state after warm-up")
+    dev_err = _lib.read_device_error()
+    if dev_err:
+        raise RuntimeError(f"device error word 0x{dev_err:08x}")
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(device)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        start.record()
+        for _ in range(args.steps):
+            stack.step(h, BODY)
+        end.record()
+        end.synchronize()
+    t = start.elapsed_time(end) * 1e-3
+    host_in = torch.empty(body.shape, dtype=torch.bfloat16, pin_memory=True)
+    host_in.copy_(body.cpu())
+    host_out = torch.empty_like(host_in, pin_memory=True)
+    torch.cuda.synchronize(device)
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        h.copy_(host_in, non_blocking=True)
+        stack.step(h, BODY)
+        host_out.copy_(h, non_blocking=True)
+    e1.record()
+    e1.synchronize()
+    te = e0.elapsed_time(e1) * 1e-3
+    if world > 1:
+        tt = torch.tensor([t, te], device=device)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        t, te = float(tt[0]), float(tt[1])
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    tokens = BODY * T_4K * args.steps
+    value = tokens / t
+    launches_per_layer = 15   # LN x3, GEMM x6, RMSNorm x2, gather + attention, NVFP4 quantize, cross attention
+    print(json.dumps({
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": warm, "ms_per_step": t / args.steps * 1e3, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "nvfp4 linears / bf16 attention",
+        "data": "synthetic (random-init weights, N(0,1) hidden/prompt states)",
+        "config": {"workload": "cfg5 single stream 3840x2176 -> 68x120 tokens (T=8160), 2-frame body "
+                               "block (16320 tokens), 30 layers, released router, 22x40 local windows",
+                   "global_batch": 1, "seq_len": BODY * T_4K,
+                   "parallelism": f"heads x{world} (token-sharded linears, all-to-all at attention)",
+                   "l2": "working set > 126 MB L2 (no flush)", "cuda_graph": False},
+        "out_fps": value * 4 / T_4K,
+        "e2e": {"value": tokens / te, "unit": "tokens/s",
+                "h2d_bytes_per_step": body.numel() * 2 * world, "d2h_bytes_per_step": body.numel() * 2 * world,
+                "path": "per rank: copy shard in, HeadShardedStack.step, copy shard out (one stream)"},
+        "gpu_launches": args.steps * (LAYERS * launches_per_layer + sum(
+            1 for c in stack.caches if c.capacity)),
+        "clocks": clk.summary(),
+    }), flush=True)
+
+
 # ------------------------------------------------------------------- main
 def main():
     ap = argparse.ArgumentParser()
@@ -321,12 +424,16 @@ def main():
     ap.add_argument("--eager", action="store_true", help="no CUDA graph (launch from Python)")
     ap.add_argument("--no-kernel-timing", action="store_true",
                     help="skip the per-kernel roofline timing (e.g. for an ncu launch list)")
+    ap.add_argument("--head-shard", action="store_true",
+                    help="one 3840x2176 stream split by heads over the ranks (strong scaling)")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
     local = int(os.environ.get("LOCAL_RANK", 0))
     if args.impl == "reference":
         return run_reference(args, rank, world)
+    if args.head_shard:
+        return run_head_shard(args, rank, world, local)
 
     import torch
     import torch.distributed as dist
