@@ -190,6 +190,44 @@ int rc_cross_attention_ws(const void* q, const void* k, const void* v, const lon
                           uint8_t* out_codes, uint8_t* out_scales, void* workspace,
                           long long workspace_bytes, rc_stream_t stream);
 
+/* ---- session glue around the layer loop ---------------------------------- */
+/* im2col of the LQ projector's CausalConv3d (recavsr_infer/models/lq_proj.py:44-139:
+ * kernel (4, 3, 3), padding (0, 1, 1), stride (stride_t, stride_s, stride_s)) over
+ * frames_in source frames the caller has already laid out (history, replicated
+ * first frame), for the tcgen05 bf16 GEMM against the weight permuted to
+ * [cout, kt, kh, kw, cin]. out: [frames_out * Ho * Wo, 36 * cin] bf16 (row stride
+ * ldo), Ho = (h_in - 1) / stride_s + 1. Source element (frame t, row y, column x,
+ * channel c), bf16, 16-byte aligned strides:
+ *   unshuffle == 0: channels-last, src + t*frame_stride + y*row_stride + x*col_stride + c;
+ *   unshuffle == r: planar RGB pixel-unshuffled by r (lq_proj.py:279-285, c = (rgb*r + i)*r + j),
+ *                   src + t*frame_stride + rgb*chan_stride + (y*r + i)*row_stride + x*r + j. */
+int rc_conv3d_im2col(const void* src, long long frame_stride, long long chan_stride,
+                     long long row_stride, long long col_stride, int unshuffle, int cin,
+                     int frames_in, int h_in, int w_in, int stride_t, int stride_s, int frames_out,
+                     void* out, long long ldo, rc_stream_t stream);
+
+/* ChannelRMSNorm3d + SiLU of lq_proj.py:26-40,196-204 on channels-last rows:
+ * out = bf16(silu(bf16(x * rsqrt(mean(x^2) + eps) * weight))), C <= 8192,
+ * C % 8 == 0, in place allowed. */
+int rc_channel_rmsnorm_silu(const void* x, long long ldx, int M, int C, const void* weight, float eps,
+                            void* out, long long ldo, rc_stream_t stream);
+
+/* Patch gather of the patch embedding Conv3d (kernel = stride = (1, ph, pw);
+ * recavsr_infer/models/transformer_wan.py:1020-1022, used at runtime/transformer.py:321-328):
+ * src [C, F, H, W] (fp32 or bf16, element strides chan / frame / row, unit column
+ * stride) -> out [F*(H/ph)*(W/pw), C*ph*pw] bf16, column (c*ph + i)*pw + j. */
+int rc_patchify(const void* src, int src_is_bf16, long long chan_stride, long long frame_stride,
+                long long row_stride, int C, int F, int H, int W, int ph, int pw, void* out,
+                long long ldo, rc_stream_t stream);
+
+/* Output head tail of recavsr_infer/runtime/transformer.py:333-348: unpatchify the
+ * proj_out rows pred [F*(H/ph)*(W/pw), ph*pw*C] bf16 and return
+ * out = noise - float(prediction) (fp32 [C, F, H, W]); the last recycle_frames
+ * frames of out also as bf16 into recycle [C, recycle_frames, H, W]. */
+int rc_unpatchify_residual(const void* pred, long long ldp, const float* noise, float* out,
+                           void* recycle, int C, int F, int H, int W, int ph, int pw,
+                           int recycle_frames, rc_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

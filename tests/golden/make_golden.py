@@ -342,11 +342,131 @@ def gen_block(out, tag="block", dim=256, heads=2, ffn=512, H=4, W=6, enc_len=16,
                                   + list(ppos), np.int64)
 
 
+class _SessionModel(nn.Module):
+    """The attributes TransformerSession (runtime/transformer.py:148-349) reads
+    from the Wan model: patch_embedding, lq_proj (the reference's own LQ4xProj),
+    sr_proj, blocks, norm_out (FP32LayerNorm without affine), proj_out,
+    scale_shift_table, config, the static KV router and the streaming
+    conditioning cache (here given directly: temb, timestep projection and the
+    already projected prompt states)."""
+
+    def __init__(self, blocks, actions, channels, dim, heads, h1, h2, temb, timestep_proj):
+        super().__init__()
+        from recavsr_infer.models.lq_proj import LQ4xProj
+        self.patch_embedding = nn.Conv3d(channels, dim, kernel_size=(1, 2, 2), stride=(1, 2, 2))
+        self.lq_proj = LQ4xProj(3, dim, h1, h2)
+        self.sr_proj = nn.Linear(dim, dim)
+        self.blocks = nn.ModuleList(blocks)
+        self.norm_out = _FP32LayerNorm(dim, 1e-6, elementwise_affine=False)
+        self.proj_out = nn.Linear(dim, channels * 4)
+        self.scale_shift_table = nn.Parameter(torch.zeros(1, 2, dim))
+        self.config = types.SimpleNamespace(in_channels=channels, patch_size=(1, 2, 2),
+                                            num_attention_heads=heads, attention_head_dim=dim // heads)
+        self._static_kv_router = types.SimpleNamespace(layer_actions=list(actions), anchor_initial_index=5,
+                                                       anchor_stride_latents=6, anchor_capacity_latents=2)
+        self._temb, self._tproj = temb, timestep_proj
+
+    def _cache_streaming_conditioning(self, timestep, prompt):
+        return types.SimpleNamespace(temb=self._temb, timestep_proj=self._tproj, encoder_hidden_states=prompt)
+
+
+def gen_session(out, dim=256, heads=2, ffn=512, channels=8, height=128, width=192, h1=64, h2=96,
+                enc_len=16, actions=("recent_2", "none")):
+    """Three TransformerSession.step calls (prefix 21 RGB frames, then two
+    8-frame body blocks) of a 2-layer stand-in model, NVFP4 block linears
+    emulated as in gen_block; weights and inputs from tests/golden/recipes.py
+    (session_params, block_params, session_inputs). Records the LQ projector's
+    outputs, the hidden state entering the first block, the hidden state
+    leaving the last block and the step results."""
+    from recavsr_infer.runtime.transformer import TransformerSession
+    bp = [recipes.block_params(dim, heads, ffn, enc_len=enc_len, seed=70 + i) for i in range(len(actions))]
+    blocks = []
+    for p in bp:
+        b = _Block(dim, heads, ffn)
+        with torch.no_grad():
+            names = {"q": b.attn1.to_q, "k": b.attn1.to_k, "v": b.attn1.to_v, "o": b.attn1.to_out[0],
+                     "cq": b.attn2.to_q, "ck": b.attn2.to_k, "cv": b.attn2.to_v, "co": b.attn2.to_out[0],
+                     "up": b.ffn.net[0].proj, "down": b.ffn.net[2]}
+            for n, lin in names.items():
+                lin.weight.copy_(torch.from_numpy(p[n + "_w"]))
+                lin.bias.copy_(torch.from_numpy(p[n + "_b"]))
+            b.attn1.norm_q.weight.copy_(torch.from_numpy(p["norm_q"]))
+            b.attn1.norm_k.weight.copy_(torch.from_numpy(p["norm_k"]))
+            b.attn2.norm_q.weight.copy_(torch.from_numpy(p["cnorm_q"]))
+            b.attn2.norm_k.weight.copy_(torch.from_numpy(p["cnorm_k"]))
+            b.norm2.weight.copy_(torch.from_numpy(p["norm2_w"]))
+            b.norm2.bias.copy_(torch.from_numpy(p["norm2_b"]))
+            b.scale_shift_table.copy_(torch.from_numpy(p["scale_shift_table"]))
+        blocks.append(b)
+    g = recipes.session_params(dim, channels, h1, h2)
+    temb = g["temb"]
+    model = _SessionModel(blocks, actions, channels, dim, heads, h1, h2, t16(temb),
+                          t16(bp[0]["timestep_proj"]))
+    with torch.no_grad():
+        model.patch_embedding.weight.copy_(torch.from_numpy(g["patch_w"]))
+        model.patch_embedding.bias.copy_(torch.from_numpy(g["patch_b"]))
+        model.sr_proj.weight.copy_(torch.from_numpy(g["sr_w"]))
+        model.sr_proj.bias.copy_(torch.from_numpy(g["sr_b"]))
+        model.proj_out.weight.copy_(torch.from_numpy(g["proj_out_w"]))
+        model.proj_out.bias.copy_(torch.from_numpy(g["proj_out_b"]))
+        lq = model.lq_proj
+        lq.conv1.weight.copy_(torch.from_numpy(g["conv1_w"]))
+        lq.conv1.bias.copy_(torch.from_numpy(g["conv1_b"]))
+        lq.norm1.weight.copy_(torch.from_numpy(g["norm1_w"]).reshape(-1, 1, 1, 1))
+        lq.conv2.weight.copy_(torch.from_numpy(g["conv2_w"]))
+        lq.conv2.bias.copy_(torch.from_numpy(g["conv2_b"]))
+        lq.norm2.weight.copy_(torch.from_numpy(g["norm2_w"]).reshape(-1, 1, 1, 1))
+        lq.out_proj.weight.copy_(torch.from_numpy(g["out_w"]))
+        lq.out_proj.bias.copy_(torch.from_numpy(g["out_b"]))
+    model = model.to(torch.bfloat16)
+    model.scale_shift_table = nn.Parameter(torch.from_numpy(g["scale_shift_table"]))   # fp32, as the
+    # reference keeps scale_shift_table in fp32 (models/transformer_wan.py:945)
+    session = TransformerSession(model, t16(bp[0]["encoder"]), height, width, seed=0)
+    for b in model.blocks:                 # quantize_block_linears (transformer.py:217-224), emulated
+        for mod in list(b.modules()):
+            for name, child in list(mod.named_children()):
+                if isinstance(child, nn.Linear):
+                    setattr(mod, name, _QuantLinear(child))
+    seen = {"lq": [], "first_in": [], "last_out": []}
+    lq_fwd = model.lq_proj.forward_streaming
+    model.lq_proj.forward_streaming = lambda v, s: seen["lq"].append(lq_fwd(v, s)) or seen["lq"][-1]
+    first, last = session.cores[0], session.cores[-1]
+    first_fwd, last_fwd = first.forward, last.forward
+
+    def first_hook(hidden, *a):
+        seen["first_in"].append(hidden.clone())
+        return first_fwd(hidden, *a)
+
+    def last_hook(*a):
+        r = last_fwd(*a)
+        seen["last_out"].append(r[0].clone())
+        return r
+    first.forward, last.forward = first_hook, last_hook
+    out["session_meta"] = np.array([dim, heads, ffn, channels, height, width, h1, h2, enc_len], np.int64)
+    with torch.inference_mode():
+        for i, (video, noise) in enumerate(recipes.session_inputs(channels, height, width)):
+            result = session.step(t16(video), noise=torch.from_numpy(noise))
+            out[f"session_step{i}_result"] = result.float().numpy()
+            out[f"session_step{i}_lqproj"] = bits(seen["lq"][-1])
+            out[f"session_step{i}_hidden_in"] = bits(seen["first_in"][-1])
+            out[f"session_step{i}_hidden_out"] = bits(seen["last_out"][-1])
+
+
 def main():
-    ref = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("RECAVSR_REFERENCE")
+    args = [a for a in sys.argv[1:] if not a.startswith("--")]
+    ref = args[0] if args else os.environ.get("RECAVSR_REFERENCE")
     if not ref:
-        raise SystemExit("usage: make_golden.py <reference checkout>  (or set RECAVSR_REFERENCE)")
+        raise SystemExit("usage: make_golden.py <reference checkout> [--session]  (or set RECAVSR_REFERENCE)")
     _install_shims(ref)
+    if "--session" in sys.argv:
+        # The session-glue fixtures live in their own file (the reference's
+        # TransformerSession.step with a stand-in model; CPU only).
+        torch.manual_seed(0)
+        out = {}
+        gen_session(out)
+        np.savez_compressed(os.path.join(HERE, "session_outputs.npz"), **out)
+        print("wrote", len(out), "session arrays")
+        return
     torch.manual_seed(0)
     out = {}
     gen_quant(out)

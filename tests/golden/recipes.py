@@ -85,3 +85,35 @@ def block_inputs(n_tokens, cap_tokens, dim=256, seed=12):
     pk = bf16_normal(rs, (1, cap_tokens, dim))
     pv = bf16_normal(rs, (1, cap_tokens, dim))
     return hidden, pk, pv
+
+
+def session_params(dim=256, channels=8, h1=64, h2=96, seed=31):
+    """Weights of the session glue of a stand-in model (runtime/transformer.py:317-349,
+    models/lq_proj.py): patch embedding, sr_proj, proj_out, the LQ projector
+    (conv1 over 16x16-unshuffled RGB = 768 channels, conv2, channel norms,
+    out_proj), the output scale_shift_table (kept fp32) and temb."""
+    rs = np.random.RandomState(seed)
+    bn = lambda shape, std: bf16_normal(rs, shape, std)
+    norm = lambda n: bf16_round(1.0 + 0.1 * rs.standard_normal(n).astype(np.float32))
+    return {
+        "patch_w": bn((dim, channels, 1, 2, 2), 0.1), "patch_b": bn((dim,), 0.02),
+        "sr_w": bn((dim, dim), 0.02), "sr_b": bn((dim,), 0.02),
+        "proj_out_w": bn((channels * 4, dim), 0.02), "proj_out_b": bn((channels * 4,), 0.02),
+        "conv1_w": bn((h1, 768, 4, 3, 3), 0.02), "conv1_b": bn((h1,), 0.02), "norm1_w": norm(h1),
+        "conv2_w": bn((h2, h1, 4, 3, 3), 0.02), "conv2_b": bn((h2,), 0.02), "norm2_w": norm(h2),
+        "out_w": bn((dim, h2), 0.02), "out_b": bn((dim,), 0.02),
+        "scale_shift_table": bn((1, 2, dim), dim ** -0.5), "temb": bn((1, 1, dim), 1.0),
+    }
+
+
+def session_inputs(channels=8, height=128, width=192, seed=32, rgb_frames=(21, 8, 8)):
+    """Per step: (LQ RGB video [1, 3, T, H, W] uniform(-1, 1) in bf16 values,
+    noise [1, C, frames, H/16, W/16] N(0, 1) fp32); prefix then body blocks."""
+    rs = np.random.RandomState(seed)
+    steps = []
+    for i, rgb in enumerate(rgb_frames):
+        frames = 6 if i == 0 else 2
+        video = bf16_round(rs.uniform(-1, 1, (1, 3, rgb, height, width)).astype(np.float32))
+        noise = rs.standard_normal((1, channels, frames, height // 16, width // 16)).astype(np.float32)
+        steps.append((video, noise))
+    return steps

@@ -1,0 +1,85 @@
+"""The session-glue oracle (oracle/session.py) against the reference's own
+TransformerSession.step (tests/golden/session_outputs.npz, made by
+`tests/golden/make_golden.py <reference> --session`): the LQ projector's
+streaming output per block, the hidden state entering the first DiT block
+(patch embedding + LQ projection + sr_proj of the recycled latents) and the
+step result (output head, unpatchify, noise - prediction), each from the
+reference's own inputs to that stage."""
+import os
+
+import numpy as np
+import pytest
+
+from oracle import session as osess
+from oracle.numerics import bf16_from_bits, bf16_round
+from tests.golden import recipes
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+@pytest.fixture(scope="module")
+def sgold():
+    return np.load(os.path.join(ROOT, "tests", "golden", "session_outputs.npz"))
+
+
+def session_setup(meta):
+    dim, heads, ffn, channels, height, width, h1, h2, enc_len = (int(v) for v in meta)
+    p = recipes.session_params(dim, channels, h1, h2)
+    sst = p["scale_shift_table"].astype(np.float32) + p["temb"].astype(np.float32).reshape(1, 1, dim)
+    p["head_shift"], p["head_scale"] = sst[0, 0], sst[0, 1]
+    return p, recipes.session_inputs(channels, height, width)
+
+
+def _rel(got, ref):
+    return float(np.abs(got - ref).max() / max(np.abs(ref).max(), 1e-30))
+
+
+def recycled(sgold, i, p, steps):
+    """The recycled latents entering step i: zeros for the prefix, else the
+    bf16 copy of the last two frames of the reference's previous result."""
+    if i == 0:
+        return np.zeros(steps[0][1].shape[1:], np.float32)
+    return bf16_round(sgold[f"session_step{i - 1}_result"][0][:, -2:])
+
+
+def test_lq_projector_streaming_matches_reference(sgold):
+    p, steps = session_setup(sgold["session_meta"])
+    state = osess.new_lq_state()
+    for i, (video, _) in enumerate(steps):
+        got = osess.lq_project_stream(video[0], state, p)
+        ref = bf16_from_bits(sgold[f"session_step{i}_lqproj"])[0]
+        assert got.shape == ref.shape
+        # about one bf16 ulp: the reference's bf16 convolutions accumulate in
+        # another order (measured 0.4 % max, 0.28 % relative L2)
+        rel_l2 = np.linalg.norm(got - ref) / np.linalg.norm(ref)
+        assert _rel(got, ref) < 1e-2 and rel_l2 < 5e-3, (i, _rel(got, ref), rel_l2)
+
+
+def test_streaming_window_arithmetic():
+    # prefix of 21 RGB frames, then 8-frame body blocks (runtime/constants.py)
+    assert osess.streaming_window(0, 21, 2) == (0, 20, -3, 11)
+    assert osess.streaming_window(21, 8, 2) == (22, 28, 19, 4)
+    assert osess.streaming_window(11, 4, 2) == (12, 14, 9, 2)
+    with pytest.raises(ValueError):
+        osess.streaming_window(21, 1, 2)
+
+
+def test_embedding_matches_reference(sgold):
+    p, steps = session_setup(sgold["session_meta"])
+    state = osess.new_lq_state()
+    for i, (video, noise) in enumerate(steps):
+        got = osess.embed(noise[0], video[0], recycled(sgold, i, p, steps), state, p)
+        ref = bf16_from_bits(sgold[f"session_step{i}_hidden_in"])[0]
+        assert _rel(got, ref) < 2e-2, (i, _rel(got, ref))
+
+
+def test_head_matches_reference(sgold):
+    p, steps = session_setup(sgold["session_meta"])
+    for i, (_, noise) in enumerate(steps):
+        hidden = bf16_from_bits(sgold[f"session_step{i}_hidden_out"])[0]
+        result, rec = osess.head(hidden, noise[0], p)
+        ref = sgold[f"session_step{i}_result"][0]
+        # compare the predictions (result = noise - prediction; the noise dominates)
+        got_pred, ref_pred = noise[0] - result, noise[0] - ref
+        assert _rel(got_pred, ref_pred) < 2e-2, (i, _rel(got_pred, ref_pred))
+        np.testing.assert_array_equal(rec, bf16_round(result[:, -2:]))
