@@ -325,6 +325,9 @@ class LayerStack:
         self.reset()
 
     def reset(self):
+        """Start a new stream: fresh routers and zeroed caches. Graphs captured
+        before hold the old cache pointers and are dropped."""
+        self._graphs.clear()
         ini, st, an = self.router
         self.caches = [FixedKVCache(a, initial=ini, stride=st, anchors=an) for a in self.actions]
         self.max_cap = max(c.capacity for c in self.caches)

@@ -95,6 +95,14 @@ def conv_input(x: torch.Tensor, state: ConvStreamState, frame_dim: int, stride: 
     return inp.contiguous(), n_out
 
 
+def _device(device) -> torch.device:
+    """A CUDA device with its index ("cuda" -> the current device)."""
+    dev = torch.device(device)
+    if dev.type == "cuda" and dev.index is None:
+        dev = torch.device("cuda", torch.cuda.current_device())
+    return dev
+
+
 def _conv_weight(w: torch.Tensor, device) -> torch.Tensor:
     """[cout, cin, kt, kh, kw] -> [cout, kt*kh*kw*cin] bf16 (the im2col column order)."""
     cout = w.shape[0]
@@ -108,8 +116,9 @@ class LQProjector:
     [h2, h1, 4, 3, 3], conv2_b, norm2_w [h2], out_w [out, h2], out_b."""
 
     def __init__(self, weights: dict, device):
+        device = _device(device)
         bf = lambda t: t.to(device=device, dtype=torch.bfloat16).reshape(-1).contiguous()
-        self.device = torch.device(device)
+        self.device = device
         self.w1, self.b1 = _conv_weight(weights["conv1_w"], device), bf(weights["conv1_b"])
         self.w2, self.b2 = _conv_weight(weights["conv2_w"], device), bf(weights["conv2_b"])
         self.n1, self.n2 = bf(weights["norm1_w"]), bf(weights["norm2_w"])
@@ -119,6 +128,9 @@ class LQProjector:
         self.cin = weights["conv1_w"].shape[1]
         if self.cin % (_UNSHUFFLE * _UNSHUFFLE) or self.w1.shape[1] != 36 * self.cin:
             raise ValueError("conv1 must read 16x16-unshuffled RGB with a (4, 3, 3) kernel")
+        if self.h1 % 16 or self.h2 % 64 or self.out_dim % 16:
+            raise ValueError("LQ projector widths: hidden_dim1 % 16, hidden_dim2 % 64 and out_dim % 16 "
+                             "must be 0 (GEMM K and N granules)")
 
     def create_streaming_state(self):
         return (ConvStreamState(), ConvStreamState())
@@ -179,13 +191,16 @@ class SessionGlue:
     weights (LQProjector)."""
 
     def __init__(self, weights: dict, device):
-        dev = torch.device(device)
+        dev = _device(device)
         bf = lambda t: t.to(device=dev, dtype=torch.bfloat16).contiguous()
         self.device = dev
         pw = weights["patch_w"]
         self.dim, self.channels = pw.shape[0], pw.shape[1]
         if tuple(pw.shape[2:]) != (1, 2, 2):
             raise ValueError("patch embedding must be a (1, 2, 2) Conv3d")
+        if (self.channels * 4) % 64 or self.dim % 64:
+            raise ValueError("latent channels * 4 and the model width must be multiples of 64 "
+                             "(GEMM K granule)")
         self.patch_w, self.patch_b = bf(pw.reshape(self.dim, -1)), bf(weights["patch_b"])
         self.sr_w, self.sr_b = bf(weights["sr_w"]), bf(weights["sr_b"])
         self.out_w, self.out_b = bf(weights["proj_out_w"]), bf(weights["proj_out_b"])

@@ -370,7 +370,7 @@ class _SessionModel(nn.Module):
         return types.SimpleNamespace(temb=self._temb, timestep_proj=self._tproj, encoder_hidden_states=prompt)
 
 
-def gen_session(out, dim=256, heads=2, ffn=512, channels=8, height=128, width=192, h1=64, h2=96,
+def gen_session(out, dim=256, heads=2, ffn=512, channels=16, height=128, width=192, h1=64, h2=128,
                 enc_len=16, actions=("recent_2", "none")):
     """Three TransformerSession.step calls (prefix 21 RGB frames, then two
     8-frame body blocks) of a 2-layer stand-in model, NVFP4 block linears

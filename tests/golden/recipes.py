@@ -87,7 +87,7 @@ def block_inputs(n_tokens, cap_tokens, dim=256, seed=12):
     return hidden, pk, pv
 
 
-def session_params(dim=256, channels=8, h1=64, h2=96, seed=31):
+def session_params(dim=256, channels=16, h1=64, h2=128, seed=31):
     """Weights of the session glue of a stand-in model (runtime/transformer.py:317-349,
     models/lq_proj.py): patch embedding, sr_proj, proj_out, the LQ projector
     (conv1 over 16x16-unshuffled RGB = 768 channels, conv2, channel norms,
@@ -106,7 +106,7 @@ def session_params(dim=256, channels=8, h1=64, h2=96, seed=31):
     }
 
 
-def session_inputs(channels=8, height=128, width=192, seed=32, rgb_frames=(21, 8, 8)):
+def session_inputs(channels=16, height=128, width=192, seed=32, rgb_frames=(21, 8, 8)):
     """Per step: (LQ RGB video [1, 3, T, H, W] uniform(-1, 1) in bf16 values,
     noise [1, C, frames, H/16, W/16] N(0, 1) fp32); prefix then body blocks."""
     rs = np.random.RandomState(seed)
