@@ -11,12 +11,13 @@ projection. One step = one body block through all 30 layers; the 6-frame
 prefix block and enough body blocks to fill every layer's cache run as
 warm-up. Inputs/weights/caches (~4 GB) exceed L2 (126 MB), so no flush.
 
-  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference] [--head-shard]
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference] [--head-shard | --session]
 
 Under torchrun each rank runs an independent stream (weak scaling, no
 collective); rank 0 prints one JSON line with the max-over-ranks time.
 --head-shard instead runs one 3840x2176 stream split by heads over the ranks
-(NCCL all-to-all at the attention boundary; strong scaling).
+(NCCL all-to-all at the attention boundary; strong scaling); --session times the
+whole one-step DiT stream step (LQ projector, patch embedding, layers, head).
 """
 from __future__ import annotations
 
@@ -413,6 +414,137 @@ def run_head_shard(args, rank, world, local):
     }), flush=True)
 
 
+# ------------------------------------------- whole one-step DiT stream (glue)
+LQ_H1, LQ_H2, LATENT_C = 2048, 3072, 48
+
+
+def build_glue(device, seed):
+    """Random-init session glue of the released architecture: patch embedding
+    Conv3d(48 -> 3072, 1x2x2), the LQ projector (768 -> 2048 -> 3072 causal
+    Conv3d (4, 3, 3) + out_proj 3072 -> 3072), sr_proj, proj_out 3072 -> 192, the
+    output scale_shift_table + temb."""
+    import torch
+    from recavsr_b200.runtime.session import SessionGlue
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    rnd = lambda *s, std=0.02: (torch.randn(*s, generator=g, device=device) * std).bfloat16()
+    w = {"patch_w": rnd(DIM, LATENT_C, 1, 2, 2, std=0.05), "patch_b": rnd(DIM),
+         "sr_w": rnd(DIM, DIM), "sr_b": rnd(DIM), "proj_out_w": rnd(LATENT_C * 4, DIM),
+         "proj_out_b": rnd(LATENT_C * 4),
+         "conv1_w": rnd(LQ_H1, 768, 4, 3, 3), "conv1_b": rnd(LQ_H1), "norm1_w": 1 + rnd(LQ_H1, std=0.1),
+         "conv2_w": rnd(LQ_H2, LQ_H1, 4, 3, 3), "conv2_b": rnd(LQ_H2), "norm2_w": 1 + rnd(LQ_H2, std=0.1),
+         "out_w": rnd(DIM, LQ_H2), "out_b": rnd(DIM),
+         "head_shift": rnd(DIM, std=DIM ** -0.5).float(), "head_scale": rnd(DIM, std=DIM ** -0.5).float()}
+    return SessionGlue(w, device)
+
+
+def synthetic_lq(frames, device, seed):
+    """LQ RGB frames as the reference's pipeline feeds them (video.py:103-179):
+    uint8 uniform noise at 320x176, 5x5 box filter, bilinear x4 to 1280x704,
+    normalized to [-1, 1], bf16 [1, 3, frames, 704, 1280]."""
+    import torch
+    import torch.nn.functional as F
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    lr = torch.randint(0, 256, (frames, 3, 176, 320), generator=g, device=device).float()
+    lr = F.avg_pool2d(F.pad(lr, (2, 2, 2, 2), mode="replicate"), 5, stride=1)
+    hr = F.interpolate(lr, size=(704, 1280), mode="bilinear", align_corners=False)
+    return (hr / 127.5 - 1.0).clamp(-1, 1).permute(1, 0, 2, 3).unsqueeze(0).bfloat16().contiguous()
+
+
+def run_session(args, rank, world, local):
+    """--session: the whole streaming one-step DiT (TransformerSession.step) at
+    1280x704 output: LQ projector + patch embedding + sr_proj, the 30-layer loop
+    (CUDA graph), output head, noise - prediction. Each step reads its 8 LQ RGB
+    frames from pinned host memory and returns its 2 latent frames to pinned
+    host memory inside the timed region; one independent stream per rank."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+    from recavsr_b200 import _lib
+    from recavsr_b200.runtime.session import StreamingSession
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+    session = StreamingSession(build_stack(device, seed=1234 + rank), build_glue(device, 77 + rank),
+                               704, 1280, seed=rank, graphs=True)
+    prefix = synthetic_lq(21, device, 5 + rank)
+    body = synthetic_lq(8, device, 6 + rank)
+    host_lq = torch.empty(body.shape, dtype=torch.bfloat16, pin_memory=True)
+    host_lq.copy_(body.cpu())
+    out_shape = (1, LATENT_C, BODY, 44, 80)
+    host_out = torch.empty(out_shape, dtype=torch.float32, pin_memory=True)
+    session.step(prefix)
+    warm = max(args.warmup, 3)
+    for _ in range(warm):
+        session.step(host_lq.to(device, non_blocking=True))
+    torch.cuda.synchronize(device)
+    dev_err = _lib.read_device_error()
+    if dev_err:
+        raise RuntimeError(f"device error word 0x{dev_err:08x}")
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(device)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        start.record()
+        for _ in range(args.steps):
+            result = session.step(host_lq.to(device, non_blocking=True))
+            host_out.copy_(result, non_blocking=True)
+        end.record()
+        end.synchronize()
+    t = start.elapsed_time(end) * 1e-3
+    if not torch.isfinite(host_out).all():
+        raise RuntimeError("non-finite session output")
+    # Per-phase device time of the glue on body blocks (a fresh LQ stream
+    # primed with a prefix, so every timed call is a valid streaming step).
+    glue = session.glue
+    nz = torch.randn(out_shape, device=device)
+    rec = torch.zeros(out_shape, dtype=torch.bfloat16, device=device)
+    lq_dev = host_lq.to(device)
+    lq_state = glue.lq.create_streaming_state()
+    glue.lq.forward_streaming(prefix, lq_state)
+    t_embed = time_kernel(lambda: glue.embed(nz, lq_dev, rec, lq_state), 5, torch)
+    hidden = torch.randn(BODY * T, DIM, device=device).bfloat16()
+    t_head = time_kernel(lambda: glue.head(hidden, nz), 5, torch)
+    m1, m2 = 4 * 44 * 80, BODY * T                       # conv1 / conv2 output rows per body block
+    embed_flops = (2.0 * m1 * LQ_H1 * 36 * 768 + 2.0 * m2 * LQ_H2 * 36 * LQ_H1 + 2.0 * m2 * DIM * LQ_H2
+                   + 2 * 2.0 * m2 * DIM * LATENT_C * 4 + 2.0 * m2 * DIM * DIM)
+    _, bf16_peak, _, src = peaks()
+    if world > 1:
+        tt = torch.tensor([t], device=device)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        t = float(tt[0])
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    tokens = BODY * T * args.steps * world
+    value = tokens / t
+    print(json.dumps({
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": warm, "ms_per_step": t / args.steps * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "nvfp4 DiT linears / bf16 attention and glue",
+        "data": "synthetic (random-init weights; LQ frames: uint8 noise, 5x5 box filter, bilinear x4)",
+        "config": {"workload": "cfg4 whole one-step DiT stream step (LQ projector, patch embedding, "
+                               "30 layers, output head), 1280x704, 8 LQ frames -> 2 latent frames",
+                   "global_batch": world, "seq_len": BODY * T, "parallelism": f"streams x{world}",
+                   "l2": "working set > 126 MB L2 (no flush)", "cuda_graph": "layer loop"},
+        "out_fps": value * 4 / T,
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": host_lq.numel() * 2,
+                "d2h_bytes_per_step": host_out.numel() * 4,
+                "path": "StreamingSession.step: LQ frames from pinned host, latents to pinned host"},
+        "glue": {"embed_ms": t_embed * 1e3, "head_ms": t_head * 1e3,
+                 "embed_tflops": embed_flops / t_embed / 1e12,
+                 "embed_frac": embed_flops / t_embed / 1e12 / bf16_peak,
+                 "peak": f"{src} bf16 dense {bf16_peak} TFLOP/s",
+                 "embed": "LQ projector (im2col + bf16 GEMMs + channel RMSNorm/SiLU), patch embedding x2, sr_proj"},
+        "clocks": clk.summary(),
+    }), flush=True)
+
+
 # ------------------------------------------------------------------- main
 def main():
     ap = argparse.ArgumentParser()
@@ -426,6 +558,8 @@ def main():
                     help="skip the per-kernel roofline timing (e.g. for an ncu launch list)")
     ap.add_argument("--head-shard", action="store_true",
                     help="one 3840x2176 stream split by heads over the ranks (strong scaling)")
+    ap.add_argument("--session", action="store_true",
+                    help="the whole one-step DiT stream step (LQ projector, layers, head) per block")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
@@ -434,6 +568,8 @@ def main():
         return run_reference(args, rank, world)
     if args.head_shard:
         return run_head_shard(args, rank, world, local)
+    if args.session:
+        return run_session(args, rank, world, local)
 
     import torch
     import torch.distributed as dist
