@@ -299,3 +299,43 @@ class StreamingSession:
         result, self.previous_latents = self.glue.head(hidden, noise)
         self.latent_offset += frames
         return result
+
+    def step_host(self, host_lq: torch.Tensor, host_out: torch.Tensor) -> None:
+        """step() from pinned host LQ frames to pinned host latents: the
+        host-to-device copy of this block's frames and the device-to-host copy
+        of its result run on a copy stream with double-buffered staging, so they
+        overlap the neighbouring blocks' work. Asynchronous: call sync_host()
+        before reading host_out."""
+        dev = self.glue.device
+        if getattr(self, "_copy", None) is None:
+            self._copy, self._stage = torch.cuda.Stream(dev), {}
+        comp, cs = torch.cuda.current_stream(dev), self._copy
+        key = tuple(host_lq.shape)
+        if key not in self._stage:
+            st = {"lq": [torch.empty(key, dtype=torch.bfloat16, device=dev) for _ in range(2)], "k": 0,
+                  "ready": [torch.cuda.Event() for _ in range(2)],
+                  "consumed": [torch.cuda.Event() for _ in range(2)]}
+            for e in st["consumed"]:
+                e.record(comp)
+            self._stage[key] = st
+        st = self._stage[key]
+        k = st["k"] & 1
+        with torch.cuda.stream(cs):
+            cs.wait_event(st["consumed"][k])          # the block two steps back has read this buffer
+            st["lq"][k].copy_(host_lq, non_blocking=True)
+            st["ready"][k].record(cs)
+        comp.wait_event(st["ready"][k])
+        result = self.step(st["lq"][k])
+        st["consumed"][k].record(comp)
+        done = torch.cuda.Event()
+        done.record(comp)
+        with torch.cuda.stream(cs):
+            cs.wait_event(done)
+            host_out.copy_(result, non_blocking=True)
+        result.record_stream(cs)
+        st["k"] += 1
+
+    def sync_host(self) -> None:
+        """Make the current stream wait for every step_host copy issued so far."""
+        if getattr(self, "_copy", None) is not None:
+            torch.cuda.current_stream(self.glue.device).wait_stream(self._copy)

@@ -96,3 +96,40 @@ def test_streaming_session_matches_reference(sgold, graphs):
     with pytest.raises(ValueError):
         session.step(dev_bf16(steps[1][0][:, :, :4]))
     assert_no_device_error()
+
+
+def test_step_host_matches_step(sgold):
+    """The pinned-host streaming entry (copies on a side stream, double-buffered
+    staging, no host sync until the end) returns exactly what step() returns."""
+    from recavsr_b200.runtime.block import FusedBlock, LayerStack, rope_tables
+    from recavsr_b200.runtime.session import StreamingSession
+    dim, heads, ffn, channels, height, width, h1, h2, enc_len = (int(v) for v in sgold["session_meta"])
+    p, steps = session_setup(sgold["session_meta"])
+    H, W = height // 32, width // 32
+    tables = rope_tables(dim // heads, H, W, "cuda")
+    bp = [recipes.block_params(dim, heads, ffn, enc_len=enc_len, seed=70 + i) for i in range(2)]
+
+    def make():
+        blocks = []
+        for b in bp:
+            w = {k: dev_bf16(v) for k, v in b.items()}
+            w["heads"] = heads
+            blocks.append(FusedBlock(w, H, W, tables))
+        return StreamingSession(LayerStack(blocks, ["recent_2", "none"]), _glue(p), height, width,
+                                seed=7, graphs=True)
+    a, b = make(), make()
+    rs = np.random.RandomState(9)
+    lq = [steps[0][0]] + [bf16_round(rs.uniform(-1, 1, steps[1][0].shape).astype(np.float32))
+                          for _ in range(5)]
+    want = [host(a.step(dev_bf16(x)))[0] for x in lq]
+    outs = []
+    for x in lq:
+        hin = torch.from_numpy(x).bfloat16().pin_memory()
+        shape = (1, channels, 6 if not outs else 2, height // 16, width // 16)
+        outs.append(torch.empty(shape, dtype=torch.float32).pin_memory())
+        b.step_host(hin, outs[-1])
+    b.sync_host()
+    torch.cuda.synchronize()
+    for i, (o, w_) in enumerate(zip(outs, want)):
+        np.testing.assert_array_equal(o.numpy()[0], w_, err_msg=f"block {i}")
+    assert_no_device_error()
