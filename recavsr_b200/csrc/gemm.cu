@@ -87,6 +87,11 @@ struct GemmParams {
   int n_regular, split;
   float* part;                 // [units of split tiles][BM x BN] as [BN/4][BM][4]
   int* counters;               // [split tiles]; zero between launches (the merging unit resets it)
+  // Tile raster: tiles run in groups of group_m row blocks, row block fastest
+  // within a group, then column block. group_m = m_blocks is the plain
+  // row-fastest order; a smaller group keeps the operand panels one wave
+  // touches few enough to be served from L2 when A and B do not fit in it.
+  int group_m;
 };
 
 constexpr int kMaxSplit = 4;       // units per split tile
@@ -101,6 +106,15 @@ __device__ __forceinline__ Unit unit_of(const GemmParams& p, int u) {
   if (u < p.n_regular) return {u, 0, p.k_tiles, -1};
   const int t = u - p.n_regular, tt = t / p.split, pc = t - tt * p.split;
   return {p.n_regular + tt, pc * p.k_tiles / p.split, (pc + 1) * p.k_tiles / p.split, t};
+}
+// Row / column block of a tile index under the grouped raster (a bijection
+// onto [0, m_blocks) x [0, n_blocks); the last group may hold fewer rows).
+__device__ __forceinline__ void tile_coords(const GemmParams& p, int tile, int& mb, int& nb) {
+  const int per_group = p.group_m * p.n_blocks;
+  const int g = tile / per_group, r = tile - g * per_group;
+  const int gm = min(p.group_m, p.m_blocks - g * p.group_m);
+  mb = g * p.group_m + r % gm;
+  nb = r / gm;
 }
 
 template <int KIND, int BN, int STAGES>
@@ -220,7 +234,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
       bool ok = true;
       for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
         const Unit un = unit_of(p, u);
-        const int mb = un.tile % p.m_blocks, nb = un.tile / p.m_blocks;
+        int mb, nb;
+        tile_coords(p, un.tile, mb, nb);
         for (int kt = un.kt0; kt < un.kt1; ++kt) {
           if (!wait(&empty[stage], phase ^ 1, 1)) { ok = false; break; }
           uint32_t bytes = S::kA + S::kB;
@@ -375,7 +390,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
     asm volatile("bar.sync 1, %0;" ::"r"(32 * epi_warps<EPI>()) : "memory");
     for (int u = blockIdx.x; u < num_units; u += gridDim.x, ++local) {
       const Unit un = unit_of(p, u);
-      const int mb = un.tile % p.m_blocks, nb = un.tile / p.m_blocks;
+      int mb, nb;
+      tile_coords(p, un.tile, mb, nb);
       const int as = local % kAcc;
       const bool got = __all_sync(0xffffffffu, wait(&acc_full[as], (uint32_t)((local / kAcc) & 1), 4));
       if (!got && (BN != 128 || un.piece < 0)) break;
@@ -720,6 +736,13 @@ int run_gemm(int kind, int epi, const void* a, const void* b, int M, int N, int 
   p.k_tiles = (K + ept - 1) / ept;
   p.m_blocks = (M + BM - 1) / BM;
   p.sf_katoms = (K + 63) / 64;
+  // Operands beyond half the 126 MB L2 (the LQ projector's convolutions, K up
+  // to 73728): groups of 12 row blocks, so a wave of 148 tiles reads ~12 A
+  // and ~13 B panels instead of up to 110 A panels (measured on the
+  // 14080 x 2048 x 27648 bf16 GEMM: 9.8 GB of DRAM reads for 0.9 GB of
+  // operands in row-fastest order). Smaller GEMMs keep row-fastest order.
+  const double operand_bytes = ((double)M + (double)N) * (double)row_bytes;
+  p.group_m = operand_bytes > 64e6 && p.m_blocks > 12 ? 12 : p.m_blocks;
   if (wide) {
     p.n_blocks = N / 256;
     if (kind == KIND_NVF4) return dispatch_epi<KIND_NVF4, 256, 4>(epi, ta, tb, p, stream, what);

@@ -9,6 +9,9 @@
     python -m recavsr_b200.profile_case rms          # RMSNorm+spatial RoPE of q and k, 1760x3072 each
     python -m recavsr_b200.profile_case gemm_sweep   # NVFP4 / FP8 linears, M x (K, N) sweep + quantizers
     python -m recavsr_b200.profile_case attention_sweep  # 30-layer routed attention, scopes 0/1/2/4/8
+    python -m recavsr_b200.profile_case lq_conv1     # LQ projector conv1: im2col + bf16 GEMM, body block
+    python -m recavsr_b200.profile_case lq_conv2     # LQ projector conv2: im2col + bf16 GEMM, body block
+    python -m recavsr_b200.profile_case lq_norm      # channel RMSNorm + SiLU, 14080 x 2048
 
 Each case allocates fresh inputs (a few hundred MB at most), captures `--reps`
 launches in a CUDA graph, replays it and prints the mean CUDA-event time per
@@ -156,7 +159,56 @@ def _cross_attention(nk=512):
     return run, 4.0 * HD * HEADS * M * nk, "TFLOP/s"
 
 
+def _lq_conv(which):
+    """One body block of the LQ projector's causal Conv3d at 1280x704 (the
+    frames a body chunk reads): conv1 = im2col of 16x16-unshuffled RGB
+    (10 frames -> 4 outputs of 44 x 80) + bf16 GEMM 14080 x 2048 x 27648;
+    conv2 = im2col of conv1's channels-last output (6 frames -> 2 outputs of
+    22 x 40) + bf16 GEMM 1760 x 3072 x 73728. Time covers both launches."""
+    g = torch.Generator(device="cuda")
+    g.manual_seed(0)
+    lib = _lib.library()
+    if which == 1:
+        src = torch.randn(3, 10, 704, 1280, generator=g, device="cuda").bfloat16()
+        cin, cout, fin, hin, win, ss, fout = 768, 2048, 10, 44, 80, 1, 4
+        strides = (704 * 1280, 10 * 704 * 1280, 1280, 0, 16)
+    else:
+        src = torch.randn(6, 44, 80, 2048, generator=g, device="cuda").bfloat16()
+        cin, cout, fin, hin, win, ss, fout = 2048, 3072, 6, 44, 80, 2, 2
+        strides = (44 * 80 * 2048, 0, 80 * 2048, 2048, 0)
+    ho, wo = (hin - 1) // ss + 1, (win - 1) // ss + 1
+    rows, k = fout * ho * wo, 36 * cin
+    cols = torch.empty(rows, k, dtype=torch.bfloat16, device="cuda")
+    w = (torch.randn(cout, k, generator=g, device="cuda") * 0.02).bfloat16()
+    bias = torch.zeros(cout, dtype=torch.bfloat16, device="cuda")
+    out = torch.empty(rows, cout, dtype=torch.bfloat16, device="cuda")
+
+    def run():
+        _lib.check(lib.rc_conv3d_im2col(src.data_ptr(), *strides, cin, fin, hin, win, 2, ss, fout,
+                                        cols.data_ptr(), k, _lib.stream()), "im2col")
+        _lib.check(lib.rc_bf16_gemm(cols.data_ptr(), w.data_ptr(), bias.data_ptr(), rows, cout, k,
+                                    _lib.EPI_BIAS, out.data_ptr(), cout, None, _lib.stream()), "gemm")
+    return run, 2.0 * rows * cout * k, "TFLOP/s"
+
+
+def _lq_norm():
+    """Channel RMSNorm + SiLU in place on conv1's body-block output (14080 x 2048)."""
+    g = torch.Generator(device="cuda")
+    g.manual_seed(0)
+    x = torch.randn(14080, 2048, generator=g, device="cuda").bfloat16()
+    w = torch.ones(2048, dtype=torch.bfloat16, device="cuda")
+    lib = _lib.library()
+
+    def run():
+        _lib.check(lib.rc_channel_rmsnorm_silu(x.data_ptr(), 2048, 14080, 2048, w.data_ptr(), 1e-6,
+                                               x.data_ptr(), 2048, _lib.stream()), "rmsnorm_silu")
+    return run, 2.0 * 2 * 14080 * 2048, "GB/s"
+
+
 CASES = {
+    "lq_conv1": lambda: _lq_conv(1),
+    "lq_conv2": lambda: _lq_conv(2),
+    "lq_norm": _lq_norm,
     "gemm_up": lambda: _gemm(FFN, DIM, _lib.EPI_GELU_NVFP4),
     "gemm_qkv": lambda: _gemm(3 * DIM, DIM, _lib.EPI_BIAS),
     "gemm_o": lambda: _gemm(DIM, DIM, _lib.EPI_GATED_RESIDUAL),

@@ -213,3 +213,27 @@ def test_gemm_rejects_bad_k():
     with pytest.raises(ValueError):
         nvfp4.gemm(a, a, torch.zeros(512, dtype=torch.uint8, device="cuda"),
                    torch.zeros(512, dtype=torch.uint8, device="cuda"))
+
+
+def test_bf16_gemm_grouped_tile_raster():
+    """Operands beyond half the L2 (here 2 x 64 MB) run in the grouped tile
+    order (12 row blocks per group; 2000 rows = 16 row blocks, so the last
+    group is partial): every output tile must still land where it belongs.
+    Reference: fp32 matmul of the same bf16 operands, rounded to bf16."""
+    from recavsr_b200 import _lib
+    g = torch.Generator(device="cuda")
+    g.manual_seed(5)
+    m, n, k = 2000, 2048, 16384
+    a = torch.randn(m, k, generator=g, device="cuda").bfloat16()
+    w = (torch.randn(n, k, generator=g, device="cuda") * 0.02).bfloat16()
+    bias = (torch.randn(n, generator=g, device="cuda") * 0.1).bfloat16()
+    out = torch.empty(m, n, dtype=torch.bfloat16, device="cuda")
+    _lib.call("rc_bf16_gemm", a.data_ptr(), w.data_ptr(), bias.data_ptr(), m, n, k, _lib.EPI_BIAS,
+              out.data_ptr(), n, None, _lib.stream())
+    ref = (a.float() @ w.float().T + bias.float()).bfloat16().float()
+    assert_no_device_error()
+    err = (out.float() - ref).abs()
+    assert float(err.max() / ref.abs().max()) < TOL
+    # a misplaced tile would be off by O(1) in some 128 x 128 block
+    tiles = torch.nn.functional.pad(err, (0, 0, 0, 2048 - m)).reshape(16, 128, 16, 128).amax((1, 3))
+    assert float(tiles.max()) < TOL * float(ref.abs().max()), tiles
