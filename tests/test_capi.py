@@ -43,3 +43,31 @@ def test_argument_errors_raise_valueerror_without_gpu():
         _lib.call("rc_nvfp4_quantize", None, 4, 15, 15, 1.0, None, None, None)
     with pytest.raises(ValueError):
         _lib.call("rc_kv_commit", None, None, 0, None, None, 0, 24, 1, 9, None, None, None)
+
+
+def test_session_and_commit_entry_points_reject_bad_arguments():
+    """The session-glue entry points and the planned KV commit reject invalid
+    geometry and strides on the host, before any device work (every call
+    here fails validation, most with null pointers, so nothing is launched)."""
+    import pytest
+    from recavsr_b200 import _lib
+    with pytest.raises(ValueError, match="bad geometry"):          # cin % 8
+        _lib.call("rc_conv3d_im2col", None, 0, 0, 0, 0, 0, 12, 10, 4, 4, 2, 1, 4, None, 0, None)
+    with pytest.raises(ValueError, match="bad geometry"):          # unshuffle not a multiple of 8
+        _lib.call("rc_conv3d_im2col", None, 0, 0, 0, 0, 4, 768, 10, 4, 4, 2, 1, 4, None, 0, None)
+    with pytest.raises(ValueError, match="need 10 input frames"):  # (4 - 1) * 2 + 4 > 9
+        _lib.call("rc_conv3d_im2col", None, 0, 0, 0, 0, 16, 768, 9, 4, 4, 2, 1, 4, None, 0, None)
+    with pytest.raises(ValueError, match="16-byte aligned"):       # null source
+        _lib.call("rc_conv3d_im2col", None, 8, 8, 8, 8, 0, 64, 10, 4, 4, 2, 1, 4, None, 2304, None)
+    with pytest.raises(ValueError, match="bad shape"):             # C > 8192
+        _lib.call("rc_channel_rmsnorm_silu", None, 16384, 4, 16384, None, 1e-6, None, 16384, None)
+    with pytest.raises(ValueError, match="bad shape"):             # C % 8
+        _lib.call("rc_channel_rmsnorm_silu", None, 12, 4, 12, None, 1e-6, None, 12, None)
+    with pytest.raises(ValueError, match="bad shape"):             # H % ph
+        _lib.call("rc_patchify", None, 0, 1, 1, 1, 16, 2, 5, 6, 2, 2, None, 64, None)
+    with pytest.raises(ValueError, match="bad shape"):             # recycle_frames > F
+        _lib.call("rc_unpatchify_residual", None, 64, None, None, None, 16, 2, 4, 6, 2, 2, 3, None)
+    with pytest.raises(ValueError, match="row stride below row_bytes"):
+        _lib.call("rc_kv_commit_planned", 4096, 4096, 16, 32, 4096, 4096, 32, 32, 24, 2, 2, 4096, None)
+    with pytest.raises(ValueError, match="bad shape"):             # row_bytes % 16
+        _lib.call("rc_kv_commit_planned", None, None, 0, 0, None, None, 0, 24, 1, 2, 2, None, None)
