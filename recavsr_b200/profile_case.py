@@ -12,6 +12,7 @@
     python -m recavsr_b200.profile_case lq_conv1     # LQ projector conv1: im2col + bf16 GEMM, body block
     python -m recavsr_b200.profile_case lq_conv2     # LQ projector conv2: im2col + bf16 GEMM, body block
     python -m recavsr_b200.profile_case lq_norm      # channel RMSNorm + SiLU, 14080 x 2048
+    python -m recavsr_b200.profile_case gemm_vs_cublas   # NVFP4 GEMM vs the reference's _scaled_mm_v2 (cuBLASLt)
 
 Each case allocates fresh inputs (a few hundred MB at most), captures `--reps`
 launches in a CUDA graph, replays it and prints the mean CUDA-event time per
@@ -303,6 +304,47 @@ def gemm_sweep(reps=10):
             del a, w, ac, asf, wc, wsf, aq, wq, out
 
 
+def gemm_vs_cublas(reps=10):
+    """The reference's own NVFP4 GEMM call (recavsr_infer/runtime/nvfp4.py:22-39:
+    torch._scaled_mm_v2, BlockWise1x16 scales in the 32x4x4 swizzle, bias, bf16
+    out -- cuBLASLt) next to rc_nvfp4_gemm on the same codes and scales (the
+    quantizer's output is byte-identical to the reference's), cfg3 shapes; also
+    the largest difference between the two outputs relative to max |cuBLAS|."""
+    lib = _lib.library()
+    if not hasattr(torch, "_scaled_mm_v2") or not hasattr(torch, "float4_e2m1fn_x2"):
+        raise SystemExit("this torch has no _scaled_mm_v2 / float4_e2m1fn_x2")
+    g = torch.Generator(device="cuda")
+    g.manual_seed(2)
+    print("M     K      N      ours us  TFLOP/s | cuBLAS us  TFLOP/s | ours/cuBLAS time  max diff")
+    for m in (1760, 3520, 7040):
+        for k, n in ((3072, 3072), (3072, 14336), (14336, 3072)):
+            a, w = _cfg3_operands(m, n, k, g)
+            bias = (torch.randn(n, generator=g, device="cuda") * 0.02).bfloat16()
+            out = torch.empty(m, n, dtype=torch.bfloat16, device="cuda")
+            ac, asf = quantize(a)
+            wc, wsf = quantize(w)
+
+            def ours():
+                _lib.check(lib.rc_nvfp4_gemm(ac.data_ptr(), asf.data_ptr(), wc.data_ptr(), wsf.data_ptr(),
+                                             bias.data_ptr(), m, n, k, 1.0, _lib.EPI_BIAS, out.data_ptr(), n,
+                                             None, None, None, 1.0, _lib.stream()), "nvfp4_gemm")
+
+            def cublas():
+                return torch._scaled_mm_v2(
+                    ac.view(torch.float4_e2m1fn_x2), wc.view(torch.float4_e2m1fn_x2).t(),
+                    [asf.view(torch.float8_e4m3fn)], [2], [1], [wsf.view(torch.float8_e4m3fn)], [2], [1],
+                    bias, torch.bfloat16)
+            ref = cublas()
+            ours()
+            torch.cuda.synchronize()
+            diff = float((out.float() - ref.float()).abs().max() / ref.float().abs().max())
+            t, tc = _graph_time(ours, reps), _graph_time(cublas, reps)
+            fl = 2.0 * m * n * k
+            print(f"{m:5d} {k:6d} {n:6d} {t * 1e6:8.1f} {fl / t / 1e12:8.1f} | {tc * 1e6:8.1f} "
+                  f"{fl / tc / 1e12:8.1f} | {t / tc:6.3f}  {diff:.2e}")
+            del a, w, ac, asf, wc, wsf, out, ref
+
+
 def attention_sweep(reps=5):
     """Routed-attention microbenchmark: 30 layers x 24 heads x 128, T = 880
     (22 x 40), 2-frame query block (1760 queries), layer i attends to
@@ -340,7 +382,7 @@ def attention_sweep(reps=5):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=sorted(CASES) + ["gemm_sweep", "attention_sweep"])
+    ap.add_argument("case", choices=sorted(CASES) + ["gemm_sweep", "attention_sweep", "gemm_vs_cublas"])
     ap.add_argument("--reps", type=int, default=20)
     ap.add_argument("--seconds", type=float, default=0.0,
                     help="also replay for this long and report the sustained per-launch time "
@@ -350,6 +392,8 @@ def main():
         return gemm_sweep()
     if args.case == "attention_sweep":
         return attention_sweep()
+    if args.case == "gemm_vs_cublas":
+        return gemm_vs_cublas()
     run, work, unit = CASES[args.case]()
     for _ in range(3):
         run()
