@@ -1,9 +1,12 @@
 """Generate the golden fixtures of tests/golden/ by running the REFERENCE itself.
 
 Run where a checkout of the reference exists:
-    python tests/golden/make_golden.py <reference checkout>
+    python tests/golden/make_golden.py <reference checkout>            # reference_outputs.npz, router.json
+    python tests/golden/make_golden.py <reference checkout> --session  # session_outputs.npz
 (or set RECAVSR_REFERENCE). Under TRITON_INTERPRET=1 it also records the
-reference's Triton kernel on windowed cases.
+reference's Triton kernel on windowed cases. The --session fixtures come from
+the reference's TransformerSession.step on a stand-in model (its own LQ4xProj
+and torch modules; weights and inputs from recipes.py).
 
 The reference is imported with two import shims and no other change:
 * ``diffusers.models.embeddings.get_1d_rotary_pos_embed`` (diffusers 0.37.1 is
