@@ -538,6 +538,9 @@ def run_session(args, rank, world, local):
                 "d2h_bytes_per_step": host_out.numel() * 4,
                 "path": "StreamingSession.step_host: LQ frames from pinned host, latents to pinned host "
                         "(copies on a side stream, overlapping the neighbouring blocks)"},
+        # per step: the layer loop (14 per layer + one commit per cached layer) and the glue
+        # (2 im2col, 2 channel norms, 7 bf16 GEMMs, 2 patch gathers, 1 LayerNorm, 1 unpatchify)
+        "gpu_launches": args.steps * (LAYERS * 14 + sum(1 for c in session.stack.caches if c.capacity) + 15),
         "glue": {"embed_ms": t_embed * 1e3, "head_ms": t_head * 1e3,
                  "embed_tflops": embed_flops / t_embed / 1e12,
                  "embed_frac": embed_flops / t_embed / 1e12 / bf16_peak,
