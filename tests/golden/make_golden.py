@@ -3,6 +3,8 @@
 Run where a checkout of the reference exists:
     python tests/golden/make_golden.py <reference checkout>            # reference_outputs.npz, router.json
     python tests/golden/make_golden.py <reference checkout> --session  # session_outputs.npz
+    TRITON_INTERPRET=1 python tests/golden/make_golden.py <reference checkout> --flashdecoder
+                                                                        # flashdecoder_outputs.npz
 (or set RECAVSR_REFERENCE). Under TRITON_INTERPRET=1 it also records the
 reference's Triton kernel on windowed cases. The --session fixtures come from
 the reference's TransformerSession.step on a stand-in model (its own LQ4xProj
@@ -455,12 +457,43 @@ def gen_session(out, dim=256, heads=2, ffn=512, channels=16, height=128, width=1
             out[f"session_step{i}_hidden_out"] = bits(seen["last_out"][-1])
 
 
+def gen_flashdecoder(out):
+    """FlashDecoder's local GQA attention (models/flashdecoder/flashdecoder_wan22.py:38-119):
+    the reference's CPU path (fp32 SDPA under the visibility mask) on the three
+    geometries of recipes.LOCAL_GQA_CASES, and under TRITON_INTERPRET=1 its Triton forward
+    (_local_attention_triton.py:21-131, fp16) on the first."""
+    from recavsr_infer.models.flashdecoder.flashdecoder_wan22 import _local_attention
+    for tag, (b, hq, hk, d, h, w, win, grp, tw, qf, nf) in recipes.LOCAL_GQA_CASES.items():
+        q, k, v = recipes.local_gqa_inputs(tag)
+        res = _local_attention(torch.from_numpy(q), torch.from_numpy(k), torch.from_numpy(v), height=h,
+                               width=w, window=win, group_size=grp, temporal_window=tw)
+        out[f"fd_{tag}_out"] = res.numpy()
+    if os.environ.get("TRITON_INTERPRET") == "1":
+        import triton
+        from recavsr_infer.models.flashdecoder import _local_attention_triton as fl
+        b, hq, hk, d, h, w, win, grp, tw, qf, nf = recipes.LOCAL_GQA_CASES["a"]
+        q16, k16, v16 = (torch.from_numpy(x).half() for x in recipes.local_gqa_inputs("a"))
+        res = torch.empty_like(q16)
+        lse = torch.empty((b, hq, qf * h * w), dtype=torch.float32)
+        fl._forward[(qf * triton.cdiv(h, 4), triton.cdiv(w, 16), b * hq)](
+            q16, k16, v16, res, lse, h, w, hq, hk, d, (win[0],) * (tw * grp), (win[1],) * (tw * grp),
+            min(triton.next_power_of_2(win[1] + 15), triton.next_power_of_2(w)), qf, nf, nf - qf, tw, grp,
+            4, 16, 64, 64)
+        out["fd_a_triton_fp16"] = res.numpy()          # fp16 values, stored as fp16
+
+
 def main():
     args = [a for a in sys.argv[1:] if not a.startswith("--")]
     ref = args[0] if args else os.environ.get("RECAVSR_REFERENCE")
     if not ref:
         raise SystemExit("usage: make_golden.py <reference checkout> [--session]  (or set RECAVSR_REFERENCE)")
     _install_shims(ref)
+    if "--flashdecoder" in sys.argv:
+        out = {}
+        gen_flashdecoder(out)
+        np.savez_compressed(os.path.join(HERE, "flashdecoder_outputs.npz"), **out)
+        print("wrote", len(out), "flashdecoder arrays")
+        return
     if "--session" in sys.argv:
         # The session-glue fixtures live in their own file (the reference's
         # TransformerSession.step with a stand-in model; CPU only).

@@ -117,3 +117,23 @@ def session_inputs(channels=16, height=128, width=192, seed=32, rgb_frames=(21, 
         noise = rs.standard_normal((1, channels, frames, height // 16, width // 16)).astype(np.float32)
         steps.append((video, noise))
     return steps
+
+
+# FlashDecoder local GQA attention cases:
+# tag: (B, HQ, HK, D, height, width, window, group_size, temporal_window, QF, NF)
+LOCAL_GQA_CASES = {
+    "a": (1, 8, 2, 64, 6, 20, (4, 8), 4, 2, 4, 8),
+    "b": (1, 4, 1, 64, 9, 7, (6, 4), 1, 2, 1, 3),
+    "c": (2, 4, 4, 32, 5, 6, (10, 12), 2, 1, 2, 6),
+}
+
+
+def local_gqa_inputs(tag, seed=41):
+    """q [B, HQ, QF*n, D], k / v [B, HK, NF*n, D], N(0, 1) fp32, for one case."""
+    b, hq, hk, d, h, w, _, _, _, qf, nf = LOCAL_GQA_CASES[tag]
+    rs = np.random.RandomState(seed + ord(tag))
+    n = h * w
+    q = rs.standard_normal((b, hq, qf * n, d)).astype(np.float32)
+    k = rs.standard_normal((b, hk, nf * n, d)).astype(np.float32)
+    v = rs.standard_normal((b, hk, nf * n, d)).astype(np.float32)
+    return q, k, v
