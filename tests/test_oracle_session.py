@@ -127,3 +127,18 @@ def test_layer_loop_matches_reference(sgold):
         rel = np.linalg.norm(got - ref) / np.linalg.norm(ref)
         assert rel < 0.06 and _rel(got, ref) < 0.15, (i, rel, _rel(got, ref))
         start += frames
+
+
+def test_lq_projector_streaming_equals_full_sequence():
+    """LQ4xProj.forward_streaming projects "a consecutive RGB chunk exactly as
+    full-sequence forward" (lq_proj.py:231-236): the prefix / body chunks
+    21, 8, 8 streamed equal the 37 frames in one chunk (outputs 6 + 2 + 2)."""
+    p = recipes.session_params()
+    steps = recipes.session_inputs()
+    video = np.concatenate([s[0][0] for s in steps], axis=1)
+    state = osess.new_lq_state()
+    streamed = np.concatenate([osess.lq_project_stream(s[0][0], state, p) for s in steps])
+    full = osess.lq_project_stream(video, osess.new_lq_state(), p)
+    assert streamed.shape == full.shape == (10 * 4 * 6, 256)
+    # identical windows; float64 sums may differ in the last bit, flipping a rare bf16 rounding
+    assert np.mean(streamed == full) > 0.99 and _rel(streamed, full) < 1e-2
