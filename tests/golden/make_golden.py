@@ -4,6 +4,7 @@ Run where a checkout of the reference exists:
     python tests/golden/make_golden.py <reference checkout>            # reference_outputs.npz, router.json
     python tests/golden/make_golden.py <reference checkout> --session  # session_outputs.npz
     TRITON_INTERPRET=1 python tests/golden/make_golden.py <reference checkout> --flashdecoder
+    python tests/golden/make_golden.py <reference checkout> --fullsize  # fullsize_hashes.json
                                                                         # flashdecoder_outputs.npz
 (or set RECAVSR_REFERENCE). Under TRITON_INTERPRET=1 it also records the
 reference's Triton kernel on windowed cases. The --session fixtures come from
@@ -482,12 +483,54 @@ def gen_flashdecoder(out):
         out["fd_a_triton_fp16"] = res.numpy()          # fp16 values, stored as fp16
 
 
+FULLSIZE_SHAPES = ((7040, 14336), (7040, 3072))     # cfg3's largest activations
+
+
+def gen_fullsize():
+    """SHA-256 of the reference's NVFP4 codes / swizzled scales
+    (runtime/nvfp4.py:49-68) and FP8 codes + scale (runtime/fp8.py:41-42) of
+    the cfg3 activations at full size (recipes.cfg3_activation_large): a
+    size-independent pin of bit-exactness where the arrays are too large to
+    keep as fixtures."""
+    import hashlib
+    from recavsr_infer.runtime import fp8, nvfp4
+    sha = lambda a: hashlib.sha256(np.ascontiguousarray(a).tobytes()).hexdigest()
+    result = {}
+    for m, k in FULLSIZE_SHAPES:
+        x = t16(recipes.cfg3_activation_large(m, k))
+        packed, scales = nvfp4.quantize(x)
+        result[f"nvfp4_{m}x{k}"] = {"codes": sha(packed.numpy()), "scales": sha(scales.numpy())}
+        layer = object.__new__(fp8.FP8Linear)
+        nn.Module.__init__(layer)
+        captured = {}
+
+        def fake_scaled_mm(a, b, scale_a, scale_b, bias, out_dtype, use_fast_accum):
+            captured["q"], captured["scale"] = a, scale_a
+            return torch.zeros(a.shape[0], b.shape[1], dtype=out_dtype)
+        layer.in_features, layer.out_features = k, 16
+        layer.weight_packed = torch.zeros(16, k, dtype=torch.float8_e4m3fn).view(torch.bfloat16)
+        layer.bias, layer.weight_scale = None, torch.tensor(1.0)
+        real, torch._scaled_mm = torch._scaled_mm, fake_scaled_mm
+        try:
+            layer.forward(x)
+        finally:
+            torch._scaled_mm = real
+        result[f"fp8_{m}x{k}"] = {"codes": sha(captured["q"].view(torch.uint8).numpy()),
+                                  "scale": float(captured["scale"].item())}
+    return result
+
+
 def main():
     args = [a for a in sys.argv[1:] if not a.startswith("--")]
     ref = args[0] if args else os.environ.get("RECAVSR_REFERENCE")
     if not ref:
         raise SystemExit("usage: make_golden.py <reference checkout> [--session]  (or set RECAVSR_REFERENCE)")
     _install_shims(ref)
+    if "--fullsize" in sys.argv:
+        with open(os.path.join(HERE, "fullsize_hashes.json"), "w") as f:
+            json.dump(gen_fullsize(), f, indent=1)
+        print("wrote fullsize_hashes.json")
+        return
     if "--flashdecoder" in sys.argv:
         out = {}
         gen_flashdecoder(out)

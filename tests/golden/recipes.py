@@ -137,3 +137,20 @@ def local_gqa_inputs(tag, seed=41):
     k = rs.standard_normal((b, hk, nf * n, d)).astype(np.float32)
     v = rs.standard_normal((b, hk, nf * n, d)).astype(np.float32)
     return q, k, v
+
+
+def cfg3_activation_large(m: int, k: int, seed: int = 2) -> np.ndarray:
+    """cfg3 activation for the largest shapes (same distribution as
+    cfg3_activation: N(0,1), 0.1 % of the entries x20, bf16 values) drawn with
+    numpy's Generator, whose sampling without replacement stays fast at 1e8
+    entries."""
+    rng = np.random.default_rng(seed)
+    x = rng.standard_normal((m, k), dtype=np.float32)
+    idx = rng.choice(m * k, size=max(1, (m * k) // 1000), replace=False)
+    x.reshape(-1)[idx] *= 20.0
+    # bf16_round's ties-to-even in place on the 32-bit patterns: every value
+    # is finite and far below overflow, so the 32-bit sum cannot wrap
+    u = x.view(np.uint32)
+    u += np.uint32(0x7FFF) + ((u >> np.uint32(16)) & np.uint32(1))
+    u &= np.uint32(0xFFFF0000)
+    return x

@@ -198,3 +198,22 @@ def test_nvfp4_quantize_every_bf16_amax():
     rc, rs = onv.quantize(x)
     np.testing.assert_array_equal(scales.cpu().numpy(), rs)
     np.testing.assert_array_equal(codes.cpu().numpy(), rc)
+
+
+@pytest.mark.parametrize("m,k", [(7040, 14336), (7040, 3072)])
+def test_quantizers_bit_exact_at_full_size(m, k):
+    """The device NVFP4 and FP8 quantizers on cfg3's full-size activations
+    produce the reference's exact bytes: SHA-256 of codes and swizzled scales
+    (and the FP8 scale) against tests/golden/fullsize_hashes.json, recorded
+    from the reference's own quantizers."""
+    from recavsr_b200.runtime import fp8, nvfp4
+    from tests.test_oracle_fullsize import fullsize_hashes, sha
+    ref = fullsize_hashes()
+    x = torch.from_numpy(recipes.cfg3_activation_large(m, k)).cuda().bfloat16()   # bf16 values: exact
+    codes, scales = nvfp4.quantize(x)
+    assert sha(codes.cpu().numpy()) == ref[f"nvfp4_{m}x{k}"]["codes"]
+    assert sha(scales.cpu().numpy()) == ref[f"nvfp4_{m}x{k}"]["scales"]
+    q, scale = fp8.quantize(x)
+    assert np.float32(scale.item()) == np.float32(ref[f"fp8_{m}x{k}"]["scale"])
+    assert sha(q.cpu().numpy()) == ref[f"fp8_{m}x{k}"]["codes"]
+    assert_no_device_error()
