@@ -237,3 +237,32 @@ def test_bf16_gemm_grouped_tile_raster():
     # a misplaced tile would be off by O(1) in some 128 x 128 block
     tiles = torch.nn.functional.pad(err, (0, 0, 0, 2048 - m)).reshape(16, 128, 16, 128).amax((1, 3))
     assert float(tiles.max()) < TOL * float(ref.abs().max()), tiles
+
+
+def test_nvfp4_gemm_grouped_raster_matches_row_chunks():
+    """cfg3's 7040 x 3072 x 14336 NVFP4 GEMM has 72 MB of operands, so it runs in
+    the grouped tile order (55 row blocks: four groups of 12 and one of 7); the
+    same GEMM as four 1760-row chunks (35 MB each) runs row-fastest. Neither
+    splits K (rc_nvfp4_gemm), so every output element is accumulated the same
+    way and the two must agree bit for bit."""
+    from recavsr_b200 import _lib
+    from recavsr_b200.runtime import nvfp4
+    g = torch.Generator(device="cuda")
+    g.manual_seed(7)
+    m, n, k = 7040, 3072, 14336
+    a = torch.randn(m, k, generator=g, device="cuda").bfloat16()
+    w = (torch.randn(n, k, generator=g, device="cuda") * 0.02).bfloat16()
+    bias = (torch.randn(n, generator=g, device="cuda") * 0.1).bfloat16()
+    wc, wsf = nvfp4.quantize(w)
+
+    def run(rows):
+        ac, asf = nvfp4.quantize(rows)
+        out = torch.empty(rows.shape[0], n, dtype=torch.bfloat16, device="cuda")
+        _lib.call("rc_nvfp4_gemm", ac.data_ptr(), asf.data_ptr(), wc.data_ptr(), wsf.data_ptr(),
+                  bias.data_ptr(), rows.shape[0], n, k, 1.0, _lib.EPI_BIAS, out.data_ptr(), n, None,
+                  None, None, 1.0, _lib.stream())
+        return out
+    full = run(a)
+    chunks = torch.cat([run(a[r:r + 1760]) for r in range(0, m, 1760)])
+    assert_no_device_error()
+    assert torch.equal(full, chunks)
