@@ -177,3 +177,52 @@ def test_head_shard_exchange_over_gloo_ranks(world):
     assert sorted(got) == list(range(world))
     for rank, err in got.items():
         assert err is None, f"rank {rank}:\n{err}"
+
+
+def _failing_rank_main(rank, world, port, results):
+    """Rank 1 leaves before the exchange (a host-side failure); rank 0's
+    all-to-all must end with an error, not hang."""
+    import time
+
+    import torch.distributed as dist
+    from recavsr_b200.runtime.head_shard import AllToAll
+    os.environ["MASTER_ADDR"], os.environ["MASTER_PORT"] = "127.0.0.1", str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=5))
+    if rank == 1:
+        results.put((rank, "left"))
+        return                                   # never joins the collective
+    send = torch.zeros(world, 3, 4, 8)
+    recv = torch.empty_like(send)
+    t0 = time.monotonic()
+    try:
+        AllToAll()(recv, send)
+        results.put((rank, "no error"))
+    except Exception as e:                      # noqa: BLE001 - any collective error is the expected outcome
+        results.put((rank, f"error after {time.monotonic() - t0:.1f} s: {type(e).__name__}"))
+    finally:
+        try:
+            dist.destroy_process_group()
+        except Exception:                        # noqa: BLE001
+            pass
+
+
+def test_head_shard_exchange_fails_cleanly_when_a_rank_leaves():
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    results = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_failing_rank_main, args=(r, 2, port, results)) for r in range(2)]
+    for p in procs:
+        p.start()
+    got = {}
+    try:
+        for _ in range(2):
+            rank, msg = results.get(timeout=120)
+            got[rank] = msg
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+    assert got[1] == "left"
+    assert got[0].startswith("error after"), got[0]
