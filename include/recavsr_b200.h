@@ -95,6 +95,16 @@ int rc_ln_modulate_quant(const void* x, long long ldx, int M, int N, const void*
                          void* out, long long ldo, uint8_t* codes, uint8_t* scales_swizzled,
                          float global_scale, rc_stream_t stream);
 
+/* Replaces recavsr_infer/kernels/native_norm.py:7-17 (`native_layer_norm`,
+ * rms = 0) and :25-28 (`native_rms_norm`, rms = 1) for any floating input:
+ * the norm of each row of x [M, N] (row stride ldx) in fp32 with the fp32
+ * affine weight / bias (nullable; bias unused when rms = 1), written in x's
+ * type into out (row stride ldo). dtype: 0 fp32, 1 bf16, 2 fp16. The
+ * reference's only caller passes fp32 rows (runtime/transformer.py:91,121,130). */
+int rc_layer_norm(const void* x, int dtype, long long ldx, int M, int N, const float* weight,
+                  const float* bias, float eps, int rms, void* out, long long ldo,
+                  rc_stream_t stream);
+
 /* RMSNorm across heads (+ spatial rotary) of up to two tensors:
  * recavsr_infer/runtime/transformer.py:99-100,122 (norm_q/norm_k, PreparedBlock.spatial),
  * kernels/native_norm.py:25-28, runtime/rope.py:23-30. */

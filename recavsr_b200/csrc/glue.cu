@@ -12,6 +12,7 @@
 //   RMSNorm: bf16(x * rsqrt(mean(x^2) + eps) * w) with one rounding;
 //   rotary: (e*c - o*s, e*s + o*c) in fp32, then bf16 (runtime/rope.py:23-30).
 #include "common.cuh"
+#include <cuda_fp16.h>
 
 namespace {
 
@@ -436,6 +437,69 @@ __global__ void __launch_bounds__(kCommitThreads) kv_commit_planned_kernel(Commi
   }
 }
 
+// Row norm of any floating input type, result in the same type: the drop-in
+// recavsr_math::layer_norm / rms_norm contract (kernels/native_norm.py:7-28
+// returns .to(x.dtype) of an fp32 computation; PreparedBlock.layer_norm passes
+// fp32 rows, runtime/transformer.py:91,121,130). One CTA per row; the row is
+// read three times (sum, centred squares, output), the re-reads hit L1.
+// dtype: 0 fp32, 1 bf16, 2 fp16. weight / bias: fp32 (nullable).
+constexpr int kNormThreads = 256;
+
+__device__ __forceinline__ float load_any(const void* p, size_t i, int dtype) {
+  if (dtype == 0) return rc::ld_in(reinterpret_cast<const float*>(p) + i);
+  const unsigned short h = rc::ld_in(reinterpret_cast<const unsigned short*>(p) + i);
+  if (dtype == 1) return __uint_as_float((uint32_t)h << 16);
+  return __half2float(__ushort_as_half(h));
+}
+__device__ __forceinline__ void store_any(void* p, size_t i, int dtype, float v) {
+  if (dtype == 0) reinterpret_cast<float*>(p)[i] = v;
+  else if (dtype == 1) reinterpret_cast<unsigned short*>(p)[i] = rc::bf16_bits(v);
+  else reinterpret_cast<__half*>(p)[i] = __float2half_rn(v);
+}
+__device__ __forceinline__ float block_sum(float v, float* red) {
+  v = warp_sum(v);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  float t = 0.f;
+#pragma unroll
+  for (int i = 0; i < kNormThreads / 32; ++i) t += red[i];
+  __syncthreads();
+  return t;
+}
+
+struct NormArgs {
+  const void* x; long long ldx; int dtype;
+  const float* weight; const float* bias; float eps; int rms;
+  void* out; long long ldo;
+  int M, N;
+};
+
+__global__ void __launch_bounds__(kNormThreads) row_norm_kernel(NormArgs a) {
+  __shared__ float red[kNormThreads / 32];
+  rc::pdl_trigger();
+  rc::pdl_wait();
+  const size_t row = blockIdx.x;
+  const size_t xo = row * (size_t)a.ldx, oo = row * (size_t)a.ldo;
+  float mean = 0.f;
+  if (!a.rms) {
+    float s = 0.f;
+    for (int i = threadIdx.x; i < a.N; i += kNormThreads) s += load_any(a.x, xo + i, a.dtype);
+    mean = __fdiv_rn(block_sum(s, red), (float)a.N);
+  }
+  float m2 = 0.f;
+  for (int i = threadIdx.x; i < a.N; i += kNormThreads) {
+    const float d = load_any(a.x, xo + i, a.dtype) - mean;
+    m2 = fmaf(d, d, m2);
+  }
+  const float rstd = rsqrtf(__fdiv_rn(block_sum(m2, red), (float)a.N) + a.eps);
+  for (int i = threadIdx.x; i < a.N; i += kNormThreads) {
+    float y = __fmul_rn(__fsub_rn(load_any(a.x, xo + i, a.dtype), mean), rstd);
+    if (a.weight) y = __fmul_rn(y, rc::ld_in(a.weight + i));
+    if (a.bias) y = __fadd_rn(y, rc::ld_in(a.bias + i));
+    store_any(a.out, oo + i, a.dtype, y);
+  }
+}
+
 int grid_for(long long work, int threads) {
   long long b = (work + threads - 1) / threads;
   return (int)(b < 1 ? 1 : (b > 148LL * 16 ? 148LL * 16 : b));
@@ -483,6 +547,25 @@ int rc_ln_modulate_quant(const void* x, long long ldx, int M, int N, const void*
   const K kern = table[ch - 1][(aff ? 1 : 0) + (mod ? 2 : 0)];
   return rc::check_launch(rc::launch_pdl(kern, dim3(M + ((codes && M % 128) ? 1 : 0)), dim3(kRowThreads), 0, stream, a),
                           "rc_ln_modulate_quant");
+}
+
+// LayerNorm (rms = 0) or RMSNorm (rms = 1) over the last dim N of x [M, N]
+// in fp32 with fp32 affine weight / bias (nullable; bias ignored for RMS),
+// output in x's type (dtype 0 fp32, 1 bf16, 2 fp16).
+int rc_layer_norm(const void* x, int dtype, long long ldx, int M, int N, const float* weight,
+                  const float* bias, float eps, int rms, void* out, long long ldo,
+                  cudaStream_t stream) {
+  if (dtype < 0 || dtype > 2 || M < 0 || N <= 0 || ldx < N || ldo < N)
+    return rc::set_error(RC_ERR_ARG, "rc_layer_norm: bad shape or dtype (dtype=%d M=%d N=%d)", dtype, M, N);
+  if (!x || !out) return rc::set_error(RC_ERR_ARG, "rc_layer_norm: missing pointer");
+  const int es = dtype == 0 ? 4 : 2;
+  if (reinterpret_cast<uintptr_t>(x) % es || reinterpret_cast<uintptr_t>(out) % es ||
+      (weight && reinterpret_cast<uintptr_t>(weight) % 4) || (bias && reinterpret_cast<uintptr_t>(bias) % 4))
+    return rc::set_error(RC_ERR_ARG, "rc_layer_norm: misaligned pointer");
+  if (M == 0) return RC_OK;
+  NormArgs a{x, ldx, dtype, weight, rms ? nullptr : bias, eps, rms, out, ldo, M, N};
+  return rc::check_launch(rc::launch_pdl(row_norm_kernel, dim3(M), dim3(kNormThreads), 0, stream, a),
+                          "rc_layer_norm");
 }
 
 // RMSNorm across the full row (eps, affine bf16 weight) of up to two tensors

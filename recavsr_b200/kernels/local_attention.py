@@ -10,69 +10,9 @@ per-query windows of the Triton kernel.
 """
 from __future__ import annotations
 
-import ctypes as C
-
 import torch
 
-from .. import _lib
-
-
-def _check(q, ck, cv, pk, pv, slots, past_positions, query_positions, cos, sin, height, width,
-           window_h, window_w):
-    if q.device.type != "cuda" or q.dtype != torch.bfloat16:
-        raise ValueError("The B200 attention kernel requires CUDA BF16 tensors.")
-    if q.shape != ck.shape or q.shape != cv.shape or pk.shape != pv.shape:
-        raise ValueError("Q/current KV and past KV shapes disagree.")
-    span = height * width
-    if height <= 0 or width <= 0 or q.shape[1] % span:
-        raise ValueError("Invalid token geometry.")
-    frames = q.shape[1] // span
-    if q.shape[-1] != 128:
-        raise ValueError("The B200 attention kernel supports head_dim 128.")
-    if slots.numel() * span != pk.shape[1] or past_positions.shape != slots.shape:
-        raise ValueError("Cache slot metadata mismatch.")
-    if query_positions.numel() != frames or cos.shape != sin.shape:
-        raise ValueError("Rolling RoPE metadata mismatch.")
-    if min(window_h, window_w) <= 0:
-        raise ValueError("Spatial windows must be positive.")
-    if any(x.stride(-1) != 1 for x in (q, ck, cv, pk, pv) if x.numel()):
-        raise ValueError("Head dimensions must be contiguous.")
-    return frames
-
-
-def _i32(t: torch.Tensor, device) -> torch.Tensor:
-    if t.dtype == torch.int32 and t.device == device and t.is_contiguous():
-        return t
-    return t.to(device=device, dtype=torch.int32).contiguous()
-
-
-def routed_attention(q, ck, cv, pk, pv, slots, past_positions, query_positions, cos, sin,
-                     height, width, window_h, window_w, *, out=None):
-    """Shared launcher: out [B, QT*H*W, heads, d] bf16 (contiguous unless `out` given)."""
-    frames = _check(q, ck, cv, pk, pv, slots, past_positions, query_positions, cos, sin,
-                    height, width, window_h, window_w)
-    b, tokens, heads, d = q.shape
-    cap = slots.numel()
-    dev = q.device
-    if out is None:
-        out = torch.empty((b, tokens, heads, d), dtype=q.dtype, device=dev)
-    ws_bytes = _lib.library().rc_paired_attention_workspace(b, frames, cap, height, width, heads, d)
-    ws = torch.empty((ws_bytes,), dtype=torch.uint8, device=dev)
-    strides = []
-    for t in (q, ck, cv, pk, pv):
-        strides += [t.stride(0), t.stride(1), t.stride(2)]
-    st = (C.c_longlong * 15)(*strides)
-    si = _i32(slots, dev) if cap else None
-    pp = _i32(past_positions, dev) if cap else None
-    qp = _i32(query_positions, dev)
-    cc = cos.to(device=dev, dtype=torch.float32).contiguous()
-    ss = sin.to(device=dev, dtype=torch.float32).contiguous()
-    _lib.call("rc_paired_attention", q.data_ptr(), ck.data_ptr(), cv.data_ptr(),
-              pk.data_ptr() if cap else None, pv.data_ptr() if cap else None, st,
-              _lib.ptr(si), _lib.ptr(pp), qp.data_ptr(), cc.data_ptr(), ss.data_ptr(),
-              b, frames, cap, height, width, heads, d, cos.shape[-1] * 2, window_h, window_w,
-              ws.data_ptr(), ws_bytes, out.data_ptr(), out.stride(1), None, None, _lib.stream(dev))
-    return out
+from ..runtime.ops import routed_attention  # noqa: F401  (re-exported)
 
 
 @torch.library.custom_op("recavsr_local::paired", mutates_args=())
@@ -115,8 +55,24 @@ def _fake(q, ck, cv, pk, pv, slots, past_positions, query_positions, cos, sin, h
 def sdpa_attention(q, ck, cv, pk, pv, slots, past_positions, query_positions, cos, sin,
                    height, width, window_h, window_w):
     """local_attention.py:286-325: full-spatial attention with the router's sparse
-    temporal visibility (the same kernel with a window covering the grid)."""
+    temporal visibility (the same kernel with a window covering the grid). Runs
+    as the custom op recavsr_b200::sdpa_routed, so a torch.compile(fullgraph=True)
+    caller traces through it as it traces the reference's torch formulation."""
     if window_h < height or window_w < width:
         raise ValueError("SDPA requires a window covering the full spatial grid.")
+    return _sdpa_routed(q, ck, cv, pk, pv, slots, past_positions, query_positions, cos, sin,
+                        height, width)
+
+
+@torch.library.custom_op("recavsr_b200::sdpa_routed", mutates_args=())
+def _sdpa_routed(q: torch.Tensor, ck: torch.Tensor, cv: torch.Tensor, pk: torch.Tensor,
+                 pv: torch.Tensor, slots: torch.Tensor, past_positions: torch.Tensor,
+                 query_positions: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, height: int,
+                 width: int) -> torch.Tensor:
     return routed_attention(q, ck, cv, pk, pv, slots, past_positions, query_positions, cos, sin,
                             height, width, height, width)
+
+
+@_sdpa_routed.register_fake
+def _sdpa_fake(q, ck, cv, pk, pv, slots, past_positions, query_positions, cos, sin, height, width):
+    return torch.empty_like(q, memory_format=torch.contiguous_format)

@@ -26,7 +26,7 @@ import ctypes as C
 import torch
 
 from . import _lib
-from .runtime.nvfp4 import quantize, scale_numel
+from .runtime.ops import quantize, scale_numel
 
 M, DIM, FFN, HEADS, HD, H, W = 1760, 3072, 14336, 24, 128, 22, 40
 
@@ -59,7 +59,7 @@ def _attention(planes=4, h=H, w=W, window=None):
     """Routed attention of a 2-frame query block over `planes` routed planes
     plus the 2 current frames; window None = the grid (the sdpa path), else
     (wh, ww) local windows. FLOPs count visible keys only."""
-    from .kernels.local_attention import routed_attention
+    from .runtime.ops import routed_attention
     from .runtime.block import rope_tables
     g = torch.Generator(device="cuda")
     g.manual_seed(0)
@@ -350,7 +350,7 @@ def attention_sweep(reps=5):
     (22 x 40), 2-frame query block (1760 queries), layer i attends to
     [0, 1, 2, 4, 8][i % 5] routed planes of an 8-plane ring plus the 2 current
     frames; FLOPs count visible keys only: 4 d heads Nq T sum(scope + 2)."""
-    from .kernels.local_attention import routed_attention
+    from .runtime.ops import routed_attention
     from .runtime.block import rope_tables
     g = torch.Generator(device="cuda")
     g.manual_seed(1)

@@ -32,8 +32,8 @@ import torch
 from .. import _lib
 from .cache import FixedKVCache
 from .constants import DEFAULT_SPATIAL_WINDOW
-from .nvfp4 import quantize as nvfp4_quantize
-from .nvfp4 import scale_numel
+from .ops import quantize as nvfp4_quantize
+from .ops import scale_numel
 
 _EPS = 1e-6
 
@@ -49,7 +49,7 @@ def _bf16_linear(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor | None) -> to
 
 
 def _rms(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
-    from ..kernels.native_norm import rms_norm_rope
+    from .ops import rms_norm_rope
     return rms_norm_rope(x, w, _EPS)
 
 
@@ -74,6 +74,16 @@ def block_weights_from_module(block, conditioning) -> dict:
         "heads": a1.heads,
     }
     return {k: (v.detach() if isinstance(v, torch.Tensor) else v) for k, v in w.items()}
+
+
+@dataclass
+class HostStep:
+    """Events of one step_host call: `input_consumed` completes once the
+    pinned input buffer has been copied to the device (the caller may then
+    refill it), `output_ready` once the result has reached the pinned output
+    buffer. Wait with .synchronize() or test with .query()."""
+    input_consumed: torch.cuda.Event
+    output_ready: torch.cuda.Event
 
 
 @dataclass
@@ -418,12 +428,18 @@ class LayerStack:
         hidden.copy_(self._static[n])
         return hidden
 
-    def step_host(self, host_in: torch.Tensor, host_out: torch.Tensor, frames: int) -> None:
+    def step_host(self, host_in: torch.Tensor, host_out: torch.Tensor, frames: int) -> "HostStep":
         """One body block from pinned host memory to pinned host memory through
         the captured graph: the host-to-device copy of this block's hidden state
         and the device-to-host copy of its result run on a copy stream, so they
         overlap the previous / next block's layer loop (double-buffered staging).
-        Asynchronous: call sync_host() before reading host_out."""
+
+        Asynchronous: the call returns before either copy has run. The returned
+        HostStep says when the caller may touch the buffers again: host_in must
+        not be rewritten before `input_consumed` has completed (the copy reads
+        it on the device's schedule, possibly after later step_host calls were
+        issued), and host_out holds the result once `output_ready` has
+        completed. sync_host() waits for every copy issued so far."""
         n = host_in.shape[0]
         if n != frames * self.span or host_out.shape != host_in.shape:
             raise ValueError("host_in / host_out must hold `frames` complete planes.")
@@ -444,10 +460,12 @@ class LayerStack:
             self._copy_stream = torch.cuda.Stream(self.device)
         k = io["k"] & 1
         comp, cs = torch.cuda.current_stream(self.device), self._copy_stream
+        handle = HostStep(torch.cuda.Event(), torch.cuda.Event())
         with torch.cuda.stream(cs):
             cs.wait_event(io["consumed"][k])          # the block two steps back has read this buffer
             io["in"][k].copy_(host_in, non_blocking=True)
             io["in_ready"][k].record(cs)
+            handle.input_consumed.record(cs)
         self._plan(frames)
         self._upload_route()
         comp.wait_event(io["in_ready"][k])
@@ -461,7 +479,9 @@ class LayerStack:
             cs.wait_event(io["done"][k])
             host_out.copy_(io["out"][k], non_blocking=True)
             io["drained"][k].record(cs)
+            handle.output_ready.record(cs)
         io["k"] += 1
+        return handle
 
     def _upload_route(self) -> None:
         """Host-to-device copy of the table _plan just filled, on the current stream."""
@@ -473,9 +493,12 @@ class LayerStack:
         self._route_i += 1
 
     def sync_host(self) -> None:
-        """Make the current stream wait for every step_host copy issued so far."""
+        """Block the host until every step_host copy issued so far has run (every
+        host_in was read, every host_out written); the current stream also
+        waits for them."""
         if self._copy_stream is not None:
             torch.cuda.current_stream(self.device).wait_stream(self._copy_stream)
+            self._copy_stream.synchronize()
 
     def capture(self, n: int, frames: int):
         """Capture one block of the layer loop for a token count n (after at

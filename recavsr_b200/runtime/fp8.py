@@ -15,7 +15,13 @@ FP8_MAX = 448.0
 
 
 def quantize(matrix: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
-    """fp8.py:41-42 on the device: (e4m3 bytes [M, K] as uint8, fp32 scale [] tensor)."""
+    """fp8.py:41-42 on the device: (e4m3 bytes [M, K] as uint8, fp32 scale [] tensor);
+    the custom op recavsr_b200::fp8_quantize (opaque under torch.compile)."""
+    return _quantize(matrix)
+
+
+@torch.library.custom_op("recavsr_b200::fp8_quantize", mutates_args=())
+def _quantize(matrix: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
     _lib.require_cuda(matrix, "fp8.quantize")
     if matrix.dim() != 2 or matrix.dtype != torch.bfloat16:
         raise ValueError("fp8.quantize expects a 2-D bf16 matrix.")
@@ -28,6 +34,31 @@ def quantize(matrix: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
     _lib.call("rc_fp8_quantize", matrix.data_ptr(), m, k, matrix.stride(0), scratch.data_ptr(),
               scale.data_ptr(), q.data_ptr(), _lib.stream(matrix.device))
     return q, scale
+
+
+@_quantize.register_fake
+def _quantize_fake(matrix):
+    return (matrix.new_empty(matrix.shape, dtype=torch.uint8),
+            matrix.new_empty((), dtype=torch.float32))
+
+
+@torch.library.custom_op("recavsr_b200::fp8_mm", mutates_args=())
+def fp8_mm(q: torch.Tensor, scale: torch.Tensor, weight: torch.Tensor, weight_scale: torch.Tensor,
+           bias: torch.Tensor | None) -> torch.Tensor:
+    """The torch._scaled_mm call of fp8.py:44-47 (e4m3 A [M, K] . B [N, K]^T,
+    per-tensor device scales, bias, bf16 out) on the tcgen05 kind::f8f6f4 GEMM."""
+    m, k = q.shape
+    n = weight.shape[0]
+    out = torch.empty((m, n), dtype=torch.bfloat16, device=q.device)
+    _lib.call("rc_fp8_gemm", q.data_ptr(), scale.data_ptr(), weight.data_ptr(), weight_scale.data_ptr(),
+              _lib.ptr(bias), m, n, k, 1.0, _lib.EPI_BIAS, out.data_ptr(), out.stride(0), None,
+              _lib.stream(q.device))
+    return out
+
+
+@fp8_mm.register_fake
+def _fp8_mm_fake(q, scale, weight, weight_scale, bias):
+    return q.new_empty((q.shape[0], weight.shape[0]), dtype=torch.bfloat16)
 
 
 class FP8Linear(nn.Module):
@@ -47,14 +78,11 @@ class FP8Linear(nn.Module):
         self.register_buffer("weight_scale", scale)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if x.dtype != torch.bfloat16:
+            raise ValueError("FP8 linears on B200 take BF16 inputs and produce BF16 outputs.")
         matrix = x.reshape(-1, self.in_features)
         q, scale = quantize(matrix)
-        w = self.weight_packed.view(torch.uint8)
-        out = torch.empty((matrix.shape[0], self.out_features), dtype=torch.bfloat16, device=x.device)
-        _lib.call("rc_fp8_gemm", q.data_ptr(), scale.data_ptr(), w.data_ptr(),
-                  self.weight_scale.data_ptr(), _lib.ptr(self.bias), matrix.shape[0],
-                  self.out_features, self.in_features, 1.0, _lib.EPI_BIAS, out.data_ptr(),
-                  out.stride(0), None, _lib.stream(x.device))
+        out = fp8_mm(q, scale, self.weight_packed.view(torch.uint8), self.weight_scale, self.bias)
         return out.reshape(*x.shape[:-1], self.out_features)
 
 

@@ -12,6 +12,7 @@ import torch
 from torch import nn
 
 from .. import _lib
+from .ops import gemm, quantize, scale_numel, split_workspace  # noqa: F401  (re-exported)
 
 
 def validate_support(device: torch.device) -> None:
@@ -21,64 +22,6 @@ def validate_support(device: torch.device) -> None:
         raise RuntimeError("NVFP4 DiT requires a CUDA device.")
     if torch.cuda.get_device_capability(device) < (10, 0):
         raise ValueError("NVFP4 DiT requires an NVIDIA Blackwell GPU or later.")
-
-
-def scale_numel(m: int, k: int) -> int:
-    return (m + 127) // 128 * 128 * (((k // 16) + 3) // 4 * 4)
-
-
-def quantize(matrix: torch.Tensor, global_scale: float = 1.0) -> tuple[torch.Tensor, torch.Tensor]:
-    """nvfp4.py:49-68: (packed E2M1 u8 [M, K/2], swizzled E4M3 scales u8 flat).
-
-    global_scale = 1 is the reference formula bit for bit; another value
-    selects the per-tensor global-scale mode (the GEMM then needs
-    alpha = 1 / (g_a * g_b))."""
-    _lib.require_cuda(matrix, "nvfp4.quantize")
-    if matrix.dim() != 2 or matrix.dtype != torch.bfloat16:
-        raise ValueError("nvfp4.quantize expects a 2-D bf16 matrix.")
-    m, k = matrix.shape
-    if k % 16:
-        raise ValueError("NVFP4 rows must be a multiple of 16 elements.")
-    if matrix.stride(1) != 1 or (matrix.stride(0) * 2) % 16 or matrix.data_ptr() % 16:
-        matrix = matrix.contiguous()
-    packed = torch.empty((m, k // 2), dtype=torch.uint8, device=matrix.device)
-    scales = torch.empty((scale_numel(m, k),), dtype=torch.uint8, device=matrix.device)
-    _lib.call("rc_nvfp4_quantize", matrix.data_ptr(), m, k, matrix.stride(0), float(global_scale),
-              packed.data_ptr(), scales.data_ptr(), _lib.stream(matrix.device))
-    return packed, scales
-
-
-_SPLIT_WS: dict = {}
-
-
-def split_workspace(device: torch.device) -> torch.Tensor:
-    """The zero-filled split-K workspace of the NVFP4 GEMM, one per (device,
-    stream): calls sharing a workspace must be ordered on one stream."""
-    device = torch.device(device)
-    key = (device.index if device.index is not None else torch.cuda.current_device(), _lib.stream(device))
-    ws = _SPLIT_WS.get(key)
-    if ws is None:
-        ws = torch.zeros((_lib.library().rc_gemm_split_workspace(),), dtype=torch.uint8, device=device)
-        _SPLIT_WS[key] = ws
-    return ws
-
-
-def gemm(values, weights, scales, weight_scales, bias=None, *, alpha=1.0,
-         out: torch.Tensor | None = None) -> torch.Tensor:
-    """bf16 [M, N] = alpha * A . B^T + bias on the tcgen05 block-scaled path."""
-    a = values.view(torch.uint8)
-    b = weights.view(torch.uint8)
-    m, n, k = a.shape[0], b.shape[0], a.shape[1] * 2
-    if b.shape[1] * 2 != k:
-        raise ValueError("NVFP4 operand widths disagree.")
-    if out is None:
-        out = torch.empty((m, n), dtype=torch.bfloat16, device=a.device)
-    ws = split_workspace(a.device)
-    _lib.call("rc_nvfp4_gemm_ws", a.data_ptr(), scales.view(torch.uint8).data_ptr(), b.data_ptr(),
-              weight_scales.view(torch.uint8).data_ptr(), _lib.ptr(bias), m, n, k, float(alpha),
-              _lib.EPI_BIAS, out.data_ptr(), out.stride(0), None, None, None, 1.0,
-              ws.data_ptr(), ws.numel(), _lib.stream(a.device))
-    return out
 
 
 @torch.library.custom_op("recavsr_nvfp4::linear", mutates_args=())

@@ -29,7 +29,13 @@ def rotary_table(dim, size, *, device):
 
 
 def apply_rotary(x, cos, sin):
-    """rope.py:23-30 for x [..., span, heads, d] with cos/sin holding span*d values."""
+    """rope.py:23-30 for x [..., span, heads, d] with cos/sin holding span*d values
+    (custom op recavsr_b200::rotary, opaque under torch.compile)."""
+    return _rotary(x, cos, sin)
+
+
+@torch.library.custom_op("recavsr_b200::rotary", mutates_args=())
+def _rotary(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
     _lib.require_cuda(x, "apply_rotary")
     d, heads = x.shape[-1], x.shape[-2]
     span = cos.numel() // d
@@ -48,8 +54,20 @@ def apply_rotary(x, cos, sin):
     return out.reshape(x.shape)
 
 
+@_rotary.register_fake
+def _rotary_fake(x, cos, sin):
+    return torch.empty_like(x, memory_format=torch.contiguous_format)
+
+
 def apply_temporal(x, positions, cos, sin, *, span):
-    """rope.py:33-47: rotate the first 2*cos.shape[-1] dims of each plane by its position."""
+    """rope.py:33-47: rotate the first 2*cos.shape[-1] dims of each plane by its
+    position (custom op recavsr_b200::temporal, opaque under torch.compile)."""
+    return _temporal(x, positions, cos, sin, span)
+
+
+@torch.library.custom_op("recavsr_b200::temporal", mutates_args=())
+def _temporal(x: torch.Tensor, positions: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
+              span: int) -> torch.Tensor:
     _lib.require_cuda(x, "apply_temporal")
     if x.dtype != torch.bfloat16:
         raise ValueError("apply_temporal on B200 supports bf16 inputs.")
@@ -66,6 +84,11 @@ def apply_temporal(x, positions, cos, sin, *, span):
               pos.data_ptr(), cos.float().contiguous().data_ptr(), sin.float().contiguous().data_ptr(),
               b * tokens, span, heads, d, cos.shape[-1] * 2, _lib.stream(x.device))
     return out.reshape(x.shape)
+
+
+@_temporal.register_fake
+def _temporal_fake(x, positions, cos, sin, span):
+    return torch.empty_like(x, memory_format=torch.contiguous_format)
 
 
 class RollingRoPE:
