@@ -904,14 +904,8 @@ long long split_offset(long long planes_bytes) { return (planes_bytes + 255) / 2
 // Tail split of `units` equal units over the SMs (one CTA per SM at a time):
 // the units of the last, partial wave run as `split` pieces each, so that wave
 // ends about `split` times sooner. `max_tiles` bounds the key tiles of a unit.
-// RECAVSR_ATTN_SPLIT=n caps the pieces per unit (1 = no split).
 void plan_split(int units, int max_tiles, bool can_split, int& n_regular, int& split) {
-  static int cap = -1;
-  if (cap < 0) {
-    const char* e = getenv("RECAVSR_ATTN_SPLIT");
-    cap = e ? atoi(e) : kMaxSplit;
-    cap = cap < 1 ? 1 : (cap > kMaxSplit ? kMaxSplit : cap);
-  }
+  constexpr int cap = kMaxSplit;
   n_regular = units;
   split = 1;
   if (!can_split) return;
@@ -927,16 +921,11 @@ void plan_split(int units, int max_tiles, bool can_split, int& n_regular, int& s
   split = s;
 }
 
-int g_attr_set = 0;
+rc::SmemAttrFlags g_attr_flags = {};
 
 int ensure_smem_attr(const char* what) {
-  if (!g_attr_set) {
-    if (cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             SmemLayout::kAlloc) != cudaSuccess)
-      return rc::set_error(RC_ERR_CUDA, "%s: shared memory attribute", what);
-    g_attr_set = 1;
-  }
-  return RC_OK;
+  return rc::ensure_smem_attr(g_attr_flags, reinterpret_cast<const void*>(attention_kernel),
+                              SmemLayout::kAlloc, what);
 }
 
 // ---------------------------------------------------------------------------
@@ -948,7 +937,7 @@ int ensure_smem_attr(const char* what) {
 // cudaGetSymbolAddress once per device (with that device current) and cached.
 constexpr long long kStaticScratchBytes = 64LL << 20;
 static __device__ __align__(256) uint8_t g_attention_scratch[kStaticScratchBytes];
-constexpr int kMaxDevices = 64;
+using rc::kMaxDevices;
 void* g_scratch_addr[kMaxDevices] = {};   // per-device cache of the array's address
 std::mutex g_scratch_mu;
 

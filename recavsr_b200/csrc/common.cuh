@@ -51,6 +51,16 @@ int check_launch(const char* what);
 int check_launch(cudaError_t launched, const char* what);   // result of launch_pdl
 int sm_count();   // streaming multiprocessors of the current device (cached per device)
 
+// cudaFuncSetAttribute(MaxDynamicSharedMemorySize) applies to the current
+// device only, so each kernel keeps one flag per device. A flag is set after
+// the attribute call succeeded; two threads may both make the (idempotent)
+// call before either sets it.
+constexpr int kMaxDevices = 64;
+struct SmemAttrFlags {
+  volatile int set[kMaxDevices];
+};
+int ensure_smem_attr(SmemAttrFlags& flags, const void* func, int bytes, const char* what);
+
 // cuTensorMapEncodeTiled through the runtime's driver entry point (no -lcuda).
 // dims/strides: innermost first; strides are in bytes for dims 1..rank-1.
 int encode_tmap(CUtensorMap* map, CUtensorMapDataType dtype, int rank, void* base,

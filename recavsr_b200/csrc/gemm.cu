@@ -621,14 +621,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
 // partials costs about as much as 4-8 k-tiles of MMA, so every range keeps at
 // least 8 k-tiles (measured on M = 1760: the split gains 3% on ffn_down,
 // K = 14336, and loses 16% on o-proj, K = 3072, which therefore stays whole).
-// RECAVSR_GEMM_SPLIT=n caps the units per tile (1 = no split).
 void plan_split(int tiles, int sms, bool can_split, GemmParams& p) {
-  static int cap = -1;
-  if (cap < 0) {
-    const char* e = getenv("RECAVSR_GEMM_SPLIT");
-    cap = e ? atoi(e) : kMaxSplit;
-    cap = cap < 1 ? 1 : (cap > kMaxSplit ? kMaxSplit : cap);
-  }
+  constexpr int cap = kMaxSplit;
   p.n_regular = tiles;
   p.split = 1;
   const int tail = tiles % sms;
@@ -650,12 +644,9 @@ int launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, cu
            const char* what) {
   using S = Smem<KIND, BN, STAGES>;
   auto kern = gemm_kernel<KIND, BN, STAGES, EPI>;
-  static bool attr_set = false;
-  if (!attr_set) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kAlloc) != cudaSuccess)
-      return rc::set_error(RC_ERR_CUDA, "%s: cannot reserve %d bytes of shared memory", what, S::kAlloc);
-    attr_set = true;
-  }
+  static rc::SmemAttrFlags attr_flags = {};
+  if (const int st = rc::ensure_smem_attr(attr_flags, reinterpret_cast<const void*>(kern), S::kAlloc, what))
+    return st;
   const int tiles = p.m_blocks * p.n_blocks;
   const int sms = rc::sm_count();
   GemmParams q = p;
@@ -681,15 +672,8 @@ int dispatch_epi(int epi, const CUtensorMap& ta, const CUtensorMap& tb, const Ge
 // epilogue) move a third less operand data per FLOP than 128 x 128 tiles, but
 // the 128 x 128 tiles overlap each tile's epilogue with the next tile's
 // mainloop (double-buffered accumulator) and quantize better onto 148 SMs.
-// RECAVSR_GEMM_BN=128 / 256 forces one width.
 bool gemm_prefer_wide(int epi, int M, int N, int K) {
-  static int forced = -2;
-  if (forced == -2) {
-    const char* e = getenv("RECAVSR_GEMM_BN");
-    forced = e ? (atoi(e) == 256 ? 1 : (atoi(e) == 128 ? 0 : -1)) : -1;
-  }
   if (N % 256) return false;
-  if (forced >= 0) return forced == 1;
   // Measured on M = 1760 (same box, A/B): the 256-column tile wins only for
   // the wide GELU + NVFP4 GEMM (ffn_up, N = 14336: 45.9 vs 48.0 us), where
   // halving the MMA and scale-copy instructions per FLOP outweighs the

@@ -39,8 +39,21 @@ int check_launch(cudaError_t launched, const char* what) {
   return check_launch(what);
 }
 
+int ensure_smem_attr(SmemAttrFlags& flags, const void* func, int bytes, const char* what) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
+    return set_error(RC_ERR_CUDA, "%s: no usable current device", what);
+  if (flags.set[dev]) return RC_OK;
+  if (cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess) {
+    cudaGetLastError();
+    return set_error(RC_ERR_CUDA, "%s: cannot reserve %d bytes of shared memory on device %d", what, bytes, dev);
+  }
+  __sync_synchronize();
+  flags.set[dev] = 1;
+  return RC_OK;
+}
+
 int sm_count() {
-  constexpr int kMaxDevices = 64;
   static int cache[kMaxDevices] = {};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return 148;

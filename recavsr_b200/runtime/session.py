@@ -26,6 +26,7 @@ from dataclasses import dataclass
 import torch
 
 from .. import _lib
+from .block import HostStep
 from .constants import (BODY_LATENT_FRAMES, BODY_RGB_FRAMES, PREFIX_LATENT_FRAMES, PREFIX_RGB_FRAMES,
                         SPATIAL_TOKEN_STRIDE, VAE_SPATIAL_STRIDE)
 
@@ -300,12 +301,16 @@ class StreamingSession:
         self.latent_offset += frames
         return result
 
-    def step_host(self, host_lq: torch.Tensor, host_out: torch.Tensor) -> None:
+    def step_host(self, host_lq: torch.Tensor, host_out: torch.Tensor) -> HostStep:
         """step() from pinned host LQ frames to pinned host latents: the
         host-to-device copy of this block's frames and the device-to-host copy
         of its result run on a copy stream with double-buffered staging, so they
-        overlap the neighbouring blocks' work. Asynchronous: call sync_host()
-        before reading host_out."""
+        overlap the neighbouring blocks' work.
+
+        Asynchronous: the call returns before either copy has run. host_lq must
+        not be rewritten before the returned HostStep's `input_consumed` has
+        completed, and host_out holds the latents once `output_ready` has
+        completed; sync_host() waits for every copy issued so far."""
         dev = self.glue.device
         if getattr(self, "_copy", None) is None:
             self._copy, self._stage = torch.cuda.Stream(dev), {}
@@ -320,10 +325,12 @@ class StreamingSession:
             self._stage[key] = st
         st = self._stage[key]
         k = st["k"] & 1
+        handle = HostStep(torch.cuda.Event(), torch.cuda.Event())
         with torch.cuda.stream(cs):
             cs.wait_event(st["consumed"][k])          # the block two steps back has read this buffer
             st["lq"][k].copy_(host_lq, non_blocking=True)
             st["ready"][k].record(cs)
+            handle.input_consumed.record(cs)
         comp.wait_event(st["ready"][k])
         result = self.step(st["lq"][k])
         st["consumed"][k].record(comp)
@@ -332,10 +339,14 @@ class StreamingSession:
         with torch.cuda.stream(cs):
             cs.wait_event(done)
             host_out.copy_(result, non_blocking=True)
+            handle.output_ready.record(cs)
         result.record_stream(cs)
         st["k"] += 1
+        return handle
 
     def sync_host(self) -> None:
-        """Make the current stream wait for every step_host copy issued so far."""
+        """Block the host until every step_host copy issued so far has run; the
+        current stream also waits for them."""
         if getattr(self, "_copy", None) is not None:
             torch.cuda.current_stream(self.glue.device).wait_stream(self._copy)
+            self._copy.synchronize()

@@ -307,3 +307,46 @@ def test_layer_stack_streaming_and_graph_replay():
     for hin, hout, got in pending:
         np.testing.assert_array_equal(hout.float().numpy(), got)
     assert_no_device_error()
+
+
+def test_layer_stack_step_host_reuses_one_pinned_buffer():
+    """LayerStack.step_host with one pinned input buffer refilled with new data
+    every block once the previous block's HostStep.input_consumed completed,
+    and each result read after its output_ready: bit-identical to step()."""
+    from recavsr_b200.runtime.block import FusedBlock, LayerStack, rope_tables
+    dim, heads, ffn, H, W = 256, 2, 512, 4, 6
+    span = H * W
+    actions = ["recent_2", "recent_2_anchor", "none"]
+    tables = rope_tables(128, H, W, "cuda")
+    ps = [recipes.block_params(dim, heads, ffn, seed=40 + i) for i in range(3)]
+
+    def make():
+        return LayerStack([FusedBlock(_weights(p, heads), H, W, tables) for p in ps], actions)
+
+    ref, streamed = make(), make()
+    rs = np.random.RandomState(8)
+    xs = [bf16_round(rs.standard_normal(((6 if i == 0 else 2) * span, dim)).astype(np.float32))
+          for i in range(10)]
+    want = []
+    for i, x in enumerate(xs):
+        h = dev_bf16(x)
+        ref.step(h, 6 if i == 0 else 2)
+        want.append(host(h))
+    streamed.step(dev_bf16(xs[0]), 6)
+    h = dev_bf16(xs[1])
+    streamed.step(h, 2)                       # eager first body step, then capture
+    streamed.capture(2 * span, 2)
+    np.testing.assert_array_equal(host(h), want[1])
+    hin = torch.empty((2 * span, dim), dtype=torch.bfloat16).pin_memory()
+    outs, handles = [], []
+    for x in xs[2:]:
+        if handles:
+            handles[-1].input_consumed.synchronize()
+        hin.copy_(torch.from_numpy(x))
+        outs.append(torch.empty_like(hin).pin_memory())
+        handles.append(streamed.step_host(hin, outs[-1], 2))
+    for i, (o, hd) in enumerate(zip(outs, handles)):
+        hd.output_ready.synchronize()
+        np.testing.assert_array_equal(o.float().numpy(), want[i + 2], err_msg=f"block {i + 2}")
+    streamed.sync_host()
+    assert_no_device_error()

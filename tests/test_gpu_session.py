@@ -100,7 +100,8 @@ def test_streaming_session_matches_reference(sgold, graphs):
 
 def test_step_host_matches_step(sgold):
     """The pinned-host streaming entry (copies on a side stream, double-buffered
-    staging, no host sync until the end) returns exactly what step() returns."""
+    staging) returns exactly what step() returns while the caller refills one
+    pinned input buffer after each step's input_consumed event."""
     from recavsr_b200.runtime.block import FusedBlock, LayerStack, rope_tables
     from recavsr_b200.runtime.session import StreamingSession
     dim, heads, ffn, channels, height, width, h1, h2, enc_len = (int(v) for v in sgold["session_meta"])
@@ -122,14 +123,22 @@ def test_step_host_matches_step(sgold):
     lq = [steps[0][0]] + [bf16_round(rs.uniform(-1, 1, steps[1][0].shape).astype(np.float32))
                           for _ in range(5)]
     want = [host(a.step(dev_bf16(x)))[0] for x in lq]
-    outs = []
+    # One pinned input buffer per block shape, refilled as soon as the previous
+    # step has consumed it (HostStep.input_consumed), the way a streaming
+    # decoder reuses its frame buffer; each output read after output_ready.
+    outs, handles, bufs = [], [], {}
     for x in lq:
-        hin = torch.from_numpy(x).bfloat16().pin_memory()
+        hin = bufs.get(x.shape)
+        if hin is None:
+            hin = bufs[x.shape] = torch.empty(x.shape, dtype=torch.bfloat16).pin_memory()
+        elif handles:
+            handles[-1].input_consumed.synchronize()
+        hin.copy_(torch.from_numpy(x))
         shape = (1, channels, 6 if not outs else 2, height // 16, width // 16)
         outs.append(torch.empty(shape, dtype=torch.float32).pin_memory())
-        b.step_host(hin, outs[-1])
-    b.sync_host()
-    torch.cuda.synchronize()
-    for i, (o, w_) in enumerate(zip(outs, want)):
+        handles.append(b.step_host(hin, outs[-1]))
+    for i, (o, h, w_) in enumerate(zip(outs, handles, want)):
+        h.output_ready.synchronize()
         np.testing.assert_array_equal(o.numpy()[0], w_, err_msg=f"block {i}")
+    b.sync_host()
     assert_no_device_error()
