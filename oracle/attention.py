@@ -26,9 +26,12 @@ def window_bounds(coord, extent, window):
 
 
 def routed_attention(q, ck, cv, pk, pv, slots, past_positions, query_positions, cos, sin,
-                     height, width, window_h, window_w, dtype="bf16", compute_dtype=np.float64):
+                     height, width, window_h, window_w, dtype="bf16", compute_dtype=np.float64,
+                     query_rows=None):
     """Arrays are [B, tokens, heads, d] float32 holding bf16 (or fp16, with
-    dtype="fp16") values; returns the same shape rounded to that dtype."""
+    dtype="fp16") values; returns the same shape rounded to that dtype.
+    query_rows (optional): compute only these query tokens (indices into the
+    query block); the result is then [B, len(query_rows), heads, d]."""
     q = np.asarray(q, np.float32)
     span = height * width
     bsz, nq, heads, d = q.shape
@@ -59,7 +62,13 @@ def routed_attention(q, ck, cv, pk, pv, slots, past_positions, query_positions, 
         kk = np.concatenate(keys, 0).astype(compute_dtype)   # [nk, heads, d]
         vv = np.concatenate(vals, 0).astype(compute_dtype)
         mm = np.concatenate(masks, 1)                      # [span, nk]
-        mask = np.tile(mm, (frames, 1))                    # [nq, nk]
+        if query_rows is None:
+            mask = np.tile(mm, (frames, 1))                # [nq, nk]
+        else:                                              # query token i sees row i % span of mm
+            rows = np.asarray(query_rows)
+            qr, mask = qr[rows], mm[rows % span]
+            if b == 0:
+                out = np.zeros((bsz, len(rows), heads, d), np.float32)
         scale = d ** -0.5
         for h in range(heads):
             sc = (qr[:, h] @ kk[:, h].T) * scale
