@@ -223,34 +223,53 @@ def time_kernel(fn, reps, torch):
 
 def kernel_roofline(stack, torch):
     """Time the ffn_up NVFP4 GEMM (the largest launch of the step) and the
-    routed attention of a recent_4_anchor layer on the step's own buffers."""
+    routed attention of the recent_4_anchor layers on the step's own buffers,
+    as the layer loop runs them: each call uses the next layer's weights (30 x
+    25 MB of ffn_up weights) or the next recent_4_anchor layer's KV cache (4 x
+    65 MB), so those operands come from HBM as in the step, not from L2. The
+    activations (32 MB or less) are L2-resident, as they are in the step, where
+    the kernel before wrote them. Also the same launches on one layer's
+    operands repeated (L2-warm), for comparison."""
     from recavsr_b200 import _lib
     lib = _lib.library()
-    blk = stack.blocks[11]
     n = BODY * T
     ws = stack.workspace(n)
     st = _lib.stream()
+    cursor = {"up": 0, "att": 0}
 
-    def up():
+    def up_on(blk):
         _lib.check(lib.rc_nvfp4_gemm_ws(ws.a_codes.data_ptr(), ws.a_scales.data_ptr(), blk.up.codes.data_ptr(),
                                         blk.up.scales.data_ptr(), blk.up.bias.data_ptr(), n, FFN, DIM, 1.0,
                                         _lib.EPI_GELU_NVFP4, None, 0, None, ws.f_codes.data_ptr(),
                                         ws.f_scales.data_ptr(), 1.0, ws.gemm_ws.data_ptr(),
                                         ws.gemm_ws.numel(), st), "up")
-    t_up = time_kernel(up, 50, torch)
-    rd = stack.route_dev
-    o = 11 * stack._row
-    cap = stack.caches[11].capacity
-    qpos = rd[LAYERS * stack._row:]
 
-    def att():
-        blk._attention(lib, ws, stack.cache_k[11], stack.cache_v[11], rd[o:o + cap], rd[o + 8:o + 8 + cap],
-                       qpos, n, st)
-    t_att = time_kernel(att, 20, torch)
-    vis = int((stack.route_host[o:o + cap] >= 0).sum())
+    def up_rot():
+        up_on(stack.blocks[cursor["up"] % LAYERS])
+        cursor["up"] += 1
+    t_up = time_kernel(up_rot, 60, torch)
+    t_up_warm = time_kernel(lambda: up_on(stack.blocks[11]), 50, torch)
+    rd = stack.route_dev
+    qpos = rd[LAYERS * stack._row:]
+    att_layers = [i for i, a in enumerate(ACTIONS) if a == "recent_4_anchor"]
+
+    def att_on(i):
+        o = i * stack._row
+        cap = stack.caches[i].capacity
+        stack.blocks[i]._attention(lib, ws, stack.cache_k[i], stack.cache_v[i], rd[o:o + cap],
+                                   rd[o + 8:o + 8 + cap], qpos, n, st)
+
+    def att_rot():
+        att_on(att_layers[cursor["att"] % len(att_layers)])
+        cursor["att"] += 1
+    t_att = time_kernel(att_rot, 20, torch)
+    t_att_warm = time_kernel(lambda: att_on(11), 20, torch)
+    o = 11 * stack._row
+    vis = int((stack.route_host[o:o + stack.caches[11].capacity] >= 0).sum())
     att_flops = 4 * HEAD_DIM * HEADS * n * T * (vis + BODY)
-    return {"ffn_up_s": t_up, "ffn_up_flops": 2.0 * n * FFN * DIM,
-            "attn_s": t_att, "attn_flops": float(att_flops), "attn_planes": vis + BODY}
+    return {"ffn_up_s": t_up, "ffn_up_warm_s": t_up_warm, "ffn_up_flops": 2.0 * n * FFN * DIM,
+            "attn_s": t_att, "attn_warm_s": t_att_warm, "attn_flops": float(att_flops),
+            "attn_planes": vis + BODY, "attn_layers": att_layers}
 
 
 def ffn_up_bytes():
@@ -452,32 +471,23 @@ def synthetic_lq(frames, device, seed):
     return (hr / 127.5 - 1.0).clamp(-1, 1).permute(1, 0, 2, 3).unsqueeze(0).bfloat16().contiguous()
 
 
-def run_session(args, rank, world, local):
-    """--session: the whole streaming one-step DiT (TransformerSession.step) at
-    1280x704 output: LQ projector + patch embedding + sr_proj, the 30-layer loop
-    (CUDA graph), output head, noise - prediction. Each step reads its 8 LQ RGB
-    frames from pinned host memory and returns its 2 latent frames to pinned
-    host memory inside the timed region; one independent stream per rank."""
-    import datetime
-
+def measure_session(session, device, rank, world, steps, warm):
+    """Time `steps` body blocks of the whole streaming one-step DiT through its
+    public host-buffer entry, StreamingSession.step_host: each step's 8 LQ RGB
+    frames are copied from pinned host memory and its 2 latent frames back to
+    pinned host memory inside the timed region (copies on a side stream,
+    overlapping the neighbouring blocks). A fresh stream (reset, prefix block)
+    precedes the warm-up. Returns (seconds, h2d bytes, d2h bytes, clocks, host LQ frames)."""
     import torch
     import torch.distributed as dist
     from recavsr_b200 import _lib
-    from recavsr_b200.runtime.session import StreamingSession
-    torch.cuda.set_device(local)
-    device = torch.device("cuda", local)
-    if world > 1:
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
-    session = StreamingSession(build_stack(device, seed=1234 + rank), build_glue(device, 77 + rank),
-                               704, 1280, seed=rank, graphs=True)
+    session.reset(seed=rank)
     prefix = synthetic_lq(21, device, 5 + rank)
     body = synthetic_lq(8, device, 6 + rank)
     host_lq = torch.empty(body.shape, dtype=torch.bfloat16, pin_memory=True)
     host_lq.copy_(body.cpu())
-    out_shape = (1, LATENT_C, BODY, 44, 80)
-    host_out = torch.empty(out_shape, dtype=torch.float32, pin_memory=True)
+    host_out = torch.empty((1, LATENT_C, BODY, 44, 80), dtype=torch.float32, pin_memory=True)
     session.step(prefix)
-    warm = max(args.warmup, 3)
     for _ in range(warm):
         session.step_host(host_lq, host_out)
     session.sync_host()
@@ -489,9 +499,9 @@ def run_session(args, rank, world, local):
         dist.barrier()
     torch.cuda.synchronize(device)
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clk:
+    with ClockSampler(device.index or 0) as clk:
         start.record()
-        for _ in range(args.steps):
+        for _ in range(steps):
             session.step_host(host_lq, host_out)
         session.sync_host()
         end.record()
@@ -499,14 +509,40 @@ def run_session(args, rank, world, local):
     t = start.elapsed_time(end) * 1e-3
     if not torch.isfinite(host_out).all():
         raise RuntimeError("non-finite session output")
+    return t, host_lq.numel() * 2, host_out.numel() * 4, clk.summary(), host_lq
+
+
+SESSION_GLUE_LAUNCHES = 15   # 2 im2col, 2 channel norms, 7 bf16 GEMMs, 2 patch gathers, 1 LayerNorm, 1 unpatchify
+
+
+def run_session(args, rank, world, local):
+    """--session: the whole streaming one-step DiT (TransformerSession.step) at
+    1280x704 output: LQ projector + patch embedding + sr_proj, the 30-layer loop
+    (CUDA graph), output head, noise - prediction, timed through step_host
+    (pinned host frames in, latents out), plus the glue's per-phase device
+    times; one independent stream per rank."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+    from recavsr_b200.runtime.session import StreamingSession
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+    session = StreamingSession(build_stack(device, seed=1234 + rank), build_glue(device, 77 + rank),
+                               704, 1280, seed=rank, graphs=True)
+    warm = max(args.warmup, 3)
+    t, h2d, d2h, clocks, host_lq = measure_session(session, device, rank, world, args.steps, warm)
     # Per-phase device time of the glue on body blocks (a fresh LQ stream
     # primed with a prefix, so every timed call is a valid streaming step).
     glue = session.glue
+    out_shape = (1, LATENT_C, BODY, 44, 80)
     nz = torch.randn(out_shape, device=device)
     rec = torch.zeros(out_shape, dtype=torch.bfloat16, device=device)
     lq_dev = host_lq.to(device)
     lq_state = glue.lq.create_streaming_state()
-    glue.lq.forward_streaming(prefix, lq_state)
+    glue.lq.forward_streaming(synthetic_lq(21, device, 5 + rank), lq_state)
     t_embed = time_kernel(lambda: glue.embed(nz, lq_dev, rec, lq_state), 5, torch)
     hidden = torch.randn(BODY * T, DIM, device=device).bfloat16()
     t_head = time_kernel(lambda: glue.head(hidden, nz), 5, torch)
@@ -533,20 +569,20 @@ def run_session(args, rank, world, local):
                                "30 layers, output head), 1280x704, 8 LQ frames -> 2 latent frames",
                    "global_batch": world, "seq_len": BODY * T, "parallelism": f"streams x{world}",
                    "l2": "working set > 126 MB L2 (no flush)", "cuda_graph": "layer loop"},
+        "value_is": "aggregate tokens/s over all GPUs; tokens_per_s_per_gpu is the metric's per-GPU figure",
+        "tokens_per_s_per_gpu": value / world,
         "out_fps": value * 4 / T,
-        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": host_lq.numel() * 2,
-                "d2h_bytes_per_step": host_out.numel() * 4,
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "path": "StreamingSession.step_host: LQ frames from pinned host, latents to pinned host "
                         "(copies on a side stream, overlapping the neighbouring blocks)"},
-        # per step: the layer loop (14 per layer + one commit per cached layer) and the glue
-        # (2 im2col, 2 channel norms, 7 bf16 GEMMs, 2 patch gathers, 1 LayerNorm, 1 unpatchify)
-        "gpu_launches": args.steps * (LAYERS * 14 + sum(1 for c in session.stack.caches if c.capacity) + 15),
+        "gpu_launches": args.steps * (LAYERS * 14 + sum(1 for c in session.stack.caches if c.capacity)
+                                      + SESSION_GLUE_LAUNCHES),
         "glue": {"embed_ms": t_embed * 1e3, "head_ms": t_head * 1e3,
                  "embed_tflops": embed_flops / t_embed / 1e12,
                  "embed_frac": embed_flops / t_embed / 1e12 / bf16_peak,
                  "peak": f"{src} bf16 dense {bf16_peak} TFLOP/s",
                  "embed": "LQ projector (im2col + bf16 GEMMs + channel RMSNorm/SiLU), patch embedding x2, sr_proj"},
-        "clocks": clk.summary(),
+        "clocks": clocks,
     }), flush=True)
 
 
@@ -564,7 +600,9 @@ def main():
     ap.add_argument("--head-shard", action="store_true",
                     help="one 3840x2176 stream split by heads over the ranks (strong scaling)")
     ap.add_argument("--session", action="store_true",
-                    help="the whole one-step DiT stream step (LQ projector, layers, head) per block")
+                    help="only the whole one-step DiT stream step (LQ projector, layers, head) per block")
+    ap.add_argument("--no-session", action="store_true",
+                    help="skip the whole-step session measurement of the default line")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
@@ -648,13 +686,21 @@ def main():
         e1.record()
     e1.synchronize()
     te = e0.elapsed_time(e1) * 1e-3
-    if world > 1:
-        tt = torch.tensor([t, te], device=device)
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        t, te = float(tt[0]), float(tt[1])
     kr = kernel_roofline(stack, torch) if rank == 0 and not args.no_kernel_timing else None
     att_flops, planes = attention_flops_per_block(stack)
+    layer_launches = LAYERS * 14 + sum(1 for c in stack.caches if c.capacity)
+    # ---- the whole streaming step (TransformerSession.step) through its public
+    # host-buffer entry: LQ frames in from pinned host memory, latents out.
+    ts = None
+    if not args.no_session:
+        from recavsr_b200.runtime.session import StreamingSession
+        session = StreamingSession(stack, build_glue(device, 77 + rank), 704, 1280, seed=rank, graphs=True)
+        ts, s_h2d, s_d2h, s_clk, _ = measure_session(session, device, rank, world, args.steps, warm)
     if world > 1:
+        tt = torch.tensor([t, te, ts or 0.0], device=device)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        t, te = float(tt[0]), float(tt[1])
+        ts = float(tt[2]) if ts is not None else None
         dist.barrier()
         dist.destroy_process_group()
     if rank != 0:
@@ -664,45 +710,68 @@ def main():
     hbm, bf16_peak, bf16_sus, src = peaks()
     fp4_peak = 4 * bf16_peak
     if kr is None:
-        kr = {"ffn_up_flops": 1.0, "ffn_up_s": float("inf"), "attn_flops": 1.0, "attn_s": float("inf"),
-              "attn_planes": 0}
+        kr = {"ffn_up_flops": 1.0, "ffn_up_s": float("inf"), "ffn_up_warm_s": float("inf"), "attn_flops": 1.0,
+              "attn_s": float("inf"), "attn_warm_s": float("inf"), "attn_planes": 0, "attn_layers": []}
     achieved = kr["ffn_up_flops"] / kr["ffn_up_s"] / 1e12
     cpu = None if args.no_cpu_baseline else cpu_baseline()
-    launches_per_layer = 14   # see FusedBlock.run: LN x3, GEMM x6, RMSNorm x2, gather + attention, cross attention
+    layer_e2e = {"value": tokens / te, "unit": "tokens/s",
+                 "h2d_bytes_per_step": BODY * T * DIM * 2 + stack.route_dev.numel() * 4,   # block + routing table
+                 "d2h_bytes_per_step": BODY * T * DIM * 2,
+                 "path": "LayerStack.step_host (pinned host -> device -> pinned host; copies overlap the "
+                         "neighbouring blocks)" if not args.eager else "copy, step, copy on one stream"}
     out = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": warm, "ms_per_step": t / args.steps * 1e3, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "nvfp4 linears / bf16 attention",
-        "data": "synthetic (random-init weights, N(0,1) hidden/prompt states)",
+        "data": "synthetic (random-init weights, N(0,1) hidden/prompt states; LQ frames: uint8 noise, "
+                "5x5 box filter, bilinear x4)",
         "config": {"workload": "cfg4 DiT layer loop (30 layers, released router), 1280x704 -> 22x40 "
-                               "tokens, 2-frame body block (1760 tokens), B=1",
+                               "tokens, 2-frame body block (1760 tokens), B=1; e2e / out_fps: the whole "
+                               "one-step stream step (LQ projector, patch embedding, layers, head)",
                    "global_batch": world, "seq_len": BODY * T, "parallelism": f"streams x{world}",
                    "l2": "working set > 126 MB L2 (no flush)", "cuda_graph": use_graph},
-        "out_fps": value * 4 / T,
+        "value_is": "aggregate tokens/s over all GPUs; tokens_per_s_per_gpu is the metric's per-GPU figure",
+        "tokens_per_s_per_gpu": value / world,
+        "out_fps_layer_loop": value * 4 / T,
         "linear_tflops": value * algorithmic_flops_per_token() / 1e12,
         "attention_tflops": att_flops * (value / (BODY * T)) / 1e12,
         "roofline": {"bound": "tensor", "kernel": "nvfp4 ffn_up GEMM 1760x14336x3072 (+GELU+NVFP4 epilogue)",
                      "achieved": achieved, "peak": fp4_peak, "unit": "TFLOP/s", "frac": achieved / fp4_peak,
                      "peak_source": f"4 x {src} bf16 dense ({bf16_peak} TFLOP/s): FP4:BF16 dense ratio 4",
+                     "timing": "CUDA events over 60 launches, each on the next layer's weights (HBM-resident "
+                               "as in the step); L2-warm (one layer repeated): "
+                               f"{kr['ffn_up_flops'] / kr['ffn_up_warm_s'] / 1e12:.1f} TFLOP/s",
                      "traffic": PROFILED_DRAM["ffn_up"]["read"] + PROFILED_DRAM["ffn_up"]["write"],
                      "traffic_source": PROFILED_DRAM["ffn_up"]["source"],
                      "algorithmic_bytes": ffn_up_bytes(),
                      "attention": {"achieved": kr["attn_flops"] / kr["attn_s"] / 1e12, "peak": bf16_peak,
                                    "frac": kr["attn_flops"] / kr["attn_s"] / 1e12 / bf16_peak,
                                    "planes": kr["attn_planes"], "unit": "TFLOP/s",
+                                   "timing": f"each launch on the next recent_4_anchor layer's KV cache "
+                                             f"(layers {kr['attn_layers']}); L2-warm: "
+                                             f"{kr['attn_flops'] / kr['attn_warm_s'] / 1e12:.1f} TFLOP/s",
                                    "traffic": PROFILED_DRAM["attention"]["read"] + PROFILED_DRAM["attention"]["write"],
                                    "traffic_source": PROFILED_DRAM["attention"]["source"]}},
         "cpu_baseline": cpu,
-        "e2e": {"value": tokens / te, "unit": "tokens/s",
-                "h2d_bytes_per_step": BODY * T * DIM * 2 + stack.route_dev.numel() * 4,   # block + routing table
-                "d2h_bytes_per_step": BODY * T * DIM * 2,
-                "path": "LayerStack.step_host (pinned host -> device -> pinned host; copies overlap the "
-                        "neighbouring blocks)" if not args.eager else "copy, step, copy on one stream"},
-        "gpu_launches": args.steps * (LAYERS * launches_per_layer + sum(
-            1 for c in stack.caches if c.capacity)),
+        "e2e": layer_e2e,
+        "gpu_launches": args.steps * layer_launches,
         "clocks": clk.summary(),
         "attention_planes_per_block": planes + BODY * LAYERS,
     }
+    if ts is not None:
+        stokens = BODY * T * args.steps * world
+        out["out_fps"] = stokens / ts * 4 / T
+        out["e2e"] = {"value": stokens / ts, "unit": "tokens/s", "h2d_bytes_per_step": s_h2d,
+                      "d2h_bytes_per_step": s_d2h,
+                      "path": "StreamingSession.step_host: the whole one-step DiT stream step (LQ projector, "
+                              "patch embedding, 30 layers, head, noise - prediction) from 8 LQ RGB frames in "
+                              "pinned host memory to 2 latent frames in pinned host memory"}
+        out["e2e_layer_loop"] = layer_e2e
+        out["session"] = {"ms_per_step": ts / args.steps * 1e3, "tokens_s": stokens / ts,
+                          "gpu_launches": args.steps * (layer_launches + SESSION_GLUE_LAUNCHES),
+                          "clocks": s_clk}
+    else:
+        out["out_fps"] = value * 4 / T
     print(json.dumps(out), flush=True)
 
 
