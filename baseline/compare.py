@@ -15,6 +15,7 @@ on the GPU is its own code: the Triton `_paired_local` kernel, `sdpa_attention`
     python baseline/compare.py attention   # cfg2/cfg4: routed attention at 1280x704, scopes 0..8 planes
     python baseline/compare.py local       # cfg5: 22x40-window attention at 1920x1088 and 3840x2176
     python baseline/compare.py layers      # cfg4: the 30-layer DiT loop, PreparedBlock x 30 compiled
+    python baseline/compare.py pipeline    # frame preparation (enlarge + normalize + pad) and strip blend
     python baseline/compare.py all
 
 This library's side is imported from recavsr_b200.runtime (ops, fp8, block):
@@ -433,18 +434,93 @@ def case_layers(rows, steps, warmup):
              "FixedKVCache, as TransformerSession.step runs them")
 
 
+# ----------------------------------------------------------- host pipeline
+def case_pipeline(rows, reps):
+    """One body block (8 LQ frames) to the model input, from uint8 frames in
+    pinned host memory: the reference's prepare_block (video.py:138-150: CPU
+    cv2.resize of every frame into a pinned buffer, its upload, block_tensor on
+    the GPU) next to recavsr_b200.runtime.pipeline (upload of the LQ frames,
+    one rc_enlarge_block launch); wall time per block, host included, with a
+    device sync per block. Then one blended 1920x1080 frame from 4 strips: the
+    reference's CPU canvas loop (strips.py:85-97) next to rc_strip_blend
+    (device frames; device time)."""
+    import numpy as np
+    from recavsr_b200.runtime import pipeline as ours
+    from recavsr_infer import strips as ref_strips
+    from recavsr_infer import video as ref_video
+    rs = np.random.RandomState(0)
+    for (h, w) in ((176, 320), (270, 480)):
+        lq = rs.randint(0, 256, (8, h, w, 3)).astype(np.uint8)
+        lq_pinned = torch.from_numpy(lq).pin_memory()
+        size = ref_video.scaled_size(h, w, 4.0)
+
+        def theirs():
+            x = ref_video.enlarge_block(lq, size, block=8, pin=True)
+            return ref_video.block_tensor(x, 8, device="cuda")
+
+        def mine():
+            return ours.enlarge_block(lq_pinned.to("cuda", non_blocking=True), size, block=8)
+        r, o = theirs(), mine()
+        torch.cuda.synchronize()
+        equal = bool(torch.equal(r, o))
+
+        def wall(fn):
+            for _ in range(2):
+                fn()
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            for _ in range(reps):
+                fn()
+                torch.cuda.synchronize()
+            return (time.perf_counter() - t0) / reps
+        t_r, t_o = wall(theirs), wall(mine)
+        dev = lq_pinned.cuda()
+        t_k = graph_time(lambda: ours.enlarge_block(dev, size, block=8), reps)
+        out_bytes = 3 * 8 * (-(-size[0] // 32) * 32) * size[1] * 4
+        emit(rows, case="pipeline", step=f"prepare_block 8 frames {w}x{h} -> {size[1]}x{size[0]} fp32",
+             ours_ms=t_o * 1e3, ref_ms=t_r * 1e3, speedup=t_r / t_o, outputs_equal=equal,
+             kernel_us=t_k * 1e6, kernel_gbs=(out_bytes + lq.nbytes) / t_k / 1e9,
+             ref="recavsr_infer.video.enlarge_block (cv2, CPU) + block_tensor (torch, GPU)")
+    cols = ref_strips.strip_columns(480, 4, 48, 4.0)
+    width = 1920
+    weights = ref_strips.column_weights(cols, 4.0, width)
+    frames = [rs.randint(0, 256, (1080, len(w), 3)).astype(np.uint8) for _, w in weights]
+    total = np.zeros(width, dtype=np.float32)
+    for o0, w in weights:
+        total[o0:o0 + len(w)] += w
+
+    def ref_blend():
+        canvas = np.zeros((1080, width, 3), dtype=np.float32)
+        for f, (o0, w) in zip(frames, weights):
+            canvas[:, o0:o0 + len(w)] += f * w[None, :, None]
+        canvas /= total[None, :, None]
+        return np.clip(canvas + 0.5, 0, 255).astype(np.uint8)
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        want = ref_blend()
+    t_r = (time.perf_counter() - t0) / reps
+    blender = ours.StripBlender(cols, 4.0, 1080, width, device="cuda")
+    dframes = [torch.from_numpy(f).cuda() for f in frames]
+    got = blender.blend(dframes)
+    t_o = graph_time(lambda: blender.blend(dframes), reps)
+    emit(rows, case="pipeline", step="strip blend, 4 strips -> 1920x1080 uint8", ours_us=t_o * 1e6,
+         ref_us=t_r * 1e6, speedup=t_r / t_o, outputs_equal=bool(np.array_equal(got.cpu().numpy(), want)),
+         ref="the canvas loop of recavsr_infer.strips.blend_strips (numpy, CPU)")
+
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=["gemm", "attention", "local", "layers", "all"])
+    ap.add_argument("case", choices=["gemm", "attention", "local", "layers", "pipeline", "all"])
     ap.add_argument("--reps", type=int, default=10)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     args = ap.parse_args()
     install_reference()
+    sys.modules.setdefault("av", types.ModuleType("av"))   # PyAV only opens video files; not needed here
     torch.cuda.set_device(0)
     torch._dynamo.config.recompile_limit = 64     # one compiled graph per shape, as the reference allows
     rows = []
-    todo = ["gemm", "attention", "local", "layers"] if args.case == "all" else [args.case]
+    todo = ["gemm", "attention", "local", "layers", "pipeline"] if args.case == "all" else [args.case]
     for c in todo:
         if c == "gemm":
             case_gemm(rows, args.reps)
@@ -452,6 +528,8 @@ def main():
             case_attention(rows, args.reps)
         elif c == "local":
             case_local(rows, args.reps)
+        elif c == "pipeline":
+            case_pipeline(rows, args.reps)
         else:
             case_layers(rows, args.steps, args.warmup)
         torch.cuda.empty_cache()

@@ -238,6 +238,32 @@ int rc_unpatchify_residual(const void* pred, long long ldp, const float* noise, 
                            void* recycle, int C, int F, int H, int W, int ph, int pw,
                            int recycle_frames, rc_stream_t stream);
 
+/* ---- frame preparation and strip blending -------------------------------- */
+/* Replaces recavsr_infer/video.py:153-179 (`enlarge_block` + `block_tensor`,
+ * called by `prepare_block` :138-150): src = `valid` uint8 RGB frames [h, w, 3]
+ * (byte strides frame_stride / row_stride, contiguous pixels), bilinearly
+ * enlarged to out_h x out_w exactly as cv2.resize INTER_LINEAR does for 8-bit
+ * images, the last frame repeated up to `block` frames, normalized to
+ * x / 127.5 - 1 and padded to Hp x Wp (out_h, out_w rounded up to multiples of
+ * 32; reflect, or replicate when the pad is not smaller than the size). out:
+ * [3, block, Hp, Wp] contiguous, fp32 (out_bf16 = 0) or bf16 (1), 16-byte aligned. */
+int rc_enlarge_block(const uint8_t* src, long long frame_stride, long long row_stride, int valid,
+                     int block, int h, int w, int out_h, int out_w, int out_bf16, void* out,
+                     rc_stream_t stream);
+
+/* One output frame of recavsr_infer/strips.py:72-99 (`blend_strips`): strip s's
+ * uint8 frame [height, widths[s], 3] (device pointer frames[s], row stride
+ * row_strides[s] bytes) placed at column offsets[s] and weighted by its feather
+ * ramp weights[s] (device fp32 [widths[s]]); canvas summed in strip order in
+ * fp32, divided by total (device fp32 [width]), + 0.5, clipped to [0, 255] and
+ * truncated into out (device uint8 [height, width, 3], row stride
+ * out_row_stride bytes). frames / row_strides / offsets / widths / weights are
+ * host arrays of n_strips (<= 16) entries. */
+int rc_strip_blend(int n_strips, const uint8_t* const* frames, const long long* row_strides,
+                   const int* offsets, const int* widths, const float* const* weights,
+                   const float* total, int height, int width, uint8_t* out, long long out_row_stride,
+                   rc_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

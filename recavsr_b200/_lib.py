@@ -45,6 +45,8 @@ _SIGNATURES = {
     "rc_conv3d_im2col": [_P, _LL, _LL, _LL, _LL, _I, _I, _I, _I, _I, _I, _I, _I, _P, _LL, _P],
     "rc_channel_rmsnorm_silu": [_P, _LL, _I, _I, _P, _F, _P, _LL, _P],
     "rc_patchify": [_P, _I, _LL, _LL, _LL, _I, _I, _I, _I, _I, _I, _P, _LL, _P],
+    "rc_enlarge_block": [_P, _LL, _LL, _I, _I, _I, _I, _I, _I, _I, _P, _P],
+    "rc_strip_blend": [_I, _P, _P, _P, _P, _P, _P, _I, _I, _P, _LL, _P],
     "rc_unpatchify_residual": [_P, _LL, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _P],
 }
 _RESTYPES = {"rc_paired_attention_workspace": C.c_longlong, "rc_gemm_split_workspace": C.c_longlong,

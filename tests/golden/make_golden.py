@@ -5,6 +5,7 @@ Run where a checkout of the reference exists:
     python tests/golden/make_golden.py <reference checkout> --session  # session_outputs.npz
     TRITON_INTERPRET=1 python tests/golden/make_golden.py <reference checkout> --flashdecoder
     python tests/golden/make_golden.py <reference checkout> --fullsize  # fullsize_hashes.json
+    python tests/golden/make_golden.py <reference checkout> --pipeline  # pipeline_outputs.npz
                                                                         # flashdecoder_outputs.npz
 (or set RECAVSR_REFERENCE). Under TRITON_INTERPRET=1 it also records the
 reference's Triton kernel on windowed cases. The --session fixtures come from
@@ -520,6 +521,58 @@ def gen_fullsize():
     return result
 
 
+# ------------------------------------------------------------ host pipeline
+PIPELINE_ENLARGE = [            # (LQ frames, h, w, block, output size or None for x4 scale)
+    (5, 22, 40, 8, None),       # x4 -> 88 x 160: height padded by 8 (reflect)
+    (3, 13, 21, 3, (50, 75)),   # non-integer scale, both axes reflect-padded
+    (2, 5, 6, 4, (10, 12)),     # pads >= size: replicate
+]
+PIPELINE_BLEND = [              # (LQ width, strips, overlap, scale, out height, frames)
+    (40, 3, 6, 4.0, 24, 2),
+    (33, 2, 5, 2.0, 16, 2),
+]
+
+
+def gen_pipeline(out):
+    """The reference's video.prepare_block pieces (enlarge_block: cv2.resize
+    INTER_LINEAR + block padding; block_tensor: normalize + pad) and
+    strips.blend_strips (its own canvas loop, fed in-memory frames in place of
+    the decoded strip videos). `av` (PyAV) is not installed and only opens
+    files, so it is stubbed; cv2 is the real opencv-python-headless."""
+    import hashlib
+    sys.modules.setdefault("av", types.ModuleType("av"))
+    from recavsr_infer import strips, video
+    for i, (n, h, w, block, size) in enumerate(PIPELINE_ENLARGE):
+        frames = recipes.lq_frames_u8(n, h, w, seed=60 + i)
+        size = size or video.scaled_size(h, w, 4.0)
+        enlarged = video.enlarge_block(frames, size, block=block)
+        x = video.block_tensor(enlarged, block, device="cpu")
+        out[f"enlarge{i}_u8"] = enlarged.numpy()                  # [1, 3, block, H, W] uint8
+        out[f"enlarge{i}_sha256"] = np.frombuffer(
+            hashlib.sha256(x.contiguous().numpy().tobytes()).digest(), np.uint8)
+        out[f"enlarge{i}_shape"] = np.array(x.shape, np.int64)
+        if x.numel() <= 65536:
+            out[f"enlarge{i}_f32"] = x.numpy()
+    for i, (lq_w, n_strips, overlap, scale, height, n_frames) in enumerate(PIPELINE_BLEND):
+        cols = strips.strip_columns(lq_w, n_strips, overlap, scale)
+        width = strips.scaled_size(1, lq_w, scale)[1]
+        widths = [round(x1 * scale) - round(x0 * scale) for x0, x1 in cols]
+        rs = np.random.RandomState(80 + i)
+        strip_frames = [[rs.randint(0, 256, (height, sw, 3)).astype(np.uint8) for _ in range(n_frames)]
+                        for sw in widths]
+        feed = dict(zip(map(str, range(n_strips)), strip_frames))
+        saved = strips._decode
+        strips._decode = lambda p: iter(feed[str(p)])
+        try:
+            blended = list(strips.blend_strips([str(k) for k in range(n_strips)], cols, scale, height, width))
+        finally:
+            strips._decode = saved
+        out[f"blend{i}_columns"] = np.array(cols, np.int64)
+        out[f"blend{i}_out"] = np.stack(blended)
+        for s_i, fr in enumerate(strip_frames):
+            out[f"blend{i}_strip{s_i}"] = np.stack(fr)
+
+
 def main():
     args = [a for a in sys.argv[1:] if not a.startswith("--")]
     ref = args[0] if args else os.environ.get("RECAVSR_REFERENCE")
@@ -530,6 +583,12 @@ def main():
         with open(os.path.join(HERE, "fullsize_hashes.json"), "w") as f:
             json.dump(gen_fullsize(), f, indent=1)
         print("wrote fullsize_hashes.json")
+        return
+    if "--pipeline" in sys.argv:
+        out = {}
+        gen_pipeline(out)
+        np.savez_compressed(os.path.join(HERE, "pipeline_outputs.npz"), **out)
+        print("wrote", len(out), "pipeline arrays")
         return
     if "--flashdecoder" in sys.argv:
         out = {}

@@ -154,3 +154,13 @@ def cfg3_activation_large(m: int, k: int, seed: int = 2) -> np.ndarray:
     u += np.uint32(0x7FFF) + ((u >> np.uint32(16)) & np.uint32(1))
     u &= np.uint32(0xFFFF0000)
     return x
+
+
+def lq_frames_u8(n: int, h: int, w: int, seed: int = 60) -> np.ndarray:
+    """LQ RGB frames as a decoder delivers them, uint8 [n, h, w, 3]: uniform
+    noise smoothed by a 3x3 box filter along both axes (integer mean), so
+    neighbouring pixels are correlated like video."""
+    rs = np.random.RandomState(seed)
+    x = rs.randint(0, 256, (n, h + 2, w + 2, 3)).astype(np.int32)
+    acc = sum(x[:, dy:dy + h, dx:dx + w] for dy in range(3) for dx in range(3))
+    return (acc // 9).astype(np.uint8)
