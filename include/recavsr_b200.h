@@ -246,9 +246,15 @@ int rc_unpatchify_residual(const void* pred, long long ldp, const float* noise, 
  * images, the last frame repeated up to `block` frames, normalized to
  * x / 127.5 - 1 and padded to Hp x Wp (out_h, out_w rounded up to multiples of
  * 32; reflect, or replicate when the pad is not smaller than the size). out:
- * [3, block, Hp, Wp] contiguous, fp32 (out_bf16 = 0) or bf16 (1), 16-byte aligned. */
+ * [3, block, Hp, Wp] contiguous, 16-byte aligned; fp32, or bf16 with
+ * RC_ENLARGE_BF16. The normalization divides by 127.5 as the reference's
+ * block_tensor does on the CPU, or with RC_ENLARGE_RECIPROCAL multiplies by
+ * fl32(1/127.5) as it does on CUDA (torch's scalar division there), the
+ * device the reference's inference uses. */
+#define RC_ENLARGE_BF16 1
+#define RC_ENLARGE_RECIPROCAL 2
 int rc_enlarge_block(const uint8_t* src, long long frame_stride, long long row_stride, int valid,
-                     int block, int h, int w, int out_h, int out_w, int out_bf16, void* out,
+                     int block, int h, int w, int out_h, int out_w, int flags, void* out,
                      rc_stream_t stream);
 
 /* One output frame of recavsr_infer/strips.py:72-99 (`blend_strips`): strip s's

@@ -104,12 +104,17 @@ def _pad_index(n: int, pad: int) -> np.ndarray:
     return idx
 
 
-def block_tensor(enlarged: np.ndarray) -> np.ndarray:
+def block_tensor(enlarged: np.ndarray, reciprocal: bool = False) -> np.ndarray:
     """video.py:165-179 on the enlarged uint8 [block, H, W, 3] frames:
-    fp32 [1, 3, block, Hp, Wp], x / 127.5 - 1, padded to the token stride."""
+    fp32 [1, 3, block, Hp, Wp], x / 127.5 - 1, padded to the token stride.
+    torch divides by the scalar on the CPU but multiplies by its fp32
+    reciprocal on CUDA; reciprocal=True restates the CUDA arithmetic."""
     frames, h, w, _ = enlarged.shape
     x = np.transpose(enlarged, (3, 0, 1, 2)).astype(np.float32)
-    x = (x / np.float32(127.5) - np.float32(1.0)).astype(np.float32)
+    if reciprocal:
+        x = (x * (np.float32(1) / np.float32(127.5)) - np.float32(1.0)).astype(np.float32)
+    else:
+        x = (x / np.float32(127.5) - np.float32(1.0)).astype(np.float32)
     ph, pw = (-h) % TOKEN_STRIDE, (-w) % TOKEN_STRIDE
     x = x[:, :, _pad_index(h, ph)][:, :, :, _pad_index(w, pw)]
     return x[None]

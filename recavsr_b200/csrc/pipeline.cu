@@ -8,6 +8,11 @@
 // or replicate when the pad is not smaller than the size, video.py:165-179),
 // in one pass. The host uploads only the small LQ frames (1/16 of the
 // enlarged bytes at x4) and the enlarged block never exists in uint8.
+// The reference's block_tensor normalizes with torch, whose CUDA kernel
+// multiplies by the fp32 reciprocal of a scalar divisor (x * fl32(1/127.5))
+// while its CPU kernel divides (x / 127.5): the two differ by one fp32 ulp for
+// 111 of the 256 byte values. Both are offered (flags bit RC_ENLARGE_RECIPROCAL);
+// the reference's inference runs block_tensor on CUDA.
 //
 // rc_strip_blend: one output frame of recavsr_infer/strips.py:72-99 -- the
 // strips' uint8 frames weighted by their feather ramps, summed in strip order
@@ -60,7 +65,7 @@ struct EnlargeArgs {
   const uint8_t* src;
   long long frame_stride, row_stride;   // bytes
   int valid, block, h, w, out_h, out_w, hp, wp;
-  int bf16;
+  int bf16, reciprocal;
   void* out;                            // [3, block, hp, wp]
 };
 
@@ -87,7 +92,8 @@ __global__ void __launch_bounds__(256) enlarge_block_kernel(EnlargeArgs a) {
       const int s1 = (int)rc::ld_in(r1 + 3 * tx.i0 + c) * tx.w0 + (int)rc::ld_in(r1 + 3 * tx.i1 + c) * tx.w1;
       const int q = (((s0 >> 4) * ty.w0) >> 16) + (((s1 >> 4) * ty.w1) >> 16);
       const int u = min(max((q + 2) >> 2, 0), 255);
-      v[c][j] = __fsub_rn(__fdiv_rn((float)u, 127.5f), 1.0f);
+      const float x = a.reciprocal ? __fmul_rn((float)u, 1.0f / 127.5f) : __fdiv_rn((float)u, 127.5f);
+      v[c][j] = __fsub_rn(x, 1.0f);
     }
   }
   // wp is a multiple of 32, so every thread's 8 columns lie inside the row.
@@ -153,7 +159,7 @@ __global__ void __launch_bounds__(256) strip_blend_kernel(BlendArgs a) {
 extern "C" {
 
 int rc_enlarge_block(const uint8_t* src, long long frame_stride, long long row_stride, int valid,
-                     int block, int h, int w, int out_h, int out_w, int out_bf16, void* out,
+                     int block, int h, int w, int out_h, int out_w, int flags, void* out,
                      cudaStream_t stream) {
   if (!src || !out)
     return rc::set_error(RC_ERR_ARG, "rc_enlarge_block: missing pointer");
@@ -166,7 +172,9 @@ int rc_enlarge_block(const uint8_t* src, long long frame_stride, long long row_s
     return rc::set_error(RC_ERR_ARG, "rc_enlarge_block: output must be 16-byte aligned");
   if (hp > 65535 || block > 65535)
     return rc::set_error(RC_ERR_ARG, "rc_enlarge_block: raster too tall (%d rows)", hp);
-  EnlargeArgs a{src, frame_stride, row_stride, valid, block, h, w, out_h, out_w, hp, wp, out_bf16 ? 1 : 0, out};
+  if (flags & ~3) return rc::set_error(RC_ERR_ARG, "rc_enlarge_block: unknown flags 0x%x", flags);
+  EnlargeArgs a{src, frame_stride, row_stride, valid, block, h, w, out_h, out_w, hp, wp,
+                (flags & 1) ? 1 : 0, (flags & 2) ? 1 : 0, out};
   const int per_row = wp / kEnlargeCols;
   const dim3 grid((per_row + 255) / 256, hp, block);
   return rc::check_launch(rc::launch_pdl(enlarge_block_kernel, grid, dim3(256), 0, stream, a),

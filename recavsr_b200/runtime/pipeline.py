@@ -57,12 +57,19 @@ def padded_size(height: int, width: int) -> tuple[int, int]:
     return -(-height // s) * s, -(-width // s) * s
 
 
+ENLARGE_BF16, ENLARGE_RECIPROCAL = 1, 2
+
+
 def enlarge_block(chunk: torch.Tensor, size, *, block: int, dtype=torch.float32,
-                  out: torch.Tensor | None = None) -> torch.Tensor:
+                  out: torch.Tensor | None = None, normalize: str = "cuda") -> torch.Tensor:
     """enlarge_block + block_tensor (video.py:153-179) of uint8 frames
     [valid, h, w, 3] already on the device: [1, 3, block, Hp, Wp] in `dtype`
     (fp32 as the reference's block_tensor returns; bf16 is what the session
-    consumes)."""
+    consumes). normalize="cuda" reproduces block_tensor on a CUDA device (torch
+    multiplies by the fp32 reciprocal of 127.5 there), "cpu" on the CPU (a
+    true division); the two differ by one fp32 ulp on some byte values."""
+    if normalize not in ("cuda", "cpu"):
+        raise ValueError("normalize must be 'cuda' or 'cpu'.")
     if chunk.device.type != "cuda" or chunk.dtype != torch.uint8 or chunk.dim() != 4 or chunk.shape[-1] != 3:
         raise ValueError("enlarge_block expects CUDA uint8 frames [valid, h, w, 3].")
     valid, h, w, _ = chunk.shape
@@ -79,12 +86,14 @@ def enlarge_block(chunk: torch.Tensor, size, *, block: int, dtype=torch.float32,
         out = torch.empty(shape, dtype=dtype, device=chunk.device)
     elif tuple(out.shape) != shape or out.dtype != dtype or not out.is_contiguous():
         raise ValueError("out must be a contiguous tensor of the padded block shape.")
+    flags = (ENLARGE_BF16 if dtype == torch.bfloat16 else 0) | (ENLARGE_RECIPROCAL if normalize == "cuda" else 0)
     _lib.call("rc_enlarge_block", chunk.data_ptr(), chunk.stride(0), chunk.stride(1), valid, block, h, w,
-              srh, srw, int(dtype == torch.bfloat16), out.data_ptr(), _lib.stream(chunk.device))
+              srh, srw, flags, out.data_ptr(), _lib.stream(chunk.device))
     return out
 
 
-def prepare_block(frames, start, valid, block, *, device, scale=4.0, size=None, dtype=torch.float32):
+def prepare_block(frames, start, valid, block, *, device, scale=4.0, size=None, dtype=torch.float32,
+                  normalize="cuda"):
     """video.py:138-150: upsample one LQ block to the model raster on the
     device. `frames` is the uint8 [N, h, w, 3] video (numpy, a CPU tensor,
     ideally pinned, or a CUDA tensor); only frames [start, start + valid) are
@@ -97,7 +106,7 @@ def prepare_block(frames, start, valid, block, *, device, scale=4.0, size=None, 
     chunk = chunk.to(device=device, non_blocking=True)
     height, width = chunk.shape[1:3]
     size = size or scaled_size(height, width, scale)
-    return enlarge_block(chunk, size, block=block, dtype=dtype)
+    return enlarge_block(chunk, size, block=block, dtype=dtype, normalize=normalize)
 
 
 def strip_columns(width: int, strips: int, overlap: int, scale: float):
@@ -149,7 +158,10 @@ class StripBlender:
         total = np.zeros(width, dtype=np.float32)
         for o0, w in self.weights:
             total[o0:o0 + len(w)] += w
-        self.height, self.width, self.device = height, width, torch.device(device)
+        device = torch.device(device)
+        if device.type == "cuda" and device.index is None:
+            device = torch.device("cuda", torch.cuda.current_device())
+        self.height, self.width, self.device = height, width, device
         self.total = torch.from_numpy(total).to(self.device)
         self.ramps = [torch.from_numpy(w).to(self.device) for _, w in self.weights]
 

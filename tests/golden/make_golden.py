@@ -6,6 +6,8 @@ Run where a checkout of the reference exists:
     TRITON_INTERPRET=1 python tests/golden/make_golden.py <reference checkout> --flashdecoder
     python tests/golden/make_golden.py <reference checkout> --fullsize  # fullsize_hashes.json
     python tests/golden/make_golden.py <reference checkout> --pipeline  # pipeline_outputs.npz
+    python tests/golden/make_golden.py <reference checkout> --pipeline-cuda [out.npz]
+                                        # pipeline_cuda_outputs.npz (needs a CUDA device)
                                                                         # flashdecoder_outputs.npz
 (or set RECAVSR_REFERENCE). Under TRITON_INTERPRET=1 it also records the
 reference's Triton kernel on windowed cases. The --session fixtures come from
@@ -573,6 +575,26 @@ def gen_pipeline(out):
             out[f"blend{i}_strip{s_i}"] = np.stack(fr)
 
 
+def gen_pipeline_cuda(out):
+    """block_tensor as the reference's inference runs it (device="cuda",
+    inference.py:285): torch normalizes there by multiplying with the fp32
+    reciprocal of 127.5 instead of dividing, so its output differs from the
+    CPU fixture by one fp32 ulp on some byte values. The enlarged frames come
+    from the reference's own enlarge_block (cv2, CPU), as in inference."""
+    import hashlib
+    sys.modules.setdefault("av", types.ModuleType("av"))
+    from recavsr_infer import video
+    for i, (n, h, w, block, size) in enumerate(PIPELINE_ENLARGE):
+        frames = recipes.lq_frames_u8(n, h, w, seed=60 + i)
+        size = size or video.scaled_size(h, w, 4.0)
+        x = video.block_tensor(video.enlarge_block(frames, size, block=block), block, device="cuda").cpu()
+        out[f"enlarge{i}_sha256"] = np.frombuffer(
+            hashlib.sha256(x.contiguous().numpy().tobytes()).digest(), np.uint8)
+        out[f"enlarge{i}_shape"] = np.array(x.shape, np.int64)
+        if x.numel() <= 65536:
+            out[f"enlarge{i}_f32"] = x.numpy()
+
+
 def main():
     args = [a for a in sys.argv[1:] if not a.startswith("--")]
     ref = args[0] if args else os.environ.get("RECAVSR_REFERENCE")
@@ -583,6 +605,13 @@ def main():
         with open(os.path.join(HERE, "fullsize_hashes.json"), "w") as f:
             json.dump(gen_fullsize(), f, indent=1)
         print("wrote fullsize_hashes.json")
+        return
+    if "--pipeline-cuda" in sys.argv:
+        out = {}
+        gen_pipeline_cuda(out)
+        path = args[1] if len(args) > 1 else os.path.join(HERE, "pipeline_cuda_outputs.npz")
+        np.savez_compressed(path, **out)
+        print("wrote", len(out), "pipeline (cuda) arrays to", path)
         return
     if "--pipeline" in sys.argv:
         out = {}

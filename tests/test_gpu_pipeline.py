@@ -18,6 +18,7 @@ from tests.util import assert_no_device_error
 
 pytestmark = pytest.mark.gpu
 GOLDEN = os.path.join(os.path.dirname(__file__), "golden", "pipeline_outputs.npz")
+GOLDEN_CUDA = os.path.join(os.path.dirname(__file__), "golden", "pipeline_cuda_outputs.npz")
 
 
 @pytest.fixture(scope="module")
@@ -26,15 +27,24 @@ def pg():
 
 
 def test_enlarge_block_matches_reference_fixtures(pg):
+    """normalize="cpu" against the reference's block_tensor on the CPU, the
+    default ("cuda") against the oracle's reciprocal form and, where it was
+    generated, against the reference's block_tensor run on CUDA."""
     from recavsr_b200.runtime.pipeline import enlarge_block
+    pc = np.load(GOLDEN_CUDA) if os.path.exists(GOLDEN_CUDA) else None
     for i, (n, h, w, block, size) in enumerate(make_golden.PIPELINE_ENLARGE):
-        frames = torch.from_numpy(recipes.lq_frames_u8(n, h, w, seed=60 + i)).cuda()
+        host_frames = recipes.lq_frames_u8(n, h, w, seed=60 + i)
+        frames = torch.from_numpy(host_frames).cuda()
         size = size or op.scaled_size(h, w, 4.0)
-        x = enlarge_block(frames, size, block=block).cpu().numpy()
+        x = enlarge_block(frames, size, block=block, normalize="cpu").cpu().numpy()
         assert tuple(x.shape) == tuple(pg[f"enlarge{i}_shape"])
         assert hashlib.sha256(x.tobytes()).digest() == pg[f"enlarge{i}_sha256"].tobytes(), i
+        xc = enlarge_block(frames, size, block=block).cpu().numpy()
+        np.testing.assert_array_equal(xc, op.block_tensor(op.enlarge_block(host_frames, size, block), True))
+        if pc is not None:
+            assert hashlib.sha256(xc.tobytes()).digest() == pc[f"enlarge{i}_sha256"].tobytes(), i
         xb = enlarge_block(frames, size, block=block, dtype=torch.bfloat16).float().cpu().numpy()
-        np.testing.assert_array_equal(xb, bf16_round(x))
+        np.testing.assert_array_equal(xb, bf16_round(xc))
     assert_no_device_error()
 
 
@@ -46,7 +56,7 @@ def test_enlarge_block_bench_geometries(h, w, n, block):
     frames = recipes.lq_frames_u8(n, h, w, seed=h + w)
     size = op.scaled_size(h, w, 4.0)
     got = enlarge_block(torch.from_numpy(frames).cuda(), size, block=block, dtype=torch.bfloat16)
-    want = op.block_tensor(op.enlarge_block(frames, size, block))
+    want = op.block_tensor(op.enlarge_block(frames, size, block), reciprocal=True)
     assert_no_device_error()
     np.testing.assert_array_equal(got.float().cpu().numpy(), bf16_round(want))
 
@@ -59,7 +69,7 @@ def test_prepare_block_from_pinned_host_frames():
     got = [(s, v, b, prepare_block(video, s, v, b, device="cuda")) for s, v, b in block_schedule(31)]
     assert [(s, v, b) for s, v, b, _ in got] == [(0, 21, 21), (21, 8, 8), (29, 2, 8)]
     for s, v, b, x in got:
-        want = op.block_tensor(op.enlarge_block(video.numpy()[s:s + v], (176, 320), b))
+        want = op.block_tensor(op.enlarge_block(video.numpy()[s:s + v], (176, 320), b), reciprocal=True)
         np.testing.assert_array_equal(x.cpu().numpy(), want)
     with pytest.raises(ValueError):
         prepare_block(video, 30, 2, 8, device="cuda")

@@ -19,6 +19,7 @@ from oracle import pipeline as op
 from tests.golden import make_golden, recipes
 
 GOLDEN = os.path.join(os.path.dirname(__file__), "golden", "pipeline_outputs.npz")
+GOLDEN_CUDA = os.path.join(os.path.dirname(__file__), "golden", "pipeline_cuda_outputs.npz")
 
 
 @pytest.fixture(scope="module")
@@ -59,6 +60,21 @@ def test_enlarge_and_block_tensor_match_reference(pg):
         assert hashlib.sha256(np.ascontiguousarray(x).tobytes()).digest() == pg[f"enlarge{i}_sha256"].tobytes()
         if f"enlarge{i}_f32" in pg:
             np.testing.assert_array_equal(x, pg[f"enlarge{i}_f32"])
+
+
+def test_block_tensor_cuda_arithmetic_matches_reference():
+    """The reference's block_tensor on CUDA (fixture made on a B200 by
+    make_golden.py --pipeline-cuda): the oracle's reciprocal form."""
+    if not os.path.exists(GOLDEN_CUDA):
+        pytest.skip("pipeline_cuda_outputs.npz not generated")
+    pc = np.load(GOLDEN_CUDA)
+    for i, (n, h, w, block, size) in enumerate(make_golden.PIPELINE_ENLARGE):
+        frames = recipes.lq_frames_u8(n, h, w, seed=60 + i)
+        size = size or op.scaled_size(h, w, 4.0)
+        x = op.block_tensor(op.enlarge_block(frames, size, block), reciprocal=True)
+        assert hashlib.sha256(np.ascontiguousarray(x).tobytes()).digest() == pc[f"enlarge{i}_sha256"].tobytes(), i
+        if f"enlarge{i}_f32" in pc:
+            np.testing.assert_array_equal(x, pc[f"enlarge{i}_f32"])
 
 
 def test_strip_blend_matches_reference(pg):
