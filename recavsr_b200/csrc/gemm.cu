@@ -39,10 +39,12 @@ constexpr int kRowBytes = 128;                     // K bytes per smem row / k-t
 // Epilogue warps per CTA: 4 per TMEM lane quadrant for the GELU + NVFP4
 // epilogue (latency-bound math), 2 per quadrant for the light epilogues (more
 // warps there only compete with the MMA issuer for its SM sub-partition).
-template <int EPI>
-constexpr int epi_warps() { return EPI == EPI_GELU_NVF4 ? 16 : 8; }
-template <int EPI>
-constexpr int gemm_threads() { return 64 + 32 * epi_warps<EPI>(); }   // producer, MMA, epilogue
+// A CTA pair (PAIR) drains a 128 x 256 accumulator per CTA into registers, so
+// it always uses 16 epilogue warps (64 accumulator columns per thread).
+template <int EPI, bool PAIR = false>
+constexpr int epi_warps() { return (PAIR || EPI == EPI_GELU_NVF4) ? 16 : 8; }
+template <int EPI, bool PAIR = false>
+constexpr int gemm_threads() { return 64 + 32 * epi_warps<EPI, PAIR>(); }   // producer, MMA, epilogue
 constexpr int kSfAtomBytes = 512;                  // 128 rows x 4 scale bytes
 
 template <int KIND>
@@ -117,10 +119,10 @@ __device__ __forceinline__ void tile_coords(const GemmParams& p, int tile, int& 
   nb = r / gm;
 }
 
-template <int KIND, int BN, int STAGES>
+template <int KIND, int BN, int STAGES, bool PAIR = false>
 struct Smem {
   static constexpr int kA = BM * kRowBytes;
-  static constexpr int kB = BN * kRowBytes;
+  static constexpr int kB = (PAIR ? BN / 2 : BN) * kRowBytes;   // a pair splits B's rows between its CTAs
   static constexpr int kSfa = KindTraits<KIND>::kScaled ? 4 * kSfAtomBytes : 0;
   static constexpr int kSfb = KindTraits<KIND>::kScaled ? (BN / 128) * 4 * kSfAtomBytes : 0;
   static constexpr int offA = 0;
@@ -159,11 +161,13 @@ __device__ __forceinline__ void unpack_bf16x2(uint32_t w, float& a, float& b) {
   b = __uint_as_float(w & 0xffff0000u);
 }
 
-template <int KIND, int BN, int STAGES, int EPI>
-__global__ void __launch_bounds__(gemm_threads<EPI>(), 1)
+template <int KIND, int BN, int STAGES, int EPI, bool PAIR>
+__global__ void __launch_bounds__(gemm_threads<EPI, PAIR>(), 1)
 gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+            const __grid_constant__ CUtensorMap tmap_sfa, const __grid_constant__ CUtensorMap tmap_sfb,
             const GemmParams p) {
-  using S = Smem<KIND, BN, STAGES>;
+  using S = Smem<KIND, BN, STAGES, PAIR>;
+  static_assert(!PAIR || (KIND == KIND_NVF4 && BN == 256), "CTA pairs run 256 x 256 NVFP4 tiles");
   constexpr bool kScaled = KindTraits<KIND>::kScaled;
   constexpr int kMmaPerTile = 4;                     // 4 x 32 bytes of K per 128-byte row
   constexpr int kTmemCols = 512;
@@ -185,6 +189,12 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int num_units = p.n_regular + (p.m_blocks * p.n_blocks - p.n_regular) * p.split;
+  // CTA pair: both CTAs of a cluster walk the same units (256-row tiles); the
+  // even one (leader) issues the MMAs, each CTA owns 128 of the rows.
+  const uint32_t rank = PAIR ? sm100::cluster_ctarank() : 0u;
+  const bool leader = rank == 0;
+  const int unit0 = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+  const int unit_step = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -193,18 +203,25 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
     }
     for (int a = 0; a < 2; ++a) {
       sm100::mbar_init(&acc_full[a], 1);
-      sm100::mbar_init(&acc_empty[a], 32 * epi_warps<EPI>());
+      // A pair's leader counts one arrival per epilogue warp of both CTAs.
+      sm100::mbar_init(&acc_empty[a], PAIR ? 2 * epi_warps<EPI, PAIR>() : 32 * epi_warps<EPI, PAIR>());
     }
     sm100::mbar_init(done, 1);
     *abort_flag = 0;
     sm100::fence_mbar_init();
   }
   if (warp == 1) {
-    sm100::tmem_alloc(tmem_slot, kTmemCols);
-    sm100::tmem_relinquish();
+    if constexpr (PAIR) {
+      sm100::tmem_alloc_pair(tmem_slot, kTmemCols);
+      sm100::tmem_relinquish_pair();
+    } else {
+      sm100::tmem_alloc(tmem_slot, kTmemCols);
+      sm100::tmem_relinquish();
+    }
   }
   sm100::tc_fence_before();
   __syncthreads();
+  if constexpr (PAIR) sm100::cluster_sync();   // both CTAs' barriers initialised before any remote use
   sm100::tc_fence_after();
   rc::pdl_trigger();
   rc::pdl_wait();   // the previous kernel's outputs (our A operand) are visible from here
@@ -232,10 +249,32 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
       uint32_t phase = 0;
       long long issued = 0;
       bool ok = true;
-      for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
+      for (int u = unit0; u < num_units && ok; u += unit_step) {
         const Unit un = unit_of(p, u);
         int mb, nb;
         tile_coords(p, un.tile, mb, nb);
+        if constexpr (PAIR) {
+          // Each CTA loads its own 128 A rows, its half of B's rows, its A
+          // scale atoms and all of B's; the loads count on the leader's full
+          // barrier, which the leader arms with both CTAs' bytes.
+          constexpr uint32_t kSfBox = 4 * kSfAtomBytes;
+          constexpr uint32_t kCtaBytes = S::kA + S::kB + kSfBox + (BN / 128) * kSfBox;
+          const int mrow = mb * 2 + (int)rank;
+          for (int kt = un.kt0; kt < un.kt1; ++kt) {
+            if (!wait(&empty[stage], phase ^ 1, 1)) { ok = false; break; }
+            const uint32_t full_leader = sm100::mapa(sm100::smem_u32(&full[stage]), 0);
+            if (leader) sm100::mbar_arrive_expect_tx(&full[stage], 2 * kCtaBytes);
+            sm100::tma_load_2d_pair(smem + S::offA + stage * S::kA, &tmap_a, full_leader, kt * kRowBytes, mrow * BM);
+            sm100::tma_load_2d_pair(smem + S::offB + stage * S::kB, &tmap_b, full_leader, kt * kRowBytes,
+                                    nb * BN + (int)rank * (BN / 2));
+            sm100::tma_load_3d_pair(smem + S::offSfa + stage * S::kSfa, &tmap_sfa, full_leader, 0, kt * 16, mrow);
+            for (int r = 0; r < BN / 128; ++r)
+              sm100::tma_load_3d_pair(smem + S::offSfb + stage * S::kSfb + r * kSfBox, &tmap_sfb, full_leader, 0,
+                                      kt * 16, nb * (BN / 128) + r);
+            ++issued;
+            if (++stage == STAGES) { stage = 0; phase ^= 1; }
+          }
+        } else {
         for (int kt = un.kt0; kt < un.kt1; ++kt) {
           if (!wait(&empty[stage], phase ^ 1, 1)) { ok = false; break; }
           uint32_t bytes = S::kA + S::kB;
@@ -272,8 +311,13 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
           ++issued;
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }
+        }
       }
       // Drain: every load this thread issued must land before the CTA exits.
+      // (In a pair the loads of both CTAs count on the leader's barriers, so
+      // the leader drains for both; the final cluster barrier keeps the other
+      // CTA resident until then.)
+      if (PAIR && !leader) issued = 0;
       for (int s = 0; s < STAGES && issued > 0; ++s, --issued) {
         if (stage == 0) { stage = STAGES; phase ^= 1; }
         --stage;
@@ -282,9 +326,9 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    if (sm100::elect_one_sync()) {
+    if (leader && sm100::elect_one_sync()) {
       uint32_t idesc;
-      if constexpr (KIND == KIND_NVF4) idesc = sm100::idesc_nvf4(BM, BN);
+      if constexpr (KIND == KIND_NVF4) idesc = sm100::idesc_nvf4(PAIR ? 2 * BM : BM, BN);
       else if constexpr (KIND == KIND_E4M3) idesc = sm100::idesc_e4m3(BM, BN);
       else idesc = sm100::idesc_bf16(BM, BN, 0, 0);
       int stage = 0;
@@ -304,23 +348,37 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
       // One k-step j (0..3) of a k-tile: its scale copies (block-scaled kinds)
       // and its MMA.
       auto copy_sf = [&](int j, uint32_t sfa_t, uint32_t sfb_t, uint64_t dsa, uint64_t dsb) {
-        sm100::tmem_cp_32x128b_warpx4(sfa_t + 4 * j, sm100::desc_add(dsa, j * kSfAtomBytes));
+        if constexpr (PAIR) {
+          sm100::tmem_cp_32x128b_warpx4_pair(sfa_t + 4 * j, sm100::desc_add(dsa, j * kSfAtomBytes));
 #pragma unroll
-        for (int r = 0; r < BN / 128; ++r)
-          sm100::tmem_cp_32x128b_warpx4(sfb_t + j * (BN / 32) + 4 * r,
-                                        sm100::desc_add(dsb, (r * 4 + j) * kSfAtomBytes));
+          for (int r = 0; r < BN / 128; ++r)
+            sm100::tmem_cp_32x128b_warpx4_pair(sfb_t + j * (BN / 32) + 4 * r,
+                                               sm100::desc_add(dsb, (r * 4 + j) * kSfAtomBytes));
+        } else {
+          sm100::tmem_cp_32x128b_warpx4(sfa_t + 4 * j, sm100::desc_add(dsa, j * kSfAtomBytes));
+#pragma unroll
+          for (int r = 0; r < BN / 128; ++r)
+            sm100::tmem_cp_32x128b_warpx4(sfb_t + j * (BN / 32) + 4 * r,
+                                          sm100::desc_add(dsb, (r * 4 + j) * kSfAtomBytes));
+        }
       };
       auto mma = [&](int j, uint32_t d_tmem, uint64_t da, uint64_t db, uint32_t sfa_t, uint32_t sfb_t,
                      uint32_t acc) {
         const uint64_t a = sm100::desc_add(da, 32 * j), b = sm100::desc_add(db, 32 * j);
-        if constexpr (KIND == KIND_NVF4)
+        if constexpr (KIND == KIND_NVF4 && PAIR)
+          sm100::mma_nvf4_ss_pair(d_tmem, a, b, idesc, sfa_t + 4 * j, sfb_t + j * (BN / 32), acc);
+        else if constexpr (KIND == KIND_NVF4)
           sm100::mma_nvf4_ss(d_tmem, a, b, idesc, sfa_t + 4 * j, sfb_t + j * (BN / 32), acc);
         else if constexpr (KIND == KIND_E4M3)
           sm100::mma_f8f6f4_ss(d_tmem, a, b, idesc, acc);
         else
           sm100::mma_f16_ss(d_tmem, a, b, idesc, acc);
       };
-      for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x, ++local) {
+      auto commit = [&](uint64_t* bar) {
+        if constexpr (PAIR) sm100::tc_commit_pair(bar);   // arrives in both CTAs
+        else sm100::tc_commit(bar);
+      };
+      for (int u = unit0; u < num_units && ok; u += unit_step, ++local) {
         const Unit un = unit_of(p, u);
         const int as = local % kAcc;
         const uint32_t acc_parity = (uint32_t)((local / kAcc) & 1);
@@ -360,14 +418,17 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
             }
             for (int j = 0; j < steps; ++j) mma(j, d_tmem, da, db, sfa_t, sfb_t, (kt != un.kt0) | (j != 0));
           }
-          sm100::tc_commit(&empty[stage]);
+          commit(&empty[stage]);
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }
         if (!ok) break;
-        sm100::tc_commit(&acc_full[as]);
+        commit(&acc_full[as]);
       }
-      // Make sure no MMA is still writing TMEM when the CTA tears down.
-      sm100::tc_commit(done);
+      // Make sure no MMA is still writing TMEM when the CTA (pair) tears down.
+      commit(done);
+      sm100::mbar_wait(done, 0);
+    } else if (PAIR && !leader && sm100::elect_one_sync()) {
+      // The leader's last commit also arrives here: let it land before leaving.
       sm100::mbar_wait(done, 0);
     }
   } else {
@@ -378,7 +439,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
     const int quad = warp & 3;                 // TMEM lane quadrant of this warp
     const int part = (warp - 2) >> 2;          // which share of the tile's columns
     const int row_in_tile = quad * 32 + lane;
-    constexpr int kCols = BN / (epi_warps<EPI>() / 4);
+    constexpr int kCols = BN / (epi_warps<EPI, PAIR>() / 4);
     int local = 0;
     float alpha = p.alpha;
     if constexpr (KIND == KIND_E4M3) {
@@ -387,11 +448,22 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
     }
     int* s_flags = reinterpret_cast<int*>(done + 4);   // [0] last unit of the tile, [1] a warp failed
     if (threadIdx.x == 64) s_flags[1] = 0;
-    asm volatile("bar.sync 1, %0;" ::"r"(32 * epi_warps<EPI>()) : "memory");
-    for (int u = blockIdx.x; u < num_units; u += gridDim.x, ++local) {
+    asm volatile("bar.sync 1, %0;" ::"r"(32 * epi_warps<EPI, PAIR>()) : "memory");
+    // Accumulator release: every epilogue thread has read its columns.
+    auto release = [&](int as) {
+      sm100::tc_fence_before();
+      if constexpr (PAIR) {
+        __syncwarp();
+        if (lane == 0) sm100::mbar_arrive_cluster(sm100::mapa(sm100::smem_u32(&acc_empty[as]), 0));
+      } else {
+        sm100::mbar_arrive(&acc_empty[as]);
+      }
+    };
+    for (int u = unit0; u < num_units; u += unit_step, ++local) {
       const Unit un = unit_of(p, u);
       int mb, nb;
       tile_coords(p, un.tile, mb, nb);
+      if constexpr (PAIR) mb = mb * 2 + (int)rank;   // this CTA's 128-row block of the pair's tile
       const int as = local % kAcc;
       const bool got = __all_sync(0xffffffffu, wait(&acc_full[as], (uint32_t)((local / kAcc) & 1), 4));
       if (!got && (BN != 128 || un.piece < 0)) break;
@@ -430,8 +502,10 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
         const int n0 = nb * BN + part * kCols + cc;
         if (n0 >= p.N) return;
         if (!row_ok) {
-          // Padding rows of the next linear's scale atoms must read as zero.
-          if constexpr (EPI == EPI_GELU_NVF4) p.q_sf[rc::sf_offset(row, n0 >> 4, (p.N + 63) >> 6)] = 0;
+          // Padding rows of the next linear's scale atoms must read as zero
+          // (a pair's last tile may reach past the padded rows: skip those).
+          if constexpr (EPI == EPI_GELU_NVF4)
+            if (row < ((p.M + 127) & ~127)) p.q_sf[rc::sf_offset(row, n0 >> 4, (p.N + 63) >> 6)] = 0;
           return;
         }
         // y = bf16(acc * alpha + bias), two columns per packed fp32 op.
@@ -524,15 +598,14 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
           s_flags[1] = 1;
         }
         __threadfence();
-        asm volatile("bar.sync 1, %0;" ::"r"(32 * epi_warps<EPI>()) : "memory");
+        asm volatile("bar.sync 1, %0;" ::"r"(32 * epi_warps<EPI, PAIR>()) : "memory");
         const int tail_tile = un.tile - p.n_regular;
         if (threadIdx.x == 64)
           s_flags[0] = !s_flags[1] && atomicAdd(&p.counters[tail_tile], 1) == p.split - 1;
-        asm volatile("bar.sync 1, %0;" ::"r"(32 * epi_warps<EPI>()) : "memory");
+        asm volatile("bar.sync 1, %0;" ::"r"(32 * epi_warps<EPI, PAIR>()) : "memory");
         if (s_flags[1]) break;
         if (!s_flags[0]) {
-          sm100::tc_fence_before();
-          sm100::mbar_arrive(&acc_empty[as]);      // accumulator free: next tile may start
+          release(as);                             // accumulator free: next tile may start
           continue;
         }
         __threadfence();   // acquire: the other units' partials are visible from here
@@ -586,8 +659,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
           emit_chunk(cc, a16, cur);
           cur = nxt;
         }
-        sm100::tc_fence_before();
-        sm100::mbar_arrive(&acc_empty[as]);      // accumulator free
+        release(as);                             // accumulator free
       } else {
         // Other epilogues: drain the tile's columns from TMEM into registers
         // and release the accumulator first, so the next tile's MMAs overlap
@@ -598,8 +670,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
         for (int c = 0; c < kCols; c += 16)
           sm100::tmem_ld16(t_row + c, *reinterpret_cast<uint32_t(*)[16]>(&acc[c]));
         sm100::tmem_ld_wait();
-        sm100::tc_fence_before();
-        sm100::mbar_arrive(&acc_empty[as]);      // accumulator free: next tile may start
+        release(as);                             // accumulator free: next tile may start
 #pragma unroll
         for (int cc = 0; cc < kCols; cc += 16) emit_chunk(cc, &acc[cc], load_ops(cc));
       }
@@ -608,10 +679,14 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
 
   sm100::tc_fence_before();
   __syncthreads();
+  // A pair's CTAs leave together: the leader's MMAs read the other CTA's
+  // shared memory and write its tensor memory until its `done` wait returns.
+  if constexpr (PAIR) sm100::cluster_sync();
   if (warp == 1) {
     __syncwarp();
     sm100::tc_fence_after();
-    sm100::tmem_dealloc(tmem, kTmemCols);
+    if constexpr (PAIR) sm100::tmem_dealloc_pair(tmem, kTmemCols);
+    else sm100::tmem_dealloc(tmem, kTmemCols);
   }
 }
 
@@ -639,33 +714,67 @@ void plan_split(int tiles, int sms, bool can_split, GemmParams& p) {
 constexpr long long kSplitPartBytes = (long long)kMaxPieces * BM * 128 * 4;
 constexpr long long kSplitWorkspaceBytes = kSplitPartBytes + kMaxPieces * 4;
 
-template <int KIND, int BN, int STAGES, int EPI>
-int launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, cudaStream_t stream,
-           const char* what) {
-  using S = Smem<KIND, BN, STAGES>;
-  auto kern = gemm_kernel<KIND, BN, STAGES, EPI>;
+// The four tensor maps of a launch: A and B operand rows, and (CTA pairs
+// only) A's and B's scale atoms viewed as [row blocks][4 * k atoms][128 B].
+struct Maps {
+  CUtensorMap a, b, sfa, sfb;
+};
+
+template <int KIND, int BN, int STAGES, int EPI, bool PAIR>
+int launch(const Maps& m, const GemmParams& p, cudaStream_t stream, const char* what) {
+  using S = Smem<KIND, BN, STAGES, PAIR>;
+  auto kern = gemm_kernel<KIND, BN, STAGES, EPI, PAIR>;
   static rc::SmemAttrFlags attr_flags = {};
   if (const int st = rc::ensure_smem_attr(attr_flags, reinterpret_cast<const void*>(kern), S::kAlloc, what))
     return st;
   const int tiles = p.m_blocks * p.n_blocks;
   const int sms = rc::sm_count();
   GemmParams q = p;
+  if constexpr (PAIR) {
+    // One 2-CTA cluster per pair of SMs, each walking whole 256 x 256 tiles.
+    q.n_regular = tiles;
+    q.split = 1;
+    const int pairs = tiles < sms / 2 ? tiles : sms / 2;
+    return rc::check_launch(rc::launch_pdl_cluster(kern, dim3(2 * pairs), dim3(gemm_threads<EPI, PAIR>()), S::kAlloc,
+                                                   stream, 2, m.a, m.b, m.sfa, m.sfb, q),
+                            what);
+  }
   plan_split(tiles, sms, BN == 128 && p.part != nullptr, q);
   const int units = q.n_regular + (tiles - q.n_regular) * q.split;
   const int grid = units < sms ? units : sms;
-  return rc::check_launch(rc::launch_pdl(kern, grid, dim3(gemm_threads<EPI>()), S::kAlloc, stream, ta, tb, q), what);
+  return rc::check_launch(rc::launch_pdl(kern, grid, dim3(gemm_threads<EPI>()), S::kAlloc, stream, m.a, m.b,
+                                         m.a, m.b, q), what);
 }
 
-template <int KIND, int BN, int STAGES>
-int dispatch_epi(int epi, const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p,
-                 cudaStream_t stream, const char* what) {
+template <int KIND, int BN, int STAGES, bool PAIR = false>
+int dispatch_epi(int epi, const Maps& m, const GemmParams& p, cudaStream_t stream, const char* what) {
   switch (epi) {
-    case EPI_BIAS: return launch<KIND, BN, STAGES, EPI_BIAS>(ta, tb, p, stream, what);
-    case EPI_GATED_RESIDUAL: return launch<KIND, BN, STAGES, EPI_GATED_RESIDUAL>(ta, tb, p, stream, what);
-    case EPI_RESIDUAL: return launch<KIND, BN, STAGES, EPI_RESIDUAL>(ta, tb, p, stream, what);
-    case EPI_GELU_NVF4: return launch<KIND, BN, STAGES, EPI_GELU_NVF4>(ta, tb, p, stream, what);
+    case EPI_BIAS: return launch<KIND, BN, STAGES, EPI_BIAS, PAIR>(m, p, stream, what);
+    case EPI_GATED_RESIDUAL: return launch<KIND, BN, STAGES, EPI_GATED_RESIDUAL, PAIR>(m, p, stream, what);
+    case EPI_RESIDUAL: return launch<KIND, BN, STAGES, EPI_RESIDUAL, PAIR>(m, p, stream, what);
+    case EPI_GELU_NVF4: return launch<KIND, BN, STAGES, EPI_GELU_NVF4, PAIR>(m, p, stream, what);
   }
   return rc::set_error(RC_ERR_ARG, "%s: unknown epilogue %d", what, epi);
+}
+
+// Whether an NVFP4 GEMM runs on CTA pairs (256 x 256 tiles over two SMs):
+// one MMA-issuing thread feeds 256 rows, each SM stages only half of B and a
+// quarter less operand data per FLOP crosses L2. Measured (B200, same box,
+// A/B against the single-CTA kernel; per-k-tile timestamps of the issuing
+// thread): a pair keeps its tensor pipes busy to within ~15% once a tile has
+// many k-tiles (7040 x 3072 x 14336: 118.7 vs 145.0 us, 5.2 PFLOP/s), but its
+// single 256-column accumulator (two would not fit tensor memory beside the
+// scale factors) is handed to the epilogue with the tensor pipe idle for
+// ~2-3k cycles per tile, which a 12-k-tile tile (K = 3072) does not amortize,
+// and 256 x 256 tiles quantize coarsely onto 74 SM pairs. So pairs take the
+// GEMMs with at least two waves of pair tiles and a long K or a wide N
+// (ffn_up 1760 x 14336 x 3072: 44.7 vs 46.2 us; M = 3520 / 7040 with K or
+// N = 14336: 7-18% faster); the N = 3072 linears at M = 1760 (o-proj, cross,
+// ffn_down with its tail split) and QKV stay on single CTAs.
+bool gemm_use_pair(int kind, int M, int N, int K) {
+  if (kind != KIND_NVF4 || N % 256) return false;
+  const long long pair_tiles = (long long)((M + 255) / 256) * (N / 256);
+  return pair_tiles >= rc::sm_count() && (K >= 8192 || N >= 12288);
 }
 
 // Tile width. 128 x 256 tiles (single accumulator, register-drained
@@ -702,17 +811,34 @@ int run_gemm(int kind, int epi, const void* a, const void* b, int M, int N, int 
     return rc::set_error(RC_ERR_ARG, "%s: GELU/NVFP4 epilogue needs codes, scales and N %% 64 == 0", what);
   if (M == 0) return RC_OK;
   const uint64_t row_bytes = (uint64_t)K * ebx2 / 2;
-  CUtensorMap ta, tb;
+  Maps maps;
   const uint64_t da[2] = {row_bytes, (uint64_t)M}, db[2] = {row_bytes, (uint64_t)N};
   const uint64_t sa[1] = {row_bytes}, sb[1] = {row_bytes};
-  const bool wide = gemm_prefer_wide(epi, M, N, K);
+  const bool pair = gemm_use_pair(kind, M, N, K);
+  const bool wide = !pair && gemm_prefer_wide(epi, M, N, K);
   const uint32_t boxa[2] = {128, 128}, boxb[2] = {128, (uint32_t)(wide ? 256 : 128)};
-  int r = rc::encode_tmap(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(a), da, sa, boxa,
+  int r = rc::encode_tmap(&maps.a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(a), da, sa, boxa,
                           CU_TENSOR_MAP_SWIZZLE_128B, what);
   if (r) return r;
-  r = rc::encode_tmap(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(b), db, sb, boxb,
+  r = rc::encode_tmap(&maps.b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(b), db, sb, boxb,
                       CU_TENSOR_MAP_SWIZZLE_128B, what);
   if (r) return r;
+  if (pair) {
+    // Scale atoms (512 B = 128 rows x 4 k-blocks) as 128-byte lines: one box
+    // is a k-tile's 4 atoms of one 128-row block; lines past the last atom
+    // (K % 256 != 0) and row blocks past the matrix read as zero.
+    const uint64_t katoms = (uint64_t)(K + 63) / 64;
+    const uint64_t dsa[3] = {128, 4 * katoms, (uint64_t)(M + 127) / 128};
+    const uint64_t dsb[3] = {128, 4 * katoms, (uint64_t)(N + 127) / 128};
+    const uint64_t ss[2] = {128, katoms * kSfAtomBytes};
+    const uint32_t box[3] = {128, 16, 1};
+    r = rc::encode_tmap(&maps.sfa, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<uint8_t*>(p.sfa), dsa, ss, box,
+                        CU_TENSOR_MAP_SWIZZLE_NONE, what);
+    if (r) return r;
+    r = rc::encode_tmap(&maps.sfb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<uint8_t*>(p.sfb), dsb, ss, box,
+                        CU_TENSOR_MAP_SWIZZLE_NONE, what);
+    if (r) return r;
+  }
   const int ept = kind == KIND_NVF4 ? 256 : (kind == KIND_E4M3 ? 128 : 64);
   p.M = M;
   p.N = N;
@@ -727,16 +853,23 @@ int run_gemm(int kind, int epi, const void* a, const void* b, int M, int N, int 
   // operands in row-fastest order). Smaller GEMMs keep row-fastest order.
   const double operand_bytes = ((double)M + (double)N) * (double)row_bytes;
   p.group_m = operand_bytes > 64e6 && p.m_blocks > 12 ? 12 : p.m_blocks;
+  if (pair) {
+    p.m_blocks = (M + 2 * BM - 1) / (2 * BM);     // 256-row tiles
+    p.n_blocks = N / 256;
+    p.group_m = operand_bytes > 64e6 && p.m_blocks > 6 ? 6 : p.m_blocks;
+    p.part = nullptr;                             // no split-K on pairs
+    return dispatch_epi<KIND_NVF4, 256, 5, true>(epi, maps, p, stream, what);
+  }
   if (wide) {
     p.n_blocks = N / 256;
-    if (kind == KIND_NVF4) return dispatch_epi<KIND_NVF4, 256, 4>(epi, ta, tb, p, stream, what);
-    if (kind == KIND_E4M3) return dispatch_epi<KIND_E4M3, 256, 4>(epi, ta, tb, p, stream, what);
-    return dispatch_epi<KIND_BF16, 256, 4>(epi, ta, tb, p, stream, what);
+    if (kind == KIND_NVF4) return dispatch_epi<KIND_NVF4, 256, 4>(epi, maps, p, stream, what);
+    if (kind == KIND_E4M3) return dispatch_epi<KIND_E4M3, 256, 4>(epi, maps, p, stream, what);
+    return dispatch_epi<KIND_BF16, 256, 4>(epi, maps, p, stream, what);
   }
   p.n_blocks = (N + 127) / 128;
-  if (kind == KIND_NVF4) return dispatch_epi<KIND_NVF4, 128, 6>(epi, ta, tb, p, stream, what);
-  if (kind == KIND_E4M3) return dispatch_epi<KIND_E4M3, 128, 6>(epi, ta, tb, p, stream, what);
-  return dispatch_epi<KIND_BF16, 128, 6>(epi, ta, tb, p, stream, what);
+  if (kind == KIND_NVF4) return dispatch_epi<KIND_NVF4, 128, 6>(epi, maps, p, stream, what);
+  if (kind == KIND_E4M3) return dispatch_epi<KIND_E4M3, 128, 6>(epi, maps, p, stream, what);
+  return dispatch_epi<KIND_BF16, 128, 6>(epi, maps, p, stream, what);
 }
 
 }  // namespace

@@ -266,3 +266,66 @@ def test_nvfp4_gemm_grouped_raster_matches_row_chunks():
     chunks = torch.cat([run(a[r:r + 1760]) for r in range(0, m, 1760)])
     assert_no_device_error()
     assert torch.equal(full, chunks)
+
+
+def _pair_rows(m):
+    """Sampled 128-row blocks: first, middle, last (ragged)."""
+    mid = (m // 2) // 128 * 128
+    return np.r_[0:128, mid:mid + 128, m - 128:m]
+
+
+@pytest.mark.parametrize("epi", ["gated", "residual"])
+def test_nvfp4_gemm_pair_residual_epilogues(epi):
+    """3520 x 3072 x 14336 runs on CTA pairs (256 x 256 tiles over two SMs):
+    the in-place residual epilogues against the oracle on sampled rows."""
+    from recavsr_b200 import _lib
+    from recavsr_b200.runtime import nvfp4
+    m, n, k = 3520, 3072, 14336
+    a, w, bias, ac, asf, wc, wsf = _operands(m, n, k, seed=51)
+    rs = np.random.RandomState(52)
+    h0 = recipes.bf16_normal(rs, (m, n))
+    gate = rs.standard_normal(n).astype(np.float32)
+    out = dev_bf16(h0)
+    gd = torch.from_numpy(gate).cuda()
+    code = _lib.EPI_GATED_RESIDUAL if epi == "gated" else _lib.EPI_RESIDUAL
+    da, dsa, dw, dsw, db = dev_u8(ac), dev_u8(asf), dev_u8(wc), dev_u8(wsf), dev_bf16(bias)
+    ws = nvfp4.split_workspace(da.device)
+    _lib.call("rc_nvfp4_gemm_ws", da.data_ptr(), dsa.data_ptr(), dw.data_ptr(), dsw.data_ptr(), db.data_ptr(),
+              m, n, k, 1.0, code, out.data_ptr(), n, gd.data_ptr() if epi == "gated" else None, None, None, 1.0,
+              ws.data_ptr(), ws.numel(), _lib.stream())
+    assert_no_device_error()
+    rows = _pair_rows(m)
+    rc_, rsf = onv.quantize(a[rows])
+    y = onv.nvfp4_mm(rc_, rsf, wc, wsf, bias, len(rows), n, k)
+    add = y * gate[None, :] if epi == "gated" else y
+    ref = bf16_round(h0[rows] + bf16_round(add))
+    assert max_rel(host(out)[rows], ref) < TOL
+
+
+def test_nvfp4_gemm_pair_gelu_ragged_rows():
+    """M = 3400 has 27 row blocks of 128, so the last 256-row pair tile's
+    second CTA lies wholly past the matrix: its rows must be skipped, the
+    scale atoms of the padding rows (3400..3455) written as zero and nothing
+    written past them. GELU + NVFP4 epilogue, N = 14336 (pair path)."""
+    from recavsr_b200 import _lib
+    from recavsr_b200.runtime.nvfp4 import scale_numel
+    m, n, k = 3400, 14336, 3072
+    a, w, bias, ac, asf, wc, wsf = _operands(m, n, k, seed=53)
+    pad = 4096                                   # canary bytes after the scale buffer
+    qs_all = torch.full((scale_numel(m, n) + pad,), 0xAB, dtype=torch.uint8, device="cuda")
+    qc = torch.empty(m, n // 2, dtype=torch.uint8, device="cuda")
+    out = torch.empty(m, n, dtype=torch.bfloat16, device="cuda")
+    _lib_gemm(_lib.EPI_GELU_NVFP4, m, n, k, dev_u8(ac), dev_u8(asf), dev_u8(wc), dev_u8(wsf),
+              dev_bf16(bias), out, qc=qc, qs=qs_all)
+    assert_no_device_error()
+    qs = qs_all[:scale_numel(m, n)].cpu().numpy()
+    assert (qs_all[scale_numel(m, n):].cpu().numpy() == 0xAB).all()          # nothing past the buffer
+    sf = onv.unswizzle_scales(qs, (m + 127) // 128 * 128, n)
+    assert (sf[m:] == 0).all()                                               # padding rows zeroed
+    rows = _pair_rows(m)
+    rc_, rsf = onv.quantize(a[rows])
+    y = bf16_round(gelu_tanh(onv.nvfp4_mm(rc_, rsf, wc, wsf, bias, len(rows), n, k)))
+    yo = host(out)
+    assert max_rel(yo[rows], y) < TOL
+    ec, es = onv.quantize(yo[m - 128:m])
+    np.testing.assert_array_equal(qc.cpu().numpy()[m - 128:m], ec)
