@@ -16,6 +16,7 @@ on the GPU is its own code: the Triton `_paired_local` kernel, `sdpa_attention`
     python baseline/compare.py local       # cfg5: 22x40-window attention at 1920x1088 and 3840x2176
     python baseline/compare.py layers      # cfg4: the 30-layer DiT loop, PreparedBlock x 30 compiled
     python baseline/compare.py pipeline    # frame preparation (enlarge + normalize + pad) and strip blend
+    python baseline/compare.py decoder     # FlashDecoder local GQA attention (its Triton forward)
     python baseline/compare.py all
 
 This library's side is imported from recavsr_b200.runtime (ops, fp8, block):
@@ -272,6 +273,51 @@ def case_local(rows, reps):
         del q, ck, cv, pk, pv, out, ref_out
 
 
+def visible_pairs(h, w, qf, nf, window, group_size, temporal_window):
+    """(query, key) pairs the FlashDecoder mask admits, counted per axis."""
+    import numpy as np
+
+    def axis(n, win):
+        d = np.arange(n)[:, None] - np.arange(n)[None, :]      # key - query
+        return int(((d >= -(win // 2)) & (d < win // 2)).sum())
+    frames = 0
+    for qt in range(qf):
+        qg = (qt + nf - qf) // group_size
+        frames += sum(1 for kt in range(nf) if qg - temporal_window < kt // group_size <= qg)
+    return frames * axis(h, window[0]) * axis(w, window[1])
+
+
+def case_decoder(rows, reps):
+    """FlashDecoder's local attention (flashdecoder_wan22.py:38-119) at its
+    decoder geometry: 8 query heads on 2 KV heads, head_dim 64, 24x24 window;
+    the backbone step (1 new frame, 2-frame window) and the temporal
+    refinement (4 new frames, 8-frame window), at 704x1280 (44x80 latent) and
+    1088x1920 (68x120) frames, bf16. The reference runs its Triton forward
+    (_local_attention_triton.py:21-131)."""
+    from recavsr_b200.runtime.flashdecoder import local_attention as ours_fd
+    from recavsr_infer.models.flashdecoder.flashdecoder_wan22 import _local_attention as ref_fd
+    g = torch.Generator(device="cuda").manual_seed(4)
+    for h, w in ((44, 80), (68, 120)):
+        n = h * w
+        for qf, nf, batch in ((1, 2, 1), (4, 8, 1), (4, 8, 4)):
+            kw = dict(height=h, width=w, window=(24, 24), group_size=qf, temporal_window=2)
+            q = torch.randn(batch, 8, qf * n, 64, device="cuda", generator=g).to(torch.bfloat16)
+            k = torch.randn(batch, 2, nf * n, 64, device="cuda", generator=g).to(torch.bfloat16)
+            v = torch.randn(batch, 2, nf * n, 64, device="cuda", generator=g).to(torch.bfloat16)
+            ref_out = ref_fd(q, k, v, **kw)
+            out = ours_fd(q, k, v, **kw)
+            torch.cuda.synchronize()
+            diff = float((out.float() - ref_out.float()).abs().max())
+            t_o = graph_time(lambda: ours_fd(q, k, v, **kw), reps)
+            t_r = graph_time(lambda: ref_fd(q, k, v, **kw), reps)
+            fl = 4.0 * 64 * 8 * batch * visible_pairs(h, w, qf, nf, (24, 24), qf, 2)
+            emit(rows, case="decoder", geometry=f"{w * 16}x{h * 16} ({h}x{w} latent), batch {batch}, "
+                 f"{qf} query frames on {nf}", ours_us=t_o * 1e6, ref_us=t_r * 1e6,
+                 ours_tflops=fl / t_o / 1e12, ref_tflops=fl / t_r / 1e12, speedup=t_r / t_o,
+                 max_abs_diff=diff, ref="flashdecoder_wan22._local_attention (Triton forward)")
+            del q, k, v, out, ref_out
+
+
 # ------------------------------------------------------------- the layer loop
 class _FP32LayerNorm(nn.LayerNorm):
     """diffusers FP32LayerNorm as the released block uses it (norm1/norm3 without
@@ -510,7 +556,7 @@ def case_pipeline(rows, reps):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=["gemm", "attention", "local", "layers", "pipeline", "all"])
+    ap.add_argument("case", choices=["gemm", "attention", "local", "layers", "pipeline", "decoder", "all"])
     ap.add_argument("--reps", type=int, default=10)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
@@ -520,7 +566,7 @@ def main():
     torch.cuda.set_device(0)
     torch._dynamo.config.recompile_limit = 64     # one compiled graph per shape, as the reference allows
     rows = []
-    todo = ["gemm", "attention", "local", "layers", "pipeline"] if args.case == "all" else [args.case]
+    todo = ["gemm", "attention", "local", "layers", "pipeline", "decoder"] if args.case == "all" else [args.case]
     for c in todo:
         if c == "gemm":
             case_gemm(rows, args.reps)
@@ -530,6 +576,8 @@ def main():
             case_local(rows, args.reps)
         elif c == "pipeline":
             case_pipeline(rows, args.reps)
+        elif c == "decoder":
+            case_decoder(rows, args.reps)
         else:
             case_layers(rows, args.steps, args.warmup)
         torch.cuda.empty_cache()

@@ -238,6 +238,21 @@ int rc_unpatchify_residual(const void* pred, long long ldp, const float* noise, 
                            void* recycle, int C, int F, int H, int W, int ph, int pw,
                            int recycle_frames, rc_stream_t stream);
 
+/* ---- FlashDecoder ----------------------------------------------------------- */
+/* Replaces recavsr_infer/models/flashdecoder/_local_attention_triton.py:21-131
+ * (the Triton forward called by flashdecoder_wan22.py:38-119 `_local_attention`):
+ * streaming local grouped-query attention. q [B, HQ, QF*H*W, D], k / v
+ * [B, HK, NF*H*W, D], fp16 (fp16 = 1) or bf16, head dim contiguous, element
+ * strides[9] = (batch, head, token) of q, k, v (multiples of 8). Query head h
+ * reads key / value head h / (HQ / HK); a query of frame qt sees the key frames
+ * of temporal groups (qg - temporal_window, qg], qg = (qt + NF - QF) / group_size,
+ * and within a frame the keys at dy in [-window_h/2, window_h/2), dx in
+ * [-window_w/2, window_w/2), truncated at the grid border. out [B, HQ, QF*H*W, D]
+ * contiguous, in q's type. D = 64 (RC_ERR_UNSUPPORTED otherwise). */
+int rc_local_gqa_attention(const void* q, const void* k, const void* v, const long long* strides, int B,
+                           int HQ, int HK, int QF, int NF, int H, int W, int D, int window_h, int window_w,
+                           int group_size, int temporal_window, int fp16, void* out, rc_stream_t stream);
+
 /* ---- frame preparation and strip blending -------------------------------- */
 /* Replaces recavsr_infer/video.py:153-179 (`enlarge_block` + `block_tensor`,
  * called by `prepare_block` :138-150): src = `valid` uint8 RGB frames [h, w, 3]

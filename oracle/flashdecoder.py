@@ -15,13 +15,14 @@ from __future__ import annotations
 import numpy as np
 
 
-def visibility(height, width, qf, nf, window, group_size, temporal_window):
-    """Boolean mask [qf*n, nf*n] of flashdecoder_wan22.py:91-107."""
+def visibility(height, width, qf, nf, window, group_size, temporal_window, query_rows=None):
+    """Boolean mask [qf*n, nf*n] of flashdecoder_wan22.py:91-107 (only the
+    rows `query_rows` when given)."""
     n = height * width
     wh, ww = window
     k = np.arange(nf * n)
     kg, ky, kx = k // (group_size * n), (k % n) // width, k % width
-    q = np.arange(qf * n)
+    q = np.arange(qf * n) if query_rows is None else np.asarray(query_rows)
     qg = (q // n + nf - qf) // group_size
     dy = ky[None, :] - ((q % n) // width)[:, None]
     dx = kx[None, :] - (q % width)[:, None]
@@ -29,16 +30,19 @@ def visibility(height, width, qf, nf, window, group_size, temporal_window):
             & (dy >= -(wh // 2)) & (dy < wh // 2) & (dx >= -(ww // 2)) & (dx < ww // 2))
 
 
-def local_gqa_attention(q, k, v, height, width, window, group_size, temporal_window):
-    """q [B, HQ, QF*n, D], k / v [B, HK, NF*n, D] -> [B, HQ, QF*n, D] (float32)."""
+def local_gqa_attention(q, k, v, height, width, window, group_size, temporal_window, query_rows=None):
+    """q [B, HQ, QF*n, D], k / v [B, HK, NF*n, D] -> [B, HQ, QF*n, D] (float32);
+    with `query_rows`, only those query tokens: [B, HQ, len(query_rows), D]."""
     b, hq, tq, d = q.shape
     hk, tk = k.shape[1], k.shape[2]
     n = height * width
     qf, nf = tq // n, tk // n
     if tq % n or tk % n or qf % group_size or nf % group_size or nf < qf or hq % hk:
         raise ValueError("Invalid local grid, GQA heads or temporal group alignment.")
-    mask = visibility(height, width, qf, nf, window, group_size, temporal_window)
-    out = np.empty((b, hq, tq, d), np.float32)
+    mask = visibility(height, width, qf, nf, window, group_size, temporal_window, query_rows)
+    if query_rows is not None:
+        q = q[:, :, np.asarray(query_rows)]
+    out = np.empty((b, hq, q.shape[2], d), np.float32)
     q64, k64, v64 = (np.asarray(x, np.float64) for x in (q, k, v))
     for bi in range(b):
         for h in range(hq):

@@ -47,6 +47,7 @@ _SIGNATURES = {
     "rc_patchify": [_P, _I, _LL, _LL, _LL, _I, _I, _I, _I, _I, _I, _P, _LL, _P],
     "rc_enlarge_block": [_P, _LL, _LL, _I, _I, _I, _I, _I, _I, _I, _P, _P],
     "rc_strip_blend": [_I, _P, _P, _P, _P, _P, _P, _I, _I, _P, _LL, _P],
+    "rc_local_gqa_attention": [_P, _P, _P, _P] + [_I] * 13 + [_P, _P],
     "rc_unpatchify_residual": [_P, _LL, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _P],
 }
 _RESTYPES = {"rc_paired_attention_workspace": C.c_longlong, "rc_gemm_split_workspace": C.c_longlong,

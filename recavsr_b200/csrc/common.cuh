@@ -41,7 +41,7 @@ static __device__ unsigned int g_rc_device_error;
 // Kernel ids stored in the low byte of the error word.
 enum RcKernelId : unsigned int {
   kKernQuant = 1, kKernGemmNvf4 = 2, kKernGemmFp8 = 3, kKernAttention = 4,
-  kKernGlue = 5, kKernCache = 6,
+  kKernGlue = 5, kKernCache = 6, kKernDecoderAttention = 7,
 };
 
 namespace rc {

@@ -101,6 +101,7 @@ unsigned int rc_take_device_error_glue();
 unsigned int rc_take_device_error_gemm_nvf4();
 unsigned int rc_take_device_error_gemm_fp8();
 unsigned int rc_take_device_error_attention();
+unsigned int rc_take_device_error_decoder_attention();
 
 extern "C" {
 
@@ -114,7 +115,7 @@ int rc_read_device_error(unsigned int* word) {
   if (!word) return rc::set_error(RC_ERR_ARG, "rc_read_device_error: null output");
   unsigned int all[] = {rc_take_device_error_quant(), rc_take_device_error_glue(),
                         rc_take_device_error_gemm_nvf4(), rc_take_device_error_gemm_fp8(),
-                        rc_take_device_error_attention()};
+                        rc_take_device_error_attention(), rc_take_device_error_decoder_attention()};
   *word = 0;
   for (unsigned int v : all)
     if (v && !*word) *word = v;

@@ -7,12 +7,11 @@
     python -m recavsr_b200.profile_case quant        # NVFP4 quantizer 1760x3072
     python -m recavsr_b200.profile_case ln           # LayerNorm+AdaLN+NVFP4 1760x3072
     python -m recavsr_b200.profile_case rms          # RMSNorm+spatial RoPE of q and k, 1760x3072 each
-    python -m recavsr_b200.profile_case gemm_sweep   # NVFP4 / FP8 linears, M x (K, N) sweep + quantizers
-    python -m recavsr_b200.profile_case attention_sweep  # 30-layer routed attention, scopes 0/1/2/4/8
+    python -m recavsr_b200.profile_case gemm_cfg3_long_k   # NVFP4 7040x3072x14336 (CTA-pair tiles)
+    python -m recavsr_b200.profile_case decoder      # FlashDecoder local GQA attention, 704x1280 refinement step
     python -m recavsr_b200.profile_case lq_conv1     # LQ projector conv1: im2col + bf16 GEMM, body block
     python -m recavsr_b200.profile_case lq_conv2     # LQ projector conv2: im2col + bf16 GEMM, body block
     python -m recavsr_b200.profile_case lq_norm      # channel RMSNorm + SiLU, 14080 x 2048
-    python -m recavsr_b200.profile_case gemm_vs_cublas   # NVFP4 GEMM vs the reference's _scaled_mm_v2 (cuBLASLt)
 
 Each case allocates fresh inputs (a few hundred MB at most), captures `--reps`
 launches in a CUDA graph, replays it and prints the mean CUDA-event time per
@@ -31,28 +30,28 @@ from .runtime.ops import quantize, scale_numel
 M, DIM, FFN, HEADS, HD, H, W = 1760, 3072, 14336, 24, 128, 22, 40
 
 
-def _gemm(n, k, epi):
+def _gemm(n, k, epi, m=M):
     g = torch.Generator(device="cuda")
     g.manual_seed(0)
-    a = torch.randn(M, k, generator=g, device="cuda").bfloat16()
+    a = torch.randn(m, k, generator=g, device="cuda").bfloat16()
     w = (torch.randn(n, k, generator=g, device="cuda") * 0.02).bfloat16()
     ac, asf = quantize(a)
     wc, wsf = quantize(w)
     bias = torch.zeros(n, dtype=torch.bfloat16, device="cuda")
-    out = torch.randn(M, n, generator=g, device="cuda").bfloat16()
+    out = torch.randn(m, n, generator=g, device="cuda").bfloat16()
     gate = torch.ones(n, device="cuda")
-    qc = torch.empty(M, n // 2, dtype=torch.uint8, device="cuda")
-    qs = torch.empty(scale_numel(M, n), dtype=torch.uint8, device="cuda")
+    qc = torch.empty(m, n // 2, dtype=torch.uint8, device="cuda")
+    qs = torch.empty(scale_numel(m, n), dtype=torch.uint8, device="cuda")
     lib = _lib.library()
     sws = torch.zeros(lib.rc_gemm_split_workspace(), dtype=torch.uint8, device="cuda")
 
     def run():
         _lib.check(lib.rc_nvfp4_gemm_ws(ac.data_ptr(), asf.data_ptr(), wc.data_ptr(), wsf.data_ptr(),
-                                        bias.data_ptr(), M, n, k, 1.0, epi,
+                                        bias.data_ptr(), m, n, k, 1.0, epi,
                                         None if epi == _lib.EPI_GELU_NVFP4 else out.data_ptr(), n,
                                         gate.data_ptr(), qc.data_ptr(), qs.data_ptr(), 1.0,
                                         sws.data_ptr(), sws.numel(), _lib.stream()), "gemm")
-    return run, 2.0 * M * n * k, "TFLOP/s"
+    return run, 2.0 * m * n * k, "TFLOP/s"
 
 
 def _attention(planes=4, h=H, w=W, window=None):
@@ -206,7 +205,31 @@ def _lq_norm():
     return run, 2.0 * 2 * 14080 * 2048, "GB/s"
 
 
+def _decoder(h=44, w=80, qf=4, nf=8, batch=1):
+    """FlashDecoder local attention (8 query heads on 2 KV heads, head_dim
+    64, 24x24 window, groups of qf frames, 2 groups visible), bf16."""
+    from .runtime.flashdecoder import local_attention
+    g = torch.Generator(device="cuda")
+    g.manual_seed(0)
+    n = h * w
+    q = torch.randn(batch, 8, qf * n, 64, generator=g, device="cuda").bfloat16()
+    k = torch.randn(batch, 2, nf * n, 64, generator=g, device="cuda").bfloat16()
+    v = torch.randn(batch, 2, nf * n, 64, generator=g, device="cuda").bfloat16()
+    kw = dict(height=h, width=w, window=(24, 24), group_size=qf, temporal_window=2)
+
+    def axis(size):
+        d = torch.arange(size)[:, None] - torch.arange(size)[None, :]
+        return int(((d >= -12) & (d < 12)).sum())
+    frames = sum(min(nf, ((t + nf - qf) // qf + 1) * qf) - max(0, ((t + nf - qf) // qf - 1) * qf)
+                 for t in range(qf))
+    return (lambda: local_attention(q, k, v, **kw)), 4.0 * 64 * 8 * batch * frames * axis(h) * axis(w), "TFLOP/s"
+
+
 CASES = {
+    "decoder": _decoder,
+    "decoder_backbone": lambda: _decoder(qf=1, nf=2),
+    "gemm_cfg3_long_k": lambda: _gemm(DIM, FFN, _lib.EPI_BIAS, m=7040),
+    "gemm_cfg3_wide_n": lambda: _gemm(FFN, DIM, _lib.EPI_BIAS, m=7040),
     "lq_conv1": lambda: _lq_conv(1),
     "lq_conv2": lambda: _lq_conv(2),
     "lq_norm": _lq_norm,
@@ -250,150 +273,14 @@ def _graph_time(run, reps):
     return a.elapsed_time(b) / reps * 1e-3
 
 
-def _cfg3_operands(m, n, k, g):
-    """Activation N(0,1) with 0.1% of the entries x20 (outliers), weight N(0, 0.02)."""
-    a = torch.randn(m, k, generator=g, device="cuda")
-    mask = torch.rand(m, k, generator=g, device="cuda") < 1e-3
-    a = torch.where(mask, a * 20, a).bfloat16()
-    w = (torch.randn(n, k, generator=g, device="cuda") * 0.02).bfloat16()
-    return a, w
-
-
-def gemm_sweep(reps=10):
-    """NVFP4 / FP8 linear sweep: M in {1760, 3520, 7040} x (K, N) in {(3072, 3072),
-    (3072, 14336), (14336, 3072)}, bias epilogue, plus the NVFP4 and FP8
-    quantizers on the activation (GB/s of algorithmic bytes)."""
-    from .runtime import fp8
-    lib = _lib.library()
-    g = torch.Generator(device="cuda")
-    g.manual_seed(2)
-    print("path   M     K      N      us       TFLOP/s  | quant us  GB/s")
-    for m in (1760, 3520, 7040):
-        for k, n in ((3072, 3072), (3072, 14336), (14336, 3072)):
-            a, w = _cfg3_operands(m, n, k, g)
-            bias = torch.zeros(n, dtype=torch.bfloat16, device="cuda")
-            out = torch.empty(m, n, dtype=torch.bfloat16, device="cuda")
-            ac, asf = quantize(a)
-            wc, wsf = quantize(w)
-
-            def nvf4():
-                _lib.check(lib.rc_nvfp4_gemm(ac.data_ptr(), asf.data_ptr(), wc.data_ptr(), wsf.data_ptr(),
-                                             bias.data_ptr(), m, n, k, 1.0, _lib.EPI_BIAS, out.data_ptr(), n,
-                                             None, None, None, 1.0, _lib.stream()), "nvfp4_gemm")
-
-            def nvf4_quant():
-                quantize(a)
-            t = _graph_time(nvf4, reps)
-            tq = _graph_time(nvf4_quant, reps)
-            print(f"nvfp4 {m:5d} {k:6d} {n:6d} {t * 1e6:8.1f} {2.0 * m * n * k / t / 1e12:9.1f}"
-                  f"  | {tq * 1e6:7.1f} {m * k * 2.5625 / tq / 1e9:7.1f}")
-            aq, sa = fp8.quantize(a)
-            wq, sw = fp8.quantize(w)
-
-            def f8():
-                _lib.check(lib.rc_fp8_gemm(aq.data_ptr(), sa.data_ptr(), wq.data_ptr(), sw.data_ptr(),
-                                           bias.data_ptr(), m, n, k, 1.0, _lib.EPI_BIAS, out.data_ptr(), n,
-                                           None, _lib.stream()), "fp8_gemm")
-
-            def f8_quant():
-                fp8.quantize(a)
-            t = _graph_time(f8, reps)
-            tq = _graph_time(f8_quant, reps)
-            print(f"fp8   {m:5d} {k:6d} {n:6d} {t * 1e6:8.1f} {2.0 * m * n * k / t / 1e12:9.1f}"
-                  f"  | {tq * 1e6:7.1f} {m * k * 3.0 / tq / 1e9:7.1f}")
-            del a, w, ac, asf, wc, wsf, aq, wq, out
-
-
-def gemm_vs_cublas(reps=10):
-    """The reference's own NVFP4 GEMM call (recavsr_infer/runtime/nvfp4.py:22-39:
-    torch._scaled_mm_v2, BlockWise1x16 scales in the 32x4x4 swizzle, bias, bf16
-    out -- cuBLASLt) next to rc_nvfp4_gemm on the same codes and scales (the
-    quantizer's output is byte-identical to the reference's), cfg3 shapes; also
-    the largest difference between the two outputs relative to max |cuBLAS|."""
-    lib = _lib.library()
-    if not hasattr(torch, "_scaled_mm_v2") or not hasattr(torch, "float4_e2m1fn_x2"):
-        raise SystemExit("this torch has no _scaled_mm_v2 / float4_e2m1fn_x2")
-    g = torch.Generator(device="cuda")
-    g.manual_seed(2)
-    print("M     K      N      ours us  TFLOP/s | cuBLAS us  TFLOP/s | ours/cuBLAS time  max diff")
-    for m in (1760, 3520, 7040):
-        for k, n in ((3072, 3072), (3072, 14336), (14336, 3072)):
-            a, w = _cfg3_operands(m, n, k, g)
-            bias = (torch.randn(n, generator=g, device="cuda") * 0.02).bfloat16()
-            out = torch.empty(m, n, dtype=torch.bfloat16, device="cuda")
-            ac, asf = quantize(a)
-            wc, wsf = quantize(w)
-
-            def ours():
-                _lib.check(lib.rc_nvfp4_gemm(ac.data_ptr(), asf.data_ptr(), wc.data_ptr(), wsf.data_ptr(),
-                                             bias.data_ptr(), m, n, k, 1.0, _lib.EPI_BIAS, out.data_ptr(), n,
-                                             None, None, None, 1.0, _lib.stream()), "nvfp4_gemm")
-
-            def cublas():
-                return torch._scaled_mm_v2(
-                    ac.view(torch.float4_e2m1fn_x2), wc.view(torch.float4_e2m1fn_x2).t(),
-                    [asf.view(torch.float8_e4m3fn)], [2], [1], [wsf.view(torch.float8_e4m3fn)], [2], [1],
-                    bias, torch.bfloat16)
-            ref = cublas()
-            ours()
-            torch.cuda.synchronize()
-            diff = float((out.float() - ref.float()).abs().max() / ref.float().abs().max())
-            t, tc = _graph_time(ours, reps), _graph_time(cublas, reps)
-            fl = 2.0 * m * n * k
-            print(f"{m:5d} {k:6d} {n:6d} {t * 1e6:8.1f} {fl / t / 1e12:8.1f} | {tc * 1e6:8.1f} "
-                  f"{fl / tc / 1e12:8.1f} | {t / tc:6.3f}  {diff:.2e}")
-            del a, w, ac, asf, wc, wsf, out, ref
-
-
-def attention_sweep(reps=5):
-    """Routed-attention microbenchmark: 30 layers x 24 heads x 128, T = 880
-    (22 x 40), 2-frame query block (1760 queries), layer i attends to
-    [0, 1, 2, 4, 8][i % 5] routed planes of an 8-plane ring plus the 2 current
-    frames; FLOPs count visible keys only: 4 d heads Nq T sum(scope + 2)."""
-    from .runtime.ops import routed_attention
-    from .runtime.block import rope_tables
-    g = torch.Generator(device="cuda")
-    g.manual_seed(1)
-    t = H * W
-    r = lambda *sh: (torch.randn(*sh, generator=g, device="cuda") / HD ** 0.5).bfloat16()
-    q, k, v = r(1, 2 * t, HEADS, HD), r(1, 2 * t, HEADS, HD), r(1, 2 * t, HEADS, HD)
-    ring_k, ring_v = r(1, 8 * t, HEADS, HD), r(1, 8 * t, HEADS, HD)
-    tb = rope_tables(HD, H, W, "cuda")
-    out = torch.empty_like(q)
-    calls = []
-    for layer in range(30):
-        scope = (0, 1, 2, 4, 8)[layer % 5]
-        slots = torch.full((8,), -1, dtype=torch.int32, device="cuda")
-        slots[:scope] = torch.arange(8 - scope, 8, dtype=torch.int32, device="cuda")
-        ppos = torch.zeros(8, dtype=torch.int32, device="cuda")
-        ppos[:scope] = torch.arange(12 - scope, 12, dtype=torch.int32, device="cuda")
-        calls.append((slots, ppos))
-    qpos = torch.tensor([12, 13], dtype=torch.int32, device="cuda")
-
-    def run():
-        for slots, ppos in calls:
-            routed_attention(q, k, v, ring_k, ring_v, slots, ppos, qpos, tb["temporal_cos"],
-                             tb["temporal_sin"], H, W, H, W, out=out)
-    flops = 4.0 * HD * HEADS * (2 * t) * t * sum((0, 1, 2, 4, 8)[i % 5] + 2 for i in range(30))
-    dt = _graph_time(run, reps)
-    print(f"attention sweep: {dt * 1e3:.3f} ms per 30-layer block, {flops / dt / 1e12:.1f} TFLOP/s "
-          f"({flops:.3e} FLOP, {flops / (2 * t):.3e} FLOP/token)")
-
-
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=sorted(CASES) + ["gemm_sweep", "attention_sweep", "gemm_vs_cublas"])
+    ap.add_argument("case", choices=sorted(CASES))
     ap.add_argument("--reps", type=int, default=20)
     ap.add_argument("--seconds", type=float, default=0.0,
                     help="also replay for this long and report the sustained per-launch time "
                          "(sample clocks / power alongside to see the power cap)")
     args = ap.parse_args()
-    if args.case == "gemm_sweep":
-        return gemm_sweep()
-    if args.case == "attention_sweep":
-        return attention_sweep()
-    if args.case == "gemm_vs_cublas":
-        return gemm_vs_cublas()
     run, work, unit = CASES[args.case]()
     for _ in range(3):
         run()
