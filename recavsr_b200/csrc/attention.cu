@@ -185,36 +185,9 @@ struct Ring {
 };
 
 using rc::pack_bf16x2;
-__device__ __forceinline__ float max3(float a, float b, float c) {   // three-input max (sm_100)
-  float d;
-  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
-  return d;
-}
-__device__ __forceinline__ float fast_exp2(float x) {   // MUFU ex2 (as tl.exp2)
-  float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
-
-// 2^x for two x <= 2^7 on the FMA pipe: x = j + f with j = rint(x) (by the
-// 1.5 * 2^23 rounding constant) and |f| <= 1/2; 2^f by a degree-4 polynomial
-// (coefficients fitted here: relative error <= 8.5e-6 on [-1/2, 1/2], far
-// below the bf16 rounding of P) and j added to the exponent field. x < -126
-// gives 0, as the flush-to-zero MUFU exp2 does.
-__device__ __forceinline__ float2 exp2_poly2(float2 x) {
-  constexpr float kRound = 12582912.0f;
-  const float2 xc = make_float2(fmaxf(x.x, -127.0f), fmaxf(x.y, -127.0f));
-  const float2 t = __fadd2_rn(xc, make_float2(kRound, kRound));
-  const float2 j = __fadd2_rn(t, make_float2(-kRound, -kRound));
-  const float2 f = __ffma2_rn(j, make_float2(-1.0f, -1.0f), xc);
-  float2 q = __ffma2_rn(make_float2(0.00925496f, 0.00925496f), f, make_float2(0.05585603f, 0.05585603f));
-  q = __ffma2_rn(q, f, make_float2(0.24031252f, 0.24031252f));
-  q = __ffma2_rn(q, f, make_float2(0.6931306f, 0.6931306f));
-  q = __ffma2_rn(q, f, make_float2(0.9999978f, 0.9999978f));
-  const float ex = __uint_as_float(__float_as_uint(q.x) + (__float_as_uint(t.x) << 23));
-  const float ey = __uint_as_float(__float_as_uint(q.y) + (__float_as_uint(t.y) << 23));
-  return make_float2(x.x < -126.0f ? 0.0f : ex, x.y < -126.0f ? 0.0f : ey);
-}
+using rc::exp2_poly2;
+using rc::fast_exp2;
+using rc::max3;
 
 // Rotates the bf16 pairs (even, odd) = (lo, hi) half of each word by the
 // angle of `pair0 + j` (fp32 math, bf16 rounding of each output).

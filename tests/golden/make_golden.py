@@ -6,6 +6,7 @@ Run where a checkout of the reference exists:
     TRITON_INTERPRET=1 python tests/golden/make_golden.py <reference checkout> --flashdecoder
     python tests/golden/make_golden.py <reference checkout> --fullsize  # fullsize_hashes.json
     python tests/golden/make_golden.py <reference checkout> --pipeline  # pipeline_outputs.npz
+    python tests/golden/make_golden.py <reference checkout> --decoder-step  # decoder_step_outputs.npz
     python tests/golden/make_golden.py <reference checkout> --pipeline-cuda [out.npz]
                                         # pipeline_cuda_outputs.npz (needs a CUDA device)
                                                                         # flashdecoder_outputs.npz
@@ -486,6 +487,35 @@ def gen_flashdecoder(out):
         out["fd_a_triton_fp16"] = res.numpy()          # fp16 values, stored as fp16
 
 
+def gen_decoder_step(out):
+    """FlashDecoder's streaming decode (models/flashdecoder/flashdecoder_wan22.py:759-874
+    through runtime/flashdecoder.py:140-175 FlashDecoderSession.step) on the CPU in
+    fp32, for each recipes.DECODER_CASES entry: the RGB chunk of every step (the
+    first step 1 frame, then 4), the hidden states leaving the backbone and the
+    temporal refinement of every step (forward hooks)."""
+    from recavsr_infer.models.flashdecoder.flashdecoder_wan22 import FlashDecoder
+    from recavsr_infer.runtime.flashdecoder import FlashDecoderSession
+    for tag, c in recipes.DECODER_CASES.items():
+        model = FlashDecoder(dim=c["dim"], depth=c["depth"], num_heads=c["num_heads"],
+                             num_kv_groups=c["num_kv_groups"], refinement_depth=c["refinement_depth"],
+                             mlp_ratio=c["mlp_ratio"], spatial_window_size=c["window"])
+        params = recipes.decoder_params(tag)
+        model.load_state_dict({k: torch.from_numpy(v) for k, v in params.items()}, strict=True)
+        model.eval()
+        latents, mean, std, lr_up = recipes.decoder_inputs(tag)
+        model.vae_config = {"latents_mean": mean.tolist(), "latents_std": std.tolist()}
+        seen = {"backbone": [], "refinement": []}
+        model.backbone.register_forward_hook(lambda m, a, o: seen["backbone"].append(o[0].detach().clone()))
+        model.temporal_refinement.register_forward_hook(
+            lambda m, a, o: seen["refinement"].append(o[0].detach().clone()))
+        session = FlashDecoderSession(model)
+        rgb = list(session.step(torch.from_numpy(latents), lr_up=torch.from_numpy(lr_up)))
+        for i, r in enumerate(rgb):
+            out[f"dec_{tag}_rgb{i}"] = r.numpy()
+            out[f"dec_{tag}_backbone{i}"] = seen["backbone"][i].numpy()
+            out[f"dec_{tag}_refine{i}"] = seen["refinement"][i].numpy()
+
+
 FULLSIZE_SHAPES = ((7040, 14336), (7040, 3072))     # cfg3's largest activations
 
 
@@ -618,6 +648,13 @@ def main():
         gen_pipeline(out)
         np.savez_compressed(os.path.join(HERE, "pipeline_outputs.npz"), **out)
         print("wrote", len(out), "pipeline arrays")
+        return
+    if "--decoder-step" in sys.argv:
+        torch.manual_seed(0)
+        out = {}
+        gen_decoder_step(out)
+        np.savez_compressed(os.path.join(HERE, "decoder_step_outputs.npz"), **out)
+        print("wrote", len(out), "decoder step arrays")
         return
     if "--flashdecoder" in sys.argv:
         out = {}

@@ -164,3 +164,80 @@ def lq_frames_u8(n: int, h: int, w: int, seed: int = 60) -> np.ndarray:
     x = rs.randint(0, 256, (n, h + 2, w + 2, 3)).astype(np.int32)
     acc = sum(x[:, dy:dy + h, dx:dx + w] for dy in range(3) for dx in range(3))
     return (acc // 9).astype(np.uint8)
+
+
+# FlashDecoder decode-step cases: model size (dim, query heads, KV heads,
+# backbone depth, refinement depth, mlp ratio), spatial window, latent grid
+# (h, w) and the number of decode steps. "s" is a small stand-in; "S" has the
+# released variant's widths (dim 512, 8 / 2 heads, SwiGLU 2048) at a reduced
+# depth and window.
+DECODER_CASES = {
+    "s": dict(dim=128, num_heads=2, num_kv_groups=1, depth=2, refinement_depth=1, mlp_ratio=2.0,
+              window=(4, 4), h=4, w=6, steps=4),
+    "S": dict(dim=512, num_heads=8, num_kv_groups=2, depth=2, refinement_depth=1, mlp_ratio=4.0,
+              window=(6, 6), h=6, w=8, steps=3),
+}
+
+
+def decoder_params(tag, seed=51):
+    """fp32 state dict of a FlashDecoder (the reference's parameter names,
+    flashdecoder_wan22.py:655-688) for one DECODER_CASES entry: linear weights
+    N(0, 1/fan_in), biases N(0, 0.02), norm weights 1 + N(0, 0.1)."""
+    c = DECODER_CASES[tag]
+    rs = np.random.RandomState(seed + ord(tag))
+    dim, hd = c["dim"], 64
+    kv = c["num_kv_groups"] * hd
+    hidden = int(dim * c["mlp_ratio"])
+    p = {}
+
+    def lin(name, n, k, bias=True):
+        p[name + ".weight"] = (rs.standard_normal((n, k)) / np.sqrt(k)).astype(np.float32)
+        if bias:
+            p[name + ".bias"] = (rs.standard_normal(n) * 0.02).astype(np.float32)
+
+    def norm(name, n):
+        p[name + ".weight"] = (1.0 + rs.standard_normal(n) * 0.1).astype(np.float32)
+
+    def block(prefix):
+        norm(prefix + "attention_norm", dim)
+        lin(prefix + "attention.query", dim, dim)
+        lin(prefix + "attention.key", kv, dim)
+        lin(prefix + "attention.value", kv, dim)
+        norm(prefix + "attention.key_norm", hd)
+        norm(prefix + "attention.value_norm", hd)
+        lin(prefix + "attention.output", dim, dim)
+        norm(prefix + "feed_forward_norm", dim)
+        lin(prefix + "feed_forward.gate", hidden, dim)
+        lin(prefix + "feed_forward.up", hidden, dim)
+        lin(prefix + "feed_forward.down", dim, hidden)
+
+    lin("latent_projection", dim, 48)
+    for i in range(c["depth"]):
+        block(f"backbone.blocks.{i}.")
+    lin("temporal_projection", 4 * dim, dim)
+    for i in range(c["refinement_depth"]):
+        block(f"temporal_refinement.blocks.{i}.")
+    lin("spatial_projection.0", hidden, dim)
+    lin("spatial_projection.2", 3 * 16 * 16, hidden)
+    lin("lr_stem", 48, 3 * 16 * 16)
+    lin("lr_early_projection", dim, 4 * 48, bias=False)
+    lin("lr_late_projection", dim, 48, bias=False)
+    return p
+
+
+def decoder_inputs(tag, seed=52):
+    """The decoder's streaming inputs for one case: normalized DiT latents
+    [1, 48, steps, h, w] N(0, 1); the latent normalization (mean N(0, 0.5),
+    std U(0.5, 2), 48 each); the target-resolution LQ frames lr_up
+    [1, 3, 1 + 4 (steps - 1), 16 h, 16 w] in [-1, 1] (uniform noise smoothed
+    over 4 x 4 pixels)."""
+    c = DECODER_CASES[tag]
+    rs = np.random.RandomState(seed + ord(tag))
+    steps, h, w = c["steps"], c["h"], c["w"]
+    latents = rs.standard_normal((1, 48, steps, h, w)).astype(np.float32)
+    mean = (rs.standard_normal(48) * 0.5).astype(np.float32)
+    std = rs.uniform(0.5, 2.0, 48).astype(np.float32)
+    frames = 1 + 4 * (steps - 1)
+    coarse = rs.uniform(-1, 1, (1, 3, frames, 4 * h, 4 * w)).astype(np.float32)
+    lr_up = np.repeat(np.repeat(coarse, 4, axis=3), 4, axis=4)
+    return latents, mean, std, np.ascontiguousarray(lr_up)

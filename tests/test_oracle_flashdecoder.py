@@ -53,3 +53,28 @@ def test_visibility_is_local_and_grouped():
     seen = sorted(int(k) % n for k in np.flatnonzero(m[q]) if k < 3 * n)
     assert seen == [1, 2, 5, 6]
     assert sorted(int(k) % n for k in np.flatnonzero(m[0]) if k < 3 * n) == [0]
+
+
+@pytest.mark.parametrize("tag", sorted(recipes.DECODER_CASES))
+def test_decode_step_matches_reference_session(tag):
+    """oracle.flashdecoder.DecoderOracle against the reference's own
+    FlashDecoderSession.step (fp32, CPU; tests/golden/decoder_step_outputs.npz,
+    `make_golden.py <reference> --decoder-step`): every step's RGB chunk and the
+    hidden states leaving the backbone and the temporal refinement, over enough
+    steps to trim both caches."""
+    g = np.load(os.path.join(ROOT, "tests", "golden", "decoder_step_outputs.npz"))
+    c = recipes.DECODER_CASES[tag]
+    lat, mean, std, lr = recipes.decoder_inputs(tag)
+    o = ofd.DecoderOracle(recipes.decoder_params(tag), dim=c["dim"], num_heads=c["num_heads"],
+                          num_kv_groups=c["num_kv_groups"], depth=c["depth"],
+                          refinement_depth=c["refinement_depth"], window=c["window"], mean=mean, std=std)
+    off = 0
+    for i in range(c["steps"]):
+        take = 1 if i == 0 else 4
+        rgb, backbone, refine = o.step(lat[0, :, i], lr[0, :, off:off + take])
+        off += take
+        # fp32 on both sides, different summation orders: measured <= 5e-6
+        np.testing.assert_allclose(rgb, g[f"dec_{tag}_rgb{i}"][0], rtol=0, atol=2e-5)
+        for name, got in (("backbone", backbone), ("refine", refine)):
+            ref = g[f"dec_{tag}_{name}{i}"][0]
+            assert np.abs(got - ref).max() <= 2e-6 * np.abs(ref).max(), (name, i)
