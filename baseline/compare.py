@@ -17,6 +17,7 @@ on the GPU is its own code: the Triton `_paired_local` kernel, `sdpa_attention`
     python baseline/compare.py layers      # cfg4: the 30-layer DiT loop, PreparedBlock x 30 compiled
     python baseline/compare.py pipeline    # frame preparation (enlarge + normalize + pad) and strip blend
     python baseline/compare.py decoder     # FlashDecoder local GQA attention (its Triton forward)
+    python baseline/compare.py decoder_step  # FlashDecoder decode step (its FlashDecoderSession, eager and compiled)
     python baseline/compare.py all
 
 This library's side is imported from recavsr_b200.runtime (ops, fp8, block):
@@ -32,6 +33,7 @@ from __future__ import annotations
 import argparse
 import json
 import os
+import statistics
 import sys
 import time
 import types
@@ -318,6 +320,58 @@ def case_decoder(rows, reps):
             del q, k, v, out, ref_out
 
 
+def case_decoder_step(rows, steps, warmup, h=44, w=80):
+    """The FlashDecoder decode step (flashdecoder_wan22.py:759-874) of the
+    released S variant (12 backbone + 2 refinement blocks, dim 512), random
+    weights, on a 704x1280 stream (44x80 latent grid): the reference's own
+    FlashDecoderSession (runtime/flashdecoder.py:54-175; bf16 autocast, eager
+    and torch.compile'd as --compile-decoder does) against DecoderSession with
+    CUDA-graph replay, per latent frame in the steady state (4 RGB frames out),
+    CUDA events; plus the largest RGB difference over the stream."""
+    from recavsr_b200.runtime.decoder import DecoderSession
+    from recavsr_infer.models.flashdecoder.flashdecoder_wan22 import FlashDecoder
+    from recavsr_infer.runtime.flashdecoder import FlashDecoderSession
+    torch.manual_seed(0)
+    model = FlashDecoder.from_variant("S").cuda().eval()
+    g = torch.Generator().manual_seed(1)
+    mean, std = torch.randn(48, generator=g) * 0.5, torch.rand(48, generator=g) * 1.5 + 0.5
+    model.vae_config = {"latents_mean": mean.tolist(), "latents_std": std.tolist()}
+    frames = warmup + steps + 2
+    lat = torch.randn(1, 48, frames, h, w, generator=g).cuda()
+    lr = (torch.rand(1, 3, 1 + 4 * (frames - 1), 16 * h, 16 * w, generator=g) * 2 - 1).cuda()
+    ours = DecoderSession.from_module(model, height=h, width=w, mean=mean, std=std)
+
+    def run(session, capture_at=None):
+        outs, times = [], []
+        off = 0
+        for i in range(frames):
+            take = 1 if i == 0 else 4
+            if capture_at is not None and i == capture_at:
+                session.capture()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            out = next(iter(session.step(lat[:, :, i:i + 1], lr_up=lr[:, :, off:off + take])))
+            b.record()
+            b.synchronize()
+            outs.append(out.float().clone())
+            times.append(a.elapsed_time(b) * 1e-3)
+            off += take
+        return outs, times[warmup + 2:]
+
+    with torch.inference_mode():
+        o_out, o_t = run(ours, capture_at=2)
+        r_out, r_t = run(FlashDecoderSession(model))
+        rc_out, rc_t = run(FlashDecoderSession(model, compile_decoder=True))
+    diff = max(float((a - b).abs().max()) for a, b in zip(o_out, r_out))
+    mean_diff = max(float((a - b).abs().mean()) for a, b in zip(o_out, r_out))
+    t_o, t_r, t_c = (statistics.median(t) for t in (o_t, r_t, rc_t))
+    emit(rows, case="decoder_step", geometry=f"{16 * w}x{16 * h} ({h}x{w} latent), S variant (12 + 2 blocks)",
+         ours_ms=t_o * 1e3, ref_eager_ms=t_r * 1e3, ref_compiled_ms=t_c * 1e3,
+         ours_out_fps=4 / t_o, ref_compiled_out_fps=4 / t_c, speedup_vs_compiled=t_c / t_o,
+         speedup_vs_eager=t_r / t_o, max_abs_diff=diff, max_mean_abs_diff=mean_diff,
+         ref="recavsr_infer.runtime.flashdecoder.FlashDecoderSession (bf16 autocast)")
+
+
 # ------------------------------------------------------------- the layer loop
 class _FP32LayerNorm(nn.LayerNorm):
     """diffusers FP32LayerNorm as the released block uses it (norm1/norm3 without
@@ -556,7 +610,8 @@ def case_pipeline(rows, reps):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=["gemm", "attention", "local", "layers", "pipeline", "decoder", "all"])
+    ap.add_argument("case", choices=["gemm", "attention", "local", "layers", "pipeline", "decoder", "decoder_step",
+                                     "all"])
     ap.add_argument("--reps", type=int, default=10)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
@@ -566,7 +621,8 @@ def main():
     torch.cuda.set_device(0)
     torch._dynamo.config.recompile_limit = 64     # one compiled graph per shape, as the reference allows
     rows = []
-    todo = ["gemm", "attention", "local", "layers", "pipeline", "decoder"] if args.case == "all" else [args.case]
+    todo = (["gemm", "attention", "local", "layers", "pipeline", "decoder", "decoder_step"] if args.case == "all"
+            else [args.case])
     for c in todo:
         if c == "gemm":
             case_gemm(rows, args.reps)
@@ -578,6 +634,8 @@ def main():
             case_pipeline(rows, args.reps)
         elif c == "decoder":
             case_decoder(rows, args.reps)
+        elif c == "decoder_step":
+            case_decoder_step(rows, args.steps, args.warmup)
         else:
             case_layers(rows, args.steps, args.warmup)
         torch.cuda.empty_cache()

@@ -253,6 +253,56 @@ int rc_local_gqa_attention(const void* q, const void* k, const void* v, const lo
                            int HQ, int HK, int QF, int NF, int H, int W, int D, int window_h, int window_w,
                            int group_size, int temporal_window, int fp16, void* out, rc_stream_t stream);
 
+/* FlashDecoder decode step glue (recavsr_infer/models/flashdecoder/flashdecoder_wan22.py,
+ * runtime/flashdecoder.py:140-175), bf16 in the reference's CUDA autocast arithmetic.
+ * Frame rings: a layer's K (fp32) / V (bf16) cache of `slots` frames is
+ * [heads][slots * n][64], element head stride ring_head; global frame g lives
+ * in slot g % slots. */
+
+/* runtime/flashdecoder.py:168: raw = bf16(bf16(bf16(latent) * std) + mean) of a
+ * normalized latent frame (fp32, channel c at latent + c * channel_stride, n
+ * tokens contiguous) as GEMM rows out [n, 64] bf16 (columns 48..63 zero). */
+int rc_fd_latent_in(const float* latent, long long channel_stride, int n, const void* mean, const void* stdv,
+                    void* out, rc_stream_t stream);
+
+/* flashdecoder_wan22.py:704-707: F.pixel_unshuffle(lr_up, 16) of `frames` LR
+ * frames (dtype 0 fp32 / 1 bf16; element strides[3] = channel, frame, row;
+ * pixels contiguous) -> bf16 [frames * h * w, 768], columns (c, i, j). */
+int rc_fd_lr_unshuffle(const void* lr, int dtype, const long long* strides, int frames, int h, int w, void* out,
+                       rc_stream_t stream);
+
+/* flashdecoder_wan22.py:708-719: LR features [F, n, 48] (row stride ldf) ->
+ * grouped [n, 192] (4 frames x 48) and late [4n, 64] (columns 48..63 zero);
+ * first != 0 repeats frame 0 four times (the first chunk). */
+int rc_fd_lr_group(const void* feats, long long ldf, int n, int first, void* grouped, void* late,
+                   rc_stream_t stream);
+
+/* flashdecoder_wan22.py:310-322: key_norm / value_norm (RMSNorm over each
+ * 64-dim head, fp32 weights) of the K / V columns of fused q|k|v rows (K at
+ * column q_cols, V at q_cols + 64 hk) into ring rows token0 .. token0 + tokens. */
+int rc_fd_kv_norm(const void* qkv, long long ldq, int tokens, int q_cols, int hk, const float* wk,
+                  const float* wv, float eps, float* k_ring, void* v_ring, long long ring_head, long long token0,
+                  rc_stream_t stream);
+
+/* flashdecoder_wan22.py:198-242,324-331: 3D RoPE of the current queries
+ * (temporal position prev + frame) into q_out [cur*n, hq*64], of the window's
+ * nf key frames (temporal positions 0..nf-1, ring slots (slot0 + t) % slots)
+ * into k_out [hk][nf*n][64] bf16, and the window's V frames into v_out.
+ * tables: fp32 cos_t [max_t][8] | sin_t | cos_h [h][12] | sin_h | cos_w [w][12] | sin_w. */
+int rc_fd_rope_gather(const void* qkv, long long ldq, int hq, int hk, int cur, int prev, int nf, int slot0,
+                      int slots, int h, int w, const float* k_ring, const void* v_ring, long long ring_head,
+                      const float* tables, int max_t, void* q_out, void* k_out, void* v_out, rc_stream_t stream);
+
+/* flashdecoder_wan22.py:344-345 (mode 0: out [M, H] = bf16(bf16(silu(x[:, :H])) * x[:, H:])
+ * from x [M, 2H]) and :680-684 (mode 1: x [M, H] = bf16(silu(x)) in place). */
+int rc_fd_silu(void* x, int M, int H, int mode, void* out, rc_stream_t stream);
+
+/* flashdecoder_wan22.py:845-866 + runtime/flashdecoder.py:175: frames f0 .. f0+frames-1
+ * of the spatial projection y [4n, 768] (row stride ldy) pixel-shuffled by 16
+ * into out [3, out_frames, 16h, 16w] bf16 (frames 0 .. frames-1), clamped to [-1, 1]. */
+int rc_fd_pixel_shuffle(const void* y, long long ldy, int f0, int frames, int out_frames, int h, int w, void* out,
+                        rc_stream_t stream);
+
 /* ---- frame preparation and strip blending -------------------------------- */
 /* Replaces recavsr_infer/video.py:153-179 (`enlarge_block` + `block_tensor`,
  * called by `prepare_block` :138-150): src = `valid` uint8 RGB frames [h, w, 3]

@@ -47,7 +47,14 @@ _SIGNATURES = {
     "rc_patchify": [_P, _I, _LL, _LL, _LL, _I, _I, _I, _I, _I, _I, _P, _LL, _P],
     "rc_enlarge_block": [_P, _LL, _LL, _I, _I, _I, _I, _I, _I, _I, _P, _P],
     "rc_strip_blend": [_I, _P, _P, _P, _P, _P, _P, _I, _I, _P, _LL, _P],
-    "rc_local_gqa_attention": [_P, _P, _P, _P] + [_I] * 13 + [_P, _P],
+    "rc_local_gqa_attention": [_P, _P, _P, _P] + [_I] * 13 + [_P, _P, _P],
+    "rc_fd_latent_in": [_P, _LL, _I, _P, _P, _P, _P],
+    "rc_fd_lr_unshuffle": [_P, _I, _P, _I, _I, _I, _P, _P],
+    "rc_fd_lr_group": [_P, _LL, _I, _I, _P, _P, _P],
+    "rc_fd_kv_norm": [_P, _LL, _I, _I, _I, _P, _P, _F, _P, _P, _LL, _LL, _P],
+    "rc_fd_rope_gather": [_P, _LL] + [_I] * 9 + [_P, _P, _LL, _P, _I, _P, _P, _P, _P],
+    "rc_fd_silu": [_P, _I, _I, _I, _P, _P],
+    "rc_fd_pixel_shuffle": [_P, _LL, _I, _I, _I, _I, _I, _P, _P],
     "rc_unpatchify_residual": [_P, _LL, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _P],
 }
 _RESTYPES = {"rc_paired_attention_workspace": C.c_longlong, "rc_gemm_split_workspace": C.c_longlong,

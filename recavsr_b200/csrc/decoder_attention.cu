@@ -56,7 +56,8 @@ struct FdParams {
   int tiles_y, tiles_x;
   float scale_log2;                    // D^-0.5 * log2(e)
   int fp16;
-  void* out;                           // [HQ, QF*n, D] of this batch item, contiguous
+  long long out_head, out_token;       // element strides of the output
+  void* out;                           // this batch item's output
 };
 
 // Instruction descriptor, kind::f16, fp32 accumulator, A / B bf16 or fp16.
@@ -389,7 +390,7 @@ fd_attention_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_con
         const float inv = 1.f / l;
         const long long n = (long long)p.H * p.W;
         uint8_t* dst = reinterpret_cast<uint8_t*>(p.out) +
-                       (((long long)hq * p.QF * n + (long long)qt * n + (long long)qy * p.W + qx) * kD) * 2;
+                       ((long long)hq * p.out_head + ((long long)qt * n + (long long)qy * p.W + qx) * p.out_token) * 2;
 #pragma unroll
         for (int d = 0; d < kD; d += 8) {
           uint4 w;
@@ -431,7 +432,8 @@ extern "C" {
 
 int rc_local_gqa_attention(const void* q, const void* k, const void* v, const long long* strides, int B,
                            int HQ, int HK, int QF, int NF, int H, int W, int D, int window_h, int window_w,
-                           int group_size, int temporal_window, int fp16, void* out, cudaStream_t stream) {
+                           int group_size, int temporal_window, int fp16, void* out,
+                           const long long* out_strides, cudaStream_t stream) {
   const char* what = "rc_local_gqa_attention";
   if (D != kD) return rc::set_error(RC_ERR_UNSUPPORTED, "%s: head_dim %d (64 supported)", what, D);
   if (B < 1 || HQ < 1 || HK < 1 || HQ % HK || H < 1 || W < 1 || QF < 1 || NF < QF || group_size < 1 ||
@@ -441,6 +443,13 @@ int rc_local_gqa_attention(const void* q, const void* k, const void* v, const lo
   if (!q || !k || !v || !out || !strides) return rc::set_error(RC_ERR_ARG, "%s: missing pointer", what);
   for (int i = 0; i < 9; ++i)
     if (strides[i] % 8) return rc::set_error(RC_ERR_ARG, "%s: strides must be multiples of 8 elements", what);
+  const long long n = (long long)H * W;
+  // Output strides (batch, head, token) in elements; NULL = contiguous [B, HQ, QF*n, D].
+  const long long ob = out_strides ? out_strides[0] : (long long)HQ * QF * n * kD;
+  const long long oh = out_strides ? out_strides[1] : (long long)QF * n * kD;
+  const long long ot = out_strides ? out_strides[2] : kD;
+  if (ob % 8 || oh % 8 || ot % 8 || ot < kD || (reinterpret_cast<uintptr_t>(out) & 15))
+    return rc::set_error(RC_ERR_ARG, "%s: output must be 16-byte aligned with strides in multiples of 8", what);
   const int ty = (H + kBH - 1) / kBH, tx = (W + kBW - 1) / kBW;
   if ((long long)QF * ty * tx > 2147483647LL || HQ > 65535)
     return rc::set_error(RC_ERR_ARG, "%s: grid too large", what);
@@ -448,7 +457,6 @@ int rc_local_gqa_attention(const void* q, const void* k, const void* v, const lo
   if (const int st = rc::ensure_smem_attr(attr_flags, reinterpret_cast<const void*>(fd_attention_kernel),
                                           Layout::kAlloc, what))
     return st;
-  const long long n = (long long)H * W;
   for (int b = 0; b < B; ++b) {
     // strides: (batch, head, token) of q, k, v in elements.
     const uint8_t* qb = reinterpret_cast<const uint8_t*>(q) + strides[0] * 2 * b;
@@ -460,8 +468,8 @@ int rc_local_gqa_attention(const void* q, const void* k, const void* v, const lo
     if (!r) r = make_map(&mv, vb, fp16, W, H, NF, HK, strides[8], strides[7], kKW, kKH, what);
     if (r) return r;
     FdParams p{H, W, QF, NF, HQ, HK, group_size, temporal_window, window_h, window_w, ty, tx,
-               1.4426950408889634f / sqrtf((float)kD), fp16 ? 1 : 0,
-               reinterpret_cast<uint8_t*>(out) + (long long)b * HQ * QF * n * kD * 2};
+               1.4426950408889634f / sqrtf((float)kD), fp16 ? 1 : 0, oh, ot,
+               reinterpret_cast<uint8_t*>(out) + b * ob * 2};
     r = rc::check_launch(rc::launch_pdl(fd_attention_kernel, dim3(QF * ty * tx, HQ), dim3(kThreads),
                                         Layout::kAlloc, stream, mq, mk, mv, p),
                          what);

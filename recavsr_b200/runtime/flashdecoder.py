@@ -55,5 +55,5 @@ def local_attention(query, key, value, *, height, width, window, group_size, tem
     strides = (C.c_longlong * 9)(*[s for t in (q, k, v) for s in t.stride()[:3]])
     _lib.call("rc_local_gqa_attention", q.data_ptr(), k.data_ptr(), v.data_ptr(), strides, q.shape[0],
               q.shape[1], k.shape[1], qf, nf, height, width, q.shape[-1], window[0], window[1], group_size,
-              temporal_window, int(q.dtype == torch.float16), out.data_ptr(), _lib.stream(q.device))
+              temporal_window, int(q.dtype == torch.float16), out.data_ptr(), None, _lib.stream(q.device))
     return out

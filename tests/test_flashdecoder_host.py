@@ -33,3 +33,13 @@ def test_argument_errors():
         local_attention(*_qkv(qf=3, nf=6), **kw)
     with pytest.raises(ValueError, match="CUDA fp16 / bf16"):
         local_attention(q, k, v, **kw)
+
+
+def test_decoder_session_rejects_unsupported_layouts():
+    from recavsr_b200.runtime.decoder import DecoderSession
+    with pytest.raises(ValueError, match="64-dimensional heads"):
+        DecoderSession({}, height=2, width=2, mean=[0.0] * 48, std=[1.0] * 48, dim=384, num_heads=8)
+    with pytest.raises(ValueError, match="two positive even integers"):
+        DecoderSession({}, height=2, width=2, mean=[0.0] * 48, std=[1.0] * 48, window=(3, 4))
+    with pytest.raises(ValueError, match="CUDA device"):
+        DecoderSession({}, height=2, width=2, mean=[0.0] * 48, std=[1.0] * 48, device="cpu")
