@@ -11,14 +11,24 @@ from .numerics import bf16_round, e4m3_decode, e4m3_encode
 FP8_MAX = 448.0
 
 
+def scale_of(amax) -> np.float32:
+    """fp8.py:41: max(amax, 1e-12) / 448 in fp32."""
+    return np.float32(max(np.float32(amax), np.float32(1e-12)) / np.float32(FP8_MAX))
+
+
+def encode(matrix: np.ndarray, scale) -> np.ndarray:
+    """fp8.py:42: e4m3(clamp(x / scale, -448, 448))."""
+    x = np.asarray(matrix, dtype=np.float32)
+    with np.errstate(invalid="ignore"):
+        z = np.clip((x / np.float32(scale)).astype(np.float32), -FP8_MAX, FP8_MAX)
+    return e4m3_encode(z)
+
+
 def quantize(matrix: np.ndarray) -> tuple[np.ndarray, np.float32]:
     """fp8.py:41-42: scale = max(amax, 1e-12)/448; q = e4m3(clamp(x/scale))."""
     x = np.asarray(matrix, dtype=np.float32)
-    amax = np.float32(np.abs(x).max()) if x.size else np.float32(0.0)
-    scale = np.float32(max(amax, np.float32(1e-12)) / np.float32(FP8_MAX))
-    with np.errstate(invalid="ignore"):
-        z = np.clip((x / scale).astype(np.float32), -FP8_MAX, FP8_MAX)
-    return e4m3_encode(z), scale
+    scale = scale_of(np.abs(x).max() if x.size else 0.0)
+    return encode(x, scale), scale
 
 
 def fp8_mm(a_q, scale_a, w_q, scale_w, bias) -> np.ndarray:

@@ -33,20 +33,22 @@ def bf16_from_bits(bits) -> np.ndarray:
 
 def e4m3_encode(x) -> np.ndarray:
     """float32 -> float8_e4m3fn byte, round-to-nearest-even, subnormals kept,
-    |x| >= 480 and NaN -> 0x7f (sign kept); equals torch's CPU cast."""
-    a32 = np.asarray(x, dtype=np.float32)
-    sign = ((a32.view(np.uint32) >> 24) & 0x80).astype(np.uint8)
-    a = np.abs(a32).astype(np.float64)
-    out = np.zeros(a.shape, dtype=np.int64)
-    sub = a < 2.0 ** -6
-    out[sub] = np.rint(a[sub] * 512.0).astype(np.int64)
-    nrm = ~sub & (a < 480.0)
-    m, e = np.frexp(a[nrm])
-    j = np.rint((2.0 * m - 1.0) * 8.0).astype(np.int64)
-    out[nrm] = ((e.astype(np.int64) + 6) << 3) + j
-    big = ~(a < 480.0)  # includes NaN
-    out[big] = 0x7F
-    return (out.astype(np.uint8) | sign)
+    |x| >= 480 and NaN -> 0x7f (sign kept); equals torch's CPU cast.
+
+    On the float32 bit pattern: a normal result rounds the 23-bit mantissa to
+    3 bits (ties to even) with the carry running into the exponent field, then
+    rebiases the exponent (127 -> 7); |x| < 2^-6 gives rint(|x| * 512)."""
+    a32 = np.ascontiguousarray(x, dtype=np.float32)
+    bits = a32.view(np.uint32)
+    sign = ((bits >> np.uint32(24)) & np.uint32(0x80)).astype(np.uint8)
+    mag = bits & np.uint32(0x7FFFFFFF)
+    normal = (mag + np.uint32(0x7FFFF) + ((mag >> np.uint32(20)) & np.uint32(1))) >> np.uint32(20)
+    code = normal.astype(np.int64) - (120 << 3)
+    a = mag.view(np.float32)
+    sub = mag < np.uint32(0x3C800000)                   # |x| < 2^-6
+    code = np.where(sub, np.rint(a * np.float32(512.0)).astype(np.int64), code)
+    code = np.where(mag >= np.uint32(0x43F00000), 0x7F, code)    # |x| >= 480 or NaN
+    return code.astype(np.uint8) | sign
 
 
 def e4m3_decode(b) -> np.ndarray:
