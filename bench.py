@@ -13,6 +13,11 @@ warm-up. Inputs/weights/caches (~4 GB) exceed L2 (126 MB), so no flush.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference] [--head-shard | --session]
 
+The default line also times, per stream, the whole one-step DiT step through
+its host-buffer entry (`e2e`, `out_fps`) and the whole pipeline of a body
+block (`pipeline`: LQ uint8 frames in -> enlarge -> DiT step -> FlashDecoder ->
+RGB frames out, the "720p x4 out frames/s" of the metric).
+
 Under torchrun each rank runs an independent stream (weak scaling, no
 collective); rank 0 prints one JSON line with the max-over-ranks time.
 --head-shard instead runs one 3840x2176 stream split by heads over the ranks
@@ -513,6 +518,135 @@ def measure_session(session, device, rank, world, steps, warm):
 
 
 SESSION_GLUE_LAUNCHES = 15   # 2 im2col, 2 channel norms, 7 bf16 GEMMs, 2 patch gathers, 1 LayerNorm, 1 unpatchify
+DEC_DIM, DEC_HIDDEN, DEC_DEPTH, DEC_REFINE = 512, 2048, 12, 2   # FlashDecoder-S (flashdecoder_wan22.py:590-600)
+# Launches of one decode step: 6 before the backbone, 10 per block, 5 between the
+# stacks, 4 after the refinement.
+DECODER_LAUNCHES = 6 + 10 * (DEC_DEPTH + DEC_REFINE) + 5 + 4
+
+
+def build_decoder(device, seed, h=44, w=80):
+    """Random-init FlashDecoder-S (the released variant: dim 512, 8 query / 2
+    KV heads, 12 backbone + 2 refinement blocks, SwiGLU 2048, 24x24 windows)
+    as a DecoderSession at the 704x1280 latent grid; linear weights
+    N(0, 1/fan_in), biases N(0, 0.02), norm weights 1 + N(0, 0.1), latent
+    normalization mean N(0, 0.5), std U(0.5, 2)."""
+    import torch
+    from recavsr_b200.runtime.decoder import DecoderSession
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    p = {}
+
+    def lin(name, n, k, bias=True):
+        p[name + ".weight"] = torch.randn(n, k, generator=g, device=device) / k ** 0.5
+        if bias:
+            p[name + ".bias"] = torch.randn(n, generator=g, device=device) * 0.02
+
+    def norm(name, n):
+        p[name + ".weight"] = 1 + torch.randn(n, generator=g, device=device) * 0.1
+
+    for prefix, depth in (("backbone", DEC_DEPTH), ("temporal_refinement", DEC_REFINE)):
+        for i in range(depth):
+            b = f"{prefix}.blocks.{i}."
+            norm(b + "attention_norm", DEC_DIM)
+            for name, n in (("query", DEC_DIM), ("key", 128), ("value", 128), ("output", DEC_DIM)):
+                lin(b + "attention." + name, n, DEC_DIM)
+            norm(b + "attention.key_norm", 64)
+            norm(b + "attention.value_norm", 64)
+            norm(b + "feed_forward_norm", DEC_DIM)
+            lin(b + "feed_forward.gate", DEC_HIDDEN, DEC_DIM)
+            lin(b + "feed_forward.up", DEC_HIDDEN, DEC_DIM)
+            lin(b + "feed_forward.down", DEC_DIM, DEC_HIDDEN)
+    lin("latent_projection", DEC_DIM, LATENT_C)
+    lin("temporal_projection", 4 * DEC_DIM, DEC_DIM)
+    lin("spatial_projection.0", DEC_HIDDEN, DEC_DIM)
+    lin("spatial_projection.2", 768, DEC_HIDDEN)
+    lin("lr_stem", LATENT_C, 768)
+    lin("lr_early_projection", DEC_DIM, 4 * LATENT_C, bias=False)
+    lin("lr_late_projection", DEC_DIM, LATENT_C, bias=False)
+    mean = torch.randn(LATENT_C, generator=g, device=device) * 0.5
+    std = torch.rand(LATENT_C, generator=g, device=device) * 1.5 + 0.5
+    return DecoderSession(p, height=h, width=w, mean=mean, std=std, dim=DEC_DIM, num_heads=8, num_kv_groups=2,
+                          depth=DEC_DEPTH, refinement_depth=DEC_REFINE, mlp_ratio=DEC_HIDDEN / DEC_DIM,
+                          device=device)
+
+
+def lq_u8(frames, seed):
+    """LQ RGB frames as a video decoder delivers them, uint8 [frames, 176, 320, 3]:
+    uniform noise smoothed by a 5x5 box filter (integer mean)."""
+    rs = np.random.RandomState(seed)
+    x = rs.randint(0, 256, (frames, 180, 324, 3)).astype(np.int32)
+    acc = sum(x[:, dy:dy + 176, dx:dx + 320] for dy in range(5) for dx in range(5))
+    return (acc // 25).astype(np.uint8)
+
+
+def measure_pipeline(session, decoder, device, rank, world, steps, warm):
+    """The whole per-block pipeline of one stream, timed end to end with CUDA
+    events: the block's 8 LQ uint8 frames (320x176) copied from pinned host
+    memory, enlarged, normalized and padded on the device (rc_enlarge_block,
+    video.py:138-179), the one-step DiT (StreamingSession.step: LQ projector,
+    patch embedding, 30 layers as a CUDA graph, head), the FlashDecoder on its
+    2 latent frames (DecoderSession, CUDA graphs) and the 8 RGB output frames
+    (704x1280, bf16) copied to pinned host memory, all on one stream. The
+    stream starts with its 21-frame prefix block; the decoder's graphs are
+    captured during warm-up. Returns (seconds, decoder seconds per body block,
+    h2d bytes, d2h bytes, clocks)."""
+    import torch
+    import torch.distributed as dist
+    from recavsr_b200 import _lib
+    from recavsr_b200.runtime.pipeline import enlarge_block
+    session.reset(seed=rank)
+    decoder.reset()
+    prefix = torch.from_numpy(lq_u8(21, 8 + rank)).pin_memory()
+    body = torch.from_numpy(lq_u8(8, 9 + rank)).pin_memory()
+    rgb_host = torch.empty((3, 8, 704, 1280), dtype=torch.bfloat16, pin_memory=True)
+    rgb_prefix = torch.empty((3, 21, 704, 1280), dtype=torch.bfloat16, pin_memory=True)
+
+    def block(host, n_rgb, out):
+        x = enlarge_block(host.to(device, non_blocking=True), (704, 1280), block=n_rgb, dtype=torch.bfloat16)
+        lat = session.step(x)
+        off = 0
+        for chunk in decoder.step(lat, lr_up=x):
+            f = chunk.shape[2]
+            out[:, off:off + f].copy_(chunk[0], non_blocking=True)
+            off += f
+        return lat
+
+    block(prefix, 21, rgb_prefix)
+    for i in range(warm):
+        if i == 1:
+            decoder.capture()
+        block(body, 8, rgb_host)
+    torch.cuda.synchronize(device)
+    dev_err = _lib.read_device_error()
+    if dev_err:
+        raise RuntimeError(f"device error word 0x{dev_err:08x}")
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(device)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(device.index or 0) as clk:
+        start.record()
+        for _ in range(steps):
+            block(body, 8, rgb_host)
+        end.record()
+        end.synchronize()
+    t = start.elapsed_time(end) * 1e-3
+    if not torch.isfinite(rgb_host.float()).all():
+        raise RuntimeError("non-finite decoder output")
+    # The decoder alone on the same inputs (steady-state body blocks, graphs).
+    lat = torch.randn((1, LATENT_C, BODY, 44, 80), device=device)
+    x = enlarge_block(body.to(device), (704, 1280), block=8, dtype=torch.bfloat16)
+    for _ in range(2):
+        list(decoder.step(lat, lr_up=x))
+    torch.cuda.synchronize(device)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(steps):
+        list(decoder.step(lat, lr_up=x))
+    b.record()
+    b.synchronize()
+    t_dec = a.elapsed_time(b) * 1e-3 / steps
+    return t, t_dec, body.numel(), rgb_host.numel() * 2, clk.summary()
 
 
 def run_session(args, rank, world, local):
@@ -602,7 +736,9 @@ def main():
     ap.add_argument("--session", action="store_true",
                     help="only the whole one-step DiT stream step (LQ projector, layers, head) per block")
     ap.add_argument("--no-session", action="store_true",
-                    help="skip the whole-step session measurement of the default line")
+                    help="skip the whole-step session and pipeline measurements of the default line")
+    ap.add_argument("--no-decoder", action="store_true",
+                    help="skip the whole-pipeline measurement (DiT step + FlashDecoder) of the default line")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
@@ -696,11 +832,17 @@ def main():
         from recavsr_b200.runtime.session import StreamingSession
         session = StreamingSession(stack, build_glue(device, 77 + rank), 704, 1280, seed=rank, graphs=True)
         ts, s_h2d, s_d2h, s_clk, _ = measure_session(session, device, rank, world, args.steps, warm)
+    # ---- the whole pipeline of a stream: LQ uint8 frames in, RGB frames out
+    tp = None
+    if not args.no_session and not args.no_decoder:
+        decoder = build_decoder(device, 91 + rank)
+        tp, t_dec, p_h2d, p_d2h, p_clk = measure_pipeline(session, decoder, device, rank, world, args.steps, warm)
     if world > 1:
-        tt = torch.tensor([t, te, ts or 0.0], device=device)
+        tt = torch.tensor([t, te, ts or 0.0, tp or 0.0], device=device)
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         t, te = float(tt[0]), float(tt[1])
         ts = float(tt[2]) if ts is not None else None
+        tp = float(tt[3]) if tp is not None else None
         dist.barrier()
         dist.destroy_process_group()
     if rank != 0:
@@ -772,6 +914,21 @@ def main():
                           "clocks": s_clk}
     else:
         out["out_fps"] = value * 4 / T
+    if tp is not None:
+        frames = 4 * BODY * args.steps * world
+        out["pipeline"] = {
+            "out_fps": frames / tp, "ms_per_body_block": tp / args.steps * 1e3,
+            "out_fps_per_gpu": frames / tp / world,
+            "decoder_ms_per_latent_frame": t_dec / BODY * 1e3,
+            "decoder_out_fps": 4 * BODY / t_dec,
+            "h2d_bytes_per_step": p_h2d, "d2h_bytes_per_step": p_d2h,
+            "gpu_launches": args.steps * (1 + layer_launches + SESSION_GLUE_LAUNCHES + BODY * DECODER_LAUNCHES),
+            "path": "per body block on one stream: 8 LQ uint8 frames 320x176 from pinned host -> rc_enlarge_block "
+                    "(bf16 704x1280) -> StreamingSession.step (one-step DiT) -> DecoderSession.step (FlashDecoder-S, "
+                    "2 latent frames, CUDA graphs) -> 8 RGB frames 704x1280 bf16 to pinned host",
+            "excluded": "video decode / encode and colour correction",
+            "clocks": p_clk,
+        }
     print(json.dumps(out), flush=True)
 
 
