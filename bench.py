@@ -527,47 +527,18 @@ DECODER_LAUNCHES = 6 + 10 * (DEC_DEPTH + DEC_REFINE) + 5 + 4
 def build_decoder(device, seed, h=44, w=80):
     """Random-init FlashDecoder-S (the released variant: dim 512, 8 query / 2
     KV heads, 12 backbone + 2 refinement blocks, SwiGLU 2048, 24x24 windows)
-    as a DecoderSession at the 704x1280 latent grid; linear weights
-    N(0, 1/fan_in), biases N(0, 0.02), norm weights 1 + N(0, 0.1), latent
-    normalization mean N(0, 0.5), std U(0.5, 2)."""
+    as a DecoderSession at the 704x1280 latent grid (weights from
+    runtime.decoder.random_params); latent normalization mean N(0, 0.5),
+    std U(0.5, 2)."""
     import torch
-    from recavsr_b200.runtime.decoder import DecoderSession
+    from recavsr_b200.runtime.decoder import DecoderSession, random_params
     g = torch.Generator(device=device)
-    g.manual_seed(seed)
-    p = {}
-
-    def lin(name, n, k, bias=True):
-        p[name + ".weight"] = torch.randn(n, k, generator=g, device=device) / k ** 0.5
-        if bias:
-            p[name + ".bias"] = torch.randn(n, generator=g, device=device) * 0.02
-
-    def norm(name, n):
-        p[name + ".weight"] = 1 + torch.randn(n, generator=g, device=device) * 0.1
-
-    for prefix, depth in (("backbone", DEC_DEPTH), ("temporal_refinement", DEC_REFINE)):
-        for i in range(depth):
-            b = f"{prefix}.blocks.{i}."
-            norm(b + "attention_norm", DEC_DIM)
-            for name, n in (("query", DEC_DIM), ("key", 128), ("value", 128), ("output", DEC_DIM)):
-                lin(b + "attention." + name, n, DEC_DIM)
-            norm(b + "attention.key_norm", 64)
-            norm(b + "attention.value_norm", 64)
-            norm(b + "feed_forward_norm", DEC_DIM)
-            lin(b + "feed_forward.gate", DEC_HIDDEN, DEC_DIM)
-            lin(b + "feed_forward.up", DEC_HIDDEN, DEC_DIM)
-            lin(b + "feed_forward.down", DEC_DIM, DEC_HIDDEN)
-    lin("latent_projection", DEC_DIM, LATENT_C)
-    lin("temporal_projection", 4 * DEC_DIM, DEC_DIM)
-    lin("spatial_projection.0", DEC_HIDDEN, DEC_DIM)
-    lin("spatial_projection.2", 768, DEC_HIDDEN)
-    lin("lr_stem", LATENT_C, 768)
-    lin("lr_early_projection", DEC_DIM, 4 * LATENT_C, bias=False)
-    lin("lr_late_projection", DEC_DIM, LATENT_C, bias=False)
+    g.manual_seed(seed + 1)
     mean = torch.randn(LATENT_C, generator=g, device=device) * 0.5
     std = torch.rand(LATENT_C, generator=g, device=device) * 1.5 + 0.5
-    return DecoderSession(p, height=h, width=w, mean=mean, std=std, dim=DEC_DIM, num_heads=8, num_kv_groups=2,
-                          depth=DEC_DEPTH, refinement_depth=DEC_REFINE, mlp_ratio=DEC_HIDDEN / DEC_DIM,
-                          device=device)
+    return DecoderSession(random_params(device, seed), height=h, width=w, mean=mean, std=std, dim=DEC_DIM,
+                          num_heads=8, num_kv_groups=2, depth=DEC_DEPTH, refinement_depth=DEC_REFINE,
+                          mlp_ratio=DEC_HIDDEN / DEC_DIM, device=device)
 
 
 def lq_u8(frames, seed):
@@ -586,7 +557,8 @@ def measure_pipeline(session, decoder, device, rank, world, steps, warm):
     video.py:138-179), the one-step DiT (StreamingSession.step: LQ projector,
     patch embedding, 30 layers as a CUDA graph, head), the FlashDecoder on its
     2 latent frames (DecoderSession, CUDA graphs) and the 8 RGB output frames
-    (704x1280, bf16) copied to pinned host memory, all on one stream. The
+    (704x1280, bf16) copied to pinned host memory on a copy stream that
+    overlaps the next frames' decode (DecoderSession.step_host). The
     stream starts with its 21-frame prefix block; the decoder's graphs are
     captured during warm-up. Returns (seconds, decoder seconds per body block,
     h2d bytes, d2h bytes, clocks)."""
@@ -604,18 +576,14 @@ def measure_pipeline(session, decoder, device, rank, world, steps, warm):
     def block(host, n_rgb, out):
         x = enlarge_block(host.to(device, non_blocking=True), (704, 1280), block=n_rgb, dtype=torch.bfloat16)
         lat = session.step(x)
-        off = 0
-        for chunk in decoder.step(lat, lr_up=x):
-            f = chunk.shape[2]
-            out[:, off:off + f].copy_(chunk[0], non_blocking=True)
-            off += f
-        return lat
+        return decoder.step_host(lat, x, out)      # RGB copies overlap the next frames' work
 
     block(prefix, 21, rgb_prefix)
     for i in range(warm):
         if i == 1:
             decoder.capture()
         block(body, 8, rgb_host)
+    decoder.sync_host()
     torch.cuda.synchronize(device)
     dev_err = _lib.read_device_error()
     if dev_err:
@@ -627,7 +595,8 @@ def measure_pipeline(session, decoder, device, rank, world, steps, warm):
     with ClockSampler(device.index or 0) as clk:
         start.record()
         for _ in range(steps):
-            block(body, 8, rgb_host)
+            st = block(body, 8, rgb_host)
+        torch.cuda.current_stream(device).wait_event(st.output_ready)
         end.record()
         end.synchronize()
     t = start.elapsed_time(end) * 1e-3
@@ -923,9 +892,10 @@ def main():
             "decoder_out_fps": 4 * BODY / t_dec,
             "h2d_bytes_per_step": p_h2d, "d2h_bytes_per_step": p_d2h,
             "gpu_launches": args.steps * (1 + layer_launches + SESSION_GLUE_LAUNCHES + BODY * DECODER_LAUNCHES),
-            "path": "per body block on one stream: 8 LQ uint8 frames 320x176 from pinned host -> rc_enlarge_block "
-                    "(bf16 704x1280) -> StreamingSession.step (one-step DiT) -> DecoderSession.step (FlashDecoder-S, "
-                    "2 latent frames, CUDA graphs) -> 8 RGB frames 704x1280 bf16 to pinned host",
+            "path": "per body block of one stream: 8 LQ uint8 frames 320x176 from pinned host -> rc_enlarge_block "
+                    "(bf16 704x1280) -> StreamingSession.step (one-step DiT) -> DecoderSession.step_host "
+                    "(FlashDecoder-S, 2 latent frames, CUDA graphs) -> 8 RGB frames 704x1280 bf16 to pinned host "
+                    "(copies on a side stream, overlapping the next frames); timed to the last frame's arrival",
             "excluded": "video decode / encode and colour correction",
             "clocks": p_clk,
         }

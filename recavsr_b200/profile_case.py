@@ -9,6 +9,7 @@
     python -m recavsr_b200.profile_case rms          # RMSNorm+spatial RoPE of q and k, 1760x3072 each
     python -m recavsr_b200.profile_case gemm_cfg3_long_k   # NVFP4 7040x3072x14336 (CTA-pair tiles)
     python -m recavsr_b200.profile_case decoder      # FlashDecoder local GQA attention, 704x1280 refinement step
+    python -m recavsr_b200.profile_case decoder_step # one FlashDecoder-S decode step at 704x1280 (eager launches)
     python -m recavsr_b200.profile_case lq_conv1     # LQ projector conv1: im2col + bf16 GEMM, body block
     python -m recavsr_b200.profile_case lq_conv2     # LQ projector conv2: im2col + bf16 GEMM, body block
     python -m recavsr_b200.profile_case lq_norm      # channel RMSNorm + SiLU, 14080 x 2048
@@ -225,8 +226,28 @@ def _decoder(h=44, w=80, qf=4, nf=8, batch=1):
     return (lambda: local_attention(q, k, v, **kw)), 4.0 * 64 * 8 * batch * frames * axis(h) * axis(w), "TFLOP/s"
 
 
+def _decoder_step(h=44, w=80):
+    """One steady-state FlashDecoder-S decode step (12 + 2 blocks, random
+    weights) at a 44x80 latent grid, launched eagerly (one unit = one latent
+    frame, 0.91 TFLOP)."""
+    from .runtime.decoder import DecoderSession, random_params
+    dev = torch.device("cuda", torch.cuda.current_device())
+    sess = DecoderSession(random_params(dev, 0), height=h, width=w, mean=torch.zeros(48), std=torch.ones(48),
+                          device=dev)
+    g = torch.Generator(device=dev)
+    g.manual_seed(1)
+    lat = torch.randn(1, 48, 1, h, w, generator=g, device=dev)
+    lr1 = torch.rand(1, 3, 1, 16 * h, 16 * w, generator=g, device=dev) * 2 - 1
+    lr4 = torch.rand(1, 3, 4, 16 * h, 16 * w, generator=g, device=dev) * 2 - 1
+    list(sess.step(lat, lr_up=lr1))
+    for _ in range(2):
+        list(sess.step(lat, lr_up=lr4))
+    return (lambda: list(sess.step(lat, lr_up=lr4))), 0.91e12, "TFLOP/s"
+
+
 CASES = {
     "decoder": _decoder,
+    "decoder_step": _decoder_step,
     "decoder_backbone": lambda: _decoder(qf=1, nf=2),
     "gemm_cfg3_long_k": lambda: _gemm(DIM, FFN, _lib.EPI_BIAS, m=7040),
     "gemm_cfg3_wide_n": lambda: _gemm(FFN, DIM, _lib.EPI_BIAS, m=7040),

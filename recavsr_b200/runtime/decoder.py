@@ -160,7 +160,11 @@ class DecoderSession:
         self.grouped, self.late_in = e(n, 192), e(t4, 64)
         kv_tokens = 4 * window_size * n
         self.kbuf, self.vbuf = e(self.hk, kv_tokens, HEAD_DIM), e(self.hk, kv_tokens, HEAD_DIM)
-        self.rgb = e(3, 4, 16 * height, 16 * width)
+        # RGB output per frame parity: a frame's copy to the host can overlap the
+        # next frame's decode (step_host).
+        self.rgb_bufs = [e(3, 4, 16 * height, 16 * width), e(3, 4, 16 * height, 16 * width)]
+        self._copied = [None, None]         # copy-finished event per buffer
+        self._copy = None
         self.lat_stage = e(48, n, dt=torch.float32)
         self.lr_stage = e(3, 4, 16 * height, 16 * width, dt=torch.float32)
         self.frame_index = 0
@@ -205,7 +209,7 @@ class DecoderSession:
             self._gemm(self.act, L["d_w"], L["d_b"], tokens, dim, self.hidden, EPI_RESIDUAL, x, dim)
         st.total += cur
 
-    def _decode(self, first: bool, bpos, rpos):
+    def _decode(self, first: bool, bpos, rpos, rgb):
         """One decode step from the staged latent frame (lat_stage) and LR
         frames (lr_stage[:, :F]) into rgb[:, :F]."""
         n, dim, h, w = self.n, self.dim, self.h, self.w
@@ -230,7 +234,7 @@ class DecoderSession:
         _lib.call("rc_fd_silu", self.act.data_ptr(), 4 * n, self.hidden, 1, None, self.stream)
         self._gemm(self.act, self.s2_w, self.s2_b, 4 * n, 768, self.hidden, EPI_BIAS, self.s2, 768)
         _lib.call("rc_fd_pixel_shuffle", self.s2.data_ptr(), 768, 3 if first else 0, f_lr, 4, h, w,
-                  self.rgb.data_ptr(), self.stream)
+                  rgb.data_ptr(), self.stream)
 
     # -------------------------------------------------------------- public API
     @property
@@ -259,7 +263,11 @@ class DecoderSession:
         f_lr = 1 if first else 4
         if tuple(latent.shape) != (48, self.h, self.w) or tuple(lr_up.shape) != (3, f_lr, 16 * self.h, 16 * self.w):
             raise ValueError("Latent frame or lr_up does not match the session geometry.")
+        parity = self.frame_index % 2
+        rgb = self.rgb_bufs[parity]
         with torch.cuda.device(self.device):
+            if self._copied[parity] is not None:       # the buffer's previous frame has reached the host
+                torch.cuda.current_stream(self.device).wait_event(self._copied[parity])
             self.lat_stage.copy_(latent.reshape(48, self.n), non_blocking=True)
             self.lr_stage[:, :f_lr].copy_(lr_up, non_blocking=True)
             bpos, rpos = self.backbone.positions(), self.refinement.positions()
@@ -270,9 +278,9 @@ class DecoderSession:
                 self.backbone.total += 1
                 self.refinement.total += 4
             else:
-                self._decode(first, bpos, rpos)
+                self._decode(first, bpos, rpos, rgb)
         self.frame_index += 1
-        return self.rgb[:, :f_lr]
+        return rgb[:, :f_lr]
 
     def capture(self):
         """Record the two steady-state steps (one per ring parity) as CUDA
@@ -285,13 +293,13 @@ class DecoderSession:
         side = torch.cuda.Stream(self.device)
         side.wait_stream(torch.cuda.current_stream(self.device))
         with torch.cuda.device(self.device), torch.cuda.stream(side):
-            for _ in range(2):
+            for i in range(2):
                 key = self._key()
                 bpos, rpos = self.backbone.positions(), self.refinement.positions()
                 g = torch.cuda.CUDAGraph()
                 with torch.cuda.graph(g, stream=side):
-                    self._decode(False, bpos, rpos)
-                self.graphs[key] = g
+                    self._decode(False, bpos, rpos, self.rgb_bufs[(self.frame_index + i) % 2])
+                self.graphs[key] = g        # _decode advanced the stacks' frame counters
         torch.cuda.current_stream(self.device).wait_stream(side)
         self.backbone.total, self.refinement.total = saved
 
@@ -314,6 +322,45 @@ class DecoderSession:
             offset += take
             yield rgb.unsqueeze(0)
 
+    def step_host(self, latents: torch.Tensor, lr_up: torch.Tensor, host_out: torch.Tensor):
+        """step() into pinned host memory: host_out [3, F, 16h, 16w] bf16 (F =
+        4T, minus 3 on a stream's first block) receives the block's RGB frames.
+        Each frame's device-to-host copy runs on a copy stream and overlaps the
+        next frame's decode (the two frame parities have their own RGB buffer).
+        Asynchronous: returns a HostStep whose `input_consumed` completes once
+        latents / lr_up have been read and `output_ready` once host_out holds
+        every frame of the block; sync_host() waits for every copy issued."""
+        from .block import HostStep
+        if not host_out.is_pinned() or host_out.dtype != torch.bfloat16:
+            raise ValueError("host_out must be pinned bf16 memory.")
+        expected = 4 * latents.shape[2] - (3 if self.frame_index == 0 else 0)
+        if tuple(host_out.shape) != (3, expected, 16 * self.h, 16 * self.w):
+            raise ValueError(f"host_out must have shape {(3, expected, 16 * self.h, 16 * self.w)}.")
+        if self._copy is None:
+            self._copy = torch.cuda.Stream(self.device)
+        compute = torch.cuda.current_stream(self.device)
+        off = 0
+        for chunk in self.step(latents, lr_up=lr_up):
+            f = chunk.shape[2]
+            parity = (self.frame_index - 1) % 2
+            decoded = torch.cuda.Event()
+            decoded.record(compute)
+            self._copy.wait_event(decoded)
+            with torch.cuda.stream(self._copy):
+                host_out[:, off:off + f].copy_(chunk[0], non_blocking=True)
+            done = torch.cuda.Event()
+            done.record(self._copy)
+            self._copied[parity] = done
+            off += f
+        consumed = torch.cuda.Event()
+        consumed.record(compute)
+        return HostStep(input_consumed=consumed, output_ready=self._copied[(self.frame_index - 1) % 2])
+
+    def sync_host(self):
+        """Block the host until every copy step_host issued has finished."""
+        if self._copy is not None:
+            self._copy.synchronize()
+
     @classmethod
     def from_module(cls, model, *, height, width, mean, std, device=None):
         """From a reference FlashDecoder module (its state dict and sizes)."""
@@ -322,3 +369,42 @@ class DecoderSession:
                    depth=model.depth, refinement_depth=model.refinement_depth,
                    mlp_ratio=model.backbone.blocks[0].feed_forward.gate.out_features / model.dim,
                    window=model.spatial_window_size, window_size=model.window_size, device=device)
+
+
+def random_params(device, seed=0, *, dim=512, hidden=2048, depth=12, refinement_depth=2, kv_dim=128):
+    """Random-init FlashDecoder weights with the reference's state-dict names
+    (for benchmarks and profiling; the released variant's sizes by default):
+    linear weights N(0, 1/fan_in), biases N(0, 0.02), norm weights 1 + N(0, 0.1)."""
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    p = {}
+
+    def lin(name, n, k, bias=True):
+        p[name + ".weight"] = torch.randn(n, k, generator=g, device=device) / k ** 0.5
+        if bias:
+            p[name + ".bias"] = torch.randn(n, generator=g, device=device) * 0.02
+
+    def norm(name, n):
+        p[name + ".weight"] = 1 + torch.randn(n, generator=g, device=device) * 0.1
+
+    for prefix, n_blocks in (("backbone", depth), ("temporal_refinement", refinement_depth)):
+        for i in range(n_blocks):
+            b = f"{prefix}.blocks.{i}."
+            norm(b + "attention_norm", dim)
+            for name, n in (("query", dim), ("key", kv_dim), ("value", kv_dim), ("output", dim)):
+                lin(b + "attention." + name, n, dim)
+            norm(b + "attention.key_norm", HEAD_DIM)
+            norm(b + "attention.value_norm", HEAD_DIM)
+            norm(b + "feed_forward_norm", dim)
+            lin(b + "feed_forward.gate", hidden, dim)
+            lin(b + "feed_forward.up", hidden, dim)
+            lin(b + "feed_forward.down", dim, hidden)
+    lin("latent_projection", dim, 48)
+    lin("temporal_projection", 4 * dim, dim)
+    lin("spatial_projection.0", hidden, dim)
+    lin("spatial_projection.2", 768, hidden)
+    lin("lr_stem", 48, 768)
+    lin("lr_early_projection", dim, 192, bias=False)
+    lin("lr_late_projection", dim, 48, bias=False)
+    return p
+

@@ -119,3 +119,30 @@ def test_layout_kernels_match_torch():
     _lib.call("rc_fd_silu", x.data_ptr(), 64, 256, 1, None, _lib.stream())
     assert (x != F.silu(gu[:, :256])).float().mean() <= 1e-3
     assert_no_device_error()
+
+
+def test_step_host_equals_step():
+    """DecoderSession.step_host (RGB copies to pinned host memory on a copy
+    stream, overlapping the next frame) delivers the frames step() returns, bit
+    for bit, over a stream of blocks with graphs captured mid-stream, reusing
+    one pinned buffer per block size after output_ready."""
+    tag = "s"
+    c = recipes.DECODER_CASES[tag]
+    g = torch.Generator().manual_seed(11)
+    blocks = 4
+    h16, w16 = 16 * c["h"], 16 * c["w"]
+    lats = [torch.randn(1, 48, 2, c["h"], c["w"], generator=g).cuda() for _ in range(blocks)]
+    lrs = [(torch.rand(1, 3, 5 if i == 0 else 8, h16, w16, generator=g) * 2 - 1).cuda() for i in range(blocks)]
+    ref, got = _session(tag), _session(tag)
+    first = torch.empty((3, 5, h16, w16), dtype=torch.bfloat16).pin_memory()
+    body = torch.empty((3, 8, h16, w16), dtype=torch.bfloat16).pin_memory()
+    for i in range(blocks):
+        want = torch.cat([r[0].clone() for r in ref.step(lats[i], lr_up=lrs[i])], dim=1).cpu()
+        if i == 2:
+            got.capture()
+        out = first if i == 0 else body
+        st = got.step_host(lats[i], lrs[i], out)
+        st.output_ready.synchronize()
+        assert torch.equal(out, want), i
+    got.sync_host()
+    assert_no_device_error()
