@@ -500,6 +500,73 @@ __global__ void __launch_bounds__(kNormThreads) row_norm_kernel(NormArgs a) {
   }
 }
 
+// bf16 rows of N = 256 V: one warp per row, V 16-byte vectors per lane
+// (vector c = v * 32 + lane covers columns 8c .. 8c + 7), the same formula as
+// row_norm_kernel with warp-shuffle sums.
+template <int V>
+__global__ void __launch_bounds__(256) row_norm_warp_kernel(NormArgs a) {
+  rc::pdl_trigger();
+  rc::pdl_wait();
+  const int lane = threadIdx.x & 31;
+  const long long row = (long long)blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (row >= a.M) return;
+  const uint4* xp = reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(a.x) + row * a.ldx);
+  float f[V * 8];
+#pragma unroll
+  for (int v = 0; v < V; ++v) {
+    const uint4 w = rc::ld_in(xp + v * 32 + lane);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const uint32_t u = (&w.x)[k];
+      f[8 * v + 2 * k] = __uint_as_float(u << 16);
+      f[8 * v + 2 * k + 1] = __uint_as_float(u & 0xffff0000u);
+    }
+  }
+  auto warp_sum = [](float x) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+    return x;
+  };
+  float mean = 0.f;
+  if (!a.rms) {
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < V * 8; ++i) s += f[i];
+    mean = __fdiv_rn(warp_sum(s), (float)a.N);
+  }
+  float m2 = 0.f;
+#pragma unroll
+  for (int i = 0; i < V * 8; ++i) {
+    const float d = f[i] - mean;
+    m2 = fmaf(d, d, m2);
+  }
+  const float rstd = rsqrtf(__fdiv_rn(warp_sum(m2), (float)a.N) + a.eps);
+  uint4* op = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(a.out) + row * a.ldo);
+#pragma unroll
+  for (int v = 0; v < V; ++v) {
+    const int c0 = (v * 32 + lane) * 8;
+    float y[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) y[k] = __fmul_rn(__fsub_rn(f[8 * v + k], mean), rstd);
+    if (a.weight) {
+      const float4 w0 = rc::ld_in(reinterpret_cast<const float4*>(a.weight + c0));
+      const float4 w1 = rc::ld_in(reinterpret_cast<const float4*>(a.weight + c0) + 1);
+      const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+      for (int k = 0; k < 8; ++k) y[k] = __fmul_rn(y[k], wv[k]);
+    }
+    if (a.bias) {
+      const float4 b0 = rc::ld_in(reinterpret_cast<const float4*>(a.bias + c0));
+      const float4 b1 = rc::ld_in(reinterpret_cast<const float4*>(a.bias + c0) + 1);
+      const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+      for (int k = 0; k < 8; ++k) y[k] = __fadd_rn(y[k], bv[k]);
+    }
+    op[v * 32 + lane] = make_uint4(rc::pack_bf16x2(y[0], y[1]), rc::pack_bf16x2(y[2], y[3]),
+                                   rc::pack_bf16x2(y[4], y[5]), rc::pack_bf16x2(y[6], y[7]));
+  }
+}
+
 int grid_for(long long work, int threads) {
   long long b = (work + threads - 1) / threads;
   return (int)(b < 1 ? 1 : (b > 148LL * 16 ? 148LL * 16 : b));
@@ -564,6 +631,17 @@ int rc_layer_norm(const void* x, int dtype, long long ldx, int M, int N, const f
     return rc::set_error(RC_ERR_ARG, "rc_layer_norm: misaligned pointer");
   if (M == 0) return RC_OK;
   NormArgs a{x, ldx, dtype, weight, rms ? nullptr : bias, eps, rms, out, ldo, M, N};
+  // bf16 rows of 256 / 512 / 1024 with 16-byte aligned rows and vectors: a warp per row.
+  const bool vec = dtype == 1 && (N == 256 || N == 512 || N == 1024) && aligned16(x) && aligned16(out) &&
+                   ldx % 8 == 0 && ldo % 8 == 0 && (!weight || aligned16(weight)) &&
+                   (rms || !bias || aligned16(bias));
+  if (vec) {
+    const dim3 grid((unsigned)((M + 7) / 8));
+    cudaError_t e = N == 256 ? rc::launch_pdl(row_norm_warp_kernel<1>, grid, dim3(256), 0, stream, a)
+                  : N == 512 ? rc::launch_pdl(row_norm_warp_kernel<2>, grid, dim3(256), 0, stream, a)
+                             : rc::launch_pdl(row_norm_warp_kernel<4>, grid, dim3(256), 0, stream, a);
+    return rc::check_launch(e, "rc_layer_norm");
+  }
   return rc::check_launch(rc::launch_pdl(row_norm_kernel, dim3(M), dim3(kNormThreads), 0, stream, a),
                           "rc_layer_norm");
 }

@@ -347,7 +347,11 @@ class DecoderSession:
             decoded.record(compute)
             self._copy.wait_event(decoded)
             with torch.cuda.stream(self._copy):
-                host_out[:, off:off + f].copy_(chunk[0], non_blocking=True)
+                # per channel: each channel's frame range is contiguous on both
+                # sides, so every copy is one asynchronous DMA (a strided pinned
+                # destination would be staged through a synchronous copy)
+                for c in range(3):
+                    host_out[c, off:off + f].copy_(chunk[0, c], non_blocking=True)
             done = torch.cuda.Event()
             done.record(self._copy)
             self._copied[parity] = done

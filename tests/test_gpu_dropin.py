@@ -213,3 +213,26 @@ def test_native_rms_norm_any_dtype(dtype):
     ref = F.rms_norm(x.float(), (3072,), w.float(), 1e-6)
     tol = 1e-5 if dtype == torch.float32 else 2 ** -9 * 4
     assert (got.float() - ref).abs().max().item() <= tol
+
+
+@pytest.mark.parametrize("n", [256, 512, 1024])
+@pytest.mark.parametrize("rms", [False, True])
+def test_layer_norm_bf16_warp_rows(n, rms):
+    """rc_layer_norm's warp-per-row path (bf16 rows of 256 / 512 / 1024, the
+    FlashDecoder's RMSNorm over 512): against torch's fp32 norm of the same
+    rows, within one bf16 rounding; a ragged row count (not a multiple of 8)
+    and a row stride wider than the row."""
+    from recavsr_b200 import _lib
+    g = torch.Generator(device="cuda").manual_seed(7 + n)
+    m = 1003
+    base = (torch.randn(m, n + 64, generator=g, device="cuda") * 2 + 0.3).bfloat16()
+    x = base[:, :n]
+    w = 1 + 0.1 * torch.randn(n, generator=g, device="cuda")
+    b = 0.1 * torch.randn(n, generator=g, device="cuda")
+    out = torch.full((m, n + 32), 7.0, dtype=torch.bfloat16, device="cuda")
+    _lib.call("rc_layer_norm", x.data_ptr(), 1, n + 64, m, n, w.data_ptr(), None if rms else b.data_ptr(), 1e-5,
+              int(rms), out.data_ptr(), n + 32, _lib.stream())
+    ref = (F.rms_norm(x.float(), (n,), w, 1e-5) if rms else F.layer_norm(x.float(), (n,), w, b, 1e-5))
+    err = (out[:, :n].float() - ref).abs() / ref.abs().clamp_min(1e-3)
+    assert err.max().item() <= 2 ** -7
+    assert torch.all(out[:, n:] == 7.0)
