@@ -18,6 +18,7 @@ on the GPU is its own code: the Triton `_paired_local` kernel, `sdpa_attention`
     python baseline/compare.py pipeline    # frame preparation (enlarge + normalize + pad) and strip blend
     python baseline/compare.py decoder     # FlashDecoder local GQA attention (its Triton forward)
     python baseline/compare.py decoder_step  # FlashDecoder decode step (its FlashDecoderSession, eager and compiled)
+    python baseline/compare.py colorfix    # AdaIN / wavelet colour correction of a body block's 8 frames
     python baseline/compare.py all
 
 This library's side is imported from recavsr_b200.runtime (ops, fp8, block):
@@ -372,6 +373,44 @@ def case_decoder_step(rows, steps, warmup, h=44, w=80):
          ref="recavsr_infer.runtime.flashdecoder.FlashDecoderSession (bf16 autocast)")
 
 
+def case_colorfix(rows, reps):
+    """The colour correction of one body block's output (8 RGB frames at
+    704x1280, bf16 from the decoder; LQ 176x320 uint8): the reference's own
+    adain_color_fix / wavelet_color_fix (color_fix.py:58-117, torch on the GPU)
+    against this library's drop-ins, through the same public calls (the
+    wavelet's uint8 result comes back to the host on both sides); wall time per
+    call with a device sync, and the device-only wavelet beside it."""
+    import numpy as np
+    from recavsr_b200.runtime import colorfix as ours
+    from recavsr_infer import color_fix as theirs
+    g = torch.Generator(device="cuda").manual_seed(5)
+    dec = (torch.rand(1, 3, 8, 704, 1280, generator=g, device="cuda") * 2 - 1).bfloat16()
+    ref = torch.rand(1, 3, 8, 704, 1280, generator=g, device="cuda") * 2 - 1
+    lq = np.random.RandomState(5).randint(0, 256, (8, 176, 320, 3)).astype(np.uint8)
+    lq_dev = torch.from_numpy(lq).cuda()
+
+    def wall(fn):
+        for _ in range(2):
+            fn()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            fn()
+        torch.cuda.synchronize()
+        return (time.perf_counter() - t0) / reps
+    a_o, a_r = ours.adain_color_fix(dec, ref), theirs.adain_color_fix(dec, ref)
+    w_o, w_r = ours.wavelet_color_fix(dec, lq), theirs.wavelet_color_fix(dec, lq)
+    d = np.abs(w_o.astype(np.int16) - w_r.astype(np.int16))
+    emit(rows, case="colorfix", step="adain, 8 frames 704x1280", ours_ms=wall(lambda: ours.adain_color_fix(dec, ref)) * 1e3,
+         ref_ms=wall(lambda: theirs.adain_color_fix(dec, ref)) * 1e3,
+         max_abs_diff=float((a_o - a_r.float()).abs().max()))
+    emit(rows, case="colorfix", step="wavelet, 8 frames 704x1280 -> uint8 on the host",
+         ours_ms=wall(lambda: ours.wavelet_color_fix(dec, lq)) * 1e3,
+         ref_ms=wall(lambda: theirs.wavelet_color_fix(dec, lq)) * 1e3,
+         ours_device_ms=graph_time(lambda: ours.wavelet_color_fix_device(dec, lq_dev), reps) * 1e3,
+         max_abs_diff=int(d.max()), frac_differing=float((d > 0).mean()))
+
+
 # ------------------------------------------------------------- the layer loop
 class _FP32LayerNorm(nn.LayerNorm):
     """diffusers FP32LayerNorm as the released block uses it (norm1/norm3 without
@@ -611,7 +650,7 @@ def case_pipeline(rows, reps):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("case", choices=["gemm", "attention", "local", "layers", "pipeline", "decoder", "decoder_step",
-                                     "all"])
+                                     "colorfix", "all"])
     ap.add_argument("--reps", type=int, default=10)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
@@ -621,8 +660,8 @@ def main():
     torch.cuda.set_device(0)
     torch._dynamo.config.recompile_limit = 64     # one compiled graph per shape, as the reference allows
     rows = []
-    todo = (["gemm", "attention", "local", "layers", "pipeline", "decoder", "decoder_step"] if args.case == "all"
-            else [args.case])
+    todo = (["gemm", "attention", "local", "layers", "pipeline", "decoder", "decoder_step", "colorfix"]
+            if args.case == "all" else [args.case])
     for c in todo:
         if c == "gemm":
             case_gemm(rows, args.reps)
@@ -636,6 +675,8 @@ def main():
             case_decoder(rows, args.reps)
         elif c == "decoder_step":
             case_decoder_step(rows, args.steps, args.warmup)
+        elif c == "colorfix":
+            case_colorfix(rows, args.reps)
         else:
             case_layers(rows, args.steps, args.warmup)
         torch.cuda.empty_cache()

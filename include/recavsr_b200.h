@@ -303,6 +303,32 @@ int rc_fd_silu(void* x, int M, int H, int mode, void* out, rc_stream_t stream);
 int rc_fd_pixel_shuffle(const void* y, long long ldy, int f0, int frames, int out_frames, int h, int w, void* out,
                         rc_stream_t stream);
 
+/* ---- colour correction (recavsr_infer/color_fix.py) ------------------------ */
+/* color_fix.py:18-29,58-81 (adain_color_fix): per plane (frame, RGB channel) of
+ * `planes` planes of hw values (content / reference in [-1, 1], dtype 0 fp32,
+ * 1 bf16, same plane order), mean and sample variance of (x + 1) * 0.5, out
+ * fp32 = ((c - mean_c) * sqrt((var_r + 1e-5) / (var_c + 1e-5)) + mean_r) * 2 - 1.
+ * workspace: rc_cf_adain_workspace(planes, hw) bytes, 8-byte aligned. */
+long long rc_cf_adain_workspace(int planes, long long hw);
+int rc_cf_adain(const void* content, int content_dtype, const void* reference, int reference_dtype, int planes,
+                long long hw, void* workspace, long long workspace_bytes, float* out, rc_stream_t stream);
+
+/* color_fix.py:102-110: clamp(bicubic(lq / 255), 0, 1) of uint8 frames
+ * [T, h, w, 3] at H x W (torch's upsample_bicubic2d, align_corners = false)
+ * into out [T * 3, H, W] fp32. */
+int rc_cf_bicubic_u8(const uint8_t* lq, int T, int h, int w, int H, int W, float* out, rc_stream_t stream);
+
+/* color_fix.py:32-55,111-117: one level (dilation `radius`) of the wavelet
+ * correction over [T * 3, H, W] fp32 planes: blur_c / blur_r = the [1,2,1]^2 / 16
+ * blur (replicate padding) of low_c / low_r, high += low_c - blur_c. first:
+ * the content is clamp((decoded + 1) * 0.5, 0, 1) read from decoded
+ * [3, T, H, W] (dtype 0 fp32, 1 bf16) and high starts at 0. last: writes
+ * uint8 round(clamp(high + blur_r, 0, 1) * 255) into out [T, H, W, 3]
+ * (blur_c, blur_r and high are not written). */
+int rc_cf_wavelet_level(const void* decoded, int dtype, const float* low_c, const float* low_r, float* blur_c,
+                        float* blur_r, float* high, uint8_t* out, int T, int H, int W, int radius, int first,
+                        int last, rc_stream_t stream);
+
 /* ---- frame preparation and strip blending -------------------------------- */
 /* Replaces recavsr_infer/video.py:153-179 (`enlarge_block` + `block_tensor`,
  * called by `prepare_block` :138-150): src = `valid` uint8 RGB frames [h, w, 3]

@@ -49,6 +49,10 @@ _SIGNATURES = {
     "rc_strip_blend": [_I, _P, _P, _P, _P, _P, _P, _I, _I, _P, _LL, _P],
     "rc_local_gqa_attention": [_P, _P, _P, _P] + [_I] * 13 + [_P, _P, _P],
     "rc_fd_latent_in": [_P, _LL, _I, _P, _P, _P, _P],
+    "rc_cf_adain_workspace": [_I, _LL],
+    "rc_cf_adain": [_P, _I, _P, _I, _I, _LL, _P, _LL, _P, _P],
+    "rc_cf_bicubic_u8": [_P, _I, _I, _I, _I, _I, _P, _P],
+    "rc_cf_wavelet_level": [_P, _I, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P],
     "rc_fd_lr_unshuffle": [_P, _I, _P, _I, _I, _I, _P, _P],
     "rc_fd_lr_group": [_P, _LL, _I, _I, _P, _P, _P],
     "rc_fd_kv_norm": [_P, _LL, _I, _I, _I, _P, _P, _F, _P, _P, _LL, _LL, _P],
@@ -58,7 +62,7 @@ _SIGNATURES = {
     "rc_unpatchify_residual": [_P, _LL, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _P],
 }
 _RESTYPES = {"rc_paired_attention_workspace": C.c_longlong, "rc_gemm_split_workspace": C.c_longlong,
-             "rc_cross_attention_workspace": C.c_longlong}
+             "rc_cross_attention_workspace": C.c_longlong, "rc_cf_adain_workspace": C.c_longlong}
 
 _lib = None
 _lock = threading.Lock()

@@ -19,7 +19,7 @@ PKG = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(PKG, "csrc")
 OBJ = os.path.join(PKG, "_build")
 LIB = os.path.join(PKG, "librecavsr_b200.so")
-SOURCES = ["runtime.cu", "quant.cu", "glue.cu", "gemm.cu", "attention.cu", "session.cu", "pipeline.cu", "decoder_attention.cu", "decoder.cu"]
+SOURCES = ["runtime.cu", "quant.cu", "glue.cu", "gemm.cu", "attention.cu", "session.cu", "pipeline.cu", "decoder_attention.cu", "decoder.cu", "colorfix.cu"]
 HEADERS = ["common.cuh", "sm100.cuh"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", "-O2",

@@ -7,6 +7,7 @@ Run where a checkout of the reference exists:
     python tests/golden/make_golden.py <reference checkout> --fullsize  # fullsize_hashes.json
     python tests/golden/make_golden.py <reference checkout> --pipeline  # pipeline_outputs.npz
     python tests/golden/make_golden.py <reference checkout> --decoder-step  # decoder_step_outputs.npz
+    python tests/golden/make_golden.py <reference checkout> --colorfix      # colorfix_outputs.npz
     python tests/golden/make_golden.py <reference checkout> --pipeline-cuda [out.npz]
                                         # pipeline_cuda_outputs.npz (needs a CUDA device)
                                                                         # flashdecoder_outputs.npz
@@ -516,6 +517,16 @@ def gen_decoder_step(out):
             out[f"dec_{tag}_refine{i}"] = seen["refinement"][i].numpy()
 
 
+def gen_colorfix(out):
+    """recavsr_infer/color_fix.py:58-117 on the CPU: adain_color_fix and
+    wavelet_color_fix on recipes.COLORFIX_CASES."""
+    from recavsr_infer.color_fix import adain_color_fix, wavelet_color_fix
+    for tag in recipes.COLORFIX_CASES:
+        dec, ref, lq = recipes.colorfix_inputs(tag)
+        out[f"cf_{tag}_adain"] = adain_color_fix(torch.from_numpy(dec), torch.from_numpy(ref)).numpy()
+        out[f"cf_{tag}_wavelet"] = wavelet_color_fix(torch.from_numpy(dec), lq)
+
+
 FULLSIZE_SHAPES = ((7040, 14336), (7040, 3072))     # cfg3's largest activations
 
 
@@ -648,6 +659,12 @@ def main():
         gen_pipeline(out)
         np.savez_compressed(os.path.join(HERE, "pipeline_outputs.npz"), **out)
         print("wrote", len(out), "pipeline arrays")
+        return
+    if "--colorfix" in sys.argv:
+        out = {}
+        gen_colorfix(out)
+        np.savez_compressed(os.path.join(HERE, "colorfix_outputs.npz"), **out)
+        print("wrote", len(out), "colour-correction arrays")
         return
     if "--decoder-step" in sys.argv:
         torch.manual_seed(0)

@@ -241,3 +241,20 @@ def decoder_inputs(tag, seed=52):
     coarse = rs.uniform(-1, 1, (1, 3, frames, 4 * h, 4 * w)).astype(np.float32)
     lr_up = np.repeat(np.repeat(coarse, 4, axis=3), 4, axis=4)
     return latents, mean, std, np.ascontiguousarray(lr_up)
+
+
+# Colour correction cases: (frames, decoded height, width, LQ height, width).
+COLORFIX_CASES = {"a": (2, 48, 80, 12, 20), "b": (3, 36, 52, 9, 13)}
+
+
+def colorfix_inputs(tag, seed=71):
+    """decoded [1, 3, T, H, W] fp32 in [-1, 1] (smooth noise plus a colour
+    cast), the AdaIN reference of the same shape, and LQ uint8 [T, h, w, 3]."""
+    t, hh, ww, h, w = COLORFIX_CASES[tag]
+    rs = np.random.RandomState(seed + ord(tag))
+    coarse = rs.uniform(-1, 1, (1, 3, t, hh // 4 + 1, ww // 4 + 1)).astype(np.float32)
+    dec = np.repeat(np.repeat(coarse, 4, axis=3), 4, axis=4)[:, :, :, :hh, :ww]
+    dec = np.clip(dec * 0.8 + rs.uniform(-0.2, 0.2, dec.shape) + 0.1, -1, 1).astype(np.float32)
+    ref = np.clip(rs.uniform(-1, 1, dec.shape) * 0.5 - 0.2, -1, 1).astype(np.float32)
+    lq = rs.randint(0, 256, (t, h, w, 3)).astype(np.uint8)
+    return dec, ref, lq
