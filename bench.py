@@ -519,9 +519,9 @@ def measure_session(session, device, rank, world, steps, warm):
 
 SESSION_GLUE_LAUNCHES = 15   # 2 im2col, 2 channel norms, 7 bf16 GEMMs, 2 patch gathers, 1 LayerNorm, 1 unpatchify
 DEC_DIM, DEC_HIDDEN, DEC_DEPTH, DEC_REFINE = 512, 2048, 12, 2   # FlashDecoder-S (flashdecoder_wan22.py:590-600)
-# Launches of one decode step: 6 before the backbone, 10 per block, 5 between the
+# Launches of one decode step: 6 before the backbone, 9 per block, 5 between the
 # stacks, 4 after the refinement.
-DECODER_LAUNCHES = 6 + 10 * (DEC_DEPTH + DEC_REFINE) + 5 + 4
+DECODER_LAUNCHES = 6 + 9 * (DEC_DEPTH + DEC_REFINE) + 5 + 4
 
 
 def build_decoder(device, seed, h=44, w=80):

@@ -54,6 +54,10 @@ int rc_fp8_quantize(const void* x, int M, int K, long long ldx, unsigned int* am
 #define RC_EPI_GATED_RESIDUAL 1
 #define RC_EPI_RESIDUAL 2
 #define RC_EPI_GELU_NVFP4 3
+/* bf16 only: the columns come as 16-column chunks of 8 gate then 8 up
+ * columns; out [M, N/2] = bf16(bf16(silu(y_gate)) * y_up) (the SwiGLU of
+ * recavsr_infer/models/flashdecoder/flashdecoder_wan22.py:344-345). */
+#define RC_EPI_SWIGLU 4
 
 /* Replaces recavsr_infer/runtime/nvfp4.py:22-39 `nvfp4_mm` (torch._scaled_mm_v2,
  * BlockWise1x16 / SWIZZLE_32_4_4, bias, bf16 out). */

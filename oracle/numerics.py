@@ -46,7 +46,8 @@ def e4m3_encode(x) -> np.ndarray:
     code = normal.astype(np.int64) - (120 << 3)
     a = mag.view(np.float32)
     sub = mag < np.uint32(0x3C800000)                   # |x| < 2^-6
-    code = np.where(sub, np.rint(a * np.float32(512.0)).astype(np.int64), code)
+    with np.errstate(over="ignore", invalid="ignore"):  # lanes where sub is False are discarded
+        code = np.where(sub, np.rint(a * np.float32(512.0)).astype(np.int64), code)
     code = np.where(mag >= np.uint32(0x43F00000), 0x7F, code)    # |x| >= 480 or NaN
     return code.astype(np.uint8) | sign
 

@@ -16,7 +16,7 @@ _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "librecavsr_b200.so")
 
 RC_OK, RC_ERR_ARG, RC_ERR_CUDA, RC_ERR_TIMEOUT, RC_ERR_UNSUPPORTED = range(5)
-EPI_BIAS, EPI_GATED_RESIDUAL, EPI_RESIDUAL, EPI_GELU_NVFP4 = range(4)
+EPI_BIAS, EPI_GATED_RESIDUAL, EPI_RESIDUAL, EPI_GELU_NVFP4, EPI_SWIGLU = range(5)
 
 _P, _I, _LL, _F = C.c_void_p, C.c_int, C.c_longlong, C.c_float
 _SIGNATURES = {

@@ -25,6 +25,9 @@
 //   RESIDUAL       h   = bf16(h + bf16(acc*alpha + bias))            (in place)
 //   GELU_NVF4      y   = bf16(gelu_tanh(bf16(acc*alpha + bias))), quantized to
 //                  NVFP4 (16 columns = one block) for the next linear.
+//   SWIGLU (bf16)  each 16-column chunk is 8 gate then 8 up columns (weights
+//                  interleaved by the caller): out[:, n/2 ..] =
+//                  bf16(bf16(silu(y_gate)) * y_up), y = bf16(acc + bias).
 #include <stdlib.h>
 
 #include "sm100.cuh"
@@ -32,7 +35,7 @@
 namespace {
 
 enum Kind : int { KIND_NVF4 = 0, KIND_E4M3 = 1, KIND_BF16 = 2 };
-enum Epi : int { EPI_BIAS = 0, EPI_GATED_RESIDUAL = 1, EPI_RESIDUAL = 2, EPI_GELU_NVF4 = 3 };
+enum Epi : int { EPI_BIAS = 0, EPI_GATED_RESIDUAL = 1, EPI_RESIDUAL = 2, EPI_GELU_NVF4 = 3, EPI_SWIGLU = 4 };
 
 constexpr int BM = 128;
 constexpr int kRowBytes = 128;                     // K bytes per smem row / k-tile
@@ -526,6 +529,25 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
             unpack_bf16x2(w[j], v[2 * j], v[2 * j + 1]);
           }
         }
+        if constexpr (EPI == EPI_SWIGLU) {
+          // Columns n0 .. n0 + 7 hold gate, n0 + 8 .. n0 + 15 up for output
+          // columns n0 / 2 .. n0 / 2 + 7: bf16(bf16(silu(gate)) * up), SiLU as
+          // x / (1 + exp(-x)) in fp32.
+          uint32_t sw[4];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            float s2[2];
+#pragma unroll
+            for (int k = 0; k < 2; ++k) {
+              const float g = v[2 * j + k];
+              const float sg = __bfloat162float(__float2bfloat16_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g)))));
+              s2[k] = __fmul_rn(sg, v[8 + 2 * j + k]);
+            }
+            sw[j] = rc::pack_bf16x2(s2[0], s2[1]);
+          }
+          *reinterpret_cast<uint4*>(p.out + (size_t)row * p.ldo + (n0 >> 1)) = make_uint4(sw[0], sw[1], sw[2], sw[3]);
+          return;
+        }
         if constexpr (EPI == EPI_GATED_RESIDUAL || EPI == EPI_RESIDUAL) {
           const uint32_t hw[8] = {o.h0.x, o.h0.y, o.h0.z, o.h0.w, o.h1.x, o.h1.y, o.h1.z, o.h1.w};
 #pragma unroll
@@ -753,6 +775,9 @@ int dispatch_epi(int epi, const Maps& m, const GemmParams& p, cudaStream_t strea
     case EPI_GATED_RESIDUAL: return launch<KIND, BN, STAGES, EPI_GATED_RESIDUAL, PAIR>(m, p, stream, what);
     case EPI_RESIDUAL: return launch<KIND, BN, STAGES, EPI_RESIDUAL, PAIR>(m, p, stream, what);
     case EPI_GELU_NVF4: return launch<KIND, BN, STAGES, EPI_GELU_NVF4, PAIR>(m, p, stream, what);
+    case EPI_SWIGLU:
+      if constexpr (KIND == KIND_BF16 && !PAIR) return launch<KIND, BN, STAGES, EPI_SWIGLU, PAIR>(m, p, stream, what);
+      break;
   }
   return rc::set_error(RC_ERR_ARG, "%s: unknown epilogue %d", what, epi);
 }
@@ -802,8 +827,10 @@ int run_gemm(int kind, int epi, const void* a, const void* b, int M, int N, int 
   if (K % 64)
     return rc::set_error(RC_ERR_UNSUPPORTED, "%s: K must be a multiple of 64 (K=%d)", what, K);
   if (!a || !b) return rc::set_error(RC_ERR_ARG, "%s: null operand", what);
+  if (epi == EPI_SWIGLU && (kind != KIND_BF16 || N % 16))
+    return rc::set_error(RC_ERR_ARG, "%s: the SwiGLU epilogue is bf16-only", what);
   if (epi != EPI_GELU_NVF4 || p.out) {
-    if (!p.out || p.ldo < N || p.ldo % 8 || reinterpret_cast<uintptr_t>(p.out) % 16)
+    if (!p.out || p.ldo < (epi == EPI_SWIGLU ? N / 2 : N) || p.ldo % 8 || reinterpret_cast<uintptr_t>(p.out) % 16)
       return rc::set_error(RC_ERR_ARG, "%s: output rows must be 16-byte aligned (ldo=%lld)", what, p.ldo);
   }
   if (epi == EPI_GATED_RESIDUAL && !p.gate) return rc::set_error(RC_ERR_ARG, "%s: gate missing", what);

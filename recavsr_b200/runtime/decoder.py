@@ -16,7 +16,7 @@ frames, 2 refinement blocks over 4n tokens (an 8-frame window), the spatial
 projection and the pixel shuffle. A block is RMSNorm -> fused q|k|v GEMM ->
 K / V RMSNorm into the rings -> 3D RoPE of q and of the window's keys ->
 rc_local_gqa_attention -> output GEMM (+ residual) -> RMSNorm -> fused
-gate|up GEMM -> SiLU * up -> down GEMM (+ residual): ten launches, all of
+gate|up GEMM with the SwiGLU epilogue -> down GEMM (+ residual): nine launches, all of
 this library's kernels. Steady-state steps are replayed from CUDA graphs
 (capture(): one per parity of the ring positions, which repeat every two steps).
 """
@@ -30,7 +30,7 @@ import torch
 
 from .. import _lib
 
-EPI_BIAS, EPI_RESIDUAL = 0, 2
+EPI_BIAS, EPI_RESIDUAL, EPI_SWIGLU = 0, 2, 4
 HEAD_DIM = 64
 
 
@@ -45,6 +45,15 @@ def _pad_k(w: torch.Tensor, k: int) -> torch.Tensor:
     out = torch.zeros((w.shape[0], k), dtype=w.dtype, device=w.device)
     out[:, :w.shape[1]] = w
     return out
+
+
+def _swiglu_rows(gate, up, device) -> torch.Tensor:
+    """Gate and up rows (or biases) interleaved in blocks of 8, the layout of
+    the GEMM's SwiGLU epilogue: [g0..g7, u0..u7, g8..g15, u8..u15, ...]."""
+    g, u = torch.as_tensor(gate), torch.as_tensor(up)
+    n = g.shape[0]
+    both = torch.stack([g.reshape(n // 8, 8, *g.shape[1:]), u.reshape(n // 8, 8, *u.shape[1:])], 1)
+    return _dev(both.reshape(2 * n, *g.shape[1:]), device, torch.bfloat16)
 
 
 def rope_tables(height: int, width: int, max_t: int, device, theta: float = 10000.0, dims=(16, 24, 24)):
@@ -84,10 +93,9 @@ class _Stack:
                 vn=_dev(w[a + "value_norm.weight"], dev, torch.float32),
                 o_w=_dev(w[a + "output.weight"], dev, torch.bfloat16),
                 o_b=_dev(w[a + "output.bias"], dev, torch.bfloat16),
-                gu_w=_dev(torch.cat([torch.as_tensor(w[pre + "feed_forward.gate.weight"]),
-                                     torch.as_tensor(w[pre + "feed_forward.up.weight"])]), dev, torch.bfloat16),
-                gu_b=_dev(torch.cat([torch.as_tensor(w[pre + "feed_forward.gate.bias"]),
-                                     torch.as_tensor(w[pre + "feed_forward.up.bias"])]), dev, torch.bfloat16),
+                gu_w=_swiglu_rows(w[pre + "feed_forward.gate.weight"], w[pre + "feed_forward.up.weight"],
+                                  dev),
+                gu_b=_swiglu_rows(w[pre + "feed_forward.gate.bias"], w[pre + "feed_forward.up.bias"], dev),
                 d_w=_dev(w[pre + "feed_forward.down.weight"], dev, torch.bfloat16),
                 d_b=_dev(w[pre + "feed_forward.down.bias"], dev, torch.bfloat16),
                 k_ring=torch.zeros((d.hk, ring_tokens, HEAD_DIM), dtype=torch.float32, device=dev),
@@ -154,7 +162,7 @@ class DecoderSession:
         e = lambda *s, dt=bf: torch.empty(s, dtype=dt, device=dev)
         self.x, self.hr, self.xn = e(n, dim), e(t4, dim), e(t4, dim)
         self.qkv, self.q_rot, self.att = e(t4, qkv_n), e(t4, dim), e(t4, dim)
-        self.gu, self.act = e(t4, 2 * self.hidden), e(t4, self.hidden)
+        self.act = e(t4, self.hidden)
         self.s2 = e(t4, 768)
         self.lat_in, self.unsh, self.feats = e(n, 64), e(t4, 768), e(t4, 48)
         self.grouped, self.late_in = e(n, 192), e(t4, 64)
@@ -203,9 +211,9 @@ class DecoderSession:
                       self.window[1], cur, st.max_frames // cur, 0, self.att.data_ptr(), o_str, self.stream)
             self._gemm(self.att, L["o_w"], L["o_b"], tokens, dim, dim, EPI_RESIDUAL, x, dim)
             self._rms(x, L["ffn_w"], tokens, self.xn)
-            self._gemm(self.xn, L["gu_w"], L["gu_b"], tokens, 2 * self.hidden, dim, EPI_BIAS, self.gu,
-                       2 * self.hidden)
-            _lib.call("rc_fd_silu", self.gu.data_ptr(), tokens, self.hidden, 0, self.act.data_ptr(), self.stream)
+            # gate | up GEMM with the SwiGLU epilogue: act = bf16(bf16(silu(gate)) * up)
+            self._gemm(self.xn, L["gu_w"], L["gu_b"], tokens, 2 * self.hidden, dim, EPI_SWIGLU, self.act,
+                       self.hidden)
             self._gemm(self.act, L["d_w"], L["d_b"], tokens, dim, self.hidden, EPI_RESIDUAL, x, dim)
         st.total += cur
 

@@ -329,3 +329,34 @@ def test_nvfp4_gemm_pair_gelu_ragged_rows():
     assert max_rel(yo[rows], y) < TOL
     ec, es = onv.quantize(yo[m - 128:m])
     np.testing.assert_array_equal(qc.cpu().numpy()[m - 128:m], ec)
+
+
+def test_bf16_gemm_swiglu_epilogue():
+    """RC_EPI_SWIGLU: weights with gate / up rows interleaved in blocks of 8;
+    the fused output equals torch's bf16 SiLU(gate) * up applied to the same
+    GEMM's bias-epilogue output (within one bf16 rounding on <= 0.1% of the
+    values); ragged M, output row stride wider than N / 2."""
+    from recavsr_b200 import _lib
+    from recavsr_b200.runtime.decoder import _swiglu_rows
+    import torch.nn.functional as F
+    g = torch.Generator(device="cuda").manual_seed(21)
+    m, k, h = 1003, 512, 1024
+    x = torch.randn(m, k, generator=g, device="cuda").bfloat16()
+    wg, wu = (torch.randn(h, k, generator=g, device="cuda") / k ** 0.5 for _ in range(2))
+    bg, bu = (torch.randn(h, generator=g, device="cuda") * 0.1 for _ in range(2))
+    w, b = _swiglu_rows(wg, wu, x.device), _swiglu_rows(bg, bu, x.device)
+    y = torch.empty(m, 2 * h, dtype=torch.bfloat16, device="cuda")
+    _lib.call("rc_bf16_gemm", x.data_ptr(), w.data_ptr(), b.data_ptr(), m, 2 * h, k, _lib.EPI_BIAS, y.data_ptr(),
+              2 * h, None, _lib.stream())
+    out = torch.full((m, h + 64), 3.0, dtype=torch.bfloat16, device="cuda")
+    _lib.call("rc_bf16_gemm", x.data_ptr(), w.data_ptr(), b.data_ptr(), m, 2 * h, k, _lib.EPI_SWIGLU,
+              out.data_ptr(), h + 64, None, _lib.stream())
+    yy = y.view(m, h // 8, 2, 8)
+    ref = (F.silu(yy[:, :, 0]) * yy[:, :, 1]).reshape(m, h)
+    got = out[:, :h]
+    diff = (got.float() - ref.float()).abs() / ref.float().abs().clamp_min(1e-20)
+    assert (diff > 0).float().mean().item() <= 1e-3 and diff.max().item() <= 2 ** -7
+    assert torch.all(out[:, h:] == 3.0)
+    with pytest.raises(ValueError):
+        _lib.call("rc_bf16_gemm", x.data_ptr(), w.data_ptr(), b.data_ptr(), m, 2 * h, k, _lib.EPI_SWIGLU,
+                  out.data_ptr(), h // 2, None, _lib.stream())
