@@ -71,3 +71,47 @@ def test_session_and_commit_entry_points_reject_bad_arguments():
         _lib.call("rc_kv_commit_planned", 4096, 4096, 16, 32, 4096, 4096, 32, 32, 24, 2, 2, 4096, None)
     with pytest.raises(ValueError, match="bad shape"):             # row_bytes % 16
         _lib.call("rc_kv_commit_planned", None, None, 0, 0, None, None, 0, 24, 1, 2, 2, None, None)
+
+
+def test_decoder_pipeline_colorfix_entry_points_reject_bad_arguments():
+    """The FlashDecoder, frame-preparation and colour-correction entry points
+    validate on the host before any device work (every call fails validation)."""
+    import ctypes as C
+
+    import pytest
+    from recavsr_b200 import _lib
+    st9 = (C.c_longlong * 9)(*([64] * 9))
+    with pytest.raises(ValueError, match="head_dim 32"):
+        _lib.call("rc_local_gqa_attention", None, None, None, st9, 1, 8, 2, 4, 8, 6, 20, 32, 4, 8, 4, 2, 0, None,
+                  None, None)
+    with pytest.raises(ValueError, match="alignment"):       # HQ % HK
+        _lib.call("rc_local_gqa_attention", None, None, None, st9, 1, 6, 4, 4, 8, 6, 20, 64, 4, 8, 4, 2, 0, None,
+                  None, None)
+    with pytest.raises(ValueError, match="alignment"):       # odd window
+        _lib.call("rc_local_gqa_attention", None, None, None, st9, 1, 8, 2, 4, 8, 6, 20, 64, 3, 8, 4, 2, 0, None,
+                  None, None)
+    with pytest.raises(ValueError, match="missing pointer"):
+        _lib.call("rc_local_gqa_attention", None, None, None, st9, 1, 8, 2, 4, 8, 6, 20, 64, 4, 8, 4, 2, 0, None,
+                  None, None)
+    with pytest.raises(ValueError, match="bad arguments"):
+        _lib.call("rc_fd_kv_norm", None, 768, 10, 512, 2, None, None, 1e-5, None, None, 640, 0, None)
+    with pytest.raises(ValueError, match="bad arguments"):   # nf < cur
+        _lib.call("rc_fd_rope_gather", None, 768, 8, 2, 4, 0, 2, 0, 8, 4, 6, None, None, 0, None, 8, None, None,
+                  None, None)
+    with pytest.raises(ValueError, match="bad arguments"):   # H % 8
+        _lib.call("rc_fd_silu", None, 4, 12, 0, None, None)
+    with pytest.raises(ValueError, match="bad arguments"):   # f0 + frames > 4
+        _lib.call("rc_fd_pixel_shuffle", None, 768, 3, 2, 4, 4, 6, None, None)
+    with pytest.raises(ValueError, match="bad arguments"):
+        _lib.call("rc_fd_lr_group", None, 48, 24, 0, None, None, None)
+    with pytest.raises(ValueError, match="bad arguments"):
+        _lib.call("rc_cf_adain", None, 0, None, 0, 3, 100, None, 0, None, None)
+    with pytest.raises(ValueError, match="bad arguments"):   # radius 0
+        _lib.call("rc_cf_wavelet_level", None, 0, None, None, None, None, None, None, 1, 8, 8, 0, 1, 0, None)
+    with pytest.raises(ValueError, match="bad arguments"):
+        _lib.call("rc_cf_bicubic_u8", None, 1, 4, 4, 16, 16, None, None)
+    with pytest.raises(ValueError, match="missing pointer"):
+        _lib.call("rc_enlarge_block", None, 0, 0, 1, 8, 4, 4, 16, 16, 0, None, None)
+    with pytest.raises(ValueError, match="bad shape"):       # no strips
+        _lib.call("rc_strip_blend", 0, None, None, None, None, None, None, 8, 8, None, 24, None)
+    assert _lib.library().rc_cf_adain_workspace(6, 100000) == 6 * 7 * 4 * 8
