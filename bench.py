@@ -289,9 +289,10 @@ def ffn_up_bytes():
 
 # ---------------------------------------------------------------- CPU side
 def cpu_baseline(sample_tokens_note=True):
-    """Oracle port of one DiT block forward (NVFP4 linears emulated, fp32
-    matmuls, numpy/BLAS on all host cores) at the bench geometry; tokens/s is
-    extrapolated to the 30-layer step."""
+    """Oracle port of one DiT block forward in the reference's CPU formulation
+    (fp32 linears as nn.Linear runs them there -- its NVFP4 GEMM needs CUDA --,
+    fp32 attention and softmax; numpy/BLAS on all host cores) at the bench
+    geometry; tokens/s is extrapolated to the 30-layer step."""
     from oracle import block as oblock
     from oracle import rope as orope
     rs = np.random.RandomState(0)
@@ -299,7 +300,8 @@ def cpu_baseline(sample_tokens_note=True):
     lin = {}
     for name, (n, k) in {"q": (DIM, DIM), "k": (DIM, DIM), "v": (DIM, DIM), "o": (DIM, DIM),
                          "cq": (DIM, DIM), "co": (DIM, DIM), "up": (FFN, DIM), "down": (DIM, FFN)}.items():
-        lin[name] = oblock.QuantLinear(f32(n, k, std=0.02), f32(n, std=0.02), matmul_dtype=np.float32)
+        lin[name] = oblock.QuantLinear(f32(n, k, std=0.02), f32(n, std=0.02), matmul_dtype=np.float32,
+                                       quantized=False)
     tc, ts, sc, ss = orope.rolling_tables(HEAD_DIM, H_TOK, W_TOK)
     p = {"_linears": lin, "modulation": f32(6, DIM), "norm_q": 1 + f32(DIM, std=0.1),
          "norm_k": 1 + f32(DIM, std=0.1), "cnorm_q": 1 + f32(DIM, std=0.1),
@@ -314,7 +316,8 @@ def cpu_baseline(sample_tokens_note=True):
     dt = time.perf_counter() - t0
     tokens_per_s = BODY * T / (dt * LAYERS)
     return {"value": tokens_per_s, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
-            "sample": f"1 of 30 layers (recent_2 cache, 1760 tokens), {dt:.2f} s, extrapolated x30"}
+            "sample": f"1 of 30 layers (recent_2 cache, 1760 tokens, fp32 linears and attention), {dt:.2f} s, "
+                      "extrapolated x30"}
 
 
 def run_reference(args, rank, world):

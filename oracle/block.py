@@ -44,18 +44,29 @@ def gelu_tanh(x):
 
 class QuantLinear:
     """NVFP4Linear with the weight quantized once (nvfp4.py:82-84).
-    matmul_dtype float64 for parity checks, float32 for the timed CPU baseline."""
+    matmul_dtype float64 for parity checks, float32 for the timed CPU baseline.
+    quantized=False: the fp32 nn.Linear of the reference's CPU formulation (its
+    NVFP4 GEMM needs CUDA), i.e. x @ W^T + b in fp32 without quantization."""
 
-    def __init__(self, weight, bias, matmul_dtype=np.float64):
+    def __init__(self, weight, bias, matmul_dtype=np.float64, quantized: bool = True):
         self.n, self.k = weight.shape
-        self.codes, self.scales = nvfp4.quantize(np.asarray(weight, np.float32))
         self.bias = None if bias is None else np.asarray(bias, np.float32)
         self.dtype = matmul_dtype
-        self.w = nvfp4.dequantize(self.codes, self.scales, self.n, self.k).astype(matmul_dtype)
+        self.quantized = quantized
+        if quantized:
+            self.codes, self.scales = nvfp4.quantize(np.asarray(weight, np.float32))
+            self.w = nvfp4.dequantize(self.codes, self.scales, self.n, self.k).astype(matmul_dtype)
+        else:
+            self.w = np.ascontiguousarray(np.asarray(weight, np.float32).T)
 
     def __call__(self, x):
         x = np.asarray(x, np.float32)
         shape = x.shape
+        if not self.quantized:
+            out = x.reshape(-1, self.k) @ self.w
+            if self.bias is not None:
+                out += self.bias
+            return out.reshape(*shape[:-1], self.n)
         a = x.reshape(-1, self.k)
         ac, asf = nvfp4.quantize(a)
         out = nvfp4.nvfp4_mm(ac, asf, None, None, self.bias, a.shape[0], self.n, self.k,
