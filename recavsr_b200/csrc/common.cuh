@@ -91,6 +91,11 @@ __device__ __forceinline__ T ld_in(const T* p) {
   return *p;
 }
 
+// Pull the 128-byte line holding p into L1 (no register result, no wait).
+__device__ __forceinline__ void prefetch_l1(const void* p) {
+  asm volatile("prefetch.global.L1 [%0];" ::"l"(p));
+}
+
 // launch_pdl with thread-block clusters of `cluster_x` CTAs along x.
 template <typename... KArgs, typename... Args>
 inline cudaError_t launch_pdl_cluster(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,

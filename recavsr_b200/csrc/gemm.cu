@@ -16,8 +16,10 @@
 // global; two or four warps per TMEM lane quadrant, each on an equal share of
 // the tile's columns, see epi_warps). With
 // BN = 128 the accumulator is double-buffered in TMEM so the epilogue of one
-// tile overlaps the MMAs of the next; with BN = 256 the epilogue drains the
-// accumulator into registers first and releases it, which gives the same
+// tile overlaps the MMAs of the next, and the bf16 output tile is staged in
+// shared memory and written by TMA stores (residual epilogues TMA-load the
+// residual tile into the same boxes first); with BN = 256 the epilogue drains
+// the accumulator into registers first and releases it, which gives the same
 // overlap with a single accumulator.
 // Epilogues fuse the block's follow-up element-wise work:
 //   BIAS           out = bf16(acc*alpha + bias)
@@ -132,8 +134,12 @@ struct Smem {
   static constexpr int offB = offA + STAGES * kA;
   static constexpr int offSfa = offB + STAGES * kB;
   static constexpr int offSfb = offSfa + STAGES * kSfa;
-  static constexpr int offBar = offSfb + STAGES * kSfb;
-  static constexpr int kBars = 2 * STAGES + 6 + 1;
+  // Single-CTA 128-column tiles stage the epilogue's bf16 output (and the
+  // residual input) in shared memory: BN / 64 boxes of 128 rows x 128 bytes.
+  static constexpr int kOut = (!PAIR && BN == 128) ? BM * BN * 2 : 0;
+  static constexpr int offOut = offSfb + STAGES * kSfb;
+  static constexpr int offBar = offOut + kOut;
+  static constexpr int kBars = 2 * STAGES + 6 + 2;
   static constexpr int kTotal = offBar + kBars * 8 + 16;
   static constexpr int kAlloc = kTotal;
 };
@@ -168,7 +174,7 @@ template <int KIND, int BN, int STAGES, int EPI, bool PAIR>
 __global__ void __launch_bounds__(gemm_threads<EPI, PAIR>(), 1)
 gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
             const __grid_constant__ CUtensorMap tmap_sfa, const __grid_constant__ CUtensorMap tmap_sfb,
-            const GemmParams p) {
+            const __grid_constant__ CUtensorMap tmap_out, const GemmParams p) {
   using S = Smem<KIND, BN, STAGES, PAIR>;
   static_assert(!PAIR || (KIND == KIND_NVF4 && BN == 256), "CTA pairs run 256 x 256 NVFP4 tiles");
   constexpr bool kScaled = KindTraits<KIND>::kScaled;
@@ -188,6 +194,13 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
   uint64_t* done = acc_empty + 2;          // [1]
   volatile int* abort_flag = reinterpret_cast<volatile int*>(done + 2);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 3);
+  uint64_t* h_full = done + 5;             // [1] residual tile staged (kStaged)
+  // Epilogues that stage their bf16 output tile in shared memory and write it
+  // with TMA stores (residual epilogues first TMA-load the residual tile into
+  // the same boxes): one 128-byte line per row per box instead of each lane
+  // storing its own row, which kept the SM's memory pipeline busy enough to
+  // slow the next tile's operand loads and MMAs.
+  constexpr bool kStaged = !PAIR && BN == 128 && EPI != EPI_GELU_NVF4;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -210,6 +223,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
       sm100::mbar_init(&acc_empty[a], PAIR ? 2 * epi_warps<EPI, PAIR>() : 32 * epi_warps<EPI, PAIR>());
     }
     sm100::mbar_init(done, 1);
+    sm100::mbar_init(h_full, 1);
     *abort_flag = 0;
     sm100::fence_mbar_init();
   }
@@ -462,17 +476,56 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
         sm100::mbar_arrive(&acc_empty[as]);
       }
     };
+    constexpr bool kRes = EPI == EPI_GATED_RESIDUAL || EPI == EPI_RESIDUAL;
+    // Staged output: BN / 64 boxes of 128 rows x 64 bf16 columns (the SwiGLU
+    // epilogue writes half as many columns: one box).
+    uint8_t* const out_smem = smem + S::offOut;
+    constexpr int kOutBoxes = EPI == EPI_SWIGLU ? BN / 128 : BN / 64;
+    static_assert(!kStaged || kCols == 64, "staged epilogue: 64 columns per thread");
+    // Address in the staging boxes of bf16 column c (a multiple of 8) of this thread's row.
+    auto stage_at = [&](int c) -> uint8_t* {
+      return out_smem + (c >> 6) * (BM * 128) + sm100::sw128_offset(row_in_tile, (c & 63) >> 3);
+    };
+    int h_issued = 0, h_used = 0;               // residual tiles loaded into / consumed from the boxes
+    // Residual tile of (mb, nb) into the boxes (one elected thread), once the
+    // previous tile's TMA stores have finished reading them.
+    auto stage_residual = [&](int mb, int nb) {
+      ++h_issued;
+      if (threadIdx.x != 64) return;
+      sm100::bulk_wait_group_read0();
+      sm100::mbar_arrive_expect_tx(h_full, kOutBoxes * BM * 128);
+      for (int b = 0; b < kOutBoxes; ++b)
+        sm100::tma_load_2d(out_smem + b * (BM * 128), &tmap_out, h_full, nb * BN + 64 * b, mb * BM);
+    };
+    if constexpr (kStaged) {
+      if (threadIdx.x == 64) sm100::tma_prefetch_desc(&tmap_out);
+    }
     for (int u = unit0; u < num_units; u += unit_step, ++local) {
       const Unit un = unit_of(p, u);
       int mb, nb;
       tile_coords(p, un.tile, mb, nb);
       if constexpr (PAIR) mb = mb * 2 + (int)rank;   // this CTA's 128-row block of the pair's tile
       const int as = local % kAcc;
-      const bool got = __all_sync(0xffffffffu, wait(&acc_full[as], (uint32_t)((local / kAcc) & 1), 4));
-      if (!got && (BN != 128 || un.piece < 0)) break;
-      const uint32_t t_row = tmem_acc + as * BN + part * kCols + ((uint32_t)(quad * 32) << 16);
       const int row = mb * BM + row_in_tile;
       const bool row_ok = row < p.M;
+      const int ncol0 = nb * BN + part * kCols;   // first column of this thread's share
+      // Before the accumulator is ready, start this tile's epilogue operand
+      // loads (the residual tile into the staging boxes, the bias / gate lines
+      // into L1), so their L2 round trips overlap the tile's last MMAs. (A
+      // split tile's merging unit loads the residual after the merge.)
+      if constexpr (kStaged && kRes)
+        if (un.piece < 0) stage_residual(mb, nb);
+      if (lane == 0 && ncol0 < p.N) {
+        const int ncols = min(kCols, p.N - ncol0);
+        if (p.bias)
+          for (int c = 0; c < ncols; c += 64) rc::prefetch_l1(p.bias + ncol0 + c);
+        if constexpr (EPI == EPI_GATED_RESIDUAL)
+          for (int c = 0; c < ncols; c += 32) rc::prefetch_l1(p.gate + ncol0 + c);
+      }
+      const bool got = __all_sync(0xffffffffu, wait(&acc_full[as], (uint32_t)((local / kAcc) & 1), 4));
+      // (Staged epilogues decide at their first barrier, all warps alike.)
+      if (!kStaged && !got && (BN != 128 || un.piece < 0)) break;
+      const uint32_t t_row = tmem_acc + as * BN + part * kCols + ((uint32_t)(quad * 32) << 16);
       // Per 16-column chunk: the bias / residual / gate operands (zero-filled
       // past the matrix edge).
       struct Ops {
@@ -488,7 +541,10 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
           o.b0 = rc::ld_in(bp);
           o.b1 = rc::ld_in(bp + 1);
         }
-        if constexpr (EPI == EPI_GATED_RESIDUAL || EPI == EPI_RESIDUAL) {
+        if constexpr (kStaged && kRes) {
+          o.h0 = *reinterpret_cast<const uint4*>(stage_at(part * kCols + cc));
+          o.h1 = *reinterpret_cast<const uint4*>(stage_at(part * kCols + cc + 8));
+        } else if constexpr (kRes) {
           const uint4* hp = reinterpret_cast<const uint4*>(p.out + (size_t)row * p.ldo + n0);
           o.h0 = hp[0];
           o.h1 = hp[1];
@@ -500,7 +556,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
         }
         return o;
       };
-      // Epilogue math and stores of one chunk from its accumulator words.
+      // Epilogue math of one chunk from its accumulator words; the bf16
+      // results go to the staging boxes (kStaged) or straight to global memory.
       auto emit_chunk = [&](int cc, const uint32_t* a16, const Ops& o) {
         const int n0 = nb * BN + part * kCols + cc;
         if (n0 >= p.N) return;
@@ -545,10 +602,12 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
             }
             sw[j] = rc::pack_bf16x2(s2[0], s2[1]);
           }
-          *reinterpret_cast<uint4*>(p.out + (size_t)row * p.ldo + (n0 >> 1)) = make_uint4(sw[0], sw[1], sw[2], sw[3]);
+          const uint4 r = make_uint4(sw[0], sw[1], sw[2], sw[3]);
+          if constexpr (kStaged) *reinterpret_cast<uint4*>(stage_at((part * kCols + cc) >> 1)) = r;
+          else *reinterpret_cast<uint4*>(p.out + (size_t)row * p.ldo + (n0 >> 1)) = r;
           return;
         }
-        if constexpr (EPI == EPI_GATED_RESIDUAL || EPI == EPI_RESIDUAL) {
+        if constexpr (kRes) {
           const uint32_t hw[8] = {o.h0.x, o.h0.y, o.h0.z, o.h0.w, o.h1.x, o.h1.y, o.h1.z, o.h1.w};
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
@@ -593,9 +652,14 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
           p.q_sf[rc::sf_offset(row, n0 >> 4, (p.N + 63) >> 6)] = sfb;
           if (!p.out) return;
         }
-        uint4* dst = reinterpret_cast<uint4*>(p.out + (size_t)row * p.ldo + n0);
-        dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
-        dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+        if constexpr (kStaged) {
+          *reinterpret_cast<uint4*>(stage_at(part * kCols + cc)) = make_uint4(w[0], w[1], w[2], w[3]);
+          *reinterpret_cast<uint4*>(stage_at(part * kCols + cc + 8)) = make_uint4(w[4], w[5], w[6], w[7]);
+        } else {
+          uint4* dst = reinterpret_cast<uint4*>(p.out + (size_t)row * p.ldo + n0);
+          dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+          dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+        }
       };
       if (BN == 128 && un.piece >= 0) {   // (the host splits 128-column tiles only)
         // Split tile: store this unit's partial, count the arrival. The last
@@ -630,6 +694,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
           release(as);                             // accumulator free: next tile may start
           continue;
         }
+        if constexpr (kStaged && kRes) stage_residual(mb, nb);
         __threadfence();   // acquire: the other units' partials are visible from here
         const float4* src = reinterpret_cast<const float4*>(p.part + (size_t)tail_tile * p.split * (BM * BN)) +
                             ((part * kCols) >> 2) * BM + row_in_tile;
@@ -661,27 +726,40 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
         sm100::tmem_st_wait();
         if (threadIdx.x == 64) p.counters[tail_tile] = 0;   // ready for the next launch
       }
-      if constexpr (kAcc == 2 && (EPI == EPI_GATED_RESIDUAL || EPI == EPI_RESIDUAL)) {
-        // Residual epilogues: per 16-column chunk, a TMEM load of its
-        // accumulator words; the next chunk's residual / gate / bias are loaded
-        // before this chunk's stores (a store to the residual buffer would
-        // otherwise keep them behind its round trip). The accumulator stays
-        // allocated until the tile's last chunk has been read; with two
-        // accumulator stages the MMA needs it again only two tiles later.
-        // (o-proj 1760 x 3072 x 3072: 23.6 -> 22.3 us.)
+      if constexpr (kStaged) {
+        // Staged epilogue: the boxes are free (residual: its tile has landed
+        // in them; otherwise: the previous tile's stores have read them), then
+        // per 16-column chunk a TMEM load, the operands, the math into the
+        // boxes; the accumulator is released after the last chunk (with two
+        // accumulator stages the MMA needs it again only two tiles later) and
+        // one thread stores the boxes.
+        bool ok = got;
+        if constexpr (kRes) {
+          ++h_used;
+          ok = wait(h_full, (uint32_t)((h_used - 1) & 1), 5) && ok;
+        } else {
+          if (threadIdx.x == 64) sm100::bulk_wait_group_read0();
+        }
+        if (!sm100::bar_and(1, 32 * epi_warps<EPI, PAIR>(), ok)) break;
         sm100::tc_fence_after();
-        Ops cur = load_ops(0);
 #pragma unroll
         for (int cc = 0; cc < kCols; cc += 16) {
           uint32_t a16[16];
           sm100::tmem_ld16(t_row + cc, a16);
+          const Ops o = load_ops(cc);
           sm100::tmem_ld_wait();
-          Ops nxt;
-          if (cc + 16 < kCols) nxt = load_ops(cc + 16);
-          emit_chunk(cc, a16, cur);
-          cur = nxt;
+          emit_chunk(cc, a16, o);
         }
         release(as);                             // accumulator free
+        sm100::fence_proxy_async_smem();         // the boxes' writes, visible to the TMA stores
+        asm volatile("bar.sync 1, %0;" ::"r"(32 * epi_warps<EPI, PAIR>()) : "memory");
+        if (threadIdx.x == 64) {
+          const int x0 = EPI == EPI_SWIGLU ? nb * (BN / 2) : nb * BN;
+          const int n_out = EPI == EPI_SWIGLU ? p.N / 2 : p.N;
+          for (int b = 0; b < kOutBoxes; ++b)
+            if (x0 + 64 * b < n_out) sm100::tma_store_2d(&tmap_out, out_smem + b * (BM * 128), x0 + 64 * b, mb * BM);
+          sm100::bulk_commit_group();
+        }
       } else {
         // Other epilogues: drain the tile's columns from TMEM into registers
         // and release the accumulator first, so the next tile's MMAs overlap
@@ -695,6 +773,14 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
         release(as);                             // accumulator free: next tile may start
 #pragma unroll
         for (int cc = 0; cc < kCols; cc += 16) emit_chunk(cc, &acc[cc], load_ops(cc));
+      }
+    }
+    if constexpr (kStaged) {
+      if (threadIdx.x == 64) {
+        // A residual tile still in flight (a wait gave up) lands before the
+        // CTA leaves; every TMA store has completed.
+        if (h_issued > 0) sm100::mbar_wait(h_full, (uint32_t)((h_issued - 1) & 1));
+        sm100::bulk_wait_group0();
       }
     }
   }
@@ -736,10 +822,11 @@ void plan_split(int tiles, int sms, bool can_split, GemmParams& p) {
 constexpr long long kSplitPartBytes = (long long)kMaxPieces * BM * 128 * 4;
 constexpr long long kSplitWorkspaceBytes = kSplitPartBytes + kMaxPieces * 4;
 
-// The four tensor maps of a launch: A and B operand rows, and (CTA pairs
-// only) A's and B's scale atoms viewed as [row blocks][4 * k atoms][128 B].
+// The tensor maps of a launch: A and B operand rows, (CTA pairs only) A's
+// and B's scale atoms viewed as [row blocks][4 * k atoms][128 B], and (staged
+// epilogues only) the bf16 output as boxes of 128 rows x 64 columns.
 struct Maps {
-  CUtensorMap a, b, sfa, sfb;
+  CUtensorMap a, b, sfa, sfb, out;
 };
 
 template <int KIND, int BN, int STAGES, int EPI, bool PAIR>
@@ -758,14 +845,14 @@ int launch(const Maps& m, const GemmParams& p, cudaStream_t stream, const char* 
     q.split = 1;
     const int pairs = tiles < sms / 2 ? tiles : sms / 2;
     return rc::check_launch(rc::launch_pdl_cluster(kern, dim3(2 * pairs), dim3(gemm_threads<EPI, PAIR>()), S::kAlloc,
-                                                   stream, 2, m.a, m.b, m.sfa, m.sfb, q),
+                                                   stream, 2, m.a, m.b, m.sfa, m.sfb, m.a, q),
                             what);
   }
   plan_split(tiles, sms, BN == 128 && p.part != nullptr, q);
   const int units = q.n_regular + (tiles - q.n_regular) * q.split;
   const int grid = units < sms ? units : sms;
   return rc::check_launch(rc::launch_pdl(kern, grid, dim3(gemm_threads<EPI>()), S::kAlloc, stream, m.a, m.b,
-                                         m.a, m.b, q), what);
+                                         m.a, m.b, m.out, q), what);
 }
 
 template <int KIND, int BN, int STAGES, bool PAIR = false>
@@ -843,6 +930,7 @@ int run_gemm(int kind, int epi, const void* a, const void* b, int M, int N, int 
   const uint64_t sa[1] = {row_bytes}, sb[1] = {row_bytes};
   const bool pair = gemm_use_pair(kind, M, N, K);
   const bool wide = !pair && gemm_prefer_wide(epi, M, N, K);
+  const bool staged = !pair && !wide && epi != EPI_GELU_NVF4;   // the kernel's kStaged
   const uint32_t boxa[2] = {128, 128}, boxb[2] = {128, (uint32_t)(wide ? 256 : 128)};
   int r = rc::encode_tmap(&maps.a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(a), da, sa, boxa,
                           CU_TENSOR_MAP_SWIZZLE_128B, what);
@@ -850,6 +938,16 @@ int run_gemm(int kind, int epi, const void* a, const void* b, int M, int N, int 
   r = rc::encode_tmap(&maps.b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(b), db, sb, boxb,
                       CU_TENSOR_MAP_SWIZZLE_128B, what);
   if (r) return r;
+  maps.out = maps.a;
+  if (staged) {
+    // bf16 output [M, N] (SwiGLU: N / 2) with row stride ldo, 128 x 64 boxes.
+    const uint64_t dout[2] = {(uint64_t)(epi == EPI_SWIGLU ? N / 2 : N), (uint64_t)M};
+    const uint64_t sout[1] = {(uint64_t)p.ldo * 2};
+    const uint32_t boxo[2] = {64, 128};
+    r = rc::encode_tmap(&maps.out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, p.out, dout, sout, boxo,
+                        CU_TENSOR_MAP_SWIZZLE_128B, what);
+    if (r) return r;
+  }
   if (pair) {
     // Scale atoms (512 B = 128 rows x 4 k-blocks) as 128-byte lines: one box
     // is a k-tile's 4 atoms of one 128-row block; lines past the last atom
@@ -894,7 +992,7 @@ int run_gemm(int kind, int epi, const void* a, const void* b, int M, int N, int 
     return dispatch_epi<KIND_BF16, 256, 4>(epi, maps, p, stream, what);
   }
   p.n_blocks = (N + 127) / 128;
-  if (kind == KIND_NVF4) return dispatch_epi<KIND_NVF4, 128, 6>(epi, maps, p, stream, what);
+  if (kind == KIND_NVF4) return dispatch_epi<KIND_NVF4, 128, 5>(epi, maps, p, stream, what);
   if (kind == KIND_E4M3) return dispatch_epi<KIND_E4M3, 128, 6>(epi, maps, p, stream, what);
   return dispatch_epi<KIND_BF16, 128, 6>(epi, maps, p, stream, what);
 }
