@@ -89,6 +89,12 @@ int rc_fp8_gemm(const uint8_t* a, const float* scale_a, const uint8_t* b, const 
  * recavsr_infer/runtime/transformer.py:95-133). */
 int rc_bf16_gemm(const void* a, const void* b, const void* bias, int M, int N, int K, int epilogue,
                  void* out, long long ldo, const float* gate, rc_stream_t stream);
+/* rc_bf16_gemm with a split-K workspace (the rules of rc_nvfp4_gemm_ws): the
+ * LQ projector's long-K convolution GEMMs (recavsr_infer/models/lq_proj.py:80-139
+ * as TransformerSession runs them, transformer.py:279-300). */
+int rc_bf16_gemm_ws(const void* a, const void* b, const void* bias, int M, int N, int K, int epilogue,
+                    void* out, long long ldo, const float* gate, void* workspace, long long workspace_bytes,
+                    rc_stream_t stream);
 
 /* ---- glue --------------------------------------------------------------- */
 /* LayerNorm (+affine) (+AdaLN modulation) (+fused NVFP4 quantize) of

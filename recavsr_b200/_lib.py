@@ -30,6 +30,7 @@ _SIGNATURES = {
     "rc_nvfp4_gemm_ws": [_P, _P, _P, _P, _P, _I, _I, _I, _F, _I, _P, _LL, _P, _P, _P, _F, _P, _LL, _P],
     "rc_fp8_gemm": [_P, _P, _P, _P, _P, _I, _I, _I, _F, _I, _P, _LL, _P, _P],
     "rc_bf16_gemm": [_P, _P, _P, _I, _I, _I, _I, _P, _LL, _P, _P],
+    "rc_bf16_gemm_ws": [_P, _P, _P, _I, _I, _I, _I, _P, _LL, _P, _P, _LL, _P],
     "rc_ln_modulate_quant": [_P, _LL, _I, _I, _P, _P, _P, _P, _F, _P, _LL, _P, _P, _F, _P],
     "rc_layer_norm": [_P, _I, _LL, _I, _I, _P, _P, _F, _I, _P, _LL, _P],
     "rc_rmsnorm_rope": [_I, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P, _P, _F, _P],

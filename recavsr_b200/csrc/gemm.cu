@@ -1092,4 +1092,26 @@ int rc_bf16_gemm(const void* a, const void* b, const void* bias, int M, int N, i
   return run_gemm(KIND_BF16, epilogue, a, b, M, N, K, p, stream, "rc_bf16_gemm");
 }
 
+// rc_bf16_gemm with the split-K workspace of rc_nvfp4_gemm_ws (same size,
+// alignment, zero-fill and ordering rules): the tiles of the partial last
+// wave run as k-ranges (the LQ projector's K = 73728 convolution GEMM).
+int rc_bf16_gemm_ws(const void* a, const void* b, const void* bias, int M, int N, int K, int epilogue,
+                    void* out, long long ldo, const float* gate, void* workspace, long long workspace_bytes,
+                    cudaStream_t stream) {
+  const char* what = "rc_bf16_gemm_ws";
+  if (!workspace || workspace_bytes < kSplitWorkspaceBytes || reinterpret_cast<uintptr_t>(workspace) % 16)
+    return rc::set_error(RC_ERR_ARG, "%s: workspace of %lld bytes (16-byte aligned) required", what,
+                         kSplitWorkspaceBytes);
+  GemmParams p{};
+  p.alpha = 1.0f;
+  p.bias = reinterpret_cast<const __nv_bfloat16*>(bias);
+  p.out = reinterpret_cast<__nv_bfloat16*>(out);
+  p.ldo = ldo;
+  p.gate = gate;
+  p.part = reinterpret_cast<float*>(workspace);
+  p.counters = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(workspace) + kSplitPartBytes);
+  if (epilogue == EPI_GELU_NVF4) return rc::set_error(RC_ERR_ARG, "%s: GELU/NVFP4 epilogue is NVFP4-only", what);
+  return run_gemm(KIND_BF16, epilogue, a, b, M, N, K, p, stream, what);
+}
+
 }  // extern "C"

@@ -35,12 +35,29 @@ _KT = 4                      # temporal kernel of both causal convolutions (lq_p
 _UNSHUFFLE = 16              # pixel unshuffle factor (lq_proj.py:168)
 
 
+_GLUE_WS: dict = {}
+
+
+def _glue_workspace(device: torch.device) -> torch.Tensor:
+    """The glue GEMMs' split-K workspace, one per device (allocated on first
+    use, zero-filled; the glue issues its GEMMs in order on one stream)."""
+    key = torch.device(device).index
+    ws = _GLUE_WS.get(key)
+    if ws is None:
+        ws = torch.zeros((_lib.library().rc_gemm_split_workspace(),), dtype=torch.uint8, device=device)
+        _GLUE_WS[key] = ws
+    return ws
+
+
 def _gemm(a: torch.Tensor, w: torch.Tensor, bias, out: torch.Tensor, epi: int) -> torch.Tensor:
-    """out[M, N] (epilogue epi) = a[M, K] @ w[N, K]^T + bias on the tcgen05 bf16 GEMM."""
+    """out[M, N] (epilogue epi) = a[M, K] @ w[N, K]^T + bias on the tcgen05 bf16
+    GEMM (tail split-K through the glue's workspace)."""
     if not a.is_contiguous():
         raise ValueError("GEMM operand rows must be contiguous")
-    _lib.call("rc_bf16_gemm", a.data_ptr(), w.data_ptr(), _lib.ptr(bias), a.shape[0], w.shape[0],
-              a.shape[1], epi, out.data_ptr(), out.stride(0), None, _lib.stream(a.device))
+    ws = _glue_workspace(a.device)
+    _lib.call("rc_bf16_gemm_ws", a.data_ptr(), w.data_ptr(), _lib.ptr(bias), a.shape[0], w.shape[0],
+              a.shape[1], epi, out.data_ptr(), out.stride(0), None, ws.data_ptr(), ws.numel(),
+              _lib.stream(a.device))
     return out
 
 

@@ -360,3 +360,35 @@ def test_bf16_gemm_swiglu_epilogue():
     with pytest.raises(ValueError):
         _lib.call("rc_bf16_gemm", x.data_ptr(), w.data_ptr(), b.data_ptr(), m, 2 * h, k, _lib.EPI_SWIGLU,
                   out.data_ptr(), h // 2, None, _lib.stream())
+
+
+def test_bf16_gemm_split_workspace_matches_plain():
+    """rc_bf16_gemm_ws (the session glue's convolution GEMMs): 336 tiles of
+    128 x 128, the last 40 run as 3 k-ranges; the result equals rc_bf16_gemm's
+    up to the fp32 summation order, repeats exactly, and leaves the workspace's
+    counters at zero. Both against the fp32 matmul."""
+    from recavsr_b200 import _lib
+    from recavsr_b200.runtime.ops import split_workspace
+    m, n, k = 1760, 3072, 4096
+    rs = np.random.RandomState(31)
+    a = recipes.bf16_normal(rs, (m, k))
+    w = recipes.bf16_normal(rs, (n, k), 0.02)
+    b = recipes.bf16_normal(rs, (n,), 0.1)
+    ad, wd, bd = dev_bf16(a), dev_bf16(w), dev_bf16(b)
+    ws = split_workspace(ad.device)
+    outs = []
+    for _ in range(3):
+        o = torch.empty(m, n, dtype=torch.bfloat16, device="cuda")
+        _lib.call("rc_bf16_gemm_ws", ad.data_ptr(), wd.data_ptr(), bd.data_ptr(), m, n, k, _lib.EPI_BIAS,
+                  o.data_ptr(), n, None, ws.data_ptr(), ws.numel(), _lib.stream())
+        outs.append(o)
+    plain = torch.empty(m, n, dtype=torch.bfloat16, device="cuda")
+    _lib.call("rc_bf16_gemm", ad.data_ptr(), wd.data_ptr(), bd.data_ptr(), m, n, k, _lib.EPI_BIAS,
+              plain.data_ptr(), n, None, _lib.stream())
+    assert_no_device_error()
+    ref = a.astype(np.float64) @ w.astype(np.float64).T + b
+    for o in outs:
+        assert torch.equal(o, outs[0])
+    assert max_rel(host(outs[0]), ref) < TOL
+    assert max_rel(host(outs[0]), host(plain)) < 2 ** -8
+    assert int(ws[-640:].count_nonzero()) == 0
