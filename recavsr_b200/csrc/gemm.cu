@@ -466,12 +466,16 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
     int* s_flags = reinterpret_cast<int*>(done + 4);   // [0] last unit of the tile, [1] a warp failed
     if (threadIdx.x == 64) s_flags[1] = 0;
     asm volatile("bar.sync 1, %0;" ::"r"(32 * epi_warps<EPI, PAIR>()) : "memory");
-    // Accumulator release: every epilogue thread has read its columns.
+    // Accumulator release: every epilogue thread has read its columns. In a
+    // pair the arrival is relaxed: the MMA needs only the TMEM reads, which
+    // tcgen05.wait::ld has completed; a release at cluster scope would first
+    // wait for the warp's earlier global stores (the previous tile's outputs)
+    // to be performed, with the MMA idle meanwhile.
     auto release = [&](int as) {
       sm100::tc_fence_before();
       if constexpr (PAIR) {
         __syncwarp();
-        if (lane == 0) sm100::mbar_arrive_cluster(sm100::mapa(sm100::smem_u32(&acc_empty[as]), 0));
+        if (lane == 0) sm100::mbar_arrive_cluster_relaxed(sm100::mapa(sm100::smem_u32(&acc_empty[as]), 0));
       } else {
         sm100::mbar_arrive(&acc_empty[as]);
       }

@@ -367,6 +367,13 @@ __device__ __forceinline__ void cluster_sync() {
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
+// Relaxed arrive on a barrier of either CTA of the cluster: orders none of
+// the thread's earlier memory operations (a release at cluster scope waits
+// for its earlier global stores to be performed). For signals whose consumer
+// needs no data from this thread's generic-proxy stores.
+__device__ __forceinline__ void mbar_arrive_cluster_relaxed(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
 // Tiled TMA loads into this CTA's shared memory whose completion is counted
 // on an mbarrier of either CTA of the pair (no multicast: each CTA loads its
 // own tile).
