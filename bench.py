@@ -57,8 +57,8 @@ METRIC = "DiT latent tokens/s/GPU (routed attn+NVFP4 linears); 720p x4 out frame
 # `python -m recavsr_b200.profile_case gemm_up|attention`); a profiler figure,
 # not measured by this script.
 PROFILED_DRAM = {
-    "ffn_up": {"read": 28012288, "write": 86272,
-               "source": "ncu on profile_case gemm_up (1760x14336x3072, GELU+NVFP4 epilogue, 128x256 tiles)"},
+    "ffn_up": {"read": 28039936, "write": 129280,
+               "source": "ncu on profile_case gemm_up (1760x14336x3072, GELU+NVFP4 epilogue, 256x256 CTA-pair tiles)"},
     "attention": {"read": 75758080, "write": 2477824,
                   "source": "ncu on profile_case attention (1760 queries, 4 routed + 2 current planes)"},
 }
