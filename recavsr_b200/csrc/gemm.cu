@@ -593,7 +593,11 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
         if constexpr (EPI == EPI_SWIGLU) {
           // Columns n0 .. n0 + 7 hold gate, n0 + 8 .. n0 + 15 up for output
           // columns n0 / 2 .. n0 / 2 + 7: bf16(bf16(silu(gate)) * up), SiLU as
-          // x / (1 + exp(-x)) in fp32.
+          // x / (1 + exp(-x)) in fp32 with the MUFU exp2 (of -x log2 e) and
+          // reciprocal, without flush to zero: a few fp32 ulps from the IEEE
+          // quotient, which the bf16 rounding hides on all but ~1e-4 of the
+          // values (the exact quotient made this epilogue, not the MMA, bound
+          // the decoder's K = 512 gate|up GEMMs).
           uint32_t sw[4];
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
@@ -601,7 +605,10 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
 #pragma unroll
             for (int k = 0; k < 2; ++k) {
               const float g = v[2 * j + k];
-              const float sg = __bfloat162float(__float2bfloat16_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g)))));
+              float e, r;
+              asm("ex2.approx.f32 %0, %1;" : "=f"(e) : "f"(__fmul_rn(g, -1.4426950408889634f)));
+              asm("rcp.approx.f32 %0, %1;" : "=f"(r) : "f"(__fadd_rn(1.0f, e)));
+              const float sg = __bfloat162float(__float2bfloat16_rn(__fmul_rn(g, r)));
               s2[k] = __fmul_rn(sg, v[8 + 2 * j + k]);
             }
             sw[j] = rc::pack_bf16x2(s2[0], s2[1]);
