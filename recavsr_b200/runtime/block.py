@@ -330,7 +330,8 @@ class LayerStack:
         self.rope = b0.tables["rope"]
         self._ws: dict[int, Workspace] = {}
         self._io: dict[int, dict] = {}          # step_host staging buffers and events per token count
-        self._copy_stream = None
+        self._copy_stream = None          # host -> device inputs of step_host
+        self._copy_out_stream = None      # device -> host results of step_host
         self._graphs: dict[int, torch.cuda.CUDAGraph] = {}
         self.reset()
 
@@ -431,8 +432,10 @@ class LayerStack:
     def step_host(self, host_in: torch.Tensor, host_out: torch.Tensor, frames: int) -> "HostStep":
         """One body block from pinned host memory to pinned host memory through
         the captured graph: the host-to-device copy of this block's hidden state
-        and the device-to-host copy of its result run on a copy stream, so they
-        overlap the previous / next block's layer loop (double-buffered staging).
+        and the device-to-host copy of its result run on two copy streams
+        (inputs, outputs), so they overlap the previous / next block's layer
+        loop (double-buffered staging) and the next input copy never queues
+        behind an output copy waiting for its block's compute.
 
         Asynchronous: the call returns before either copy has run. The returned
         HostStep says when the caller may touch the buffers again: host_in must
@@ -458,8 +461,9 @@ class LayerStack:
             self._io[n] = io
         if self._copy_stream is None:
             self._copy_stream = torch.cuda.Stream(self.device)
+            self._copy_out_stream = torch.cuda.Stream(self.device)
         k = io["k"] & 1
-        comp, cs = torch.cuda.current_stream(self.device), self._copy_stream
+        comp, cs, co = torch.cuda.current_stream(self.device), self._copy_stream, self._copy_out_stream
         handle = HostStep(torch.cuda.Event(), torch.cuda.Event())
         with torch.cuda.stream(cs):
             cs.wait_event(io["consumed"][k])          # the block two steps back has read this buffer
@@ -475,11 +479,11 @@ class LayerStack:
         comp.wait_event(io["drained"][k])             # its previous result has left the device
         io["out"][k].copy_(self._static[n])
         io["done"][k].record(comp)
-        with torch.cuda.stream(cs):
-            cs.wait_event(io["done"][k])
+        with torch.cuda.stream(co):
+            co.wait_event(io["done"][k])
             host_out.copy_(io["out"][k], non_blocking=True)
-            io["drained"][k].record(cs)
-            handle.output_ready.record(cs)
+            io["drained"][k].record(co)
+            handle.output_ready.record(co)
         io["k"] += 1
         return handle
 
@@ -497,8 +501,9 @@ class LayerStack:
         host_in was read, every host_out written); the current stream also
         waits for them."""
         if self._copy_stream is not None:
-            torch.cuda.current_stream(self.device).wait_stream(self._copy_stream)
-            self._copy_stream.synchronize()
+            for s in (self._copy_stream, self._copy_out_stream):
+                torch.cuda.current_stream(self.device).wait_stream(s)
+                s.synchronize()
 
     def capture(self, n: int, frames: int):
         """Capture one block of the layer loop for a token count n (after at

@@ -321,8 +321,10 @@ class StreamingSession:
     def step_host(self, host_lq: torch.Tensor, host_out: torch.Tensor) -> HostStep:
         """step() from pinned host LQ frames to pinned host latents: the
         host-to-device copy of this block's frames and the device-to-host copy
-        of its result run on a copy stream with double-buffered staging, so they
-        overlap the neighbouring blocks' work.
+        of its result run on two copy streams (inputs, outputs) with
+        double-buffered staging, so they overlap the neighbouring blocks' work:
+        the next block's input copy does not queue behind this block's output
+        copy, which has to wait for this block's compute.
 
         Asynchronous: the call returns before either copy has run. host_lq must
         not be rewritten before the returned HostStep's `input_consumed` has
@@ -330,8 +332,8 @@ class StreamingSession:
         completed; sync_host() waits for every copy issued so far."""
         dev = self.glue.device
         if getattr(self, "_copy", None) is None:
-            self._copy, self._stage = torch.cuda.Stream(dev), {}
-        comp, cs = torch.cuda.current_stream(dev), self._copy
+            self._copy, self._copy_out, self._stage = torch.cuda.Stream(dev), torch.cuda.Stream(dev), {}
+        comp, cs, co = torch.cuda.current_stream(dev), self._copy, self._copy_out
         key = tuple(host_lq.shape)
         if key not in self._stage:
             st = {"lq": [torch.empty(key, dtype=torch.bfloat16, device=dev) for _ in range(2)], "k": 0,
@@ -353,11 +355,11 @@ class StreamingSession:
         st["consumed"][k].record(comp)
         done = torch.cuda.Event()
         done.record(comp)
-        with torch.cuda.stream(cs):
-            cs.wait_event(done)
+        with torch.cuda.stream(co):
+            co.wait_event(done)
             host_out.copy_(result, non_blocking=True)
-            handle.output_ready.record(cs)
-        result.record_stream(cs)
+            handle.output_ready.record(co)
+        result.record_stream(co)
         st["k"] += 1
         return handle
 
@@ -365,5 +367,6 @@ class StreamingSession:
         """Block the host until every step_host copy issued so far has run; the
         current stream also waits for them."""
         if getattr(self, "_copy", None) is not None:
-            torch.cuda.current_stream(self.glue.device).wait_stream(self._copy)
-            self._copy.synchronize()
+            for s in (self._copy, self._copy_out):
+                torch.cuda.current_stream(self.glue.device).wait_stream(s)
+                s.synchronize()
