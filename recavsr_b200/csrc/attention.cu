@@ -231,7 +231,6 @@ attention_kernel(const __grid_constant__ CUtensorMap tm_k,
   int* s_planes = reinterpret_cast<int*>(smem + L::offMisc + 16);   // kMaxPlanes
 
   rc::pdl_trigger();
-  rc::pdl_wait();   // the previous kernel's outputs are visible from here
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // Unit (query tile, head) and key-tile piece of this CTA.
   int unit = blockIdx.x, piece = 0, nsplit = 1;
@@ -274,17 +273,22 @@ attention_kernel(const __grid_constant__ CUtensorMap tm_k,
     }
     sm100::mbar_init(done, 1);
     *abort_flag = 0;
+    sm100::fence_mbar_init();
+  }
+  if (warp == 1) {
+    sm100::tmem_alloc(tmem_slot, 512);
+    sm100::tmem_relinquish();
+  }
+  // The set-up above (barriers, tensor memory) overlaps the previous kernel's
+  // tail; its outputs, and the routing table, are read only from here.
+  rc::pdl_wait();
+  if (threadIdx.x == 0) {
     // Visible planes: routed past planes (slot >= 0), then the current frames.
     int n = 0;
     for (int i = 0; i < p.CAP; ++i)
       if (p.slots[i] >= 0 && p.slots[i] < p.CAP) s_planes[n++] = i;
     for (int f = 0; f < p.QT; ++f) s_planes[n++] = p.CAP + f;
     *s_nplanes = n;
-    sm100::fence_mbar_init();
-  }
-  if (warp == 1) {
-    sm100::tmem_alloc(tmem_slot, 512);
-    sm100::tmem_relinquish();
   }
   sm100::tc_fence_before();
   __syncthreads();
