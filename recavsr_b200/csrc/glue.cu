@@ -158,6 +158,27 @@ __global__ void __launch_bounds__(kRowThreads, ln_min_blocks<CH, AFF, MOD>()) ln
     raw[i] = c < nch ? rc::ld_in(reinterpret_cast<const uint4*>(a.x + (size_t)row * a.ldx) + c)
                      : make_uint4(0, 0, 0, 0);
   }
+  // Every per-column vector of this thread's chunks, loaded with the row,
+  // before the reductions (their latency overlaps the two block barriers)
+  // and before the first store (a store through a byte pointer may alias
+  // them, so a load inside the chunk loop would wait behind the previous
+  // chunk's stores).
+  uint4 wraw[AFF ? CH : 1], braw[AFF ? CH : 1];
+  float sc[MOD ? CH : 1][8], sh[MOD ? CH : 1][8];
+#pragma unroll
+  for (int i = 0; i < CH; ++i) {
+    const int c = t + i * kRowThreads;
+    const bool live = c < nch;
+    const int n0 = c * 8;
+    if constexpr (AFF) {
+      wraw[i] = live && a.weight ? rc::ld_in(reinterpret_cast<const uint4*>(a.weight + n0)) : make_uint4(0, 0, 0, 0);
+      braw[i] = live && a.bias ? rc::ld_in(reinterpret_cast<const uint4*>(a.bias + n0)) : make_uint4(0, 0, 0, 0);
+    }
+    if constexpr (MOD) {
+      if (live && a.scale) loadf8(a.scale + n0, sc[i]);
+      if (live && a.shift) loadf8(a.shift + n0, sh[i]);
+    }
+  }
   float s = 0.f;
 #pragma unroll
   for (int i = 0; i < CH; ++i) {
@@ -181,25 +202,6 @@ __global__ void __launch_bounds__(kRowThreads, ln_min_blocks<CH, AFF, MOD>()) ln
     }
   }
   const float rstd = rsqrtf(__fdiv_rn(row_sum(m2, red), (float)a.N) + a.eps);
-  // Every per-column vector of this thread's chunks, loaded together before
-  // the first store (a store through a byte pointer may alias them, so a load
-  // inside the chunk loop would wait behind the previous chunk's stores).
-  uint4 wraw[AFF ? CH : 1], braw[AFF ? CH : 1];
-  float sc[MOD ? CH : 1][8], sh[MOD ? CH : 1][8];
-#pragma unroll
-  for (int i = 0; i < CH; ++i) {
-    const int c = t + i * kRowThreads;
-    const bool live = c < nch;
-    const int n0 = c * 8;
-    if constexpr (AFF) {
-      wraw[i] = live && a.weight ? rc::ld_in(reinterpret_cast<const uint4*>(a.weight + n0)) : make_uint4(0, 0, 0, 0);
-      braw[i] = live && a.bias ? rc::ld_in(reinterpret_cast<const uint4*>(a.bias + n0)) : make_uint4(0, 0, 0, 0);
-    }
-    if constexpr (MOD) {
-      if (live && a.scale) loadf8(a.scale + n0, sc[i]);
-      if (live && a.shift) loadf8(a.shift + n0, sh[i]);
-    }
-  }
   const int katoms = ((a.N >> 4) + 3) >> 2;
   const float2 nmean = make_float2(-mean, -mean), rstd2 = make_float2(rstd, rstd);
   const float2 one2 = make_float2(1.0f, 1.0f);
