@@ -914,6 +914,13 @@ bool gemm_prefer_wide(int epi, int M, int N, int K) {
   (void)M; (void)K;
   return epi == EPI_GELU_NVF4 && N >= 12288;
 }
+// bf16 GEMMs with a long K and at least four waves of 128 x 256 tiles (the LQ
+// projector's first convolution, 14080 x 2048 x 27648).
+bool gemm_prefer_wide_bf16(int epi, int M, int N, int K) {
+  if (N % 256 || epi == EPI_SWIGLU) return false;
+  const long long wide_tiles = (long long)((M + 127) / 128) * (N / 256);
+  return K >= 16384 && wide_tiles >= 4LL * rc::sm_count();
+}
 
 // Shared argument checks + tensor maps; `elem_bytes_x2` = 2 * bytes/element
 // (1 for fp4, 2 for fp8, 4 for bf16).
@@ -940,7 +947,7 @@ int run_gemm(int kind, int epi, const void* a, const void* b, int M, int N, int 
   const uint64_t da[2] = {row_bytes, (uint64_t)M}, db[2] = {row_bytes, (uint64_t)N};
   const uint64_t sa[1] = {row_bytes}, sb[1] = {row_bytes};
   const bool pair = gemm_use_pair(kind, M, N, K);
-  const bool wide = !pair && gemm_prefer_wide(epi, M, N, K);
+  const bool wide = !pair && (kind == KIND_BF16 ? gemm_prefer_wide_bf16(epi, M, N, K) : gemm_prefer_wide(epi, M, N, K));
   const bool staged = !pair && !wide && epi != EPI_GELU_NVF4;   // the kernel's kStaged
   const uint32_t boxa[2] = {128, 128}, boxb[2] = {128, (uint32_t)(wide ? 256 : 128)};
   int r = rc::encode_tmap(&maps.a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(a), da, sa, boxa,
