@@ -392,3 +392,29 @@ def test_bf16_gemm_split_workspace_matches_plain():
     assert max_rel(host(outs[0]), ref) < TOL
     assert max_rel(host(outs[0]), host(plain)) < 2 ** -8
     assert int(ws[-640:].count_nonzero()) == 0
+
+
+def test_bf16_gemm_wide_tiles_long_k():
+    """bf16 GEMMs with K >= 16384 and at least four waves of 128 x 256 tiles
+    (the LQ projector's conv1 shape class) run on the wide single-accumulator
+    tiles: 9472 x 2048 x 16384 with bias and with the residual epilogue
+    against torch's fp32 matmul of the same bf16 operands."""
+    from recavsr_b200 import _lib
+    g = torch.Generator(device="cuda").manual_seed(41)
+    m, n, k = 9472, 2048, 16384
+    a = torch.randn(m, k, generator=g, device="cuda").bfloat16()
+    w = (torch.randn(n, k, generator=g, device="cuda") * 0.02).bfloat16()
+    b = (torch.randn(n, generator=g, device="cuda") * 0.1).bfloat16()
+    ref = a.float() @ w.float().T + b.float()
+    out = torch.empty(m, n, dtype=torch.bfloat16, device="cuda")
+    _lib.call("rc_bf16_gemm", a.data_ptr(), w.data_ptr(), b.data_ptr(), m, n, k, _lib.EPI_BIAS, out.data_ptr(), n,
+              None, _lib.stream())
+    h = (torch.randn(m, n, generator=g, device="cuda")).bfloat16()
+    res = h.clone()
+    _lib.call("rc_bf16_gemm", a.data_ptr(), w.data_ptr(), b.data_ptr(), m, n, k, _lib.EPI_RESIDUAL, res.data_ptr(),
+              n, None, _lib.stream())
+    assert_no_device_error()
+    scale = ref.abs().max().item()
+    assert (out.float() - ref).abs().max().item() < TOL * scale
+    ref_res = h.float() + ref.bfloat16().float()
+    assert (res.float() - ref_res).abs().max().item() < TOL * ref_res.abs().max().item()
